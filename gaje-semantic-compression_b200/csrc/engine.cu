@@ -1,0 +1,889 @@
+// engine.cu -- the B200 decode engine behind include/gaje_cuda.h.
+//
+// Host side of GenomicLLM for `.gaje.flat` models: load_genomic_auto
+// (src/io/flat_reader.rs:240-251) becomes mmap + validate + one device upload
+// with the Q4_0 blocks repacked; forward_core (src/nn/llm/forward.rs:7-63)
+// becomes one replay of a captured CUDA graph of the step kernels in
+// kernels.cuh; generate_native_core (src/nn/llm/forward.rs:215-330) is the
+// same host loop around it with the token selection done on the device.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "flat_format.h"
+#include "kernels.cuh"
+
+using namespace gaje;
+
+namespace {
+
+#define CK(expr)                                                                         \
+  do {                                                                                   \
+    cudaError_t e_ = (expr);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      return set_error(GAJE_ERR_CUDA, std::string(#expr) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// One device allocation carved into aligned pieces.
+struct Arena {
+  char* base = nullptr;
+  size_t size = 0, used = 0;
+  template <class T>
+  T* take(size_t count) {
+    size_t off = align_up(used, 256);
+    used = off + count * sizeof(T);
+    return base ? reinterpret_cast<T*>(base + off) : nullptr;
+  }
+};
+
+struct Q4Dev {
+  uint4* qs = nullptr;
+  uint32_t* sm = nullptr;
+  float* bias = nullptr;
+  int N = 0, K = 0, nb = 0;
+  Q4View view() const { return Q4View{qs, sm, bias, N, K, nb}; }
+};
+
+// splitmix64 uniforms in [0,1) with 24 bits, as rand's gen::<f32>() builds them.
+struct Rng {
+  uint64_t s = 0;
+  float uniform() {
+    uint64_t z = (s += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    z ^= z >> 31;
+    return float(uint32_t(z >> 32) >> 8) * (1.0f / 16777216.0f);
+  }
+};
+
+}  // namespace
+
+// Token selection of generate_native_core on the device, one CTA:
+// mode 0 greedy (first max), mode 1 temperature sampling with a host uniform r:
+// probs = exp((v - max)/T), choose the first index whose running sum >= r*sum.
+__global__ void __launch_bounds__(1024) k_select(const float* logits, int n, int mode, float temperature,
+                                                 float r, unsigned* out) {
+  __shared__ float redf[32];
+  __shared__ unsigned long long redk[32];
+  __shared__ float scan[1024];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (mode == 0) {
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const unsigned long long k = amax_key(logits[i], (unsigned)i);
+      best = k > best ? k : best;
+    }
+    best = warp_max_u64(best);
+    if (lane == 0) redk[wid] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long b = 0;
+      for (int i = 0; i < nw; ++i) b = redk[i] > b ? redk[i] : b;
+      *out = amax_index(b);
+    }
+    return;
+  }
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) m = fmaxf(m, logits[i]);
+  m = warp_max(m);
+  if (lane == 0) redf[wid] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float b = -INFINITY;
+    for (int i = 0; i < nw; ++i) b = fmaxf(b, redf[i]);
+    redf[0] = b;
+  }
+  __syncthreads();
+  m = redf[0];
+  // contiguous chunk per thread, sequential inside the chunk
+  const int per = (n + blockDim.x - 1) / blockDim.x;
+  const int lo = min(n, (int)threadIdx.x * per), hi = min(n, lo + per);
+  float local = 0.f;
+  for (int i = lo; i < hi; ++i) local += expf((logits[i] - m) / temperature);
+  scan[threadIdx.x] = local;
+  __syncthreads();
+  for (int off = 1; off < (int)blockDim.x; off <<= 1) {  // inclusive Hillis-Steele scan
+    const float v = threadIdx.x >= (unsigned)off ? scan[threadIdx.x - off] : 0.f;
+    __syncthreads();
+    scan[threadIdx.x] += v;
+    __syncthreads();
+  }
+  const float total = scan[blockDim.x - 1];
+  const float target = r * total;
+  float cum = threadIdx.x ? scan[threadIdx.x - 1] : 0.f;
+  if (threadIdx.x == 0) *out = 0u;  // the reference's fallback index
+  __syncthreads();
+  if (!(target <= scan[threadIdx.x]) || (threadIdx.x && target <= cum)) return;
+  for (int i = lo; i < hi; ++i) {
+    cum += expf((logits[i] - m) / temperature);
+    if (target <= cum) {
+      *out = (unsigned)i;
+      return;
+    }
+  }
+}
+
+// Repetition penalty of generate_native_core (llm/forward.rs:243-260).
+__global__ void k_penalty(float* logits, int n, const unsigned* ids, int n_ids, float p) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n_ids; i += gridDim.x * blockDim.x) {
+    const unsigned t = ids[i];
+    if (t < (unsigned)n) {
+      const float v = logits[t];
+      logits[t] = v < 0.0f ? v * p : v / p;
+    }
+  }
+}
+
+struct gaje_model {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  gaje_flat_info info{};
+  int d = 0, nh = 0, nkv = 0, hd = 0, ff = 0, V = 0, L = 0, max_ctx = 0;
+  // device memory
+  Arena arena;
+  std::vector<Q4Dev> qkv, wo, gate_up, down;
+  std::vector<float*> attn_norm, ffn_norm;
+  float* out_norm = nullptr;
+  float* embd = nullptr;
+  float* lm_head = nullptr;
+  float* lm_bias = nullptr;
+  float* kcache = nullptr;
+  float* vcache = nullptr;
+  float2* rope = nullptr;
+  float *x = nullptr, *q = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
+  float *part_o = nullptr, *part_ml = nullptr;
+  unsigned* attn_cnt = nullptr;
+  unsigned long long* amax_part = nullptr;
+  unsigned* amax_cnt = nullptr;
+  unsigned* tok_hist = nullptr;
+  unsigned* sel_out = nullptr;
+  unsigned* pen_ids = nullptr;
+  DevState* st = nullptr;
+  // pinned host staging
+  DevState* h_st = nullptr;
+  unsigned* h_tok = nullptr;
+  // step
+  StepParams P{};
+  int lm_grid = 0, attn_chunk_max = 0;
+  size_t attn_smem = 0;
+  float k_wta_ratio = 0.5f;        // flat_reader.rs:234
+  float block_k_wta_ratio = 0.0f;  // block/init.rs:42
+  bool use_graph = true;
+  cudaGraphExec_t graph = nullptr;
+  int graph_kwta_k = -1, graph_block_k = -1;
+  uint32_t host_pos = 0;
+  Rng rng;
+
+  ~gaje_model() {
+    if (graph) cudaGraphExecDestroy(graph);
+    if (arena.base) cudaFree(arena.base);
+    if (h_st) cudaFreeHost(h_st);
+    if (h_tok) cudaFreeHost(h_tok);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  int logits_k() const {
+    if (k_wta_ratio > 0.0f && k_wta_ratio < 1.0f) {
+      float kf = float(V) * k_wta_ratio;  // (len as f32 * ratio) as usize, max 1
+      return std::max(1, int(kf));
+    }
+    return 0;
+  }
+  int block_k() const {
+    if (block_k_wta_ratio > 0.0f && block_k_wta_ratio < 1.0f) {
+      float kf = float(d) * block_k_wta_ratio;
+      return std::max(1, int(kf));
+    }
+    return 0;
+  }
+
+  LayerW layer(int l) const {
+    LayerW w;
+    w.qkv = qkv[l].view();
+    w.wo = wo[l].view();
+    w.gate_up = gate_up[l].view();
+    w.down = down[l].view();
+    w.attn_norm = attn_norm[l];
+    w.ffn_norm = ffn_norm[l];
+    w.kc = kcache + (size_t)l * nkv * max_ctx * hd;
+    w.vc = vcache + (size_t)l * nkv * max_ctx * hd;
+    return w;
+  }
+
+  // The step's kernel sequence on `stream` (captured once into the graph).
+  int launch_step(int kk, int bk) {
+    const int nw = kGemvThreads / kWarp;
+    for (int l = 0; l < L; ++l) {
+      LayerW w = layer(l);
+      k_qkv<<<(w.qkv.N / 2 + nw - 1) / nw, kGemvThreads, d * sizeof(float), stream>>>(P, w, l);
+      k_attn<<<dim3(nkv, kAttnMaxSplits), kAttnThreads, attn_smem, stream>>>(P, w);
+      k_oproj<<<(d + nw - 1) / nw, kGemvThreads, w.wo.K * sizeof(float), stream>>>(P, w);
+      k_gateup<<<(ff + nw - 1) / nw, kGemvThreads, d * sizeof(float), stream>>>(P, w, l);
+      k_down<<<(d + nw - 1) / nw, kGemvThreads, ff * sizeof(float), stream>>>(P, w, l);
+      if (bk > 0) k_kwta<<<1, kKwtaThreads, 0, stream>>>(x, d, bk);
+    }
+    k_lmhead<<<lm_grid, kLmThreads, d * sizeof(float), stream>>>(P);
+    if (kk > 0) k_kwta<<<1, kKwtaThreads, 0, stream>>>(logits, V, kk);
+    CK(cudaGetLastError());
+    return GAJE_OK;
+  }
+
+  int run_step() {
+    const int kk = logits_k(), bk = block_k();
+    if (!use_graph) return launch_step(kk, bk);
+    if (!graph || kk != graph_kwta_k || bk != graph_block_k) {
+      if (graph) {
+        cudaGraphExecDestroy(graph);
+        graph = nullptr;
+      }
+      cudaGraph_t g = nullptr;
+      CK(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+      int s = launch_step(kk, bk);
+      cudaError_t e = cudaStreamEndCapture(stream, &g);
+      if (s) {
+        if (g) cudaGraphDestroy(g);
+        return s;
+      }
+      if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+      e = cudaGraphInstantiate(&graph, g, 0);
+      cudaGraphDestroy(g);
+      if (e != cudaSuccess) {
+        graph = nullptr;
+        return set_error(GAJE_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+      }
+      graph_kwta_k = kk;
+      graph_block_k = bk;
+    }
+    CK(cudaGraphLaunch(graph, stream));
+    return GAJE_OK;
+  }
+
+  // Reads the device state after a synchronised step and maps a NaN guard to
+  // the reference's error string.
+  int check_nan() {
+    if (h_st->nan_code == 0xFFFFFFFFu) return GAJE_OK;
+    const unsigned code = h_st->nan_code & 4095u;
+    static const char* msgs[] = {"Input x is NaN", "NaN after attn rms_norm", "NaN in up",
+                                 "NaN in ffn_out", "NaN in projected_ffn",
+                                 "NaN after projected_ffn addition"};
+    const unsigned check = code & 7u, layer = code >> 3;
+    std::string m = check < 6 ? msgs[check] : "NaN";
+    m += " (block " + std::to_string(layer) + ", position " + std::to_string(h_st->nan_code >> 12) + ")";
+    // re-arm the guard word
+    h_st->nan_code = 0xFFFFFFFFu;
+    cudaMemcpyAsync(&st->nan_code, &h_st->nan_code, 4, cudaMemcpyHostToDevice, stream);
+    cudaStreamSynchronize(stream);
+    return set_error(GAJE_ERR_NAN, m);
+  }
+
+  int set_pos(uint32_t p) {
+    host_pos = p;
+    h_st->pos = p;
+    CK(cudaMemcpyAsync(&st->pos, &h_st->pos, 4, cudaMemcpyHostToDevice, stream));
+    return GAJE_OK;
+  }
+};
+
+namespace {
+
+int upload_q4(gaje_model* m, const FlatFile& f, const MatrixRef& ref, Q4Dev& dst, uint32_t* staging) {
+  size_t row0 = 0;
+  for (const FlatEntry* e : ref.parts) {
+    const size_t nb = e->in / 32, nblk = e->out * nb;
+    const uint8_t* src = f.blob(e->dna_off, e->dna_len);
+    CK(cudaMemcpyAsync(staging, src, e->dna_len, cudaMemcpyHostToDevice, m->stream));
+    const int threads = 256, blocks = int(std::min<size_t>((nblk + threads - 1) / threads, 4096));
+    k_repack_q4<<<blocks, threads, 0, m->stream>>>(staging, nblk, dst.qs + row0 * nb, dst.sm + row0 * nb);
+    CK(cudaGetLastError());
+    if (dst.bias) {
+      std::vector<float> b(e->out, 0.0f);
+      if (e->bias_len) memcpy(b.data(), f.blob(e->bias_off, e->bias_len), e->bias_len);
+      CK(cudaMemcpyAsync(dst.bias + row0, b.data(), e->out * 4, cudaMemcpyHostToDevice, m->stream));
+      CK(cudaStreamSynchronize(m->stream));  // b is a host temporary
+    }
+    CK(cudaStreamSynchronize(m->stream));  // staging is reused
+    row0 += e->out;
+  }
+  return GAJE_OK;
+}
+
+// Host libm RoPE table (attention.rs:62-84): freq = 1/powf(base, 2i/hd),
+// theta = pos*freq, (cosf, sinf) -- the same glibc calls Rust std makes.
+std::vector<float2> rope_table(int max_ctx, int hd, float base) {
+  const int half = hd / 2;
+  std::vector<float2> t(size_t(max_ctx) * half);
+  std::vector<float> freq(half);
+  for (int i = 0; i < half; ++i) {
+    volatile float e = (2.0f * float(i)) / float(hd);
+    volatile float p = powf(base, e);
+    freq[i] = 1.0f / p;
+  }
+  for (int pos = 0; pos < max_ctx; ++pos)
+    for (int i = 0; i < half; ++i) {
+      volatile float th = float(pos) * freq[i];
+      t[size_t(pos) * half + i] = make_float2(cosf(th), sinf(th));
+    }
+  return t;
+}
+
+int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
+  FlatFile f;
+  std::string err;
+  if (int s = f.open(path, err)) return set_error(s, err);
+  const gaje_flat_info& I = f.info;
+  if (I.embd_bit_depth != 32 || I.lm_head_bit_depth != 32)
+    return set_error(GAJE_ERR_UNSUPPORTED, "Q8_0 token_embd/lm_head are not implemented on the device yet");
+  if (I.n_embd % 32 != 0)
+    return set_error(GAJE_ERR_UNSUPPORTED, "n_embd must be a multiple of 32");
+  m->info = I;
+  m->d = int(I.n_embd);
+  m->nh = int(I.n_head);
+  m->nkv = int(I.n_head_kv);
+  m->hd = int(I.head_dim);
+  m->ff = int(I.ffn_dim);
+  m->V = int(I.vocab_size);
+  m->L = int(I.n_blocks);
+  m->max_ctx = int(opts && opts->max_ctx ? opts->max_ctx : 4096);
+  m->use_graph = !opts || opts->use_graph;
+  m->rng.s = opts ? opts->seed : 0;
+  if (m->nh / m->nkv > kAttnMaxGroup)
+    return set_error(GAJE_ERR_UNSUPPORTED, "more than 16 query heads per KV head");
+  if (m->max_ctx > (1 << 20)) return set_error(GAJE_ERR_INVALID, "max_ctx above 2^20");
+  CK(cudaSetDevice(m->device));
+  CK(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
+  m->lm_grid = sms * 4;
+  {
+    // chunk(ctx) <= kAttnMinChunk while ctx <= kAttnMinChunk*kAttnMaxSplits,
+    // then ceil(ctx/kAttnMaxSplits): bound it over every ctx <= max_ctx
+    const int chunk = std::max(kAttnMinChunk, (m->max_ctx + kAttnMaxSplits - 1) / kAttnMaxSplits);
+    m->attn_chunk_max = chunk;
+    const int G = m->nh / m->nkv;
+    m->attn_smem = size_t(G) * (m->hd + chunk) * sizeof(float);
+  }
+  // ---- plan the arena (sizes only), then allocate and carve for real
+  const size_t V = m->V, d = m->d, L = m->L;
+  size_t staging_bytes = 0;
+  auto plan = [&](Arena& a) {
+    m->qkv.assign(L, Q4Dev());
+    m->wo.assign(L, Q4Dev());
+    m->gate_up.assign(L, Q4Dev());
+    m->down.assign(L, Q4Dev());
+    m->attn_norm.assign(L, nullptr);
+    m->ffn_norm.assign(L, nullptr);
+    for (size_t l = 0; l < L; ++l) {
+      const BlockRefs& b = f.blocks[l];
+      const MatrixRef* refs[4] = {&b.qkv, &b.wo, &b.gate_up, &b.down};
+      Q4Dev* dsts[4] = {&m->qkv[l], &m->wo[l], &m->gate_up[l], &m->down[l]};
+      for (int k = 0; k < 4; ++k) {
+        Q4Dev& q = *dsts[k];
+        q.N = int(refs[k]->out);
+        q.K = int(refs[k]->in);
+        q.nb = q.K / 32;
+        q.qs = a.take<uint4>(size_t(q.N) * q.nb);
+        q.sm = a.take<uint32_t>(size_t(q.N) * q.nb);
+        q.bias = refs[k]->has_bias ? a.take<float>(q.N) : nullptr;
+        for (const FlatEntry* e : refs[k]->parts) staging_bytes = std::max<size_t>(staging_bytes, e->dna_len);
+      }
+      m->attn_norm[l] = a.take<float>(d);
+      m->ffn_norm[l] = a.take<float>(d);
+    }
+    m->out_norm = a.take<float>(d);
+    m->embd = a.take<float>(V * d);
+    m->lm_head = a.take<float>(V * d);
+    m->lm_bias = f.lm_head->bias_len ? a.take<float>(V) : nullptr;
+    const size_t cache = L * size_t(m->nkv) * m->max_ctx * m->hd;
+    m->kcache = a.take<float>(cache);
+    m->vcache = a.take<float>(cache);
+    m->rope = a.take<float2>(size_t(m->max_ctx) * (m->hd / 2));
+    m->x = a.take<float>(d);
+    m->q = a.take<float>(size_t(m->nh) * m->hd);
+    m->attn = a.take<float>(size_t(m->nh) * m->hd);
+    m->act = a.take<float>(m->ff);
+    m->logits = a.take<float>(V);
+    m->part_o = a.take<float>(size_t(m->nkv) * kAttnMaxSplits * (m->nh / m->nkv) * m->hd);
+    m->part_ml = a.take<float>(size_t(m->nkv) * kAttnMaxSplits * (m->nh / m->nkv) * 2);
+    m->attn_cnt = a.take<unsigned>(m->nkv);
+    m->amax_part = a.take<unsigned long long>(m->lm_grid);
+    m->amax_cnt = a.take<unsigned>(1);
+    m->tok_hist = a.take<unsigned>(m->max_ctx);
+    m->sel_out = a.take<unsigned>(1);
+    m->pen_ids = a.take<unsigned>(m->max_ctx);
+    m->st = a.take<DevState>(1);
+  };
+  Arena sizing;
+  plan(sizing);
+  const size_t staging_words = (staging_bytes + 3) / 4;
+  const size_t total = align_up(sizing.used, 256) + staging_words * 4 + 256;
+  CK(cudaMalloc(&m->arena.base, total));
+  m->arena.size = total;
+  plan(m->arena);
+  uint32_t* staging = m->arena.take<uint32_t>(staging_words);
+  // zero the counters, scratch and state
+  CK(cudaMemsetAsync(m->attn_cnt, 0, m->nkv * sizeof(unsigned), m->stream));
+  CK(cudaMemsetAsync(m->amax_cnt, 0, sizeof(unsigned), m->stream));
+  CK(cudaMemsetAsync(m->kcache, 0, L * size_t(m->nkv) * m->max_ctx * m->hd * 4, m->stream));
+  CK(cudaMemsetAsync(m->vcache, 0, L * size_t(m->nkv) * m->max_ctx * m->hd * 4, m->stream));
+  // ---- upload
+  for (size_t l = 0; l < L; ++l) {
+    const BlockRefs& b = f.blocks[l];
+    if (int s = upload_q4(m, f, b.qkv, m->qkv[l], staging)) return s;
+    if (int s = upload_q4(m, f, b.wo, m->wo[l], staging)) return s;
+    if (int s = upload_q4(m, f, b.gate_up, m->gate_up[l], staging)) return s;
+    if (int s = upload_q4(m, f, b.down, m->down[l], staging)) return s;
+    CK(cudaMemcpy(m->attn_norm[l], f.blob(b.attn_norm->dna_off, d * 4), d * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(m->ffn_norm[l], f.blob(b.ffn_norm->dna_off, d * 4), d * 4, cudaMemcpyHostToDevice));
+  }
+  CK(cudaMemcpy(m->out_norm, f.blob(f.output_norm->dna_off, d * 4), d * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(m->embd, f.blob(f.token_embd->dna_off, V * d * 4), V * d * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(m->lm_head, f.blob(f.lm_head->dna_off, V * d * 4), V * d * 4, cudaMemcpyHostToDevice));
+  if (m->lm_bias) {
+    std::vector<float> b(V, 0.0f);
+    memcpy(b.data(), f.blob(f.lm_head->bias_off, f.lm_head->bias_len), f.lm_head->bias_len);
+    CK(cudaMemcpy(m->lm_bias, b.data(), V * 4, cudaMemcpyHostToDevice));
+  }
+  {
+    std::vector<float2> rt = rope_table(m->max_ctx, m->hd, I.rope_base);
+    CK(cudaMemcpy(m->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  }
+  CK(cudaHostAlloc(&m->h_st, sizeof(DevState), cudaHostAllocDefault));
+  CK(cudaHostAlloc(&m->h_tok, 64 * sizeof(unsigned), cudaHostAllocDefault));
+  memset(m->h_st, 0, sizeof(DevState));
+  m->h_st->nan_code = 0xFFFFFFFFu;
+  CK(cudaMemcpyAsync(m->st, m->h_st, sizeof(DevState), cudaMemcpyHostToDevice, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  // ---- step parameters
+  StepParams& P = m->P;
+  P.d = m->d;
+  P.nh = m->nh;
+  P.nkv = m->nkv;
+  P.hd = m->hd;
+  P.ff = m->ff;
+  P.V = m->V;
+  P.max_ctx = m->max_ctx;
+  P.n_layers = m->L;
+  P.eps = I.eps;
+  P.attn_scale = 1.0f / sqrtf(float(m->hd));
+  P.rope_split = I.rope_split;
+  P.use_genomic_norm = I.use_genomic_norm;
+  P.embd = m->embd;
+  P.lm_head = m->lm_head;
+  P.lm_bias = m->lm_bias;
+  P.out_norm = m->out_norm;
+  P.rope = m->rope;
+  P.x = m->x;
+  P.q = m->q;
+  P.attn = m->attn;
+  P.act = m->act;
+  P.logits = m->logits;
+  P.part_o = m->part_o;
+  P.part_ml = m->part_ml;
+  P.attn_cnt = m->attn_cnt;
+  P.amax_part = m->amax_part;
+  P.amax_cnt = m->amax_cnt;
+  P.tok_hist = m->tok_hist;
+  P.hist_cap = unsigned(m->max_ctx);
+  P.st = m->st;
+  // dynamic shared memory above 48 KB needs an opt-in
+  const int big = int(std::max<size_t>(size_t(std::max(m->ff, m->nh * m->hd)) * 4, m->attn_smem));
+  if (big > 48 * 1024) {
+    CK(cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+    CK(cudaFuncSetAttribute(k_oproj, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+    CK(cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
+  }
+  return GAJE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+void gaje_load_opts_init(gaje_load_opts* o) {
+  if (!o) return;
+  o->device = 0;
+  o->max_ctx = 4096;
+  o->seed = 0;
+  o->use_graph = 1;
+}
+
+gaje_model* gaje_cuda_load(const char* flat_path, const gaje_load_opts* opts) {
+  std::unique_ptr<gaje_model> m(new gaje_model());
+  m->device = opts ? opts->device : 0;
+  if (int s = load_impl(m.get(), flat_path, opts)) {
+    (void)s;
+    return nullptr;
+  }
+  clear_error();
+  return m.release();
+}
+
+void gaje_cuda_free(gaje_model* m) {
+  if (!m) return;
+  cudaSetDevice(m->device);
+  delete m;
+}
+
+int gaje_cuda_model_info(gaje_model* m, gaje_model_info* o) {
+  if (!m || !o) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  o->vocab_size = uint32_t(m->V);
+  o->n_embd = uint32_t(m->d);
+  o->n_head = uint32_t(m->nh);
+  o->n_head_kv = uint32_t(m->nkv);
+  o->n_blocks = uint32_t(m->L);
+  o->head_dim = uint32_t(m->hd);
+  o->ffn_dim = uint32_t(m->ff);
+  o->max_ctx = uint32_t(m->max_ctx);
+  o->cache_len = m->host_pos;
+  o->eps = m->info.eps;
+  o->rope_base = m->info.rope_base;
+  o->k_wta_ratio = m->k_wta_ratio;
+  o->device_bytes = m->arena.size;
+  return GAJE_OK;
+}
+
+void* gaje_cuda_stream(gaje_model* m) { return m ? (void*)m->stream : nullptr; }
+
+int gaje_cuda_clear_cache(gaje_model* m) {
+  if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  CK(cudaSetDevice(m->device));
+  if (int s = m->set_pos(0)) return s;
+  CK(cudaStreamSynchronize(m->stream));
+  return GAJE_OK;
+}
+
+int gaje_cuda_set_k_wta_ratio(gaje_model* m, float ratio) {
+  if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  m->k_wta_ratio = ratio;
+  m->block_k_wta_ratio = ratio;
+  return GAJE_OK;
+}
+
+int gaje_cuda_set_seed(gaje_model* m, uint64_t seed) {
+  if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  m->rng.s = seed;
+  return GAJE_OK;
+}
+
+int gaje_cuda_forward(gaje_model* m, uint32_t token_id, int clear_cache, float* logits_out,
+                      uint32_t* argmax_out) {
+  if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  CK(cudaSetDevice(m->device));
+  if (clear_cache)
+    if (int s = m->set_pos(0)) return s;
+  if (m->host_pos >= uint32_t(m->max_ctx))
+    return set_error(GAJE_ERR_CONTEXT, "KV cache is full (max_ctx positions)");
+  m->h_tok[0] = token_id;
+  CK(cudaMemcpyAsync(&m->st->token, m->h_tok, 4, cudaMemcpyHostToDevice, m->stream));
+  if (int s = m->run_step()) return s;
+  CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
+  if (logits_out) CK(cudaMemcpyAsync(logits_out, m->logits, size_t(m->V) * 4, cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  m->host_pos += 1;
+  if (int s = m->check_nan()) return s;
+  if (argmax_out) *argmax_out = m->h_st->argmax;
+  return GAJE_OK;
+}
+
+int gaje_cuda_decode_greedy(gaje_model* m, uint32_t first_token, size_t n_steps, uint32_t* tokens_out) {
+  if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  CK(cudaSetDevice(m->device));
+  if (size_t(m->host_pos) + n_steps > size_t(m->max_ctx))
+    return set_error(GAJE_ERR_CONTEXT, "KV cache would overflow (max_ctx positions)");
+  m->h_st->token = first_token;
+  m->h_st->hist_len = 0;
+  CK(cudaMemcpyAsync(&m->st->token, &m->h_st->token, 4, cudaMemcpyHostToDevice, m->stream));
+  CK(cudaMemcpyAsync(&m->st->hist_len, &m->h_st->hist_len, 4, cudaMemcpyHostToDevice, m->stream));
+  for (size_t i = 0; i < n_steps; ++i)
+    if (int s = m->run_step()) return s;
+  CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
+  if (tokens_out && n_steps)
+    CK(cudaMemcpyAsync(tokens_out, m->tok_hist, n_steps * 4, cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  m->host_pos += uint32_t(n_steps);
+  return m->check_nan();
+}
+
+int gaje_cuda_generate(gaje_model* m, const uint32_t* prompt, size_t n_prompt, size_t max_new,
+                       float temperature, float rep_penalty, const uint32_t* eos, size_t n_eos,
+                       uint32_t* out, size_t* n_out) {
+  if (!m || !n_out || (n_prompt && !prompt) || (n_eos && !eos) || (max_new && !out))
+    return set_error(GAJE_ERR_INVALID, "NULL argument");
+  *n_out = 0;
+  if (n_prompt == 0) return set_error(GAJE_ERR_INVALID, "Prompt tokens cannot be empty");
+  CK(cudaSetDevice(m->device));
+  if (n_prompt + max_new > size_t(m->max_ctx))
+    return set_error(GAJE_ERR_CONTEXT, "prompt + max_new exceeds max_ctx");
+  if (int s = m->set_pos(0)) return s;
+  // prefill token by token, as the reference does
+  for (size_t i = 0; i < n_prompt; ++i) {
+    m->h_tok[0] = prompt[i];
+    CK(cudaMemcpyAsync(&m->st->token, m->h_tok, 4, cudaMemcpyHostToDevice, m->stream));
+    if (int s = m->run_step()) return s;
+    CK(cudaStreamSynchronize(m->stream));  // h_tok is reused
+    m->host_pos += 1;
+  }
+  CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  if (int s = m->check_nan()) return s;
+  std::vector<uint32_t> gen;
+  std::set<uint32_t> eos_set(eos, eos + n_eos);
+  std::vector<unsigned> seen_host;
+  for (size_t step = 0; step < max_new; ++step) {
+    uint32_t next;
+    const bool penal = rep_penalty > 1.0f;
+    if (penal) {
+      std::set<uint32_t> seen(gen.begin(), gen.end());
+      for (uint32_t e : eos_set) seen.erase(e);
+      seen_host.assign(seen.begin(), seen.end());
+      if (!seen_host.empty()) {
+        CK(cudaMemcpyAsync(m->pen_ids, seen_host.data(), seen_host.size() * 4, cudaMemcpyHostToDevice, m->stream));
+        k_penalty<<<1, 256, 0, m->stream>>>(m->logits, m->V, m->pen_ids, int(seen_host.size()), rep_penalty);
+        CK(cudaGetLastError());
+      }
+    }
+    if (temperature <= 1e-5f) {
+      if (penal) {
+        k_select<<<1, 1024, 0, m->stream>>>(m->logits, m->V, 0, 1.0f, 0.0f, m->sel_out);
+        CK(cudaGetLastError());
+        CK(cudaMemcpyAsync(m->h_tok, m->sel_out, 4, cudaMemcpyDeviceToHost, m->stream));
+        CK(cudaStreamSynchronize(m->stream));
+        next = m->h_tok[0];
+      } else {
+        next = m->h_st->argmax;  // the lm_head kernel's first-max argmax
+      }
+    } else {
+      const float r = m->rng.uniform();
+      k_select<<<1, 1024, 0, m->stream>>>(m->logits, m->V, 1, temperature, r, m->sel_out);
+      CK(cudaGetLastError());
+      CK(cudaMemcpyAsync(m->h_tok, m->sel_out, 4, cudaMemcpyDeviceToHost, m->stream));
+      CK(cudaStreamSynchronize(m->stream));
+      next = m->h_tok[0];
+    }
+    gen.push_back(next);
+    if (eos_set.count(next)) break;
+    bool repeated = false;
+    for (size_t w = 2; w <= 48 && !repeated; ++w) {
+      if (gen.size() >= w * 3) {
+        const size_t L = gen.size();
+        repeated = std::equal(gen.begin() + (L - w), gen.end(), gen.begin() + (L - 2 * w)) &&
+                   std::equal(gen.begin() + (L - w), gen.end(), gen.begin() + (L - 3 * w));
+      }
+    }
+    if (repeated) break;
+    if (m->host_pos >= uint32_t(m->max_ctx)) return set_error(GAJE_ERR_CONTEXT, "KV cache is full");
+    m->h_tok[0] = next;
+    CK(cudaMemcpyAsync(&m->st->token, m->h_tok, 4, cudaMemcpyHostToDevice, m->stream));
+    if (int s = m->run_step()) return s;
+    CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
+    CK(cudaStreamSynchronize(m->stream));
+    m->host_pos += 1;
+    if (int s = m->check_nan()) return s;
+  }
+  for (size_t i = 0; i < gen.size(); ++i) out[i] = gen[i];
+  *n_out = gen.size();
+  clear_error();
+  return GAJE_OK;
+}
+
+}  // extern "C"
+
+// ================================================================ op level
+struct gaje_q4_matrix {
+  int device = 0;
+  Q4Dev m;
+  void* mem = nullptr;
+};
+
+namespace {
+
+// One scratch area per device for the op-level entry points (argmax partials
+// and attention split partials).  Calls that overlap on the GPU share it.
+struct OpWorkspace {
+  std::mutex mu;
+  void* mem = nullptr;
+  size_t size = 0;
+};
+OpWorkspace g_ws[64];
+// layout: [argmax partials, kWsArgmaxParts x u64][argmax counter] ... attention from kWsAttnBase
+constexpr size_t kWsArgmaxParts = 4096;
+constexpr size_t kWsAttnBase = kWsArgmaxParts * 8 + 4096;
+
+int ws_get(int dev, size_t bytes, void** out) {
+  if (dev < 0 || dev >= 64) return set_error(GAJE_ERR_INVALID, "device ordinal out of range");
+  OpWorkspace& w = g_ws[dev];
+  std::lock_guard<std::mutex> lk(w.mu);
+  if (w.size < bytes) {
+    if (w.mem) {
+      cudaDeviceSynchronize();
+      cudaFree(w.mem);
+      w.mem = nullptr;
+      w.size = 0;
+    }
+    CK(cudaMalloc(&w.mem, bytes));
+    CK(cudaMemset(w.mem, 0, bytes));
+    w.size = bytes;
+  }
+  *out = w.mem;
+  return GAJE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+gaje_q4_matrix* gaje_cuda_q4_0_upload(const uint8_t* blocks, size_t N, size_t K, const float* bias,
+                                      int device) {
+  if (!blocks || !N || !K || K % 32) {
+    set_error(GAJE_ERR_INVALID, "blocks must be non-NULL with K a multiple of 32");
+    return nullptr;
+  }
+  if (cudaSetDevice(device) != cudaSuccess) {
+    set_error(GAJE_ERR_CUDA, "cudaSetDevice failed");
+    return nullptr;
+  }
+  std::unique_ptr<gaje_q4_matrix> h(new gaje_q4_matrix());
+  h->device = device;
+  const size_t nb = K / 32, nblk = N * nb;
+  Arena a;
+  auto carve = [&](Arena& ar, uint32_t** raw) {
+    h->m.qs = ar.take<uint4>(nblk);
+    h->m.sm = ar.take<uint32_t>(nblk);
+    h->m.bias = bias ? ar.take<float>(N) : nullptr;
+    *raw = ar.take<uint32_t>(nblk * 5);
+  };
+  uint32_t* raw = nullptr;
+  carve(a, &raw);
+  if (cudaMalloc(&h->mem, a.used) != cudaSuccess) {
+    set_error(GAJE_ERR_CUDA, "cudaMalloc failed");
+    return nullptr;
+  }
+  Arena b;
+  b.base = static_cast<char*>(h->mem);
+  carve(b, &raw);
+  h->m.N = int(N);
+  h->m.K = int(K);
+  h->m.nb = int(nb);
+  if (cudaMemcpy(raw, blocks, nblk * 20, cudaMemcpyHostToDevice) != cudaSuccess ||
+      (bias && cudaMemcpy(h->m.bias, bias, N * 4, cudaMemcpyHostToDevice) != cudaSuccess)) {
+    cudaFree(h->mem);
+    set_error(GAJE_ERR_CUDA, "upload failed");
+    return nullptr;
+  }
+  k_repack_q4<<<int(std::min<size_t>((nblk + 255) / 256, 4096)), 256>>>(raw, nblk, h->m.qs, h->m.sm);
+  if (cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(h->mem);
+    set_error(GAJE_ERR_CUDA, "repack failed");
+    return nullptr;
+  }
+  clear_error();
+  return h.release();
+}
+
+void gaje_cuda_q4_0_release(gaje_q4_matrix* h) {
+  if (!h) return;
+  cudaSetDevice(h->device);
+  cudaFree(h->mem);
+  delete h;
+}
+
+int gaje_cuda_q4_0_gemv(const gaje_q4_matrix* h, const float* x, float* y, size_t M, void* stream) {
+  if (!h || !x || !y) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  if (M == 0) return GAJE_OK;
+  if (M > 65535) return set_error(GAJE_ERR_INVALID, "M above 65535");
+  CK(cudaSetDevice(h->device));
+  const int nw = kGemvThreads / kWarp;
+  const int ctas = (h->m.N + nw - 1) / nw;
+  const size_t smem = size_t(h->m.K) * 4;
+  if (smem > 48 * 1024) CK(cudaFuncSetAttribute(k_q4_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  k_q4_gemv<<<dim3(ctas, unsigned(M)), kGemvThreads, smem, (cudaStream_t)stream>>>(h->m.view(), x, y);
+  CK(cudaGetLastError());
+  return GAJE_OK;
+}
+
+int gaje_cuda_q4_0_dequant(const gaje_q4_matrix* h, float* w, void* stream) {
+  if (!h || !w) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  CK(cudaSetDevice(h->device));
+  k_dequant_q4<<<1184, 256, 0, (cudaStream_t)stream>>>(h->m.view(), w);
+  CK(cudaGetLastError());
+  return GAJE_OK;
+}
+
+int gaje_cuda_f32_gemv_argmax(const float* W, const float* x, size_t N, size_t K, float* logits,
+                              uint32_t* argmax, void* stream) {
+  if (!W || !x || !argmax || !N || !K) return set_error(GAJE_ERR_INVALID, "bad argument");
+  if (K % 4 || N > 0x7FFFFFFFu) return set_error(GAJE_ERR_UNSUPPORTED, "K must be a multiple of 4");
+  int dev;
+  CK(cudaGetDevice(&dev));
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int grid = std::min(sms * 4, int(kWsArgmaxParts));
+  void* ws;
+  if (int s = ws_get(dev, kWsAttnBase, &ws)) return s;
+  unsigned long long* part = static_cast<unsigned long long*>(ws);
+  unsigned* cnt = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + kWsArgmaxParts * 8);
+  const size_t smem = K * 4;
+  if (smem > 48 * 1024) CK(cudaFuncSetAttribute(k_f32_gemv_argmax, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  k_f32_gemv_argmax<<<grid, kLmThreads, smem, (cudaStream_t)stream>>>(W, x, int(N), int(K), logits, part, cnt, argmax);
+  CK(cudaGetLastError());
+  return GAJE_OK;
+}
+
+int gaje_cuda_rms_norm(const float* x, const float* w, float eps, size_t n, float* out, void* stream) {
+  if (!x || !w || !out || !n) return set_error(GAJE_ERR_INVALID, "bad argument");
+  k_rmsnorm<<<1, 1024, 0, (cudaStream_t)stream>>>(x, w, eps, int(n), out);
+  CK(cudaGetLastError());
+  return GAJE_OK;
+}
+
+int gaje_cuda_attention_decode(const float* q, const float* k_cache, const float* v_cache, size_t ctx,
+                               size_t cache_stride, size_t n_head, size_t n_head_kv, size_t head_dim,
+                               float* out, void* stream) {
+  if (!q || !k_cache || !v_cache || !out || !ctx || !n_head || !n_head_kv || !head_dim)
+    return set_error(GAJE_ERR_INVALID, "bad argument");
+  if (n_head % n_head_kv || n_head / n_head_kv > size_t(kAttnMaxGroup) || ctx > cache_stride)
+    return set_error(GAJE_ERR_UNSUPPORTED, "unsupported attention geometry");
+  int dev;
+  CK(cudaGetDevice(&dev));
+  int nsplit, chunk;
+  attn_splits(int(ctx), nsplit, chunk);
+  const size_t G = n_head / n_head_kv;
+  const size_t po = n_head_kv * kAttnMaxSplits * G * head_dim, pml = n_head_kv * kAttnMaxSplits * G * 2;
+  // workspace: [counters 256 B][part_ml][part_o], behind the argmax area
+  const size_t base = kWsAttnBase;
+  void* ws;
+  if (int s = ws_get(dev, base + 256 + (pml + po) * 4 + 256, &ws)) return s;
+  char* w = static_cast<char*>(ws) + base;
+  unsigned* cnt = reinterpret_cast<unsigned*>(w);
+  float* part_ml = reinterpret_cast<float*>(w + 256);
+  float* part_o = part_ml + pml;
+  if (n_head_kv > 64) return set_error(GAJE_ERR_UNSUPPORTED, "more than 64 KV heads");
+  const size_t smem = G * (head_dim + chunk) * 4;
+  if (smem > 48 * 1024) CK(cudaFuncSetAttribute(k_attn_op, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
+  const float scale = 1.0f / sqrtf(float(head_dim));
+  k_attn_op<<<dim3(unsigned(n_head_kv), kAttnMaxSplits), kAttnThreads, smem, (cudaStream_t)stream>>>(
+      q, k_cache, v_cache, out, int(ctx), int(cache_stride), int(n_head), int(n_head_kv), int(head_dim), scale,
+      part_o, part_ml, cnt);
+  CK(cudaGetLastError());
+  return GAJE_OK;
+}
+
+int gaje_cuda_kwta(float* scores, size_t n, size_t k, void* stream) {
+  if (!scores) return set_error(GAJE_ERR_INVALID, "scores is NULL");
+  if (n > 0x7FFFFFFFu) return set_error(GAJE_ERR_INVALID, "n too large");
+  k_kwta<<<1, kKwtaThreads, 0, (cudaStream_t)stream>>>(scores, int(n), int(std::min<size_t>(k, 0x7FFFFFFF)));
+  CK(cudaGetLastError());
+  return GAJE_OK;
+}
+
+}  // extern "C"

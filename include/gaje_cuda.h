@@ -1,0 +1,231 @@
+/*
+ * gaje_cuda.h -- C ABI of the B200 decode engine for GAJE `.gaje.flat` v2 models.
+ *
+ * This is the drop-in boundary for the reference's decode path.  The reference
+ * exposes that path only as Rust/PyO3 functions (its one C ABI, src/ffi.rs,
+ * reaches redb `.gaje` sessions, not `.flat` files); each entry point below
+ * names the reference function it replaces, by path:line inside the reference
+ * project.  Conventions follow src/ffi.rs:13-90: opaque handles created by a
+ * *_load call and released by the matching *_free, NULL on failure, every
+ * pointer NULL-checked.  Because Result<_, String> has no C analogue, calls
+ * return a status code (GAJE_OK == 0) and the message is available from
+ * gaje_cuda_last_error() (thread-local).
+ *
+ * Threading: a gaje_model is not thread-safe (the reference methods take
+ * &mut self).  Each model owns one CUDA stream, its KV cache and its scratch.
+ *
+ * Device errors become status codes: kernels never trap or assert.
+ */
+#ifndef GAJE_CUDA_H
+#define GAJE_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status codes */
+enum gaje_status {
+  GAJE_OK = 0,
+  GAJE_ERR_INVALID = 1,     /* NULL pointer or argument out of range            */
+  GAJE_ERR_IO = 2,          /* open/mmap failure, truncated file, bad magic,
+                               malformed JSON (io::ErrorKind::InvalidData)       */
+  GAJE_ERR_NOT_FOUND = 3,   /* tensor missing from the directory (NotFound)     */
+  GAJE_ERR_SHAPE = 4,       /* tensor shapes/sizes inconsistent with the config */
+  GAJE_ERR_UNSUPPORTED = 5, /* a format arm this engine does not implement      */
+  GAJE_ERR_CUDA = 6,        /* CUDA runtime failure                             */
+  GAJE_ERR_NAN = 7,         /* a NaN guard of src/nn/block/forward.rs fired      */
+  GAJE_ERR_CONTEXT = 8,     /* KV cache full (max_ctx positions)                */
+  GAJE_ERR_TIMEOUT = 9      /* a bounded device-side wait ran out               */
+};
+
+/* Thread-local message for the last failing call on this thread ("" if none). */
+const char* gaje_cuda_last_error(void);
+
+/* ------------------------------------------------------------- file format */
+/* The fixed fields of FlatHeaderV2 (src/io/header/flat.rs:14-42). */
+typedef struct gaje_flat_header {
+  uint32_t version, flags, num_tensors;
+  uint64_t meta_len, dir_len, weights_offset, weights_len;
+  uint32_t group_size, quant_format;
+  uint32_t arch_family, arch_n_embd, arch_n_head, arch_n_head_kv, arch_n_blocks,
+      arch_qk_permute;
+} gaje_flat_header;
+
+/* The model configuration load_genomic derives (src/io/flat_reader.rs:124-142):
+ * metadata JSON ModelConfig (src/io/config.rs:137-145) with the header's
+ * ArchitectureDescriptor override (src/io/header/flat.rs:82-148). */
+typedef struct gaje_flat_info {
+  gaje_flat_header header;
+  uint32_t n_embd, n_head, n_head_kv, n_blocks, head_dim, ffn_dim, vocab_size;
+  float eps, rope_base;
+  int rope_split;       /* 1 = "split" RoPE, 0 = "interleaved"              */
+  int use_genomic_norm; /* ArchConfig.use_genomic_norm                        */
+  int fused_qkv, fused_gate_up;
+  int embd_bit_depth, lm_head_bit_depth, body_bit_depth;
+  uint32_t n_entries;   /* tensors in the directory                         */
+} gaje_flat_info;
+
+/* Parse-only open: header, metadata and directory, every tensor the loader
+ * needs, offsets against the file size.  No device is touched.
+ * Replaces GajeFlatFileReader::open + the validation part of load_genomic
+ * (src/io/flat_reader.rs:33-69, 124-237). */
+int gaje_flat_inspect(const char* path, gaje_flat_info* info);
+
+/* The offline Q4_0 "Variant B" quantiser, 32 floats -> one 20-byte block
+ * {f16 scale, f16 min, u8 qs[16]} (src/compute/quantize/python.rs:152-232).
+ * n must be a multiple of 32; out holds n/32*20 bytes. */
+int gaje_quantize_q4_0(const float* w, size_t n, uint8_t* out);
+/* Q8_0, 32 floats -> {f16 scale, i8 qs[32]} (src/compute/quantize/python.rs:235-303). */
+int gaje_quantize_q8_0(const float* w, size_t n, uint8_t* out);
+
+/* `.gaje.flat` v2 writer with the layout of scripts/export_gaje_flat.py:184-483:
+ * metadata JSON at 4096, directory JSON after it, 64-byte aligned blobs from a
+ * 4 KiB aligned weights_offset, the packed 4096-byte header. */
+typedef struct gaje_flat_writer gaje_flat_writer;
+typedef struct gaje_flat_meta {
+  const char* name;          /* config.name                                  */
+  const char* tokenizer_id;  /* config.tokenizer_id                          */
+  const char* tokenizer;     /* embedded tokenizer JSON string ("" if none)  */
+  uint32_t arch_family;      /* 1 Llama, 2 SmolLM, 3 Qwen2, 4 Qwen2.5, 5 Gemma */
+  uint32_t qk_permute;
+  uint32_t n_embd, n_head, n_head_kv, n_blocks, vocab_size;
+  float eps;
+  double rope_base;
+} gaje_flat_meta;
+gaje_flat_writer* gaje_flat_writer_open(const char* path, const gaje_flat_meta* meta);
+/* bit_depth 4 quantises to Q4_0, 8 to Q8_0, 32 stores raw f32.  bias may be NULL. */
+int gaje_flat_writer_add_linear(gaje_flat_writer* w, const char* name, int bit_depth,
+                                size_t out_features, size_t in_features,
+                                const float* weights, const float* bias);
+/* A norm vector (bit_depth 32, in_features 1), as the exporter writes them. */
+int gaje_flat_writer_add_norm(gaje_flat_writer* w, const char* name, const float* v,
+                              size_t n);
+/* Writes header + metadata + directory + blobs; frees the writer. */
+int gaje_flat_writer_close(gaje_flat_writer* w);
+
+/* Seeded synthetic model: every matrix N(0, std), norms 1.0, optional QKV
+ * bias N(0, std), tied embedding / lm_head written twice as the exporter does
+ * (scripts/export_gaje_flat.py:338-341).  Body Q4_0, embeddings f32 or Q8_0. */
+typedef struct gaje_synth_spec {
+  uint32_t arch_family, n_embd, n_head, n_head_kv, n_blocks, ffn_dim, vocab_size;
+  float eps;
+  double rope_base;
+  int qkv_bias;       /* 1: attn_qkv carries a bias (Qwen2 families)          */
+  int embd_bit_depth; /* 32 (default) or 8                                    */
+  float std;          /* 0 -> 0.02                                            */
+  uint64_t seed;
+} gaje_synth_spec;
+int gaje_flat_write_synthetic(const char* path, const gaje_synth_spec* spec);
+
+/* ------------------------------------------------------------------ model */
+typedef struct gaje_model gaje_model;
+
+typedef struct gaje_load_opts {
+  int device;        /* CUDA device ordinal                                  */
+  uint32_t max_ctx;  /* KV-cache capacity in positions; 0 -> 4096             */
+  uint64_t seed;     /* sampling RNG seed for generate (temperature > 0)      */
+  int use_graph;     /* 1 (default): replay the decode step as a CUDA graph   */
+} gaje_load_opts;
+void gaje_load_opts_init(gaje_load_opts* opts);
+
+/* load_genomic_auto (src/io/flat_reader.rs:240-251) for `.gaje.flat` files:
+ * mmap, parse, repack on the device.  The returned model starts with the
+ * reference's post-load state: K-WTA ratio 0.5 on the logits, 0.0 in the
+ * blocks (src/io/flat_reader.rs:228-236, src/nn/block/init.rs:42).
+ * NULL on error (gaje_cuda_last_error() says why). */
+gaje_model* gaje_cuda_load(const char* flat_path, const gaje_load_opts* opts);
+void gaje_cuda_free(gaje_model* model);
+
+typedef struct gaje_model_info {
+  uint32_t vocab_size, n_embd, n_head, n_head_kv, n_blocks, head_dim, ffn_dim;
+  uint32_t max_ctx, cache_len;
+  float eps, rope_base, k_wta_ratio;
+  size_t device_bytes; /* weights + KV cache + scratch held on the device */
+} gaje_model_info;
+int gaje_cuda_model_info(gaje_model* model, gaje_model_info* info);
+
+/* GenomicLLM::forward_core (src/nn/llm/forward.rs:7-63): one decode step at
+ * position = cache length.  logits_out (host, vocab_size floats) may be NULL;
+ * argmax_out (host) may be NULL and receives the first index of the maximum
+ * logit (the greedy choice of src/nn/llm/forward.rs:262-271). */
+int gaje_cuda_forward(gaje_model* model, uint32_t token_id, int clear_cache,
+                      float* logits_out, uint32_t* argmax_out);
+
+/* generate_native_core (src/nn/llm/forward.rs:215-330): clears the cache,
+ * prefills the prompt token by token, then greedy (temperature <= 1e-5) or
+ * temperature sampling with repetition penalty, EOS stop and the 3x n-gram
+ * repeat stop.  out holds max_new entries; *n_out receives the count.
+ * Sampling draws from a seeded stream (the reference's thread_rng is not). */
+int gaje_cuda_generate(gaje_model* model, const uint32_t* prompt, size_t n_prompt,
+                       size_t max_new, float temperature, float repetition_penalty,
+                       const uint32_t* eos_ids, size_t n_eos, uint32_t* out,
+                       size_t* n_out);
+
+/* clear_cache_core (src/nn/llm/forward.rs:174-178). */
+int gaje_cuda_clear_cache(gaje_model* model);
+/* set_k_wta_ratio (src/nn/llm/python.rs:53-59): model and every block. */
+int gaje_cuda_set_k_wta_ratio(gaje_model* model, float ratio);
+int gaje_cuda_set_seed(gaje_model* model, uint64_t seed);
+
+/* Greedy decode kept on the device: n_steps forward steps, each fed the
+ * previous step's argmax, the first fed first_token, with no host round trip
+ * between steps (the loop of benchmarks/performance/bench_decode.py:182-192
+ * with the argmax moved to the device).  tokens_out (host, n_steps entries,
+ * nullable) receives the argmax of each step. */
+int gaje_cuda_decode_greedy(gaje_model* model, uint32_t first_token, size_t n_steps,
+                            uint32_t* tokens_out);
+
+/* The model's CUDA stream (a cudaStream_t), for callers that time it. */
+void* gaje_cuda_stream(gaje_model* model);
+
+/* ---------------------------------------------------------------- op level */
+/* Device-pointer entry points for the isolated kernel checks and sweeps.
+ * `stream` is a cudaStream_t (NULL = legacy default stream). */
+
+/* A Q4_0 matrix resident on the device in the engine's layout. */
+typedef struct gaje_q4_matrix gaje_q4_matrix;
+/* Uploads N rows of K/32 20-byte blocks (host memory, file layout) and an
+ * optional bias[N] (host).  Replaces GenomicLinear::new's Q4_0 arm
+ * (src/nn/linear/init.rs:29-35). */
+gaje_q4_matrix* gaje_cuda_q4_0_upload(const uint8_t* blocks, size_t N, size_t K,
+                                      const float* bias, int device);
+void gaje_cuda_q4_0_release(gaje_q4_matrix* m);
+/* y[m][n] = row_dot(n, x[m]) with the reference's |y|<1e-6 -> 0 flush and
+ * +bias, for M input vectors x[M][K] (device) -> y[M][N] (device).
+ * compute_single_row's Q4_0 arm (src/nn/linear/forward.rs:84-92, 113-115). */
+int gaje_cuda_q4_0_gemv(const gaje_q4_matrix* m, const float* x, float* y, size_t M,
+                        void* stream);
+/* Dequantised weights w[N][K] (device) with the AVX2 kernel's fused
+ * fma(q, scale, min) (src/compute/kernels/genomic.rs:298). */
+int gaje_cuda_q4_0_dequant(const gaje_q4_matrix* m, float* w, void* stream);
+
+/* logits[n] = dot(x, W[n]) for an f32 W[N][K] (device), then the first index of
+ * the maximum into *argmax (device u32).  logits may be NULL.
+ * compute_single_row's F32 arm (src/nn/linear/forward.rs:20-32). */
+int gaje_cuda_f32_gemv_argmax(const float* W, const float* x, size_t N, size_t K,
+                              float* logits, uint32_t* argmax, void* stream);
+
+/* rms_norm (src/compute/kernels/norm.rs:17-87): out = x * (1/sqrt(ss/n+eps)) * w. */
+int gaje_cuda_rms_norm(const float* x, const float* w, float eps, size_t n, float* out,
+                       void* stream);
+
+/* Decode attention for one new position (src/nn/attention.rs:88-127): q[n_head*hd]
+ * against ctx cached positions; k/v caches are [n_head_kv][cache_stride][hd]
+ * (device).  out[n_head*hd]. */
+int gaje_cuda_attention_decode(const float* q, const float* k_cache, const float* v_cache,
+                               size_t ctx, size_t cache_stride, size_t n_head,
+                               size_t n_head_kv, size_t head_dim, float* out,
+                               void* stream);
+
+/* lateral_inhibition_kwta (src/compute/kernels/lut.rs:45-61) in place on
+ * scores[n] (device): values below the k-th largest become -1e9. */
+int gaje_cuda_kwta(float* scores, size_t n, size_t k, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GAJE_CUDA_H */
