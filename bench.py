@@ -1,0 +1,369 @@
+"""Decode benchmark for the B200 `.gaje.flat` engine.
+
+Workload (N=1): the Qwen2-0.5B-shaped model of BASELINE.json configs[1] --
+random-init weights N(0, 0.02) written as `.gaje.flat` v2 by the synthetic
+writer (Q4_0 body, tied FP32 embedding / lm_head), batch 1, a 256-token
+uniform-random prompt, then greedy decode.  One "step" is one decode step
+(one token).  K-WTA is off, as benchmarks/performance/bench_decode.py:158-159
+sets it.
+
+  value      decode tok/s with the model resident in HBM: K steps of the
+             device-resident greedy loop (gaje_cuda_decode_greedy), timed
+             with CUDA events on the model's stream, max over ranks.
+  e2e        the same K steps through gaje_cuda_forward (the reference-facing
+             call: host token in, host argmax out, a host sync every step).
+  roofline   the lm_head GEMV (70 % of the step's bytes), from per-kernel CUDA
+             events around each launch (gaje_cuda_profile_steps).
+  cpu_baseline  the CPU oracle (the reference's AVX2 decode path restated in
+             C++, all host threads) on a bounded sample of the same workload.
+
+Multi-GPU (torchrun): batch-1 decode does not shard ("replicas only"): every
+rank decodes its own stream on its own GPU; value = all ranks' tokens / the
+slowest rank's time.
+
+--impl reference runs the reference's CPU decode path (the C++ restatement
+under oracle/, as the Rust crate cannot be built here) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+CONFIG_KEY = "qwen2-0.5b"
+PROMPT_LEN = 256
+SEED = 1234
+
+
+def _pkg():
+    return importlib.import_module("gaje-semantic-compression_b200")
+
+
+def _model_path(cfg_key: str, seed: int) -> str:
+    base = "/dev/shm" if os.path.isdir("/dev/shm") and os.access("/dev/shm", os.W_OK) else "/tmp"
+    return os.path.join(base, f"gaje_bench_{cfg_key}_{seed}.flat")
+
+
+def _ensure_model(g, cfg_key: str, seed: int, rank: int, dist) -> str:
+    path = _model_path(cfg_key, seed)
+    if rank == 0 and not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        g.write_synthetic(tmp, seed=seed, **g.configs.CONFIGS[cfg_key])
+        os.replace(tmp, path)
+    if dist is not None:
+        dist.barrier()
+    return path
+
+
+def _prompt(vocab: int, n: int, seed: int):
+    import numpy as np
+
+    return [int(t) for t in np.random.default_rng(seed).integers(0, vocab, n)]
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([c.strip() for c in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in self.samples for i in range(4)
+                          if len(s) > 5 + i and s[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+def _peaks() -> dict:
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def _ncu_traffic(kernel: str, cfg_key: str):
+    """Per-launch DRAM bytes of a kernel from the committed ncu summary, if any."""
+    p = os.path.join(REPO, "profiles", "ncu_traffic.json")
+    if not os.path.exists(p):
+        return None
+    try:
+        return json.load(open(p)).get(f"{kernel}@{cfg_key}")
+    except Exception:
+        return None
+
+
+def cpu_oracle_decode(path: str, prompt, budget_s: float, max_tokens: int, threads: int = 0):
+    """The CPU oracle decoding greedily after the prompt: (tok/s, tokens, cores)."""
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    import numpy as np
+    import oracle
+
+    oracle.build()
+    if threads:
+        oracle.set_threads(threads)
+    cores = oracle.max_threads()
+    m = oracle.OracleModel(path)
+    m.set_k_wta_ratio(0.0)
+    logits = None
+    for i, t in enumerate(prompt):
+        logits = m.forward(t, i == 0)
+    tok = int(np.argmax(logits))
+    n, t0 = 0, time.perf_counter()
+    while n < max_tokens and (time.perf_counter() - t0) < budget_s:
+        logits = m.forward(tok)
+        tok = int(np.argmax(logits))
+        n += 1
+    dt = time.perf_counter() - t0
+    return n / dt, n, cores
+
+
+def run_reference(args, rank: int) -> None:
+    """The reference arm: the reference's CPU decode path on the host cores."""
+    if rank != 0:
+        return
+    g = _pkg()
+    path = _ensure_model(g, args.config, SEED, 0, None)
+    cfg = g.configs.CONFIGS[args.config]
+    prompt = _prompt(cfg["vocab_size"], PROMPT_LEN, SEED)
+    budget = max(5.0, min(120.0, 0.05 * (args.steps + args.warmup) + 20.0))
+    tps, n, cores = cpu_oracle_decode(path, prompt, budget_s=budget, max_tokens=args.steps)
+    line = {
+        "impl": "reference",
+        "metric": "decode tok/s (batch 1)",
+        "value": round(tps, 3),
+        "unit": "tok/s",
+        "n_gpus": args.gpus,
+        "steps": n,
+        "warmup": args.warmup,
+        "ms_per_step": round(1000.0 / tps, 3),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: seeded random-init weights, uniform random prompt ids",
+        "config": {"workload": f"{args.config} batch-1 greedy decode after a {PROMPT_LEN}-token prompt",
+                   "global_batch": 1, "prompt_len": PROMPT_LEN},
+        "cpu_baseline": {"value": round(tps, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} greedy decode steps after a {PROMPT_LEN}-token prompt "
+                                   f"(time-bounded to {budget:.0f} s)"},
+        "e2e": {"value": round(tps, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank: int, world: int, local_rank: int, dist) -> None:
+    import numpy as np
+    import torch
+
+    g = _pkg()
+    torch.cuda.set_device(local_rank)
+    cfg_key = args.config
+    cfg = g.configs.CONFIGS[cfg_key]
+    path = _ensure_model(g, cfg_key, SEED, rank, dist)
+    K, W = args.steps, args.warmup
+    max_ctx = PROMPT_LEN + max(K, W) + 64
+    model = g.load_genomic_auto(path, device=local_rank, max_ctx=max_ctx)
+    model.set_k_wta_ratio(0.0)
+    prompt = _prompt(model.vocab_size, PROMPT_LEN, SEED + rank)
+    stream = torch.cuda.ExternalStream(model.stream, device=local_rank)
+
+    def prefill():
+        model.clear_cache_py()
+        last = 0
+        for i, t in enumerate(prompt):
+            last = model.forward_argmax(t, i == 0)
+        return last
+
+    # warm-up: graph capture, caches, clocks
+    first = prefill()
+    model.decode_greedy(first, W)
+    first = prefill()
+    torch.cuda.synchronize()
+
+    # ---- value: device-resident loop, CUDA events on the model stream
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        torch.cuda.nvtx.range_push("timed_decode")
+        e0.record(stream)
+        toks = model.decode_greedy(first, K)
+        e1.record(stream)
+        e1.synchronize()
+        torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    ms = e0.elapsed_time(e1)
+    ms_max = ms
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local_rank}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_max = float(t.item())
+    value = world * K / (ms_max / 1000.0)
+
+    # ---- e2e: the reference-facing call, one host round trip per step
+    first2 = prefill()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    t0 = time.perf_counter()
+    tok = first2
+    e2e_toks = []
+    for _ in range(K):
+        tok = model.forward_argmax(tok)
+        e2e_toks.append(tok)
+    e2e_s = time.perf_counter() - t0
+    if dist is not None:
+        t = torch.tensor([e2e_s], dtype=torch.float64, device=f"cuda:{local_rank}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = world * K / e2e_s
+    same_stream = e2e_toks == toks
+
+    # ---- per-kernel profile for the roofline (separate pass, events per launch)
+    prof_steps = min(K, 64)
+    first3 = prefill()
+    prof = model.profile_steps(first3, prof_steps)
+    ctx_mean = PROMPT_LEN + prof_steps / 2.0
+    sb = g.configs.step_bytes(cfg, int(ctx_mean))
+    peaks = _peaks()
+    lm_ms = prof["lmhead"][0]
+    d, V = cfg["n_embd"], cfg["vocab_size"]
+    lm_bytes = V * d * 4 + V * 4 + 2 * d * 4  # weights + logits written + x and norm
+    lm_gbs = lm_bytes / (lm_ms / 1000.0) / 1e9
+    step_ms_dev = ms / K
+    step_gbs = g.configs.step_bytes(cfg, PROMPT_LEN + K // 2)["total"] / (step_ms_dev / 1000.0) / 1e9
+    launches_per_step = sum(n for _, n in prof.values())
+
+    if rank != 0:
+        return
+    # ---- CPU baseline (rank 0, N=1 only): bounded oracle sample of the same workload
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        tps, n, cores = cpu_oracle_decode(path, prompt, budget_s=12.0, max_tokens=K)
+        cpu = {"value": round(tps, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+               "sample": f"{n} greedy decode steps after the same {PROMPT_LEN}-token prompt, "
+                         f"oracle/ AVX2 restatement, {cores} OpenMP threads, 12 s budget"}
+    line = {
+        "metric": "decode tok/s (batch 1)",
+        "value": round(value, 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": W,
+        "ms_per_step": round(ms_max / K, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: seeded random-init N(0,0.02) weights quantised by the Q4_0 exporter "
+                "restatement, uniform random prompt ids",
+        "config": {"workload": f"{cfg_key} batch-1 greedy decode after a {PROMPT_LEN}-token prompt",
+                   "global_batch": world, "prompt_len": PROMPT_LEN, "decode_steps": K,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2 (778 MB of weights streamed per step vs 126 MB L2)"},
+        "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4, "d2h_bytes_per_step": 32,
+                "path": "gaje_cuda_forward (host token in, host argmax out)",
+                "same_tokens_as_device_loop": same_stream},
+        "roofline": {"bound": "hbm", "kernel": "k_lmhead (final RMSNorm + f32 lm_head GEMV + argmax)",
+                     "achieved": round(lm_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(lm_gbs / peaks["hbm_gbs"], 4),
+                     "traffic": _ncu_traffic("k_lmhead", cfg_key),
+                     "algorithmic_bytes": lm_bytes, "ms_per_launch": round(lm_ms, 4),
+                     "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs)"},
+        "step_roofline": {"algorithmic_bytes": sb["total"], "achieved_gbs": round(step_gbs, 1),
+                          "frac": round(step_gbs / peaks["hbm_gbs"], 4),
+                          "note": "whole decode step, bytes of configs.step_bytes at the mean context"},
+        "kernel_ms_per_step": {k: round(v[0], 4) for k, v in prof.items()},
+        "gpu_launches": int(launches_per_step * K),
+        "clocks": clk.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default=CONFIG_KEY)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank)
+        return
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as tdist
+
+        torch.cuda.set_device(local_rank)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                 device_id=torch.device(f"cuda:{local_rank}"))
+        dist = tdist
+    try:
+        run_ours(args, rank, world, local_rank, dist)
+    finally:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -13,6 +13,7 @@ from .runtime import (  # noqa: F401
     GenomicLLM,
     Q4Matrix,
     attention_decode,
+    decode_header,
     f32_gemv_argmax,
     inspect_flat,
     kwta,

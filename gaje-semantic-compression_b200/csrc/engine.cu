@@ -221,19 +221,55 @@ struct gaje_model {
   }
 
   // The step's kernel sequence on `stream` (captured once into the graph).
-  int launch_step(int kk, int bk) {
+  // With `prof`, every launch is bracketed by events and its time added to
+  // prof_ms[class] (profiling only; never captured).
+  int launch_step(int kk, int bk, float* prof_ms = nullptr, uint32_t* prof_n = nullptr) {
     const int nw = kGemvThreads / kWarp;
-    for (int l = 0; l < L; ++l) {
-      LayerW w = layer(l);
-      k_qkv<<<(w.qkv.N / 2 + nw - 1) / nw, kGemvThreads, d * sizeof(float), stream>>>(P, w, l);
-      k_attn<<<dim3(nkv, kAttnMaxSplits), kAttnThreads, attn_smem, stream>>>(P, w);
-      k_oproj<<<(d + nw - 1) / nw, kGemvThreads, w.wo.K * sizeof(float), stream>>>(P, w);
-      k_gateup<<<(ff + nw - 1) / nw, kGemvThreads, d * sizeof(float), stream>>>(P, w, l);
-      k_down<<<(d + nw - 1) / nw, kGemvThreads, ff * sizeof(float), stream>>>(P, w, l);
-      if (bk > 0) k_kwta<<<1, kKwtaThreads, 0, stream>>>(x, d, bk);
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (prof_ms) {
+      CK(cudaEventCreate(&e0));
+      CK(cudaEventCreate(&e1));
     }
-    k_lmhead<<<lm_grid, kLmThreads, d * sizeof(float), stream>>>(P);
-    if (kk > 0) k_kwta<<<1, kKwtaThreads, 0, stream>>>(logits, V, kk);
+    auto timed = [&](int cls, auto&& launch) -> int {
+      if (!prof_ms) {
+        launch();
+        return GAJE_OK;
+      }
+      CK(cudaEventRecord(e0, stream));
+      launch();
+      CK(cudaEventRecord(e1, stream));
+      CK(cudaEventSynchronize(e1));
+      float ms = 0.f;
+      CK(cudaEventElapsedTime(&ms, e0, e1));
+      prof_ms[cls] += ms;
+      if (prof_n) prof_n[cls] += 1;
+      return GAJE_OK;
+    };
+    int s = GAJE_OK;
+    for (int l = 0; l < L && !s; ++l) {
+      LayerW w = layer(l);
+      s |= timed(GAJE_K_QKV, [&] {
+        k_qkv<<<(w.qkv.N / 2 + nw - 1) / nw, kGemvThreads, d * sizeof(float), stream>>>(P, w, l);
+      });
+      s |= timed(GAJE_K_ATTN, [&] {
+        k_attn<<<dim3(nkv, kAttnMaxSplits), kAttnThreads, attn_smem, stream>>>(P, w);
+      });
+      s |= timed(GAJE_K_OPROJ, [&] {
+        k_oproj<<<(d + nw - 1) / nw, kGemvThreads, w.wo.K * sizeof(float), stream>>>(P, w);
+      });
+      s |= timed(GAJE_K_GATEUP, [&] {
+        k_gateup<<<(ff + nw - 1) / nw, kGemvThreads, d * sizeof(float), stream>>>(P, w, l);
+      });
+      s |= timed(GAJE_K_DOWN, [&] {
+        k_down<<<(d + nw - 1) / nw, kGemvThreads, ff * sizeof(float), stream>>>(P, w, l);
+      });
+      if (bk > 0) s |= timed(GAJE_K_KWTA, [&] { k_kwta<<<1, kKwtaThreads, 0, stream>>>(x, d, bk); });
+    }
+    if (!s) s |= timed(GAJE_K_LMHEAD, [&] { k_lmhead<<<lm_grid, kLmThreads, d * sizeof(float), stream>>>(P); });
+    if (!s && kk > 0) s |= timed(GAJE_K_KWTA, [&] { k_kwta<<<1, kKwtaThreads, 0, stream>>>(logits, V, kk); });
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (s) return s;
     CK(cudaGetLastError());
     return GAJE_OK;
   }
@@ -611,6 +647,30 @@ int gaje_cuda_decode_greedy(gaje_model* m, uint32_t first_token, size_t n_steps,
     CK(cudaMemcpyAsync(tokens_out, m->tok_hist, n_steps * 4, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
   m->host_pos += uint32_t(n_steps);
+  return m->check_nan();
+}
+
+int gaje_cuda_profile_steps(gaje_model* m, uint32_t first_token, size_t n_steps, float* ms,
+                            uint32_t* launches) {
+  if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  CK(cudaSetDevice(m->device));
+  if (size_t(m->host_pos) + n_steps > size_t(m->max_ctx))
+    return set_error(GAJE_ERR_CONTEXT, "KV cache would overflow (max_ctx positions)");
+  float acc[GAJE_K_COUNT] = {0};
+  uint32_t cnt[GAJE_K_COUNT] = {0};
+  m->h_st->token = first_token;
+  m->h_st->hist_len = 0;
+  CK(cudaMemcpyAsync(&m->st->token, &m->h_st->token, 4, cudaMemcpyHostToDevice, m->stream));
+  CK(cudaMemcpyAsync(&m->st->hist_len, &m->h_st->hist_len, 4, cudaMemcpyHostToDevice, m->stream));
+  for (size_t i = 0; i < n_steps; ++i)
+    if (int s = m->launch_step(m->logits_k(), m->block_k(), acc, cnt)) return s;
+  CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  m->host_pos += uint32_t(n_steps);
+  for (int c = 0; c < GAJE_K_COUNT; ++c) {
+    if (ms) ms[c] = n_steps ? acc[c] / float(n_steps) : 0.f;
+    if (launches) launches[c] = n_steps ? uint32_t(cnt[c] / n_steps) : 0u;
+  }
   return m->check_nan();
 }
 

@@ -339,6 +339,36 @@ const uint8_t* FlatFile::blob(uint64_t off, uint64_t len) const {
   return data_ + s;
 }
 
+int decode_header(const uint8_t* p, size_t len, gaje_flat_header& h, std::string& err) {
+  if (len < 4096) {
+    err = "header buffer is shorter than 4096 bytes";
+    return GAJE_ERR_IO;
+  }
+  if (memcmp(p, "GAJE", 4) != 0) {
+    err = "invalid magic (expected \"GAJE\")";
+    return GAJE_ERR_IO;
+  }
+  // Little-endian packed layout "<4sIIIQQQQIIIIIIII" (export_gaje_flat.py:450-471).
+  auto u32 = [&](size_t o) { uint32_t v; memcpy(&v, p + o, 4); return v; };
+  auto u64 = [&](size_t o) { uint64_t v; memcpy(&v, p + o, 8); return v; };
+  h.version = u32(4);
+  h.flags = u32(8);
+  h.num_tensors = u32(12);
+  h.meta_len = u64(16);
+  h.dir_len = u64(24);
+  h.weights_offset = u64(32);
+  h.weights_len = u64(40);
+  h.group_size = u32(48);
+  h.quant_format = u32(52);
+  h.arch_family = u32(56);
+  h.arch_n_embd = u32(60);
+  h.arch_n_head = u32(64);
+  h.arch_n_head_kv = u32(68);
+  h.arch_n_blocks = u32(72);
+  h.arch_qk_permute = u32(76);
+  return GAJE_OK;
+}
+
 int FlatFile::open(const char* path, std::string& err) {
   if (!path) { err = "path is NULL"; return GAJE_ERR_INVALID; }
   int fd = ::open(path, O_RDONLY);
@@ -359,25 +389,7 @@ int FlatFile::open(const char* path, std::string& err) {
   if (m == MAP_FAILED) { err = "mmap failed"; return GAJE_ERR_IO; }
   data_ = static_cast<const uint8_t*>(m);
   madvise(m, size_, MADV_SEQUENTIAL);
-  if (memcmp(data_, "GAJE", 4) != 0) { err = "invalid magic (expected \"GAJE\")"; return GAJE_ERR_IO; }
-  // Little-endian packed layout "<4sIIIQQQQIIIIIIII" (export_gaje_flat.py:450-471).
-  auto u32 = [&](size_t o) { uint32_t v; memcpy(&v, data_ + o, 4); return v; };
-  auto u64 = [&](size_t o) { uint64_t v; memcpy(&v, data_ + o, 8); return v; };
-  hdr.version = u32(4);
-  hdr.flags = u32(8);
-  hdr.num_tensors = u32(12);
-  hdr.meta_len = u64(16);
-  hdr.dir_len = u64(24);
-  hdr.weights_offset = u64(32);
-  hdr.weights_len = u64(40);
-  hdr.group_size = u32(48);
-  hdr.quant_format = u32(52);
-  hdr.arch_family = u32(56);
-  hdr.arch_n_embd = u32(60);
-  hdr.arch_n_head = u32(64);
-  hdr.arch_n_head_kv = u32(68);
-  hdr.arch_n_blocks = u32(72);
-  hdr.arch_qk_permute = u32(76);
+  if (int s = decode_header(data_, size_, hdr, err)) return s;
   info.header = hdr;
   if (hdr.meta_len > size_ || hdr.dir_len > size_ || 4096 + hdr.meta_len + hdr.dir_len > size_) {
     err = "metadata/directory extend past the end of the file";
@@ -698,6 +710,14 @@ int gaje_quantize_q8_0(const float* w, size_t n, uint8_t* out) {
   const long long nb = (long long)(n / 32);
 #pragma omp parallel for schedule(static)
   for (long long i = 0; i < nb; ++i) q8_block(w + i * 32, out + i * 34);
+  return GAJE_OK;
+}
+
+int gaje_flat_header_decode(const uint8_t* bytes, size_t len, gaje_flat_header* out) {
+  if (!bytes || !out) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  std::string err;
+  if (int s = decode_header(bytes, len, *out, err)) return set_error(s, err);
+  clear_error();
   return GAJE_OK;
 }
 

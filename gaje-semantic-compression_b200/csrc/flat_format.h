@@ -64,6 +64,9 @@ class FlatFile {
   size_t size_ = 0;
 };
 
+// FlatHeaderV2::from_bytes: decode the fixed fields, validate the magic.
+int decode_header(const uint8_t* p, size_t len, gaje_flat_header& h, std::string& err);
+
 // f16 <-> f32 (round to nearest even), the conversions of the `half` crate.
 uint16_t f32_to_f16(float f);
 float f16_to_f32(uint16_t h);

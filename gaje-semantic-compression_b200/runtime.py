@@ -113,6 +113,7 @@ def lib() -> C.CDLL:
     vp, sz, u32, u64, i32, f32 = C.c_void_p, C.c_size_t, C.c_uint32, C.c_uint64, C.c_int, C.c_float
     sig = {
         "gaje_cuda_last_error": ([], C.c_char_p),
+        "gaje_flat_header_decode": ([C.c_char_p, sz, C.POINTER(FlatHeader)], i32),
         "gaje_flat_inspect": ([C.c_char_p, C.POINTER(FlatInfo)], i32),
         "gaje_quantize_q4_0": ([vp, sz, vp], i32),
         "gaje_quantize_q8_0": ([vp, sz, vp], i32),
@@ -132,6 +133,7 @@ def lib() -> C.CDLL:
         "gaje_cuda_set_seed": ([vp, u64], i32),
         "gaje_cuda_decode_greedy": ([vp, u32, sz, vp], i32),
         "gaje_cuda_stream": ([vp], vp),
+        "gaje_cuda_profile_steps": ([vp, u32, sz, vp, vp], i32),
         "gaje_cuda_q4_0_upload": ([vp, sz, sz, vp, i32], vp),
         "gaje_cuda_q4_0_release": ([vp], None),
         "gaje_cuda_q4_0_gemv": ([vp, vp, vp, sz, vp], i32),
@@ -163,6 +165,20 @@ def _ptr(a: np.ndarray) -> int:
 
 
 # ------------------------------------------------------------------ format
+QUANT_FORMATS = {0: "LegacyCentroids", 1: "Q4_0", 2: "Q8_0"}
+
+
+def decode_header(buf: bytes) -> dict:
+    """FlatHeaderV2::from_bytes on a byte buffer, plus quantization_type() and
+    effective_group_size() (src/io/header/flat.rs:47-79)."""
+    h = FlatHeader()
+    _check(lib().gaje_flat_header_decode(buf, len(buf), C.byref(h)), GajeIOError)
+    out = {f: getattr(h, f) for f, _ in FlatHeader._fields_}
+    out["quantization_type"] = QUANT_FORMATS.get(h.quant_format, "Unknown")
+    out["effective_group_size"] = 16 if h.group_size == 0 else h.group_size
+    return out
+
+
 def inspect_flat(path: str) -> dict:
     """Parse-only open of a `.gaje.flat` file (header, config, directory)."""
     info = FlatInfo()
@@ -319,6 +335,16 @@ class GenomicLLM:
         out = np.zeros(max(1, n_steps), dtype=np.uint32)
         _check(lib().gaje_cuda_decode_greedy(self._m, int(first_token), int(n_steps), _ptr(out)))
         return [int(t) for t in out[:n_steps]]
+
+    KERNEL_CLASSES = ("qkv", "attn", "oproj", "gateup", "down", "lmhead", "kwta")
+
+    def profile_steps(self, first_token: int, n_steps: int) -> dict:
+        """Greedy steps with every kernel bracketed by CUDA events: mean ms per
+        step and launches per step for each kernel class."""
+        ms = np.zeros(len(self.KERNEL_CLASSES), dtype=np.float32)
+        n = np.zeros(len(self.KERNEL_CLASSES), dtype=np.uint32)
+        _check(lib().gaje_cuda_profile_steps(self._m, int(first_token), int(n_steps), _ptr(ms), _ptr(n)))
+        return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(self.KERNEL_CLASSES)}
 
     def generate_native_py(self, prompt_tokens: Sequence[int], max_new_tokens: int = 30,
                            temperature: float = 0.7, repetition_penalty: float = 1.0,

@@ -68,6 +68,12 @@ typedef struct gaje_flat_info {
   uint32_t n_entries;   /* tensors in the directory                         */
 } gaje_flat_info;
 
+/* Decodes the 4096-byte FlatHeaderV2 from memory (FlatHeaderV2::from_bytes,
+ * src/io/header/flat.rs:47-60: only the magic is validated).  quant_format
+ * 0/1/2 = LegacyCentroids/Q4_0/Q8_0 (flat.rs:62-70); a group_size of 0 means
+ * the legacy 16 (flat.rs:73-79).  GAJE_ERR_IO on a short buffer or bad magic. */
+int gaje_flat_header_decode(const uint8_t* bytes, size_t len, gaje_flat_header* out);
+
 /* Parse-only open: header, metadata and directory, every tensor the loader
  * needs, offsets against the file size.  No device is touched.
  * Replaces GajeFlatFileReader::open + the validation part of load_genomic
@@ -180,6 +186,20 @@ int gaje_cuda_decode_greedy(gaje_model* model, uint32_t first_token, size_t n_st
 
 /* The model's CUDA stream (a cudaStream_t), for callers that time it. */
 void* gaje_cuda_stream(gaje_model* model);
+
+/* Kernel classes of one decode step, for gaje_cuda_profile_steps. */
+enum gaje_kernel_class {
+  GAJE_K_QKV = 0, GAJE_K_ATTN = 1, GAJE_K_OPROJ = 2, GAJE_K_GATEUP = 3, GAJE_K_DOWN = 4,
+  GAJE_K_LMHEAD = 5, GAJE_K_KWTA = 6, GAJE_K_COUNT = 7
+};
+/* Runs n_steps greedy steps like gaje_cuda_decode_greedy but launches each
+ * kernel on its own, bracketed by CUDA events on the model stream, and writes
+ * the mean milliseconds per step spent in each kernel class into
+ * ms[GAJE_K_COUNT] and the launches per step into launches[GAJE_K_COUNT]
+ * (either may be NULL).  The reference's counterpart is the
+ * GAJE_PROFILE_VERBOSE timing of src/nn/llm/forward.rs:23-55. */
+int gaje_cuda_profile_steps(gaje_model* model, uint32_t first_token, size_t n_steps,
+                            float* ms, uint32_t* launches);
 
 /* ---------------------------------------------------------------- op level */
 /* Device-pointer entry points for the isolated kernel checks and sweeps.

@@ -1,0 +1,96 @@
+"""Independent numpy/struct restatement of the `.gaje.flat` v2 packing of
+scripts/export_gaje_flat.py:184-483 (metadata dict, directory list, 64-byte
+aligned blobs, 4 KiB aligned weights, "<4sIIIQQQQIIIIIIII" header), used to
+check the product writer byte for byte.  Quantisation goes through the CPU
+oracle's restatement of quantize_q4_0_native / quantize_q8_0_native.
+"""
+from __future__ import annotations
+
+import json
+import struct
+
+import numpy as np
+
+import oracle
+
+
+def write_flat(path, *, name, arch_family, n_embd, n_head, n_head_kv, n_blocks, vocab_size, eps,
+               rope_base, qk_permute, tensors, config_extra=None):
+    """tensors: list of ("linear", name, bit_depth, W[out][in], bias|None) or
+    ("norm", name, v) in file order.  config_extra updates metadata["config"]."""
+    metadata_dict = {
+        "config": {
+            "name": name,
+            "version": "0.9.8",
+            "tokenizer_id": "",
+            "rope_base": float(np.float32(rope_base)),
+            "ffn_act": "swiglu" if arch_family != 5 else "geglu",
+            "use_genomic_norm": False,
+        },
+        "n_embd": n_embd,
+        "n_head": n_head,
+        "n_head_kv": n_head_kv,
+        "n_blocks": n_blocks,
+        "vocab_size": vocab_size,
+        "eps": float(np.float32(eps)),
+        "tokenizer": "",
+    }
+    if config_extra:
+        metadata_dict["config"].update(config_extra)
+    metadata_json_bytes = json.dumps(metadata_dict).encode("utf-8")
+    tensor_directory = []
+    blob_bytes = bytearray()
+
+    def add_blob_data(raw):
+        offset = len(blob_bytes)
+        blob_bytes.extend(raw)
+        padding = (64 - (len(blob_bytes) % 64)) % 64
+        blob_bytes.extend(b"\x00" * padding)
+        return offset, len(raw)
+
+    for t in tensors:
+        if t[0] == "norm":
+            _, nm, v = t
+            off, ln = add_blob_data(np.asarray(v, np.float32).tobytes())
+            tensor_directory.append({"name": nm, "bit_depth": 32, "out_features": n_embd,
+                                     "in_features": 1, "dna_off": off, "dna_len": ln, "c_off": 0,
+                                     "c_len": 0, "anc_off": 0, "anc_len": 0, "bias_off": 0,
+                                     "bias_len": 0})
+            continue
+        _, nm, bits, W, bias = t
+        W = np.ascontiguousarray(W, np.float32)
+        if bits == 4:
+            dna = oracle.quantize_q4_0(W).tobytes()
+        elif bits == 8:
+            dna = oracle.quantize_q8_0(W).tobytes()
+        else:
+            dna = W.tobytes()
+        dna_off, dna_len = add_blob_data(dna)
+        c_off, c_len = add_blob_data(b"")
+        anc_off, anc_len = add_blob_data(b"")
+        bias_off, bias_len = 0, 0
+        if bias is not None and len(bias) > 0:
+            bias_off, bias_len = add_blob_data(np.asarray(bias, np.float32).tobytes())
+        tensor_directory.append({"name": nm, "bit_depth": int(bits), "out_features": int(W.shape[0]),
+                                 "in_features": int(W.shape[1]), "dna_off": int(dna_off),
+                                 "dna_len": int(dna_len), "c_off": int(c_off), "c_len": int(c_len),
+                                 "anc_off": int(anc_off), "anc_len": int(anc_len),
+                                 "bias_off": int(bias_off), "bias_len": int(bias_len)})
+    dir_json_bytes = json.dumps(tensor_directory).encode("utf-8")
+    meta_len, dir_len = len(metadata_json_bytes), len(dir_json_bytes)
+    weights_offset = 4096 + meta_len + dir_len
+    if weights_offset % 4096 != 0:
+        weights_offset = ((weights_offset // 4096) + 1) * 4096
+    header_bin = bytearray(4096)
+    struct.pack_into("<4sIIIQQQQIIIIIIII", header_bin, 0, b"GAJE", 0x000908, 0x0003,
+                     len(tensor_directory), meta_len, dir_len, weights_offset, len(blob_bytes), 32, 1,
+                     arch_family, n_embd, n_head, n_head_kv, n_blocks, 1 if qk_permute else 0)
+    with open(path, "wb") as f:
+        f.write(header_bin)
+        f.write(metadata_json_bytes)
+        f.write(dir_json_bytes)
+        pad = weights_offset - (4096 + meta_len + dir_len)
+        if pad > 0:
+            f.write(b"\x00" * pad)
+        f.write(blob_bytes)
+    return path
