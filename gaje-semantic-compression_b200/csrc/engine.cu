@@ -50,9 +50,56 @@ struct Q4Dev {
   uint4* qs = nullptr;
   uint32_t* sm = nullptr;
   float* bias = nullptr;
-  int N = 0, K = 0, nb = 0;
-  Q4View view() const { return Q4View{qs, sm, bias, N, K, nb}; }
+  int N = 0, K = 0, nb = 0, nbp = 0;
+  Q4View view() const { return Q4View{qs, sm, bias, N, K, nb, nbp}; }
 };
+
+constexpr int kMaxDynSmem = 227 * 1024;
+
+// Launch with cudaLaunchKernelEx; `pdl` lets the kernel start before its
+// predecessor finishes (programmatic stream serialization): the kernel itself
+// calls griddepcontrol.wait before touching its predecessor's outputs.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                     Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+// Work split of one GEMV: units (rows or pairs) per CTA, grid, shared memory.
+struct GemvPlan {
+  int units = 0, upc = 0, grid = 0;
+  size_t smem = 0;
+};
+
+GemvPlan plan_gemv(int mode, const Q4Dev& m, int units, int sms) {
+  GemvPlan p;
+  p.units = units;
+  p.upc = (units + sms - 1) / sms;
+  while (p.upc > 1 && gemv_smem_bytes(mode, m.K, m.nb, m.nbp, p.upc) > size_t(kMaxDynSmem)) p.upc = (p.upc + 1) / 2;
+  p.grid = (units + p.upc - 1) / p.upc;
+  p.smem = gemv_smem_bytes(mode, m.K, m.nb, m.nbp, p.upc);
+  return p;
+}
+
+int smem_optin(const void* kern, size_t bytes) {
+  if (bytes > size_t(kMaxDynSmem))
+    return set_error(GAJE_ERR_UNSUPPORTED, "a kernel needs more than 227 KB of shared memory for this shape");
+  if (bytes > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+    if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  }
+  return GAJE_OK;
+}
 
 // splitmix64 uniforms in [0,1) with 24 bits, as rand's gen::<f32>() builds them.
 struct Rng {
@@ -148,7 +195,7 @@ struct gaje_model {
   int device = 0;
   cudaStream_t stream = nullptr;
   gaje_flat_info info{};
-  int d = 0, nh = 0, nkv = 0, hd = 0, ff = 0, V = 0, L = 0, max_ctx = 0;
+  int d = 0, nh = 0, nkv = 0, hd = 0, ff = 0, V = 0, L = 0, max_ctx = 0, sms = 148;
   // device memory
   Arena arena;
   std::vector<Q4Dev> qkv, wo, gate_up, down;
@@ -174,8 +221,10 @@ struct gaje_model {
   unsigned* h_tok = nullptr;
   // step
   StepParams P{};
-  int lm_grid = 0, attn_chunk_max = 0;
+  GemvPlan pq, po, pg, pd;
   size_t attn_smem = 0;
+  int lm_grid = 0, lm_rows = 0, lm_stage_n = 0;
+  size_t lm_smem = 0;
   float k_wta_ratio = 0.5f;        // flat_reader.rs:234
   float block_k_wta_ratio = 0.0f;  // block/init.rs:42
   bool use_graph = true;
@@ -220,58 +269,123 @@ struct gaje_model {
     return w;
   }
 
+  AttnArgs attn_args(const LayerW& w) const {
+    AttnArgs a;
+    a.q = q;
+    a.kc = w.kc;
+    a.vc = w.vc;
+    a.out = attn;
+    a.part_o = part_o;
+    a.part_ml = part_ml;
+    a.cnt = attn_cnt;
+    a.ctx = 0;
+    a.stride = max_ctx;
+    a.nh = nh;
+    a.nkv = nkv;
+    a.hd = hd;
+    a.scale = P.attn_scale;
+    a.st = st;
+    return a;
+  }
+
+  LmArgs lm_args() const {
+    LmArgs a;
+    a.W = lm_head;
+    a.bias = lm_bias;
+    a.x = x;
+    a.norm_w = out_norm;
+    a.eps = P.eps;
+    a.logits = logits;
+    a.N = V;
+    a.K = d;
+    a.rows_per_cta = lm_rows;
+    a.stages = lm_stage_n;
+    a.part = amax_part;
+    a.cnt = amax_cnt;
+    a.result = &st->argmax;
+    a.st = st;
+    a.tok_hist = tok_hist;
+    a.hist_cap = unsigned(max_ctx);
+    return a;
+  }
+
   // The step's kernel sequence on `stream` (captured once into the graph).
-  // With `prof`, every launch is bracketed by events and its time added to
+  // Every kernel but the step's first and the K-WTA ones is a PDL launch.
+  // With `prof_ms`, every launch is bracketed by events and its time added to
   // prof_ms[class] (profiling only; never captured).
   int launch_step(int kk, int bk, float* prof_ms = nullptr, uint32_t* prof_n = nullptr) {
-    const int nw = kGemvThreads / kWarp;
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (prof_ms) {
       CK(cudaEventCreate(&e0));
       CK(cudaEventCreate(&e1));
     }
-    auto timed = [&](int cls, auto&& launch) -> int {
-      if (!prof_ms) {
-        launch();
-        return GAJE_OK;
+    int status = GAJE_OK;
+    auto run = [&](int cls, cudaError_t (*fn)(gaje_model*, int, bool), int l, bool pdl) {
+      if (status) return;
+      if (prof_ms) cudaEventRecord(e0, stream);
+      cudaError_t e = fn(this, l, pdl && !prof_ms);
+      if (e != cudaSuccess) {
+        status = set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+        return;
       }
-      CK(cudaEventRecord(e0, stream));
-      launch();
-      CK(cudaEventRecord(e1, stream));
-      CK(cudaEventSynchronize(e1));
-      float ms = 0.f;
-      CK(cudaEventElapsedTime(&ms, e0, e1));
-      prof_ms[cls] += ms;
-      if (prof_n) prof_n[cls] += 1;
-      return GAJE_OK;
+      if (prof_ms) {
+        cudaEventRecord(e1, stream);
+        cudaEventSynchronize(e1);
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        prof_ms[cls] += ms;
+        if (prof_n) prof_n[cls] += 1;
+      }
     };
-    int s = GAJE_OK;
-    for (int l = 0; l < L && !s; ++l) {
-      LayerW w = layer(l);
-      s |= timed(GAJE_K_QKV, [&] {
-        k_qkv<<<(w.qkv.N / 2 + nw - 1) / nw, kGemvThreads, d * sizeof(float), stream>>>(P, w, l);
-      });
-      s |= timed(GAJE_K_ATTN, [&] {
-        k_attn<<<dim3(nkv, kAttnMaxSplits), kAttnThreads, attn_smem, stream>>>(P, w);
-      });
-      s |= timed(GAJE_K_OPROJ, [&] {
-        k_oproj<<<(d + nw - 1) / nw, kGemvThreads, w.wo.K * sizeof(float), stream>>>(P, w);
-      });
-      s |= timed(GAJE_K_GATEUP, [&] {
-        k_gateup<<<(ff + nw - 1) / nw, kGemvThreads, d * sizeof(float), stream>>>(P, w, l);
-      });
-      s |= timed(GAJE_K_DOWN, [&] {
-        k_down<<<(d + nw - 1) / nw, kGemvThreads, ff * sizeof(float), stream>>>(P, w, l);
-      });
-      if (bk > 0) s |= timed(GAJE_K_KWTA, [&] { k_kwta<<<1, kKwtaThreads, 0, stream>>>(x, d, bk); });
+    for (int l = 0; l < L; ++l) {
+      run(GAJE_K_QKV, &gaje_model::launch_qkv, l, l != 0);
+      run(GAJE_K_ATTN, &gaje_model::launch_attn, l, true);
+      run(GAJE_K_OPROJ, &gaje_model::launch_oproj, l, true);
+      run(GAJE_K_GATEUP, &gaje_model::launch_gateup, l, true);
+      run(GAJE_K_DOWN, &gaje_model::launch_down, l, true);
+      if (bk > 0) run(GAJE_K_KWTA, &gaje_model::launch_block_kwta, bk, false);
     }
-    if (!s) s |= timed(GAJE_K_LMHEAD, [&] { k_lmhead<<<lm_grid, kLmThreads, d * sizeof(float), stream>>>(P); });
-    if (!s && kk > 0) s |= timed(GAJE_K_KWTA, [&] { k_kwta<<<1, kKwtaThreads, 0, stream>>>(logits, V, kk); });
+    run(GAJE_K_LMHEAD, &gaje_model::launch_lm, 0, true);
+    if (kk > 0) run(GAJE_K_KWTA, &gaje_model::launch_logit_kwta, kk, false);
     if (e0) cudaEventDestroy(e0);
     if (e1) cudaEventDestroy(e1);
-    if (s) return s;
-    CK(cudaGetLastError());
-    return GAJE_OK;
+    return status;
+  }
+
+  static cudaError_t launch_qkv(gaje_model* m, int l, bool pdl) {
+    GemvArgs a{m->qkv[l].view(), m->pq.units, m->pq.upc, nullptr, nullptr, l};
+    return launch_k(k_gemv<G_QKV>, dim3(m->pq.grid), dim3(kGemvThreads), m->pq.smem, m->stream, pdl, m->P,
+                    m->layer(l), a);
+  }
+  static cudaError_t launch_attn(gaje_model* m, int l, bool pdl) {
+    return launch_k(k_attn, dim3(m->nkv, kAttnMaxSplits), dim3(kAttnThreads), m->attn_smem, m->stream, pdl,
+                    m->attn_args(m->layer(l)));
+  }
+  static cudaError_t launch_oproj(gaje_model* m, int l, bool pdl) {
+    GemvArgs a{m->wo[l].view(), m->po.units, m->po.upc, nullptr, nullptr, l};
+    return launch_k(k_gemv<G_OPROJ>, dim3(m->po.grid), dim3(kGemvThreads), m->po.smem, m->stream, pdl, m->P,
+                    m->layer(l), a);
+  }
+  static cudaError_t launch_gateup(gaje_model* m, int l, bool pdl) {
+    GemvArgs a{m->gate_up[l].view(), m->pg.units, m->pg.upc, nullptr, nullptr, l};
+    return launch_k(k_gemv<G_GATEUP>, dim3(m->pg.grid), dim3(kGemvThreads), m->pg.smem, m->stream, pdl, m->P,
+                    m->layer(l), a);
+  }
+  static cudaError_t launch_down(gaje_model* m, int l, bool pdl) {
+    GemvArgs a{m->down[l].view(), m->pd.units, m->pd.upc, nullptr, nullptr, l};
+    return launch_k(k_gemv<G_DOWN>, dim3(m->pd.grid), dim3(kGemvThreads), m->pd.smem, m->stream, pdl, m->P,
+                    m->layer(l), a);
+  }
+  static cudaError_t launch_lm(gaje_model* m, int, bool pdl) {
+    return launch_k(k_lmhead, dim3(m->lm_grid), dim3(kLmThreads), m->lm_smem, m->stream, pdl, m->lm_args());
+  }
+  static cudaError_t launch_block_kwta(gaje_model* m, int k, bool) {
+    k_kwta<<<1, kKwtaThreads, 0, m->stream>>>(m->x, m->d, k);
+    return cudaGetLastError();
+  }
+  static cudaError_t launch_logit_kwta(gaje_model* m, int k, bool) {
+    k_kwta<<<1, kKwtaThreads, 0, m->stream>>>(m->logits, m->V, k);
+    return cudaGetLastError();
   }
 
   int run_step() {
@@ -304,9 +418,18 @@ struct gaje_model {
     return GAJE_OK;
   }
 
-  // Reads the device state after a synchronised step and maps a NaN guard to
-  // the reference's error string.
-  int check_nan() {
+  // Reads the device state after a synchronised step: a timed-out bounded wait
+  // becomes GAJE_ERR_TIMEOUT, a NaN guard the reference's error string.
+  int check_state() {
+    if (h_st->err) {
+      static const char* kid[] = {"qkv", "oproj", "gateup", "down", "gemv", "", "", "", "attention", "lm_head"};
+      const unsigned k = h_st->err - 1;
+      std::string m = std::string("a bounded device wait ran out in the ") + (k < 10 ? kid[k] : "?") + " kernel";
+      h_st->err = 0;
+      cudaMemcpyAsync(&st->err, &h_st->err, 4, cudaMemcpyHostToDevice, stream);
+      cudaStreamSynchronize(stream);
+      return set_error(GAJE_ERR_TIMEOUT, m);
+    }
     if (h_st->nan_code == 0xFFFFFFFFu) return GAJE_OK;
     const unsigned code = h_st->nan_code & 4095u;
     static const char* msgs[] = {"Input x is NaN", "NaN after attn rms_norm", "NaN in up",
@@ -315,8 +438,7 @@ struct gaje_model {
     const unsigned check = code & 7u, layer = code >> 3;
     std::string m = check < 6 ? msgs[check] : "NaN";
     m += " (block " + std::to_string(layer) + ", position " + std::to_string(h_st->nan_code >> 12) + ")";
-    // re-arm the guard word
-    h_st->nan_code = 0xFFFFFFFFu;
+    h_st->nan_code = 0xFFFFFFFFu;  // re-arm the guard word
     cudaMemcpyAsync(&st->nan_code, &h_st->nan_code, 4, cudaMemcpyHostToDevice, stream);
     cudaStreamSynchronize(stream);
     return set_error(GAJE_ERR_NAN, m);
@@ -332,24 +454,33 @@ struct gaje_model {
 
 namespace {
 
-int upload_q4(gaje_model* m, const FlatFile& f, const MatrixRef& ref, Q4Dev& dst, uint32_t* staging) {
-  size_t row0 = 0;
+// Uploads one engine matrix: its file parts are copied back to back into the
+// staging buffer (raw 20-byte blocks, rows in file order), then repacked into
+// qs/sm with the row permutation `mode` (see repack_src_row).  The bias is
+// concatenated (zero where a part has none) and permuted the same way.
+int upload_q4(gaje_model* m, const FlatFile& f, const MatrixRef& ref, Q4Dev& dst, uint32_t* staging, int mode) {
+  size_t off = 0;
   for (const FlatEntry* e : ref.parts) {
-    const size_t nb = e->in / 32, nblk = e->out * nb;
-    const uint8_t* src = f.blob(e->dna_off, e->dna_len);
-    CK(cudaMemcpyAsync(staging, src, e->dna_len, cudaMemcpyHostToDevice, m->stream));
-    const int threads = 256, blocks = int(std::min<size_t>((nblk + threads - 1) / threads, 4096));
-    k_repack_q4<<<blocks, threads, 0, m->stream>>>(staging, nblk, dst.qs + row0 * nb, dst.sm + row0 * nb);
-    CK(cudaGetLastError());
-    if (dst.bias) {
+    CK(cudaMemcpyAsync(reinterpret_cast<char*>(staging) + off, f.blob(e->dna_off, e->dna_len), e->dna_len,
+                       cudaMemcpyHostToDevice, m->stream));
+    off += e->dna_len;
+  }
+  CK(cudaMemsetAsync(dst.sm, 0, size_t(dst.N) * dst.nbp * 4, m->stream));
+  const size_t nblk = size_t(dst.N) * dst.nb;
+  const int blocks = int(std::min<size_t>((nblk + 255) / 256, 8192));
+  k_repack_q4<<<blocks, 256, 0, m->stream>>>(staging, dst.N, dst.nb, dst.nbp, mode, m->hd, dst.N / 2, dst.qs, dst.sm);
+  CK(cudaGetLastError());
+  if (dst.bias) {
+    std::vector<float> cat, perm(dst.N, 0.0f);
+    for (const FlatEntry* e : ref.parts) {
       std::vector<float> b(e->out, 0.0f);
       if (e->bias_len) memcpy(b.data(), f.blob(e->bias_off, e->bias_len), e->bias_len);
-      CK(cudaMemcpyAsync(dst.bias + row0, b.data(), e->out * 4, cudaMemcpyHostToDevice, m->stream));
-      CK(cudaStreamSynchronize(m->stream));  // b is a host temporary
+      cat.insert(cat.end(), b.begin(), b.end());
     }
-    CK(cudaStreamSynchronize(m->stream));  // staging is reused
-    row0 += e->out;
+    for (int r = 0; r < dst.N; ++r) perm[r] = cat[repack_src_row(mode, r, m->hd, dst.N / 2)];
+    CK(cudaMemcpyAsync(dst.bias, perm.data(), size_t(dst.N) * 4, cudaMemcpyHostToDevice, m->stream));
   }
+  CK(cudaStreamSynchronize(m->stream));  // staging and host temporaries are reused
   return GAJE_OK;
 }
 
@@ -379,8 +510,7 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   const gaje_flat_info& I = f.info;
   if (I.embd_bit_depth != 32 || I.lm_head_bit_depth != 32)
     return set_error(GAJE_ERR_UNSUPPORTED, "Q8_0 token_embd/lm_head are not implemented on the device yet");
-  if (I.n_embd % 32 != 0)
-    return set_error(GAJE_ERR_UNSUPPORTED, "n_embd must be a multiple of 32");
+  if (I.n_embd % 32 != 0) return set_error(GAJE_ERR_UNSUPPORTED, "n_embd must be a multiple of 32");
   m->info = I;
   m->d = int(I.n_embd);
   m->nh = int(I.n_head);
@@ -392,22 +522,12 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   m->max_ctx = int(opts && opts->max_ctx ? opts->max_ctx : 4096);
   m->use_graph = !opts || opts->use_graph;
   m->rng.s = opts ? opts->seed : 0;
-  if (m->nh / m->nkv > kAttnMaxGroup)
-    return set_error(GAJE_ERR_UNSUPPORTED, "more than 16 query heads per KV head");
+  if (m->nh / m->nkv > kAttnMaxGroup) return set_error(GAJE_ERR_UNSUPPORTED, "more than 16 query heads per KV head");
+  if (m->hd % 4 != 0) return set_error(GAJE_ERR_UNSUPPORTED, "head_dim must be a multiple of 4");
   if (m->max_ctx > (1 << 20)) return set_error(GAJE_ERR_INVALID, "max_ctx above 2^20");
   CK(cudaSetDevice(m->device));
   CK(cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking));
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, m->device);
-  m->lm_grid = sms * 4;
-  {
-    // chunk(ctx) <= kAttnMinChunk while ctx <= kAttnMinChunk*kAttnMaxSplits,
-    // then ceil(ctx/kAttnMaxSplits): bound it over every ctx <= max_ctx
-    const int chunk = std::max(kAttnMinChunk, (m->max_ctx + kAttnMaxSplits - 1) / kAttnMaxSplits);
-    m->attn_chunk_max = chunk;
-    const int G = m->nh / m->nkv;
-    m->attn_smem = size_t(G) * (m->hd + chunk) * sizeof(float);
-  }
+  cudaDeviceGetAttribute(&m->sms, cudaDevAttrMultiProcessorCount, m->device);
   // ---- plan the arena (sizes only), then allocate and carve for real
   const size_t V = m->V, d = m->d, L = m->L;
   size_t staging_bytes = 0;
@@ -427,10 +547,13 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
         q.N = int(refs[k]->out);
         q.K = int(refs[k]->in);
         q.nb = q.K / 32;
+        q.nbp = (q.nb + 3) / 4 * 4;
         q.qs = a.take<uint4>(size_t(q.N) * q.nb);
-        q.sm = a.take<uint32_t>(size_t(q.N) * q.nb);
+        q.sm = a.take<uint32_t>(size_t(q.N) * q.nbp);
         q.bias = refs[k]->has_bias ? a.take<float>(q.N) : nullptr;
-        for (const FlatEntry* e : refs[k]->parts) staging_bytes = std::max<size_t>(staging_bytes, e->dna_len);
+        size_t tot = 0;
+        for (const FlatEntry* e : refs[k]->parts) tot += e->dna_len;
+        staging_bytes = std::max(staging_bytes, tot);
       }
       m->attn_norm[l] = a.take<float>(d);
       m->ffn_norm[l] = a.take<float>(d);
@@ -451,7 +574,7 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     m->part_o = a.take<float>(size_t(m->nkv) * kAttnMaxSplits * (m->nh / m->nkv) * m->hd);
     m->part_ml = a.take<float>(size_t(m->nkv) * kAttnMaxSplits * (m->nh / m->nkv) * 2);
     m->attn_cnt = a.take<unsigned>(m->nkv);
-    m->amax_part = a.take<unsigned long long>(m->lm_grid);
+    m->amax_part = a.take<unsigned long long>(m->sms);
     m->amax_cnt = a.take<unsigned>(1);
     m->tok_hist = a.take<unsigned>(m->max_ctx);
     m->sel_out = a.take<unsigned>(1);
@@ -466,18 +589,36 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   m->arena.size = total;
   plan(m->arena);
   uint32_t* staging = m->arena.take<uint32_t>(staging_words);
-  // zero the counters, scratch and state
+  // ---- launch plans
+  m->pq = plan_gemv(G_QKV, m->qkv[0], m->qkv[0].N / 2, m->sms);
+  m->po = plan_gemv(G_OPROJ, m->wo[0], m->wo[0].N, m->sms);
+  m->pg = plan_gemv(G_GATEUP, m->gate_up[0], m->gate_up[0].N / 2, m->sms);
+  m->pd = plan_gemv(G_DOWN, m->down[0], m->down[0].N, m->sms);
+  m->attn_smem = attn_smem_bytes(m->nh / m->nkv, m->hd, attn_chunk_max(m->max_ctx));
+  m->lm_grid = m->sms;
+  m->lm_rows = (m->V + m->lm_grid - 1) / m->lm_grid;
+  m->lm_stage_n = lm_stages(m->d);
+  m->lm_smem = lm_smem_bytes(m->d, m->lm_stage_n);
+  if (m->lm_stage_n < 2) return set_error(GAJE_ERR_UNSUPPORTED, "n_embd too large for the lm_head ring");
+  if (int s = smem_optin((const void*)k_gemv<G_QKV>, m->pq.smem)) return s;
+  if (int s = smem_optin((const void*)k_gemv<G_OPROJ>, m->po.smem)) return s;
+  if (int s = smem_optin((const void*)k_gemv<G_GATEUP>, m->pg.smem)) return s;
+  if (int s = smem_optin((const void*)k_gemv<G_DOWN>, m->pd.smem)) return s;
+  if (int s = smem_optin((const void*)k_attn, m->attn_smem)) return s;
+  if (int s = smem_optin((const void*)k_lmhead, m->lm_smem)) return s;
+  // zero the counters, scratch, state and caches
   CK(cudaMemsetAsync(m->attn_cnt, 0, m->nkv * sizeof(unsigned), m->stream));
   CK(cudaMemsetAsync(m->amax_cnt, 0, sizeof(unsigned), m->stream));
   CK(cudaMemsetAsync(m->kcache, 0, L * size_t(m->nkv) * m->max_ctx * m->hd * 4, m->stream));
   CK(cudaMemsetAsync(m->vcache, 0, L * size_t(m->nkv) * m->max_ctx * m->hd * 4, m->stream));
   // ---- upload
+  const int qkv_mode = I.rope_split ? 1 : 2;
   for (size_t l = 0; l < L; ++l) {
     const BlockRefs& b = f.blocks[l];
-    if (int s = upload_q4(m, f, b.qkv, m->qkv[l], staging)) return s;
-    if (int s = upload_q4(m, f, b.wo, m->wo[l], staging)) return s;
-    if (int s = upload_q4(m, f, b.gate_up, m->gate_up[l], staging)) return s;
-    if (int s = upload_q4(m, f, b.down, m->down[l], staging)) return s;
+    if (int s = upload_q4(m, f, b.qkv, m->qkv[l], staging, qkv_mode)) return s;
+    if (int s = upload_q4(m, f, b.wo, m->wo[l], staging, 0)) return s;
+    if (int s = upload_q4(m, f, b.gate_up, m->gate_up[l], staging, 3)) return s;
+    if (int s = upload_q4(m, f, b.down, m->down[l], staging, 0)) return s;
     CK(cudaMemcpy(m->attn_norm[l], f.blob(b.attn_norm->dna_off, d * 4), d * 4, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(m->ffn_norm[l], f.blob(b.ffn_norm->dna_off, d * 4), d * 4, cudaMemcpyHostToDevice));
   }
@@ -531,13 +672,6 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   P.tok_hist = m->tok_hist;
   P.hist_cap = unsigned(m->max_ctx);
   P.st = m->st;
-  // dynamic shared memory above 48 KB needs an opt-in
-  const int big = int(std::max<size_t>(size_t(std::max(m->ff, m->nh * m->hd)) * 4, m->attn_smem));
-  if (big > 48 * 1024) {
-    CK(cudaFuncSetAttribute(k_down, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
-    CK(cudaFuncSetAttribute(k_oproj, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
-    CK(cudaFuncSetAttribute(k_attn, cudaFuncAttributeMaxDynamicSharedMemorySize, big));
-  }
   return GAJE_OK;
 }
 
@@ -626,7 +760,7 @@ int gaje_cuda_forward(gaje_model* m, uint32_t token_id, int clear_cache, float* 
   if (logits_out) CK(cudaMemcpyAsync(logits_out, m->logits, size_t(m->V) * 4, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
   m->host_pos += 1;
-  if (int s = m->check_nan()) return s;
+  if (int s = m->check_state()) return s;
   if (argmax_out) *argmax_out = m->h_st->argmax;
   return GAJE_OK;
 }
@@ -647,7 +781,7 @@ int gaje_cuda_decode_greedy(gaje_model* m, uint32_t first_token, size_t n_steps,
     CK(cudaMemcpyAsync(tokens_out, m->tok_hist, n_steps * 4, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
   m->host_pos += uint32_t(n_steps);
-  return m->check_nan();
+  return m->check_state();
 }
 
 int gaje_cuda_profile_steps(gaje_model* m, uint32_t first_token, size_t n_steps, float* ms,
@@ -671,7 +805,7 @@ int gaje_cuda_profile_steps(gaje_model* m, uint32_t first_token, size_t n_steps,
     if (ms) ms[c] = n_steps ? acc[c] / float(n_steps) : 0.f;
     if (launches) launches[c] = n_steps ? uint32_t(cnt[c] / n_steps) : 0u;
   }
-  return m->check_nan();
+  return m->check_state();
 }
 
 int gaje_cuda_generate(gaje_model* m, const uint32_t* prompt, size_t n_prompt, size_t max_new,
@@ -695,7 +829,7 @@ int gaje_cuda_generate(gaje_model* m, const uint32_t* prompt, size_t n_prompt, s
   }
   CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
-  if (int s = m->check_nan()) return s;
+  if (int s = m->check_state()) return s;
   std::vector<uint32_t> gen;
   std::set<uint32_t> eos_set(eos, eos + n_eos);
   std::vector<unsigned> seen_host;
@@ -748,7 +882,7 @@ int gaje_cuda_generate(gaje_model* m, const uint32_t* prompt, size_t n_prompt, s
     CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
     CK(cudaStreamSynchronize(m->stream));
     m->host_pos += 1;
-    if (int s = m->check_nan()) return s;
+    if (int s = m->check_state()) return s;
   }
   for (size_t i = 0; i < gen.size(); ++i) out[i] = gen[i];
   *n_out = gen.size();
@@ -767,19 +901,23 @@ struct gaje_q4_matrix {
 
 namespace {
 
-// One scratch area per device for the op-level entry points (argmax partials
-// and attention split partials).  Calls that overlap on the GPU share it.
+// One scratch area per device for the op-level entry points, shared by every
+// op call on that device: a DevState for status words, argmax partials and
+// the attention split partials.  Op calls that overlap on the GPU race on it.
 struct OpWorkspace {
   std::mutex mu;
   void* mem = nullptr;
   size_t size = 0;
 };
 OpWorkspace g_ws[64];
-// layout: [argmax partials, kWsArgmaxParts x u64][argmax counter] ... attention from kWsAttnBase
+// layout: [DevState][argmax partials, kWsArgmaxParts x u64][argmax counter]
+//         then, from kWsAttnBase: [attention counters][part_ml][part_o]
 constexpr size_t kWsArgmaxParts = 4096;
-constexpr size_t kWsAttnBase = kWsArgmaxParts * 8 + 4096;
+constexpr size_t kWsPartsOff = 256;
+constexpr size_t kWsCntOff = kWsPartsOff + kWsArgmaxParts * 8;
+constexpr size_t kWsAttnBase = kWsCntOff + 4096;
 
-int ws_get(int dev, size_t bytes, void** out) {
+int ws_get(int dev, size_t bytes, char** out) {
   if (dev < 0 || dev >= 64) return set_error(GAJE_ERR_INVALID, "device ordinal out of range");
   OpWorkspace& w = g_ws[dev];
   std::lock_guard<std::mutex> lk(w.mu);
@@ -794,17 +932,22 @@ int ws_get(int dev, size_t bytes, void** out) {
     CK(cudaMemset(w.mem, 0, bytes));
     w.size = bytes;
   }
-  *out = w.mem;
+  *out = static_cast<char*>(w.mem);
   return GAJE_OK;
+}
+
+int sm_count(int dev) {
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
 }
 
 }  // namespace
 
 extern "C" {
 
-gaje_q4_matrix* gaje_cuda_q4_0_upload(const uint8_t* blocks, size_t N, size_t K, const float* bias,
-                                      int device) {
-  if (!blocks || !N || !K || K % 32) {
+gaje_q4_matrix* gaje_cuda_q4_0_upload(const uint8_t* blocks, size_t N, size_t K, const float* bias, int device) {
+  if (!blocks || !N || !K || K % 32 || N > 0x7FFFFFFF || K > 0x7FFFFFFF) {
     set_error(GAJE_ERR_INVALID, "blocks must be non-NULL with K a multiple of 32");
     return nullptr;
   }
@@ -814,33 +957,36 @@ gaje_q4_matrix* gaje_cuda_q4_0_upload(const uint8_t* blocks, size_t N, size_t K,
   }
   std::unique_ptr<gaje_q4_matrix> h(new gaje_q4_matrix());
   h->device = device;
-  const size_t nb = K / 32, nblk = N * nb;
-  Arena a;
-  auto carve = [&](Arena& ar, uint32_t** raw) {
-    h->m.qs = ar.take<uint4>(nblk);
-    h->m.sm = ar.take<uint32_t>(nblk);
-    h->m.bias = bias ? ar.take<float>(N) : nullptr;
-    *raw = ar.take<uint32_t>(nblk * 5);
-  };
+  const size_t nb = K / 32, nbp = (nb + 3) / 4 * 4, nblk = N * nb;
   uint32_t* raw = nullptr;
-  carve(a, &raw);
+  auto carve = [&](Arena& ar) {
+    h->m.qs = ar.take<uint4>(nblk);
+    h->m.sm = ar.take<uint32_t>(N * nbp);
+    h->m.bias = bias ? ar.take<float>(N) : nullptr;
+    raw = ar.take<uint32_t>(nblk * 5);
+  };
+  Arena a;
+  carve(a);
   if (cudaMalloc(&h->mem, a.used) != cudaSuccess) {
     set_error(GAJE_ERR_CUDA, "cudaMalloc failed");
     return nullptr;
   }
   Arena b;
   b.base = static_cast<char*>(h->mem);
-  carve(b, &raw);
+  carve(b);
   h->m.N = int(N);
   h->m.K = int(K);
   h->m.nb = int(nb);
+  h->m.nbp = int(nbp);
   if (cudaMemcpy(raw, blocks, nblk * 20, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemset(h->m.sm, 0, N * nbp * 4) != cudaSuccess ||
       (bias && cudaMemcpy(h->m.bias, bias, N * 4, cudaMemcpyHostToDevice) != cudaSuccess)) {
     cudaFree(h->mem);
     set_error(GAJE_ERR_CUDA, "upload failed");
     return nullptr;
   }
-  k_repack_q4<<<int(std::min<size_t>((nblk + 255) / 256, 4096)), 256>>>(raw, nblk, h->m.qs, h->m.sm);
+  k_repack_q4<<<int(std::min<size_t>((nblk + 255) / 256, 8192)), 256>>>(raw, int(N), int(nb), int(nbp), 0, 0, 0,
+                                                                        h->m.qs, h->m.sm);
   if (cudaDeviceSynchronize() != cudaSuccess) {
     cudaFree(h->mem);
     set_error(GAJE_ERR_CUDA, "repack failed");
@@ -862,11 +1008,23 @@ int gaje_cuda_q4_0_gemv(const gaje_q4_matrix* h, const float* x, float* y, size_
   if (M == 0) return GAJE_OK;
   if (M > 65535) return set_error(GAJE_ERR_INVALID, "M above 65535");
   CK(cudaSetDevice(h->device));
-  const int nw = kGemvThreads / kWarp;
-  const int ctas = (h->m.N + nw - 1) / nw;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M == 1) {  // the decode kernel itself (staged rows, one CTA per SM)
+    char* ws;
+    if (int st = ws_get(h->device, kWsAttnBase, &ws)) return st;
+    GemvPlan p = plan_gemv(G_PLAIN, h->m, h->m.N, sm_count(h->device));
+    if (int st = smem_optin((const void*)k_gemv<G_PLAIN>, p.smem)) return st;
+    StepParams P{};
+    P.st = reinterpret_cast<DevState*>(ws);
+    LayerW L{};
+    GemvArgs a{h->m.view(), p.units, p.upc, x, y, 0};
+    CK(launch_k(k_gemv<G_PLAIN>, dim3(p.grid), dim3(kGemvThreads), p.smem, s, false, P, L, a));
+    return GAJE_OK;
+  }
+  const int ctas = (h->m.N + 7) / 8;
   const size_t smem = size_t(h->m.K) * 4;
-  if (smem > 48 * 1024) CK(cudaFuncSetAttribute(k_q4_gemv, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  k_q4_gemv<<<dim3(ctas, unsigned(M)), kGemvThreads, smem, (cudaStream_t)stream>>>(h->m.view(), x, y);
+  if (int st = smem_optin((const void*)k_q4_gemv, smem)) return st;
+  k_q4_gemv<<<dim3(ctas, unsigned(M)), 256, smem, s>>>(h->m.view(), x, y);
   CK(cudaGetLastError());
   return GAJE_OK;
 }
@@ -879,23 +1037,30 @@ int gaje_cuda_q4_0_dequant(const gaje_q4_matrix* h, float* w, void* stream) {
   return GAJE_OK;
 }
 
-int gaje_cuda_f32_gemv_argmax(const float* W, const float* x, size_t N, size_t K, float* logits,
-                              uint32_t* argmax, void* stream) {
+int gaje_cuda_f32_gemv_argmax(const float* W, const float* x, size_t N, size_t K, float* logits, uint32_t* argmax,
+                              void* stream) {
   if (!W || !x || !argmax || !N || !K) return set_error(GAJE_ERR_INVALID, "bad argument");
-  if (K % 4 || N > 0x7FFFFFFFu) return set_error(GAJE_ERR_UNSUPPORTED, "K must be a multiple of 4");
+  if (K % 4 || N > 0x7FFFFFFFu || K > (1u << 20)) return set_error(GAJE_ERR_UNSUPPORTED, "K must be a multiple of 4");
   int dev;
   CK(cudaGetDevice(&dev));
-  int sms = 148;
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int grid = std::min(sms * 4, int(kWsArgmaxParts));
-  void* ws;
+  char* ws;
   if (int s = ws_get(dev, kWsAttnBase, &ws)) return s;
-  unsigned long long* part = static_cast<unsigned long long*>(ws);
-  unsigned* cnt = reinterpret_cast<unsigned*>(static_cast<char*>(ws) + kWsArgmaxParts * 8);
-  const size_t smem = K * 4;
-  if (smem > 48 * 1024) CK(cudaFuncSetAttribute(k_f32_gemv_argmax, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  k_f32_gemv_argmax<<<grid, kLmThreads, smem, (cudaStream_t)stream>>>(W, x, int(N), int(K), logits, part, cnt, argmax);
-  CK(cudaGetLastError());
+  LmArgs a{};
+  a.W = W;
+  a.x = x;
+  a.logits = logits;
+  a.N = int(N);
+  a.K = int(K);
+  const int grid = std::min(sm_count(dev), int(kWsArgmaxParts));
+  a.rows_per_cta = int((N + grid - 1) / grid);
+  a.stages = lm_stages(int(K));
+  if (a.stages < 2) return set_error(GAJE_ERR_UNSUPPORTED, "K too large for the streaming ring");
+  a.part = reinterpret_cast<unsigned long long*>(ws + kWsPartsOff);
+  a.cnt = reinterpret_cast<unsigned*>(ws + kWsCntOff);
+  a.result = argmax;
+  const size_t smem = lm_smem_bytes(int(K), a.stages);
+  if (int s = smem_optin((const void*)k_lmhead, smem)) return s;
+  CK(launch_k(k_lmhead, dim3(grid), dim3(kLmThreads), smem, (cudaStream_t)stream, false, a));
   return GAJE_OK;
 }
 
@@ -907,34 +1072,41 @@ int gaje_cuda_rms_norm(const float* x, const float* w, float eps, size_t n, floa
 }
 
 int gaje_cuda_attention_decode(const float* q, const float* k_cache, const float* v_cache, size_t ctx,
-                               size_t cache_stride, size_t n_head, size_t n_head_kv, size_t head_dim,
-                               float* out, void* stream) {
+                               size_t cache_stride, size_t n_head, size_t n_head_kv, size_t head_dim, float* out,
+                               void* stream) {
   if (!q || !k_cache || !v_cache || !out || !ctx || !n_head || !n_head_kv || !head_dim)
     return set_error(GAJE_ERR_INVALID, "bad argument");
-  if (n_head % n_head_kv || n_head / n_head_kv > size_t(kAttnMaxGroup) || ctx > cache_stride)
+  if (n_head % n_head_kv || n_head / n_head_kv > size_t(kAttnMaxGroup) || ctx > cache_stride || head_dim % 4 ||
+      n_head_kv > 64 || cache_stride > (1u << 24))
     return set_error(GAJE_ERR_UNSUPPORTED, "unsupported attention geometry");
   int dev;
   CK(cudaGetDevice(&dev));
-  int nsplit, chunk;
-  attn_splits(int(ctx), nsplit, chunk);
   const size_t G = n_head / n_head_kv;
   const size_t po = n_head_kv * kAttnMaxSplits * G * head_dim, pml = n_head_kv * kAttnMaxSplits * G * 2;
-  // workspace: [counters 256 B][part_ml][part_o], behind the argmax area
-  const size_t base = kWsAttnBase;
-  void* ws;
-  if (int s = ws_get(dev, base + 256 + (pml + po) * 4 + 256, &ws)) return s;
-  char* w = static_cast<char*>(ws) + base;
-  unsigned* cnt = reinterpret_cast<unsigned*>(w);
-  float* part_ml = reinterpret_cast<float*>(w + 256);
-  float* part_o = part_ml + pml;
-  if (n_head_kv > 64) return set_error(GAJE_ERR_UNSUPPORTED, "more than 64 KV heads");
-  const size_t smem = G * (head_dim + chunk) * 4;
-  if (smem > 48 * 1024) CK(cudaFuncSetAttribute(k_attn_op, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem)));
-  const float scale = 1.0f / sqrtf(float(head_dim));
-  k_attn_op<<<dim3(unsigned(n_head_kv), kAttnMaxSplits), kAttnThreads, smem, (cudaStream_t)stream>>>(
-      q, k_cache, v_cache, out, int(ctx), int(cache_stride), int(n_head), int(n_head_kv), int(head_dim), scale,
-      part_o, part_ml, cnt);
-  CK(cudaGetLastError());
+  char* ws;
+  if (int s = ws_get(dev, kWsAttnBase + 256 + (pml + po) * 4 + 256, &ws)) return s;
+  char* w = ws + kWsAttnBase;
+  AttnArgs a{};
+  a.q = q;
+  a.kc = k_cache;
+  a.vc = v_cache;
+  a.out = out;
+  a.cnt = reinterpret_cast<unsigned*>(w);
+  a.part_ml = reinterpret_cast<float*>(w + 256);
+  a.part_o = a.part_ml + pml;
+  a.ctx = int(ctx);
+  a.stride = int(cache_stride);
+  a.nh = int(n_head);
+  a.nkv = int(n_head_kv);
+  a.hd = int(head_dim);
+  a.scale = 1.0f / sqrtf(float(head_dim));
+  a.st = nullptr;
+  int nsplit, chunk;
+  attn_splits(int(ctx), nsplit, chunk);
+  const size_t smem = attn_smem_bytes(int(G), int(head_dim), chunk);
+  if (int s = smem_optin((const void*)k_attn, smem)) return s;
+  CK(launch_k(k_attn, dim3(unsigned(n_head_kv), kAttnMaxSplits), dim3(kAttnThreads), smem, (cudaStream_t)stream,
+              false, a));
   return GAJE_OK;
 }
 

@@ -1,29 +1,41 @@
 // kernels.cuh -- sm_100a kernels of the batch-1 decode step.
 //
 // One decode step of GenomicLLM::forward_core (src/nn/llm/forward.rs:7-63) is
-// five kernels per block plus the lm_head:
-//   k_qkv     RMSNorm prologue (norm.rs:17-87) + Q4_0 GEMV of attn_qkv
-//             (genomic.rs:267-336, flush + bias of linear/forward.rs:84-115)
-//             + RoPE (attention.rs:62-84) + KV-cache append (attention.rs:85-86)
-//   k_attn    split-K flash-decode GQA attention (attention.rs:88-127); the
-//             last CTA of each KV head combines the splits
-//   k_oproj   Q4_0 GEMV of attn_output + residual add (block/forward.rs:76-82)
-//   k_gateup  RMSNorm prologue + Q4_0 GEMV of ffn_gate_up, gate row n and up
-//             row ff+n in one warp, SwiGLU epilogue (activation.rs:35-51)
-//   k_down    Q4_0 GEMV of ffn_down + residual add (block/forward.rs:124-136)
-//   k_lmhead  final RMSNorm + FP32 GEMV (dot.rs:46-67) + first-max argmax
-//             (llm/forward.rs:262-271); the last CTA finishes the argmax
+// five kernels per block plus the lm_head, chained with programmatic dependent
+// launch (PDL):
+//   k_gemv<G_QKV>     attn_norm RMSNorm (norm.rs:17-87) + Q4_0 GEMV of attn_qkv
+//                     (genomic.rs:267-336 with the flush and bias of
+//                     linear/forward.rs:84-115) + RoPE (attention.rs:62-84)
+//                     + KV-cache append (attention.rs:85-86)
+//   k_attn            split-K flash-decode GQA attention (attention.rs:88-127);
+//                     the last CTA of each KV head combines the splits
+//   k_gemv<G_OPROJ>   attn_output GEMV + residual (block/forward.rs:76-82)
+//   k_gemv<G_GATEUP>  ffn_norm RMSNorm + ffn_gate_up GEMV + SwiGLU
+//                     (activation.rs:35-51)
+//   k_gemv<G_DOWN>    ffn_down GEMV + residual (block/forward.rs:124-136)
+//   k_lmhead          output_norm RMSNorm + FP32 lm_head GEMV (dot.rs:46-67)
+//                     + first-max argmax (llm/forward.rs:262-271)
 // Optional: k_kwta (lut.rs:45-61) on the logits or on the hidden state.
 //
-// Numerics: the file is compiled with --fmad=false, so every FMA below is an
-// explicit fmaf(); products and sums elsewhere round exactly as written, as
-// in the Rust reference (which never contracts).  The Q4_0 dequantised weight
-// is fmaf(q, scale, min) -- bit-identical to the AVX2 kernel's fused dequant
-// (genomic.rs:298).  Summation order differs from the AVX2 8-lane order, so
-// dot products agree to rounding, not bit for bit.
+// Data movement (B200): every CTA stages the bytes it will consume into shared
+// memory with 1-D TMA bulk copies (cp.async.bulk, no multicast) completing on
+// an mbarrier.  Weights and cached K/V do not depend on the previous kernel,
+// so each kernel issues those copies first, then griddepcontrol.wait, then
+// griddepcontrol.launch_dependents: the next kernel's copies overlap this
+// kernel's math.  A kernel triggers its dependents only after its own wait,
+// so when a kernel's pre-wait code runs, every kernel before its predecessor
+// has completed (the decode position and earlier cache rows are stable).
+// Data the immediately preceding kernel wrote is read after the wait with
+// L2-only loads (ld.global.cg).
+//
+// Numerics: compiled with --fmad=false; every FMA is an explicit fmaf().  The
+// Q4_0 dequantised weight is fmaf(q, scale, min), bit-identical to the AVX2
+// kernel's fused dequant (genomic.rs:298).  Summation orders differ from the
+// AVX2 8-lane order, so dot products agree to rounding, not bit for bit.
 //
 // Device errors are status words, never traps: NaN guards (block/forward.rs
-// :11-140) record the earliest (layer, check) with atomicMin.
+// :11-140) record the first (position, layer, check) with atomicMin; a bounded
+// mbarrier wait that runs out sets DevState::err and the kernel returns.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -33,13 +45,19 @@
 namespace gaje {
 
 constexpr int kWarp = 32;
-constexpr int kGemvThreads = 256;       // 8 warps per GEMV CTA
-constexpr int kAttnThreads = 128;
-constexpr int kAttnMinChunk = 16;       // positions per attention split (minimum)
+constexpr int kGemvThreads = 512;       // 16 warps per GEMV CTA
+constexpr int kAttnThreads = 256;
+constexpr int kAttnMinChunk = 32;       // positions per attention split (minimum)
 constexpr int kAttnMaxSplits = 64;
 constexpr int kAttnMaxGroup = 16;       // q heads per kv head
-constexpr int kLmThreads = 256;
+constexpr int kLmConsumerWarps = 8;
+constexpr int kLmThreads = (kLmConsumerWarps + 1) * 32;  // + one producer warp
+constexpr int kLmRowsPerStage = 8;
+constexpr int kLmMaxStages = 8;
+constexpr size_t kLmSmemBudget = 200 * 1024;  // ring + x, below the 227 KB per-CTA limit
 constexpr int kKwtaThreads = 1024;
+constexpr int kSmemHeader = 128;        // mbarriers at the start of dynamic smem
+constexpr unsigned long long kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s
 
 // NaN guard codes, in the order block/forward.rs checks them.
 enum NanCheck : unsigned {
@@ -59,23 +77,24 @@ struct DevState {
   unsigned argmax;     // first index of the max logit of the last step
   unsigned nan_code;   // 0xFFFFFFFF, or pos*4096 + layer*8 + check of the first NaN guard
   unsigned hist_len;   // entries written to the token history
-  unsigned pad[3];
+  unsigned err;        // 0, or 1 + the kernel id of a bounded wait that ran out
+  unsigned pad[2];
 };
 
 // A Q4_0 matrix in the engine's layout: per row, nb = K/32 blocks; qs[row][b]
 // holds the block's 16 nibble bytes unchanged (element 2k = low nibble of
-// byte k), sm[row][b] = f16 scale | f16 min << 16.  Same 20 bytes per block as
-// the file, split into 16-byte-aligned arrays so a lane reads a block with one
-// 128-bit load.
+// byte k); sm[row][b] = f16 scale | f16 min << 16 with a row stride of nbp
+// (nb rounded up to a multiple of 4) so that any row range is a 16-byte
+// multiple for the bulk copies.  20 bytes per 32 weights, as in the file.
 struct Q4View {
   const uint4* qs;
   const uint32_t* sm;
   const float* bias;  // [N] or nullptr
-  int N, K, nb;
+  int N, K, nb, nbp;
 };
 
 struct LayerW {
-  Q4View qkv, wo, gate_up, down;
+  Q4View qkv, wo, gate_up, down;  // qkv and gate_up rows are stored pair-interleaved
   const float* attn_norm;
   const float* ffn_norm;
   float* kc;  // [nkv][max_ctx][hd]
@@ -105,6 +124,61 @@ struct StepParams {
   unsigned hist_cap;
   DevState* st;
 };
+
+// ------------------------------------------------------------------ PTX
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+// Makes mbarrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait on an mbarrier phase: false after kWaitNs without completion.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_ns() - t0 > kWaitNs) return false;
+  return true;
+}
+// 1-D TMA bulk copy global -> this CTA's shared memory (no multicast).
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Records a timed-out wait (kernel id), keeping the first one.
+__device__ __forceinline__ void flag_timeout(DevState* st, unsigned kid) { atomicCAS(&st->err, 0u, 1u + kid); }
 
 // ------------------------------------------------------------------ helpers
 __device__ __forceinline__ float warp_sum(float v) {
@@ -188,11 +262,19 @@ __device__ __forceinline__ float q4_block_dot(const uint4 q, uint32_t smv, const
   return (a0 + a1) + (a2 + a3);
 }
 
-// Full row dot of one Q4_0 row by one warp (lanes stride the blocks).  The
-// returned value is flushed and biased like compute_single_row.
-__device__ __forceinline__ float q4_row(const Q4View& W, int row, const float* xs, int lane) {
+// Row dot of one Q4_0 row held in shared memory (qs_row[nb], sm_row[nb]), one
+// warp, lanes striding the blocks; flushed like compute_single_row (no bias).
+__device__ __forceinline__ float q4_row_smem(const uint4* qs_row, const uint32_t* sm_row, int nb,
+                                             const float* xs, int lane) {
+  float acc = 0.f;
+  for (int b = lane; b < nb; b += kWarp) acc += q4_block_dot(qs_row[b], sm_row[b], xs, b);
+  return flush_small(warp_sum(acc));
+}
+
+// Row dot straight from global memory (op-level M > 1 path).
+__device__ __forceinline__ float q4_row_global(const Q4View& W, int row, const float* xs, int lane) {
   const uint4* qs = W.qs + (size_t)row * W.nb;
-  const uint32_t* sm = W.sm + (size_t)row * W.nb;
+  const uint32_t* sm = W.sm + (size_t)row * W.nbp;
   float acc = 0.f;
 #pragma unroll 4
   for (int b = lane; b < W.nb; b += kWarp) acc += q4_block_dot(__ldg(qs + b), __ldg(sm + b), xs, b);
@@ -201,240 +283,10 @@ __device__ __forceinline__ float q4_row(const Q4View& W, int row, const float* x
   return y;
 }
 
-// Two rows at once (more loads in flight per lane).
-__device__ __forceinline__ void q4_row2(const Q4View& W, int r0, int r1, const float* xs, int lane,
-                                        float& y0, float& y1) {
-  const uint4* qs0 = W.qs + (size_t)r0 * W.nb;
-  const uint4* qs1 = W.qs + (size_t)r1 * W.nb;
-  const uint32_t* sm0 = W.sm + (size_t)r0 * W.nb;
-  const uint32_t* sm1 = W.sm + (size_t)r1 * W.nb;
-  float a = 0.f, c = 0.f;
-#pragma unroll 2
-  for (int b = lane; b < W.nb; b += kWarp) {
-    const uint4 qa = __ldg(qs0 + b), qc = __ldg(qs1 + b);
-    const uint32_t sa = __ldg(sm0 + b), sc = __ldg(sm1 + b);
-    a += q4_block_dot(qa, sa, xs, b);
-    c += q4_block_dot(qc, sc, xs, b);
-  }
-  y0 = flush_small(warp_sum(a));
-  y1 = flush_small(warp_sum(c));
-  if (W.bias) {
-    y0 += __ldg(W.bias + r0);
-    y1 += __ldg(W.bias + r1);
-  }
-}
-
 // NaN guard code: position * 4096 + layer * 8 + check, so atomicMin keeps the
 // first failing check of the first failing step, the one the reference stops at.
-__device__ __forceinline__ void nan_flag(DevState* st, int layer, unsigned check) {
-  atomicMin(&st->nan_code, st->pos * 4096u + unsigned(layer) * 8u + check);
-}
-
-// RMSNorm of src[0..n) into swizzled smem xs (norm.rs:17-87):
-// inv = 1/sqrt(sum(x^2)/n + eps); out = (x*inv)*w.  The sum is a tree here
-// (the reference uses an 8-lane FMA sweep), so inv agrees to rounding.
-// Returns true if src held a NaN (nan_in) or the output did (nan_out).
-__device__ __forceinline__ void rmsnorm_smem(const float* __restrict__ src, const float* __restrict__ w,
-                                             float eps, int n, float* xs, float* red, bool& nan_in,
-                                             bool& nan_out) {
-  float ss = 0.f;
-  int bad = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = src[i];
-    ss = fmaf(v, v, ss);
-    bad |= (v != v);
-  }
-  ss = block_sum(ss, red);
-  const int any_bad_in = __syncthreads_or(bad);
-  const float inv = 1.0f / sqrtf(ss / (float)n + eps);
-  int bad_out = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float o = (src[i] * inv) * w[i];
-    bad_out |= (o != o);
-    xs[swz(i)] = o;
-  }
-  nan_out = __syncthreads_or(bad_out) != 0;
-  nan_in = any_bad_in != 0;
-}
-
-// ------------------------------------------------------------------ kernels
-
-// attn_qkv with the attn_norm prologue; layer 0 reads the embedding row of
-// the step's token (get_row_core, linear/forward.rs:195-209: row token % V)
-// and also materialises the residual stream x.
-__global__ void __launch_bounds__(kGemvThreads) k_qkv(StepParams P, LayerW W, int layer) {
-  extern __shared__ float smem[];
-  float* xs = smem;           // [d] swizzled
-  __shared__ float red[32];
-  const unsigned pos = P.st->pos;
-  const float* src = P.x;
-  if (layer == 0) {
-    const unsigned tok = P.st->token % (unsigned)P.V;
-    src = P.embd + (size_t)tok * P.d;
-    if (blockIdx.x == 0)
-      for (int i = threadIdx.x; i < P.d; i += blockDim.x) P.x[i] = src[i];
-  }
-  bool nan_in, nan_out;
-  rmsnorm_smem(src, W.attn_norm, P.eps, P.d, xs, red, nan_in, nan_out);
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    if (nan_in) nan_flag(P.st, layer, kNanInput);
-    if (nan_out) nan_flag(P.st, layer, kNanAttnNorm);
-  }
-  const int lane = threadIdx.x & 31;
-  const int half = P.hd >> 1;
-  const int npairs = W.qkv.N >> 1;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int nwarps = (gridDim.x * blockDim.x) >> 5;
-  const float2* rope = P.rope + (size_t)pos * half;
-  for (int p = gw; p < npairs; p += nwarps) {
-    const int head = p / half, i = p - head * half;  // head over q, k, v heads
-    const int r0 = head * P.hd + (P.rope_split ? i : 2 * i);
-    const int r1 = r0 + (P.rope_split ? half : 1);
-    float y0, y1;
-    q4_row2(W.qkv, r0, r1, xs, lane, y0, y1);
-    if (lane == 0) {
-      if (head < P.nh + P.nkv) {  // RoPE on q and k: v0*cos - v1*sin, v0*sin + v1*cos
-        const float2 cs = rope[i];
-        const float o0 = y0 * cs.x - y1 * cs.y;
-        const float o1 = y0 * cs.y + y1 * cs.x;
-        y0 = o0;
-        y1 = o1;
-      }
-      const int c0 = r0 - head * P.hd, c1 = r1 - head * P.hd;
-      if (head < P.nh) {
-        P.q[r0] = y0;
-        P.q[r1] = y1;
-      } else {
-        const bool is_k = head < P.nh + P.nkv;
-        const int g = is_k ? head - P.nh : head - P.nh - P.nkv;
-        float* c = (is_k ? W.kc : W.vc) + ((size_t)g * P.max_ctx + pos) * P.hd;
-        c[c0] = y0;
-        c[c1] = y1;
-      }
-    }
-  }
-}
-
-// Split bookkeeping shared by the attention kernel and its host wrapper.
-__host__ __device__ __forceinline__ void attn_splits(int ctx, int& nsplit, int& chunk) {
-  int n0 = (ctx + kAttnMinChunk - 1) / kAttnMinChunk;
-  if (n0 > kAttnMaxSplits) n0 = kAttnMaxSplits;
-  if (n0 < 1) n0 = 1;
-  chunk = (ctx + n0 - 1) / n0;
-  nsplit = (ctx + chunk - 1) / chunk;
-}
-
-// One CTA per (kv head g, split s).  Scores for the G query heads of the group
-// over the split's positions, exp against the split max, unnormalised P*V;
-// the last CTA of the group to finish combines the splits:
-//   out = (sum_s O_s e^{m_s-M}) * (1/(sum_s l_s e^{m_s-M} + 1e-12))
-// (the reference's inv_s = 1/(sum_e + 1e-12), attention.rs:110).
-__device__ __forceinline__ void attn_core(const float* __restrict__ q, const float* __restrict__ kc,
-                                          const float* __restrict__ vc, float* __restrict__ out,
-                                          int ctx, int cache_stride, int nh, int nkv, int hd,
-                                          float scale, float* part_o, float* part_ml,
-                                          unsigned* cnt) {
-  extern __shared__ float smem[];
-  const int G = nh / nkv;
-  const int g = blockIdx.x, s = blockIdx.y;
-  int nsplit, chunk;
-  attn_splits(ctx, nsplit, chunk);
-  if (s >= nsplit) return;
-  const int t0 = s * chunk;
-  const int n = min(ctx, t0 + chunk) - t0;
-  float* qs = smem;            // [G][hd]
-  float* ps = qs + G * hd;     // [G][chunk]
-  __shared__ float mls[2 * kAttnMaxGroup];
-  __shared__ int is_last;
-  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = q[(size_t)g * G * hd + i];
-  __syncthreads();
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
-  const float* kbase = kc + ((size_t)g * cache_stride + t0) * hd;
-  const float* vbase = vc + ((size_t)g * cache_stride + t0) * hd;
-  // scores: one warp per position, lanes across head_dim
-  for (int t = wid; t < n; t += nw) {
-    const float* kr = kbase + (size_t)t * hd;
-    for (int j = 0; j < G; ++j) {
-      float a = 0.f;
-      for (int e = lane; e < hd; e += kWarp) a = fmaf(qs[j * hd + e], kr[e], a);
-      a = warp_sum(a);
-      if (lane == 0) ps[j * chunk + t] = a * scale;
-    }
-  }
-  __syncthreads();
-  // softmax pieces per head: one warp per head
-  for (int j = wid; j < G; j += nw) {
-    float m = -INFINITY;
-    for (int t = lane; t < n; t += kWarp) m = fmaxf(m, ps[j * chunk + t]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int t = lane; t < n; t += kWarp) {
-      const float e = expf(ps[j * chunk + t] - m);
-      ps[j * chunk + t] = e;
-      l += e;
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
-      mls[2 * j] = m;
-      mls[2 * j + 1] = l;
-    }
-  }
-  __syncthreads();
-  const size_t pbase = ((size_t)g * kAttnMaxSplits + s) * G;
-  for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
-    const int j = idx / hd, e = idx - j * hd;
-    float a = 0.f;
-    for (int t = 0; t < n; ++t) a = fmaf(ps[j * chunk + t], vbase[(size_t)t * hd + e], a);
-    part_o[(pbase + j) * hd + e] = a;
-  }
-  if (threadIdx.x < G) {
-    part_ml[(pbase + threadIdx.x) * 2] = mls[2 * threadIdx.x];
-    part_ml[(pbase + threadIdx.x) * 2 + 1] = mls[2 * threadIdx.x + 1];
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) is_last = (atomicAdd(cnt + g, 1u) == (unsigned)nsplit - 1u);
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
-    const int j = idx / hd, e = idx - j * hd;
-    float M = -INFINITY;
-    for (int r = 0; r < nsplit; ++r)
-      M = fmaxf(M, __ldcg(part_ml + (((size_t)g * kAttnMaxSplits + r) * G + j) * 2));
-    float L = 0.f, O = 0.f;
-    for (int r = 0; r < nsplit; ++r) {
-      const size_t pj = ((size_t)g * kAttnMaxSplits + r) * G + j;
-      const float w = expf(__ldcg(part_ml + pj * 2) - M);
-      L += __ldcg(part_ml + pj * 2 + 1) * w;
-      O += __ldcg(part_o + pj * hd + e) * w;
-    }
-    const float inv = 1.0f / (L + 1e-12f);
-    out[((size_t)g * G + j) * hd + e] = O * inv;
-  }
-  if (threadIdx.x == 0) cnt[g] = 0u;  // ready for the next launch
-}
-
-__global__ void __launch_bounds__(kAttnThreads) k_attn(StepParams P, LayerW W) {
-  const int ctx = (int)P.st->pos + 1;
-  attn_core(P.q, W.kc, W.vc, P.attn, ctx, P.max_ctx, P.nh, P.nkv, P.hd, P.attn_scale, P.part_o,
-            P.part_ml, P.attn_cnt);
-}
-
-// attn_output GEMV + residual: x[n] = x[n] + y[n].
-__global__ void __launch_bounds__(kGemvThreads) k_oproj(StepParams P, LayerW W) {
-  extern __shared__ float smem[];
-  float* xs = smem;  // [nh*hd] swizzled
-  const int K = W.wo.K;
-  for (int i = threadIdx.x; i < K; i += blockDim.x) xs[swz(i)] = P.attn[i];
-  __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int nwarps = (gridDim.x * blockDim.x) >> 5;
-  for (int r = gw; r < W.wo.N; r += nwarps) {
-    const float y = q4_row(W.wo, r, xs, lane);
-    if (lane == 0) P.x[r] = P.x[r] + y;
-  }
+__device__ __forceinline__ void nan_flag(DevState* st, unsigned pos, int layer, unsigned check) {
+  atomicMin(&st->nan_code, pos * 4096u + unsigned(layer) * 8u + check);
 }
 
 // SwiGLU of activation.rs:35-51 (swiglu_balanced).
@@ -450,63 +302,368 @@ __device__ __forceinline__ float swiglu_balanced(float g, float u) {
   return (g * sig) * u;
 }
 
-// ffn_norm prologue + ffn_gate_up GEMV (rows n and ff+n per warp) + SwiGLU.
-__global__ void __launch_bounds__(kGemvThreads) k_gateup(StepParams P, LayerW W, int layer) {
-  extern __shared__ float smem[];
-  float* xs = smem;  // [d] swizzled
-  __shared__ float red[32];
-  bool nan_in, nan_out;
-  rmsnorm_smem(P.x, W.ffn_norm, P.eps, P.d, xs, red, nan_in, nan_out);
-  const int lane = threadIdx.x & 31;
-  const int ff = W.gate_up.N >> 1;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int nwarps = (gridDim.x * blockDim.x) >> 5;
-  for (int n = gw; n < ff; n += nwarps) {
-    float g, u;
-    q4_row2(W.gate_up, n, n + ff, xs, lane, g, u);
-    if (lane == 0) {
-      if (u != u) nan_flag(P.st, layer, kNanUp);
-      const float a = swiglu_balanced(g, u);
-      if (a != a) nan_flag(P.st, layer, kNanFfnOut);
-      P.act[n] = a;
-    }
-  }
+// ------------------------------------------------------------ Q4_0 GEMV
+enum GemvMode { G_QKV = 0, G_OPROJ = 1, G_GATEUP = 2, G_DOWN = 3, G_PLAIN = 4 };
+
+struct GemvArgs {
+  Q4View W;
+  int units;      // work units: rows (OPROJ, DOWN, PLAIN) or row pairs (QKV, GATEUP)
+  int upc;        // units per CTA
+  const float* x; // PLAIN: input vector
+  float* y;       // PLAIN: output vector
+  int layer;
+};
+
+__host__ __device__ constexpr int gemv_rows_per_unit(int mode) { return (mode == G_QKV || mode == G_GATEUP) ? 2 : 1; }
+
+// Dynamic shared memory of a GEMV CTA: header + x (K floats) + staged rows.
+__host__ __device__ inline size_t gemv_smem_bytes(int mode, int K, int nb, int nbp, int upc) {
+  const size_t rows = size_t(upc) * gemv_rows_per_unit(mode);
+  return kSmemHeader + size_t(K) * 4 + rows * nb * 16 + rows * nbp * 4;
 }
 
-// ffn_down GEMV + residual.  With use_genomic_norm (block/forward.rs:115-123)
-// every CTA first rescales act by h_scale/rms when rms > h_scale (h_scale = 1).
-__global__ void __launch_bounds__(kGemvThreads) k_down(StepParams P, LayerW W, int layer) {
-  extern __shared__ float smem[];
-  float* xs = smem;  // [ff] swizzled
+// One CTA owns units [u0, u1) = a contiguous row range of the (pair-
+// interleaved) matrix, staged into shared memory by two bulk copies.
+template <int MODE>
+__global__ void __launch_bounds__(kGemvThreads) k_gemv(StepParams P, LayerW L, GemvArgs A) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);
   __shared__ float red[32];
-  const int K = W.down.K;
-  float s = 1.0f;
-  if (P.use_genomic_norm) {
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < K; i += blockDim.x) ss = fmaf(P.act[i], P.act[i], ss);
-    ss = block_sum(ss, red);
-    const float rms = sqrtf(ss / (float)K + P.eps);
-    if (rms > 1.0f) s = 1.0f / rms;
-  }
-  for (int i = threadIdx.x; i < K; i += blockDim.x) {
-    const float a = P.act[i];
-    xs[swz(i)] = P.use_genomic_norm && s != 1.0f ? a * s : a;
+  constexpr int RPU = gemv_rows_per_unit(MODE);
+  const Q4View& W = A.W;
+  const int K = W.K, nb = W.nb, nbp = W.nbp;
+  float* xs = reinterpret_cast<float*>(smem_raw + kSmemHeader);
+  uint4* qs_s = reinterpret_cast<uint4*>(xs + K);
+  const int u0 = blockIdx.x * A.upc;
+  const int u1 = min(A.units, u0 + A.upc);
+  const int r0 = u0 * RPU, nrows = (u1 - u0) * RPU;
+  uint32_t* sm_s = reinterpret_cast<uint32_t*>(qs_s + (size_t)A.upc * RPU * nb);
+
+  // 1. stage this CTA's weight rows (independent of the previous kernel)
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int nwarps = (gridDim.x * blockDim.x) >> 5;
-  for (int r = gw; r < W.down.N; r += nwarps) {
-    const float y = q4_row(W.down, r, xs, lane);
-    if (lane == 0) {
-      if (y != y) nan_flag(P.st, layer, kNanProjFfn);
-      const float xn = P.x[r] + y;
-      if (xn != xn) nan_flag(P.st, layer, kNanResidual);
-      P.x[r] = xn;
+  if (threadIdx.x == 0) {
+    const uint32_t qb = uint32_t(nrows) * nb * 16, sb = uint32_t(nrows) * nbp * 4;
+    mbar_expect_tx(bar, qb + sb);
+    bulk_g2s(qs_s, W.qs + (size_t)r0 * nb, qb, bar);
+    bulk_g2s(sm_s, W.sm + (size_t)r0 * nbp, sb, bar);
+  }
+  // 2. wait for the previous kernel, release the next one
+  pdl_wait();
+  pdl_trigger();
+  DevState* st = P.st;
+  const unsigned pos = __ldcg(&st->pos);
+
+  // 3. activation vector -> swizzled smem (RMSNorm where the reference has one)
+  if (MODE == G_QKV || MODE == G_GATEUP) {
+    const float* src = P.x;
+    const float* nw = MODE == G_QKV ? L.attn_norm : L.ffn_norm;
+    if (MODE == G_QKV && A.layer == 0) {
+      const unsigned tok = __ldcg(&st->token) % (unsigned)P.V;
+      src = P.embd + (size_t)tok * P.d;  // get_row_core: row token % V
+    }
+    float ss = 0.f;
+    int bad = 0;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+      const float v = __ldcg(src + i);
+      xs[swz(i)] = v;
+      ss = fmaf(v, v, ss);
+      bad |= (v != v);
+    }
+    ss = block_sum(ss, red);
+    const int bad_in = __syncthreads_or(bad);
+    const float inv = 1.0f / sqrtf(ss / (float)K + P.eps);
+    int bad_out = 0;
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+      const int si = swz(i);
+      const float o = (xs[si] * inv) * nw[i];
+      bad_out |= (o != o);
+      xs[si] = o;
+    }
+    bad_out = __syncthreads_or(bad_out);
+    if (MODE == G_QKV && blockIdx.x == 0) {
+      if (threadIdx.x == 0) {
+        if (bad_in) nan_flag(st, pos, A.layer, kNanInput);
+        if (bad_out) nan_flag(st, pos, A.layer, kNanAttnNorm);
+      }
+      if (A.layer == 0)  // the residual stream starts as the embedding row
+        for (int i = threadIdx.x; i < K; i += blockDim.x) P.x[i] = __ldcg(src + i);
+    }
+  } else {
+    const float* src = MODE == G_OPROJ ? P.attn : (MODE == G_DOWN ? P.act : A.x);
+    float s = 1.0f;
+    if (MODE == G_DOWN && P.use_genomic_norm) {  // block/forward.rs:115-123, h_scale = 1
+      float ss = 0.f;
+      for (int i = threadIdx.x; i < K; i += blockDim.x) {
+        const float v = __ldcg(src + i);
+        ss = fmaf(v, v, ss);
+      }
+      ss = block_sum(ss, red);
+      const float rms = sqrtf(ss / (float)K + P.eps);
+      if (rms > 1.0f) s = 1.0f / rms;
+    }
+    for (int i = threadIdx.x; i < K; i += blockDim.x) {
+      const float v = __ldcg(src + i);
+      xs[swz(i)] = (s != 1.0f) ? v * s : v;
+    }
+    __syncthreads();
+  }
+
+  // 4. weights staged?
+  if (!mbar_wait(bar, 0)) {
+    if (threadIdx.x == 0) flag_timeout(st, MODE);
+    mbar_wait(bar, 0);  // do not free smem under an in-flight copy (bounded again)
+    return;
+  }
+
+  // 5. one warp per unit
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  for (int u = u0 + wid; u < u1; u += nwarps) {
+    const int lr = (u - u0) * RPU;
+    if (RPU == 1) {
+      float y = q4_row_smem(qs_s + (size_t)lr * nb, sm_s + (size_t)lr * nbp, nb, xs, lane);
+      if (lane == 0) {
+        const int r = r0 + lr;
+        if (W.bias) y += W.bias[r];
+        if (MODE == G_PLAIN) {
+          A.y[r] = y;
+        } else if (MODE == G_OPROJ) {
+          P.x[r] = __ldcg(P.x + r) + y;
+        } else {  // G_DOWN
+          if (y != y) nan_flag(st, pos, A.layer, kNanProjFfn);
+          const float xn = __ldcg(P.x + r) + y;
+          if (xn != xn) nan_flag(st, pos, A.layer, kNanResidual);
+          P.x[r] = xn;
+        }
+      }
+    } else {
+      float y0 = q4_row_smem(qs_s + (size_t)lr * nb, sm_s + (size_t)lr * nbp, nb, xs, lane);
+      float y1 = q4_row_smem(qs_s + (size_t)(lr + 1) * nb, sm_s + (size_t)(lr + 1) * nbp, nb, xs, lane);
+      if (lane == 0) {
+        if (W.bias) {
+          y0 += W.bias[r0 + lr];
+          y1 += W.bias[r0 + lr + 1];
+        }
+        if (MODE == G_GATEUP) {
+          if (y1 != y1) nan_flag(st, pos, A.layer, kNanUp);
+          const float a = swiglu_balanced(y0, y1);
+          if (a != a) nan_flag(st, pos, A.layer, kNanFfnOut);
+          P.act[u] = a;
+        } else {  // G_QKV: pair u = (head, i) in the interleaved row order
+          const int half = P.hd >> 1;
+          const int head = u / half, i = u - head * half;
+          const int c0 = P.rope_split ? i : 2 * i;
+          const int c1 = P.rope_split ? i + half : 2 * i + 1;
+          if (head < P.nh + P.nkv) {  // RoPE on q and k: v0*cos - v1*sin, v0*sin + v1*cos
+            const float2 cs = P.rope[(size_t)pos * half + i];
+            const float o0 = y0 * cs.x - y1 * cs.y;
+            const float o1 = y0 * cs.y + y1 * cs.x;
+            y0 = o0;
+            y1 = o1;
+          }
+          if (head < P.nh) {
+            P.q[head * P.hd + c0] = y0;
+            P.q[head * P.hd + c1] = y1;
+          } else {
+            const bool is_k = head < P.nh + P.nkv;
+            const int g = is_k ? head - P.nh : head - P.nh - P.nkv;
+            float* c = (is_k ? L.kc : L.vc) + ((size_t)g * P.max_ctx + pos) * P.hd;
+            c[c0] = y0;
+            c[c1] = y1;
+          }
+        }
+      }
     }
   }
 }
 
+// ------------------------------------------------------------ attention
+// Split bookkeeping shared by the attention kernels and the host.
+__host__ __device__ __forceinline__ void attn_splits(int ctx, int& nsplit, int& chunk) {
+  int n0 = (ctx + kAttnMinChunk - 1) / kAttnMinChunk;
+  if (n0 > kAttnMaxSplits) n0 = kAttnMaxSplits;
+  if (n0 < 1) n0 = 1;
+  chunk = (ctx + n0 - 1) / n0;
+  nsplit = (ctx + chunk - 1) / chunk;
+}
+__host__ __device__ inline int attn_chunk_max(int max_ctx) {
+  const int c = (max_ctx + kAttnMaxSplits - 1) / kAttnMaxSplits;
+  return c > kAttnMinChunk ? c : kAttnMinChunk;
+}
+__host__ __device__ inline size_t attn_smem_bytes(int G, int hd, int chunk_max) {
+  return kSmemHeader + size_t(2 * chunk_max * hd + G * hd + G * chunk_max) * 4;
+}
+
+struct AttnArgs {
+  const float* q;   // [nh*hd]
+  const float* kc;  // [nkv][stride][hd]
+  const float* vc;
+  float* out;       // [nh*hd]
+  float* part_o;
+  float* part_ml;
+  unsigned* cnt;    // [nkv]
+  int ctx;          // >0: fixed context (op level); 0: st->pos + 1
+  int stride, nh, nkv, hd;
+  float scale;
+  DevState* st;     // decode state (step) or nullptr (op level)
+};
+
+// One CTA per (kv head g, split s).  The split's cached K/V rows (positions
+// before the new one) are bulk-copied to smem before the PDL wait; the new
+// row and q are read after it.  Scores for the G query heads of the group,
+// exp against the split max, unnormalised P*V; the last CTA of the group
+// combines the splits:
+//   out = (sum_s O_s e^{m_s-M}) * (1/(sum_s l_s e^{m_s-M} + 1e-12))
+// (the reference's inv_s = 1/(sum_e + 1e-12), attention.rs:110).
+__global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs A) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);
+  __shared__ float mls[2 * kAttnMaxGroup];
+  __shared__ float wsh[kAttnMaxGroup * kAttnMaxSplits];
+  __shared__ float linv[kAttnMaxGroup];
+  __shared__ int is_last;
+  const int G = A.nh / A.nkv, hd = A.hd;
+  const int g = blockIdx.x, s = blockIdx.y;
+  // the decode position is stable here (written two or more kernels back)
+  const int ctx = A.ctx > 0 ? A.ctx : (int)__ldcg(&A.st->pos) + 1;
+  int nsplit, chunk;
+  attn_splits(ctx, nsplit, chunk);
+  if (s >= nsplit) return;
+  const int t0 = s * chunk;
+  const int n = min(ctx, t0 + chunk) - t0;
+  // rows already in the cache before this step; the step's own row (ctx-1)
+  // is written by the preceding kernel
+  const int newest = A.ctx > 0 ? ctx : ctx - 1;
+  const int n_old = max(0, min(n, newest - t0));
+  const int cm = chunk;  // smem row capacity used by this launch
+  float* Ks = reinterpret_cast<float*>(smem_raw + kSmemHeader);
+  float* Vs = Ks + (size_t)cm * hd;
+  float* qs = Vs + (size_t)cm * hd;
+  float* ps = qs + (size_t)G * hd;
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const float* kbase = A.kc + ((size_t)g * A.stride + t0) * hd;
+  const float* vbase = A.vc + ((size_t)g * A.stride + t0) * hd;
+  if (threadIdx.x == 0) {
+    const uint32_t bytes = uint32_t(n_old) * hd * 4;
+    mbar_expect_tx(bar, 2 * bytes);
+    if (bytes) {
+      bulk_g2s(Ks, kbase, bytes, bar);
+      bulk_g2s(Vs, vbase, bytes, bar);
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
+  for (int i = threadIdx.x; i < G * hd; i += blockDim.x) qs[i] = __ldcg(A.q + (size_t)g * G * hd + i);
+  for (int i = threadIdx.x; i < (n - n_old) * hd; i += blockDim.x) {  // the new row
+    Ks[(size_t)n_old * hd + i] = __ldcg(kbase + (size_t)n_old * hd + i);
+    Vs[(size_t)n_old * hd + i] = __ldcg(vbase + (size_t)n_old * hd + i);
+  }
+  __syncthreads();
+  if (!mbar_wait(bar, 0)) {
+    if (threadIdx.x == 0 && A.st) flag_timeout(A.st, 8);
+    mbar_wait(bar, 0);
+    return;
+  }
+  // scores: thread per (head j, position t); the (e + t) % hd walk keeps the
+  // 32 positions of a warp on 32 different banks
+  for (int idx = threadIdx.x; idx < G * n; idx += blockDim.x) {
+    const int j = idx / n, t = idx - j * n;
+    const float* qr = qs + j * hd;
+    const float* kr = Ks + (size_t)t * hd;
+    float a0 = 0.f, a1 = 0.f;
+    int e0 = (t % hd) & ~1;  // head_dim is even, so e0 + 1 never wraps past hd
+    for (int e = 0; e < hd; e += 2) {
+      a0 = fmaf(qr[e0], kr[e0], a0);
+      a1 = fmaf(qr[e0 + 1], kr[e0 + 1], a1);
+      e0 += 2;
+      if (e0 >= hd) e0 -= hd;
+    }
+    ps[j * cm + t] = (a0 + a1) * A.scale;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int j = wid; j < G; j += nw) {
+    float m = -INFINITY;
+    for (int t = lane; t < n; t += kWarp) m = fmaxf(m, ps[j * cm + t]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int t = lane; t < n; t += kWarp) {
+      const float e = expf(ps[j * cm + t] - m);
+      ps[j * cm + t] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      mls[2 * j] = m;
+      mls[2 * j + 1] = l;
+    }
+  }
+  __syncthreads();
+  const size_t pbase = ((size_t)g * kAttnMaxSplits + s) * G;
+  for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
+    const int j = idx / hd, e = idx - j * hd;
+    const float* pr = ps + j * cm;
+    float a0 = 0.f, a1 = 0.f;
+    int t = 0;
+    for (; t + 1 < n; t += 2) {
+      a0 = fmaf(pr[t], Vs[(size_t)t * hd + e], a0);
+      a1 = fmaf(pr[t + 1], Vs[(size_t)(t + 1) * hd + e], a1);
+    }
+    if (t < n) a0 = fmaf(pr[t], Vs[(size_t)t * hd + e], a0);
+    A.part_o[(pbase + j) * hd + e] = a0 + a1;
+  }
+  if (threadIdx.x < G) {
+    A.part_ml[(pbase + threadIdx.x) * 2] = mls[2 * threadIdx.x];
+    A.part_ml[(pbase + threadIdx.x) * 2 + 1] = mls[2 * threadIdx.x + 1];
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = (atomicAdd(A.cnt + g, 1u) == (unsigned)nsplit - 1u);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  // combine: per-split weights w = e^{m_s - M} in smem, then O in parallel
+  for (int idx = threadIdx.x; idx < G * nsplit; idx += blockDim.x) {
+    const int j = idx / nsplit, r = idx - j * nsplit;
+    wsh[idx] = __ldcg(A.part_ml + (((size_t)g * kAttnMaxSplits + r) * G + j) * 2);
+  }
+  __syncthreads();
+  for (int j = wid; j < G; j += nw) {
+    float M = -INFINITY;
+    for (int r = lane; r < nsplit; r += kWarp) M = fmaxf(M, wsh[j * nsplit + r]);
+    M = warp_max(M);
+    float Lsum = 0.f;
+    for (int r = lane; r < nsplit; r += kWarp) {
+      const float w = expf(wsh[j * nsplit + r] - M);
+      wsh[j * nsplit + r] = w;
+      Lsum += __ldcg(A.part_ml + (((size_t)g * kAttnMaxSplits + r) * G + j) * 2 + 1) * w;
+    }
+    Lsum = warp_sum(Lsum);
+    if (lane == 0) linv[j] = 1.0f / (Lsum + 1e-12f);
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
+    const int j = idx / hd, e = idx - j * hd;
+    float O0 = 0.f, O1 = 0.f;
+    int r = 0;
+    for (; r + 1 < nsplit; r += 2) {
+      O0 += __ldcg(A.part_o + (((size_t)g * kAttnMaxSplits + r) * G + j) * hd + e) * wsh[j * nsplit + r];
+      O1 += __ldcg(A.part_o + (((size_t)g * kAttnMaxSplits + r + 1) * G + j) * hd + e) * wsh[j * nsplit + r + 1];
+    }
+    if (r < nsplit) O0 += __ldcg(A.part_o + (((size_t)g * kAttnMaxSplits + r) * G + j) * hd + e) * wsh[j * nsplit + r];
+    A.out[((size_t)g * G + j) * hd + e] = (O0 + O1) * linv[j];
+  }
+  if (threadIdx.x == 0) A.cnt[g] = 0u;  // ready for the next launch
+}
+
+// ------------------------------------------------------------ lm_head
 // Orderable key for the first-max argmax: larger value wins, then the lower
 // index.  NaN and -inf never win (the reference's strict `val > max_val`
 // against a -inf start, llm/forward.rs:262-271); -0.0 ties with +0.0.
@@ -521,28 +678,156 @@ __host__ __device__ __forceinline__ unsigned amax_index(unsigned long long key) 
   return key ? 0xFFFFFFFFu - (unsigned)(key & 0xFFFFFFFFull) : 0u;
 }
 
-// Final-CTA argmax reduction shared by the lm_head kernels.
-__device__ __forceinline__ void amax_finish(unsigned long long best, unsigned long long* part,
-                                            unsigned* cnt, unsigned* result, StepParams* P) {
+struct LmArgs {
+  const float* W;      // [N][K]
+  const float* bias;   // [N] or nullptr
+  const float* x;      // input (normalised unless norm_w is set)
+  const float* norm_w; // final RMSNorm weight, or nullptr for a plain GEMV
+  float eps;
+  float* logits;       // [N] or nullptr
+  int N, K, rows_per_cta, stages;
+  unsigned long long* part;
+  unsigned* cnt;
+  unsigned* result;
+  DevState* st;        // non-null: advance the decode state
+  unsigned* tok_hist;
+  unsigned hist_cap;
+};
+
+// Ring depth for a row length K: as many 8-row stages as fit the budget.
+__host__ __device__ inline int lm_stages(int K) {
+  const size_t stage = size_t(kLmRowsPerStage) * K * 4;
+  const size_t avail = kLmSmemBudget - size_t(K) * 4;
+  int s = int(avail / stage);
+  return s > kLmMaxStages ? kLmMaxStages : s;
+}
+__host__ __device__ inline size_t lm_smem_bytes(int K, int stages) {
+  return kSmemHeader + size_t(K) * 4 + size_t(stages) * kLmRowsPerStage * K * 4;
+}
+
+// Persistent streaming GEMV: each CTA owns a contiguous row range; a producer
+// warp streams kLmRowsPerStage rows per stage into a ring of A.stages smem
+// with bulk copies (full/empty mbarrier pairs), the first stages before the
+// PDL wait; consumer warps compute one row each per stage from smem.
+__global__ void __launch_bounds__(kLmThreads) k_lmhead(LmArgs A) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem_raw);
+  uint64_t* empty = full + kLmMaxStages;
+  const int S = A.stages;
+  float* xs = reinterpret_cast<float*>(smem_raw + kSmemHeader);
+  float* ring = xs + A.K;
+  __shared__ float red[32];
   __shared__ unsigned long long wbest[32];
   __shared__ int is_last;
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int rbeg = blockIdx.x * A.rows_per_cta;
+  const int rend = min(A.N, rbeg + A.rows_per_cta);
+  const int nrows = max(0, rend - rbeg);
+  const int nstage = (nrows + kLmRowsPerStage - 1) / kLmRowsPerStage;
+  const size_t stage_floats = size_t(kLmRowsPerStage) * A.K;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < S; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, kLmConsumerWarps);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  unsigned long long best = 0ull;
+  bool timed_out = false;
+  if (wid == kLmConsumerWarps) {
+    // ---------------- producer warp
+    if (lane == 0) {
+      for (int k = 0; k < nstage; ++k) {
+        const int slot = k % S;
+        if (k >= S && !mbar_wait(empty + slot, ((k / S) - 1) & 1)) {
+          timed_out = true;
+          break;
+        }
+        const int row = rbeg + k * kLmRowsPerStage;
+        const int rows = min(kLmRowsPerStage, rend - row);
+        const uint32_t bytes = uint32_t(rows) * A.K * 4;
+        mbar_expect_tx(full + slot, bytes);
+        bulk_g2s(ring + slot * stage_floats, A.W + (size_t)row * A.K, bytes, full + slot);
+      }
+    }
+    pdl_wait();
+    pdl_trigger();
+  } else {
+    // ---------------- consumer warps
+    pdl_wait();
+    pdl_trigger();
+    const int cthreads = kLmConsumerWarps * 32;
+    if (A.norm_w) {  // output_norm RMSNorm (llm/forward.rs:28)
+      float ss = 0.f;
+      for (int i = threadIdx.x; i < A.K; i += cthreads) {
+        const float v = __ldcg(A.x + i);
+        xs[i] = v;
+        ss = fmaf(v, v, ss);
+      }
+      ss = warp_sum(ss);
+      if (lane == 0) red[wid] = ss;
+      asm volatile("bar.sync 1, %0;" ::"r"(cthreads));
+      float t = lane < kLmConsumerWarps ? red[lane] : 0.f;
+      t = warp_sum(t);
+      const float inv = 1.0f / sqrtf(t / (float)A.K + A.eps);
+      for (int i = threadIdx.x; i < A.K; i += cthreads) xs[i] = (xs[i] * inv) * A.norm_w[i];
+    } else {
+      for (int i = threadIdx.x; i < A.K; i += cthreads) xs[i] = __ldcg(A.x + i);
+    }
+    asm volatile("bar.sync 1, %0;" ::"r"(cthreads));
+    const float4* x4 = reinterpret_cast<const float4*>(xs);
+    const int K4 = A.K >> 2;
+    for (int k = 0; k < nstage; ++k) {
+      const int slot = k % S;
+      if (!mbar_wait(full + slot, (k / S) & 1)) {
+        timed_out = true;
+        break;
+      }
+      const int row = rbeg + k * kLmRowsPerStage + wid;
+      if (row < rend) {
+        const float4* w4 = reinterpret_cast<const float4*>(ring + slot * stage_floats + (size_t)wid * A.K);
+        float a0 = 0.f, a1 = 0.f;
+        for (int j = lane; j < K4; j += kWarp) {
+          const float4 u = w4[j], xv = x4[j];
+          a0 = fmaf(u.x, xv.x, a0);
+          a1 = fmaf(u.y, xv.y, a1);
+          a0 = fmaf(u.z, xv.z, a0);
+          a1 = fmaf(u.w, xv.w, a1);
+        }
+        float a = warp_sum(a0 + a1);
+        if (A.bias) a += A.bias[row];
+        if (lane == 0 && A.logits) A.logits[row] = a;
+        const unsigned long long key = amax_key(a, (unsigned)row);
+        best = key > best ? key : best;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + slot);
+    }
+  }
+  if (timed_out && lane == 0 && A.st) flag_timeout(A.st, 9);
+  // drain: never leave a bulk copy in flight into freed smem
+  if (wid == kLmConsumerWarps && lane == 0 && timed_out) {
+    for (int i = 0; i < S; ++i) mbar_wait(full + i, 0);
+  }
+  // ---------------- CTA argmax, then the last CTA finishes the job
   best = warp_max_u64(best);
   if (lane == 0) wbest[wid] = best;
   __syncthreads();
+  const int nw = blockDim.x >> 5;
   if (threadIdx.x == 0) {
     unsigned long long b = 0;
     for (int i = 0; i < nw; ++i) b = wbest[i] > b ? wbest[i] : b;
-    part[blockIdx.x] = b;
+    A.part[blockIdx.x] = b;
     __threadfence();
-    is_last = (atomicAdd(cnt, 1u) == gridDim.x - 1u);
+    is_last = (atomicAdd(A.cnt, 1u) == gridDim.x - 1u);
   }
   __syncthreads();
   if (!is_last) return;
   __threadfence();
   unsigned long long b = 0;
   for (int i = threadIdx.x; i < (int)gridDim.x; i += blockDim.x) {
-    const unsigned long long v = __ldcg(part + i);
+    const unsigned long long v = __ldcg(A.part + i);
     b = v > b ? v : b;
   }
   b = warp_max_u64(b);
@@ -553,90 +838,17 @@ __device__ __forceinline__ void amax_finish(unsigned long long best, unsigned lo
     unsigned long long r = 0;
     for (int i = 0; i < nw; ++i) r = wbest[i] > r ? wbest[i] : r;
     const unsigned idx = amax_index(r);
-    *result = idx;
-    *cnt = 0u;
-    if (P) {  // advance the decode state
-      DevState* st = P->st;
+    *A.result = idx;
+    *A.cnt = 0u;
+    if (A.st) {  // advance the decode state
+      DevState* st = A.st;
       st->argmax = idx;
       st->token = idx;
-      if (st->hist_len < P->hist_cap) P->tok_hist[st->hist_len] = idx;
+      if (st->hist_len < A.hist_cap) A.tok_hist[st->hist_len] = idx;
       st->hist_len += 1u;
       st->pos += 1u;
     }
   }
-}
-
-// FP32 GEMV core: warp per row, float4 loads with an evict-first hint (the
-// matrix is streamed once per step), x from smem.  Requires K % 4 == 0.
-__device__ __forceinline__ unsigned long long f32_rows(const float* __restrict__ W,
-                                                       const float* __restrict__ bias,
-                                                       const float* xs, int N, int K,
-                                                       float* __restrict__ logits) {
-  const int lane = threadIdx.x & 31;
-  const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int nwarps = (gridDim.x * blockDim.x) >> 5;
-  const int K4 = K >> 2;
-  const float4* x4 = reinterpret_cast<const float4*>(xs);
-  unsigned long long best = 0ull;
-  int r = gw;
-  for (; r + nwarps < N; r += 2 * nwarps) {
-    const float4* w0 = reinterpret_cast<const float4*>(W + (size_t)r * K);
-    const float4* w1 = reinterpret_cast<const float4*>(W + (size_t)(r + nwarps) * K);
-    float a = 0.f, c = 0.f;
-#pragma unroll 4
-    for (int j = lane; j < K4; j += kWarp) {
-      const float4 u = __ldcs(w0 + j), v = __ldcs(w1 + j), xv = x4[j];
-      a = fmaf(u.x, xv.x, a); a = fmaf(u.y, xv.y, a); a = fmaf(u.z, xv.z, a); a = fmaf(u.w, xv.w, a);
-      c = fmaf(v.x, xv.x, c); c = fmaf(v.y, xv.y, c); c = fmaf(v.z, xv.z, c); c = fmaf(v.w, xv.w, c);
-    }
-    a = warp_sum(a);
-    c = warp_sum(c);
-    if (bias) { a += bias[r]; c += bias[r + nwarps]; }
-    if (lane == 0 && logits) { logits[r] = a; logits[r + nwarps] = c; }
-    const unsigned long long ka = amax_key(a, r), kc = amax_key(c, r + nwarps);
-    best = ka > best ? ka : best;
-    best = kc > best ? kc : best;
-  }
-  for (; r < N; r += nwarps) {
-    const float4* w0 = reinterpret_cast<const float4*>(W + (size_t)r * K);
-    float a = 0.f;
-    for (int j = lane; j < K4; j += kWarp) {
-      const float4 u = __ldcs(w0 + j), xv = x4[j];
-      a = fmaf(u.x, xv.x, a); a = fmaf(u.y, xv.y, a); a = fmaf(u.z, xv.z, a); a = fmaf(u.w, xv.w, a);
-    }
-    a = warp_sum(a);
-    if (bias) a += bias[r];
-    if (lane == 0 && logits) logits[r] = a;
-    const unsigned long long ka = amax_key(a, r);
-    best = ka > best ? ka : best;
-  }
-  return best;
-}
-
-// Final RMSNorm + lm_head + argmax, advancing the decode state.
-__global__ void __launch_bounds__(kLmThreads) k_lmhead(StepParams P) {
-  extern __shared__ float smem[];
-  float* xs = smem;  // [d] plain layout
-  __shared__ float red[32];
-  float ss = 0.f;
-  for (int i = threadIdx.x; i < P.d; i += blockDim.x) ss = fmaf(P.x[i], P.x[i], ss);
-  ss = block_sum(ss, red);
-  const float inv = 1.0f / sqrtf(ss / (float)P.d + P.eps);
-  for (int i = threadIdx.x; i < P.d; i += blockDim.x) xs[i] = (P.x[i] * inv) * P.out_norm[i];
-  __syncthreads();
-  const unsigned long long best = f32_rows(P.lm_head, P.lm_bias, xs, P.V, P.d, P.logits);
-  amax_finish(best, P.amax_part, P.amax_cnt, &P.st->argmax, &P);
-}
-
-// Stand-alone FP32 GEMV + argmax (op-level entry point).
-__global__ void __launch_bounds__(kLmThreads) k_f32_gemv_argmax(const float* W, const float* x, int N, int K,
-                                                            float* logits, unsigned long long* part,
-                                                            unsigned* cnt, unsigned* result) {
-  extern __shared__ float smem[];
-  for (int i = threadIdx.x; i < K; i += blockDim.x) smem[i] = x[i];
-  __syncthreads();
-  const unsigned long long best = f32_rows(W, nullptr, smem, N, K, logits);
-  amax_finish(best, part, cnt, result, nullptr);
 }
 
 // ------------------------------------------------------------------ K-WTA
@@ -690,46 +902,59 @@ __global__ void __launch_bounds__(kKwtaThreads) k_kwta(float* s, int n, int k) {
 }
 
 // ---------------------------------------------------------- setup kernels
-// File blocks (20 bytes, 4-byte aligned) -> qs/sm arrays, row offset `row0`.
-__global__ void k_repack_q4(const uint32_t* __restrict__ raw, size_t nblocks, uint4* qs, uint32_t* sm) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < nblocks;
-       i += (size_t)gridDim.x * blockDim.x) {
-    const uint32_t* b = raw + i * 5;
-    sm[i] = b[0];
-    qs[i] = make_uint4(b[1], b[2], b[3], b[4]);
+// File blocks (20 bytes, 4-byte aligned, rows in file order) -> qs/sm arrays
+// in the engine's row order: dst row r takes source row perm(r).
+//   mode 0: identity
+//   mode 1: attn_qkv pairs, split RoPE:       dst 2p+s <- head*hd + i + s*hd/2
+//   mode 2: attn_qkv pairs, interleaved RoPE: dst 2p+s <- head*hd + 2i + s
+//   mode 3: ffn_gate_up pairs:                dst 2n+s <- n + s*ff
+__host__ __device__ inline int repack_src_row(int mode, int r, int hd, int ff) {
+  if (mode == 0) return r;
+  const int p = r >> 1, s = r & 1;
+  if (mode == 3) return p + s * ff;
+  const int half = hd >> 1, head = p / half, i = p - head * half;
+  return mode == 1 ? head * hd + i + s * half : head * hd + 2 * i + s;
+}
+
+__global__ void k_repack_q4(const uint32_t* __restrict__ raw, int N, int nb, int nbp, int mode, int hd, int ff,
+                            uint4* qs, uint32_t* sm) {
+  const size_t total = (size_t)N * nb;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int r = int(i / nb), b = int(i - (size_t)r * nb);
+    const uint32_t* src = raw + ((size_t)repack_src_row(mode, r, hd, ff) * nb + b) * 5;
+    sm[(size_t)r * nbp + b] = src[0];
+    qs[(size_t)r * nb + b] = make_uint4(src[1], src[2], src[3], src[4]);
   }
 }
 
 // Bit-exact dequantisation: w = fmaf(q, scale, min) (genomic.rs:298).
 __global__ void k_dequant_q4(Q4View W, float* out) {
   const size_t total = (size_t)W.N * W.K;
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
-       i += (size_t)gridDim.x * blockDim.x) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
     const size_t row = i / W.K;
     const int col = (int)(i - row * W.K);
     const int b = col >> 5, e = col & 31;
     const uint4 q = W.qs[row * W.nb + b];
-    const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
     float scale, mn;
-    unpack_sm(W.sm[row * W.nb + b], scale, mn);
-    const uint32_t word = wd[e >> 3];
+    unpack_sm(W.sm[row * W.nbp + b], scale, mn);
+    const uint32_t word = (e < 8) ? q.x : (e < 16) ? q.y : (e < 24) ? q.z : q.w;
     const int byte = (e & 7) >> 1;
     const uint32_t code = (word >> (8 * byte + 4 * (e & 1))) & 0xFu;
     out[i] = fmaf((float)code, scale, mn);
   }
 }
 
-// Op-level Q4_0 GEMV over M input vectors: grid (ctas, M).
-__global__ void __launch_bounds__(kGemvThreads) k_q4_gemv(Q4View W, const float* x, float* y) {
-  extern __shared__ float smem[];
+// Op-level Q4_0 GEMV over M > 1 input vectors: grid (ctas, M).
+__global__ void __launch_bounds__(256) k_q4_gemv(Q4View W, const float* x, float* y) {
+  extern __shared__ float xsm[];
   const float* xm = x + (size_t)blockIdx.y * W.K;
-  for (int i = threadIdx.x; i < W.K; i += blockDim.x) smem[swz(i)] = xm[i];
+  for (int i = threadIdx.x; i < W.K; i += blockDim.x) xsm[swz(i)] = xm[i];
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int nwarps = (gridDim.x * blockDim.x) >> 5;
   for (int r = gw; r < W.N; r += nwarps) {
-    const float v = q4_row(W, r, smem, lane);
+    const float v = q4_row_global(W, r, xsm, lane);
     if (lane == 0) y[(size_t)blockIdx.y * W.N + r] = v;
   }
 }
@@ -741,13 +966,6 @@ __global__ void k_rmsnorm(const float* x, const float* w, float eps, int n, floa
   ss = block_sum(ss, red);
   const float inv = 1.0f / sqrtf(ss / (float)n + eps);
   for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = (x[i] * inv) * w[i];
-}
-
-__global__ void __launch_bounds__(kAttnThreads) k_attn_op(const float* q, const float* kc, const float* vc,
-                                                      float* out, int ctx, int stride, int nh, int nkv,
-                                                      int hd, float scale, float* part_o, float* part_ml,
-                                                      unsigned* cnt) {
-  attn_core(q, kc, vc, out, ctx, stride, nh, nkv, hd, scale, part_o, part_ml, cnt);
 }
 
 }  // namespace gaje
