@@ -20,6 +20,7 @@
 
 #include "flat_format.h"
 #include "kernels.cuh"
+#include "megakernel.cuh"
 
 using namespace gaje;
 
@@ -232,8 +233,17 @@ struct gaje_model {
   int graph_kwta_k = -1, graph_block_k = -1;
   uint32_t host_pos = 0;
   Rng rng;
+  // persistent decode kernel
+  bool use_mega = false;
+  MegaPlan mplan{};
+  size_t mega_smem = 0;
+  LayerW* d_layers = nullptr;
+  unsigned* bar = nullptr;
+  unsigned long long* phase_ns = nullptr;
+  size_t phase_ns_cap = 0;
 
   ~gaje_model() {
+    if (phase_ns) cudaFree(phase_ns);
     if (graph) cudaGraphExecDestroy(graph);
     if (arena.base) cudaFree(arena.base);
     if (h_st) cudaFreeHost(h_st);
@@ -388,6 +398,48 @@ struct gaje_model {
     return cudaGetLastError();
   }
 
+  // n consecutive greedy steps, each fed the previous step's argmax (the first
+  // one fed DevState::token).  With the persistent kernel this is one launch.
+  int run_steps(size_t n, unsigned long long* stamps = nullptr) {
+    if (n == 0) return GAJE_OK;
+    if (!use_mega) {
+      for (size_t i = 0; i < n; ++i)
+        if (int s = run_step()) return s;
+      return GAJE_OK;
+    }
+    while (n > 0) {
+      const int chunk = int(std::min<size_t>(n, 1u << 16));
+      MegaArgs a;
+      a.P = P;
+      a.layers = d_layers;
+      a.plan = mplan;
+      a.bar = bar;
+      a.n_steps = chunk;
+      a.block_k = block_k();
+      a.phase_ns = stamps;
+      CK(cudaMemsetAsync(bar, 0, sizeof(unsigned), stream));
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(sms);
+      cfg.blockDim = dim3(kMkThreads);
+      cfg.dynamicSmemBytes = mega_smem;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeCooperative;
+      attr[0].val.cooperative = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      CK(cudaLaunchKernelEx(&cfg, k_decode_mega, a));
+      n -= size_t(chunk);
+      if (stamps) stamps += size_t(chunk) * (5 * L + 1);
+    }
+    const int kk = logits_k();
+    if (kk > 0) {  // masks the returned logits; the argmax is unaffected
+      k_kwta<<<1, kKwtaThreads, 0, stream>>>(logits, V, kk);
+      CK(cudaGetLastError());
+    }
+    return GAJE_OK;
+  }
+
   int run_step() {
     const int kk = logits_k(), bk = block_k();
     if (!use_graph) return launch_step(kk, bk);
@@ -422,9 +474,10 @@ struct gaje_model {
   // becomes GAJE_ERR_TIMEOUT, a NaN guard the reference's error string.
   int check_state() {
     if (h_st->err) {
-      static const char* kid[] = {"qkv", "oproj", "gateup", "down", "gemv", "", "", "", "attention", "lm_head"};
+      static const char* kid[] = {"qkv", "oproj", "gateup", "down", "gemv", "", "", "", "attention", "lm_head",
+                                  "decode (grid barrier)", "decode (producer)", "decode (consumer)"};
       const unsigned k = h_st->err - 1;
-      std::string m = std::string("a bounded device wait ran out in the ") + (k < 10 ? kid[k] : "?") + " kernel";
+      std::string m = std::string("a bounded device wait ran out in the ") + (k < 13 ? kid[k] : "?") + " kernel";
       h_st->err = 0;
       cudaMemcpyAsync(&st->err, &h_st->err, 4, cudaMemcpyHostToDevice, stream);
       cudaStreamSynchronize(stream);
@@ -501,6 +554,47 @@ std::vector<float2> rope_table(int max_ctx, int hd, float base) {
       t[size_t(pos) * half + i] = make_float2(cosf(th), sinf(th));
     }
   return t;
+}
+
+// Slot ring and work split of the persistent kernel; false when the shape does
+// not fit (the kernel-per-phase engine is used instead).
+bool plan_mega(gaje_model* m) {
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, k_decode_mega) != cudaSuccess) return false;
+  const int G = m->nh / m->nkv;
+  const int qd = m->nh * m->hd;
+  const int xs = (std::max({m->d, qd, m->ff}) + 31) / 32 * 32;
+  if (xs > kMkMaxVecPerThread * kMkConsumers) return false;
+  MegaPlan& p = m->mplan;
+  p.xs_floats = xs;
+  if (m->nkv > m->sms) return false;  // one (head, split) unit per CTA at least
+  p.attn_chunk_cap = attn_chunk_max(m->max_ctx, mk_split_cap(m->nkv, m->sms));
+  p.ps_floats = (G * p.attn_chunk_cap + 31) / 32 * 32;
+  const size_t budget = size_t(kMaxDynSmem) - fa.sharedSizeBytes - 1024;
+  const size_t base = kMkHeader + size_t(p.xs_floats) * 4 + size_t(p.ps_floats) * 4 + size_t(kMkPartFloats) * 4;
+  if (base >= budget) return false;
+  auto unit_bytes = [](const Q4Dev& q, int rpu) { return size_t(rpu) * (size_t(q.nb) * 16 + size_t(q.nbp) * 4); };
+  const size_t need = std::max({size_t(2) * p.attn_chunk_cap * m->hd * 4, unit_bytes(m->qkv[0], 2),
+                                unit_bytes(m->wo[0], 1), unit_bytes(m->gate_up[0], 2), unit_bytes(m->down[0], 1),
+                                size_t(m->d) * 4});
+  int nslots = int(std::min<size_t>(6, (budget - base) / need));
+  if (nslots < 2) return false;
+  p.nslots = nslots;
+  p.slot_bytes = unsigned((budget - base) / nslots / 128 * 128);
+  auto split = [&](MkGemv& g, const Q4Dev& q, int units, int rpu) {
+    g.units = units;
+    g.upc = (units + m->sms - 1) / m->sms;
+    const int fit = int(p.slot_bytes / unit_bytes(q, rpu));
+    g.units_per_item = std::max(1, std::min({g.upc, fit, 512 / rpu}));
+  };
+  split(p.q, m->qkv[0], m->qkv[0].N / 2, 2);
+  split(p.o, m->wo[0], m->wo[0].N, 1);
+  split(p.g, m->gate_up[0], m->gate_up[0].N / 2, 2);
+  split(p.d, m->down[0], m->down[0].N, 1);
+  p.lm_rows_per_cta = (m->V + m->sms - 1) / m->sms;
+  p.lm_stage_rows = int(std::min<size_t>(kMkConsumerWarps, p.slot_bytes / (size_t(m->d) * 4)));
+  m->mega_smem = mega_smem_bytes(p);
+  return p.lm_stage_rows >= 1 && m->mega_smem + fa.sharedSizeBytes <= size_t(kMaxDynSmem);
 }
 
 int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
@@ -580,6 +674,8 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     m->sel_out = a.take<unsigned>(1);
     m->pen_ids = a.take<unsigned>(m->max_ctx);
     m->st = a.take<DevState>(1);
+    m->bar = a.take<unsigned>(1);
+    m->d_layers = a.take<LayerW>(L);
   };
   Arena sizing;
   plan(sizing);
@@ -606,6 +702,15 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   if (int s = smem_optin((const void*)k_gemv<G_DOWN>, m->pd.smem)) return s;
   if (int s = smem_optin((const void*)k_attn, m->attn_smem)) return s;
   if (int s = smem_optin((const void*)k_lmhead, m->lm_smem)) return s;
+  m->use_mega = (!opts || opts->use_megakernel) && plan_mega(m);
+  if (m->use_mega) {
+    if (int s = smem_optin((const void*)k_decode_mega, m->mega_smem)) return s;
+    int per_sm = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_mega, kMkThreads, m->mega_smem));
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device);
+    if (per_sm < 1 || !coop) m->use_mega = false;
+  }
   // zero the counters, scratch, state and caches
   CK(cudaMemsetAsync(m->attn_cnt, 0, m->nkv * sizeof(unsigned), m->stream));
   CK(cudaMemsetAsync(m->amax_cnt, 0, sizeof(unsigned), m->stream));
@@ -633,6 +738,11 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   {
     std::vector<float2> rt = rope_table(m->max_ctx, m->hd, I.rope_base);
     CK(cudaMemcpy(m->rope, rt.data(), rt.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  }
+  {
+    std::vector<LayerW> lw(L);
+    for (size_t l = 0; l < L; ++l) lw[l] = m->layer(int(l));
+    CK(cudaMemcpy(m->d_layers, lw.data(), L * sizeof(LayerW), cudaMemcpyHostToDevice));
   }
   CK(cudaHostAlloc(&m->h_st, sizeof(DevState), cudaHostAllocDefault));
   CK(cudaHostAlloc(&m->h_tok, 64 * sizeof(unsigned), cudaHostAllocDefault));
@@ -685,6 +795,7 @@ void gaje_load_opts_init(gaje_load_opts* o) {
   o->max_ctx = 4096;
   o->seed = 0;
   o->use_graph = 1;
+  o->use_megakernel = 1;
 }
 
 gaje_model* gaje_cuda_load(const char* flat_path, const gaje_load_opts* opts) {
@@ -755,7 +866,7 @@ int gaje_cuda_forward(gaje_model* m, uint32_t token_id, int clear_cache, float* 
     return set_error(GAJE_ERR_CONTEXT, "KV cache is full (max_ctx positions)");
   m->h_tok[0] = token_id;
   CK(cudaMemcpyAsync(&m->st->token, m->h_tok, 4, cudaMemcpyHostToDevice, m->stream));
-  if (int s = m->run_step()) return s;
+  if (int s = m->run_steps(1)) return s;
   CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
   if (logits_out) CK(cudaMemcpyAsync(logits_out, m->logits, size_t(m->V) * 4, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
@@ -774,8 +885,7 @@ int gaje_cuda_decode_greedy(gaje_model* m, uint32_t first_token, size_t n_steps,
   m->h_st->hist_len = 0;
   CK(cudaMemcpyAsync(&m->st->token, &m->h_st->token, 4, cudaMemcpyHostToDevice, m->stream));
   CK(cudaMemcpyAsync(&m->st->hist_len, &m->h_st->hist_len, 4, cudaMemcpyHostToDevice, m->stream));
-  for (size_t i = 0; i < n_steps; ++i)
-    if (int s = m->run_step()) return s;
+  if (int s = m->run_steps(n_steps)) return s;
   CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
   if (tokens_out && n_steps)
     CK(cudaMemcpyAsync(tokens_out, m->tok_hist, n_steps * 4, cudaMemcpyDeviceToHost, m->stream));
@@ -808,6 +918,52 @@ int gaje_cuda_profile_steps(gaje_model* m, uint32_t first_token, size_t n_steps,
   return m->check_state();
 }
 
+int gaje_cuda_profile_phases(gaje_model* m, uint32_t first_token, size_t n_steps, float* us, float* step_us) {
+  if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  if (!m->use_mega) return set_error(GAJE_ERR_UNSUPPORTED, "the model runs on the kernel-per-phase engine");
+  CK(cudaSetDevice(m->device));
+  if (n_steps == 0) return GAJE_OK;
+  if (size_t(m->host_pos) + n_steps > size_t(m->max_ctx))
+    return set_error(GAJE_ERR_CONTEXT, "KV cache would overflow (max_ctx positions)");
+  const size_t per = size_t(5 * m->L + 1), need = n_steps * per + 1;
+  if (m->phase_ns_cap < need) {
+    if (m->phase_ns) cudaFree(m->phase_ns);
+    m->phase_ns = nullptr;
+    CK(cudaMalloc(&m->phase_ns, need * 8));
+    m->phase_ns_cap = need;
+  }
+  m->h_st->token = first_token;
+  m->h_st->hist_len = 0;
+  CK(cudaMemcpyAsync(&m->st->token, &m->h_st->token, 4, cudaMemcpyHostToDevice, m->stream));
+  CK(cudaMemcpyAsync(&m->st->hist_len, &m->h_st->hist_len, 4, cudaMemcpyHostToDevice, m->stream));
+  // stamp 0 of each launch is taken on the host side of the stream: a tiny
+  // kernel would perturb the timing, so the first phase is measured from the
+  // previous step's end (step 0 is skipped in the means)
+  if (int s = m->run_steps(n_steps, m->phase_ns)) return s;
+  std::vector<unsigned long long> ts(n_steps * per);
+  CK(cudaMemcpyAsync(ts.data(), m->phase_ns, ts.size() * 8, cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  m->host_pos += uint32_t(n_steps);
+  double acc[GAJE_PH_COUNT] = {0}, step = 0;
+  size_t counted = 0;
+  for (size_t s = 1; s < n_steps; ++s) {
+    unsigned long long prev = ts[(s - 1) * per + per - 1];
+    const unsigned long long start = prev;
+    for (size_t k = 0; k < per; ++k) {
+      const unsigned long long t = ts[s * per + k];
+      const int ph = k + 1 == per ? GAJE_PH_LMHEAD : int(k % 5);
+      acc[ph] += double(t - prev);
+      prev = t;
+    }
+    step += double(prev - start);
+    ++counted;
+  }
+  for (int k = 0; k < GAJE_PH_COUNT; ++k) us[k] = counted ? float(acc[k] / counted / 1000.0) : 0.f;
+  if (step_us) *step_us = counted ? float(step / counted / 1000.0) : 0.f;
+  return m->check_state();
+}
+
 int gaje_cuda_generate(gaje_model* m, const uint32_t* prompt, size_t n_prompt, size_t max_new,
                        float temperature, float rep_penalty, const uint32_t* eos, size_t n_eos,
                        uint32_t* out, size_t* n_out) {
@@ -823,7 +979,7 @@ int gaje_cuda_generate(gaje_model* m, const uint32_t* prompt, size_t n_prompt, s
   for (size_t i = 0; i < n_prompt; ++i) {
     m->h_tok[0] = prompt[i];
     CK(cudaMemcpyAsync(&m->st->token, m->h_tok, 4, cudaMemcpyHostToDevice, m->stream));
-    if (int s = m->run_step()) return s;
+    if (int s = m->run_steps(1)) return s;
     CK(cudaStreamSynchronize(m->stream));  // h_tok is reused
     m->host_pos += 1;
   }
@@ -878,7 +1034,7 @@ int gaje_cuda_generate(gaje_model* m, const uint32_t* prompt, size_t n_prompt, s
     if (m->host_pos >= uint32_t(m->max_ctx)) return set_error(GAJE_ERR_CONTEXT, "KV cache is full");
     m->h_tok[0] = next;
     CK(cudaMemcpyAsync(&m->st->token, m->h_tok, 4, cudaMemcpyHostToDevice, m->stream));
-    if (int s = m->run_step()) return s;
+    if (int s = m->run_steps(1)) return s;
     CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
     CK(cudaStreamSynchronize(m->stream));
     m->host_pos += 1;

@@ -482,15 +482,16 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(StepParams P, LayerW L, G
 
 // ------------------------------------------------------------ attention
 // Split bookkeeping shared by the attention kernels and the host.
-__host__ __device__ __forceinline__ void attn_splits(int ctx, int& nsplit, int& chunk) {
+__host__ __device__ __forceinline__ void attn_splits(int ctx, int& nsplit, int& chunk,
+                                                     int max_splits = kAttnMaxSplits) {
   int n0 = (ctx + kAttnMinChunk - 1) / kAttnMinChunk;
-  if (n0 > kAttnMaxSplits) n0 = kAttnMaxSplits;
+  if (n0 > max_splits) n0 = max_splits;
   if (n0 < 1) n0 = 1;
   chunk = (ctx + n0 - 1) / n0;
   nsplit = (ctx + chunk - 1) / chunk;
 }
-__host__ __device__ inline int attn_chunk_max(int max_ctx) {
-  const int c = (max_ctx + kAttnMaxSplits - 1) / kAttnMaxSplits;
+__host__ __device__ inline int attn_chunk_max(int max_ctx, int max_splits = kAttnMaxSplits) {
+  const int c = (max_ctx + max_splits - 1) / max_splits;
   return c > kAttnMinChunk ? c : kAttnMinChunk;
 }
 __host__ __device__ inline size_t attn_smem_bytes(int G, int hd, int chunk_max) {

@@ -87,7 +87,7 @@ class SynthSpec(C.Structure):
 
 class LoadOpts(C.Structure):
     _fields_ = [("device", C.c_int), ("max_ctx", C.c_uint32), ("seed", C.c_uint64),
-                ("use_graph", C.c_int)]
+                ("use_graph", C.c_int), ("use_megakernel", C.c_int)]
 
 
 class ModelInfo(C.Structure):
@@ -134,6 +134,7 @@ def lib() -> C.CDLL:
         "gaje_cuda_decode_greedy": ([vp, u32, sz, vp], i32),
         "gaje_cuda_stream": ([vp], vp),
         "gaje_cuda_profile_steps": ([vp, u32, sz, vp, vp], i32),
+        "gaje_cuda_profile_phases": ([vp, u32, sz, vp, vp], i32),
         "gaje_cuda_q4_0_upload": ([vp, sz, sz, vp, i32], vp),
         "gaje_cuda_q4_0_release": ([vp], None),
         "gaje_cuda_q4_0_gemv": ([vp, vp, vp, sz, vp], i32),
@@ -257,10 +258,11 @@ class GenomicLLM:
     """A `.gaje.flat` model resident on one GPU (the reference's RustGenomicLLM)."""
 
     def __init__(self, path: str, device: int = 0, max_ctx: int = 4096, seed: int = 0,
-                 use_graph: bool = True):
+                 use_graph: bool = True, use_megakernel: bool = True):
         opts = LoadOpts()
         lib().gaje_load_opts_init(C.byref(opts))
         opts.device, opts.max_ctx, opts.seed, opts.use_graph = device, max_ctx, seed, int(use_graph)
+        opts.use_megakernel = int(use_megakernel)
         self._m = lib().gaje_cuda_load(path.encode(), C.byref(opts))
         if not self._m:
             raise GajeIOError(2, last_error())
@@ -345,6 +347,18 @@ class GenomicLLM:
         n = np.zeros(len(self.KERNEL_CLASSES), dtype=np.uint32)
         _check(lib().gaje_cuda_profile_steps(self._m, int(first_token), int(n_steps), _ptr(ms), _ptr(n)))
         return {k: (float(ms[i]), int(n[i])) for i, k in enumerate(self.KERNEL_CLASSES)}
+
+    PHASES = ("qkv", "attn", "oproj", "gateup", "down", "lmhead")
+
+    def profile_phases(self, first_token: int, n_steps: int) -> dict:
+        """Greedy steps in the persistent kernel with a timer stamp at every grid
+        barrier: mean microseconds per step in each phase, plus "step"."""
+        us = np.zeros(len(self.PHASES), dtype=np.float32)
+        step = C.c_float(0)
+        _check(lib().gaje_cuda_profile_phases(self._m, int(first_token), int(n_steps), _ptr(us), C.byref(step)))
+        out = {k: float(us[i]) for i, k in enumerate(self.PHASES)}
+        out["step"] = float(step.value)
+        return out
 
     def generate_native_py(self, prompt_tokens: Sequence[int], max_new_tokens: int = 30,
                            temperature: float = 0.7, repetition_penalty: float = 1.0,

@@ -130,10 +130,13 @@ int gaje_flat_write_synthetic(const char* path, const gaje_synth_spec* spec);
 typedef struct gaje_model gaje_model;
 
 typedef struct gaje_load_opts {
-  int device;        /* CUDA device ordinal                                  */
-  uint32_t max_ctx;  /* KV-cache capacity in positions; 0 -> 4096             */
-  uint64_t seed;     /* sampling RNG seed for generate (temperature > 0)      */
-  int use_graph;     /* 1 (default): replay the decode step as a CUDA graph   */
+  int device;         /* CUDA device ordinal                                  */
+  uint32_t max_ctx;   /* KV-cache capacity in positions; 0 -> 4096             */
+  uint64_t seed;      /* sampling RNG seed for generate (temperature > 0)      */
+  int use_graph;      /* kernel-per-phase engine: replay each step as a CUDA
+                         graph (1, default) or launch kernel by kernel (0)    */
+  int use_megakernel; /* 1 (default): one persistent cooperative kernel runs
+                         whole decode steps; 0: one kernel per phase          */
 } gaje_load_opts;
 void gaje_load_opts_init(gaje_load_opts* opts);
 
@@ -200,6 +203,19 @@ enum gaje_kernel_class {
  * GAJE_PROFILE_VERBOSE timing of src/nn/llm/forward.rs:23-55. */
 int gaje_cuda_profile_steps(gaje_model* model, uint32_t first_token, size_t n_steps,
                             float* ms, uint32_t* launches);
+
+/* Phases of a megakernel step, for gaje_cuda_profile_phases. */
+enum gaje_phase {
+  GAJE_PH_QKV = 0, GAJE_PH_ATTN = 1, GAJE_PH_OPROJ = 2, GAJE_PH_GATEUP = 3, GAJE_PH_DOWN = 4,
+  GAJE_PH_LMHEAD = 5, GAJE_PH_COUNT = 6
+};
+/* Runs n_steps greedy steps in the persistent decode kernel with a
+ * %globaltimer stamp at every grid barrier, and writes the mean microseconds
+ * per step spent in each phase (summed over the blocks) into us[GAJE_PH_COUNT]
+ * and the whole-step mean into *step_us.  GAJE_ERR_UNSUPPORTED when the model
+ * runs on the kernel-per-phase engine. */
+int gaje_cuda_profile_phases(gaje_model* model, uint32_t first_token, size_t n_steps,
+                             float* us, float* step_us);
 
 /* ---------------------------------------------------------------- op level */
 /* Device-pointer entry points for the isolated kernel checks and sweeps.

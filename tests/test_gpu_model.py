@@ -19,15 +19,19 @@ def _rel(a, b):
     return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
 
 
+ENGINES = [pytest.param(True, id="mega"), pytest.param(False, id="phase")]
+
+
 def _pair(g, O, path, **kw):
     gpu = g.load_genomic_auto(path, device=0, max_ctx=kw.pop("max_ctx", 1024), **kw)
     ref = O.OracleModel(path)
     return gpu, ref
 
 
+@pytest.mark.parametrize("mega", ENGINES)
 @pytest.mark.parametrize("name", ["tiny", "small"])
-def test_logits_and_greedy_stream_small_models(g, O, make_model, name):
-    gpu, ref = _pair(g, O, make_model(name, seed=3))
+def test_logits_and_greedy_stream_small_models(g, O, make_model, name, mega):
+    gpu, ref = _pair(g, O, make_model(name, seed=3), use_megakernel=mega)
     gpu.set_k_wta_ratio(0.0)
     ref.set_k_wta_ratio(0.0)
     rng = np.random.default_rng(5)
@@ -49,9 +53,10 @@ def test_logits_and_greedy_stream_small_models(g, O, make_model, name):
     assert gpu.cache_len == ref.cache_len == len(prompt) + 64
 
 
-def test_default_kwta_after_load_matches(g, O, make_model):
+@pytest.mark.parametrize("mega", ENGINES)
+def test_default_kwta_after_load_matches(g, O, make_model, mega):
     """load_genomic leaves k_wta_ratio = 0.5 on the logits (flat_reader.rs:234)."""
-    gpu, ref = _pair(g, O, make_model("small", seed=4))
+    gpu, ref = _pair(g, O, make_model("small", seed=4), use_megakernel=mega)
     assert abs(gpu.k_wta_ratio - 0.5) < 1e-7
     for i, t in enumerate([5, 99, 1234, 7]):
         lg, lr = gpu.forward(t, i == 0), ref.forward(t, i == 0)
@@ -64,9 +69,10 @@ def test_default_kwta_after_load_matches(g, O, make_model):
         assert masked_r.sum() == gpu.vocab_size - gpu.vocab_size // 2
 
 
-def test_block_kwta_after_set_ratio(g, O, make_model):
+@pytest.mark.parametrize("mega", ENGINES)
+def test_block_kwta_after_set_ratio(g, O, make_model, mega):
     """set_k_wta_ratio also sets every block's ratio (llm/python.rs:53-59)."""
-    gpu, ref = _pair(g, O, make_model("tiny", seed=6))
+    gpu, ref = _pair(g, O, make_model("tiny", seed=6), use_megakernel=mega)
     gpu.set_k_wta_ratio(0.75)
     ref.set_k_wta_ratio(0.75)
     for i, t in enumerate([1, 2, 3]):
@@ -75,9 +81,10 @@ def test_block_kwta_after_set_ratio(g, O, make_model):
         assert _rel(lg[keep], lr[keep]) <= REL_TOL
 
 
+@pytest.mark.parametrize("mega", ENGINES)
 @pytest.mark.parametrize("penalty", [1.0, 1.5])
-def test_generate_greedy_matches_oracle(g, O, make_model, penalty):
-    gpu, ref = _pair(g, O, make_model("small", seed=8))
+def test_generate_greedy_matches_oracle(g, O, make_model, penalty, mega):
+    gpu, ref = _pair(g, O, make_model("small", seed=8), use_megakernel=mega)
     for m in (gpu, ref):
         m.set_k_wta_ratio(0.0)
     prompt = [11, 22, 33, 44, 55]
@@ -111,10 +118,11 @@ def test_generate_sampling_seeded(g, O, make_model, seed):
     assert a == b
 
 
-def test_decode_greedy_device_loop_equals_host_loop(g, make_model):
+@pytest.mark.parametrize("mega", ENGINES)
+def test_decode_greedy_device_loop_equals_host_loop(g, make_model, mega):
     path = make_model("small", seed=12)
-    a = g.load_genomic_auto(path, max_ctx=512)
-    b = g.load_genomic_auto(path, max_ctx=512, use_graph=False)
+    a = g.load_genomic_auto(path, max_ctx=512, use_megakernel=mega)
+    b = g.load_genomic_auto(path, max_ctx=512, use_graph=False, use_megakernel=False)
     for m in (a, b):
         m.set_k_wta_ratio(0.0)
         m.clear_cache_py()
@@ -141,7 +149,8 @@ def test_context_overflow_is_an_error(g, make_model):
     assert m.cache_len == 1
 
 
-def test_nan_guard_reports_reference_message(g, O, tmp_path):
+@pytest.mark.parametrize("mega", ENGINES)
+def test_nan_guard_reports_reference_message(g, O, tmp_path, mega):
     """A NaN in blk.1.ffn_norm poisons x_ffn_n -> up -> "NaN in up" (block 1),
     the first guard block/forward.rs hits (:97-99)."""
     import flat_numpy
@@ -157,7 +166,7 @@ def test_nan_guard_reports_reference_message(g, O, tmp_path):
         t2.append(t)
     p = str(tmp_path / "nan.flat")
     flat_numpy.write_flat(p, tensors=t2, **meta)
-    gpu, ref = _pair(g, O, p)
+    gpu, ref = _pair(g, O, p, use_megakernel=mega)
     with pytest.raises(ValueError) as eo:
         ref.forward(3, True)
     with pytest.raises(ValueError) as eg:
@@ -167,12 +176,13 @@ def test_nan_guard_reports_reference_message(g, O, tmp_path):
     assert "block 1" in eg.value.message
 
 
-@pytest.mark.parametrize("name,steps", [("smollm2-135m", 64), ("qwen2-0.5b", 64)])
-def test_baseline_configs_parity(g, O, make_model, name, steps):
+@pytest.mark.parametrize("name,steps,mega", [("smollm2-135m", 64, True), ("smollm2-135m", 64, False),
+                                             ("qwen2-0.5b", 64, True)])
+def test_baseline_configs_parity(g, O, make_model, name, steps, mega):
     """The BASELINE shapes: 16 prompt tokens then `steps` greedy steps, logits
     every step within 1e-3 and the identical greedy stream."""
     path = make_model(name, seed=1234)
-    gpu, ref = _pair(g, O, path, max_ctx=512)
+    gpu, ref = _pair(g, O, path, max_ctx=512, use_megakernel=mega)
     gpu.set_k_wta_ratio(0.0)
     ref.set_k_wta_ratio(0.0)
     rng = np.random.default_rng(7)
@@ -194,3 +204,40 @@ def test_baseline_configs_parity(g, O, make_model, name, steps):
     print(f"{name}: max rel logit err {worst:.2e}, min top1-top2 margin {min(margins):.2e}")
     assert worst <= REL_TOL
     assert sg == sr
+
+
+def test_engines_agree_and_phase_profile(g, make_model):
+    """The persistent kernel and the kernel-per-phase engine give the same
+    greedy stream; the phase profile accounts for the whole step."""
+    path = make_model("smollm2-135m", seed=1234)
+    a = g.load_genomic_auto(path, max_ctx=512, use_megakernel=True)
+    b = g.load_genomic_auto(path, max_ctx=512, use_megakernel=False)
+    for m in (a, b):
+        m.set_k_wta_ratio(0.0)
+        m.clear_cache_py()
+    ta, tb = a.decode_greedy(123, 48), b.decode_greedy(123, 48)
+    assert ta == tb
+    a.clear_cache_py()
+    prof = a.profile_phases(123, 16)
+    parts = sum(v for k, v in prof.items() if k != "step")
+    assert prof["step"] > 0 and abs(parts - prof["step"]) <= 0.02 * prof["step"] + 1.0
+    with pytest.raises(ValueError):
+        b.profile_phases(1, 2)
+
+
+def test_megakernel_long_context_splits(g, O, make_model):
+    """Contexts past 64 splits x 32 positions (chunks grow beyond 32) and the
+    split cap of heads x splits <= CTAs, on a 3-KV-head model."""
+    path = make_model("small", seed=21, n_embd=384, n_head=6, n_head_kv=3)
+    gpu, ref = _pair(g, O, path, max_ctx=2600, use_megakernel=True)
+    gpu.set_k_wta_ratio(0.0)
+    ref.set_k_wta_ratio(0.0)
+    worst = 0.0
+    for i in range(2200):
+        t = (i * 7919) % gpu.vocab_size
+        lr = ref.forward(t, i == 0)
+        if i % 100 == 99 or i >= 2190:
+            worst = max(worst, _rel(gpu.forward(t), lr))
+        else:
+            gpu.forward_argmax(t, i == 0)
+    assert worst <= REL_TOL
