@@ -276,7 +276,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> None:
     first3 = prefill()
     mega = True
     try:
-        phases = model.profile_phases(first3, prof_steps)
+        phases = model.profile_phases(first3, prof_steps, detail=True)
     except ValueError:
         mega = False
     if mega:
@@ -285,7 +285,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> None:
         k_gbs, k_bytes, k_ms = step_gbs, sb_mean["total"], step_ms_dev
         launches = 1
         lm_us = phases["lmhead"]
-        breakdown = {k: round(v, 2) for k, v in phases.items()}
+        breakdown = {k: (round(v, 2) if not isinstance(v, dict) else v) for k, v in phases.items()}
         breakdown_unit = "us per step (grid-barrier stamps, CTA 0)"
     else:
         prof = model.profile_steps(first3, prof_steps)

@@ -238,12 +238,17 @@ struct gaje_model {
   MegaPlan mplan{};
   size_t mega_smem = 0;
   LayerW* d_layers = nullptr;
-  unsigned* bar = nullptr;
+  LLBufs ll{};
+  size_t ll_words = 0;
+  unsigned epoch = 0;  // LL epochs used so far (the next launch starts after it)
   unsigned long long* phase_ns = nullptr;
   size_t phase_ns_cap = 0;
+  unsigned long long* detail_ns = nullptr;
+  size_t detail_ns_cap = 0;
 
   ~gaje_model() {
     if (phase_ns) cudaFree(phase_ns);
+    if (detail_ns) cudaFree(detail_ns);
     if (graph) cudaGraphExecDestroy(graph);
     if (arena.base) cudaFree(arena.base);
     if (h_st) cudaFreeHost(h_st);
@@ -400,7 +405,7 @@ struct gaje_model {
 
   // n consecutive greedy steps, each fed the previous step's argmax (the first
   // one fed DevState::token).  With the persistent kernel this is one launch.
-  int run_steps(size_t n, unsigned long long* stamps = nullptr) {
+  int run_steps(size_t n, unsigned long long* stamps = nullptr, unsigned long long* detail = nullptr) {
     if (n == 0) return GAJE_OK;
     if (!use_mega) {
       for (size_t i = 0; i < n; ++i)
@@ -409,15 +414,22 @@ struct gaje_model {
     }
     while (n > 0) {
       const int chunk = int(std::min<size_t>(n, 1u << 16));
+      const unsigned long long per = (unsigned long long)chunk * unsigned(5 * L + 1);
+      if ((unsigned long long)epoch + per >= 0xFFFFFFF0ull) {  // epochs wrap: restart from clean words
+        CK(cudaMemsetAsync(ll.xa, 0, ll_words * sizeof(uint2), stream));
+        epoch = 0;
+      }
       MegaArgs a;
       a.P = P;
       a.layers = d_layers;
       a.plan = mplan;
-      a.bar = bar;
+      a.ll = ll;
+      a.epoch0 = epoch;
       a.n_steps = chunk;
       a.block_k = block_k();
       a.phase_ns = stamps;
-      CK(cudaMemsetAsync(bar, 0, sizeof(unsigned), stream));
+      a.detail_ns = detail;
+      epoch += unsigned(per);
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(sms);
       cfg.blockDim = dim3(kMkThreads);
@@ -431,6 +443,7 @@ struct gaje_model {
       CK(cudaLaunchKernelEx(&cfg, k_decode_mega, a));
       n -= size_t(chunk);
       if (stamps) stamps += size_t(chunk) * (5 * L + 1);
+      if (detail) detail += size_t(chunk) * L * 5 * kMkDetail;
     }
     const int kk = logits_k();
     if (kk > 0) {  // masks the returned logits; the argmax is unaffected
@@ -564,19 +577,20 @@ bool plan_mega(gaje_model* m) {
   const int G = m->nh / m->nkv;
   const int qd = m->nh * m->hd;
   const int xs = (std::max({m->d, qd, m->ff}) + 31) / 32 * 32;
-  if (xs > kMkMaxVecPerThread * kMkConsumers) return false;
+  if (m->d > kMkMaxNormVec * kMkConsumers || qd != m->d) return false;
   MegaPlan& p = m->mplan;
   p.xs_floats = xs;
   if (m->nkv > m->sms) return false;  // one (head, split) unit per CTA at least
   p.attn_chunk_cap = attn_chunk_max(m->max_ctx, mk_split_cap(m->nkv, m->sms));
   p.ps_floats = (G * p.attn_chunk_cap + 31) / 32 * 32;
   const size_t budget = size_t(kMaxDynSmem) - fa.sharedSizeBytes - 1024;
-  const size_t base = kMkHeader + size_t(p.xs_floats) * 4 + size_t(p.ps_floats) * 4 + size_t(kMkPartFloats) * 4;
+  p.nslots = 0;
+  p.slot_bytes = 0;
+  const size_t base = mega_smem_bytes(p, m->d, m->hd);
   if (base >= budget) return false;
   auto unit_bytes = [](const Q4Dev& q, int rpu) { return size_t(rpu) * (size_t(q.nb) * 16 + size_t(q.nbp) * 4); };
-  const size_t need = std::max({size_t(2) * p.attn_chunk_cap * m->hd * 4, unit_bytes(m->qkv[0], 2),
-                                unit_bytes(m->wo[0], 1), unit_bytes(m->gate_up[0], 2), unit_bytes(m->down[0], 1),
-                                size_t(m->d) * 4});
+  const size_t need = std::max({unit_bytes(m->qkv[0], 2), unit_bytes(m->wo[0], 1), unit_bytes(m->gate_up[0], 2),
+                                unit_bytes(m->down[0], 1), size_t(m->d) * 4});
   int nslots = int(std::min<size_t>(6, (budget - base) / need));
   if (nslots < 2) return false;
   p.nslots = nslots;
@@ -593,7 +607,7 @@ bool plan_mega(gaje_model* m) {
   split(p.d, m->down[0], m->down[0].N, 1);
   p.lm_rows_per_cta = (m->V + m->sms - 1) / m->sms;
   p.lm_stage_rows = int(std::min<size_t>(kMkConsumerWarps, p.slot_bytes / (size_t(m->d) * 4)));
-  m->mega_smem = mega_smem_bytes(p);
+  m->mega_smem = mega_smem_bytes(p, m->d, m->hd);
   return p.lm_stage_rows >= 1 && m->mega_smem + fa.sharedSizeBytes <= size_t(kMaxDynSmem);
 }
 
@@ -674,8 +688,18 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     m->sel_out = a.take<unsigned>(1);
     m->pen_ids = a.take<unsigned>(m->max_ctx);
     m->st = a.take<DevState>(1);
-    m->bar = a.take<unsigned>(1);
     m->d_layers = a.take<LayerW>(L);
+    // LL exchange words of the persistent kernel, one contiguous range
+    const size_t qd = size_t(m->nh) * m->hd, kvd = size_t(m->nkv) * m->hd;
+    m->ll_words = 2 * d + qd + 2 * kvd + qd + size_t(m->ff) + 1;
+    uint2* llb = a.take<uint2>(m->ll_words);
+    m->ll.xa = llb;
+    m->ll.xb = llb + d;
+    m->ll.q = llb + 2 * d;
+    m->ll.kv = m->ll.q + qd;
+    m->ll.attn = m->ll.kv + 2 * kvd;
+    m->ll.act = m->ll.attn + qd;
+    m->ll.tok = m->ll.act + m->ff;
   };
   Arena sizing;
   plan(sizing);
@@ -713,6 +737,7 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   }
   // zero the counters, scratch, state and caches
   CK(cudaMemsetAsync(m->attn_cnt, 0, m->nkv * sizeof(unsigned), m->stream));
+  CK(cudaMemsetAsync(m->ll.xa, 0, m->ll_words * sizeof(uint2), m->stream));
   CK(cudaMemsetAsync(m->amax_cnt, 0, sizeof(unsigned), m->stream));
   CK(cudaMemsetAsync(m->kcache, 0, L * size_t(m->nkv) * m->max_ctx * m->hd * 4, m->stream));
   CK(cudaMemsetAsync(m->vcache, 0, L * size_t(m->nkv) * m->max_ctx * m->hd * 4, m->stream));
@@ -918,7 +943,8 @@ int gaje_cuda_profile_steps(gaje_model* m, uint32_t first_token, size_t n_steps,
   return m->check_state();
 }
 
-int gaje_cuda_profile_phases(gaje_model* m, uint32_t first_token, size_t n_steps, float* us, float* step_us) {
+int gaje_cuda_profile_phases(gaje_model* m, uint32_t first_token, size_t n_steps, float* us, float* step_us,
+                             float* detail_us) {
   if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
   if (!m->use_mega) return set_error(GAJE_ERR_UNSUPPORTED, "the model runs on the kernel-per-phase engine");
   CK(cudaSetDevice(m->device));
@@ -932,6 +958,13 @@ int gaje_cuda_profile_phases(gaje_model* m, uint32_t first_token, size_t n_steps
     CK(cudaMalloc(&m->phase_ns, need * 8));
     m->phase_ns_cap = need;
   }
+  const size_t dper = size_t(m->L) * 5 * kMkDetail, dneed = n_steps * dper;
+  if (detail_us && m->detail_ns_cap < dneed) {
+    if (m->detail_ns) cudaFree(m->detail_ns);
+    m->detail_ns = nullptr;
+    CK(cudaMalloc(&m->detail_ns, dneed * 8));
+    m->detail_ns_cap = dneed;
+  }
   m->h_st->token = first_token;
   m->h_st->hist_len = 0;
   CK(cudaMemcpyAsync(&m->st->token, &m->h_st->token, 4, cudaMemcpyHostToDevice, m->stream));
@@ -939,9 +972,11 @@ int gaje_cuda_profile_phases(gaje_model* m, uint32_t first_token, size_t n_steps
   // stamp 0 of each launch is taken on the host side of the stream: a tiny
   // kernel would perturb the timing, so the first phase is measured from the
   // previous step's end (step 0 is skipped in the means)
-  if (int s = m->run_steps(n_steps, m->phase_ns)) return s;
-  std::vector<unsigned long long> ts(n_steps * per);
+  if (detail_us) CK(cudaMemsetAsync(m->detail_ns, 0, dneed * 8, m->stream));
+  if (int s = m->run_steps(n_steps, m->phase_ns, detail_us ? m->detail_ns : nullptr)) return s;
+  std::vector<unsigned long long> ts(n_steps * per), ds(detail_us ? dneed : 0);
   CK(cudaMemcpyAsync(ts.data(), m->phase_ns, ts.size() * 8, cudaMemcpyDeviceToHost, m->stream));
+  if (detail_us) CK(cudaMemcpyAsync(ds.data(), m->detail_ns, ds.size() * 8, cudaMemcpyDeviceToHost, m->stream));
   CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
   m->host_pos += uint32_t(n_steps);
@@ -961,6 +996,25 @@ int gaje_cuda_profile_phases(gaje_model* m, uint32_t first_token, size_t n_steps
   }
   for (int k = 0; k < GAJE_PH_COUNT; ++k) us[k] = counted ? float(acc[k] / counted / 1000.0) : 0.f;
   if (step_us) *step_us = counted ? float(step / counted / 1000.0) : 0.f;
+  if (detail_us) {
+    // per phase: [start, 4 in-phase stamps, barrier end] -> 5 intervals
+    double dacc[25] = {0};
+    for (size_t st = 1; st < n_steps; ++st)
+      for (int l = 0; l < m->L; ++l)
+        for (int ph = 0; ph < 5; ++ph) {
+          const size_t k = st * per + size_t(l) * 5 + ph;
+          unsigned long long pts[6];
+          pts[0] = ts[k - 1];
+          for (int j = 0; j < kMkDetail; ++j) pts[1 + j] = ds[((st * m->L + l) * 5 + ph) * kMkDetail + j];
+          pts[5] = ts[k];
+          for (int j = 0; j < 5; ++j) {  // a missing stamp (no work) counts as zero time
+            const unsigned long long a = pts[j], b = pts[j + 1];
+            if (a && b && b >= a) dacc[ph * 5 + j] += double(b - a);
+            else if (a && !b) pts[j + 1] = a;
+          }
+        }
+    for (int i = 0; i < 25; ++i) detail_us[i] = counted ? float(dacc[i] / counted / 1000.0) : 0.f;
+  }
   return m->check_state();
 }
 

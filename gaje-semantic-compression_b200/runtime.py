@@ -134,7 +134,7 @@ def lib() -> C.CDLL:
         "gaje_cuda_decode_greedy": ([vp, u32, sz, vp], i32),
         "gaje_cuda_stream": ([vp], vp),
         "gaje_cuda_profile_steps": ([vp, u32, sz, vp, vp], i32),
-        "gaje_cuda_profile_phases": ([vp, u32, sz, vp, vp], i32),
+        "gaje_cuda_profile_phases": ([vp, u32, sz, vp, vp, vp], i32),
         "gaje_cuda_q4_0_upload": ([vp, sz, sz, vp, i32], vp),
         "gaje_cuda_q4_0_release": ([vp], None),
         "gaje_cuda_q4_0_gemv": ([vp, vp, vp, sz, vp], i32),
@@ -350,14 +350,22 @@ class GenomicLLM:
 
     PHASES = ("qkv", "attn", "oproj", "gateup", "down", "lmhead")
 
-    def profile_phases(self, first_token: int, n_steps: int) -> dict:
+    DETAIL = ("to_act", "to_slot", "to_rows", "to_done", "to_barrier")
+
+    def profile_phases(self, first_token: int, n_steps: int, detail: bool = False) -> dict:
         """Greedy steps in the persistent kernel with a timer stamp at every grid
-        barrier: mean microseconds per step in each phase, plus "step"."""
+        barrier: mean microseconds per step in each phase, plus "step"; with
+        detail, the in-phase intervals of CTA 0 under "detail"."""
         us = np.zeros(len(self.PHASES), dtype=np.float32)
+        det = np.zeros(25, dtype=np.float32)
         step = C.c_float(0)
-        _check(lib().gaje_cuda_profile_phases(self._m, int(first_token), int(n_steps), _ptr(us), C.byref(step)))
+        _check(lib().gaje_cuda_profile_phases(self._m, int(first_token), int(n_steps), _ptr(us), C.byref(step),
+                                              _ptr(det) if detail else None))
         out = {k: float(us[i]) for i, k in enumerate(self.PHASES)}
         out["step"] = float(step.value)
+        if detail:
+            out["detail"] = {self.PHASES[p]: {self.DETAIL[j]: round(float(det[p * 5 + j]), 3) for j in range(5)}
+                             for p in range(5)}
         return out
 
     def generate_native_py(self, prompt_tokens: Sequence[int], max_new_tokens: int = 30,

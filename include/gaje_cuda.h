@@ -212,10 +212,17 @@ enum gaje_phase {
 /* Runs n_steps greedy steps in the persistent decode kernel with a
  * %globaltimer stamp at every grid barrier, and writes the mean microseconds
  * per step spent in each phase (summed over the blocks) into us[GAJE_PH_COUNT]
- * and the whole-step mean into *step_us.  GAJE_ERR_UNSUPPORTED when the model
- * runs on the kernel-per-phase engine. */
+ * and the whole-step mean into *step_us.  detail_us (nullable) receives, for
+ * each block phase p < 5, five means in microseconds per step:
+ *   [p*5+0] phase start -> activations in shared memory
+ *   [p*5+1] -> first staged weight (or K/V) slot ready
+ *   [p*5+2] -> first slot's rows computed
+ *   [p*5+3] -> phase work done
+ *   [p*5+4] -> grid barrier passed
+ * measured on CTA 0.  GAJE_ERR_UNSUPPORTED when the model runs on the
+ * kernel-per-phase engine. */
 int gaje_cuda_profile_phases(gaje_model* model, uint32_t first_token, size_t n_steps,
-                             float* us, float* step_us);
+                             float* us, float* step_us, float* detail_us);
 
 /* ---------------------------------------------------------------- op level */
 /* Device-pointer entry points for the isolated kernel checks and sweeps.
