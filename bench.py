@@ -348,6 +348,25 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_ncu_case(args) -> None:
+    """Two launches of the persistent kernel on one GPU: PROMPT_LEN greedy steps
+    (the context a bench step sees), then args.steps steps, the launch a
+    profiler captures.  No timing: numbers taken under a profiler are not bench
+    values."""
+    import torch
+
+    g = _pkg()
+    torch.cuda.set_device(0)
+    path = _ensure_model(g, args.config, SEED, 0, None)
+    model = g.load_genomic_auto(path, device=0, max_ctx=PROMPT_LEN + args.steps + 64)
+    model.set_k_wta_ratio(0.0)
+    model.clear_cache_py()
+    t = model.decode_greedy(5, PROMPT_LEN)[-1]
+    toks = model.decode_greedy(t, args.steps)
+    print(json.dumps({"ncu_case": args.config, "context": PROMPT_LEN, "steps": args.steps,
+                      "last_token": int(toks[-1])}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -356,6 +375,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default=CONFIG_KEY)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ncu-case", action="store_true",
+                    help="the small profiling case: one launch filling the prompt's positions, then one "
+                         "launch of --steps decode steps (capture it with -k regex:k_decode_mega -s 1 -c 1)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -364,6 +386,9 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.ncu_case:
+        run_ncu_case(args)
         return
     dist = None
     if world > 1:

@@ -243,12 +243,12 @@ struct gaje_model {
   unsigned epoch = 0;  // LL epochs used so far (the next launch starts after it)
   unsigned long long* phase_ns = nullptr;
   size_t phase_ns_cap = 0;
-  unsigned long long* detail_ns = nullptr;
-  size_t detail_ns_cap = 0;
+  unsigned long long* trace_ns = nullptr;
+  size_t trace_ns_cap = 0;
 
   ~gaje_model() {
     if (phase_ns) cudaFree(phase_ns);
-    if (detail_ns) cudaFree(detail_ns);
+    if (trace_ns) cudaFree(trace_ns);
     if (graph) cudaGraphExecDestroy(graph);
     if (arena.base) cudaFree(arena.base);
     if (h_st) cudaFreeHost(h_st);
@@ -405,7 +405,8 @@ struct gaje_model {
 
   // n consecutive greedy steps, each fed the previous step's argmax (the first
   // one fed DevState::token).  With the persistent kernel this is one launch.
-  int run_steps(size_t n, unsigned long long* stamps = nullptr, unsigned long long* detail = nullptr) {
+  // `trace` (every CTA's in-phase stamps) is only taken when n fits one launch.
+  int run_steps(size_t n, unsigned long long* stamps = nullptr, unsigned long long* trace = nullptr) {
     if (n == 0) return GAJE_OK;
     if (!use_mega) {
       for (size_t i = 0; i < n; ++i)
@@ -428,7 +429,7 @@ struct gaje_model {
       a.n_steps = chunk;
       a.block_k = block_k();
       a.phase_ns = stamps;
-      a.detail_ns = detail;
+      a.trace_ns = chunk == int(n) ? trace : nullptr;
       epoch += unsigned(per);
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(sms);
@@ -443,7 +444,6 @@ struct gaje_model {
       CK(cudaLaunchKernelEx(&cfg, k_decode_mega, a));
       n -= size_t(chunk);
       if (stamps) stamps += size_t(chunk) * (5 * L + 1);
-      if (detail) detail += size_t(chunk) * L * 5 * kMkDetail;
     }
     const int kk = logits_k();
     if (kk > 0) {  // masks the returned logits; the argmax is unaffected
@@ -855,6 +855,8 @@ int gaje_cuda_model_info(gaje_model* m, gaje_model_info* o) {
   o->rope_base = m->info.rope_base;
   o->k_wta_ratio = m->k_wta_ratio;
   o->device_bytes = m->arena.size;
+  o->grid = uint32_t(m->sms);
+  o->megakernel = m->use_mega ? 1u : 0u;
   return GAJE_OK;
 }
 
@@ -943,14 +945,17 @@ int gaje_cuda_profile_steps(gaje_model* m, uint32_t first_token, size_t n_steps,
   return m->check_state();
 }
 
-int gaje_cuda_profile_phases(gaje_model* m, uint32_t first_token, size_t n_steps, float* us, float* step_us,
-                             float* detail_us) {
-  if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+// Runs n_steps greedy steps in one launch of the persistent kernel with the
+// phase stamps of CTA 0 (stamps, [n_steps][5L+1]) and, when trace is non-null,
+// every CTA's in-phase stamps ([grid][n_steps][5L+1][kMkTrace]) copied to the
+// host vectors.
+static int mega_stamped_run(gaje_model* m, uint32_t first_token, size_t n_steps, bool want_trace,
+                            std::vector<unsigned long long>& ts, std::vector<unsigned long long>* tr) {
   if (!m->use_mega) return set_error(GAJE_ERR_UNSUPPORTED, "the model runs on the kernel-per-phase engine");
   CK(cudaSetDevice(m->device));
-  if (n_steps == 0) return GAJE_OK;
   if (size_t(m->host_pos) + n_steps > size_t(m->max_ctx))
     return set_error(GAJE_ERR_CONTEXT, "KV cache would overflow (max_ctx positions)");
+  if (want_trace && n_steps > 4096) return set_error(GAJE_ERR_INVALID, "a trace covers at most 4096 steps");
   const size_t per = size_t(5 * m->L + 1), need = n_steps * per + 1;
   if (m->phase_ns_cap < need) {
     if (m->phase_ns) cudaFree(m->phase_ns);
@@ -958,28 +963,40 @@ int gaje_cuda_profile_phases(gaje_model* m, uint32_t first_token, size_t n_steps
     CK(cudaMalloc(&m->phase_ns, need * 8));
     m->phase_ns_cap = need;
   }
-  const size_t dper = size_t(m->L) * 5 * kMkDetail, dneed = n_steps * dper;
-  if (detail_us && m->detail_ns_cap < dneed) {
-    if (m->detail_ns) cudaFree(m->detail_ns);
-    m->detail_ns = nullptr;
-    CK(cudaMalloc(&m->detail_ns, dneed * 8));
-    m->detail_ns_cap = dneed;
+  const size_t tneed = want_trace ? size_t(m->sms) * n_steps * per * kMkTrace : 0;
+  if (want_trace && m->trace_ns_cap < tneed) {
+    if (m->trace_ns) cudaFree(m->trace_ns);
+    m->trace_ns = nullptr;
+    CK(cudaMalloc(&m->trace_ns, tneed * 8));
+    m->trace_ns_cap = tneed;
   }
   m->h_st->token = first_token;
   m->h_st->hist_len = 0;
   CK(cudaMemcpyAsync(&m->st->token, &m->h_st->token, 4, cudaMemcpyHostToDevice, m->stream));
   CK(cudaMemcpyAsync(&m->st->hist_len, &m->h_st->hist_len, 4, cudaMemcpyHostToDevice, m->stream));
-  // stamp 0 of each launch is taken on the host side of the stream: a tiny
-  // kernel would perturb the timing, so the first phase is measured from the
-  // previous step's end (step 0 is skipped in the means)
-  if (detail_us) CK(cudaMemsetAsync(m->detail_ns, 0, dneed * 8, m->stream));
-  if (int s = m->run_steps(n_steps, m->phase_ns, detail_us ? m->detail_ns : nullptr)) return s;
-  std::vector<unsigned long long> ts(n_steps * per), ds(detail_us ? dneed : 0);
+  if (want_trace) CK(cudaMemsetAsync(m->trace_ns, 0, tneed * 8, m->stream));
+  if (int s = m->run_steps(n_steps, m->phase_ns, want_trace ? m->trace_ns : nullptr)) return s;
+  ts.assign(n_steps * per, 0ull);
   CK(cudaMemcpyAsync(ts.data(), m->phase_ns, ts.size() * 8, cudaMemcpyDeviceToHost, m->stream));
-  if (detail_us) CK(cudaMemcpyAsync(ds.data(), m->detail_ns, ds.size() * 8, cudaMemcpyDeviceToHost, m->stream));
+  if (want_trace) {
+    tr->assign(tneed, 0ull);
+    CK(cudaMemcpyAsync(tr->data(), m->trace_ns, tneed * 8, cudaMemcpyDeviceToHost, m->stream));
+  }
   CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
   CK(cudaStreamSynchronize(m->stream));
   m->host_pos += uint32_t(n_steps);
+  return m->check_state();
+}
+
+int gaje_cuda_profile_phases(gaje_model* m, uint32_t first_token, size_t n_steps, float* us, float* step_us,
+                             float* detail_us) {
+  if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  if (n_steps == 0) return GAJE_OK;
+  std::vector<unsigned long long> ts, tr;
+  if (int s = mega_stamped_run(m, first_token, n_steps, detail_us != nullptr, ts, &tr)) return s;
+  const size_t per = size_t(5 * m->L + 1);
+  // the first phase of a launch has no start stamp (a kernel to take one
+  // would perturb the timing): step 0 is skipped in the means
   double acc[GAJE_PH_COUNT] = {0}, step = 0;
   size_t counted = 0;
   for (size_t s = 1; s < n_steps; ++s) {
@@ -997,25 +1014,39 @@ int gaje_cuda_profile_phases(gaje_model* m, uint32_t first_token, size_t n_steps
   for (int k = 0; k < GAJE_PH_COUNT; ++k) us[k] = counted ? float(acc[k] / counted / 1000.0) : 0.f;
   if (step_us) *step_us = counted ? float(step / counted / 1000.0) : 0.f;
   if (detail_us) {
-    // per phase: [start, 4 in-phase stamps, barrier end] -> 5 intervals
-    double dacc[25] = {0};
+    // CTA 0, per phase kind: [previous phase done, 5 trace points] -> 5
+    // intervals; a missing point (no work of that kind) counts as zero time
+    double dacc[GAJE_PH_COUNT * kMkTrace] = {0};
     for (size_t st = 1; st < n_steps; ++st)
-      for (int l = 0; l < m->L; ++l)
-        for (int ph = 0; ph < 5; ++ph) {
-          const size_t k = st * per + size_t(l) * 5 + ph;
-          unsigned long long pts[6];
-          pts[0] = ts[k - 1];
-          for (int j = 0; j < kMkDetail; ++j) pts[1 + j] = ds[((st * m->L + l) * 5 + ph) * kMkDetail + j];
-          pts[5] = ts[k];
-          for (int j = 0; j < 5; ++j) {  // a missing stamp (no work) counts as zero time
-            const unsigned long long a = pts[j], b = pts[j + 1];
-            if (a && b && b >= a) dacc[ph * 5 + j] += double(b - a);
-            else if (a && !b) pts[j + 1] = a;
-          }
+      for (size_t k = 0; k < per; ++k) {
+        const int ph = k + 1 == per ? GAJE_PH_LMHEAD : int(k % 5);
+        unsigned long long pts[kMkTrace + 1];
+        pts[0] = ts[st * per + k - 1];
+        for (int j = 0; j < kMkTrace; ++j) pts[1 + j] = tr[(st * per + k) * kMkTrace + j];
+        for (int j = 0; j < kMkTrace; ++j) {
+          const unsigned long long a = pts[j], b = pts[j + 1];
+          if (a && b && b >= a) dacc[ph * kMkTrace + j] += double(b - a);
+          else if (a && !b) pts[j + 1] = a;
         }
-    for (int i = 0; i < 25; ++i) detail_us[i] = counted ? float(dacc[i] / counted / 1000.0) : 0.f;
+      }
+    for (int i = 0; i < GAJE_PH_COUNT * kMkTrace; ++i)
+      detail_us[i] = counted ? float(dacc[i] / counted / 1000.0) : 0.f;
   }
-  return m->check_state();
+  return GAJE_OK;
+}
+
+int gaje_cuda_trace_steps(gaje_model* m, uint32_t first_token, size_t n_steps, uint64_t* out, size_t out_len,
+                          size_t* n_written) {
+  if (!m || !n_written || (out_len && !out)) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  *n_written = 0;
+  if (n_steps == 0) return GAJE_OK;
+  const size_t need = size_t(m->sms) * n_steps * size_t(5 * m->L + 1) * kMkTrace;
+  if (out_len < need) return set_error(GAJE_ERR_INVALID, "trace buffer too small: need grid*n_steps*(5L+1)*5 words");
+  std::vector<unsigned long long> ts, tr;
+  if (int s = mega_stamped_run(m, first_token, n_steps, true, ts, &tr)) return s;
+  std::memcpy(out, tr.data(), need * 8);
+  *n_written = need;
+  return GAJE_OK;
 }
 
 int gaje_cuda_generate(gaje_model* m, const uint32_t* prompt, size_t n_prompt, size_t max_new,

@@ -53,9 +53,10 @@ constexpr int kMkHeader = 1024;       // mbarriers + flags
 constexpr int kMkPartFloats = 1024;   // split-K partials / row sums
 constexpr int kMkRound = 8;           // LL words per consumer thread per read round
 constexpr int kMkMaxNormVec = 4;      // norm weights per thread (d <= 1920)
-// In-phase profile points (CTA 0): 0 activations ready, 1 first slot ready,
-// 2 first slot's rows done, 3 phase done.
-constexpr int kMkDetail = 4;
+// Trace points of a phase, per CTA: 0 entry, 1 inputs arrived, 2 inputs
+// staged (attention: cached K/V landed), 3 first weight slot taken
+// (attention: split partials published), 4 done (outputs published).
+constexpr int kMkTrace = 5;
 
 // The vectors exchanged between phases, as {bits, epoch} words.
 struct LLBufs {
@@ -91,7 +92,7 @@ struct MegaArgs {
   int n_steps;
   int block_k;           // block K-WTA k (0 = off)
   unsigned long long* phase_ns;   // optional [n_steps][5*L+1] phase-done stamps (CTA 0)
-  unsigned long long* detail_ns;  // optional [n_steps][L][5][kMkDetail] (CTA 0)
+  unsigned long long* trace_ns;   // optional [grid][n_steps][5*L+1][kMkTrace] (every CTA)
 };
 
 // Epoch of the words phase `ph` (0..4) of block l publishes in step s; the
@@ -471,9 +472,9 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
     if (A.phase_ns && blockIdx.x == 0 && tid == 0)
       A.phase_ns[(size_t)step * (5 * L + 1) + k] = global_ns();
   };
-  auto dmark = [&](int step, int l, int ph, int k) {
-    if (A.detail_ns && blockIdx.x == 0 && tid == 0)
-      A.detail_ns[(((size_t)step * L + l) * 5 + ph) * kMkDetail + k] = global_ns();
+  auto tmark = [&](int step, int l, int ph, int k) {
+    if (A.trace_ns && tid == 0)
+      A.trace_ns[(((size_t)blockIdx.x * A.n_steps + step) * (5 * L + 1) + 5 * l + ph) * kMkTrace + k] = global_ns();
   };
   // one staged GEMV phase: items of this CTA's units, rows -> rowsum, epilogue per item
   auto gemv_phase = [&](const MkGemv& gp, const Q4View& W, int rpu, int step, int l, int ph,
@@ -484,9 +485,8 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
       const int b = min(u1, a + gp.units_per_item);
       const unsigned char* slot = take(A, S, item);
       if (!slot) return false;
-      if (a == u0) dmark(step, l, ph, 1);
+      if (a == u0) tmark(step, l, ph, 3);
       mk_rows(S, slot, (b - a) * rpu, W.nb, W.nbp, rowsum);
-      if (a == u0) dmark(step, l, ph, 2);
       release(A, S, item++);
       epilogue(a, b);
       consumer_sync();  // rowsum is reused by the next item
@@ -514,6 +514,7 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
                      e_gu = e_qkv + 3, e_down = e_qkv + 4;
       // ================================================ QKV
       if (has_q || has_o || au >= 0) {
+        tmark(step, l, 0, 0);
         // constant inputs first: norm weights, the RoPE row
         float wreg[kMkMaxNormVec];
 #pragma unroll
@@ -556,6 +557,7 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
           ok = ll_read(A.ll.xb, d, mk_epoch(A.epoch0, L, step, l - 1, 4), S.xraw, ss, bad);
         }
         if (!agree(S, ok, st)) return;
+        tmark(step, l, 0, 1);
         if (A.block_k > 0 && l > 0) {  // the previous block's K-WTA (block/forward.rs:145-149)
           mk_block_kwta(S.xraw, d, A.block_k, hist);
           ss = 0.f;
@@ -588,7 +590,7 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
                      S.kv_bar);
           }
         }
-        dmark(step, l, 0, 0);
+        tmark(step, l, 0, 2);
         const bool done = !has_q || gemv_phase(pl.q, Lw.qkv, 2, step, l, 0, [&](int a, int b) {
           for (int u = a + tid; u < b; u += kMkConsumers) {
             float y0 = rowsum[(u - a) * 2], y1 = rowsum[(u - a) * 2 + 1];
@@ -613,11 +615,12 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
           }
         });
         if (!done) return;
-        dmark(step, l, 0, 3);
+        tmark(step, l, 0, 4);
         mark(step, 5 * l + 0);
       }
       // ================================================ ATTN
       if (au >= 0) {
+        tmark(step, l, 1, 0);
         const int g = au % P.nkv, s = au / P.nkv, t0 = s * chunk;
         const int n = min(ctx, t0 + chunk) - t0;
         const int n_old = max(0, min(n, ctx - 1 - t0));
@@ -639,13 +642,13 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
               Lw.vc[((size_t)g * P.max_ctx + pos) * hd + i] = Vs[(size_t)n_old * hd + i];
             }
         }
-        dmark(step, l, 1, 0);
+        tmark(step, l, 1, 1);
         // every consumer observes the copy's completion (parity of this use)
         const int use = *S.kv_waited;
         if (ok && !mbar_wait(S.kv_bar, use & 1)) ok = false;
         if (!agree(S, ok, st)) return;
         if (tid == 0) *S.kv_waited = use + 1;
-        dmark(step, l, 1, 1);
+        tmark(step, l, 1, 2);
         float* ps = S.ps;
         for (int idx = tid; idx < G * n; idx += kMkConsumers) {
           const int j = idx / n, t = idx - j * n;
@@ -698,7 +701,7 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
         }
         __threadfence();  // partials and the new cache row before the arrival
         consumer_sync();
-        dmark(step, l, 1, 2);
+        tmark(step, l, 1, 3);
         if (tid == 0) is_last = (atomicAdd(P.attn_cnt + g, 1u) == (unsigned)nsplit - 1u);
         consumer_sync();
         if (is_last) {
@@ -739,19 +742,21 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
           }
         }
         consumer_sync();
-        dmark(step, l, 1, 3);
+        tmark(step, l, 1, 4);
       }
       mark(step, 5 * l + 1);
       // ================================================ OPROJ
       if (has_o) {
+        tmark(step, l, 2, 0);
         float ss = 0.f;
         int bad = 0;
         const bool ok = ll_read(A.ll.attn, Lw.wo.K, e_attn, S.xraw, ss, bad);
         if (!agree(S, ok, st)) return;
+        tmark(step, l, 2, 1);
         int bo = 0;
         mk_stage_x(S, Lw.wo.K, nullptr, 1.0f, false, bo);
         consumer_sync();
-        dmark(step, l, 2, 0);
+        tmark(step, l, 2, 2);
         const bool done = gemv_phase(pl.o, Lw.wo, 1, step, l, 2, [&](int a, int b) {
           for (int r = a + tid; r < b; r += kMkConsumers) {
             float y = rowsum[r - a];
@@ -760,11 +765,12 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
           }
         });
         if (!done) return;
-        dmark(step, l, 2, 3);
+        tmark(step, l, 2, 4);
         mark(step, 5 * l + 2);
       }
       // ================================================ GATEUP
       if (has_g || has_d) {
+        tmark(step, l, 3, 0);
         float wreg[kMkMaxNormVec];
 #pragma unroll
         for (int k = 0; k < kMkMaxNormVec; ++k) {
@@ -775,13 +781,14 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
         int bad = 0;
         const bool ok = ll_read(A.ll.xa, d, e_o, S.xraw, ss, bad);
         if (!agree(S, ok, st)) return;
+        tmark(step, l, 3, 1);
         for (int i = tid; i < d; i += kMkConsumers) S.xres[i] = S.xraw[i];
         const float tot = consumer_sum(ss, red);
         const float inv = 1.0f / sqrtf(tot / (float)d + P.eps);
         int bo = 0;
         mk_stage_x(S, d, wreg, inv, true, bo);
         consumer_sync();
-        dmark(step, l, 3, 0);
+        tmark(step, l, 3, 2);
         const bool done = !has_g || gemv_phase(pl.g, Lw.gate_up, 2, step, l, 3, [&](int a, int b) {
           for (int u = a + tid; u < b; u += kMkConsumers) {
             float gv = rowsum[(u - a) * 2], uv = rowsum[(u - a) * 2 + 1];
@@ -796,15 +803,17 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
           }
         });
         if (!done) return;
-        dmark(step, l, 3, 3);
+        tmark(step, l, 3, 4);
         mark(step, 5 * l + 3);
       }
       // ================================================ DOWN
       if (has_d) {
+        tmark(step, l, 4, 0);
         float ss = 0.f;
         int bad = 0;
         const bool ok = ll_read(A.ll.act, P.ff, e_gu, S.xraw, ss, bad);
         if (!agree(S, ok, st)) return;
+        tmark(step, l, 4, 1);
         float scale = 1.0f;
         if (P.use_genomic_norm) {  // block/forward.rs:115-123, h_scale = 1
           const float tot = consumer_sum(ss, red);
@@ -817,7 +826,7 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
         consumer_sync();
         mk_stage_x(S, P.ff, nullptr, 1.0f, false, bo);
         consumer_sync();
-        dmark(step, l, 4, 0);
+        tmark(step, l, 4, 2);
         const bool done = gemv_phase(pl.d, Lw.down, 1, step, l, 4, [&](int a, int b) {
           for (int r = a + tid; r < b; r += kMkConsumers) {
             float y = rowsum[r - a];
@@ -829,12 +838,13 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
           }
         });
         if (!done) return;
-        dmark(step, l, 4, 3);
+        tmark(step, l, 4, 4);
         mark(step, 5 * l + 4);
       }
     }
     // ================================================== LM
     {
+      tmark(step, L, 0, 0);
       float wreg[kMkMaxNormVec];
 #pragma unroll
       for (int k = 0; k < kMkMaxNormVec; ++k) {
@@ -845,6 +855,7 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
       int bad = 0;
       const bool ok = ll_read(A.ll.xb, d, mk_epoch(A.epoch0, L, step, L - 1, 4), S.xraw, ss, bad);
       if (!agree(S, ok, st)) return;
+      tmark(step, L, 0, 1);
       if (A.block_k > 0) {  // the last block's K-WTA
         mk_block_kwta(S.xraw, d, A.block_k, hist);
         ss = 0.f;
@@ -857,6 +868,7 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
         for (int i = tid; i < d; i += kMkConsumers, ++k) S.xs[i] = (S.xraw[i] * inv) * wreg[k];  // plain layout
       }
       consumer_sync();
+      tmark(step, L, 0, 2);
       const float4* x4 = reinterpret_cast<const float4*>(S.xs);
       const int K4 = d >> 2;
       unsigned long long best = 0ull;
@@ -866,6 +878,7 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
         const int rows = min(pl.lm_stage_rows, rend - r);
         const unsigned char* slot = take(A, S, item);
         if (!slot) return;
+        if (r == rbeg) tmark(step, L, 0, 3);
         for (int rr = wid; rr < rows; rr += kMkConsumerWarps) {
           const float4* w4 = reinterpret_cast<const float4*>(slot) + (size_t)rr * K4;
           float a0 = 0.f, a1 = 0.f;
@@ -921,6 +934,7 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
         }
       }
       consumer_sync();
+      tmark(step, L, 0, 4);
       mark(step, 5 * L);
     }
   }

@@ -95,7 +95,7 @@ class ModelInfo(C.Structure):
                 ("n_head_kv", C.c_uint32), ("n_blocks", C.c_uint32), ("head_dim", C.c_uint32),
                 ("ffn_dim", C.c_uint32), ("max_ctx", C.c_uint32), ("cache_len", C.c_uint32),
                 ("eps", C.c_float), ("rope_base", C.c_float), ("k_wta_ratio", C.c_float),
-                ("device_bytes", C.c_size_t)]
+                ("device_bytes", C.c_size_t), ("grid", C.c_uint32), ("megakernel", C.c_uint32)]
 
 
 _lib = None
@@ -135,6 +135,7 @@ def lib() -> C.CDLL:
         "gaje_cuda_stream": ([vp], vp),
         "gaje_cuda_profile_steps": ([vp, u32, sz, vp, vp], i32),
         "gaje_cuda_profile_phases": ([vp, u32, sz, vp, vp, vp], i32),
+        "gaje_cuda_trace_steps": ([vp, u32, sz, vp, sz, vp], i32),
         "gaje_cuda_q4_0_upload": ([vp, sz, sz, vp, i32], vp),
         "gaje_cuda_q4_0_release": ([vp], None),
         "gaje_cuda_q4_0_gemv": ([vp, vp, vp, sz, vp], i32),
@@ -350,14 +351,14 @@ class GenomicLLM:
 
     PHASES = ("qkv", "attn", "oproj", "gateup", "down", "lmhead")
 
-    DETAIL = ("to_act", "to_slot", "to_rows", "to_done", "to_barrier")
+    DETAIL = ("to_entry", "to_inputs", "to_staged", "to_slot", "to_done")
 
     def profile_phases(self, first_token: int, n_steps: int, detail: bool = False) -> dict:
         """Greedy steps in the persistent kernel with a timer stamp at every grid
         barrier: mean microseconds per step in each phase, plus "step"; with
         detail, the in-phase intervals of CTA 0 under "detail"."""
         us = np.zeros(len(self.PHASES), dtype=np.float32)
-        det = np.zeros(25, dtype=np.float32)
+        det = np.zeros(len(self.PHASES) * 5, dtype=np.float32)
         step = C.c_float(0)
         _check(lib().gaje_cuda_profile_phases(self._m, int(first_token), int(n_steps), _ptr(us), C.byref(step),
                                               _ptr(det) if detail else None))
@@ -365,7 +366,19 @@ class GenomicLLM:
         out["step"] = float(step.value)
         if detail:
             out["detail"] = {self.PHASES[p]: {self.DETAIL[j]: round(float(det[p * 5 + j]), 3) for j in range(5)}
-                             for p in range(5)}
+                             for p in range(len(self.PHASES))}
+        return out
+
+    def trace_steps(self, first_token: int, n_steps: int) -> np.ndarray:
+        """Every CTA's trace stamps (ns) of n_steps greedy steps in one launch:
+        shape [grid, n_steps, 5*n_blocks+1, 5] (points: entry, inputs arrived,
+        staged, first slot, done; 0 where a CTA had no work in that phase)."""
+        inf = self.info()
+        per = 5 * inf.n_blocks + 1
+        out = np.zeros((inf.grid, int(n_steps), per, 5), dtype=np.uint64)
+        n = C.c_size_t(0)
+        _check(lib().gaje_cuda_trace_steps(self._m, int(first_token), int(n_steps), _ptr(out), C.c_size_t(out.size),
+                                           C.byref(n)))
         return out
 
     def generate_native_py(self, prompt_tokens: Sequence[int], max_new_tokens: int = 30,

@@ -153,6 +153,8 @@ typedef struct gaje_model_info {
   uint32_t max_ctx, cache_len;
   float eps, rope_base, k_wta_ratio;
   size_t device_bytes; /* weights + KV cache + scratch held on the device */
+  uint32_t grid;        /* CTAs of the persistent kernel (one per SM) */
+  uint32_t megakernel;  /* 1 when steps run in the persistent kernel */
 } gaje_model_info;
 int gaje_cuda_model_info(gaje_model* model, gaje_model_info* info);
 
@@ -209,20 +211,32 @@ enum gaje_phase {
   GAJE_PH_QKV = 0, GAJE_PH_ATTN = 1, GAJE_PH_OPROJ = 2, GAJE_PH_GATEUP = 3, GAJE_PH_DOWN = 4,
   GAJE_PH_LMHEAD = 5, GAJE_PH_COUNT = 6
 };
-/* Runs n_steps greedy steps in the persistent decode kernel with a
- * %globaltimer stamp at every grid barrier, and writes the mean microseconds
- * per step spent in each phase (summed over the blocks) into us[GAJE_PH_COUNT]
- * and the whole-step mean into *step_us.  detail_us (nullable) receives, for
- * each block phase p < 5, five means in microseconds per step:
- *   [p*5+0] phase start -> activations in shared memory
- *   [p*5+1] -> first staged weight (or K/V) slot ready
- *   [p*5+2] -> first slot's rows computed
- *   [p*5+3] -> phase work done
- *   [p*5+4] -> grid barrier passed
- * measured on CTA 0.  GAJE_ERR_UNSUPPORTED when the model runs on the
- * kernel-per-phase engine. */
+/* Runs n_steps greedy steps in one launch of the persistent decode kernel
+ * with a %globaltimer stamp at the end of every phase on CTA 0, and writes the
+ * mean microseconds per step spent in each phase (summed over the blocks) into
+ * us[GAJE_PH_COUNT] and the whole-step mean into *step_us.  detail_us
+ * (nullable, GAJE_PH_COUNT*5 floats) receives, per phase kind p, the mean
+ * microseconds per step CTA 0 spent between consecutive trace points:
+ *   [p*5+0] previous phase done -> phase entered
+ *   [p*5+1] -> inputs arrived (attention: q and the new k/v rows)
+ *   [p*5+2] -> inputs staged in shared memory (attention: cached K/V landed)
+ *   [p*5+3] -> first weight slot taken (attention: split partials published)
+ *   [p*5+4] -> phase outputs published
+ * GAJE_ERR_UNSUPPORTED when the model runs on the kernel-per-phase engine.
+ * The reference's counterpart is the GAJE_PROFILE_VERBOSE timing of
+ * src/nn/llm/forward.rs:23-55. */
 int gaje_cuda_profile_phases(gaje_model* model, uint32_t first_token, size_t n_steps,
                              float* us, float* step_us, float* detail_us);
+
+/* The raw form of the above for every CTA: n_steps (<= 4096) greedy steps in
+ * one launch; out[((cta*n_steps + step)*(5L+1) + 5l+p)*5 + k] is the
+ * %globaltimer value (ns) of trace point k (the order above) of phase p of
+ * block l (the lm_head phase at 5L) on that CTA, 0 where the CTA had no work of
+ * that phase.  out_len must be at least grid*n_steps*(5L+1)*5 (grid =
+ * gaje_model_info.grid); *n_written receives the count.  No counterpart in the
+ * reference: a diagnostic of the persistent kernel's critical path. */
+int gaje_cuda_trace_steps(gaje_model* model, uint32_t first_token, size_t n_steps,
+                          uint64_t* out, size_t out_len, size_t* n_written);
 
 /* ---------------------------------------------------------------- op level */
 /* Device-pointer entry points for the isolated kernel checks and sweeps.
