@@ -488,9 +488,10 @@ struct gaje_model {
   int check_state() {
     if (h_st->err) {
       static const char* kid[] = {"qkv", "oproj", "gateup", "down", "gemv", "", "", "", "attention", "lm_head",
-                                  "decode (grid barrier)", "decode (producer)", "decode (consumer)"};
+                                  "decode (exchange word)", "decode (producer)", "decode (weight slot)",
+                                  "decode (exchange vector)", "decode (publication flag)"};
       const unsigned k = h_st->err - 1;
-      std::string m = std::string("a bounded device wait ran out in the ") + (k < 13 ? kid[k] : "?") + " kernel";
+      std::string m = std::string("a bounded device wait ran out in the ") + (k < 15 ? kid[k] : "?") + " kernel";
       h_st->err = 0;
       cudaMemcpyAsync(&st->err, &h_st->err, 4, cudaMemcpyHostToDevice, stream);
       cudaStreamSynchronize(stream);
@@ -581,8 +582,18 @@ bool plan_mega(gaje_model* m) {
   MegaPlan& p = m->mplan;
   p.xs_floats = xs;
   if (m->nkv > m->sms) return false;  // one (head, split) unit per CTA at least
-  p.attn_chunk_cap = attn_chunk_max(m->max_ctx, mk_split_cap(m->nkv, m->sms));
+  if (m->hd % 32 != 0) return false;  // attention rows are read in whole warps
+  p.max_splits = mk_split_cap(m->nkv, m->sms);
+  p.attn_chunk_cap = mk_chunk_cap(m->max_ctx, p.max_splits);
   p.ps_floats = (G * p.attn_chunk_cap + 31) / 32 * 32;
+  p.qbuf_floats = G * m->hd;
+  p.layers_bytes = int((size_t(m->L) * sizeof(LayerW) + 15) / 16 * 16);
+  {  // the most bias rows one CTA holds in one GEMV phase
+    auto rows = [&](int units, int rpu) { return (units + m->sms - 1) / m->sms * rpu; };
+    const int r = std::max({rows(m->qkv[0].N / 2, 2), rows(m->wo[0].N, 1), rows(m->gate_up[0].N / 2, 2),
+                            rows(m->down[0].N, 1)});
+    p.bias_floats = (r + 31) / 32 * 32;
+  }
   const size_t budget = size_t(kMaxDynSmem) - fa.sharedSizeBytes - 1024;
   p.nslots = 0;
   p.slot_bytes = 0;
@@ -691,15 +702,18 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     m->d_layers = a.take<LayerW>(L);
     // LL exchange words of the persistent kernel, one contiguous range
     const size_t qd = size_t(m->nh) * m->hd, kvd = size_t(m->nkv) * m->hd;
-    m->ll_words = 2 * d + qd + 2 * kvd + qd + size_t(m->ff) + 1;
+    // the persistent kernel's split cap (plan_mega sets the same value)
+    const size_t apart = size_t(m->nh) * mk_split_cap(m->nkv, m->sms) * (m->hd + 2);
+    m->ll_words = 2 * d + qd + 2 * kvd + apart + size_t(m->ff) + 1 + size_t(kFlCount) * m->sms;
     uint2* llb = a.take<uint2>(m->ll_words);
     m->ll.xa = llb;
     m->ll.xb = llb + d;
     m->ll.q = llb + 2 * d;
     m->ll.kv = m->ll.q + qd;
-    m->ll.attn = m->ll.kv + 2 * kvd;
-    m->ll.act = m->ll.attn + qd;
+    m->ll.apart = m->ll.kv + 2 * kvd;
+    m->ll.act = m->ll.apart + apart;
     m->ll.tok = m->ll.act + m->ff;
+    m->ll.flags = m->ll.tok + 1;
   };
   Arena sizing;
   plan(sizing);
@@ -1014,22 +1028,23 @@ int gaje_cuda_profile_phases(gaje_model* m, uint32_t first_token, size_t n_steps
   for (int k = 0; k < GAJE_PH_COUNT; ++k) us[k] = counted ? float(acc[k] / counted / 1000.0) : 0.f;
   if (step_us) *step_us = counted ? float(step / counted / 1000.0) : 0.f;
   if (detail_us) {
-    // CTA 0, per phase kind: [previous phase done, 5 trace points] -> 5
+    // CTA 0, per phase kind: [previous phase done, trace points 0-4] -> 5
     // intervals; a missing point (no work of that kind) counts as zero time
-    double dacc[GAJE_PH_COUNT * kMkTrace] = {0};
+    constexpr int kPts = 5;
+    double dacc[GAJE_PH_COUNT * kPts] = {0};
     for (size_t st = 1; st < n_steps; ++st)
       for (size_t k = 0; k < per; ++k) {
         const int ph = k + 1 == per ? GAJE_PH_LMHEAD : int(k % 5);
-        unsigned long long pts[kMkTrace + 1];
+        unsigned long long pts[kPts + 1];
         pts[0] = ts[st * per + k - 1];
-        for (int j = 0; j < kMkTrace; ++j) pts[1 + j] = tr[(st * per + k) * kMkTrace + j];
-        for (int j = 0; j < kMkTrace; ++j) {
+        for (int j = 0; j < kPts; ++j) pts[1 + j] = tr[(st * per + k) * kMkTrace + j];
+        for (int j = 0; j < kPts; ++j) {
           const unsigned long long a = pts[j], b = pts[j + 1];
-          if (a && b && b >= a) dacc[ph * kMkTrace + j] += double(b - a);
+          if (a && b && b >= a) dacc[ph * kPts + j] += double(b - a);
           else if (a && !b) pts[j + 1] = a;
         }
       }
-    for (int i = 0; i < GAJE_PH_COUNT * kMkTrace; ++i)
+    for (int i = 0; i < GAJE_PH_COUNT * kPts; ++i)
       detail_us[i] = counted ? float(dacc[i] / counted / 1000.0) : 0.f;
   }
   return GAJE_OK;
@@ -1041,7 +1056,7 @@ int gaje_cuda_trace_steps(gaje_model* m, uint32_t first_token, size_t n_steps, u
   *n_written = 0;
   if (n_steps == 0) return GAJE_OK;
   const size_t need = size_t(m->sms) * n_steps * size_t(5 * m->L + 1) * kMkTrace;
-  if (out_len < need) return set_error(GAJE_ERR_INVALID, "trace buffer too small: need grid*n_steps*(5L+1)*5 words");
+  if (out_len < need) return set_error(GAJE_ERR_INVALID, "trace buffer too small: need grid*n_steps*(5L+1)*6 words");
   std::vector<unsigned long long> ts, tr;
   if (int s = mega_stamped_run(m, first_token, n_steps, true, ts, &tr)) return s;
   std::memcpy(out, tr.data(), need * 8);

@@ -4,9 +4,8 @@
 //
 // Phases of a step, per block l:
 //   QKV     attn_norm RMSNorm + attn_qkv GEMV + RoPE        -> q, new k/v
-//   ATTN    split-K flash decode; the last CTA of a KV head
-//           combines the splits                              -> attention out
-//   OPROJ   attn_output GEMV + residual                      -> x_a
+//   ATTN    split-K flash decode, one CTA per (KV head, split) -> split partials
+//   OPROJ   combine of the split partials + attn_output GEMV + residual -> x_a
 //   GATEUP  ffn_norm RMSNorm + ffn_gate_up GEMV + SwiGLU     -> act
 //   DOWN    ffn_down GEMV + residual                         -> x_b (next block's x)
 // then LM: output_norm + f32 lm_head GEMV + argmax            -> next token.
@@ -16,8 +15,9 @@
 // access, so a reader that sees the expected epoch also has the value.  A CTA
 // starts a phase as soon as the words it needs carry the phase's epoch (a
 // bounded spin); the all-to-all dependencies between phases order the reuse of
-// each buffer.  Data that is not LL (KV-cache rows, split partials, argmax
-// partials) is ordered by release/acquire fences around the LL traffic.
+// each buffer.  The KV-cache rows (written by the attention CTA that owns the
+// step's position, read a step or more later by TMA) and the argmax partials
+// are ordered by fences.
 //
 // Warp roles: warps 0-14 compute ("consumers"); lane 0 of warp 15 is a
 // producer that walks this CTA's static schedule of weight "items" (the rows
@@ -27,7 +27,24 @@
 // consumers, so the next phases' weights are in flight while the consumers
 // wait for activations.  The cached K/V rows of a CTA's attention split are
 // fetched by the consumers themselves (TMA, at the start of the block's QKV
-// phase), once the previous step's rows are known to be written.
+// phase).
+//
+// A phase on a CTA: warp 0 polls the publication flags of the CTAs that write
+// the phase's input (the other warps wait on a named barrier), every consumer
+// reads its share of the input words once and stages them in shared memory,
+// one consumer barrier, the GEMV rows with no barrier, then warp 0 waits for
+// the others' arrival (they do not wait) and raises this CTA's flag.  A warp
+// passes the next phase's gate only after every warp finished this phase's
+// rows, which is what lets the staged input be overwritten.
+//
+// RMSNorm is applied as x*w when staging and
+// the 1/rms factor multiplies the finished row dot (the norm is linear in x),
+// so staging is a single pass.  GEMV rows are taken by a warp per task: a
+// row, or a row pair where the epilogue needs both rows (a RoPE pair, a
+// gate/up pair; the pair shares its activation loads), lanes over the blocks,
+// a shuffle reduction; a task's blocks are split over S warps with a
+// shared-memory sum when a CTA has few long rows.  A lane's blocks form a
+// serial dependency chain, so the mapping spends lanes before blocks.
 //
 // Q4_0 row dots (the AVX2 kernel's arithmetic, genomic.rs:267-336, factored):
 // y = sum_b scale_b * A_b + min_b * X_b with A_b = sum_k q_k x_k and
@@ -37,8 +54,9 @@
 // 2^-p, so (f - 2^23) * x' = q * x exactly; the subtract and the FMA run as
 // packed f32x2 instructions.
 //
-// Every wait is bounded (kWaitNs); a wait that runs out sets DevState::err,
-// the CTA stops, drains its in-flight copies (bounded) and exits.
+// Every wait is bounded (kWaitNs); a wait that runs out sets DevState::err and
+// the CTA's abort flag; the consumers leave together at their next barrier,
+// the producer drains its in-flight copies (bounded) and exits.
 #pragma once
 
 #include "kernels.cuh"
@@ -50,24 +68,34 @@ constexpr int kMkConsumerWarps = 15;
 constexpr int kMkConsumers = kMkConsumerWarps * 32;
 constexpr int kMkMaxSlots = 8;
 constexpr int kMkHeader = 1024;       // mbarriers + flags
-constexpr int kMkPartFloats = 1024;   // split-K partials / row sums
-constexpr int kMkRound = 8;           // LL words per consumer thread per read round
+constexpr int kMkPartFloats = 1024;   // split-K partials of a GEMV item
+constexpr int kMkRound = 12;          // LL words per consumer thread per read round
 constexpr int kMkMaxNormVec = 4;      // norm weights per thread (d <= 1920)
-// Trace points of a phase, per CTA: 0 entry, 1 inputs arrived, 2 inputs
-// staged (attention: cached K/V landed), 3 first weight slot taken
-// (attention: split partials published), 4 done (outputs published).
-constexpr int kMkTrace = 5;
+constexpr int kMkMinChunk = 64;       // positions per attention split (minimum)
+constexpr int kMkCombine = 4;         // attention splits combined per read round
+// Trace points of a phase, per CTA: 0 entry, 1 input flags seen, 2 input
+// staged (attention: cached K/V landed), 3 rows done (attention: scores
+// done), 4 outputs published, 5 first weight slot ready.
+constexpr int kMkTrace = 6;
 
 // The vectors exchanged between phases, as {bits, epoch} words.
 struct LLBufs {
-  uint2* xa;    // [d] after the attention residual
-  uint2* xb;    // [d] after the FFN residual (the next block's input)
-  uint2* q;     // [nh*hd] rotated q
-  uint2* kv;    // [2][nkv*hd] this step's k (rotated) and v rows
-  uint2* attn;  // [nh*hd] attention output
-  uint2* act;   // [ff] SwiGLU output
-  uint2* tok;   // [1] the step's argmax (bits = token id)
+  uint2* xa;     // [d] after the attention residual
+  uint2* xb;     // [d] after the FFN residual (the next block's input)
+  uint2* q;      // [nh*hd] rotated q
+  uint2* kv;     // [2][nkv*hd] this step's k (rotated) and v rows
+  uint2* apart;  // [nkv][max_splits][G][hd+2] attention split partials: o (unnormalised), m, l
+  uint2* act;    // [ff] SwiGLU output
+  uint2* tok;    // [1] the step's argmax (bits = token id)
+  uint2* flags;  // [kFlCount][grid] per-CTA publication flags (epoch in .y)
 };
+
+// Publication flags: a CTA that wrote its share of a vector raises its flag
+// (the vector's epoch) once all its consumer warps are past their stores; a
+// reader polls the flags of the writer CTAs with one warp before it reads the
+// vector's words once.  Polling a few flag words instead of the whole vector
+// keeps the spinning CTAs off the L2 lines the data lives in.
+enum MkFlag : int { kFlQkv = 0, kFlApart = 1, kFlXa = 2, kFlAct = 3, kFlXb = 4, kFlCount = 5 };
 
 struct MkGemv {
   int units, upc, units_per_item;
@@ -78,9 +106,13 @@ struct MegaPlan {
   unsigned slot_bytes;
   MkGemv q, o, g, d;
   int lm_rows_per_cta, lm_stage_rows;
-  int xs_floats;   // activation buffers capacity (>= max K, multiple of 32)
-  int ps_floats;   // attention scores capacity (G * chunk cap)
+  int xs_floats;    // activation buffers capacity (>= max K, multiple of 32)
+  int ps_floats;    // attention scores capacity (G * chunk cap)
   int attn_chunk_cap;
+  int qbuf_floats;  // G * hd
+  int max_splits;   // attention splits per KV head (at most)
+  int bias_floats;  // bias rows of one CTA in one GEMV phase (at most, multiple of 32)
+  int layers_bytes; // the LayerW table copied to shared memory (multiple of 16)
 };
 
 struct MegaArgs {
@@ -101,11 +133,31 @@ __host__ __device__ inline unsigned mk_epoch(unsigned e0, int L, int step, int l
   return e0 + unsigned(step) * unsigned(5 * L + 1) + unsigned(5 * l + ph) + 1u;
 }
 
+__host__ __device__ inline int mk_round32(int n) { return (n + 31) / 32 * 32; }
+
 __host__ __device__ inline size_t mega_smem_bytes(const MegaPlan& p, int d, int hd) {
   const size_t xs = p.xs_floats;
-  return kMkHeader + 4 * (2 * xs + xs / 32 + size_t(d + 31) / 32 * 32 + p.ps_floats +
-                          size_t(2) * p.attn_chunk_cap * hd + kMkPartFloats + hd) +
+  return kMkHeader + size_t(p.layers_bytes) +
+         4 * (xs + size_t(mk_round32(int(xs / 32))) + 2 * size_t(mk_round32(d)) + size_t(mk_round32(p.qbuf_floats)) + p.ps_floats +
+              size_t(2) * p.attn_chunk_cap * hd + kMkPartFloats + 2 * hd + 2 * size_t(p.bias_floats)) +
          size_t(p.nslots) * p.slot_bytes;
+}
+
+// Splits per KV head: at most one (head, split) unit per CTA.
+__host__ __device__ inline int mk_split_cap(int nkv, int grid) {
+  const int c = grid / nkv;
+  return c < 1 ? 1 : (c > kAttnMaxSplits ? kAttnMaxSplits : c);
+}
+__host__ __device__ inline void mk_attn_splits(int ctx, int max_splits, int& nsplit, int& chunk) {
+  int n0 = (ctx + kMkMinChunk - 1) / kMkMinChunk;
+  if (n0 > max_splits) n0 = max_splits;
+  if (n0 < 1) n0 = 1;
+  chunk = (ctx + n0 - 1) / n0;
+  nsplit = (ctx + chunk - 1) / chunk;
+}
+__host__ __device__ inline int mk_chunk_cap(int max_ctx, int max_splits) {
+  const int c = (max_ctx + max_splits - 1) / max_splits;
+  return c > kMkMinChunk ? c : kMkMinChunk;
 }
 
 struct MkShared {
@@ -114,21 +166,27 @@ struct MkShared {
   uint64_t* kv_bar;
   volatile int* abort_flag;  // raised by the producer
   volatile int* issued;      // items the producer has issued
-  volatile int* cabort;      // consumers' abort decision (written before, read after a consumer barrier)
+  volatile int* cabort;      // consumers' abort decision (read after a consumer barrier)
   volatile int* kv_armed;    // uses of kv_bar armed so far (thread 0 of the consumers)
   volatile int* kv_waited;   // uses of kv_bar waited for
-  float* xs;     // activations, RMSNormed where the phase has a norm, pre-scaled, swizzled
-  float* xraw;   // activations as read
-  float* xsum;   // per-32-block sums of the (normalised, unscaled) activations
-  float* xres;   // the residual input of the block's OPROJ / DOWN
-  float* ps;     // attention scores
-  float* kvbuf;  // K rows [chunk cap][hd], then V rows
-  float* part;   // split-K partials [512] + row sums [512]
-  float2* rope;  // the RoPE row of the step's position
+  float* xs;       // [xs_floats] staged GEMV input (x*w, pre-scaled, swizzled)
+  float* xsum;     // [xs_floats/32] per-32-block sums of x*w
+  float* xres[2];  // residual inputs: [0] of OPROJ (the block input), [1] of DOWN (x_a)
+  float* qbuf;     // the attention group's q rows [G][hd]
+  float* ps;       // attention scores [G][chunk cap]
+  float* kvbuf;    // K rows [chunk cap][hd], then V rows
+  float* part;     // split-K partials of a GEMV item
+  float2* rope;    // the RoPE rows of the step's position, by step parity [2][hd/2]
+  float* bias;     // [2][bias_floats] this CTA's bias rows of a GEMV phase, by phase parity
+  const LayerW* layers;  // the LayerW table
   unsigned char* slots;
 };
 
 __device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kMkConsumers) : "memory"); }
+__device__ __forceinline__ void bar_sync_n(int id) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(kMkConsumers) : "memory"); }
+__device__ __forceinline__ void bar_arrive_n(int id) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(kMkConsumers) : "memory");
+}
 __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
 
 __device__ __forceinline__ uint2 ld_ll(const uint2* p) {
@@ -140,16 +198,20 @@ __device__ __forceinline__ void st_ll(uint2* p, float v, unsigned e) {
   asm volatile("st.relaxed.gpu.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(__float_as_uint(v)), "r"(e) : "memory");
 }
 
-// Reads src[0..n) (LL words of epoch e) into dst[0..n) (plain layout), every
-// consumer thread taking elements tid + k*480, kMkRound words in flight per
-// round.  Accumulates sum(x^2) and any-NaN of this thread's elements.  Ends
-// with an acquire fence.  False if a word did not arrive in time.
-__device__ __forceinline__ bool ll_read(const uint2* src, int n, unsigned e, float* dst, float& ss, int& bad) {
+// Reads src[0..n) (LL words of epoch e) into raw[0..n) (shared memory):
+// every consumer thread takes elements i = tid + k*480, R words in flight per
+// round, and stores each once its round has arrived.  False if a word did not
+// arrive in time.  Only loads, compares and stores are unrolled; whatever
+// consumes the words runs afterwards, in a rolled loop over the same elements
+// (keeping the persistent kernel's code small: it is re-fetched into the
+// instruction cache in every phase).
+template <int R>
+__device__ __forceinline__ bool ll_gather(const uint2* src, int n, unsigned e, float* raw) {
   const int tid = threadIdx.x;
-  for (int base = 0; base < n; base += kMkRound * kMkConsumers) {
-    uint2 w[kMkRound];
+  for (int base = 0; base < n; base += R * kMkConsumers) {
+    uint2 w[R];
 #pragma unroll
-    for (int k = 0; k < kMkRound; ++k) {
+    for (int k = 0; k < R; ++k) {
       const int i = base + tid + k * kMkConsumers;
       w[k] = i < n ? ld_ll(src + i) : make_uint2(0u, e);
     }
@@ -157,7 +219,7 @@ __device__ __forceinline__ bool ll_read(const uint2* src, int n, unsigned e, flo
     for (;;) {
       bool all = true;
 #pragma unroll
-      for (int k = 0; k < kMkRound; ++k) {
+      for (int k = 0; k < R; ++k) {
         if (w[k].y != e) {
           all = false;
           w[k] = ld_ll(src + base + tid + k * kMkConsumers);
@@ -169,40 +231,80 @@ __device__ __forceinline__ bool ll_read(const uint2* src, int n, unsigned e, flo
       else if (t - t0 > kWaitNs) return false;
     }
 #pragma unroll
-    for (int k = 0; k < kMkRound; ++k) {
+    for (int k = 0; k < R; ++k) {
       const int i = base + tid + k * kMkConsumers;
-      if (i < n) {
-        const float v = __uint_as_float(w[k].x);
-        dst[i] = v;
-        ss = fmaf(v, v, ss);
-        bad |= (v != v);
-      }
+      if (i < n) raw[i] = __uint_as_float(w[k].x);
     }
   }
-  fence_acq_rel_gpu();
   return true;
 }
 
-// Sum over the consumer threads (result in every thread); red holds 16 floats.
-__device__ __forceinline__ float consumer_sum(float v, float* red) {
+// Sum of v over the consumer threads, the same value (fixed order) in every
+// thread; also the barrier that publishes what the consumers wrote before it.
+// red: 16 floats, alternated between consecutive calls by the caller.
+__device__ __forceinline__ float consumer_total(float v, float* red) {
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   v = warp_sum(v);
   if (lane == 0) red[wid] = v;
   consumer_sync();
-  float t = lane < kMkConsumerWarps ? red[lane] : 0.f;
-  t = warp_sum(t);
-  consumer_sync();
+  float t = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMkConsumerWarps; ++k) t += red[k];
   return t;
 }
-__device__ __forceinline__ int consumer_any(int v, int* redi) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-  v = __any_sync(0xffffffffu, v != 0);
-  if (lane == 0) redi[wid] = v;
-  consumer_sync();
-  int t = lane < kMkConsumerWarps ? redi[lane] : 0;
-  t = __any_sync(0xffffffffu, t != 0);
-  consumer_sync();
-  return t;
+
+// End of a phase in which this CTA wrote words of a flagged vector: warp 0
+// waits for the other consumer warps (named barrier 2; they do not wait) and
+// raises the CTA's flag.
+__device__ __forceinline__ void mk_publish(uint2* fl, unsigned e) {
+  if (threadIdx.x < 32) {
+    bar_sync_n(2);
+    if (threadIdx.x == 0) st_ll(fl + blockIdx.x, 0.f, e);
+  } else {
+    bar_arrive_n(2);
+  }
+}
+// Start of a phase reading a flagged vector written by CTAs [0, nw): warp 0
+// polls their flags (bounded), the other warps wait for it (named barrier 3).
+__device__ __forceinline__ void mk_gate(const uint2* fl, int nw, unsigned e, volatile int* cabort, DevState* st) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    bool ok = true;
+    for (int base = 0; base < nw && ok; base += 32 * 8) {
+      uint2 w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = base + lane + 32 * k;
+        w[k] = i < nw ? ld_ll(fl + i) : make_uint2(0u, e);
+      }
+      unsigned long long t0 = 0;
+      for (;;) {
+        bool all = true;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (w[k].y != e) {
+            all = false;
+            w[k] = ld_ll(fl + base + lane + 32 * k);
+          }
+        }
+        if (all) break;
+        const unsigned long long t = global_ns();
+        if (!t0) t0 = t;
+        else if (t - t0 > kWaitNs) {
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!ok) {
+      flag_timeout(st, 14);
+      *cabort = 1;
+    }
+    __syncwarp();
+    bar_arrive_n(3);
+  } else {
+    bar_sync_n(3);
+  }
 }
 
 // 2^-p for the bit position p of element k (0..7) of a word: 0,4,8,12,16,8,12,16.
@@ -211,23 +313,22 @@ __device__ __forceinline__ float nib_prescale(int k) {
   return __int_as_float((127 - p) << 23);
 }
 
-// xraw[0..K) -> xs (swizzled, scaled by `inv` and the weights in wreg when
-// norm, then pre-scaled per nibble slot) and xsum (per-32-block sums of the
-// unscaled values).  K is a multiple of 32; a warp covers whole blocks.
-__device__ __forceinline__ void mk_stage_x(const MkShared& S, int K, const float* wreg, float inv, bool norm,
-                                          int& bad_out) {
-  const int tid = threadIdx.x, lane = tid & 31;
-  int k = 0;
-  for (int i = tid; i < K; i += kMkConsumers, ++k) {
-    float v = S.xraw[i];
-    if (norm) {
-      v = (v * inv) * wreg[k < kMkMaxNormVec ? k : 0];
-      bad_out |= (v != v);
-    }
-    S.xs[swz(i)] = v * nib_prescale(i & 7);
-    const float bs = warp_sum(v);
-    if (lane == 0) S.xsum[i >> 5] = bs;
-  }
+// a[j] for a small register array and a run-time j < N.
+template <int N>
+__device__ __forceinline__ float pick(const float (&a)[N], int j) {
+  float r = a[0];
+#pragma unroll
+  for (int k = 1; k < N; ++k)
+    if (k == j) r = a[k];
+  return r;
+}
+
+// One staged element: xs (swizzled, pre-scaled per nibble slot) and the
+// block sums.  Called by whole warps (32 consecutive i).
+__device__ __forceinline__ void mk_stage_elem(float* xs, float* xsum, int i, float xv) {
+  xs[swz(i)] = xv * nib_prescale(i & 7);
+  const float bs = warp_sum(xv);
+  if ((threadIdx.x & 31) == 0) xsum[i >> 5] = bs;
 }
 
 // Packed f32x2 helpers.
@@ -251,74 +352,63 @@ __device__ __forceinline__ unsigned long long ffma2(unsigned long long a, unsign
   return d;
 }
 
-// A = sum_k q_k x_k over one 32-weight block (pre-scaled swizzled activations).
-__device__ __forceinline__ float q4_block_qx(const uint4 q, const float* xs, int b) {
-  const float4* x4 = reinterpret_cast<const float4*>(xs + (b << 5));
-  const int sw = b & 7;
-  const uint32_t M = 0x4B000000u;
+// One 32-bit word (8 weights) of a block against its 8 pre-scaled
+// activations, into two packed accumulators.
+__device__ __forceinline__ void q4_word_qx(uint32_t a, const float4 xa, const float4 xb, unsigned long long& acc0,
+                                           unsigned long long& acc1) {
+  const uint32_t M = 0x4B000000u, t = a >> 12;
   const unsigned long long neg = pack2(-8388608.0f, -8388608.0f);
-  unsigned long long acc0 = 0ull, acc1 = 0ull;  // (+0.0f, +0.0f)
-  const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    const uint32_t a = wd[w], t = a >> 12;
-    const float4 xa = x4[(2 * w) ^ sw], xb = x4[(2 * w + 1) ^ sw];
-    const float f0 = __uint_as_float((a & 0xFu) | M), f1 = __uint_as_float((a & 0xF0u) | M);
-    const float f2 = __uint_as_float((a & 0xF00u) | M), f3 = __uint_as_float((a & 0xF000u) | M);
-    const float f4 = __uint_as_float((a & 0xF0000u) | M), f5 = __uint_as_float((t & 0xF00u) | M);
-    const float f6 = __uint_as_float((t & 0xF000u) | M), f7 = __uint_as_float((t & 0xF0000u) | M);
-    acc0 = ffma2(fadd2(pack2(f0, f1), neg), pack2(xa.x, xa.y), acc0);
-    acc1 = ffma2(fadd2(pack2(f2, f3), neg), pack2(xa.z, xa.w), acc1);
-    acc0 = ffma2(fadd2(pack2(f4, f5), neg), pack2(xb.x, xb.y), acc0);
-    acc1 = ffma2(fadd2(pack2(f6, f7), neg), pack2(xb.z, xb.w), acc1);
-  }
+  const float f0 = __uint_as_float((a & 0xFu) | M), f1 = __uint_as_float((a & 0xF0u) | M);
+  const float f2 = __uint_as_float((a & 0xF00u) | M), f3 = __uint_as_float((a & 0xF000u) | M);
+  const float f4 = __uint_as_float((a & 0xF0000u) | M), f5 = __uint_as_float((t & 0xF00u) | M);
+  const float f6 = __uint_as_float((t & 0xF000u) | M), f7 = __uint_as_float((t & 0xF0000u) | M);
+  acc0 = ffma2(fadd2(pack2(f0, f1), neg), pack2(xa.x, xa.y), acc0);
+  acc1 = ffma2(fadd2(pack2(f2, f3), neg), pack2(xa.z, xa.w), acc1);
+  acc0 = ffma2(fadd2(pack2(f4, f5), neg), pack2(xb.x, xb.y), acc0);
+  acc1 = ffma2(fadd2(pack2(f6, f7), neg), pack2(xb.z, xb.w), acc1);
+}
+__device__ __forceinline__ float hsum2(unsigned long long acc0, unsigned long long acc1) {
   float a0, a1, a2, a3;
   unpack2(acc0, a0, a1);
   unpack2(acc1, a2, a3);
   return (a0 + a1) + (a2 + a3);
 }
 
-// Rows [0, R) of one staged item -> rowsum[t] (flushed; bias added by the
-// caller).  Warps split rows; with fewer rows than warps a row's blocks are
-// split across g warps and the partials summed in a fixed order.
-__device__ __forceinline__ void mk_rows(const MkShared& S, const unsigned char* slot, int R, int nb, int nbp,
-                                        float* rowsum) {
-  const uint4* qs = reinterpret_cast<const uint4*>(slot);
-  const uint32_t* sm = reinterpret_cast<const uint32_t*>(slot + (size_t)R * nb * 16);
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  const int NI = (nb + 31) / 32;
-  int g = kMkConsumerWarps / max(R, 1);
-  g = max(1, min(g, NI));
-  const int groups = kMkConsumerWarps / g;
-  if (w < groups * g) {
-    const int slice = w % g;
-    for (int rr = w / g; rr < R; rr += groups) {
-      float acc = 0.f;
-      for (int it = slice; it < NI; it += g) {
-        const int b = lane + 32 * it;
-        if (b < nb) {
-          float scale, mn;
-          unpack_sm(sm[(size_t)rr * nbp + b], scale, mn);
-          const float A = q4_block_qx(qs[(size_t)rr * nb + b], S.xs, b);
-          acc = fmaf(scale, A, fmaf(mn, S.xsum[b], acc));
-        }
-      }
-      acc = warp_sum(acc);
-      if (lane == 0) S.part[rr * g + slice] = acc;
-    }
+// A = sum_k q_k x_k of one 32-weight block for two rows sharing the staged
+// (swizzled, pre-scaled) activations of block b; the activations are loaded
+// once, a word's worth at a time.
+__device__ __forceinline__ void q4_pair_qx(const uint4 q0, const uint4 q1, bool has1, const float* xs, int b,
+                                           float& A0, float& A1) {
+  const float4* x4 = reinterpret_cast<const float4*>(xs + (b << 5));
+  const int sw = b & 7;
+  unsigned long long r00 = 0ull, r01 = 0ull, r10 = 0ull, r11 = 0ull;  // (+0.0f, +0.0f)
+  const uint32_t w0[4] = {q0.x, q0.y, q0.z, q0.w};
+  const uint32_t w1[4] = {q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const float4 xa = x4[(2 * w) ^ sw], xb = x4[(2 * w + 1) ^ sw];
+    q4_word_qx(w0[w], xa, xb, r00, r01);
+    if (has1) q4_word_qx(w1[w], xa, xb, r10, r11);
   }
-  consumer_sync();
-  for (int t = threadIdx.x; t < R; t += kMkConsumers) {
-    float s = 0.f;
-    for (int k = 0; k < g; ++k) s += S.part[t * g + k];
-    rowsum[t] = flush_small(s);
-  }
-  consumer_sync();
+  A0 = hsum2(r00, r01);
+  A1 = hsum2(r10, r11);
+}
+
+// Work shape of one GEMV item of nr rows of nb blocks: tasks of rpt rows
+// (rpt = 2 when the epilogue needs a row pair, or when single rows would not
+// fit the lanes), 32 lanes per (task, slice) -- a lane's blocks are a serial
+// chain, so the most lanes per task gives the shortest item -- and S slices
+// of a task's blocks when lanes are left over and rows are long.
+__device__ __forceinline__ void gemv_shape(int nr, int nb, bool pairs, int& rpt, int& S, int& tasks) {
+  rpt = (pairs || nr * 32 > kMkConsumers) ? 2 : 1;
+  tasks = (nr + rpt - 1) / rpt;
+  S = 1;
+  if (tasks * 64 <= kMkConsumers) S = max(1, min(kMkConsumers / (tasks * 32), nb / 48));
 }
 
 // CTA-local lateral_inhibition_kwta on x[0..d): exact k-th largest by radix
 // select, values below become -1e9 (the same mask in every CTA).
-__device__ void mk_block_kwta(float* x, int d, int k, unsigned* hist) {
+__device__ __noinline__ void mk_block_kwta(float* x, int d, int k, unsigned* hist) {
   const int tid = threadIdx.x;
   unsigned prefix = 0u, mask = 0u, kk = unsigned(k);
   for (int shift = 24; shift >= 0; shift -= 8) {
@@ -356,99 +446,181 @@ __device__ __forceinline__ void cta_units(const MkGemv& g, int& u0, int& u1) {
   u1 = min(g.units, u0 + g.upc);
   if (u0 > u1) u0 = u1;
 }
-
-// Splits per KV head: at most one (head, split) unit per CTA.
-__host__ __device__ inline int mk_split_cap(int nkv, int grid) {
-  const int c = grid / nkv;
-  return c < 1 ? 1 : (c > kAttnMaxSplits ? kAttnMaxSplits : c);
+// This CTA's bias rows of a GEMV phase into shared memory (zeros without a
+// bias): the loads run while the phase waits for its input.
+__device__ __forceinline__ float* mk_prefetch_bias(const MkShared& S, int bias_floats, const MkGemv& g,
+                                                   const Q4View& W, int rpu, int par) {
+  float* dst = S.bias + par * bias_floats;
+  int u0, u1;
+  cta_units(g, u0, u1);
+  const int n = (u1 - u0) * rpu, r0 = u0 * rpu;
+  const float* b = W.bias;
+  for (int i = threadIdx.x; i < n; i += kMkConsumers) dst[i] = b ? __ldg(b + r0 + i) : 0.f;
+  return dst;
 }
+// CTAs holding units of a GEMV phase: [0, writers).
+__device__ __forceinline__ int mk_writers(const MkGemv& g) { return min((int)gridDim.x, (g.units + g.upc - 1) / g.upc); }
 
 // Attention split owned by this CTA at context ctx (-1 if none).
-__device__ __forceinline__ int attn_unit(int ctx, int nkv, int& nsplit, int& chunk) {
-  attn_splits(ctx, nsplit, chunk, mk_split_cap(nkv, gridDim.x));
+__device__ __forceinline__ int attn_unit(int ctx, int nkv, int max_splits, int& nsplit, int& chunk) {
+  mk_attn_splits(ctx, max_splits, nsplit, chunk);
   const int units = nkv * nsplit;
   return (int)blockIdx.x < units ? (int)blockIdx.x : -1;
 }
 
 // ----------------------------------------------------------- producer
+// Walks the item sequence a step consumes -- per block, the units of each
+// GEMV phase (QKV, O-proj, gate/up, down) in items of units_per_item, then the
+// lm_head rows in stages -- and streams every item into the next ring slot.
 __device__ void mk_producer(const MegaArgs& A, const MkShared& S) {
   const StepParams& P = A.P;
   const MegaPlan& pl = A.plan;
+  const int L = P.n_layers;
+  const int rbeg = blockIdx.x * pl.lm_rows_per_cta, rend = min(P.V, rbeg + pl.lm_rows_per_cta);
   int item = 0;
-  bool ok = true;
-  auto issue = [&](const void* src0, uint32_t b0, const void* src1, uint32_t b1) {
-    if (!ok) return;
-    const int slot = item % pl.nslots;
-    if (item >= pl.nslots && !mbar_wait(S.empty + slot, ((item / pl.nslots) - 1) & 1)) {
-      flag_timeout(P.st, 11);
-      *S.abort_flag = 1;
-      ok = false;
-      return;
-    }
-    if (*S.abort_flag || *S.cabort) {
-      ok = false;
-      return;
-    }
-    unsigned char* dst = S.slots + (size_t)slot * pl.slot_bytes;
-    mbar_expect_tx(S.full + slot, b0 + b1);
-    if (b0) bulk_g2s(dst, src0, b0, S.full + slot);
-    if (b1) bulk_g2s(dst + b0, src1, b1, S.full + slot);
-    ++item;
-    *S.issued = item;
-  };
-  for (int step = 0; step < A.n_steps && ok; ++step) {
-    for (int l = 0; l < P.n_layers && ok; ++l) {
-      const LayerW& L = A.layers[l];
-      const MkGemv* gs[4] = {&pl.q, &pl.o, &pl.g, &pl.d};
-      const Q4View* ws[4] = {&L.qkv, &L.wo, &L.gate_up, &L.down};
-      const int rpus[4] = {2, 1, 2, 1};
-      for (int ph = 0; ph < 4 && ok; ++ph) {
+  for (int step = 0; step < A.n_steps; ++step) {
+    int l = 0, ph = 0, a = -1, r = rbeg;
+    for (;;) {
+      const void* src0;
+      const void* src1 = nullptr;
+      uint32_t b0, b1 = 0u;
+      if (l < L) {
+        const MkGemv& g = ph == 0 ? pl.q : ph == 1 ? pl.o : ph == 2 ? pl.g : pl.d;
         int u0, u1;
-        cta_units(*gs[ph], u0, u1);
-        const Q4View& W = *ws[ph];
-        for (int a = u0; a < u1 && ok; a += gs[ph]->units_per_item) {
-          const int ra = a * rpus[ph], nr = (min(u1, a + gs[ph]->units_per_item) - a) * rpus[ph];
-          issue(W.qs + (size_t)ra * W.nb, uint32_t(nr) * W.nb * 16, W.sm + (size_t)ra * W.nbp,
-                uint32_t(nr) * W.nbp * 4);
+        cta_units(g, u0, u1);
+        if (a < 0) a = u0;
+        if (a >= u1) {
+          a = -1;
+          if (++ph == 4) {
+            ph = 0;
+            ++l;
+          }
+          continue;
         }
+        const LayerW& Lw = A.layers[l];
+        const Q4View& W = ph == 0 ? Lw.qkv : ph == 1 ? Lw.wo : ph == 2 ? Lw.gate_up : Lw.down;
+        const int rpu = (ph == 0 || ph == 2) ? 2 : 1;
+        const int ra = a * rpu, nr = (min(u1, a + g.units_per_item) - a) * rpu;
+        src0 = W.qs + (size_t)ra * W.nb;
+        b0 = uint32_t(nr) * W.nb * 16;
+        src1 = W.sm + (size_t)ra * W.nbp;
+        b1 = uint32_t(nr) * W.nbp * 4;
+        a += g.units_per_item;
+      } else {
+        if (r >= rend) break;
+        const int rows = min(pl.lm_stage_rows, rend - r);
+        src0 = P.lm_head + (size_t)r * P.d;
+        b0 = uint32_t(rows) * P.d * 4;
+        r += pl.lm_stage_rows;
       }
-    }
-    const int rbeg = blockIdx.x * pl.lm_rows_per_cta;
-    const int rend = min(P.V, rbeg + pl.lm_rows_per_cta);
-    for (int r = rbeg; r < rend && ok; r += pl.lm_stage_rows) {
-      const int rows = min(pl.lm_stage_rows, rend - r);
-      issue(P.lm_head + (size_t)r * P.d, uint32_t(rows) * P.d * 4, nullptr, 0u);
+      const int slot = item % pl.nslots;
+      if (item >= pl.nslots && !mbar_wait(S.empty + slot, ((item / pl.nslots) - 1) & 1)) {
+        flag_timeout(P.st, 11);
+        *S.abort_flag = 1;
+        return;
+      }
+      if (*S.abort_flag || *S.cabort) return;
+      unsigned char* dst = S.slots + (size_t)slot * pl.slot_bytes;
+      mbar_expect_tx(S.full + slot, b0 + b1);
+      bulk_g2s(dst, src0, b0, S.full + slot);
+      if (b1) bulk_g2s(dst + b0, src1, b1, S.full + slot);
+      ++item;
+      *S.issued = item;
     }
   }
 }
 
 // ----------------------------------------------------------- consumers
-// Every consumer thread waits (bounded) on the slot's full barrier; then all
-// agree through a consumer barrier so that they return together on abort.
-__device__ __forceinline__ const unsigned char* take(const MegaArgs& A, const MkShared& S, int item) {
+// Every consumer thread waits (bounded) for the item's slot; a wait that runs
+// out raises the abort flag, which the consumers act on at their next barrier.
+__device__ __forceinline__ const unsigned char* wait_slot(const MegaArgs& A, const MkShared& S, int item) {
   const int slot = item % A.plan.nslots;
-  if (!mbar_wait(S.full + slot, (item / A.plan.nslots) & 1)) {
+  if (!*S.cabort && !*S.abort_flag && !mbar_wait(S.full + slot, (item / A.plan.nslots) & 1)) {
     flag_timeout(A.P.st, 12);
     *S.cabort = 1;
   }
-  if (threadIdx.x == 0 && *S.abort_flag) *S.cabort = 1;
-  consumer_sync();
-  if (*S.cabort) return nullptr;
+  if (*S.abort_flag) *S.cabort = 1;
   return S.slots + (size_t)slot * A.plan.slot_bytes;
 }
 __device__ __forceinline__ void release(const MegaArgs& A, const MkShared& S, int item) {
   __syncwarp();
   if ((threadIdx.x & 31) == 0) mbar_arrive(S.empty + item % A.plan.nslots);
 }
-// Consumers agree on whether any of them failed (a bounded LL wait).
-__device__ __forceinline__ bool agree(const MkShared& S, bool ok, DevState* st) {
-  if (!ok) {
-    flag_timeout(st, 13);
-    *S.cabort = 1;
+
+// One GEMV phase of this CTA: its units in staged items, each item's rows
+// dotted against xs/xsum, a warp per (task, slice); epi(a, r, y0, y1, has1)
+// gets the raw dots of the item's local rows r and r+1 (r+1 when has1) of the
+// item starting at unit a (its first row is a*rpu).  The epilogue has one
+// call site (the kernel's code size matters).
+template <class Epi>
+__device__ __forceinline__ void mk_gemv(const MegaArgs& A, const MkShared& S, const MkGemv& gp, const Q4View& W,
+                                        int rpu, const float* xs, const float* xsum, int& item,
+                                        unsigned long long* first_ready, Epi&& epi) {
+  const int tid = threadIdx.x, lane = tid & 31, gid = tid >> 5;
+  int u0, u1;
+  cta_units(gp, u0, u1);
+  const int nb = W.nb, nbp = W.nbp;
+  for (int a = u0; a < u1; a += gp.units_per_item) {
+    const int nr = (min(u1, a + gp.units_per_item) - a) * rpu;
+    const unsigned char* slot = wait_slot(A, S, item);
+    if (first_ready && a == u0 && tid == 0) *first_ready = global_ns();
+    const uint4* qs = reinterpret_cast<const uint4*>(slot);
+    const uint32_t* sm = reinterpret_cast<const uint32_t*>(slot + (size_t)nr * nb * 16);
+    int rpt, Sl, tasks;
+    gemv_shape(nr, nb, rpu == 2, rpt, Sl, tasks);
+    const int nts = tasks * Sl;
+    // with slices every warp runs one round (a barrier joins the slices)
+    const int iters = Sl > 1 ? 1 : (gid < nts ? (nts - gid + kMkConsumerWarps - 1) / kMkConsumerWarps : 0);
+    for (int it = 0; it < iters; ++it) {
+      const int ts = gid + it * kMkConsumerWarps;
+      int p = ts / Sl;
+      const int sl = ts - p * Sl;
+      float acc0 = 0.f, acc1 = 0.f;
+      if (ts < nts) {
+        const int r0 = rpt * p;
+        const bool h1 = rpt == 2 && r0 + 1 < nr;
+        for (int b = sl * 32 + lane; b < nb; b += Sl * 32) {
+          const uint4 q0 = qs[(size_t)r0 * nb + b];
+          const uint4 q1 = h1 ? qs[(size_t)(r0 + 1) * nb + b] : make_uint4(0u, 0u, 0u, 0u);
+          const uint32_t sm0 = sm[(size_t)r0 * nbp + b], sm1 = h1 ? sm[(size_t)(r0 + 1) * nbp + b] : 0u;
+          const float xb = xsum[b];
+          float A0, A1, sc, mn;
+          q4_pair_qx(q0, q1, h1, xs, b, A0, A1);
+          unpack_sm(sm0, sc, mn);
+          acc0 = fmaf(sc, A0, fmaf(mn, xb, acc0));
+          unpack_sm(sm1, sc, mn);
+          acc1 = fmaf(sc, A1, fmaf(mn, xb, acc1));
+        }
+        acc0 = warp_sum(acc0);
+        acc1 = warp_sum(acc1);
+      }
+      bool fire = ts < nts && lane == 0;
+      if (Sl > 1) {  // uniform over the CTA: the slices' partials, summed in slice order
+        if (fire) {
+          S.part[2 * ts] = acc0;
+          S.part[2 * ts + 1] = acc1;
+        }
+        consumer_sync();
+        p = gid;
+        fire = gid < tasks && lane == 0;
+        if (fire) {
+          acc0 = 0.f;
+          acc1 = 0.f;
+          for (int s = 0; s < Sl; ++s) {
+            acc0 += S.part[2 * (p * Sl + s)];
+            acc1 += S.part[2 * (p * Sl + s) + 1];
+          }
+        }
+      }
+      if (fire) epi(a, rpt * p, acc0, acc1, rpt == 2 && rpt * p + 1 < nr);
+    }
+    release(A, S, item++);
+    if (Sl > 1) consumer_sync();  // the partials buffer is reused by the next item
   }
-  consumer_sync();
-  return *S.cabort == 0;
 }
+
+// Phases of a block, in order, and the step's lm_head phase.
+enum MkPhase : int { kPhQkv = 0, kPhAttn = 1, kPhOproj = 2, kPhGateup = 3, kPhDown = 4, kPhLm = 5 };
 
 __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
   const StepParams& P = A.P;
@@ -456,77 +628,278 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
   DevState* st = P.st;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int L = P.n_layers, d = P.d, hd = P.hd, half = hd >> 1;
-  const int G = P.nh / P.nkv;
-  __shared__ float red[32];
-  __shared__ int redi[32];
+  const int G = P.nh / P.nkv, qd = P.nh * P.hd;
+  const int Smax = pl.max_splits, cap = pl.attn_chunk_cap;
+  __shared__ float red[2][16];
   __shared__ unsigned hist[260];
   __shared__ unsigned long long wbest[32];
   __shared__ int is_last;
   __shared__ float mls[2 * kAttnMaxGroup];
-  __shared__ float wsh[kAttnMaxGroup * kAttnMaxSplits];
-  __shared__ float linv[kAttnMaxGroup];
-  int item = 0;
+  int item = 0, ph_count = 0;
   const unsigned pos0 = __ldcg(&st->pos);
-  float* rowsum = S.part + 512;
-  auto mark = [&](int step, int k) {
-    if (A.phase_ns && blockIdx.x == 0 && tid == 0)
-      A.phase_ns[(size_t)step * (5 * L + 1) + k] = global_ns();
-  };
-  auto tmark = [&](int step, int l, int ph, int k) {
+  auto tmark = [&](int step, int pi, int k) {
     if (A.trace_ns && tid == 0)
-      A.trace_ns[(((size_t)blockIdx.x * A.n_steps + step) * (5 * L + 1) + 5 * l + ph) * kMkTrace + k] = global_ns();
+      A.trace_ns[(((size_t)blockIdx.x * A.n_steps + step) * (5 * L + 1) + pi) * kMkTrace + k] = global_ns();
   };
-  // one staged GEMV phase: items of this CTA's units, rows -> rowsum, epilogue per item
-  auto gemv_phase = [&](const MkGemv& gp, const Q4View& W, int rpu, int step, int l, int ph,
-                        auto&& epilogue) -> bool {
-    int u0, u1;
-    cta_units(gp, u0, u1);
-    for (int a = u0; a < u1; a += gp.units_per_item) {
-      const int b = min(u1, a + gp.units_per_item);
-      const unsigned char* slot = take(A, S, item);
-      if (!slot) return false;
-      if (a == u0) tmark(step, l, ph, 3);
-      mk_rows(S, slot, (b - a) * rpu, W.nb, W.nbp, rowsum);
-      release(A, S, item++);
-      epilogue(a, b);
-      consumer_sync();  // rowsum is reused by the next item
-    }
-    return true;
-  };
-
   // A CTA reads an exchanged vector only in phases where it has work whose
   // output other CTAs wait for: then every read of a buffer generation is
   // causally before the next generation's writes (no reader can be overtaken).
-  int qa, qb, oa, ob, ga, gb, da, db;
-  cta_units(pl.q, qa, qb);
-  cta_units(pl.o, oa, ob);
-  cta_units(pl.g, ga, gb);
-  cta_units(pl.d, da, db);
-  const bool has_q = qb > qa, has_o = ob > oa, has_g = gb > ga, has_d = db > da;
+  auto has = [&](const MkGemv& g) { return (int)blockIdx.x * g.upc < g.units; };
+  const bool has_q = has(pl.q), has_o = has(pl.o), has_g = has(pl.g), has_d = has(pl.d);
   for (int step = 0; step < A.n_steps; ++step) {
     const unsigned pos = pos0 + step;
     const int ctx = int(pos) + 1;
     int nsplit, chunk;
-    const int au = attn_unit(ctx, P.nkv, nsplit, chunk);
-    for (int l = 0; l < L; ++l) {
-      const LayerW& Lw = A.layers[l];
-      const unsigned e_qkv = mk_epoch(A.epoch0, L, step, l, 0), e_attn = e_qkv + 1, e_o = e_qkv + 2,
-                     e_gu = e_qkv + 3, e_down = e_qkv + 4;
-      // ================================================ QKV
-      if (has_q || has_o || au >= 0) {
-        tmark(step, l, 0, 0);
-        // constant inputs first: norm weights, the RoPE row
-        float wreg[kMkMaxNormVec];
-#pragma unroll
-        for (int k = 0; k < kMkMaxNormVec; ++k) {
-          const int i = tid + k * kMkConsumers;
-          wreg[k] = i < d ? Lw.attn_norm[i] : 0.f;
+    const int au = attn_unit(ctx, P.nkv, Smax, nsplit, chunk);
+    float2* rope = S.rope + (step & 1) * half;  // by step parity: no reader of the previous row is left
+    // phase index pi = 5l + ph over the blocks, then pi = 5L: the lm_head
+    for (int pi = 0; pi <= 5 * L; ++pi) {
+      const int l = pi < 5 * L ? pi / 5 : L - 1;
+      const int ph = pi < 5 * L ? pi - 5 * l : int(kPhLm);
+      const LayerW& Lw = S.layers[l];
+      const unsigned e_qkv = mk_epoch(A.epoch0, L, step, l, 0), e_attn = e_qkv + 1;
+      if (ph == kPhAttn) {
+        // ============================================== ATTN
+        if (au >= 0) {
+          tmark(step, pi, 0);
+          const int g = au % P.nkv, s = au / P.nkv, t0 = s * chunk;
+          const int n = min(ctx, t0 + chunk) - t0;
+          const int n_old = max(0, min(n, ctx - 1 - t0));
+          float* Ks = S.kvbuf;
+          float* Vs = S.kvbuf + (size_t)cap * hd;
+          mk_gate(A.ll.flags + kFlQkv * gridDim.x, mk_writers(pl.q), e_qkv, S.cabort, st);
+          tmark(step, pi, 1);
+          bool ok = ll_gather<2>(A.ll.q + (size_t)g * G * hd, G * hd, e_qkv, S.qbuf);
+          if (n > n_old)  // this step's own row: LL, then into the cache for later steps
+            ok = ok && ll_gather<2>(A.ll.kv + (size_t)g * hd, hd, e_qkv, Ks + (size_t)n_old * hd) &&
+                 ll_gather<2>(A.ll.kv + (size_t)(P.nkv + g) * hd, hd, e_qkv, Vs + (size_t)n_old * hd);
+          const bool wrote_row = ok && n > n_old && tid < hd;
+          if (wrote_row) {
+            Lw.kc[((size_t)g * P.max_ctx + pos) * hd + tid] = Ks[(size_t)n_old * hd + tid];
+            Lw.vc[((size_t)g * P.max_ctx + pos) * hd + tid] = Vs[(size_t)n_old * hd + tid];
+          }
+          // every consumer observes the copy's completion (parity of this use)
+          const int use = *S.kv_waited;
+          if (ok && !*S.cabort && !mbar_wait(S.kv_bar, use & 1)) ok = false;
+          if (!ok) {
+            flag_timeout(st, 13);
+            *S.cabort = 1;
+          }
+          consumer_sync();
+          if (*S.cabort) return;
+          if (tid == 0) *S.kv_waited = use + 1;
+          tmark(step, pi, 2);
+          // scores: lane = position, warps over (32-position block, head subset)
+          {
+            const int npb = (n + 31) >> 5;
+            const int nhs = max(1, min(G, kMkConsumerWarps / npb));
+            const int H4 = hd >> 2;
+            for (int task = wid; task < npb * nhs; task += kMkConsumerWarps) {
+              const int pb = task % npb, hs = task / npb;
+              const int t = pb * 32 + lane;
+              if (t < n) {
+                const float4* kr = reinterpret_cast<const float4*>(Ks + (size_t)t * hd);
+                for (int j = hs; j < G; j += nhs) {
+                  const float4* qr = reinterpret_cast<const float4*>(S.qbuf + j * hd);
+                  float a0 = 0.f, a1 = 0.f;
+                  int c = lane % H4;  // rotated start: conflict-free rows
+                  for (int k = 0; k < H4; ++k) {
+                    const float4 kk = kr[c], qq = qr[c];
+                    a0 = fmaf(qq.x, kk.x, a0);
+                    a1 = fmaf(qq.y, kk.y, a1);
+                    a0 = fmaf(qq.z, kk.z, a0);
+                    a1 = fmaf(qq.w, kk.w, a1);
+                    c = c + 1 == H4 ? 0 : c + 1;
+                  }
+                  S.ps[j * cap + t] = (a0 + a1) * P.attn_scale;
+                }
+              }
+            }
+          }
+          if (wrote_row) __threadfence();  // the new cache row before this split's partials
+          consumer_sync();
+          tmark(step, pi, 3);
+          for (int j = wid; j < G; j += kMkConsumerWarps) {
+            float* pr = S.ps + j * cap;
+            float m = -INFINITY;
+            for (int t = lane; t < n; t += kWarp) m = fmaxf(m, pr[t]);
+            m = warp_max(m);
+            float lsum = 0.f;
+            for (int t = lane; t < n; t += kWarp) {
+              const float ev = expf(pr[t] - m);
+              pr[t] = ev;
+              lsum += ev;
+            }
+            lsum = warp_sum(lsum);
+            if (lane == 0) {
+              mls[2 * j] = m;
+              mls[2 * j + 1] = lsum;
+            }
+          }
+          consumer_sync();
+          uint2* part = A.ll.apart + ((size_t)g * Smax + s) * G * (hd + 2);
+          for (int idx = tid; idx < G * hd; idx += kMkConsumers) {
+            const int j = idx / hd, e = idx - j * hd;
+            const float* pr = S.ps + j * cap;
+            float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+            int t = 0;
+            for (; t + 3 < n; t += 4) {
+              o0 = fmaf(pr[t], Vs[(size_t)t * hd + e], o0);
+              o1 = fmaf(pr[t + 1], Vs[(size_t)(t + 1) * hd + e], o1);
+              o2 = fmaf(pr[t + 2], Vs[(size_t)(t + 2) * hd + e], o2);
+              o3 = fmaf(pr[t + 3], Vs[(size_t)(t + 3) * hd + e], o3);
+            }
+            for (; t < n; ++t) o0 = fmaf(pr[t], Vs[(size_t)t * hd + e], o0);
+            uint2* pj = part + (size_t)j * (hd + 2);
+            st_ll(pj + e, (o0 + o1) + (o2 + o3), e_attn);
+            if (e == 0) {
+              st_ll(pj + hd, mls[2 * j], e_attn);
+              st_ll(pj + hd + 1, mls[2 * j + 1], e_attn);
+            }
+          }
+          mk_publish(A.ll.flags + kFlApart * gridDim.x, e_attn);
+          tmark(step, pi, 4);
         }
-        for (int i = tid; i < half; i += kMkConsumers) S.rope[i] = P.rope[(size_t)pos * half + i];
-        float ss = 0.f;
-        int bad = 0;
-        bool ok = true;
-        if (l == 0) {
+        if (A.phase_ns && blockIdx.x == 0 && tid == 0) A.phase_ns[(size_t)step * (5 * L + 1) + pi] = global_ns();
+        continue;
+      }
+      // ================================================ GEMV phases and LM
+      // QKV     attn_norm(x) -> qkv rows + RoPE -> q, k, v      (in: x_b of block l-1)
+      // OPROJ   attention combine -> attn_output rows + x      (in: split partials)
+      // GATEUP  ffn_norm(x_a) -> gate/up rows + SwiGLU -> act   (in: x_a)
+      // DOWN    act -> ffn_down rows + x_a -> x_b               (in: act)
+      // LM      output_norm(x_b) -> lm_head rows -> argmax      (in: x_b of block L-1)
+      const bool stage_here = ph == kPhQkv ? (has_q || has_o || au >= 0)
+                              : ph == kPhOproj ? has_o : ph == kPhGateup ? (has_g || has_d)
+                              : ph == kPhDown ? has_d : true;
+      if (!stage_here) continue;
+      tmark(step, pi, 0);
+      const MkGemv& gp = ph == kPhQkv ? pl.q : ph == kPhOproj ? pl.o : ph == kPhGateup ? pl.g : pl.d;
+      const Q4View& W = ph == kPhQkv ? Lw.qkv : ph == kPhOproj ? Lw.wo : ph == kPhGateup ? Lw.gate_up : Lw.down;
+      const int rpu = (ph == kPhQkv || ph == kPhGateup) ? 2 : 1;
+      const float* norm = ph == kPhQkv ? Lw.attn_norm : ph == kPhGateup ? Lw.ffn_norm : ph == kPhLm ? P.out_norm : nullptr;
+      // raw input: the residual copies for QKV / GATEUP, xres[0] for LM (free
+      // again: last read by the last block's O-proj), xs itself for DOWN
+      float* raw = ph == kPhGateup ? S.xres[1] : ph == kPhDown ? S.xs : S.xres[0];
+      const unsigned e_out = e_qkv + unsigned(ph);
+      const int K = ph == kPhDown ? P.ff : ph == kPhOproj ? qd : d;
+      float wreg[kMkMaxNormVec];
+#pragma unroll
+      for (int k = 0; k < kMkMaxNormVec; ++k) {
+        const int i = tid + k * kMkConsumers;
+        wreg[k] = norm && i < d ? norm[i] : 1.f;
+      }
+      if (ph == kPhQkv && l == 0)
+        for (int i = tid; i < half; i += kMkConsumers) rope[i] = P.rope[(size_t)pos * half + i];
+      const float* bsm = ph == kPhLm ? nullptr : mk_prefetch_bias(S, pl.bias_floats, gp, W, rpu, ph_count & 1);
+      float* xs = S.xs;
+      float* xsum = S.xsum;
+      float ss = 0.f;
+      bool ok = true;
+      if (ph == kPhOproj) {
+        mk_gate(A.ll.flags + kFlApart * gridDim.x, P.nkv * nsplit, e_attn, S.cabort, st);
+        tmark(step, pi, 1);
+        // combine of the split partials (the softmax of attention.rs:88-127
+        // across splits): weights exp(m_s - M), out = O / (L + 1e-12).  Per
+        // round of kMkCombine splits every word is requested at once: the
+        // (m, l) pairs by one thread each into shared memory, the o words of
+        // this thread's elements (at most two: qd <= 960) into registers.
+        constexpr int kE = 2;
+        float M[kE], O[kE], Ls[kE];
+        const uint2* ob[kE];
+#pragma unroll
+        for (int j = 0; j < kE; ++j) {
+          M[j] = -INFINITY;
+          O[j] = 0.f;
+          Ls[j] = 0.f;
+          const int i = min(tid + j * kMkConsumers, qd - 1);
+          const int h = i / hd, e = i - h * hd;
+          const int g = h / G, jh = h - g * G;
+          ob[j] = A.ll.apart + ((size_t)g * Smax * G + jh) * (hd + 2) + e;
+        }
+        const uint2* pml = nullptr;
+        if (tid < P.nh * kMkCombine) {
+          const int h = tid / kMkCombine, g = h / G, jh = h - g * G;
+          pml = A.ll.apart + ((size_t)g * Smax * G + jh) * (hd + 2) + hd + (size_t)(tid % kMkCombine) * G * (hd + 2);
+        }
+        const size_t sstride = (size_t)G * (hd + 2);
+        for (int s0 = 0; s0 < nsplit; s0 += kMkCombine) {
+          const int ns = min(kMkCombine, nsplit - s0);
+          float* mlp = S.part;  // [nh][kMkCombine][2]
+          const bool mine = pml && tid % kMkCombine < ns;
+          const uint2* pm = pml + (size_t)s0 * sstride;
+          uint2 wm = mine ? ld_ll(pm) : make_uint2(0u, e_attn), wl = mine ? ld_ll(pm + 1) : make_uint2(0u, e_attn);
+          uint2 wo[kE][kMkCombine];
+#pragma unroll
+          for (int j = 0; j < kE; ++j) {
+            const bool live = tid + j * kMkConsumers < qd;
+#pragma unroll
+            for (int k = 0; k < kMkCombine; ++k)
+              wo[j][k] = (live && k < ns) ? ld_ll(ob[j] + (size_t)(s0 + k) * sstride) : make_uint2(0u, e_attn);
+          }
+          unsigned long long tw = 0;
+          for (;;) {
+            bool all = true;
+            if (wm.y != e_attn) {
+              all = false;
+              wm = ld_ll(pm);
+            }
+            if (wl.y != e_attn) {
+              all = false;
+              wl = ld_ll(pm + 1);
+            }
+#pragma unroll
+            for (int j = 0; j < kE; ++j)
+#pragma unroll
+              for (int k = 0; k < kMkCombine; ++k)
+                if (wo[j][k].y != e_attn) {
+                  all = false;
+                  wo[j][k] = ld_ll(ob[j] + (size_t)(s0 + k) * sstride);
+                }
+            if (all) break;
+            const unsigned long long t = global_ns();
+            if (!tw) tw = t;
+            else if (t - tw > kWaitNs) {
+              ok = false;
+              break;
+            }
+          }
+          if (mine) {
+            mlp[tid * 2] = __uint_as_float(wm.x);
+            mlp[tid * 2 + 1] = __uint_as_float(wl.x);
+          }
+          consumer_sync();
+#pragma unroll
+          for (int j = 0; j < kE; ++j) {
+            const int i = tid + j * kMkConsumers;
+            if (i >= qd) break;
+            const float* ml = mlp + (i / hd) * kMkCombine * 2;
+            float Mn = M[j];
+            for (int k = 0; k < ns; ++k) Mn = fmaxf(Mn, ml[2 * k]);
+            const float r = expf(M[j] - Mn);  // 0 on the first round (M = -inf)
+            O[j] *= r;
+            Ls[j] *= r;
+#pragma unroll
+            for (int k = 0; k < kMkCombine; ++k) {
+              if (k < ns) {
+                const float w = expf(ml[2 * k] - Mn);
+                O[j] = fmaf(__uint_as_float(wo[j][k].x), w, O[j]);
+                Ls[j] = fmaf(ml[2 * k + 1], w, Ls[j]);
+              }
+            }
+            M[j] = Mn;
+          }
+          if (s0 + kMkCombine < nsplit) consumer_sync();  // the (m, l) buffer is refilled
+        }
+#pragma unroll
+        for (int j = 0; j < kE; ++j) {
+          const int i = tid + j * kMkConsumers;
+          if (i < qd) mk_stage_elem(xs, xsum, i, O[j] * (1.0f / (Ls[j] + 1e-12f)));
+        }
+      } else {
+        // the input vector into raw: the step's embedding row (QKV of block
+        // 0) or the flagged LL words of the previous phase
+        if (ph == kPhQkv && l == 0) {
           unsigned tok;
           if (step == 0) {
             tok = __ldcg(&st->token);
@@ -543,344 +916,80 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
               }
               w = ld_ll(A.ll.tok);
             }
-            fence_acq_rel_gpu();
             tok = w.x;
           }
+          tmark(step, pi, 1);
           const float* src = P.embd + (size_t)(tok % (unsigned)P.V) * d;  // get_row_core: row token % V
-          for (int i = tid; i < d; i += kMkConsumers) {
-            const float v = __ldg(src + i);
-            S.xraw[i] = v;
-            ss = fmaf(v, v, ss);
-            bad |= (v != v);
-          }
+          for (int i = tid; i < d; i += kMkConsumers) raw[i] = __ldg(src + i);
         } else {
-          ok = ll_read(A.ll.xb, d, mk_epoch(A.epoch0, L, step, l - 1, 4), S.xraw, ss, bad);
-        }
-        if (!agree(S, ok, st)) return;
-        tmark(step, l, 0, 1);
-        if (A.block_k > 0 && l > 0) {  // the previous block's K-WTA (block/forward.rs:145-149)
-          mk_block_kwta(S.xraw, d, A.block_k, hist);
-          ss = 0.f;
-          for (int i = tid; i < d; i += kMkConsumers) ss = fmaf(S.xraw[i], S.xraw[i], ss);
-        }
-        for (int i = tid; i < d; i += kMkConsumers) S.xres[i] = S.xraw[i];
-        const float tot = consumer_sum(ss, red);
-        const int bad_in = consumer_any(bad, redi);
-        const float inv = 1.0f / sqrtf(tot / (float)d + P.eps);
-        int bad_out = 0;
-        mk_stage_x(S, d, wreg, inv, true, bad_out);
-        bad_out = consumer_any(bad_out, redi);  // also makes xs/xsum visible
-        if (blockIdx.x == 0 && tid == 0) {
-          if (bad_in) nan_flag(st, pos, l, kNanInput);
-          if (bad_out) nan_flag(st, pos, l, kNanAttnNorm);
-        }
-        // this block's cached K/V rows for the attention split: every writer of
-        // rows < pos finished before the x read above (acquire), so fetch now
-        if (au >= 0 && tid == 0) {
-          const int g = au % P.nkv, s = au / P.nkv, t0 = s * chunk;
-          const int n = min(ctx, t0 + chunk) - t0;
-          const int n_old = max(0, min(n, ctx - 1 - t0));
-          const uint32_t bytes = uint32_t(n_old) * hd * 4;
-          asm volatile("fence.proxy.async.global;" ::: "memory");
-          *S.kv_armed = *S.kv_armed + 1;
-          mbar_expect_tx(S.kv_bar, 2 * bytes);
-          if (bytes) {
-            bulk_g2s(S.kvbuf, Lw.kc + ((size_t)g * P.max_ctx + t0) * hd, bytes, S.kv_bar);
-            bulk_g2s(S.kvbuf + (size_t)pl.attn_chunk_cap * hd, Lw.vc + ((size_t)g * P.max_ctx + t0) * hd, bytes,
-                     S.kv_bar);
+          const int fl = ph == kPhGateup ? kFlXa : ph == kPhDown ? kFlAct : kFlXb;
+          const int nw = mk_writers(ph == kPhGateup ? pl.o : ph == kPhDown ? pl.g : pl.d);
+          const unsigned e_in = ph == kPhLm ? mk_epoch(A.epoch0, L, step, L - 1, 4) : e_out - 1;
+          const uint2* src = ph == kPhGateup ? A.ll.xa : ph == kPhDown ? A.ll.act : A.ll.xb;
+          mk_gate(A.ll.flags + fl * gridDim.x, nw, e_in, S.cabort, st);
+          tmark(step, pi, 1);
+          ok = ll_gather<kMkRound>(src, K, e_in, raw);
+          // the previous block's K-WTA (block/forward.rs:145-149; the last
+          // block's before the output norm)
+          if ((ph == kPhQkv || ph == kPhLm) && A.block_k > 0) {
+            if (!ok) *S.cabort = 1;
+            consumer_sync();
+            if (*S.cabort) return;
+            mk_block_kwta(raw, d, A.block_k, hist);
           }
         }
-        tmark(step, l, 0, 2);
-        const bool done = !has_q || gemv_phase(pl.q, Lw.qkv, 2, step, l, 0, [&](int a, int b) {
-          for (int u = a + tid; u < b; u += kMkConsumers) {
-            float y0 = rowsum[(u - a) * 2], y1 = rowsum[(u - a) * 2 + 1];
-            if (Lw.qkv.bias) {
-              y0 += Lw.qkv.bias[2 * u];
-              y1 += Lw.qkv.bias[2 * u + 1];
-            }
-            const int head = u / half, i = u - head * half;
-            const int c0 = P.rope_split ? i : 2 * i;
-            const int c1 = P.rope_split ? i + half : 2 * i + 1;
-            if (head < P.nh + P.nkv) {  // RoPE: v0*cos - v1*sin, v0*sin + v1*cos
-              const float2 cs = S.rope[i];
-              const float o0 = y0 * cs.x - y1 * cs.y;
-              const float o1 = y0 * cs.y + y1 * cs.x;
-              y0 = o0;
-              y1 = o1;
-            }
-            uint2* dst = head < P.nh ? A.ll.q + head * hd
-                                     : A.ll.kv + (head - P.nh) * hd;  // k heads then v heads
-            st_ll(dst + c0, y0, e_qkv);
-            st_ll(dst + c1, y1, e_qkv);
+        // one staging pass: x*w (pre-scaled, swizzled, with block sums) for
+        // the Q4 GEMVs; plain x*w for the f32 lm_head
+        const bool plain = ph == kPhLm;
+        for (int j = 0, i = tid; i < K; i += kMkConsumers, ++j) {
+          const float v = raw[i];
+          ss = fmaf(v, v, ss);
+          const float xv = v * pick(wreg, j);
+          if (plain) {
+            xs[i] = xv;
+          } else {
+            __syncwarp();  // DOWN stages in place: the warp's block is read before it is permuted
+            mk_stage_elem(xs, xsum, i, xv);
           }
-        });
-        if (!done) return;
-        tmark(step, l, 0, 4);
-        mark(step, 5 * l + 0);
+        }
       }
-      // ================================================ ATTN
-      if (au >= 0) {
-        tmark(step, l, 1, 0);
-        const int g = au % P.nkv, s = au / P.nkv, t0 = s * chunk;
-        const int n = min(ctx, t0 + chunk) - t0;
-        const int n_old = max(0, min(n, ctx - 1 - t0));
-        const int cap = pl.attn_chunk_cap;
-        float* Ks = S.kvbuf;
-        float* Vs = S.kvbuf + (size_t)cap * hd;
-        float* qs = S.xs;  // the group's q rows
-        float dummy_ss = 0.f;
-        int dummy_bad = 0;
-        bool ok = ll_read(A.ll.q + (size_t)g * G * hd, G * hd, e_qkv, qs, dummy_ss, dummy_bad);
-        if (ok && n > n_old) {  // this step's own row: LL, then into the cache for later steps
-          const uint2* kn = A.ll.kv + (size_t)g * hd;
-          const uint2* vn = A.ll.kv + (size_t)(P.nkv + g) * hd;
-          ok = ll_read(kn, hd, e_qkv, Ks + (size_t)n_old * hd, dummy_ss, dummy_bad) &&
-               ll_read(vn, hd, e_qkv, Vs + (size_t)n_old * hd, dummy_ss, dummy_bad);
-          if (ok)
-            for (int i = tid; i < hd; i += kMkConsumers) {
-              Lw.kc[((size_t)g * P.max_ctx + pos) * hd + i] = Ks[(size_t)n_old * hd + i];
-              Lw.vc[((size_t)g * P.max_ctx + pos) * hd + i] = Vs[(size_t)n_old * hd + i];
-            }
-        }
-        tmark(step, l, 1, 1);
-        // every consumer observes the copy's completion (parity of this use)
-        const int use = *S.kv_waited;
-        if (ok && !mbar_wait(S.kv_bar, use & 1)) ok = false;
-        if (!agree(S, ok, st)) return;
-        if (tid == 0) *S.kv_waited = use + 1;
-        tmark(step, l, 1, 2);
-        float* ps = S.ps;
-        for (int idx = tid; idx < G * n; idx += kMkConsumers) {
-          const int j = idx / n, t = idx - j * n;
-          const float* qr = qs + j * hd;
-          const float* kr = Ks + (size_t)t * hd;
-          float a0 = 0.f, a1 = 0.f;
-          int e0 = (t % hd) & ~1;
-          for (int e = 0; e < hd; e += 2) {
-            a0 = fmaf(qr[e0], kr[e0], a0);
-            a1 = fmaf(qr[e0 + 1], kr[e0 + 1], a1);
-            e0 += 2;
-            if (e0 >= hd) e0 -= hd;
-          }
-          ps[j * chunk + t] = (a0 + a1) * P.attn_scale;
-        }
-        consumer_sync();
-        for (int j = wid; j < G; j += kMkConsumerWarps) {
-          float m = -INFINITY;
-          for (int t = lane; t < n; t += kWarp) m = fmaxf(m, ps[j * chunk + t]);
-          m = warp_max(m);
-          float lsum = 0.f;
-          for (int t = lane; t < n; t += kWarp) {
-            const float ev = expf(ps[j * chunk + t] - m);
-            ps[j * chunk + t] = ev;
-            lsum += ev;
-          }
-          lsum = warp_sum(lsum);
-          if (lane == 0) {
-            mls[2 * j] = m;
-            mls[2 * j + 1] = lsum;
-          }
-        }
-        consumer_sync();
-        const size_t pbase = ((size_t)g * kAttnMaxSplits + s) * G;
-        for (int idx = tid; idx < G * hd; idx += kMkConsumers) {
-          const int j = idx / hd, e = idx - j * hd;
-          const float* pr = ps + j * chunk;
-          float a0 = 0.f, a1 = 0.f;
-          int t = 0;
-          for (; t + 1 < n; t += 2) {
-            a0 = fmaf(pr[t], Vs[(size_t)t * hd + e], a0);
-            a1 = fmaf(pr[t + 1], Vs[(size_t)(t + 1) * hd + e], a1);
-          }
-          if (t < n) a0 = fmaf(pr[t], Vs[(size_t)t * hd + e], a0);
-          P.part_o[(pbase + j) * hd + e] = a0 + a1;
-        }
-        if (tid < G) {
-          P.part_ml[(pbase + tid) * 2] = mls[2 * tid];
-          P.part_ml[(pbase + tid) * 2 + 1] = mls[2 * tid + 1];
-        }
-        __threadfence();  // partials and the new cache row before the arrival
-        consumer_sync();
-        tmark(step, l, 1, 3);
-        if (tid == 0) is_last = (atomicAdd(P.attn_cnt + g, 1u) == (unsigned)nsplit - 1u);
-        consumer_sync();
-        if (is_last) {
-          __threadfence();
-          for (int idx = tid; idx < G * nsplit; idx += kMkConsumers) {
-            const int j = idx / nsplit, r = idx - j * nsplit;
-            wsh[idx] = __ldcg(P.part_ml + (((size_t)g * kAttnMaxSplits + r) * G + j) * 2);
-          }
-          consumer_sync();
-          for (int j = wid; j < G; j += kMkConsumerWarps) {
-            float M = -INFINITY;
-            for (int r = lane; r < nsplit; r += kWarp) M = fmaxf(M, wsh[j * nsplit + r]);
-            M = warp_max(M);
-            float Ls = 0.f;
-            for (int r = lane; r < nsplit; r += kWarp) {
-              const float wgt = expf(wsh[j * nsplit + r] - M);
-              wsh[j * nsplit + r] = wgt;
-              Ls += __ldcg(P.part_ml + (((size_t)g * kAttnMaxSplits + r) * G + j) * 2 + 1) * wgt;
-            }
-            Ls = warp_sum(Ls);
-            if (lane == 0) linv[j] = 1.0f / (Ls + 1e-12f);
-          }
-          consumer_sync();
-          if (tid == 0) P.attn_cnt[g] = 0u;  // reset before the release below
-          fence_acq_rel_gpu();
-          for (int idx = tid; idx < G * hd; idx += kMkConsumers) {
-            const int j = idx / hd, e = idx - j * hd;
-            float O0 = 0.f, O1 = 0.f;
-            int r = 0;
-            for (; r + 1 < nsplit; r += 2) {
-              O0 += __ldcg(P.part_o + (((size_t)g * kAttnMaxSplits + r) * G + j) * hd + e) * wsh[j * nsplit + r];
-              O1 += __ldcg(P.part_o + (((size_t)g * kAttnMaxSplits + r + 1) * G + j) * hd + e) *
-                    wsh[j * nsplit + r + 1];
-            }
-            if (r < nsplit)
-              O0 += __ldcg(P.part_o + (((size_t)g * kAttnMaxSplits + r) * G + j) * hd + e) * wsh[j * nsplit + r];
-            st_ll(A.ll.attn + ((size_t)g * G + j) * hd + e, (O0 + O1) * linv[j], e_attn);
-          }
-        }
-        consumer_sync();
-        tmark(step, l, 1, 4);
+      float tot;
+      if (!ok) {
+        flag_timeout(st, 13);
+        *S.cabort = 1;
       }
-      mark(step, 5 * l + 1);
-      // ================================================ OPROJ
-      if (has_o) {
-        tmark(step, l, 2, 0);
-        float ss = 0.f;
-        int bad = 0;
-        const bool ok = ll_read(A.ll.attn, Lw.wo.K, e_attn, S.xraw, ss, bad);
-        if (!agree(S, ok, st)) return;
-        tmark(step, l, 2, 1);
-        int bo = 0;
-        mk_stage_x(S, Lw.wo.K, nullptr, 1.0f, false, bo);
-        consumer_sync();
-        tmark(step, l, 2, 2);
-        const bool done = gemv_phase(pl.o, Lw.wo, 1, step, l, 2, [&](int a, int b) {
-          for (int r = a + tid; r < b; r += kMkConsumers) {
-            float y = rowsum[r - a];
-            if (Lw.wo.bias) y += Lw.wo.bias[r];
-            st_ll(A.ll.xa + r, S.xres[r] + y, e_o);
+      tot = consumer_total(ss, red[ph_count & 1]);
+      ++ph_count;
+      if (*S.cabort) return;
+      tmark(step, pi, 2);
+      // the norm's 1/rms (QKV, GATEUP, LM) or the genomic scale (DOWN) of the row dots
+      float scale = 1.0f;
+      if (norm) scale = 1.0f / sqrtf(tot / (float)d + P.eps);
+      if (ph == kPhDown && P.use_genomic_norm) {  // block/forward.rs:115-123, h_scale = 1
+        const float rms = sqrtf(tot / (float)P.ff + P.eps);
+        if (rms > 1.0f) scale = 1.0f / rms;
+      }
+      if (ph == kPhLm) {
+        // ============================================ lm_head + argmax
+        const float4* x4 = reinterpret_cast<const float4*>(xs);
+        const int K4 = d >> 2;
+        unsigned long long best = 0ull;
+        const int rbeg = blockIdx.x * pl.lm_rows_per_cta;
+        const int nrows = max(0, min(P.V, rbeg + pl.lm_rows_per_cta) - rbeg);
+        const int nitems = (nrows + pl.lm_stage_rows - 1) / pl.lm_stage_rows;
+        // warp w takes rows w, w+15, ...; it waits for (and releases) every
+        // stage in order, also the ones holding none of its rows
+        int cur = -1;
+        const unsigned char* slot = nullptr;
+        for (int k = wid; k < nrows; k += kMkConsumerWarps) {
+          const int it = k / pl.lm_stage_rows;
+          while (cur < it) {
+            if (cur >= 0) release(A, S, item + cur);
+            ++cur;
+            slot = wait_slot(A, S, item + cur);
           }
-        });
-        if (!done) return;
-        tmark(step, l, 2, 4);
-        mark(step, 5 * l + 2);
-      }
-      // ================================================ GATEUP
-      if (has_g || has_d) {
-        tmark(step, l, 3, 0);
-        float wreg[kMkMaxNormVec];
-#pragma unroll
-        for (int k = 0; k < kMkMaxNormVec; ++k) {
-          const int i = tid + k * kMkConsumers;
-          wreg[k] = i < d ? Lw.ffn_norm[i] : 0.f;
-        }
-        float ss = 0.f;
-        int bad = 0;
-        const bool ok = ll_read(A.ll.xa, d, e_o, S.xraw, ss, bad);
-        if (!agree(S, ok, st)) return;
-        tmark(step, l, 3, 1);
-        for (int i = tid; i < d; i += kMkConsumers) S.xres[i] = S.xraw[i];
-        const float tot = consumer_sum(ss, red);
-        const float inv = 1.0f / sqrtf(tot / (float)d + P.eps);
-        int bo = 0;
-        mk_stage_x(S, d, wreg, inv, true, bo);
-        consumer_sync();
-        tmark(step, l, 3, 2);
-        const bool done = !has_g || gemv_phase(pl.g, Lw.gate_up, 2, step, l, 3, [&](int a, int b) {
-          for (int u = a + tid; u < b; u += kMkConsumers) {
-            float gv = rowsum[(u - a) * 2], uv = rowsum[(u - a) * 2 + 1];
-            if (Lw.gate_up.bias) {
-              gv += Lw.gate_up.bias[2 * u];
-              uv += Lw.gate_up.bias[2 * u + 1];
-            }
-            if (uv != uv) nan_flag(st, pos, l, kNanUp);
-            const float act = swiglu_balanced(gv, uv);
-            if (act != act) nan_flag(st, pos, l, kNanFfnOut);
-            st_ll(A.ll.act + u, act, e_gu);
-          }
-        });
-        if (!done) return;
-        tmark(step, l, 3, 4);
-        mark(step, 5 * l + 3);
-      }
-      // ================================================ DOWN
-      if (has_d) {
-        tmark(step, l, 4, 0);
-        float ss = 0.f;
-        int bad = 0;
-        const bool ok = ll_read(A.ll.act, P.ff, e_gu, S.xraw, ss, bad);
-        if (!agree(S, ok, st)) return;
-        tmark(step, l, 4, 1);
-        float scale = 1.0f;
-        if (P.use_genomic_norm) {  // block/forward.rs:115-123, h_scale = 1
-          const float tot = consumer_sum(ss, red);
-          const float rms = sqrtf(tot / (float)P.ff + P.eps);
-          if (rms > 1.0f) scale = 1.0f / rms;
-        }
-        int bo = 0;
-        if (scale != 1.0f)
-          for (int i = tid; i < P.ff; i += kMkConsumers) S.xraw[i] = S.xraw[i] * scale;
-        consumer_sync();
-        mk_stage_x(S, P.ff, nullptr, 1.0f, false, bo);
-        consumer_sync();
-        tmark(step, l, 4, 2);
-        const bool done = gemv_phase(pl.d, Lw.down, 1, step, l, 4, [&](int a, int b) {
-          for (int r = a + tid; r < b; r += kMkConsumers) {
-            float y = rowsum[r - a];
-            if (Lw.down.bias) y += Lw.down.bias[r];
-            if (y != y) nan_flag(st, pos, l, kNanProjFfn);
-            const float xn = S.xres[r] + y;
-            if (xn != xn) nan_flag(st, pos, l, kNanResidual);
-            st_ll(A.ll.xb + r, xn, e_down);
-          }
-        });
-        if (!done) return;
-        tmark(step, l, 4, 4);
-        mark(step, 5 * l + 4);
-      }
-    }
-    // ================================================== LM
-    {
-      tmark(step, L, 0, 0);
-      float wreg[kMkMaxNormVec];
-#pragma unroll
-      for (int k = 0; k < kMkMaxNormVec; ++k) {
-        const int i = tid + k * kMkConsumers;
-        wreg[k] = i < d ? P.out_norm[i] : 0.f;
-      }
-      float ss = 0.f;
-      int bad = 0;
-      const bool ok = ll_read(A.ll.xb, d, mk_epoch(A.epoch0, L, step, L - 1, 4), S.xraw, ss, bad);
-      if (!agree(S, ok, st)) return;
-      tmark(step, L, 0, 1);
-      if (A.block_k > 0) {  // the last block's K-WTA
-        mk_block_kwta(S.xraw, d, A.block_k, hist);
-        ss = 0.f;
-        for (int i = tid; i < d; i += kMkConsumers) ss = fmaf(S.xraw[i], S.xraw[i], ss);
-      }
-      const float tot = consumer_sum(ss, red);
-      const float inv = 1.0f / sqrtf(tot / (float)d + P.eps);
-      {
-        int k = 0;
-        for (int i = tid; i < d; i += kMkConsumers, ++k) S.xs[i] = (S.xraw[i] * inv) * wreg[k];  // plain layout
-      }
-      consumer_sync();
-      tmark(step, L, 0, 2);
-      const float4* x4 = reinterpret_cast<const float4*>(S.xs);
-      const int K4 = d >> 2;
-      unsigned long long best = 0ull;
-      const int rbeg = blockIdx.x * pl.lm_rows_per_cta;
-      const int rend = min(P.V, rbeg + pl.lm_rows_per_cta);
-      for (int r = rbeg; r < rend; r += pl.lm_stage_rows) {
-        const int rows = min(pl.lm_stage_rows, rend - r);
-        const unsigned char* slot = take(A, S, item);
-        if (!slot) return;
-        if (r == rbeg) tmark(step, L, 0, 3);
-        for (int rr = wid; rr < rows; rr += kMkConsumerWarps) {
-          const float4* w4 = reinterpret_cast<const float4*>(slot) + (size_t)rr * K4;
+          if (k == 0) tmark(step, pi, 5);
+          const float4* w4 = reinterpret_cast<const float4*>(slot) + (size_t)(k - it * pl.lm_stage_rows) * K4;
           float a0 = 0.f, a1 = 0.f;
           for (int j = lane; j < K4; j += kWarp) {
             const float4 u = w4[j], xv = x4[j];
@@ -889,53 +998,140 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
             a0 = fmaf(u.z, xv.z, a0);
             a1 = fmaf(u.w, xv.w, a1);
           }
-          float sacc = warp_sum(a0 + a1);
-          const int row = r + rr;
-          if (P.lm_bias) sacc += P.lm_bias[row];
+          const int row = rbeg + k;
+          float sacc = warp_sum(a0 + a1) * scale;
+          if (P.lm_bias) sacc += __ldg(P.lm_bias + row);
           if (lane == 0) P.logits[row] = sacc;
           const unsigned long long key = amax_key(sacc, (unsigned)row);
           best = key > best ? key : best;
         }
-        release(A, S, item++);
-      }
-      best = warp_max_u64(best);
-      if (lane == 0) wbest[wid] = best;
-      consumer_sync();
-      if (tid == 0) {
-        unsigned long long b = 0;
-        for (int i = 0; i < kMkConsumerWarps; ++i) b = wbest[i] > b ? wbest[i] : b;
-        P.amax_part[blockIdx.x] = b;
-        __threadfence();
-        is_last = (atomicAdd(P.amax_cnt, 1u) == gridDim.x - 1u);
-      }
-      consumer_sync();
-      if (is_last) {
-        __threadfence();
-        unsigned long long b = 0;
-        for (int i = tid; i < (int)gridDim.x; i += kMkConsumers) {
-          const unsigned long long v = __ldcg(P.amax_part + i);
-          b = v > b ? v : b;
+        while (cur < nitems - 1) {
+          if (cur >= 0) release(A, S, item + cur);
+          ++cur;
+          wait_slot(A, S, item + cur);
         }
-        b = warp_max_u64(b);
-        if (lane == 0) wbest[wid] = b;
+        if (cur >= 0) release(A, S, item + cur);
+        item += nitems;
+        tmark(step, pi, 3);
+        best = warp_max_u64(best);
+        if (lane == 0) wbest[wid] = best;
         consumer_sync();
+        if (*S.cabort) return;
         if (tid == 0) {
-          unsigned long long r = 0;
-          for (int i = 0; i < kMkConsumerWarps; ++i) r = wbest[i] > r ? wbest[i] : r;
-          const unsigned idx = amax_index(r);
-          st->argmax = idx;
-          st->token = idx;
-          if (st->hist_len < P.hist_cap) P.tok_hist[st->hist_len] = idx;
-          st->hist_len += 1u;
-          st->pos = pos + 1u;
-          *P.amax_cnt = 0u;
-          fence_acq_rel_gpu();  // the state and the counter reset before the token word
-          st_ll(A.ll.tok, __uint_as_float(idx), mk_epoch(A.epoch0, L, step, L, 0));
+          unsigned long long b = 0;
+          for (int i = 0; i < kMkConsumerWarps; ++i) b = wbest[i] > b ? wbest[i] : b;
+          P.amax_part[blockIdx.x] = b;
+          __threadfence();
+          is_last = (atomicAdd(P.amax_cnt, 1u) == gridDim.x - 1u);
+        }
+        consumer_sync();
+        if (is_last) {
+          __threadfence();
+          unsigned long long b = 0;
+          for (int i = tid; i < (int)gridDim.x; i += kMkConsumers) {
+            const unsigned long long v = __ldcg(P.amax_part + i);
+            b = v > b ? v : b;
+          }
+          b = warp_max_u64(b);
+          if (lane == 0) wbest[wid] = b;
+          consumer_sync();
+          if (tid == 0) {
+            unsigned long long r = 0;
+            for (int i = 0; i < kMkConsumerWarps; ++i) r = wbest[i] > r ? wbest[i] : r;
+            const unsigned idx = amax_index(r);
+            st->argmax = idx;
+            st->token = idx;
+            if (st->hist_len < P.hist_cap) P.tok_hist[st->hist_len] = idx;
+            st->hist_len += 1u;
+            st->pos = pos + 1u;
+            *P.amax_cnt = 0u;
+            fence_acq_rel_gpu();  // the state and the counter reset before the token word
+            st_ll(A.ll.tok, __uint_as_float(idx), mk_epoch(A.epoch0, L, step, L, 0));
+          }
+        }
+        consumer_sync();
+        tmark(step, pi, 4);
+        if (A.phase_ns && blockIdx.x == 0 && tid == 0) A.phase_ns[(size_t)step * (5 * L + 1) + pi] = global_ns();
+        continue;
+      }
+      if (ph == kPhQkv) {
+        if (blockIdx.x == 0)  // block/forward.rs:11-13 and :22-24 on this thread's elements
+          for (int j = 0, i = tid; i < d; i += kMkConsumers, ++j) {
+            const float v = raw[i];
+            if (v != v) nan_flag(st, pos, l, kNanInput);
+            const float nv = (v * scale) * pick(wreg, j);
+            if (nv != nv) nan_flag(st, pos, l, kNanAttnNorm);
+          }
+        // this block's cached K/V rows for the attention split: every writer
+        // of rows < pos fenced its row before publishing (a step or more ago)
+        if (au >= 0 && tid == 0) {
+          const int g = au % P.nkv, s = au / P.nkv, t0 = s * chunk;
+          const int n = min(ctx, t0 + chunk) - t0;
+          const int n_old = max(0, min(n, ctx - 1 - t0));
+          const uint32_t bytes = uint32_t(n_old) * hd * 4;
+          fence_acq_rel_gpu();
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          *S.kv_armed = *S.kv_armed + 1;
+          mbar_expect_tx(S.kv_bar, 2 * bytes);
+          if (bytes) {
+            bulk_g2s(S.kvbuf, Lw.kc + ((size_t)g * P.max_ctx + t0) * hd, bytes, S.kv_bar);
+            bulk_g2s(S.kvbuf + (size_t)cap * hd, Lw.vc + ((size_t)g * P.max_ctx + t0) * hd, bytes, S.kv_bar);
+          }
         }
       }
-      consumer_sync();
-      tmark(step, L, 0, 4);
-      mark(step, 5 * L);
+      const bool gemv_here = ph == kPhQkv ? has_q : ph == kPhOproj ? has_o : ph == kPhGateup ? has_g : has_d;
+      if (gemv_here) {
+        const int ub = (int)blockIdx.x * gp.upc;  // this CTA's first unit of the phase
+        unsigned long long* fr =
+            A.trace_ns ? A.trace_ns + (((size_t)blockIdx.x * A.n_steps + step) * (5 * L + 1) + pi) * kMkTrace + 5
+                       : nullptr;
+        mk_gemv(A, S, gp, W, rpu, xs, xsum, item, fr, [&](int a, int r, float y0, float y1, bool has1) {
+          if (ph == kPhQkv) {
+            const int u = a + (r >> 1);
+            y0 = flush_small(y0 * scale) + bsm[2 * (u - ub)];
+            y1 = flush_small(y1 * scale) + bsm[2 * (u - ub) + 1];
+            const int head = u / half, i = u - head * half;
+            const int c0 = P.rope_split ? i : 2 * i;
+            const int c1 = P.rope_split ? i + half : 2 * i + 1;
+            if (head < P.nh + P.nkv) {  // RoPE: v0*cos - v1*sin, v0*sin + v1*cos
+              const float2 cs = rope[i];
+              const float o0 = y0 * cs.x - y1 * cs.y;
+              const float o1 = y0 * cs.y + y1 * cs.x;
+              y0 = o0;
+              y1 = o1;
+            }
+            uint2* dst = head < P.nh ? A.ll.q + head * hd
+                                     : A.ll.kv + (head - P.nh) * hd;  // k heads then v heads
+            st_ll(dst + c0, y0, e_out);
+            st_ll(dst + c1, y1, e_out);
+          } else if (ph == kPhGateup) {
+            const int u = a + (r >> 1);
+            const float gv = flush_small(y0 * scale) + bsm[2 * (u - ub)];
+            const float uv = flush_small(y1 * scale) + bsm[2 * (u - ub) + 1];
+            if (uv != uv) nan_flag(st, pos, l, kNanUp);
+            const float act = swiglu_balanced(gv, uv);
+            if (act != act) nan_flag(st, pos, l, kNanFfnOut);
+            st_ll(A.ll.act + u, act, e_out);
+          } else {  // OPROJ, DOWN: rows a + r (+1) with the residual
+            const int row = a + r;
+            const float* xr = ph == kPhOproj ? S.xres[0] : S.xres[1];
+            uint2* dst = ph == kPhOproj ? A.ll.xa : A.ll.xb;
+            for (int k = 0; k < 2; ++k) {
+              if (k == 1 && !has1) break;
+              const float y = flush_small((k ? y1 : y0) * scale) + bsm[row + k - ub];
+              if (ph == kPhDown && y != y) nan_flag(st, pos, l, kNanProjFfn);
+              const float xn = xr[row + k] + y;
+              if (ph == kPhDown && xn != xn) nan_flag(st, pos, l, kNanResidual);
+              st_ll(dst + row + k, xn, e_out);
+            }
+          }
+        });
+        tmark(step, pi, 3);
+        const int flo = ph == kPhQkv ? kFlQkv : ph == kPhOproj ? kFlXa : ph == kPhGateup ? kFlAct : kFlXb;
+        mk_publish(A.ll.flags + flo * gridDim.x, e_out);
+      }
+      tmark(step, pi, 4);
+      if (A.phase_ns && blockIdx.x == 0 && tid == 0) A.phase_ns[(size_t)step * (5 * L + 1) + pi] = global_ns();
     }
   }
 }
@@ -956,12 +1152,14 @@ __global__ void __launch_bounds__(kMkThreads, 1) k_decode_mega(MegaArgs A) {
   float* f = reinterpret_cast<float*>(smem_raw + kMkHeader);
   S.xs = f;
   f += pl.xs_floats;
-  S.xraw = f;
-  f += pl.xs_floats;
   S.xsum = f;
-  f += pl.xs_floats / 32;
-  S.xres = f;
-  f += (A.P.d + 31) / 32 * 32;
+  f += mk_round32(pl.xs_floats / 32);
+  for (int k = 0; k < 2; ++k) {
+    S.xres[k] = f;
+    f += mk_round32(A.P.d);
+  }
+  S.qbuf = f;
+  f += mk_round32(pl.qbuf_floats);
   S.ps = f;
   f += pl.ps_floats;
   S.kvbuf = f;
@@ -969,8 +1167,18 @@ __global__ void __launch_bounds__(kMkThreads, 1) k_decode_mega(MegaArgs A) {
   S.part = f;
   f += kMkPartFloats;
   S.rope = reinterpret_cast<float2*>(f);
-  f += hd;
-  S.slots = reinterpret_cast<unsigned char*>(f);
+  f += 2 * hd;
+  S.bias = f;
+  f += 2 * pl.bias_floats;
+  {  // the LayerW table: every phase reads its pointers and shapes from here
+    unsigned char* lb = reinterpret_cast<unsigned char*>(f);
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(A.layers);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(lb);
+    const int words = A.P.n_layers * int(sizeof(LayerW) / 4);
+    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+    S.layers = reinterpret_cast<const LayerW*>(lb);
+    S.slots = lb + pl.layers_bytes;
+  }
   if (threadIdx.x == 0) {
     for (int i = 0; i < pl.nslots; ++i) {
       mbar_init(S.full + i, 1);

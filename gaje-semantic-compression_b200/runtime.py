@@ -351,7 +351,7 @@ class GenomicLLM:
 
     PHASES = ("qkv", "attn", "oproj", "gateup", "down", "lmhead")
 
-    DETAIL = ("to_entry", "to_inputs", "to_staged", "to_slot", "to_done")
+    DETAIL = ("to_entry", "to_flags", "to_staged", "to_rows", "to_published")
 
     def profile_phases(self, first_token: int, n_steps: int, detail: bool = False) -> dict:
         """Greedy steps in the persistent kernel with a timer stamp at every grid
@@ -371,11 +371,12 @@ class GenomicLLM:
 
     def trace_steps(self, first_token: int, n_steps: int) -> np.ndarray:
         """Every CTA's trace stamps (ns) of n_steps greedy steps in one launch:
-        shape [grid, n_steps, 5*n_blocks+1, 5] (points: entry, inputs arrived,
-        staged, first slot, done; 0 where a CTA had no work in that phase)."""
+        shape [grid, n_steps, 5*n_blocks+1, 6] (points: entry, input flags
+        seen, staged, rows done, published, first weight slot ready; 0 where a
+        CTA had no work in that phase)."""
         inf = self.info()
         per = 5 * inf.n_blocks + 1
-        out = np.zeros((inf.grid, int(n_steps), per, 5), dtype=np.uint64)
+        out = np.zeros((inf.grid, int(n_steps), per, 6), dtype=np.uint64)
         n = C.c_size_t(0)
         _check(lib().gaje_cuda_trace_steps(self._m, int(first_token), int(n_steps), _ptr(out), C.c_size_t(out.size),
                                            C.byref(n)))

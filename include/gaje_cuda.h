@@ -218,10 +218,10 @@ enum gaje_phase {
  * (nullable, GAJE_PH_COUNT*5 floats) receives, per phase kind p, the mean
  * microseconds per step CTA 0 spent between consecutive trace points:
  *   [p*5+0] previous phase done -> phase entered
- *   [p*5+1] -> inputs arrived (attention: q and the new k/v rows)
- *   [p*5+2] -> inputs staged in shared memory (attention: cached K/V landed)
- *   [p*5+3] -> first weight slot taken (attention: split partials published)
- *   [p*5+4] -> phase outputs published
+ *   [p*5+1] -> the input's publication flags seen
+ *   [p*5+2] -> input staged in shared memory (attention: cached K/V landed)
+ *   [p*5+3] -> rows done (attention: scores done)
+ *   [p*5+4] -> outputs published
  * GAJE_ERR_UNSUPPORTED when the model runs on the kernel-per-phase engine.
  * The reference's counterpart is the GAJE_PROFILE_VERBOSE timing of
  * src/nn/llm/forward.rs:23-55. */
@@ -229,10 +229,12 @@ int gaje_cuda_profile_phases(gaje_model* model, uint32_t first_token, size_t n_s
                              float* us, float* step_us, float* detail_us);
 
 /* The raw form of the above for every CTA: n_steps (<= 4096) greedy steps in
- * one launch; out[((cta*n_steps + step)*(5L+1) + 5l+p)*5 + k] is the
- * %globaltimer value (ns) of trace point k (the order above) of phase p of
- * block l (the lm_head phase at 5L) on that CTA, 0 where the CTA had no work of
- * that phase.  out_len must be at least grid*n_steps*(5L+1)*5 (grid =
+ * one launch; out[((cta*n_steps + step)*(5L+1) + 5l+p)*6 + k] is the
+ * %globaltimer value (ns) of trace point k of phase p of block l (the lm_head
+ * phase at 5L) on that CTA, 0 where the CTA had no work of that phase.  Points:
+ * 0 entry, 1 input flags seen, 2 input staged (attention: cached K/V landed),
+ * 3 rows done (attention: scores done), 4 outputs published, 5 first weight
+ * slot ready.  out_len must be at least grid*n_steps*(5L+1)*6 (grid =
  * gaje_model_info.grid); *n_written receives the count.  No counterpart in the
  * reference: a diagnostic of the persistent kernel's critical path. */
 int gaje_cuda_trace_steps(gaje_model* model, uint32_t first_token, size_t n_steps,
