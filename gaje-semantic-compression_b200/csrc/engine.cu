@@ -1366,6 +1366,72 @@ int gaje_cuda_attention_decode(const float* q, const float* k_cache, const float
   return GAJE_OK;
 }
 
+// ---- decode attention without allocation
+// The same kernel as gaje_cuda_attention_decode with its split partials and
+// per-KV-head counters in this file-scope buffer instead of the per-device
+// workspace (which is allocated, and re-allocated with a device synchronise
+// when a larger geometry arrives).
+constexpr size_t kAttnStaticScratchBytes = size_t(1) << 20;  // 1 MiB per device
+static __device__ __align__(256) unsigned char g_attn_scratch[kAttnStaticScratchBytes];
+static std::mutex g_attn_scratch_mu;
+static void* g_attn_scratch_ptr[64] = {};
+
+int gaje_cuda_attention_decode_static(const float* q, const float* k_cache, const float* v_cache, size_t ctx,
+                                      size_t cache_stride, size_t n_head, size_t n_head_kv, size_t head_dim,
+                                      float* out, void* stream) {
+  if (!q || !k_cache || !v_cache || !out || !ctx || !n_head || !n_head_kv || !head_dim)
+    return set_error(GAJE_ERR_INVALID, "bad argument");
+  if (n_head % n_head_kv || n_head / n_head_kv > size_t(kAttnMaxGroup) || ctx > cache_stride || head_dim % 4 ||
+      n_head_kv > 64 || cache_stride > (1u << 24))
+    return set_error(GAJE_ERR_UNSUPPORTED, "unsupported attention geometry");
+  const size_t G = n_head / n_head_kv;
+  const size_t po = n_head_kv * kAttnMaxSplits * G * head_dim, pml = n_head_kv * kAttnMaxSplits * G * 2;
+  const size_t need = 256 + (pml + po) * 4;
+  if (need > kAttnStaticScratchBytes)
+    return set_error(GAJE_ERR_UNSUPPORTED,
+                     "attention geometry needs " + std::to_string(need) +
+                         " bytes of scratch (256 + n_head*64*(head_dim+2)*4); the static buffer holds " +
+                         std::to_string(kAttnStaticScratchBytes));
+  int dev;
+  CK(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return set_error(GAJE_ERR_INVALID, "device ordinal out of range");
+  char* w;
+  {
+    std::lock_guard<std::mutex> lk(g_attn_scratch_mu);
+    if (!g_attn_scratch_ptr[dev]) {  // once per device, with that device current
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);
+      if (e != cudaSuccess || !p)
+        return set_error(GAJE_ERR_CUDA, std::string("cudaGetSymbolAddress of the attention scratch failed: ") +
+                                            cudaGetErrorString(e));
+      g_attn_scratch_ptr[dev] = p;
+    }
+    w = static_cast<char*>(g_attn_scratch_ptr[dev]);
+  }
+  AttnArgs a{};
+  a.q = q;
+  a.kc = k_cache;
+  a.vc = v_cache;
+  a.out = out;
+  a.cnt = reinterpret_cast<unsigned*>(w);  // zero at module load; every completed call leaves them zero
+  a.part_ml = reinterpret_cast<float*>(w + 256);
+  a.part_o = a.part_ml + pml;
+  a.ctx = int(ctx);
+  a.stride = int(cache_stride);
+  a.nh = int(n_head);
+  a.nkv = int(n_head_kv);
+  a.hd = int(head_dim);
+  a.scale = 1.0f / sqrtf(float(head_dim));
+  a.st = nullptr;
+  int nsplit, chunk;
+  attn_splits(int(ctx), nsplit, chunk);
+  const size_t smem = attn_smem_bytes(int(G), int(head_dim), chunk);
+  if (int s = smem_optin((const void*)k_attn, smem)) return s;
+  CK(launch_k(k_attn, dim3(unsigned(n_head_kv), kAttnMaxSplits), dim3(kAttnThreads), smem, (cudaStream_t)stream,
+              false, a));
+  return GAJE_OK;
+}
+
 int gaje_cuda_kwta(float* scores, size_t n, size_t k, void* stream) {
   if (!scores) return set_error(GAJE_ERR_INVALID, "scores is NULL");
   if (n > 0x7FFFFFFFu) return set_error(GAJE_ERR_INVALID, "n too large");

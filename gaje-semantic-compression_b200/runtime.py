@@ -136,6 +136,7 @@ def lib() -> C.CDLL:
         "gaje_cuda_profile_steps": ([vp, u32, sz, vp, vp], i32),
         "gaje_cuda_profile_phases": ([vp, u32, sz, vp, vp, vp], i32),
         "gaje_cuda_trace_steps": ([vp, u32, sz, vp, sz, vp], i32),
+        "gaje_cuda_attention_decode_static": ([vp, vp, vp, sz, sz, sz, sz, sz, vp, vp], i32),
         "gaje_cuda_q4_0_upload": ([vp, sz, sz, vp, i32], vp),
         "gaje_cuda_q4_0_release": ([vp], None),
         "gaje_cuda_q4_0_gemv": ([vp, vp, vp, sz, vp], i32),

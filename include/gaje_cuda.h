@@ -279,6 +279,31 @@ int gaje_cuda_attention_decode(const float* q, const float* k_cache, const float
                                size_t n_head_kv, size_t head_dim, float* out,
                                void* stream);
 
+/* gaje_cuda_attention_decode without any device allocation, for callers that
+ * must not allocate device memory on the call path: a host that budgets all of
+ * its device memory at start-up, or one that cannot take the device-wide
+ * synchronisation a cudaMalloc/cudaFree brings (gaje_cuda_attention_decode
+ * allocates its per-device workspace on first use and re-allocates it, with a
+ * device synchronise, when a larger geometry arrives).  No counterpart in the
+ * reference, whose attention runs on the CPU.
+ *
+ * Same arguments, results and kernel as gaje_cuda_attention_decode.  The
+ * split partials and the per-KV-head counters live in a 1 MiB buffer of static
+ * device memory per device: the geometry must satisfy
+ *   256 + n_head * 64 * (head_dim + 2) * 4 <= 1048576 bytes
+ * (e.g. n_head 14 / head_dim 64, n_head 12 / head_dim 128); a larger one is
+ * rejected with GAJE_ERR_UNSUPPORTED and a message giving both sizes.  The
+ * counters (the first 256 bytes) must be zero when a call starts: they are
+ * zero when the library loads and every completed call leaves them zero.  The
+ * first call on a device looks the buffer's address up with
+ * cudaGetSymbolAddress (with that device current); make that first call before
+ * any stream capture.  Calls that overlap on the same device race on the one
+ * buffer: serialise them (one stream, or events). */
+int gaje_cuda_attention_decode_static(const float* q, const float* k_cache, const float* v_cache,
+                                      size_t ctx, size_t cache_stride, size_t n_head,
+                                      size_t n_head_kv, size_t head_dim, float* out,
+                                      void* stream);
+
 /* lateral_inhibition_kwta (src/compute/kernels/lut.rs:45-61) in place on
  * scores[n] (device): values below the k-th largest become -1e9. */
 int gaje_cuda_kwta(float* scores, size_t n, size_t k, void* stream);
