@@ -121,8 +121,9 @@ def _peaks() -> dict:
     p = os.path.join(REPO, "MEASURED_PEAKS.json")
     if os.path.exists(p):
         d = json.load(open(p))
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d.get("bf16_tflops", 1590.0)),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
 
 
 def _ncu_traffic(kernel: str, cfg_key: str):
@@ -348,6 +349,62 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> None:
     print(json.dumps(line), flush=True)
 
 
+SWEEP_NK = [(896, 896), (4864, 896), (896, 4864), (8960, 1536), (1536, 8960)]
+SWEEP_M = [1, 8, 64, 512]
+
+
+def run_sweep(args) -> None:
+    """the isolated Q4_0 dequant-GEMV/GEMM sweep.  One
+    JSON line per (M, N, K): weights N(0, 0.02) quantised by the Q4_0 quantiser,
+    activations N(0, 1); each launch timed alone with CUDA events after an L2
+    flush (a 256 MB write), median of the timed launches.  GB/s counts the
+    weight bytes N*(K/32)*20 plus activations and outputs 4*M*(K+N); TFLOP/s
+    counts 2*M*N*K."""
+    import numpy as np
+    import torch
+
+    g = _pkg()
+    torch.cuda.set_device(0)
+    peaks = _peaks()
+    flush = torch.empty(64 << 20, dtype=torch.float32, device="cuda")
+    reps = max(3, args.steps if args.steps != 256 else 20)
+    for (N, K) in SWEEP_NK:
+        rng = np.random.default_rng(N * 7 + K)
+        W = (rng.standard_normal((N, K)) * 0.02).astype(np.float32)
+        mat = g.Q4Matrix(np.frombuffer(g.quantize_q4_0_native(W), dtype=np.uint8), N, K)
+        for M in SWEEP_M:
+            x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).cuda()
+            y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+            times = []
+            for it in range(reps + 3):
+                flush.fill_(float(it))
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record()
+                mat.gemv(x.data_ptr(), y.data_ptr(), M)
+                e1.record()
+                e1.synchronize()
+                if it >= 3:
+                    times.append(e0.elapsed_time(e1) / 1000.0)
+            t = statistics.median(times)
+            wbytes = N * (K // 32) * 20
+            nbytes = wbytes + 4 * M * (K + N)
+            flops = 2.0 * M * N * K
+            gbs, tfl = nbytes / t / 1e9, flops / t / 1e12
+            bound = "hbm" if M <= 8 else "tensor"
+            line = {"metric": "q4_0 dequant-GEMV/GEMM", "config": {"workload": "configs[2] sweep", "M": M, "N": N,
+                                                                 "K": K, "l2": "flushed (256 MB write) before each launch"},
+                    "us": round(t * 1e6, 2), "gbs": round(gbs, 1), "tflops": round(tfl, 3),
+                    "kernel": "k_gemv<G_PLAIN>" if M == 1 else "k_q4_gemm_skinny<8> (CUDA cores)",
+                    "roofline": {"bound": bound,
+                                 "achieved": round(gbs if bound == "hbm" else tfl, 3),
+                                 "peak": peaks["hbm_gbs"] if bound == "hbm" else peaks.get("bf16_tflops"),
+                                 "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
+                                 "frac": round(gbs / peaks["hbm_gbs"] if bound == "hbm"
+                                               else tfl / peaks.get("bf16_tflops", 1.0), 4)}}
+            print(json.dumps(line), flush=True)
+        del mat
+
+
 def run_ncu_case(args) -> None:
     """Two launches of the persistent kernel on one GPU: PROMPT_LEN greedy steps
     (the context a bench step sees), then args.steps steps, the launch a
@@ -375,6 +432,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default=CONFIG_KEY)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", action="store_true",
+                    help="the isolated Q4_0 GEMV/GEMM sweep of configs[2] instead of the decode benchmark")
     ap.add_argument("--ncu-case", action="store_true",
                     help="the small profiling case: one launch filling the prompt's positions, then one "
                          "launch of --steps decode steps (capture it with -k regex:k_decode_mega -s 1 -c 1)")
@@ -389,6 +448,9 @@ def main():
         return
     if args.ncu_case:
         run_ncu_case(args)
+        return
+    if args.sweep:
+        run_sweep(args)
         return
     dist = None
     if world > 1:

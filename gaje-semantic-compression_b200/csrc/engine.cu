@@ -21,6 +21,7 @@
 #include "flat_format.h"
 #include "kernels.cuh"
 #include "megakernel.cuh"
+#include "gemm.cuh"
 
 using namespace gaje;
 
@@ -1277,10 +1278,12 @@ int gaje_cuda_q4_0_gemv(const gaje_q4_matrix* h, const float* x, float* y, size_
     CK(launch_k(k_gemv<G_PLAIN>, dim3(p.grid), dim3(kGemvThreads), p.smem, s, false, P, L, a));
     return GAJE_OK;
   }
-  const int ctas = (h->m.N + 7) / 8;
-  const size_t smem = size_t(h->m.K) * 4;
-  if (int st = smem_optin((const void*)k_q4_gemv, smem)) return st;
-  k_q4_gemv<<<dim3(ctas, unsigned(M)), 256, smem, s>>>(h->m.view(), x, y);
+  // M > 1: every weight block is dequantised once per CTA for 8 vectors
+  constexpr int MT = 8;
+  const int ctas = (h->m.N + 2 * kSkWarps - 1) / (2 * kSkWarps);
+  const size_t smem = skinny_smem_bytes(MT);
+  if (int st = smem_optin((const void*)k_q4_gemm_skinny<MT>, smem)) return st;
+  k_q4_gemm_skinny<MT><<<dim3(ctas, unsigned((M + MT - 1) / MT)), kSkThreads, smem, s>>>(h->m.view(), x, int(M), y);
   CK(cudaGetLastError());
   return GAJE_OK;
 }

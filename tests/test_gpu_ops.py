@@ -57,7 +57,7 @@ def _check_rows(got, ref, W_abs_x):
 
 
 @pytest.mark.parametrize("N,K", SWEEP)
-@pytest.mark.parametrize("M", [1, 3])
+@pytest.mark.parametrize("M", [1, 3, 8, 17])
 def test_q4_gemv_matches_oracle(g, O, N, K, M):
     W, blocks = _q4(O, N, K, 7 * N + K)
     rng = np.random.default_rng(M)
