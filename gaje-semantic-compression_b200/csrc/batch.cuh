@@ -1,0 +1,260 @@
+// batch.cuh -- one decode step for B independent streams of the same model
+// (SURVEY §8(b) gaje_cuda_forward_batch; BASELINE configs[3] decode and the
+// per-rank body of configs[4]).  Each stream has its own KV cache and
+// position; the weights of a step are read once for all B streams.
+//
+// A step is a chain of kernels on the model's stream: embedding rows, then per
+// block RMSNorm, QKV (Q4 GEMM for B vectors, RoPE at each stream's position,
+// the k/v rows written straight into the stream's cache), split-K attention
+// per (stream, KV head, split), O-proj + residual, RMSNorm, gate/up + SwiGLU,
+// down + residual; then the output norm, the f32 lm_head for B vectors and a
+// first-max argmax per stream.  Arithmetic per stream is the single-stream
+// path's (the reference's forward_core, src/nn/llm/forward.rs:7-63): RMSNorm
+// as (x*inv)*w (norm.rs:17-87), Q4 dots with the |t|<1e-6 flush then the bias
+// (genomic.rs:331-335, linear/forward.rs:113-115), split RoPE / interleaved
+// RoPE, the attention of attention.rs:88-127, swiglu_balanced.
+#pragma once
+
+#include "gemm.cuh"
+
+namespace gaje {
+
+// Per-step stream table (device arrays of B entries).
+struct BatchStreams {
+  const unsigned* tok;  // input token
+  const unsigned* pos;  // position = the stream's cache length before the step
+  const unsigned* sid;  // stream id (selects the KV cache)
+};
+
+// The batched KV caches: [stream][layer][nkv][max_ctx][hd] f32, K and V.
+struct BatchCache {
+  float* k;
+  float* v;
+  int L, nkv, max_ctx, hd;
+  __device__ __forceinline__ size_t row(unsigned sid, int l, int g, unsigned pos) const {
+    return ((((size_t)sid * L + l) * nkv + g) * max_ctx + pos) * hd;
+  }
+};
+
+__global__ void k_embed_batch(const float* embd, int V, int d, BatchStreams bs, float* x) {
+  const int b = blockIdx.x;
+  const float* src = embd + (size_t)(bs.tok[b] % (unsigned)V) * d;  // get_row_core: row token % V
+  for (int i = threadIdx.x; i < d; i += blockDim.x) x[(size_t)b * d + i] = __ldg(src + i);
+}
+
+// out[b] = (x[b] * (1/sqrt(ss/n + eps))) * w, one CTA per stream.  With st,
+// the block-input and normed-output NaN guards of block/forward.rs:11-13 and
+// :22-24 (codes at the stream's position).
+__global__ void __launch_bounds__(256) k_rmsnorm_batch(const float* x, const float* w, float eps, int n, float* out,
+                                                       DevState* st, BatchStreams bs, int layer) {
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const float* xb = x + (size_t)b * n;
+  float ss = 0.f;
+  int bad = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = xb[i];
+    ss = fmaf(v, v, ss);
+    bad |= (v != v);
+  }
+  ss = block_sum(ss, red);
+  const float inv = 1.0f / sqrtf(ss / (float)n + eps);
+  int bad_out = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float o = (xb[i] * inv) * w[i];
+    out[(size_t)b * n + i] = o;
+    bad_out |= (o != o);
+  }
+  if (st) {
+    if (bad) nan_flag(st, bs.pos[b], layer, kNanInput);
+    if (bad_out) nan_flag(st, bs.pos[b], layer, kNanAttnNorm);
+  }
+}
+
+// QKV epilogue: the unit u = r0/2 is a RoPE pair (rows stored pair-interleaved
+// by the loader): q heads go to q[b], k rows (rotated) and v rows to the
+// stream's cache at its position.
+struct EpiQkvBatch {
+  float* q;  // [B][nh*hd]
+  BatchCache cache;
+  BatchStreams bs;
+  const float2* rope;  // [max_ctx][hd/2] (cos, sin)
+  int nh, nkv, hd, rope_split, layer;
+  __device__ __forceinline__ void operator()(int b, int r0, float y0, bool, float y1) const {
+    const int half = hd >> 1;
+    const int u = r0 >> 1;
+    const int head = u / half, i = u - head * half;
+    const int c0 = rope_split ? i : 2 * i;
+    const int c1 = rope_split ? i + half : 2 * i + 1;
+    const unsigned pos = bs.pos[b];
+    if (head < nh + nkv) {  // RoPE: v0*cos - v1*sin, v0*sin + v1*cos
+      const float2 cs = rope[(size_t)pos * half + i];
+      const float o0 = y0 * cs.x - y1 * cs.y;
+      const float o1 = y0 * cs.y + y1 * cs.x;
+      y0 = o0;
+      y1 = o1;
+    }
+    float* dst;
+    if (head < nh) dst = q + (size_t)b * nh * hd + head * hd;
+    else if (head < nh + nkv) dst = cache.k + cache.row(bs.sid[b], layer, head - nh, pos);
+    else dst = cache.v + cache.row(bs.sid[b], layer, head - nh - nkv, pos);
+    dst[c0] = y0;
+    dst[c1] = y1;
+  }
+};
+
+// x[b][row] += y (the residual adds of block/forward.rs:75-77, :132-136); for
+// the down projection also the NaN guards of :128-130 and :138-140.
+struct EpiResidBatch {
+  float* x;
+  int N;
+  DevState* st;  // non-null: the down-projection guards
+  BatchStreams bs;
+  int layer;
+  __device__ __forceinline__ void operator()(int b, int r, float y0, bool has1, float y1) const {
+    for (int k = 0; k < 2; ++k) {
+      if (k == 1 && !has1) break;
+      const float y = k ? y1 : y0;
+      float* xp = x + (size_t)b * N + r + k;
+      const float xn = *xp + y;
+      if (st) {
+        if (y != y) nan_flag(st, bs.pos[b], layer, kNanProjFfn);
+        if (xn != xn) nan_flag(st, bs.pos[b], layer, kNanResidual);
+      }
+      *xp = xn;
+    }
+  }
+};
+
+// gate/up pair (rows stored pair-interleaved) -> swiglu_balanced -> act[b][u].
+struct EpiSwigluBatch {
+  float* act;
+  int ff;
+  DevState* st;
+  BatchStreams bs;
+  int layer;
+  __device__ __forceinline__ void operator()(int b, int r0, float g, bool, float u) const {
+    if (u != u) nan_flag(st, bs.pos[b], layer, kNanUp);
+    const float a = swiglu_balanced(g, u);
+    if (a != a) nan_flag(st, bs.pos[b], layer, kNanFfnOut);
+    act[(size_t)b * ff + (r0 >> 1)] = a;
+  }
+};
+
+// Attention of stream blockIdx.z over its cache (the step's row is already in
+// it): the single-stream split kernel's body with per-stream arguments.
+struct AttnBatchArgs {
+  const float* q;  // [B][nh*hd]
+  float* out;      // [B][nh*hd]
+  BatchCache cache;
+  BatchStreams bs;
+  float* part_o;   // [B][nkv][kAttnMaxSplits][G][hd]
+  float* part_ml;  // [B][nkv][kAttnMaxSplits][G][2]
+  unsigned* cnt;   // [B][nkv], zero between launches
+  int layer, nh;
+  float scale;
+};
+__global__ void __launch_bounds__(kAttnThreads) k_attn_batch(AttnBatchArgs B) {
+  const int b = blockIdx.z;
+  const int G = B.nh / B.cache.nkv, hd = B.cache.hd, nkv = B.cache.nkv;
+  AttnArgs a{};
+  a.q = B.q + (size_t)b * B.nh * hd;
+  a.out = B.out + (size_t)b * B.nh * hd;
+  a.kc = B.cache.k + B.cache.row(B.bs.sid[b], B.layer, 0, 0);
+  a.vc = B.cache.v + B.cache.row(B.bs.sid[b], B.layer, 0, 0);
+  a.part_o = B.part_o + (size_t)b * nkv * kAttnMaxSplits * G * hd;
+  a.part_ml = B.part_ml + (size_t)b * nkv * kAttnMaxSplits * G * 2;
+  a.cnt = B.cnt + (size_t)b * nkv;
+  a.ctx = int(B.bs.pos[b]) + 1;
+  a.stride = B.cache.max_ctx;
+  a.nh = B.nh;
+  a.nkv = nkv;
+  a.hd = hd;
+  a.scale = B.scale;
+  a.st = nullptr;
+  attn_split(a, blockIdx.x, blockIdx.y);
+}
+
+// f32 lm_head for B vectors (linear/forward.rs:20-32, no flush) + first-max
+// argmax per stream (llm/forward.rs:262-271): a warp per vocab row, the B
+// normed vectors in shared memory, per-CTA best keys, the last CTA reduces.
+constexpr int kLbThreads = 512;
+struct LmBatchArgs {
+  const float* W;       // [V][d]
+  const float* bias;    // [V] or nullptr
+  const float* xn;      // [B][d]
+  float* logits;        // [B][V]
+  unsigned long long* part;  // [grid][B]
+  unsigned* cnt;        // zero between launches
+  unsigned* argmax;     // [B]
+  int V, d, B, rows_per_cta;
+};
+template <int MB>
+__global__ void __launch_bounds__(kLbThreads) k_lmhead_batch(LmBatchArgs A) {
+  extern __shared__ __align__(16) float lb_smem[];
+  __shared__ unsigned long long wbest[kLbThreads / 32][MB];
+  __shared__ int is_last;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = kLbThreads / 32;
+  const int d = A.d, K4 = d >> 2;
+  for (int i = tid; i < A.B * d; i += kLbThreads) lb_smem[i] = A.xn[i];
+  __syncthreads();
+  unsigned long long best[MB];
+#pragma unroll
+  for (int b = 0; b < MB; ++b) best[b] = 0ull;
+  const int rbeg = blockIdx.x * A.rows_per_cta, rend = min(A.V, rbeg + A.rows_per_cta);
+  for (int r = rbeg + wid; r < rend; r += nw) {
+    const float4* w4 = reinterpret_cast<const float4*>(A.W + (size_t)r * d);
+    float acc[MB];
+#pragma unroll
+    for (int b = 0; b < MB; ++b) acc[b] = 0.f;
+    for (int j = lane; j < K4; j += 32) {
+      const float4 u = __ldg(w4 + j);
+#pragma unroll
+      for (int b = 0; b < MB; ++b) {
+        if (b < A.B) {
+          const float4 xv = reinterpret_cast<const float4*>(lb_smem + (size_t)b * d)[j];
+          acc[b] = fmaf(u.x, xv.x, acc[b]);
+          acc[b] = fmaf(u.y, xv.y, acc[b]);
+          acc[b] = fmaf(u.z, xv.z, acc[b]);
+          acc[b] = fmaf(u.w, xv.w, acc[b]);
+        }
+      }
+    }
+    const float bb = A.bias ? __ldg(A.bias + r) : 0.f;
+#pragma unroll
+    for (int b = 0; b < MB; ++b) {
+      if (b < A.B) {
+        const float v = warp_sum(acc[b]) + bb;
+        if (lane == 0) A.logits[(size_t)b * A.V + r] = v;
+        const unsigned long long key = amax_key(v, (unsigned)r);
+        best[b] = key > best[b] ? key : best[b];
+      }
+    }
+  }
+  if (lane == 0)
+    for (int b = 0; b < MB; ++b) wbest[wid][b] = best[b];
+  __syncthreads();
+  if (tid < A.B) {
+    unsigned long long k = 0;
+    for (int w = 0; w < nw; ++w) k = wbest[w][tid] > k ? wbest[w][tid] : k;
+    A.part[(size_t)blockIdx.x * A.B + tid] = k;
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) is_last = (atomicAdd(A.cnt, 1u) == gridDim.x - 1u);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  for (int b = wid; b < A.B; b += nw) {
+    unsigned long long k = 0;
+    for (int c = lane; c < (int)gridDim.x; c += 32) {
+      const unsigned long long v = __ldcg(A.part + (size_t)c * A.B + b);
+      k = v > k ? v : k;
+    }
+    k = warp_max_u64(k);
+    if (lane == 0) A.argmax[b] = amax_index(k);
+  }
+  if (tid == 0) *A.cnt = 0u;  // ready for the next launch
+}
+
+}  // namespace gaje

@@ -22,6 +22,7 @@
 #include "kernels.cuh"
 #include "megakernel.cuh"
 #include "gemm.cuh"
+#include "batch.cuh"
 
 using namespace gaje;
 
@@ -246,6 +247,17 @@ struct gaje_model {
   size_t phase_ns_cap = 0;
   unsigned long long* trace_ns = nullptr;
   size_t trace_ns_cap = 0;
+  // batched streams (gaje_cuda_forward_batch)
+  int max_streams = 0;
+  BatchCache bcache{};
+  float *bx = nullptr, *bxn = nullptr, *bq = nullptr, *battn = nullptr, *bact = nullptr, *blogits = nullptr;
+  float *bpart_o = nullptr, *bpart_ml = nullptr;
+  unsigned* bcnt = nullptr;
+  unsigned long long* blm_part = nullptr;
+  unsigned* blm_cnt = nullptr;
+  unsigned* bdev = nullptr;   // [3][max_streams]: tokens, positions, stream ids; then [max_streams] argmax
+  unsigned* h_bdev = nullptr; // pinned staging of the same
+  std::vector<uint32_t> bpos; // per-stream cache length (host)
 
   ~gaje_model() {
     if (phase_ns) cudaFree(phase_ns);
@@ -254,6 +266,7 @@ struct gaje_model {
     if (arena.base) cudaFree(arena.base);
     if (h_st) cudaFreeHost(h_st);
     if (h_tok) cudaFreeHost(h_tok);
+    if (h_bdev) cudaFreeHost(h_bdev);
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -641,6 +654,9 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   m->L = int(I.n_blocks);
   m->max_ctx = int(opts && opts->max_ctx ? opts->max_ctx : 4096);
   m->use_graph = !opts || opts->use_graph;
+  m->max_streams = opts ? int(opts->max_streams) : 0;
+  if (m->max_streams < 0 || m->max_streams > 1024)
+    return set_error(GAJE_ERR_INVALID, "max_streams above 1024");
   m->rng.s = opts ? opts->seed : 0;
   if (m->nh / m->nkv > kAttnMaxGroup) return set_error(GAJE_ERR_UNSUPPORTED, "more than 16 query heads per KV head");
   if (m->hd % 4 != 0) return set_error(GAJE_ERR_UNSUPPORTED, "head_dim must be a multiple of 4");
@@ -715,6 +731,24 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     m->ll.act = m->ll.apart + apart;
     m->ll.tok = m->ll.act + m->ff;
     m->ll.flags = m->ll.tok + 1;
+    if (m->max_streams > 0) {
+      const size_t S = size_t(m->max_streams), G = size_t(m->nh / m->nkv);
+      const size_t bc = S * L * size_t(m->nkv) * m->max_ctx * m->hd;
+      m->bcache.k = a.take<float>(bc);
+      m->bcache.v = a.take<float>(bc);
+      m->bx = a.take<float>(S * d);
+      m->bxn = a.take<float>(S * d);
+      m->bq = a.take<float>(S * qd);
+      m->battn = a.take<float>(S * qd);
+      m->bact = a.take<float>(S * m->ff);
+      m->blogits = a.take<float>(S * V);
+      m->bpart_o = a.take<float>(S * m->nkv * kAttnMaxSplits * G * m->hd);
+      m->bpart_ml = a.take<float>(S * m->nkv * kAttnMaxSplits * G * 2);
+      m->bcnt = a.take<unsigned>(S * m->nkv);
+      m->blm_part = a.take<unsigned long long>(size_t(m->sms) * 16);
+      m->blm_cnt = a.take<unsigned>(1);
+      m->bdev = a.take<unsigned>(4 * S);
+    }
   };
   Arena sizing;
   plan(sizing);
@@ -754,6 +788,16 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   CK(cudaMemsetAsync(m->attn_cnt, 0, m->nkv * sizeof(unsigned), m->stream));
   CK(cudaMemsetAsync(m->ll.xa, 0, m->ll_words * sizeof(uint2), m->stream));
   CK(cudaMemsetAsync(m->amax_cnt, 0, sizeof(unsigned), m->stream));
+  if (m->max_streams > 0) {
+    m->bcache.L = m->L;
+    m->bcache.nkv = m->nkv;
+    m->bcache.max_ctx = m->max_ctx;
+    m->bcache.hd = m->hd;
+    CK(cudaMemsetAsync(m->bcnt, 0, size_t(m->max_streams) * m->nkv * sizeof(unsigned), m->stream));
+    CK(cudaMemsetAsync(m->blm_cnt, 0, sizeof(unsigned), m->stream));
+    CK(cudaHostAlloc(&m->h_bdev, size_t(4) * m->max_streams * sizeof(unsigned), cudaHostAllocDefault));
+    m->bpos.assign(size_t(m->max_streams), 0u);
+  }
   CK(cudaMemsetAsync(m->kcache, 0, L * size_t(m->nkv) * m->max_ctx * m->hd * 4, m->stream));
   CK(cudaMemsetAsync(m->vcache, 0, L * size_t(m->nkv) * m->max_ctx * m->hd * 4, m->stream));
   // ---- upload
@@ -836,6 +880,7 @@ void gaje_load_opts_init(gaje_load_opts* o) {
   o->seed = 0;
   o->use_graph = 1;
   o->use_megakernel = 1;
+  o->max_streams = 0;
 }
 
 gaje_model* gaje_cuda_load(const char* flat_path, const gaje_load_opts* opts) {
@@ -915,6 +960,115 @@ int gaje_cuda_forward(gaje_model* m, uint32_t token_id, int clear_cache, float* 
   m->host_pos += 1;
   if (int s = m->check_state()) return s;
   if (argmax_out) *argmax_out = m->h_st->argmax;
+  return GAJE_OK;
+}
+
+int gaje_cuda_forward_batch(gaje_model* m, const uint32_t* stream_ids, const uint32_t* tokens, size_t B,
+                            uint32_t* argmax_out, float* logits_out) {
+  if (!m || (B && (!stream_ids || !tokens))) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  if (B == 0) return GAJE_OK;
+  if (m->max_streams <= 0)
+    return set_error(GAJE_ERR_INVALID, "the model was loaded without batched streams (gaje_load_opts.max_streams)");
+  if (B > size_t(m->max_streams)) return set_error(GAJE_ERR_INVALID, "more streams in the batch than max_streams");
+  if (m->block_k() > 0)
+    return set_error(GAJE_ERR_UNSUPPORTED, "block K-WTA is not implemented on the batched path");
+  if (m->info.use_genomic_norm)
+    return set_error(GAJE_ERR_UNSUPPORTED, "use_genomic_norm is not implemented on the batched path");
+  const size_t S = size_t(m->max_streams);
+  std::vector<char> seen(S, 0);
+  unsigned max_ctx_used = 0;
+  for (size_t b = 0; b < B; ++b) {
+    const uint32_t sid = stream_ids[b];
+    if (sid >= S) return set_error(GAJE_ERR_INVALID, "stream id out of range");
+    if (seen[sid]) return set_error(GAJE_ERR_INVALID, "a stream appears twice in one batch");
+    seen[sid] = 1;
+    if (m->bpos[sid] >= uint32_t(m->max_ctx)) return set_error(GAJE_ERR_CONTEXT, "KV cache full (max_ctx positions)");
+    m->h_bdev[b] = tokens[b];
+    m->h_bdev[S + b] = m->bpos[sid];
+    m->h_bdev[2 * S + b] = sid;
+    max_ctx_used = std::max(max_ctx_used, m->bpos[sid] + 1u);
+  }
+  CK(cudaSetDevice(m->device));
+  cudaStream_t st = m->stream;
+  CK(cudaMemcpyAsync(m->bdev, m->h_bdev, 3 * S * sizeof(unsigned), cudaMemcpyHostToDevice, st));
+  BatchStreams bs{m->bdev, m->bdev + S, m->bdev + 2 * S};
+  unsigned* d_argmax = m->bdev + 3 * S;
+  const int d = m->d, L = m->L, Bi = int(B);
+  const float eps = m->info.eps;
+  constexpr int MT = 8;
+  const unsigned mtiles = unsigned((B + MT - 1) / MT);
+  const size_t sk_smem = skinny_smem_bytes(MT);
+  auto ctas = [](const Q4Dev& q) { return unsigned((q.N + 2 * kSkWarps - 1) / (2 * kSkWarps)); };
+  if (int e = smem_optin((const void*)k_q4_gemm_skinny<MT, EpiQkvBatch>, sk_smem)) return e;
+  if (int e = smem_optin((const void*)k_q4_gemm_skinny<MT, EpiResidBatch>, sk_smem)) return e;
+  if (int e = smem_optin((const void*)k_q4_gemm_skinny<MT, EpiSwigluBatch>, sk_smem)) return e;
+  int nsplit, chunk;
+  attn_splits(int(max_ctx_used), nsplit, chunk);
+  const int G = m->nh / m->nkv;
+  const size_t at_smem = attn_smem_bytes(G, m->hd, chunk);
+  if (int e = smem_optin((const void*)k_attn_batch, at_smem)) return e;
+  constexpr int MB = 16;
+  const size_t lm_smem = size_t(MB) * d * 4;
+  if (int e = smem_optin((const void*)k_lmhead_batch<MB>, lm_smem)) return e;
+  k_embed_batch<<<Bi, 256, 0, st>>>(m->embd, m->V, d, bs, m->bx);
+  for (int l = 0; l < L; ++l) {
+    k_rmsnorm_batch<<<Bi, 256, 0, st>>>(m->bx, m->attn_norm[l], eps, d, m->bxn, m->st, bs, l);
+    EpiQkvBatch eq{m->bq, m->bcache, bs, m->rope, m->nh, m->nkv, m->hd, int(m->info.rope_split), l};
+    k_q4_gemm_skinny<MT, EpiQkvBatch><<<dim3(ctas(m->qkv[l]), mtiles), kSkThreads, sk_smem, st>>>(
+        m->qkv[l].view(), m->bxn, Bi, eq);
+    AttnBatchArgs aa{m->bq, m->battn, m->bcache, bs, m->bpart_o, m->bpart_ml, m->bcnt, l, m->nh,
+                     1.0f / sqrtf(float(m->hd))};
+    k_attn_batch<<<dim3(unsigned(m->nkv), kAttnMaxSplits, unsigned(B)), kAttnThreads, at_smem, st>>>(aa);
+    k_q4_gemm_skinny<MT, EpiResidBatch><<<dim3(ctas(m->wo[l]), mtiles), kSkThreads, sk_smem, st>>>(
+        m->wo[l].view(), m->battn, Bi, EpiResidBatch{m->bx, d, nullptr, bs, l});
+    k_rmsnorm_batch<<<Bi, 256, 0, st>>>(m->bx, m->ffn_norm[l], eps, d, m->bxn, nullptr, bs, l);
+    k_q4_gemm_skinny<MT, EpiSwigluBatch><<<dim3(ctas(m->gate_up[l]), mtiles), kSkThreads, sk_smem, st>>>(
+        m->gate_up[l].view(), m->bxn, Bi, EpiSwigluBatch{m->bact, m->ff, m->st, bs, l});
+    k_q4_gemm_skinny<MT, EpiResidBatch><<<dim3(ctas(m->down[l]), mtiles), kSkThreads, sk_smem, st>>>(
+        m->down[l].view(), m->bact, Bi, EpiResidBatch{m->bx, d, m->st, bs, l});
+  }
+  k_rmsnorm_batch<<<Bi, 256, 0, st>>>(m->bx, m->out_norm, eps, d, m->bxn, nullptr, bs, L);
+  for (int b0 = 0; b0 < Bi; b0 += MB) {
+    LmBatchArgs la{};
+    la.W = m->lm_head;
+    la.bias = m->lm_bias;
+    la.xn = m->bxn + size_t(b0) * d;
+    la.logits = m->blogits + size_t(b0) * m->V;
+    la.part = m->blm_part;
+    la.cnt = m->blm_cnt;
+    la.argmax = d_argmax + b0;
+    la.V = m->V;
+    la.d = d;
+    la.B = std::min(MB, Bi - b0);
+    la.rows_per_cta = (m->V + m->sms - 1) / m->sms;
+    k_lmhead_batch<MB><<<m->sms, kLbThreads, lm_smem, st>>>(la);
+  }
+  CK(cudaGetLastError());
+  const int kk = m->logits_k();
+  if (logits_out && kk > 0)  // K-WTA on the returned logits (llm/forward.rs:58-61); the argmax is unaffected
+    for (int b = 0; b < Bi; ++b) k_kwta<<<1, kKwtaThreads, 0, st>>>(m->blogits + size_t(b) * m->V, m->V, kk);
+  CK(cudaMemcpyAsync(m->h_bdev + 3 * S, d_argmax, B * sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+  if (logits_out)
+    CK(cudaMemcpyAsync(logits_out, m->blogits, B * size_t(m->V) * 4, cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  for (size_t b = 0; b < B; ++b) m->bpos[stream_ids[b]] += 1u;
+  if (argmax_out)
+    for (size_t b = 0; b < B; ++b) argmax_out[b] = m->h_bdev[3 * S + b];
+  return m->check_state();
+}
+
+int gaje_cuda_clear_stream(gaje_model* m, uint32_t stream_id) {
+  if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  if (stream_id >= uint32_t(std::max(0, m->max_streams))) return set_error(GAJE_ERR_INVALID, "stream id out of range");
+  m->bpos[stream_id] = 0;
+  return GAJE_OK;
+}
+
+int gaje_cuda_stream_len(gaje_model* m, uint32_t stream_id, uint32_t* len) {
+  if (!m || !len) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  if (stream_id >= uint32_t(std::max(0, m->max_streams))) return set_error(GAJE_ERR_INVALID, "stream id out of range");
+  *len = m->bpos[stream_id];
   return GAJE_OK;
 }
 
@@ -1282,8 +1436,9 @@ int gaje_cuda_q4_0_gemv(const gaje_q4_matrix* h, const float* x, float* y, size_
   constexpr int MT = 8;
   const int ctas = (h->m.N + 2 * kSkWarps - 1) / (2 * kSkWarps);
   const size_t smem = skinny_smem_bytes(MT);
-  if (int st = smem_optin((const void*)k_q4_gemm_skinny<MT>, smem)) return st;
-  k_q4_gemm_skinny<MT><<<dim3(ctas, unsigned((M + MT - 1) / MT)), kSkThreads, smem, s>>>(h->m.view(), x, int(M), y);
+  if (int st = smem_optin((const void*)k_q4_gemm_skinny<MT, EpiStore>, smem)) return st;
+  k_q4_gemm_skinny<MT, EpiStore><<<dim3(ctas, unsigned((M + MT - 1) / MT)), kSkThreads, smem, s>>>(
+      h->m.view(), x, int(M), EpiStore{y, h->m.N});
   CK(cudaGetLastError());
   return GAJE_OK;
 }

@@ -23,8 +23,20 @@ __host__ __device__ inline size_t skinny_smem_bytes(int mt) {
   return size_t(mt) * (kSkChunk + kSkChunk / 32) * 4;
 }
 
-template <int MT>
-__global__ void __launch_bounds__(kSkThreads) k_q4_gemm_skinny(Q4View W, const float* x, int M, float* y) {
+// The plain epilogue: y[m][row] = v.
+struct EpiStore {
+  float* y;
+  int N;
+  __device__ __forceinline__ void operator()(int m, int r, float v0, bool has1, float v1) const {
+    y[(size_t)m * N + r] = v0;
+    if (has1) y[(size_t)m * N + r + 1] = v1;
+  }
+};
+
+// epi(m, r0, v0, has1, v1) receives rows r0 (and r0 + 1) of vector m, flushed
+// and with the bias added.
+template <int MT, class Epi>
+__global__ void __launch_bounds__(kSkThreads) k_q4_gemm_skinny(Q4View W, const float* x, int M, Epi epi) {
   extern __shared__ __align__(16) float sk_smem[];
   float* xs = sk_smem;                    // [MT][kSkChunk]
   float* xsum = sk_smem + MT * kSkChunk;  // [MT][kSkChunk / 32]
@@ -76,14 +88,12 @@ __global__ void __launch_bounds__(kSkThreads) k_q4_gemm_skinny(Q4View W, const f
     }
   }
   if (!has0) return;
+  const float b0 = W.bias ? __ldg(W.bias + r0) : 0.f;
+  const float b1 = (W.bias && has1) ? __ldg(W.bias + r0 + 1) : 0.f;
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
     const float v0 = warp_sum(acc0[m]), v1 = warp_sum(acc1[m]);
-    if (lane == 0 && m < mt) {
-      float* yr = y + (size_t)(m0 + m) * W.N;
-      yr[r0] = flush_small(v0) + (W.bias ? __ldg(W.bias + r0) : 0.f);
-      if (has1) yr[r0 + 1] = flush_small(v1) + (W.bias ? __ldg(W.bias + r0 + 1) : 0.f);
-    }
+    if (lane == 0 && m < mt) epi(m0 + m, r0, flush_small(v0) + b0, has1, flush_small(v1) + b1);
   }
 }
 

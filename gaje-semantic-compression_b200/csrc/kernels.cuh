@@ -519,7 +519,7 @@ struct AttnArgs {
 // combines the splits:
 //   out = (sum_s O_s e^{m_s-M}) * (1/(sum_s l_s e^{m_s-M} + 1e-12))
 // (the reference's inv_s = 1/(sum_e + 1e-12), attention.rs:110).
-__global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs A) {
+__device__ __forceinline__ void attn_split(const AttnArgs& A, const int g, const int s) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   uint64_t* bar = reinterpret_cast<uint64_t*>(smem_raw);
   __shared__ float mls[2 * kAttnMaxGroup];
@@ -527,7 +527,6 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs A) {
   __shared__ float linv[kAttnMaxGroup];
   __shared__ int is_last;
   const int G = A.nh / A.nkv, hd = A.hd;
-  const int g = blockIdx.x, s = blockIdx.y;
   // the decode position is stable here (written two or more kernels back)
   const int ctx = A.ctx > 0 ? A.ctx : (int)__ldcg(&A.st->pos) + 1;
   int nsplit, chunk;
@@ -663,6 +662,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs A) {
   }
   if (threadIdx.x == 0) A.cnt[g] = 0u;  // ready for the next launch
 }
+__global__ void __launch_bounds__(kAttnThreads) k_attn(AttnArgs A) { attn_split(A, blockIdx.x, blockIdx.y); }
 
 // ------------------------------------------------------------ lm_head
 // Orderable key for the first-max argmax: larger value wins, then the lower

@@ -87,7 +87,7 @@ class SynthSpec(C.Structure):
 
 class LoadOpts(C.Structure):
     _fields_ = [("device", C.c_int), ("max_ctx", C.c_uint32), ("seed", C.c_uint64),
-                ("use_graph", C.c_int), ("use_megakernel", C.c_int)]
+                ("use_graph", C.c_int), ("use_megakernel", C.c_int), ("max_streams", C.c_uint32)]
 
 
 class ModelInfo(C.Structure):
@@ -137,6 +137,9 @@ def lib() -> C.CDLL:
         "gaje_cuda_profile_phases": ([vp, u32, sz, vp, vp, vp], i32),
         "gaje_cuda_trace_steps": ([vp, u32, sz, vp, sz, vp], i32),
         "gaje_cuda_attention_decode_static": ([vp, vp, vp, sz, sz, sz, sz, sz, vp, vp], i32),
+        "gaje_cuda_forward_batch": ([vp, vp, vp, sz, vp, vp], i32),
+        "gaje_cuda_clear_stream": ([vp, u32], i32),
+        "gaje_cuda_stream_len": ([vp, u32, vp], i32),
         "gaje_cuda_q4_0_upload": ([vp, sz, sz, vp, i32], vp),
         "gaje_cuda_q4_0_release": ([vp], None),
         "gaje_cuda_q4_0_gemv": ([vp, vp, vp, sz, vp], i32),
@@ -260,11 +263,12 @@ class GenomicLLM:
     """A `.gaje.flat` model resident on one GPU (the reference's RustGenomicLLM)."""
 
     def __init__(self, path: str, device: int = 0, max_ctx: int = 4096, seed: int = 0,
-                 use_graph: bool = True, use_megakernel: bool = True):
+                 use_graph: bool = True, use_megakernel: bool = True, max_streams: int = 0):
         opts = LoadOpts()
         lib().gaje_load_opts_init(C.byref(opts))
         opts.device, opts.max_ctx, opts.seed, opts.use_graph = device, max_ctx, seed, int(use_graph)
         opts.use_megakernel = int(use_megakernel)
+        opts.max_streams = int(max_streams)
         self._m = lib().gaje_cuda_load(path.encode(), C.byref(opts))
         if not self._m:
             raise GajeIOError(2, last_error())
@@ -369,6 +373,28 @@ class GenomicLLM:
             out["detail"] = {self.PHASES[p]: {self.DETAIL[j]: round(float(det[p * 5 + j]), 3) for j in range(5)}
                              for p in range(len(self.PHASES))}
         return out
+
+    def forward_batch(self, stream_ids: Sequence[int], tokens: Sequence[int], logits: bool = False):
+        """One decode step for each listed stream (its own KV cache and
+        position): the greedy argmax per stream, and the logits [B, vocab]
+        when asked for."""
+        sids = np.ascontiguousarray(list(stream_ids), dtype=np.uint32)
+        toks = np.ascontiguousarray(list(tokens), dtype=np.uint32)
+        if sids.size != toks.size:
+            raise ValueError("stream_ids and tokens differ in length")
+        am = np.zeros(sids.size, dtype=np.uint32)
+        lg = np.empty((sids.size, self.vocab_size), dtype=np.float32) if logits else None
+        _check(lib().gaje_cuda_forward_batch(self._m, _ptr(sids), _ptr(toks), sids.size, _ptr(am),
+                                             _ptr(lg) if logits else None))
+        return (am, lg) if logits else am
+
+    def clear_stream(self, stream_id: int) -> None:
+        _check(lib().gaje_cuda_clear_stream(self._m, int(stream_id)))
+
+    def stream_len(self, stream_id: int) -> int:
+        n = C.c_uint32(0)
+        _check(lib().gaje_cuda_stream_len(self._m, int(stream_id), C.byref(n)))
+        return int(n.value)
 
     def trace_steps(self, first_token: int, n_steps: int) -> np.ndarray:
         """Every CTA's trace stamps (ns) of n_steps greedy steps in one launch:

@@ -137,6 +137,7 @@ typedef struct gaje_load_opts {
                          graph (1, default) or launch kernel by kernel (0)    */
   int use_megakernel; /* 1 (default): one persistent cooperative kernel runs
                          whole decode steps; 0: one kernel per phase          */
+  uint32_t max_streams; /* KV caches for gaje_cuda_forward_batch (0 = none)   */
 } gaje_load_opts;
 void gaje_load_opts_init(gaje_load_opts* opts);
 
@@ -188,6 +189,24 @@ int gaje_cuda_set_seed(gaje_model* model, uint64_t seed);
  * nullable) receives the argmax of each step. */
 int gaje_cuda_decode_greedy(gaje_model* model, uint32_t first_token, size_t n_steps,
                             uint32_t* tokens_out);
+
+/* Batched decode (BASELINE configs[3]/[4]): one forward_core step
+ * (src/nn/llm/forward.rs:7-63) for each of B streams of the same model, each
+ * with its own KV cache and position (its cache length).  stream_ids[B]
+ * (distinct, < gaje_load_opts.max_streams) select the caches, tokens[B] are the
+ * inputs; argmax_out[B] (host, nullable) receives each stream's greedy choice
+ * (llm/forward.rs:262-271), logits_out (host, B x vocab_size, nullable) the
+ * logits (with the logits K-WTA of :58-61 applied when its ratio is in (0,1)).
+ * The weights of the step are read once for all B streams.  Block K-WTA and
+ * use_genomic_norm are GAJE_ERR_UNSUPPORTED here; a full cache is
+ * GAJE_ERR_CONTEXT.  Independent of the single-stream state (gaje_cuda_forward
+ * and its cache). */
+int gaje_cuda_forward_batch(gaje_model* model, const uint32_t* stream_ids, const uint32_t* tokens,
+                            size_t B, uint32_t* argmax_out, float* logits_out);
+/* clear_cache_core for one batched stream. */
+int gaje_cuda_clear_stream(gaje_model* model, uint32_t stream_id);
+/* A batched stream's cache length. */
+int gaje_cuda_stream_len(gaje_model* model, uint32_t stream_id, uint32_t* len);
 
 /* The model's CUDA stream (a cudaStream_t), for callers that time it. */
 void* gaje_cuda_stream(gaje_model* model);
