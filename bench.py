@@ -405,6 +405,99 @@ def run_sweep(args) -> None:
         del mat
 
 
+def run_batched(args, rank: int = 0, world: int = 1, local_rank: int = 0, dist=None) -> None:
+    """BASELINE.json configs[3] shape: B streams, a P-token random prompt each
+    (fed as batched steps, token by token as the reference prefills), then K
+    greedy decode steps (each stream fed its own argmax) through
+    gaje_cuda_forward_batch.  value = all streams' decode tokens / the decode
+    time (CUDA events on the model stream, max over ranks); prefill tok/s
+    likewise.  Under torchrun every rank decodes its own B streams
+    (request-parallel, no collective in the data path)."""
+    import numpy as np
+    import torch
+
+    g = _pkg()
+    torch.cuda.set_device(local_rank)
+    cfg_key = args.config
+    cfg = g.configs.CONFIGS[cfg_key]
+    path = _ensure_model(g, cfg_key, SEED, rank, dist)
+    B, P, K = args.batch, args.prompt, args.steps
+    model = g.load_genomic_auto(path, device=local_rank, max_ctx=P + K + 8, max_streams=B)
+    model.set_k_wta_ratio(0.0)
+    stream = torch.cuda.ExternalStream(model.stream, device=local_rank)
+    rng = np.random.default_rng(SEED + rank)
+    prompts = rng.integers(0, model.vocab_size, (B, P))
+    sids = list(range(B))
+    # warm-up (also the prefill timing)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if dist is not None:
+        dist.barrier()
+    e0.record(stream)
+    am = None
+    for t in range(P):
+        am = model.forward_batch(sids, [int(v) for v in prompts[:, t]])
+    e1.record(stream)
+    e1.synchronize()
+    pre_ms = e0.elapsed_time(e1)
+    with ClockSampler(local_rank) as clk:
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        toks = [int(v) for v in am]
+        for _ in range(K):
+            toks = [int(v) for v in model.forward_batch(sids, toks)]
+        e1.record(stream)
+        e1.synchronize()
+    dec_ms = e0.elapsed_time(e1)
+    dec_max, pre_max = dec_ms, pre_ms
+    if dist is not None:
+        tt = torch.tensor([dec_ms, pre_ms], dtype=torch.float64, device=f"cuda:{local_rank}")
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        dec_max, pre_max = float(tt[0].item()), float(tt[1].item())
+    if rank != 0:
+        return
+    peaks = _peaks()
+    sb = g.configs.step_bytes(cfg, P + K // 2)
+    body_plus_head = sb["total"] - sb.get("kv", 0)
+    kv_per_stream = sb.get("kv", 0)
+    step_bytes = body_plus_head + B * kv_per_stream  # weights once per step, every stream's KV
+    step_s = dec_max / 1000.0 / K
+    line = {
+        "metric": "decode tok/s (batched)",
+        "value": round(world * B * K / (dec_max / 1000.0), 2),
+        "unit": "tok/s",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": P,
+        "ms_per_step": round(dec_max / K, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic: seeded random-init N(0,0.02) weights quantised by the Q4_0 exporter restatement, "
+                "uniform random prompt ids",
+        "config": {"workload": f"{cfg_key} batched greedy decode, {B} streams per GPU after a {P}-token prompt "
+                               f"each", "global_batch": world * B, "prompt_len": P, "decode_steps": K,
+                   "parallelism": f"request-parallel x{world}" if world > 1 else "single",
+                   "l2": "inputs larger than L2"},
+        "prefill": {"value": round(world * B * P / (pre_max / 1000.0), 2), "unit": "tok/s",
+                    "how": "token by token as batched steps (the reference prefills token by token)"},
+        "e2e": {"value": round(world * B * K / (dec_max / 1000.0), 2), "unit": "tok/s",
+                "h2d_bytes_per_step": 12 * B, "d2h_bytes_per_step": 4 * B + 32,
+                "path": "gaje_cuda_forward_batch (host tokens in, host argmax out, a sync per step)"},
+        "roofline": {"bound": "hbm", "kernel": "batched step (skinny Q4 GEMMs + lm_head for B vectors)",
+                     "achieved": round(step_bytes / step_s / 1e9, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(step_bytes / step_s / 1e9 / peaks["hbm_gbs"], 4), "traffic": None,
+                     "algorithmic_bytes": step_bytes,
+                     "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs, of measured)"},
+        "gpu_launches": (7 * cfg["n_blocks"] + 3 + (B + 15) // 16) * K,
+        "clocks": clk.summary(),
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_ncu_case(args) -> None:
     """Two launches of the persistent kernel on one GPU: PROMPT_LEN greedy steps
     (the context a bench step sees), then args.steps steps, the launch a
@@ -432,6 +525,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default=CONFIG_KEY)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="batched decode of this many streams per GPU (configs[3]/[4] shape) instead of batch 1")
+    ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt tokens per stream (--batch)")
     ap.add_argument("--sweep", action="store_true",
                     help="the isolated Q4_0 GEMV/GEMM sweep of configs[2] instead of the decode benchmark")
     ap.add_argument("--ncu-case", action="store_true",
@@ -464,7 +560,10 @@ def main():
                                  device_id=torch.device(f"cuda:{local_rank}"))
         dist = tdist
     try:
-        run_ours(args, rank, world, local_rank, dist)
+        if args.batch > 0:
+            run_batched(args, rank, world, local_rank, dist)
+        else:
+            run_ours(args, rank, world, local_rank, dist)
     finally:
         if dist is not None:
             dist.barrier()
