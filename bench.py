@@ -492,7 +492,7 @@ def run_batched(args, rank: int = 0, world: int = 1, local_rank: int = 0, dist=N
                      "frac": round(step_bytes / step_s / 1e9 / peaks["hbm_gbs"], 4), "traffic": None,
                      "algorithmic_bytes": step_bytes,
                      "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs, of measured)"},
-        "gpu_launches": (7 * cfg["n_blocks"] + 3 + (B + 15) // 16) * K,
+        "gpu_launches": (5 * cfg["n_blocks"] + 1 + (B + (8 if B <= 8 else 16) - 1) // (8 if B <= 8 else 16)) * K,
         "clocks": clk.summary(),
     }
     print(json.dumps(line), flush=True)

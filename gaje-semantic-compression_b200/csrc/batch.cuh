@@ -1,18 +1,21 @@
 // batch.cuh -- one decode step for B independent streams of the same model
-// (SURVEY §8(b) gaje_cuda_forward_batch; BASELINE configs[3] decode and the
-// per-rank body of configs[4]).  Each stream has its own KV cache and
-// position; the weights of a step are read once for all B streams.
+// (gaje_cuda_forward_batch; BASELINE configs[3] decode and the per-rank body
+// of configs[4]).  Each stream has its own KV cache and position; the weights
+// of a step are read once for all B streams.
 //
-// A step is a chain of kernels on the model's stream: embedding rows, then per
-// block RMSNorm, QKV (Q4 GEMM for B vectors, RoPE at each stream's position,
-// the k/v rows written straight into the stream's cache), split-K attention
-// per (stream, KV head, split), O-proj + residual, RMSNorm, gate/up + SwiGLU,
-// down + residual; then the output norm, the f32 lm_head for B vectors and a
-// first-max argmax per stream.  Arithmetic per stream is the single-stream
-// path's (the reference's forward_core, src/nn/llm/forward.rs:7-63): RMSNorm
-// as (x*inv)*w (norm.rs:17-87), Q4 dots with the |t|<1e-6 flush then the bias
-// (genomic.rs:331-335, linear/forward.rs:113-115), split RoPE / interleaved
-// RoPE, the attention of attention.rs:88-127, swiglu_balanced.
+// A step is a chain of kernels on the model's stream, captured once per batch
+// size as a CUDA graph and chained with programmatic dependent launch: the
+// embedding rows, then per block QKV (RMSNorm of the B residual rows while
+// staging, Q4 GEMM for B vectors, RoPE at each stream's position, the k/v rows
+// written straight into the stream's cache), split-K attention per (stream,
+// KV head, split), O-proj + residual, gate/up (RMSNorm while staging) +
+// SwiGLU, down + residual; then the output norm fused into the f32 lm_head
+// for B vectors and a first-max argmax per stream.  Arithmetic per stream is
+// the single-stream path's (the reference's forward_core,
+// src/nn/llm/forward.rs:7-63): RMSNorm as (x*inv)*w (norm.rs:17-87), Q4 dots
+// with the |t|<1e-6 flush then the bias (genomic.rs:331-335,
+// linear/forward.rs:113-115), split RoPE / interleaved RoPE, the attention of
+// attention.rs:88-127, swiglu_balanced.
 #pragma once
 
 #include "gemm.cuh"
@@ -37,38 +40,11 @@ struct BatchCache {
 };
 
 __global__ void k_embed_batch(const float* embd, int V, int d, BatchStreams bs, float* x) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.x;
   const float* src = embd + (size_t)(bs.tok[b] % (unsigned)V) * d;  // get_row_core: row token % V
   for (int i = threadIdx.x; i < d; i += blockDim.x) x[(size_t)b * d + i] = __ldg(src + i);
-}
-
-// out[b] = (x[b] * (1/sqrt(ss/n + eps))) * w, one CTA per stream.  With st,
-// the block-input and normed-output NaN guards of block/forward.rs:11-13 and
-// :22-24 (codes at the stream's position).
-__global__ void __launch_bounds__(256) k_rmsnorm_batch(const float* x, const float* w, float eps, int n, float* out,
-                                                       DevState* st, BatchStreams bs, int layer) {
-  __shared__ float red[32];
-  const int b = blockIdx.x;
-  const float* xb = x + (size_t)b * n;
-  float ss = 0.f;
-  int bad = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float v = xb[i];
-    ss = fmaf(v, v, ss);
-    bad |= (v != v);
-  }
-  ss = block_sum(ss, red);
-  const float inv = 1.0f / sqrtf(ss / (float)n + eps);
-  int bad_out = 0;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const float o = (xb[i] * inv) * w[i];
-    out[(size_t)b * n + i] = o;
-    bad_out |= (o != o);
-  }
-  if (st) {
-    if (bad) nan_flag(st, bs.pos[b], layer, kNanInput);
-    if (bad_out) nan_flag(st, bs.pos[b], layer, kNanAttnNorm);
-  }
 }
 
 // QKV epilogue: the unit u = r0/2 is a RoPE pair (rows stored pair-interleaved
@@ -172,62 +148,112 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_batch(AttnBatchArgs B) {
   a.hd = hd;
   a.scale = B.scale;
   a.st = nullptr;
+  a.fresh = 1;  // the stream's row at pos is written by the QKV kernel just before
   attn_split(a, blockIdx.x, blockIdx.y);
 }
 
-// f32 lm_head for B vectors (linear/forward.rs:20-32, no flush) + first-max
-// argmax per stream (llm/forward.rs:262-271): a warp per vocab row, the B
-// normed vectors in shared memory, per-CTA best keys, the last CTA reduces.
-constexpr int kLbThreads = 512;
+// Output RMSNorm + f32 lm_head for B vectors (llm/forward.rs:28,44-46,
+// linear/forward.rs:20-32, no flush) + first-max argmax per stream
+// (llm/forward.rs:262-271).  Every CTA normalises the B residual rows into
+// shared memory ((x*inv)*w, norm.rs:17-87); a warp then takes RPW vocab rows
+// at a time, so each activation float4 read from shared memory serves RPW
+// rows, with RPW x 2 weight float4 loads in flight per lane; per-CTA best
+// keys, and the last CTA reduces them.
+constexpr int kLbThreads = 256;
 struct LmBatchArgs {
   const float* W;       // [V][d]
   const float* bias;    // [V] or nullptr
-  const float* xn;      // [B][d]
+  const float* x;       // [B][d] residual rows (before the output norm)
+  const float* norm_w;  // [d]
+  float eps;
   float* logits;        // [B][V]
   unsigned long long* part;  // [grid][B]
   unsigned* cnt;        // zero between launches
   unsigned* argmax;     // [B]
   int V, d, B, rows_per_cta;
 };
-template <int MB>
+template <int MB, int RPW>
 __global__ void __launch_bounds__(kLbThreads) k_lmhead_batch(LmBatchArgs A) {
   extern __shared__ __align__(16) float lb_smem[];
   __shared__ unsigned long long wbest[kLbThreads / 32][MB];
   __shared__ int is_last;
+  constexpr int U = 2;  // float4 steps per row in flight
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = kLbThreads / 32;
   const int d = A.d, K4 = d >> 2;
-  for (int i = tid; i < A.B * d; i += kLbThreads) lb_smem[i] = A.xn[i];
+  pdl_wait();
+  pdl_trigger();
+  for (int b = wid; b < A.B; b += nw) {  // warp b: RMSNorm of row b
+    const float4* xr = reinterpret_cast<const float4*>(A.x + (size_t)b * d);
+    float ss = 0.f;
+    for (int j = lane; j < K4; j += 32) {
+      const float4 v = __ldcg(xr + j);
+      ss = fmaf(v.x, v.x, ss);
+      ss = fmaf(v.y, v.y, ss);
+      ss = fmaf(v.z, v.z, ss);
+      ss = fmaf(v.w, v.w, ss);
+    }
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)d + A.eps);
+    float4* o = reinterpret_cast<float4*>(lb_smem + (size_t)b * d);
+    const float4* w = reinterpret_cast<const float4*>(A.norm_w);
+    for (int j = lane; j < K4; j += 32) {
+      const float4 v = __ldcg(xr + j), g = __ldg(w + j);
+      o[j] = make_float4((v.x * inv) * g.x, (v.y * inv) * g.y, (v.z * inv) * g.z, (v.w * inv) * g.w);
+    }
+  }
   __syncthreads();
   unsigned long long best[MB];
 #pragma unroll
   for (int b = 0; b < MB; ++b) best[b] = 0ull;
   const int rbeg = blockIdx.x * A.rows_per_cta, rend = min(A.V, rbeg + A.rows_per_cta);
-  for (int r = rbeg + wid; r < rend; r += nw) {
-    const float4* w4 = reinterpret_cast<const float4*>(A.W + (size_t)r * d);
-    float acc[MB];
+  for (int r0 = rbeg + wid * RPW; r0 < rend; r0 += nw * RPW) {
+    const float4* w4[RPW];
 #pragma unroll
-    for (int b = 0; b < MB; ++b) acc[b] = 0.f;
-    for (int j = lane; j < K4; j += 32) {
-      const float4 u = __ldg(w4 + j);
+    for (int q = 0; q < RPW; ++q) w4[q] = reinterpret_cast<const float4*>(A.W + (size_t)min(r0 + q, rend - 1) * d);
+    float acc[RPW][MB];
 #pragma unroll
-      for (int b = 0; b < MB; ++b) {
-        if (b < A.B) {
-          const float4 xv = reinterpret_cast<const float4*>(lb_smem + (size_t)b * d)[j];
-          acc[b] = fmaf(u.x, xv.x, acc[b]);
-          acc[b] = fmaf(u.y, xv.y, acc[b]);
-          acc[b] = fmaf(u.z, xv.z, acc[b]);
-          acc[b] = fmaf(u.w, xv.w, acc[b]);
+    for (int q = 0; q < RPW; ++q)
+#pragma unroll
+      for (int b = 0; b < MB; ++b) acc[q][b] = 0.f;
+    for (int j0 = lane; j0 < K4; j0 += 32 * U) {
+      float4 u[U][RPW];
+#pragma unroll
+      for (int t = 0; t < U; ++t)
+#pragma unroll
+        for (int q = 0; q < RPW; ++q)
+          u[t][q] = (j0 + 32 * t < K4) ? __ldcs(w4[q] + j0 + 32 * t) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int t = 0; t < U; ++t) {
+        if (j0 + 32 * t < K4) {
+#pragma unroll
+          for (int b = 0; b < MB; ++b) {
+            if (b < A.B) {
+              const float4 xv = reinterpret_cast<const float4*>(lb_smem + (size_t)b * d)[j0 + 32 * t];
+#pragma unroll
+              for (int q = 0; q < RPW; ++q) {
+                acc[q][b] = fmaf(u[t][q].x, xv.x, acc[q][b]);
+                acc[q][b] = fmaf(u[t][q].y, xv.y, acc[q][b]);
+                acc[q][b] = fmaf(u[t][q].z, xv.z, acc[q][b]);
+                acc[q][b] = fmaf(u[t][q].w, xv.w, acc[q][b]);
+              }
+            }
+          }
         }
       }
     }
-    const float bb = A.bias ? __ldg(A.bias + r) : 0.f;
 #pragma unroll
-    for (int b = 0; b < MB; ++b) {
-      if (b < A.B) {
-        const float v = warp_sum(acc[b]) + bb;
-        if (lane == 0) A.logits[(size_t)b * A.V + r] = v;
-        const unsigned long long key = amax_key(v, (unsigned)r);
-        best[b] = key > best[b] ? key : best[b];
+    for (int q = 0; q < RPW; ++q) {
+      const int r = r0 + q;
+      if (r >= rend) break;
+      const float bb = A.bias ? __ldg(A.bias + r) : 0.f;
+#pragma unroll
+      for (int b = 0; b < MB; ++b) {
+        if (b < A.B) {
+          const float v = warp_sum(acc[q][b]) + bb;
+          if (lane == 0) A.logits[(size_t)b * A.V + r] = v;
+          const unsigned long long key = amax_key(v, (unsigned)r);
+          best[b] = key > best[b] ? key : best[b];
+        }
       }
     }
   }

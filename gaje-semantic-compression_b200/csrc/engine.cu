@@ -58,6 +58,7 @@ struct Q4Dev {
 };
 
 constexpr int kMaxDynSmem = 227 * 1024;
+constexpr int kBatchMT = 8;  // activation vectors per Q4 GEMM CTA of a batched step
 
 // Launch with cudaLaunchKernelEx; `pdl` lets the kernel start before its
 // predecessor finishes (programmatic stream serialization): the kernel itself
@@ -94,13 +95,30 @@ GemvPlan plan_gemv(int mode, const Q4Dev& m, int units, int sms) {
   return p;
 }
 
+// Raises a kernel's dynamic shared-memory limit to at least `bytes` (the
+// limit is per function and process-wide, so it only ever grows: a model
+// loaded later with a smaller shape must not lower it under an earlier one).
+// Any size is raised explicitly, since static shared memory counts against
+// the default 48 KB too.
 int smem_optin(const void* kern, size_t bytes) {
   if (bytes > size_t(kMaxDynSmem))
     return set_error(GAJE_ERR_UNSUPPORTED, "a kernel needs more than 227 KB of shared memory for this shape");
-  if (bytes > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
-    if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-  }
+  static std::mutex mu;
+  static std::vector<std::pair<const void*, size_t>> done;
+  std::lock_guard<std::mutex> lk(mu);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const void* key = reinterpret_cast<const void*>(reinterpret_cast<uintptr_t>(kern) ^ (uintptr_t(dev) << 56));
+  for (auto& kv : done)
+    if (kv.first == key && kv.second >= bytes) return GAJE_OK;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes));
+  if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  for (auto& kv : done)
+    if (kv.first == key) {
+      kv.second = bytes;
+      return GAJE_OK;
+    }
+  done.emplace_back(key, bytes);
   return GAJE_OK;
 }
 
@@ -250,19 +268,27 @@ struct gaje_model {
   // batched streams (gaje_cuda_forward_batch)
   int max_streams = 0;
   BatchCache bcache{};
-  float *bx = nullptr, *bxn = nullptr, *bq = nullptr, *battn = nullptr, *bact = nullptr, *blogits = nullptr;
+  float *bx = nullptr, *bq = nullptr, *battn = nullptr, *bact = nullptr, *blogits = nullptr;
   float *bpart_o = nullptr, *bpart_ml = nullptr;
   unsigned* bcnt = nullptr;
   unsigned long long* blm_part = nullptr;
   unsigned* blm_cnt = nullptr;
+  float* bsk_part = nullptr;   // Q4 GEMM split partials
+  unsigned* bsk_cnt = nullptr; // Q4 GEMM split counters
+  size_t bsk_tiles = 0;
+  int bsk_per_sm = 1;          // resident Q4 GEMM CTAs per SM
   unsigned* bdev = nullptr;   // [3][max_streams]: tokens, positions, stream ids; then [max_streams] argmax
   unsigned* h_bdev = nullptr; // pinned staging of the same
   std::vector<uint32_t> bpos; // per-stream cache length (host)
+  std::vector<cudaGraphExec_t> bgraphs;  // [max_streams + 1]: the captured step per batch size
+  int blm_grid = 0;                      // lm_head CTAs of a batched step
 
   ~gaje_model() {
     if (phase_ns) cudaFree(phase_ns);
     if (trace_ns) cudaFree(trace_ns);
     if (graph) cudaGraphExecDestroy(graph);
+    for (cudaGraphExec_t g : bgraphs)
+      if (g) cudaGraphExecDestroy(g);
     if (arena.base) cudaFree(arena.base);
     if (h_st) cudaFreeHost(h_st);
     if (h_tok) cudaFreeHost(h_tok);
@@ -314,6 +340,7 @@ struct gaje_model {
     a.hd = hd;
     a.scale = P.attn_scale;
     a.st = st;
+    a.fresh = 0;
     return a;
   }
 
@@ -636,6 +663,122 @@ bool plan_mega(gaje_model* m) {
   return p.lm_stage_rows >= 1 && m->mega_smem + fa.sharedSizeBytes <= size_t(kMaxDynSmem);
 }
 
+// ---- batched streams (gaje_cuda_forward_batch)
+
+
+int batch_lm_mb(int B) { return B <= 8 ? 8 : 16; }
+size_t batch_attn_smem(const gaje_model* m) {
+  return attn_smem_bytes(m->nh / m->nkv, m->hd, attn_chunk_max(m->max_ctx));
+}
+
+// Shared-memory opt-ins and the lm_head grid, once at load (never during a
+// capture).
+int batch_setup(gaje_model* m) {
+  const size_t sk = skinny_smem_bytes(kBatchMT);
+  if (int e = smem_optin((const void*)k_q4_gemm_skinny<kBatchMT, true, EpiQkvBatch>, sk)) return e;
+  if (int e = smem_optin((const void*)k_q4_gemm_skinny<kBatchMT, false, EpiResidBatch>, sk)) return e;
+  if (int e = smem_optin((const void*)k_q4_gemm_skinny<kBatchMT, true, EpiSwigluBatch>, sk)) return e;
+  if (int e = smem_optin((const void*)k_attn_batch, batch_attn_smem(m))) return e;
+  const size_t lm8 = size_t(8) * m->d * 4, lm16 = size_t(16) * m->d * 4;
+  if (int e = smem_optin((const void*)k_lmhead_batch<8, 4>, lm8)) return e;
+  if (int e = smem_optin((const void*)k_lmhead_batch<16, 2>, lm16)) return e;
+  int per = 0;
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, k_lmhead_batch<16, 2>, kLbThreads, lm16));
+  m->blm_grid = m->sms * std::max(1, std::min(per, 4));
+  int sk_per = 0;
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&sk_per, k_q4_gemm_skinny<kBatchMT, true, EpiSwigluBatch>,
+                                                   kSkThreads, sk));
+  m->bsk_per_sm = std::max(1, sk_per);
+  return GAJE_OK;
+}
+
+// Grid of one Q4 GEMM of a batched step: K splits across CTAs when K spans
+// more than one split, and the fewest row pairs per warp that still fit the
+// launch in one wave of resident CTAs.
+struct SkLaunch {
+  dim3 grid;
+  SkSplit sp;
+};
+SkLaunch sk_plan(const gaje_model* m, const Q4Dev& q, int Bi) {
+  SkLaunch r;
+  const unsigned mtiles = unsigned((Bi + kBatchMT - 1) / kBatchMT);
+  const unsigned z = unsigned((q.K + kSkChunk - 1) / kSkChunk);
+  const long slots = long(m->sms) * m->bsk_per_sm;
+  int ppw = 1;
+  auto gx = [&](int p) { return unsigned((q.N + 2 * kSkWarps * p - 1) / (2 * kSkWarps * p)); };
+  while (ppw < 8 && long(gx(ppw)) * mtiles * z > slots) ++ppw;
+  r.grid = dim3(gx(ppw), mtiles, z);
+  r.sp.ppw = ppw;
+  r.sp.part = z > 1 ? m->bsk_part : nullptr;
+  r.sp.cnt = z > 1 ? m->bsk_cnt : nullptr;
+  return r;
+}
+
+// The kernels of one batched step for the first Bi entries of the stream
+// table (already on the device), in stream order, every launch after the
+// first a programmatic dependent launch.  Nothing here depends on the
+// streams' positions, so the sequence is captured once per Bi.
+int launch_batch(gaje_model* m, int Bi) {
+  cudaStream_t st = m->stream;
+  const size_t S = size_t(m->max_streams);
+  BatchStreams bs{m->bdev, m->bdev + S, m->bdev + 2 * S};
+  unsigned* d_argmax = m->bdev + 3 * S;
+  const int d = m->d, L = m->L;
+  const float eps = m->info.eps;
+  constexpr int MT = kBatchMT;
+  const size_t sk = skinny_smem_bytes(MT);
+  cudaError_t e = launch_k(k_embed_batch, dim3(Bi), dim3(256), 0, st, false, (const float*)m->embd, m->V, d, bs,
+                           m->bx);
+  for (int l = 0; l < L && e == cudaSuccess; ++l) {
+    SkNorm an{m->attn_norm[l], eps, m->st, bs.pos, l};
+    EpiQkvBatch eq{m->bq, m->bcache, bs, m->rope, m->nh, m->nkv, m->hd, int(m->info.rope_split), l};
+    SkLaunch pq = sk_plan(m, m->qkv[l], Bi);
+    e = launch_k(k_q4_gemm_skinny<MT, true, EpiQkvBatch>, pq.grid, dim3(kSkThreads), sk, st, true, m->qkv[l].view(),
+                 (const float*)m->bx, Bi, an, pq.sp, eq);
+    if (e != cudaSuccess) break;
+    AttnBatchArgs aa{m->bq, m->battn, m->bcache, bs, m->bpart_o, m->bpart_ml, m->bcnt, l, m->nh,
+                     1.0f / sqrtf(float(m->hd))};
+    e = launch_k(k_attn_batch, dim3(unsigned(m->nkv), kAttnMaxSplits, unsigned(Bi)), dim3(kAttnThreads),
+                 batch_attn_smem(m), st, true, aa);
+    if (e != cudaSuccess) break;
+    SkLaunch po = sk_plan(m, m->wo[l], Bi);
+    e = launch_k(k_q4_gemm_skinny<MT, false, EpiResidBatch>, po.grid, dim3(kSkThreads), sk, st, true,
+                 m->wo[l].view(), (const float*)m->battn, Bi, SkNorm{}, po.sp, EpiResidBatch{m->bx, d, nullptr, bs, l});
+    if (e != cudaSuccess) break;
+    SkNorm fn{m->ffn_norm[l], eps, nullptr, bs.pos, l};
+    SkLaunch pg = sk_plan(m, m->gate_up[l], Bi);
+    e = launch_k(k_q4_gemm_skinny<MT, true, EpiSwigluBatch>, pg.grid, dim3(kSkThreads), sk, st, true,
+                 m->gate_up[l].view(), (const float*)m->bx, Bi, fn, pg.sp,
+                 EpiSwigluBatch{m->bact, m->ff, m->st, bs, l});
+    if (e != cudaSuccess) break;
+    SkLaunch pd = sk_plan(m, m->down[l], Bi);
+    e = launch_k(k_q4_gemm_skinny<MT, false, EpiResidBatch>, pd.grid, dim3(kSkThreads), sk, st, true,
+                 m->down[l].view(), (const float*)m->bact, Bi, SkNorm{}, pd.sp, EpiResidBatch{m->bx, d, m->st, bs, l});
+  }
+  const int MB = batch_lm_mb(Bi);
+  for (int b0 = 0; b0 < Bi && e == cudaSuccess; b0 += MB) {
+    LmBatchArgs la{};
+    la.W = m->lm_head;
+    la.bias = m->lm_bias;
+    la.x = m->bx + size_t(b0) * d;
+    la.norm_w = m->out_norm;
+    la.eps = eps;
+    la.logits = m->blogits + size_t(b0) * m->V;
+    la.part = m->blm_part;
+    la.cnt = m->blm_cnt;
+    la.argmax = d_argmax + b0;
+    la.V = m->V;
+    la.d = d;
+    la.B = std::min(MB, Bi - b0);
+    la.rows_per_cta = (m->V + m->blm_grid - 1) / m->blm_grid;
+    const size_t smem = size_t(MB) * d * 4;
+    e = MB == 8 ? launch_k(k_lmhead_batch<8, 4>, dim3(m->blm_grid), dim3(kLbThreads), smem, st, true, la)
+                : launch_k(k_lmhead_batch<16, 2>, dim3(m->blm_grid), dim3(kLbThreads), smem, st, true, la);
+  }
+  if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  return GAJE_OK;
+}
+
 int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   FlatFile f;
   std::string err;
@@ -737,7 +880,6 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
       m->bcache.k = a.take<float>(bc);
       m->bcache.v = a.take<float>(bc);
       m->bx = a.take<float>(S * d);
-      m->bxn = a.take<float>(S * d);
       m->bq = a.take<float>(S * qd);
       m->battn = a.take<float>(S * qd);
       m->bact = a.take<float>(S * m->ff);
@@ -745,9 +887,23 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
       m->bpart_o = a.take<float>(S * m->nkv * kAttnMaxSplits * G * m->hd);
       m->bpart_ml = a.take<float>(S * m->nkv * kAttnMaxSplits * G * 2);
       m->bcnt = a.take<unsigned>(S * m->nkv);
-      m->blm_part = a.take<unsigned long long>(size_t(m->sms) * 16);
+      m->blm_part = a.take<unsigned long long>(size_t(m->sms) * 4 * 16);
       m->blm_cnt = a.take<unsigned>(1);
       m->bdev = a.take<unsigned>(4 * S);
+      // Q4 GEMM split partials [split][stream][row] and per-tile counters
+      size_t part = 0, tiles = 0;
+      const size_t shapes[4][2] = {{size_t(m->nh + 2 * m->nkv) * m->hd, size_t(d)},
+                                   {size_t(d), size_t(m->nh) * m->hd},
+                                   {size_t(2 * m->ff), size_t(d)},
+                                   {size_t(d), size_t(m->ff)}};
+      for (const auto& nk : shapes) {
+        const size_t ns = (nk[1] + kSkChunk - 1) / kSkChunk;
+        if (ns > 1) part = std::max(part, ns * nk[0] * S);
+        tiles = std::max(tiles, (nk[0] + 2 * kSkWarps - 1) / (2 * kSkWarps) * ((S + kBatchMT - 1) / kBatchMT));
+      }
+      m->bsk_part = a.take<float>(std::max<size_t>(part, 1));
+      m->bsk_cnt = a.take<unsigned>(tiles);
+      m->bsk_tiles = tiles;
     }
   };
   Arena sizing;
@@ -795,8 +951,11 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     m->bcache.hd = m->hd;
     CK(cudaMemsetAsync(m->bcnt, 0, size_t(m->max_streams) * m->nkv * sizeof(unsigned), m->stream));
     CK(cudaMemsetAsync(m->blm_cnt, 0, sizeof(unsigned), m->stream));
+    CK(cudaMemsetAsync(m->bsk_cnt, 0, m->bsk_tiles * sizeof(unsigned), m->stream));
     CK(cudaHostAlloc(&m->h_bdev, size_t(4) * m->max_streams * sizeof(unsigned), cudaHostAllocDefault));
     m->bpos.assign(size_t(m->max_streams), 0u);
+    m->bgraphs.assign(size_t(m->max_streams) + 1, nullptr);
+    if (int s = batch_setup(m)) return s;
   }
   CK(cudaMemsetAsync(m->kcache, 0, L * size_t(m->nkv) * m->max_ctx * m->hd * 4, m->stream));
   CK(cudaMemsetAsync(m->vcache, 0, L * size_t(m->nkv) * m->max_ctx * m->hd * 4, m->stream));
@@ -976,7 +1135,6 @@ int gaje_cuda_forward_batch(gaje_model* m, const uint32_t* stream_ids, const uin
     return set_error(GAJE_ERR_UNSUPPORTED, "use_genomic_norm is not implemented on the batched path");
   const size_t S = size_t(m->max_streams);
   std::vector<char> seen(S, 0);
-  unsigned max_ctx_used = 0;
   for (size_t b = 0; b < B; ++b) {
     const uint32_t sid = stream_ids[b];
     if (sid >= S) return set_error(GAJE_ERR_INVALID, "stream id out of range");
@@ -986,68 +1144,38 @@ int gaje_cuda_forward_batch(gaje_model* m, const uint32_t* stream_ids, const uin
     m->h_bdev[b] = tokens[b];
     m->h_bdev[S + b] = m->bpos[sid];
     m->h_bdev[2 * S + b] = sid;
-    max_ctx_used = std::max(max_ctx_used, m->bpos[sid] + 1u);
   }
   CK(cudaSetDevice(m->device));
   cudaStream_t st = m->stream;
+  const int Bi = int(B);
   CK(cudaMemcpyAsync(m->bdev, m->h_bdev, 3 * S * sizeof(unsigned), cudaMemcpyHostToDevice, st));
-  BatchStreams bs{m->bdev, m->bdev + S, m->bdev + 2 * S};
-  unsigned* d_argmax = m->bdev + 3 * S;
-  const int d = m->d, L = m->L, Bi = int(B);
-  const float eps = m->info.eps;
-  constexpr int MT = 8;
-  const unsigned mtiles = unsigned((B + MT - 1) / MT);
-  const size_t sk_smem = skinny_smem_bytes(MT);
-  auto ctas = [](const Q4Dev& q) { return unsigned((q.N + 2 * kSkWarps - 1) / (2 * kSkWarps)); };
-  if (int e = smem_optin((const void*)k_q4_gemm_skinny<MT, EpiQkvBatch>, sk_smem)) return e;
-  if (int e = smem_optin((const void*)k_q4_gemm_skinny<MT, EpiResidBatch>, sk_smem)) return e;
-  if (int e = smem_optin((const void*)k_q4_gemm_skinny<MT, EpiSwigluBatch>, sk_smem)) return e;
-  int nsplit, chunk;
-  attn_splits(int(max_ctx_used), nsplit, chunk);
-  const int G = m->nh / m->nkv;
-  const size_t at_smem = attn_smem_bytes(G, m->hd, chunk);
-  if (int e = smem_optin((const void*)k_attn_batch, at_smem)) return e;
-  constexpr int MB = 16;
-  const size_t lm_smem = size_t(MB) * d * 4;
-  if (int e = smem_optin((const void*)k_lmhead_batch<MB>, lm_smem)) return e;
-  k_embed_batch<<<Bi, 256, 0, st>>>(m->embd, m->V, d, bs, m->bx);
-  for (int l = 0; l < L; ++l) {
-    k_rmsnorm_batch<<<Bi, 256, 0, st>>>(m->bx, m->attn_norm[l], eps, d, m->bxn, m->st, bs, l);
-    EpiQkvBatch eq{m->bq, m->bcache, bs, m->rope, m->nh, m->nkv, m->hd, int(m->info.rope_split), l};
-    k_q4_gemm_skinny<MT, EpiQkvBatch><<<dim3(ctas(m->qkv[l]), mtiles), kSkThreads, sk_smem, st>>>(
-        m->qkv[l].view(), m->bxn, Bi, eq);
-    AttnBatchArgs aa{m->bq, m->battn, m->bcache, bs, m->bpart_o, m->bpart_ml, m->bcnt, l, m->nh,
-                     1.0f / sqrtf(float(m->hd))};
-    k_attn_batch<<<dim3(unsigned(m->nkv), kAttnMaxSplits, unsigned(B)), kAttnThreads, at_smem, st>>>(aa);
-    k_q4_gemm_skinny<MT, EpiResidBatch><<<dim3(ctas(m->wo[l]), mtiles), kSkThreads, sk_smem, st>>>(
-        m->wo[l].view(), m->battn, Bi, EpiResidBatch{m->bx, d, nullptr, bs, l});
-    k_rmsnorm_batch<<<Bi, 256, 0, st>>>(m->bx, m->ffn_norm[l], eps, d, m->bxn, nullptr, bs, l);
-    k_q4_gemm_skinny<MT, EpiSwigluBatch><<<dim3(ctas(m->gate_up[l]), mtiles), kSkThreads, sk_smem, st>>>(
-        m->gate_up[l].view(), m->bxn, Bi, EpiSwigluBatch{m->bact, m->ff, m->st, bs, l});
-    k_q4_gemm_skinny<MT, EpiResidBatch><<<dim3(ctas(m->down[l]), mtiles), kSkThreads, sk_smem, st>>>(
-        m->down[l].view(), m->bact, Bi, EpiResidBatch{m->bx, d, m->st, bs, l});
+  if (!m->use_graph) {
+    if (int s = launch_batch(m, Bi)) return s;
+  } else {
+    cudaGraphExec_t& ge = m->bgraphs[size_t(Bi)];
+    if (!ge) {
+      cudaGraph_t g = nullptr;
+      CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal));
+      const int s = launch_batch(m, Bi);
+      const cudaError_t e = cudaStreamEndCapture(st, &g);
+      if (s) {
+        if (g) cudaGraphDestroy(g);
+        return s;
+      }
+      if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(e));
+      const cudaError_t ei = cudaGraphInstantiate(&ge, g, 0);
+      cudaGraphDestroy(g);
+      if (ei != cudaSuccess) {
+        ge = nullptr;
+        return set_error(GAJE_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ei));
+      }
+    }
+    CK(cudaGraphLaunch(ge, st));
   }
-  k_rmsnorm_batch<<<Bi, 256, 0, st>>>(m->bx, m->out_norm, eps, d, m->bxn, nullptr, bs, L);
-  for (int b0 = 0; b0 < Bi; b0 += MB) {
-    LmBatchArgs la{};
-    la.W = m->lm_head;
-    la.bias = m->lm_bias;
-    la.xn = m->bxn + size_t(b0) * d;
-    la.logits = m->blogits + size_t(b0) * m->V;
-    la.part = m->blm_part;
-    la.cnt = m->blm_cnt;
-    la.argmax = d_argmax + b0;
-    la.V = m->V;
-    la.d = d;
-    la.B = std::min(MB, Bi - b0);
-    la.rows_per_cta = (m->V + m->sms - 1) / m->sms;
-    k_lmhead_batch<MB><<<m->sms, kLbThreads, lm_smem, st>>>(la);
-  }
-  CK(cudaGetLastError());
   const int kk = m->logits_k();
   if (logits_out && kk > 0)  // K-WTA on the returned logits (llm/forward.rs:58-61); the argmax is unaffected
     for (int b = 0; b < Bi; ++b) k_kwta<<<1, kKwtaThreads, 0, st>>>(m->blogits + size_t(b) * m->V, m->V, kk);
-  CK(cudaMemcpyAsync(m->h_bdev + 3 * S, d_argmax, B * sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(m->h_bdev + 3 * S, m->bdev + 3 * S, B * sizeof(unsigned), cudaMemcpyDeviceToHost, st));
   if (logits_out)
     CK(cudaMemcpyAsync(logits_out, m->blogits, B * size_t(m->V) * 4, cudaMemcpyDeviceToHost, st));
   CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, st));
@@ -1432,13 +1560,15 @@ int gaje_cuda_q4_0_gemv(const gaje_q4_matrix* h, const float* x, float* y, size_
     CK(launch_k(k_gemv<G_PLAIN>, dim3(p.grid), dim3(kGemvThreads), p.smem, s, false, P, L, a));
     return GAJE_OK;
   }
-  // M > 1: every weight block is dequantised once per CTA for 8 vectors
+  // M > 1: every weight word is turned into floats once per CTA for 8 vectors;
+  // the CTA walks the K splits itself (no workspace)
   constexpr int MT = 8;
   const int ctas = (h->m.N + 2 * kSkWarps - 1) / (2 * kSkWarps);
   const size_t smem = skinny_smem_bytes(MT);
-  if (int st = smem_optin((const void*)k_q4_gemm_skinny<MT, EpiStore>, smem)) return st;
-  k_q4_gemm_skinny<MT, EpiStore><<<dim3(ctas, unsigned((M + MT - 1) / MT)), kSkThreads, smem, s>>>(
-      h->m.view(), x, int(M), EpiStore{y, h->m.N});
+  if (reinterpret_cast<uintptr_t>(x) & 15u) return set_error(GAJE_ERR_INVALID, "x must be 16-byte aligned");
+  if (int st = smem_optin((const void*)k_q4_gemm_skinny<MT, false, EpiStore>, smem)) return st;
+  k_q4_gemm_skinny<MT, false, EpiStore><<<dim3(ctas, unsigned((M + MT - 1) / MT)), kSkThreads, smem, s>>>(
+      h->m.view(), x, int(M), SkNorm{}, SkSplit{}, EpiStore{y, h->m.N});
   CK(cudaGetLastError());
   return GAJE_OK;
 }

@@ -510,6 +510,7 @@ struct AttnArgs {
   int stride, nh, nkv, hd;
   float scale;
   DevState* st;     // decode state (step) or nullptr (op level)
+  int fresh;        // with ctx > 0: row ctx-1 is written by the preceding kernel (batched steps)
 };
 
 // One CTA per (kv head g, split s).  The split's cached K/V rows (positions
@@ -536,7 +537,7 @@ __device__ __forceinline__ void attn_split(const AttnArgs& A, const int g, const
   const int n = min(ctx, t0 + chunk) - t0;
   // rows already in the cache before this step; the step's own row (ctx-1)
   // is written by the preceding kernel
-  const int newest = A.ctx > 0 ? ctx : ctx - 1;
+  const int newest = (A.ctx > 0 && !A.fresh) ? ctx : ctx - 1;
   const int n_old = max(0, min(n, newest - t0));
   const int cm = chunk;  // smem row capacity used by this launch
   float* Ks = reinterpret_cast<float*>(smem_raw + kSmemHeader);
