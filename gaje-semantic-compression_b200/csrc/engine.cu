@@ -727,6 +727,8 @@ int launch_batch(gaje_model* m, int Bi) {
   const float eps = m->info.eps;
   constexpr int MT = kBatchMT;
   const size_t sk = skinny_smem_bytes(MT);
+  int ns_max = 1, ch_max = 1;  // attention splits at the longest context
+  attn_splits(m->max_ctx, ns_max, ch_max);
   cudaError_t e = launch_k(k_embed_batch, dim3(Bi), dim3(256), 0, st, false, (const float*)m->embd, m->V, d, bs,
                            m->bx);
   for (int l = 0; l < L && e == cudaSuccess; ++l) {
@@ -738,7 +740,7 @@ int launch_batch(gaje_model* m, int Bi) {
     if (e != cudaSuccess) break;
     AttnBatchArgs aa{m->bq, m->battn, m->bcache, bs, m->bpart_o, m->bpart_ml, m->bcnt, l, m->nh,
                      1.0f / sqrtf(float(m->hd))};
-    e = launch_k(k_attn_batch, dim3(unsigned(m->nkv), kAttnMaxSplits, unsigned(Bi)), dim3(kAttnThreads),
+    e = launch_k(k_attn_batch, dim3(unsigned(m->nkv), unsigned(ns_max), unsigned(Bi)), dim3(kAttnThreads),
                  batch_attn_smem(m), st, true, aa);
     if (e != cudaSuccess) break;
     SkLaunch po = sk_plan(m, m->wo[l], Bi);

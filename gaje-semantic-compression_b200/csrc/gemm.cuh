@@ -75,9 +75,11 @@ __device__ __forceinline__ void q4_word_pairs(uint32_t a, unsigned long long (&q
 //
 // With NORM, the staged activations are RMSNorm(x) = (x * inv) * norm_w with
 // inv = 1/sqrt(sum(x^2)/K + eps) per vector (norm.rs:17-87), computed by each
-// CTA for its MT vectors (K = d for the projections that follow a norm); with
-// `st`, CTA (0, y, 0) also raises the block-input and normed-output NaN
-// guards of block/forward.rs:11-13 and :22-24 at each vector's position.
+// CTA for its MT vectors (K = d for the projections that follow a norm) in
+// the same pass that stages the raw values, then applied in shared memory;
+// with `st`, the CTAs of column 0 also raise the block-input and
+// normed-output NaN guards of block/forward.rs:11-13 and :22-24 at each
+// vector's position.
 //
 // Launch: grid (ceil(N / (2 * kSkWarps * ppw)), ceil(M/MT), Z), kSkThreads,
 // skinny_smem_bytes(MT); x rows 16-byte aligned (K % 32 == 0).  Z = 1: the
@@ -93,8 +95,9 @@ __global__ void __launch_bounds__(kSkThreads) k_q4_gemm_skinny(Q4View W, const f
   constexpr int kMaxPpw = 8;
   extern __shared__ __align__(16) float sk_smem[];
   __shared__ float inv_s[MT];
-  __shared__ float red[kSkWarps * kMaxPpw * MT * 2];  // per-lane sums over splits (Z = 1)
+  __shared__ float red[kSkWarps * kMaxPpw * MT * 2];  // per-lane sums over splits (Z = 1); row sums of squares
   __shared__ int is_last;
+  __shared__ unsigned bad_s;
   float* xs = sk_smem;                    // [MT][kSkChunk]
   float* xsum = sk_smem + MT * kSkChunk;  // [MT][kSkChunk / 32]
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -125,87 +128,105 @@ __global__ void __launch_bounds__(kSkThreads) k_q4_gemm_skinny(Q4View W, const f
   fetch(zb, 0, qa, qb, sa, sb);
   pdl_wait();
   pdl_trigger();
-  if constexpr (NORM) {
-    for (int m = wid; m < MT; m += kSkWarps) {
-      float ss = 0.f;
-      int bad = 0;
-      if (m < mt) {
-        const float4* xr = reinterpret_cast<const float4*>(x + (size_t)(m0 + m) * W.K);
-#pragma unroll 4
-        for (int j = lane; j < (W.K >> 2); j += 32) {
-          const float4 v = __ldg(xr + j);
-          ss = fmaf(v.x, v.x, ss);
-          ss = fmaf(v.y, v.y, ss);
-          ss = fmaf(v.z, v.z, ss);
-          ss = fmaf(v.w, v.w, ss);
-          bad |= (v.x != v.x) | (v.y != v.y) | (v.z != v.z) | (v.w != v.w);
-        }
-      }
-      ss = warp_sum(ss);
-      const float inv = 1.0f / sqrtf(ss / (float)W.K + nm.eps);
-      if (lane == 0) inv_s[m] = inv;
-      if (nm.st && blockIdx.x == 0 && blockIdx.z == 0 && m < mt) {  // the guards, once per vector
-        const float4* xr = reinterpret_cast<const float4*>(x + (size_t)(m0 + m) * W.K);
-        const float4* wr = reinterpret_cast<const float4*>(nm.w);
-        int bad_out = 0;
-        for (int j = lane; j < (W.K >> 2); j += 32) {
-          const float4 v = __ldg(xr + j), w = __ldg(wr + j);
-          const float o0 = (v.x * inv) * w.x, o1 = (v.y * inv) * w.y;
-          const float o2 = (v.z * inv) * w.z, o3 = (v.w * inv) * w.w;
-          bad_out |= (o0 != o0) | (o1 != o1) | (o2 != o2) | (o3 != o3);
-        }
-        bad = __any_sync(0xffffffffu, bad);
-        bad_out = __any_sync(0xffffffffu, bad_out);
-        if (lane == 0) {
-          if (bad) nan_flag(nm.st, nm.pos[m0 + m], nm.layer, kNanInput);
-          if (bad_out) nan_flag(nm.st, nm.pos[m0 + m], nm.layer, kNanAttnNorm);
-        }
-      }
-    }
-  }
   const float4* x4 = reinterpret_cast<const float4*>(xs + (lane << 5));
   const int sw = lane & 7;
   const int m = lane >> 2;  // the vector whose two rows this lane holds after the reduction
+  const bool guard = NORM && nm.st && blockIdx.x == 0;
+  if (tid == 0) bad_s = 0u;
   for (int z = zb; z < ze; ++z) {
     const int k0 = z * kSkChunk;
     const int kc = min(kSkChunk, W.K - k0);  // a multiple of 32
+    const int nf4 = kc >> 2;                  // float4s of a vector in this split (a multiple of 8)
     const bool lane_on = lane < (kc >> 5);
-    __syncthreads();  // inv_s written; the previous split's activations consumed
-    // stage this split: float4 f of vector v -> xs (swizzled by block), the
-    // block sums of the (normed) values -> xsum
+    __syncthreads();  // the previous split's activations are consumed
+    // pass 1: this split's raw activations -> xs (swizzled by block).  With
+    // NORM, the first pass reads whole rows: their sums of squares and NaN
+    // scan (the parts outside this split are read for the sums only).
     {
-      const int nf4 = kc >> 2;  // a multiple of 8
-      for (int f0 = 0; f0 < nf4; f0 += kSkThreads) {
+      const bool whole = NORM && z == zb;
+      const int n4 = whole ? (W.K >> 2) : nf4;
+      const int fbase = whole ? (k0 >> 2) : 0;  // this split's first float4 in the loop's index space
+      float ssp[MT];
+#pragma unroll
+      for (int j = 0; j < MT; ++j) ssp[j] = 0.f;
+      unsigned badm = 0u;
+      for (int f0 = 0; f0 < n4; f0 += kSkThreads) {
         const int f = f0 + tid;
-        const bool in = f < nf4;
+        const bool in = f < n4;
+        const float* src = x + (whole ? 0 : k0);
         float4 v[MT];
 #pragma unroll
         for (int j = 0; j < MT; ++j)
-          v[j] = (in && j < mt) ? __ldg(reinterpret_cast<const float4*>(x + (size_t)(m0 + j) * W.K + k0) + f)
+          v[j] = (in && j < mt) ? __ldg(reinterpret_cast<const float4*>(src + (size_t)(m0 + j) * W.K) + f)
                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-        float4 nw = make_float4(1.f, 1.f, 1.f, 1.f);
-        if (NORM && in) nw = __ldg(reinterpret_cast<const float4*>(nm.w + k0) + f);
-        const int blk = f >> 3, c = f & 7;
+        const int fs = f - fbase;
+        const bool mine = in && fs >= 0 && fs < nf4;
+        const int blk = fs >> 3, c = fs & 7;
 #pragma unroll
         for (int j = 0; j < MT; ++j) {
-          float4 u = v[j];
+          if (whole) {
+            ssp[j] = fmaf(v[j].x, v[j].x, ssp[j]);
+            ssp[j] = fmaf(v[j].y, v[j].y, ssp[j]);
+            ssp[j] = fmaf(v[j].z, v[j].z, ssp[j]);
+            ssp[j] = fmaf(v[j].w, v[j].w, ssp[j]);
+            if ((v[j].x != v[j].x) | (v[j].y != v[j].y) | (v[j].z != v[j].z) | (v[j].w != v[j].w)) badm |= 1u << j;
+          }
+          if (mine) reinterpret_cast<float4*>(xs + j * kSkChunk)[blk * 8 + (c ^ (blk & 7))] = v[j];
+        }
+      }
+      if (whole) {
+#pragma unroll
+        for (int j = 0; j < MT; ++j) {
+          const float t = warp_sum(ssp[j]);
+          if (lane == 0) red[wid * MT + j] = t;
+        }
+        if (guard && badm) atomicOr(&bad_s, badm);
+      }
+    }
+    __syncthreads();
+    if (NORM && z == zb) {
+      if (tid < MT) {
+        float t = 0.f;
+        for (int w = 0; w < kSkWarps; ++w) t += red[w * MT + tid];
+        inv_s[tid] = 1.0f / sqrtf(t / (float)W.K + nm.eps);
+        if (guard && blockIdx.z == 0 && tid < mt && (bad_s >> tid) & 1u)
+          nan_flag(nm.st, nm.pos[m0 + tid], nm.layer, kNanInput);
+      }
+      __syncthreads();
+    }
+    // pass 2 (shared memory only): NORM -> (x * inv) * w in place (the
+    // reference's order); the block sums -> xsum
+    {
+      unsigned badn = 0u;
+      for (int f0 = 0; f0 < nf4; f0 += kSkThreads) {
+        const int f = f0 + tid;
+        const bool in = f < nf4;
+        const int blk = f >> 3, c = f & 7;
+        float4* slot0 = reinterpret_cast<float4*>(xs) + blk * 8 + (c ^ (blk & 7));
+        float4 nw = make_float4(1.f, 1.f, 1.f, 1.f);
+        if (NORM && in) nw = __ldg(reinterpret_cast<const float4*>(nm.w + k0) + f);
+#pragma unroll
+        for (int j = 0; j < MT; ++j) {
+          float4 u = in ? slot0[j * (kSkChunk / 4)] : make_float4(0.f, 0.f, 0.f, 0.f);
           if constexpr (NORM) {
             const float inv = inv_s[j];
             u.x = (u.x * inv) * nw.x;
             u.y = (u.y * inv) * nw.y;
             u.z = (u.z * inv) * nw.z;
             u.w = (u.w * inv) * nw.w;
+            if (in) slot0[j * (kSkChunk / 4)] = u;
+            if (guard && in && j < mt && ((u.x != u.x) | (u.y != u.y) | (u.z != u.z) | (u.w != u.w))) badn |= 1u << j;
           }
           float s = (u.x + u.y) + (u.z + u.w);
           s += __shfl_xor_sync(0xffffffffu, s, 1);
           s += __shfl_xor_sync(0xffffffffu, s, 2);
           s += __shfl_xor_sync(0xffffffffu, s, 4);
-          if (in) {
-            reinterpret_cast<float4*>(xs + j * kSkChunk)[blk * 8 + (c ^ (blk & 7))] = u;
-            if (c == 0) xsum[j * (kSkChunk / 32) + blk] = s;
-          }
+          if (in && c == 0) xsum[j * (kSkChunk / 32) + blk] = s;
         }
       }
+      if (guard && badn)
+        for (int j = 0; j < MT; ++j)
+          if ((badn >> j) & 1u) nan_flag(nm.st, nm.pos[m0 + j], nm.layer, kNanAttnNorm);
     }
     __syncthreads();
     for (int i = 0; i < ppw; ++i) {

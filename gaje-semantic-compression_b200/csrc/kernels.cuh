@@ -608,6 +608,8 @@ __device__ __forceinline__ void attn_split(const AttnArgs& A, const int g, const
   }
   __syncthreads();
   const size_t pbase = ((size_t)g * kAttnMaxSplits + s) * G;
+  // one split: the combine below reduces to O * (1/(l + 1e-12)), written here
+  const bool single = nsplit == 1;
   for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
     const int j = idx / hd, e = idx - j * hd;
     const float* pr = ps + j * cm;
@@ -618,8 +620,10 @@ __device__ __forceinline__ void attn_split(const AttnArgs& A, const int g, const
       a1 = fmaf(pr[t + 1], Vs[(size_t)(t + 1) * hd + e], a1);
     }
     if (t < n) a0 = fmaf(pr[t], Vs[(size_t)t * hd + e], a0);
-    A.part_o[(pbase + j) * hd + e] = a0 + a1;
+    if (single) A.out[((size_t)g * G + j) * hd + e] = (a0 + a1) * (1.0f / (mls[2 * j + 1] + 1e-12f));
+    else A.part_o[(pbase + j) * hd + e] = a0 + a1;
   }
+  if (single) return;
   if (threadIdx.x < G) {
     A.part_ml[(pbase + threadIdx.x) * 2] = mls[2 * threadIdx.x];
     A.part_ml[(pbase + threadIdx.x) * 2 + 1] = mls[2 * threadIdx.x + 1];
