@@ -23,6 +23,7 @@
 #include "megakernel.cuh"
 #include "gemm.cuh"
 #include "batch.cuh"
+#include "tc_gemm.cuh"
 
 using namespace gaje;
 
@@ -1562,12 +1563,26 @@ int gaje_cuda_q4_0_gemv(const gaje_q4_matrix* h, const float* x, float* y, size_
     CK(launch_k(k_gemv<G_PLAIN>, dim3(p.grid), dim3(kGemvThreads), p.smem, s, false, P, L, a));
     return GAJE_OK;
   }
-  // M > 1: every weight word is turned into floats once per CTA for 8 vectors;
-  // the CTA walks the K splits itself (no workspace)
+  if (reinterpret_cast<uintptr_t>(x) & 15u) return set_error(GAJE_ERR_INVALID, "x must be 16-byte aligned");
+  if (M >= 16 && h->m.K % kTcK == 0) {  // tensor cores: 128 rows x 64 or 128 vectors per CTA
+    const unsigned gx = unsigned((h->m.N + kTcRows - 1) / kTcRows);
+    if (M <= 64) {
+      if (int st = smem_optin((const void*)k_q4_gemm_tc<64, EpiStore>, tc_smem_bytes(64))) return st;
+      k_q4_gemm_tc<64, EpiStore><<<dim3(gx, unsigned((M + 63) / 64)), kTcThreads, tc_smem_bytes(64), s>>>(
+          h->m.view(), x, int(M), EpiStore{y, h->m.N}, nullptr);
+    } else {
+      if (int st = smem_optin((const void*)k_q4_gemm_tc<128, EpiStore>, tc_smem_bytes(128))) return st;
+      k_q4_gemm_tc<128, EpiStore><<<dim3(gx, unsigned((M + 127) / 128)), kTcThreads, tc_smem_bytes(128), s>>>(
+          h->m.view(), x, int(M), EpiStore{y, h->m.N}, nullptr);
+    }
+    CK(cudaGetLastError());
+    return GAJE_OK;
+  }
+  // 1 < M < 16: every weight word is turned into floats once per CTA for 8
+  // vectors; the CTA walks the K splits itself (no workspace)
   constexpr int MT = 8;
   const int ctas = (h->m.N + 2 * kSkWarps - 1) / (2 * kSkWarps);
   const size_t smem = skinny_smem_bytes(MT);
-  if (reinterpret_cast<uintptr_t>(x) & 15u) return set_error(GAJE_ERR_INVALID, "x must be 16-byte aligned");
   if (int st = smem_optin((const void*)k_q4_gemm_skinny<MT, false, EpiStore>, smem)) return st;
   k_q4_gemm_skinny<MT, false, EpiStore><<<dim3(ctas, unsigned((M + MT - 1) / MT)), kSkThreads, smem, s>>>(
       h->m.view(), x, int(M), SkNorm{}, SkSplit{}, EpiStore{y, h->m.N});

@@ -50,15 +50,18 @@ def test_dequant_edge_blocks_bit_exact(g, O):
     assert np.array_equal(out.cpu().numpy().view(np.uint32), O.q4_0_dequant(blocks, True).view(np.uint32))
 
 
-def _check_rows(got, ref, W_abs_x):
-    tol = 1e-5 * W_abs_x + 1e-6
+def _check_rows(got, ref, W_abs_x, rel=1e-5):
+    tol = rel * W_abs_x + 1e-6
     bad = np.abs(got - ref) > tol
     assert not bad.any(), f"{bad.sum()} rows off, worst {np.max(np.abs(got - ref) - tol)}"
 
 
 @pytest.mark.parametrize("N,K", SWEEP)
-@pytest.mark.parametrize("M", [1, 3, 8, 17])
+@pytest.mark.parametrize("M", [1, 3, 8, 15, 16, 17, 64, 100, 130])
 def test_q4_gemv_matches_oracle(g, O, N, K, M):
+    """M < 16: CUDA-core kernels (f32 products).  M >= 16: the tcgen05
+    kernel, whose bf16 hi/lo splits of w and x carry each product to within
+    3 * 2^-18 (< 1.2e-5) of its f32 value, hence the 2e-5 bound there."""
     W, blocks = _q4(O, N, K, 7 * N + K)
     rng = np.random.default_rng(M)
     X = rng.standard_normal((M, K)).astype(np.float32)
@@ -71,7 +74,7 @@ def test_q4_gemv_matches_oracle(g, O, N, K, M):
     deq = np.abs(O.q4_0_dequant(blocks, True).reshape(N, K))
     for i in range(M):
         ref = O.q4_0_gemv(blocks, X[i], N, K, bias=bias)
-        _check_rows(got[i], ref, deq @ np.abs(X[i]))
+        _check_rows(got[i], ref, deq @ np.abs(X[i]), 2e-5 if M >= 16 else 1e-5)
 
 
 def test_q4_gemv_reference_linear_kat(g, O):
