@@ -391,16 +391,24 @@ def run_sweep(args) -> None:
             flops = 2.0 * M * N * K
             gbs, tfl = nbytes / t / 1e9, flops / t / 1e12
             bound = "hbm" if M <= 8 else "tensor"
+            tc = M >= 16 and K % 64 == 0
+            # the tensor-core kernel issues three bf16 MMAs per product (hi*hi, hi*lo, lo*hi):
+            # its ceiling in useful TFLOP/s is a third of the measured bf16 peak
+            tpeak = peaks.get("bf16_tflops", 1.0) / (3.0 if tc else 1.0)
             line = {"metric": "q4_0 dequant-GEMV/GEMM", "config": {"workload": "configs[2] sweep", "M": M, "N": N,
                                                                  "K": K, "l2": "flushed (256 MB write) before each launch"},
                     "us": round(t * 1e6, 2), "gbs": round(gbs, 1), "tflops": round(tfl, 3),
-                    "kernel": "k_gemv<G_PLAIN>" if M == 1 else "k_q4_gemm_skinny<8> (CUDA cores)",
+                    "kernel": ("k_gemv<G_PLAIN>" if M == 1 else
+                               "k_q4_gemm_tc (tcgen05, bf16 hi/lo x3)" if tc else "k_q4_gemm_skinny<8> (CUDA cores)"),
                     "roofline": {"bound": bound,
                                  "achieved": round(gbs if bound == "hbm" else tfl, 3),
-                                 "peak": peaks["hbm_gbs"] if bound == "hbm" else peaks.get("bf16_tflops"),
+                                 "peak": round(peaks["hbm_gbs"] if bound == "hbm" else tpeak, 1),
                                  "unit": "GB/s" if bound == "hbm" else "TFLOP/s",
-                                 "frac": round(gbs / peaks["hbm_gbs"] if bound == "hbm"
-                                               else tfl / peaks.get("bf16_tflops", 1.0), 4)}}
+                                 "frac": round(gbs / peaks["hbm_gbs"] if bound == "hbm" else tfl / tpeak, 4),
+                                 "peak_source": "measured (MEASURED_PEAKS.json" +
+                                                (" hbm_gbs)" if bound == "hbm" else
+                                                 " bf16_tflops / 3: three MMAs per product)" if tc else
+                                                 " bf16_tflops)")}}
             print(json.dumps(line), flush=True)
         del mat
 

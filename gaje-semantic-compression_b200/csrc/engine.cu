@@ -668,6 +668,75 @@ bool plan_mega(gaje_model* m) {
 
 
 int batch_lm_mb(int B) { return B <= 8 ? 8 : 16; }
+// ---- tensor-core GEMM launches (k_tc_split + k_q4_gemm_tc)
+
+// The work split of one tensor-core GEMM: vectors per CTA (the MMA's N), the
+// padded vector count, and K split across CTAs when the row x vector tiles
+// alone would leave SMs idle (every CTA keeps at least two 64-K stages).
+struct TcPlan {
+  int nt = 0, mpad = 0, z = 1;
+  dim3 grid;
+  size_t part_floats = 0, tiles = 0;
+};
+TcPlan tc_plan(int N, int K, int M, int sms) {
+  TcPlan p;
+  p.nt = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : M <= 128 ? 128 : 256;
+  p.mpad = (M + p.nt - 1) / p.nt * p.nt;
+  const int gx = (N + kTcRows - 1) / kTcRows, gy = p.mpad / p.nt, nkt = K / kTcK;
+  const int want = sms / std::max(1, gx * gy);
+  p.z = std::max(1, std::min(want, nkt / 2));
+  p.grid = dim3(unsigned(gx), unsigned(gy), unsigned(p.z));
+  p.part_floats = p.z > 1 ? size_t(p.z) * M * N : 0;
+  p.tiles = size_t(gx) * gy;
+  return p;
+}
+struct TcBuffers {
+  unsigned char* hi = nullptr;  // split activation planes, tc_plane_bytes(mpad, K) each
+  unsigned char* lo = nullptr;
+  float* part = nullptr;        // z * M * N floats when z > 1
+};
+struct TcNorm {  // the RMSNorm fused into the split (w == nullptr: none)
+  const float* w = nullptr;
+  float eps = 0.f;
+  DevState* st = nullptr;
+  const unsigned* pos = nullptr;
+  int layer = 0;
+};
+
+template <int NT, class WS, class Epi>
+cudaError_t tc_launch_nt(const TcPlan& p, const WS& W, int M, Epi epi, const TcBuffers& b, cudaStream_t s, bool pdl,
+                         DevState* st) {
+  if (smem_optin((const void*)k_q4_gemm_tc<NT, WS, Epi>, tc_smem_bytes(NT))) return cudaErrorInvalidValue;
+  return launch_k(k_q4_gemm_tc<NT, WS, Epi>, p.grid, dim3(kTcThreads), tc_smem_bytes(NT), s, pdl, W,
+                  (const unsigned char*)b.hi, (const unsigned char*)b.lo, M, p.mpad, TcSplit{b.part}, epi, st);
+}
+
+// x [M][K] f32 -> split planes (RMSNorm'd when nm.w) -> y through `epi`;
+// every kernel on stream s (the first a programmatic dependent launch when
+// pdl).  WS: Q4Rows or F32Rows.
+template <class WS, class Epi>
+int tc_gemm_run(const TcPlan& p, const WS& W, const float* x, int M, Epi epi, const TcBuffers& b, cudaStream_t s,
+                bool pdl, const TcNorm& nm, DevState* st = nullptr) {
+  TcSplitArgs sa{x, M, W.K(), p.mpad, nm.w, nm.eps, b.hi, b.lo, nm.st, nm.pos, nm.layer};
+  cudaError_t e = launch_k(k_tc_split, dim3(unsigned((p.mpad + 3) / 4)), dim3(128), 0, s, pdl, sa);
+  if (e == cudaSuccess) {
+    switch (p.nt) {
+      case 16: e = tc_launch_nt<16>(p, W, M, epi, b, s, true, st); break;
+      case 32: e = tc_launch_nt<32>(p, W, M, epi, b, s, true, st); break;
+      case 64: e = tc_launch_nt<64>(p, W, M, epi, b, s, true, st); break;
+      case 128: e = tc_launch_nt<128>(p, W, M, epi, b, s, true, st); break;
+      default: e = tc_launch_nt<256>(p, W, M, epi, b, s, true, st); break;
+    }
+  }
+  if (e == cudaSuccess && p.z > 1) {
+    const long items = long(M) * ((W.N() + 1) / 2);
+    e = launch_k(k_tc_reduce<Epi>, dim3(unsigned((items + 255) / 256)), dim3(256), 0, s, true,
+                 (const float*)b.part, p.z, M, W.N(), W.bias(), epi);
+  }
+  if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  return GAJE_OK;
+}
+
 size_t batch_attn_smem(const gaje_model* m) {
   return attn_smem_bytes(m->nh / m->nkv, m->hd, attn_chunk_max(m->max_ctx));
 }
@@ -1452,6 +1521,7 @@ struct OpWorkspace {
   size_t size = 0;
 };
 OpWorkspace g_ws[64];
+OpWorkspace g_ws_tc[64];  // the tensor-core GEMM op: [split-K partials][split planes]
 // layout: [DevState][argmax partials, kWsArgmaxParts x u64][argmax counter]
 //         then, from kWsAttnBase: [attention counters][part_ml][part_o]
 constexpr size_t kWsArgmaxParts = 4096;
@@ -1459,9 +1529,9 @@ constexpr size_t kWsPartsOff = 256;
 constexpr size_t kWsCntOff = kWsPartsOff + kWsArgmaxParts * 8;
 constexpr size_t kWsAttnBase = kWsCntOff + 4096;
 
-int ws_get(int dev, size_t bytes, char** out) {
+int ws_get(int dev, size_t bytes, char** out, OpWorkspace* pool = g_ws) {
   if (dev < 0 || dev >= 64) return set_error(GAJE_ERR_INVALID, "device ordinal out of range");
-  OpWorkspace& w = g_ws[dev];
+  OpWorkspace& w = pool[dev];
   std::lock_guard<std::mutex> lk(w.mu);
   if (w.size < bytes) {
     if (w.mem) {
@@ -1564,19 +1634,17 @@ int gaje_cuda_q4_0_gemv(const gaje_q4_matrix* h, const float* x, float* y, size_
     return GAJE_OK;
   }
   if (reinterpret_cast<uintptr_t>(x) & 15u) return set_error(GAJE_ERR_INVALID, "x must be 16-byte aligned");
-  if (M >= 16 && h->m.K % kTcK == 0) {  // tensor cores: 128 rows x 64 or 128 vectors per CTA
-    const unsigned gx = unsigned((h->m.N + kTcRows - 1) / kTcRows);
-    if (M <= 64) {
-      if (int st = smem_optin((const void*)k_q4_gemm_tc<64, EpiStore>, tc_smem_bytes(64))) return st;
-      k_q4_gemm_tc<64, EpiStore><<<dim3(gx, unsigned((M + 63) / 64)), kTcThreads, tc_smem_bytes(64), s>>>(
-          h->m.view(), x, int(M), EpiStore{y, h->m.N}, nullptr);
-    } else {
-      if (int st = smem_optin((const void*)k_q4_gemm_tc<128, EpiStore>, tc_smem_bytes(128))) return st;
-      k_q4_gemm_tc<128, EpiStore><<<dim3(gx, unsigned((M + 127) / 128)), kTcThreads, tc_smem_bytes(128), s>>>(
-          h->m.view(), x, int(M), EpiStore{y, h->m.N}, nullptr);
-    }
-    CK(cudaGetLastError());
-    return GAJE_OK;
+  if (M >= 16 && h->m.K % kTcK == 0) {  // tensor cores (bf16 hi/lo x3)
+    const TcPlan p = tc_plan(h->m.N, h->m.K, int(M), sm_count(h->device));
+    const size_t part_b = (p.part_floats * 4 + 255) / 256 * 256;
+    const size_t plane = tc_plane_bytes(p.mpad, h->m.K);
+    char* ws;
+    if (int st = ws_get(h->device, part_b + 2 * plane, &ws, g_ws_tc)) return st;
+    TcBuffers tb;
+    tb.part = reinterpret_cast<float*>(ws);
+    tb.hi = reinterpret_cast<unsigned char*>(ws + part_b);
+    tb.lo = tb.hi + plane;
+    return tc_gemm_run(p, Q4Rows{h->m.view()}, x, int(M), EpiStore{y, h->m.N}, tb, s, false, TcNorm{});
   }
   // 1 < M < 16: every weight word is turned into floats once per CTA for 8
   // vectors; the CTA walks the K splits itself (no workspace)

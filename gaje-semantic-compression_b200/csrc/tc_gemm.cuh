@@ -9,20 +9,26 @@
 // into bf16 pairs, v = hi + lo with hi = bf16(v) and lo = bf16(v - hi), and
 // the product is taken as hi_w*hi_x + hi_w*lo_x + lo_w*hi_x (three
 // kind::f16 MMAs into one f32 accumulator): the dropped lo*lo term and the
-// split residues are ~2^-16 of each product, so the sums keep about 16
-// significant bits per product and full f32 accumulation.
+// split residues are below 3 * 2^-18 of each product, and accumulation is f32.
 //
-// CTA tile: 128 weight rows (the MMA's M) x NT vectors (its N), K in stages
-// of 64 (two Q4 blocks), two stages in shared memory.  All 128 threads
-// produce a stage -- thread t dequantises row t's two blocks, and the threads
-// together split the NT x 64 activation tile -- into the K-major
-// no-swizzle canonical layout (8-row x 16-byte core matrices, LBO = 128 B
-// between the two K halves of a core-matrix pair, SBO = 1024 B between
-// 8-row groups); thread 0 issues 4 k-steps x 3 MMAs per stage and commits
-// them to the stage's mbarrier, which the producers wait on before
-// overwriting that stage two stages later.  The f32 accumulator lives in
-// tensor memory (NT columns x 128 lanes); the epilogue reads it with
-// tcgen05.ld (warp w: lanes 32w..32w+31 = its 32 rows).
+// Activations are split once per GEMM by k_tc_split (optionally fused with
+// the RMSNorm that precedes the projection) into a tiled bf16 layout whose
+// (64-K stage, 8-row group) blocks are the MMA's canonical K-major
+// no-swizzle core-matrix layout: 8 rows x 16 bytes per core matrix, the
+// eight 8-element K chunks of a row group 128 B apart (LBO), row groups
+// 1 KB apart (SBO).  A CTA's activation tile for one stage is then one
+// contiguous run per plane, fetched by a 1-D TMA bulk copy.
+//
+// CTA: 128 weight rows (the MMA's M) x NT vectors (its N), S stages of 64 K.
+// Warps 0-7 dequantise one Q4 block each per row and stage (two threads per
+// row; the next stage's words fetched one stage ahead) into the A tiles and
+// arrive on a_full; warp 8 lane 0 issues the activation copies (b_full,
+// transaction bytes) and, once both halves of a stage are in, 4 k-steps x 3
+// MMAs, committed to the stage's `done` barrier, which gates the stage's
+// reuse.  The f32 accumulator is NT columns of tensor memory; warp w reads
+// lane quarter w%4, column half w/4, with tcgen05.ld for the epilogue.  With
+// gridDim.z > 1 the K stages are split across CTAs: partial tiles go to
+// sp.part and k_tc_reduce adds them in split order and runs the epilogue.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -31,19 +37,24 @@
 
 namespace gaje {
 
-constexpr int kTcThreads = 128;
-constexpr int kTcRows = 128;     // weight rows per CTA (MMA M)
-constexpr int kTcK = 64;         // K per stage
-constexpr int kTcStages = 2;
+constexpr int kTcProducers = 256;                 // warps 0-7: two threads per weight row
+constexpr int kTcThreads = kTcProducers + 32;     // + the issue warp
+constexpr int kTcRows = 128;                      // weight rows per CTA (MMA M)
+constexpr int kTcK = 64;                          // K per stage
 constexpr unsigned kTcKidTimeout = 15;
 
 __host__ __device__ constexpr size_t tc_stage_bytes(int nt) {
   return size_t(2) * kTcRows * kTcK * 2 + size_t(2) * nt * kTcK * 2;  // A hi/lo + B hi/lo (bf16)
 }
+__host__ __device__ constexpr int tc_stages(int nt) {
+  return int((200 * 1024) / tc_stage_bytes(nt)) > 4 ? 4 : int((200 * 1024) / tc_stage_bytes(nt));
+}
 __host__ __device__ constexpr size_t tc_smem_bytes(int nt) {
-  return 1024 + kTcStages * tc_stage_bytes(nt);  // 1 KB header (barriers, TMEM address) + stages
+  return 1024 + size_t(tc_stages(nt)) * tc_stage_bytes(nt);  // 1 KB header (barriers, TMEM address)
 }
 __host__ __device__ constexpr int tc_tmem_cols(int nt) { return nt < 32 ? 32 : nt; }
+// Bytes of one bf16 plane of split activations for Mpad rows x K.
+__host__ __device__ inline size_t tc_plane_bytes(int mpad, int K) { return size_t(mpad) * K * 2; }
 
 // Shared-memory matrix descriptor, K-major, no swizzle (version 1 for sm_100):
 // start >> 4 in [0,14), LBO >> 4 in [16,30), SBO >> 4 in [32,46), bit 46 set.
@@ -98,22 +109,167 @@ __device__ __forceinline__ void tc_split8(const float (&v)[8], uint4& hi, uint4&
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-// Byte offset of (row r, 8-element K chunk c) in a K-major no-swizzle tile
-// with 64 K per row: core matrix (r/8, c) at (r/8)*1024 + c*128, row r%8 at +16.
+// Byte offset of (row r, 8-element K chunk c) in a K-major no-swizzle stage
+// tile with 64 K per row: core matrix (r/8, c) at (r/8)*1024 + c*128, row
+// r%8 at +16.
 __device__ __forceinline__ uint32_t tc_off(int r, int c) { return uint32_t((r >> 3) * 1024 + c * 128 + (r & 7) * 16); }
+// Byte offset of (row r, K chunk c) in the split-activation planes of mpad rows:
+// stage c/8, row group r/8, chunk c%8, row r%8.
+__host__ __device__ __forceinline__ size_t tc_xoff(int r, int c, int mpad) {
+  return ((size_t(c >> 3) * (mpad >> 3) + (r >> 3)) * 8 + (c & 7)) * 128 + (r & 7) * 16;
+}
 
-// Launch: grid (ceil(N/128), ceil(M/NT)), kTcThreads, tc_smem_bytes(NT);
-// K % 64 == 0; x rows 16-byte aligned.  `st` receives a timeout code.
-template <int NT, class Epi>
-__global__ void __launch_bounds__(kTcThreads) k_q4_gemm_tc(Q4View W, const float* x, int M, Epi epi, DevState* st) {
+// Weight sources of the A operand: a thread owns 32 consecutive elements
+// (one Q4 block) of one row per stage; `load` fetches their raw words into
+// registers, `values` gives the 8 floats of chunk w (0..3) from them.
+struct Q4Rows {  // Q4_0: w = fma(q, scale, min) (genomic.rs:267-336)
+  Q4View W;
+  struct Regs {
+    uint4 q;
+    uint32_t s;
+  };
+  __host__ __device__ __forceinline__ int N() const { return W.N; }
+  __host__ __device__ __forceinline__ int K() const { return W.K; }
+  __host__ __device__ __forceinline__ const float* bias() const { return W.bias; }
+  __device__ __forceinline__ void load(Regs& g, int r, int blk) const {
+    g.q = __ldg(W.qs + (size_t)r * W.nb + blk);
+    g.s = __ldg(W.sm + (size_t)r * W.nbp + blk);
+  }
+  __device__ __forceinline__ void zero(Regs& g) const {
+    g.q = make_uint4(0u, 0u, 0u, 0u);
+    g.s = 0u;
+  }
+  __device__ __forceinline__ void values(const Regs& g, int w, float (&v)[8]) const {
+    float sc, mn;
+    unpack_sm(g.s, sc, mn);
+    const uint32_t wd = w == 0 ? g.q.x : w == 1 ? g.q.y : w == 2 ? g.q.z : g.q.w;
+#pragma unroll
+    for (int e = 0; e < 8; ++e)  // exact q: the nibble in the mantissa of 2^23, minus 2^23
+      v[e] = fmaf(__uint_as_float(((wd >> (4 * e)) & 0xFu) | 0x4B000000u) - 8388608.0f, sc, mn);
+  }
+};
+struct F32Rows {  // plain f32 rows [N][K] (the lm_head, linear/forward.rs:20-32)
+  const float* W;
+  const float* b;
+  int n, k;
+  struct Regs {
+    float4 f[8];
+  };
+  __host__ __device__ __forceinline__ int N() const { return n; }
+  __host__ __device__ __forceinline__ int K() const { return k; }
+  __host__ __device__ __forceinline__ const float* bias() const { return b; }
+  __device__ __forceinline__ void load(Regs& g, int r, int blk) const {
+    const float4* p = reinterpret_cast<const float4*>(W + (size_t)r * k + blk * 32);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) g.f[i] = __ldcs(p + i);
+  }
+  __device__ __forceinline__ void zero(Regs& g) const {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) g.f[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __device__ __forceinline__ void values(const Regs& g, int w, float (&v)[8]) const {
+    const float4 a = g.f[2 * w], c = g.f[2 * w + 1];
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+  }
+};
+
+// x [M][K] f32 (optionally RMSNorm'd: (x * inv) * w, norm.rs:17-87) -> the
+// split planes hi/lo [mpad rows]; rows M..mpad-1 are zero.  One warp per row;
+// launch ceil(mpad/4) CTAs of 128 threads.  With st, the block-input and
+// normed-output NaN guards (block/forward.rs:11-13, :22-24) at pos[row].
+struct TcSplitArgs {
+  const float* x;
+  int M, K, mpad;
+  const float* norm_w;  // nullptr: no norm
+  float eps;
+  unsigned char* hi;
+  unsigned char* lo;
+  DevState* st;
+  const unsigned* pos;
+  int layer;
+};
+__global__ void __launch_bounds__(128) k_tc_split(TcSplitArgs A) {
+  pdl_wait();
+  pdl_trigger();
+  const int lane = threadIdx.x & 31;
+  const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (r >= A.mpad) return;
+  const bool live = r < A.M;
+  const float* xr = A.x + (size_t)min(r, A.M - 1) * A.K;
+  float inv = 1.f;
+  if (A.norm_w && live) {
+    float ss = 0.f;
+    int bad = 0;
+    for (int j = lane; j < (A.K >> 2); j += 32) {
+      const float4 v = __ldg(reinterpret_cast<const float4*>(xr) + j);
+      ss = fmaf(v.x, v.x, ss);
+      ss = fmaf(v.y, v.y, ss);
+      ss = fmaf(v.z, v.z, ss);
+      ss = fmaf(v.w, v.w, ss);
+      bad |= (v.x != v.x) | (v.y != v.y) | (v.z != v.z) | (v.w != v.w);
+    }
+    ss = warp_sum(ss);
+    inv = 1.0f / sqrtf(ss / (float)A.K + A.eps);
+    if (A.st && __any_sync(0xffffffffu, bad) && lane == 0) nan_flag(A.st, A.pos[r], A.layer, kNanInput);
+  }
+  int bad_out = 0;
+  for (int c = lane; c < (A.K >> 3); c += 32) {
+    float v[8];
+    if (live) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(xr + c * 8));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(xr + c * 8) + 1);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+      v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      if (A.norm_w) {
+        const float4 wa = __ldg(reinterpret_cast<const float4*>(A.norm_w + c * 8));
+        const float4 wb = __ldg(reinterpret_cast<const float4*>(A.norm_w + c * 8) + 1);
+        const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v[i] = (v[i] * inv) * w[i];
+          bad_out |= (v[i] != v[i]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    }
+    uint4 hi, lo;
+    tc_split8(v, hi, lo);
+    const size_t off = tc_xoff(r, c, A.mpad);
+    *reinterpret_cast<uint4*>(A.hi + off) = hi;
+    *reinterpret_cast<uint4*>(A.lo + off) = lo;
+  }
+  if (A.st && A.norm_w && live && __any_sync(0xffffffffu, bad_out) && lane == 0)
+    nan_flag(A.st, A.pos[r], A.layer, kNanAttnNorm);
+}
+
+// Split-K work area: part[z][M][N] f32 partial tiles, finished by k_tc_reduce.
+struct TcSplit {
+  float* part = nullptr;
+};
+
+// Launch: grid (ceil(N/128), mpad/NT, Z), kTcThreads, tc_smem_bytes(NT);
+// K % 64 == 0; the K stages are divided evenly over Z (Z > 1 needs sp).
+template <int NT, class WS, class Epi>
+__global__ void __launch_bounds__(kTcThreads) k_q4_gemm_tc(WS W, const unsigned char* xhi,
+                                                           const unsigned char* xlo, int M, int mpad, TcSplit sp,
+                                                           Epi epi, DevState* st) {
   static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "MMA N");
+  constexpr int S = tc_stages(NT);
   extern __shared__ __align__(1024) unsigned char tc_smem[];
-  uint64_t* done = reinterpret_cast<uint64_t*>(tc_smem);        // [kTcStages] MMA-complete barriers
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tc_smem + 64);
+  uint64_t* a_full = reinterpret_cast<uint64_t*>(tc_smem);  // [S] 128 producer arrivals
+  uint64_t* b_full = a_full + S;                             // [S] activation copies landed
+  uint64_t* done = b_full + S;                               // [S] MMAs of the stage complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tc_smem + 512);
   unsigned char* stage0 = tc_smem + 1024;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int row0 = blockIdx.x * kTcRows, m0 = blockIdx.y * NT;
-  const int nk = W.K / kTcK;
+  const int nkt = W.K() / kTcK;
+  const int Z = gridDim.z;
+  const int kb = (nkt * (int)blockIdx.z) / Z, ke = (nkt * ((int)blockIdx.z + 1)) / Z;
+  const int n = ke - kb;  // stages of this CTA
   constexpr uint32_t kA = kTcRows * kTcK * 2, kB = NT * kTcK * 2;  // bytes of one bf16 plane
   constexpr int kCols = tc_tmem_cols(NT);
   if (wid == 0) {
@@ -122,119 +278,170 @@ __global__ void __launch_bounds__(kTcThreads) k_q4_gemm_tc(Q4View W, const float
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   if (tid == 0) {
-    for (int s = 0; s < kTcStages; ++s) mbar_init(done + s, 1);
+    for (int s = 0; s < S; ++s) {
+      mbar_init(a_full + s, kTcProducers);
+      mbar_init(b_full + s, 1);
+      mbar_init(done + s, 1);
+    }
     fence_mbar_init();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  pdl_wait();
-  pdl_trigger();
-  const int r = row0 + tid;  // this thread's weight row
-  const bool rok = r < W.N;
-  const uint4* qrow = W.qs + (size_t)min(r, W.N - 1) * W.nb;
-  const uint32_t* srow = W.sm + (size_t)min(r, W.N - 1) * W.nbp;
-  constexpr uint32_t idesc = tc_idesc(kTcRows, NT);
   bool ok = true;
-  for (int kt = 0; kt < nk; ++kt) {
-    const int s = kt & 1;
-    unsigned char* A_hi = stage0 + s * tc_stage_bytes(NT);
-    unsigned char* A_lo = A_hi + kA;
-    unsigned char* B_hi = A_lo + kA;
-    unsigned char* B_lo = B_hi + kB;
-    if (kt >= kTcStages && ok) ok = mbar_wait(done + s, ((kt - kTcStages) >> 1) & 1);  // MMAs of kt-2 done
-    // A: row r, blocks 2kt and 2kt+1 -> w = fma(q, scale, min) -> (hi, lo)
+  int issued = 0, committed = -1;  // the issue lane's copies and last commit (for the drain)
+  if (wid < kTcProducers / 32) {
+    // ---------------- A producers: thread t = weight row row0 + t/2, block half t&1 of each stage
+    const int rl = tid >> 1, h = tid & 1;
+    const int r = row0 + rl;
+    const bool rok = r < W.N();
+    typename WS::Regs g;
+    W.zero(g);
+    if (rok && n > 0) W.load(g, r, 2 * kb + h);  // weights never depend on the previous kernel
+    pdl_wait();
+    pdl_trigger();
+    for (int i = 0; i < n; ++i) {
+      const int s = i % S;
+      unsigned char* A_hi = stage0 + s * tc_stage_bytes(NT);
+      unsigned char* A_lo = A_hi + kA;
+      if (i >= S && ok) ok = mbar_wait(done + s, ((i / S) - 1) & 1);  // the stage's previous MMAs are done
+      const typename WS::Regs gc = g;
+      if (i + 1 < n && rok) W.load(g, r, 2 * (kb + i + 1) + h);  // the next stage's words, one stage ahead
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int b = 2 * kt + h;
-      uint4 q = make_uint4(0u, 0u, 0u, 0u);
-      uint32_t smv = 0u;
-      if (rok) {
-        q = __ldg(qrow + b);
-        smv = __ldg(srow + b);
-      }
-      float sc, mn;
-      unpack_sm(smv, sc, mn);
-      const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {  // word w = elements 8w..8w+7 of the block = chunk 4h + w
+      for (int w = 0; w < 4; ++w) {  // chunk w of the thread's 32 elements = stage chunk 4h + w
         float v[8];
-#pragma unroll
-        for (int n = 0; n < 8; ++n) v[n] = fmaf(float((wd[w] >> (4 * n)) & 0xFu), sc, mn);
+        W.values(gc, w, v);
         uint4 hi, lo;
         tc_split8(v, hi, lo);
-        const uint32_t off = tc_off(tid, 4 * h + w);
+        const uint32_t off = tc_off(rl, 4 * h + w);
         *reinterpret_cast<uint4*>(A_hi + off) = hi;
         *reinterpret_cast<uint4*>(A_lo + off) = lo;
       }
+      fence_async_smem();  // these generic-proxy writes, visible to the tensor cores
+      mbar_arrive(a_full + s);
     }
-    // B: NT vectors x 8 chunks of 8 floats
-    for (int it = tid; it < NT * 8; it += kTcThreads) {
-      const int vr = it >> 3, c = it & 7;
-      float v[8];
-      if (m0 + vr < M) {
-        const float4* src = reinterpret_cast<const float4*>(x + (size_t)(m0 + vr) * W.K + kt * kTcK + c * 8);
-        const float4 a = __ldg(src), bq = __ldg(src + 1);
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-        v[4] = bq.x; v[5] = bq.y; v[6] = bq.z; v[7] = bq.w;
-      } else {
+  } else {
+    // ---------------- issue warp: activation copies and the MMAs
+    pdl_wait();
+    pdl_trigger();
+    if (lane == 0) {
+      const size_t gstride = tc_plane_bytes(mpad, kTcK);  // bytes of one 64-K stage of a plane
+      auto load = [&](int j) {
+        const int s = j % S;
+        unsigned char* B_hi = stage0 + s * tc_stage_bytes(NT) + 2 * kA;
+        const size_t src = size_t(kb + j) * gstride + size_t(m0 >> 3) * 1024;
+        mbar_expect_tx(b_full + s, 2 * kB);
+        bulk_g2s(B_hi, xhi + src, kB, b_full + s);
+        bulk_g2s(B_hi + kB, xlo + src, kB, b_full + s);
+        issued = j + 1;
+      };
+      for (int j = 0; j < n && j < S; ++j) load(j);
+      constexpr uint32_t idesc = tc_idesc(kTcRows, NT);
+      for (int i = 0; i < n && ok; ++i) {
+        const int s = i % S;
+        const uint32_t ph = (i / S) & 1;
+        ok = mbar_wait(b_full + s, ph) && mbar_wait(a_full + s, ph);
+        if (!ok) break;
+        tc_fence_after();
+        unsigned char* A_hi = stage0 + s * tc_stage_bytes(NT);
+        const uint32_t ah = smem_u32(A_hi), al = ah + kA, bh = al + kA, bl = bh + kB;
 #pragma unroll
-        for (int n = 0; n < 8; ++n) v[n] = 0.f;
+        for (int k = 0; k < kTcK / 16; ++k) {  // a 16-wide k-step spans two core matrices: +256 B
+          const uint32_t o = uint32_t(k) * 256u;
+          const uint64_t dah = tc_desc(ah + o, 128, 1024), dal = tc_desc(al + o, 128, 1024);
+          const uint64_t dbh = tc_desc(bh + o, 128, 1024), dbl = tc_desc(bl + o, 128, 1024);
+          tc_mma(tmem, dah, dbh, idesc, (i > 0 || k > 0) ? 1u : 0u);
+          tc_mma(tmem, dah, dbl, idesc, 1u);
+          tc_mma(tmem, dal, dbh, idesc, 1u);
+        }
+        tc_commit(done + s);
+        committed = i;
+        // refill the stage used one step back once its MMAs are through
+        if (i >= 1 && i - 1 + S < n) {
+          const int sp_ = (i - 1) % S;
+          if (!(ok = mbar_wait(done + sp_, ((i - 1) / S) & 1))) break;
+          load(i - 1 + S);
+        }
       }
-      uint4 hi, lo;
-      tc_split8(v, hi, lo);
-      const uint32_t off = tc_off(vr, c);
-      *reinterpret_cast<uint4*>(B_hi + off) = hi;
-      *reinterpret_cast<uint4*>(B_lo + off) = lo;
-    }
-    fence_async_smem();  // the generic-proxy writes above, visible to the tensor cores
-    tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && ok) {
-      tc_fence_after();
-      const uint32_t ah = smem_u32(A_hi), al = smem_u32(A_lo), bh = smem_u32(B_hi), bl = smem_u32(B_lo);
-#pragma unroll
-      for (int k = 0; k < kTcK / 16; ++k) {  // a 16-wide k-step spans two core matrices: +256 B
-        const uint32_t o = uint32_t(k) * 256u;
-        const uint64_t dah = tc_desc(ah + o, 128, 1024), dal = tc_desc(al + o, 128, 1024);
-        const uint64_t dbh = tc_desc(bh + o, 128, 1024), dbl = tc_desc(bl + o, 128, 1024);
-        tc_mma(tmem, dah, dbh, idesc, (kt > 0 || k > 0) ? 1u : 0u);
-        tc_mma(tmem, dah, dbl, idesc, 1u);
-        tc_mma(tmem, dal, dbh, idesc, 1u);
-      }
-      tc_commit(done + s);
     }
   }
   // the last commit covers every MMA issued before it
-  if (ok && nk > 0) ok = mbar_wait(done + ((nk - 1) & 1), ((nk - 1) >> 1) & 1);
+  constexpr int kIssueWarp = kTcProducers / 32;
+  if (wid < kIssueWarp && n > 0) {
+    const bool fin = mbar_wait(done + (n - 1) % S, ((n - 1) / S) & 1);
+    ok = ok && fin;
+  }
+  ok = __syncthreads_and(ok) != 0;
   if (!ok) {
     if (tid == 0 && st) flag_timeout(st, kTcKidTimeout);
-    // let any MMA still in flight finish before the tensor memory is freed (bounded again)
-    if (nk > 0) mbar_wait(done + ((nk - 1) & 1), ((nk - 1) >> 1) & 1);
+    // nothing may still write shared or tensor memory when they are released:
+    // wait (bounded again) for the last MMAs and every stage's latest copy
+    if (wid == kIssueWarp && lane == 0) {
+      if (committed >= 0) mbar_wait(done + committed % S, (committed / S) & 1);
+      for (int s = 0; s < S && s < issued; ++s) {
+        const int j = s + S * ((issued - 1 - s) / S);  // the stage's latest copy
+        mbar_wait(b_full + s, (j / S) & 1);
+      }
+    }
   }
   tc_fence_after();
-  if (ok) {
-    const int rr = row0 + wid * 32 + lane;  // TMEM lane = tile row
-    const bool has0 = rr < W.N;
-    const float bias = (W.bias && has0) ? __ldg(W.bias + rr) : 0.f;
+  if (ok && wid < kIssueWarp) {
+    // warp w reads TMEM lanes 32*(w%4).. (its quarter), columns of half w/4
+    const int q = wid & 3;
+    const int rr = row0 + q * 32 + lane;  // TMEM lane = tile row
+    const int WN = W.N();
+    const bool has0 = rr < WN, has1 = rr + 1 < WN;
+    const float* bp = W.bias();
+    const float bias = (bp && has0) ? __ldg(bp + rr) : 0.f;
     const float bias1 = __shfl_down_sync(0xffffffffu, bias, 1);
-    const bool has1 = rr + 1 < W.N;
+    constexpr int kHalf = NT / 2 < 8 ? 8 : NT / 2;
+    const int cb = (wid >> 2) * kHalf, ce = min(NT, cb + kHalf);
 #pragma unroll 1
-    for (int c0 = 0; c0 < NT; c0 += 8) {
+    for (int c0 = cb; c0 < ce; c0 += 8) {
       float v[8];
-      tc_ld8(tmem + (uint32_t(wid * 32) << 16) + uint32_t(c0), v);
+      tc_ld8(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
+      if (Z > 1) {  // partial tile -> part[z][m][row]
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float f = flush_small(v[j]);
-        const float f1 = __shfl_down_sync(0xffffffffu, f, 1);  // row rr + 1
-        if ((lane & 1) == 0 && has0 && m0 + c0 + j < M) epi(m0 + c0 + j, rr, f + bias, has1, f1 + bias1);
+        for (int j = 0; j < 8; ++j)
+          if (has0 && m0 + c0 + j < M) sp.part[((size_t)blockIdx.z * M + m0 + c0 + j) * WN + rr] = v[j];
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float f = flush_small(v[j]);
+          const float f1 = __shfl_down_sync(0xffffffffu, f, 1);  // row rr + 1
+          if ((lane & 1) == 0 && has0 && m0 + c0 + j < M) epi(m0 + c0 + j, rr, f + bias, has1, f1 + bias1);
+        }
       }
     }
   }
   tc_fence_before();
   __syncthreads();
   if (wid == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(uint32_t(kCols)));
+}
+
+// The split-K finish: y = flush(sum_z part[z][m][row]) + bias through epi,
+// the splits added in order.  One thread per (vector, row pair); launch
+// ceil(M * ceil(N/2) / 256) CTAs of 256 threads.
+template <class Epi>
+__global__ void __launch_bounds__(256) k_tc_reduce(const float* part, int Z, int M, int N, const float* bias,
+                                                   Epi epi) {
+  pdl_wait();
+  pdl_trigger();
+  const int np = (N + 1) >> 1;
+  const long it = (long)blockIdx.x * 256 + threadIdx.x;
+  if (it >= (long)M * np) return;
+  const int m = int(it / np), r0 = 2 * int(it - (long)m * np);
+  const bool has1 = r0 + 1 < N;
+  float s0 = 0.f, s1 = 0.f;
+  for (int z = 0; z < Z; ++z) {
+    const float* p = part + ((size_t)z * M + m) * N + r0;
+    s0 += __ldcg(p);
+    if (has1) s1 += __ldcg(p + 1);
+  }
+  const float b0 = bias ? __ldg(bias + r0) : 0.f;
+  const float b1 = (bias && has1) ? __ldg(bias + r0 + 1) : 0.f;
+  epi(m, r0, flush_small(s0) + b0, has1, flush_small(s1) + b1);
 }
 
 }  // namespace gaje
