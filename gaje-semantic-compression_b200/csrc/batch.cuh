@@ -283,4 +283,27 @@ __global__ void __launch_bounds__(kLbThreads) k_lmhead_batch(LmBatchArgs A) {
   if (tid == 0) *A.cnt = 0u;  // ready for the next launch
 }
 
+// First-max argmax of each row of logits [B][V] (llm/forward.rs:262-271): one
+// CTA of 512 threads per row (the tensor-core lm_head path).
+__global__ void __launch_bounds__(512) k_argmax_rows(const float* logits, int V, unsigned* out) {
+  __shared__ unsigned long long wb[16];
+  pdl_wait();
+  pdl_trigger();
+  const float* row = logits + (size_t)blockIdx.x * V;
+  unsigned long long best = 0ull;
+#pragma unroll 4
+  for (int i = threadIdx.x; i < V; i += 512) {
+    const unsigned long long k = amax_key(__ldcg(row + i), (unsigned)i);
+    best = k > best ? k : best;
+  }
+  best = warp_max_u64(best);
+  if ((threadIdx.x & 31) == 0) wb[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long b = 0ull;
+    for (int w = 0; w < 16; ++w) b = wb[w] > b ? wb[w] : b;
+    out[blockIdx.x] = amax_index(b);
+  }
+}
+
 }  // namespace gaje

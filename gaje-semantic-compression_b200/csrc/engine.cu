@@ -16,6 +16,7 @@
 #include <mutex>
 #include <set>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "flat_format.h"
@@ -60,6 +61,7 @@ struct Q4Dev {
 
 constexpr int kMaxDynSmem = 227 * 1024;
 constexpr int kBatchMT = 8;  // activation vectors per Q4 GEMM CTA of a batched step
+constexpr int kBatchTcMin = 16;  // batch size from which the step's GEMMs run on the tensor cores
 
 // Launch with cudaLaunchKernelEx; `pdl` lets the kernel start before its
 // predecessor finishes (programmatic stream serialization): the kernel itself
@@ -274,6 +276,10 @@ struct gaje_model {
   unsigned* bcnt = nullptr;
   unsigned long long* blm_part = nullptr;
   unsigned* blm_cnt = nullptr;
+  unsigned char* btc_hi = nullptr;  // tensor-core GEMM split activation planes (B >= 16)
+  unsigned char* btc_lo = nullptr;
+  float* btc_part = nullptr;        // tensor-core split-K partials
+  int btc_mpad = 0;                 // rows the planes hold
   float* bsk_part = nullptr;   // Q4 GEMM split partials
   unsigned* bsk_cnt = nullptr; // Q4 GEMM split counters
   size_t bsk_tiles = 0;
@@ -759,6 +765,23 @@ int batch_setup(gaje_model* m) {
   CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&sk_per, k_q4_gemm_skinny<kBatchMT, true, EpiSwigluBatch>,
                                                    kSkThreads, sk));
   m->bsk_per_sm = std::max(1, sk_per);
+  if (m->btc_hi) {  // every tensor-core instantiation a step may launch (never during a capture)
+    int e = 0;
+    auto optin_nt = [&](auto nt_tag) {
+      constexpr int NT = decltype(nt_tag)::value;
+      const size_t b = tc_smem_bytes(NT);
+      e = e ? e : smem_optin((const void*)k_q4_gemm_tc<NT, Q4Rows, EpiQkvBatch>, b);
+      e = e ? e : smem_optin((const void*)k_q4_gemm_tc<NT, Q4Rows, EpiResidBatch>, b);
+      e = e ? e : smem_optin((const void*)k_q4_gemm_tc<NT, Q4Rows, EpiSwigluBatch>, b);
+      e = e ? e : smem_optin((const void*)k_q4_gemm_tc<NT, F32Rows, EpiStore>, b);
+    };
+    optin_nt(std::integral_constant<int, 16>{});
+    optin_nt(std::integral_constant<int, 32>{});
+    optin_nt(std::integral_constant<int, 64>{});
+    optin_nt(std::integral_constant<int, 128>{});
+    optin_nt(std::integral_constant<int, 256>{});
+    if (e) return e;
+  }
   return GAJE_OK;
 }
 
@@ -784,6 +807,24 @@ SkLaunch sk_plan(const gaje_model* m, const Q4Dev& q, int Bi) {
   return r;
 }
 
+// One projection of a batched step: the tensor cores (bf16 hi/lo x3) from
+// kBatchTcMin streams on, else the CUDA-core skinny GEMM.  `norm` is the
+// RMSNorm fused into the activation staging (w == nullptr: none).
+template <bool NORM, class Epi>
+cudaError_t batch_gemm(gaje_model* m, int Bi, const Q4Dev& q, const float* x, const TcNorm& norm, Epi epi) {
+  if (Bi >= kBatchTcMin && m->btc_hi && q.K % kTcK == 0) {
+    const TcPlan p = tc_plan(q.N, q.K, Bi, m->sms);
+    TcBuffers b{m->btc_hi, m->btc_lo, m->btc_part};
+    return tc_gemm_run(p, Q4Rows{q.view()}, x, Bi, epi, b, m->stream, true, norm, m->st) == GAJE_OK
+               ? cudaSuccess
+               : cudaErrorLaunchFailure;
+  }
+  SkNorm sn{norm.w, norm.eps, norm.st, norm.pos, norm.layer};
+  SkLaunch pl = sk_plan(m, q, Bi);
+  return launch_k(k_q4_gemm_skinny<kBatchMT, NORM, Epi>, pl.grid, dim3(kSkThreads), skinny_smem_bytes(kBatchMT),
+                  m->stream, true, q.view(), x, Bi, sn, pl.sp, epi);
+}
+
 // The kernels of one batched step for the first Bi entries of the stream
 // table (already on the device), in stream order, every launch after the
 // first a programmatic dependent launch.  Nothing here depends on the
@@ -802,30 +843,31 @@ int launch_batch(gaje_model* m, int Bi) {
   cudaError_t e = launch_k(k_embed_batch, dim3(Bi), dim3(256), 0, st, false, (const float*)m->embd, m->V, d, bs,
                            m->bx);
   for (int l = 0; l < L && e == cudaSuccess; ++l) {
-    SkNorm an{m->attn_norm[l], eps, m->st, bs.pos, l};
     EpiQkvBatch eq{m->bq, m->bcache, bs, m->rope, m->nh, m->nkv, m->hd, int(m->info.rope_split), l};
-    SkLaunch pq = sk_plan(m, m->qkv[l], Bi);
-    e = launch_k(k_q4_gemm_skinny<MT, true, EpiQkvBatch>, pq.grid, dim3(kSkThreads), sk, st, true, m->qkv[l].view(),
-                 (const float*)m->bx, Bi, an, pq.sp, eq);
+    e = batch_gemm<true>(m, Bi, m->qkv[l], m->bx, TcNorm{m->attn_norm[l], eps, m->st, bs.pos, l}, eq);
     if (e != cudaSuccess) break;
     AttnBatchArgs aa{m->bq, m->battn, m->bcache, bs, m->bpart_o, m->bpart_ml, m->bcnt, l, m->nh,
                      1.0f / sqrtf(float(m->hd))};
     e = launch_k(k_attn_batch, dim3(unsigned(m->nkv), unsigned(ns_max), unsigned(Bi)), dim3(kAttnThreads),
                  batch_attn_smem(m), st, true, aa);
     if (e != cudaSuccess) break;
-    SkLaunch po = sk_plan(m, m->wo[l], Bi);
-    e = launch_k(k_q4_gemm_skinny<MT, false, EpiResidBatch>, po.grid, dim3(kSkThreads), sk, st, true,
-                 m->wo[l].view(), (const float*)m->battn, Bi, SkNorm{}, po.sp, EpiResidBatch{m->bx, d, nullptr, bs, l});
+    e = batch_gemm<false>(m, Bi, m->wo[l], m->battn, TcNorm{}, EpiResidBatch{m->bx, d, nullptr, bs, l});
     if (e != cudaSuccess) break;
-    SkNorm fn{m->ffn_norm[l], eps, nullptr, bs.pos, l};
-    SkLaunch pg = sk_plan(m, m->gate_up[l], Bi);
-    e = launch_k(k_q4_gemm_skinny<MT, true, EpiSwigluBatch>, pg.grid, dim3(kSkThreads), sk, st, true,
-                 m->gate_up[l].view(), (const float*)m->bx, Bi, fn, pg.sp,
-                 EpiSwigluBatch{m->bact, m->ff, m->st, bs, l});
+    e = batch_gemm<true>(m, Bi, m->gate_up[l], m->bx, TcNorm{m->ffn_norm[l], eps, nullptr, bs.pos, l},
+                         EpiSwigluBatch{m->bact, m->ff, m->st, bs, l});
     if (e != cudaSuccess) break;
-    SkLaunch pd = sk_plan(m, m->down[l], Bi);
-    e = launch_k(k_q4_gemm_skinny<MT, false, EpiResidBatch>, pd.grid, dim3(kSkThreads), sk, st, true,
-                 m->down[l].view(), (const float*)m->bact, Bi, SkNorm{}, pd.sp, EpiResidBatch{m->bx, d, m->st, bs, l});
+    e = batch_gemm<false>(m, Bi, m->down[l], m->bact, TcNorm{}, EpiResidBatch{m->bx, d, m->st, bs, l});
+  }
+  if (e == cudaSuccess && Bi >= kBatchTcMin && m->btc_hi && d % kTcK == 0) {
+    // output norm fused into the split, f32 lm_head on the tensor cores, then the argmax per stream
+    const TcPlan p = tc_plan(m->V, d, Bi, m->sms);
+    TcBuffers b{m->btc_hi, m->btc_lo, m->btc_part};
+    if (tc_gemm_run(p, F32Rows{m->lm_head, m->lm_bias, m->V, d}, m->bx, Bi, EpiStore{m->blogits, m->V}, b, st, true,
+                    TcNorm{m->out_norm, eps, nullptr, bs.pos, L}, m->st) != GAJE_OK)
+      return set_error(GAJE_ERR_CUDA, "kernel launch: lm_head");
+    e = launch_k(k_argmax_rows, dim3(unsigned(Bi)), dim3(512), 0, st, true, (const float*)m->blogits, m->V, d_argmax);
+    if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+    return GAJE_OK;
   }
   const int MB = batch_lm_mb(Bi);
   for (int b0 = 0; b0 < Bi && e == cudaSuccess; b0 += MB) {
@@ -976,6 +1018,13 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
       m->bsk_part = a.take<float>(std::max<size_t>(part, 1));
       m->bsk_cnt = a.take<unsigned>(tiles);
       m->bsk_tiles = tiles;
+      if (S >= size_t(kBatchTcMin)) {
+        const size_t kmax = std::max({size_t(d), size_t(m->nh) * m->hd, size_t(m->ff)});
+        m->btc_mpad = int((S + 255) / 256 * 256);
+        m->btc_hi = a.take<unsigned char>(tc_plane_bytes(m->btc_mpad, int(kmax)));
+        m->btc_lo = a.take<unsigned char>(tc_plane_bytes(m->btc_mpad, int(kmax)));
+        m->btc_part = a.take<float>(size_t(m->sms) * 256 * kTcRows);  // z * M * N <= SMs * NT * 128
+      }
     }
   };
   Arena sizing;

@@ -109,3 +109,15 @@ def test_batch_argument_errors(g, make_model):
     assert m.stream_len(1) == 0
     m.forward_batch([1], [3])
     assert m.stream_len(1) == 1
+
+
+@pytest.mark.parametrize("name,n_streams", [("smollm2-135m", 20), ("qwen2-0.5b", 16)])
+def test_batch_tensor_core_path(g, O, make_model, name, n_streams):
+    """From 16 streams the step's projections and the lm_head run on the
+    tcgen05 kernels (bf16 hi/lo x3); same bar as the CUDA-core path."""
+    path = make_model(name, seed=1235)
+    V = g.load_genomic_auto(path, max_ctx=8).vocab_size
+    rng = np.random.default_rng(7)
+    schedule = [[(s, int(rng.integers(0, V))) for s in range(n_streams)] for _ in range(3)]
+    schedule += [[(s, None) for s in range(n_streams)] for _ in range(2)]
+    assert _run_schedule(g, O, path, schedule, n_streams, max_ctx=32) <= REL_TOL
