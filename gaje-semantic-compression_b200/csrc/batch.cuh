@@ -34,7 +34,7 @@ struct BatchCache {
   float* k;
   float* v;
   int L, nkv, max_ctx, hd;
-  __device__ __forceinline__ size_t row(unsigned sid, int l, int g, unsigned pos) const {
+  __host__ __device__ __forceinline__ size_t row(unsigned sid, int l, int g, unsigned pos) const {
     return ((((size_t)sid * L + l) * nkv + g) * max_ctx + pos) * hd;
   }
 };
@@ -150,6 +150,163 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_batch(AttnBatchArgs B) {
   a.st = nullptr;
   a.fresh = 1;  // the stream's row at pos is written by the QKV kernel just before
   attn_split(a, blockIdx.x, blockIdx.y);
+}
+
+// Causal attention for a prefill chunk of one stream: rows m = 0..n-1 at
+// positions p0 + m, each attending to its stream's cached positions
+// 0..p0+m (the chunk's own k/v rows are written by the QKV kernel before
+// this one).  attention.rs:88-127 per (row, head): s_t = q.k_t * scale,
+// softmax, out = sum p_t v_t with inv = 1/(sum + 1e-12); here as a
+// flash-style pass over 64-position tiles with a running max and sum (the
+// same values, another rounding order).  CTA: QB consecutive rows x the G
+// query heads of one KV head (QB*G <= 96), K/V tiles in shared memory shared
+// by all of them; 256 threads.
+constexpr int kApThreads = 256;
+constexpr int kApT = 64;  // key positions per tile
+__host__ __device__ inline int attn_prefill_qb(int G) {
+  const int q = 96 / G;
+  return q < 1 ? 1 : q > 16 ? 16 : q;
+}
+__host__ __device__ inline size_t attn_prefill_smem(int G, int hd) {
+  const int qg = attn_prefill_qb(G) * G;
+  return size_t(qg) * hd * 4 * 2                 // Qs, Os
+         + size_t(kApT) * (hd + 4) * 4          // Ks (rows padded by 4 floats)
+         + size_t(kApT) * hd * 4                // Vs
+         + size_t(qg) * kApT * 4                // scores / probabilities
+         + size_t(qg) * 3 * 4;                  // running max, sum, rescale
+}
+struct AttnPrefillArgs {
+  const float* q;   // [n][nh*hd]
+  float* out;       // [n][nh*hd]
+  const float* kc;  // this layer's cache of the stream: [nkv][max_ctx][hd]
+  const float* vc;
+  int n, p0, nh, nkv, hd, max_ctx;
+  float scale;
+};
+__global__ void __launch_bounds__(kApThreads) k_attn_prefill(AttnPrefillArgs A) {
+  extern __shared__ __align__(16) float ap_smem[];
+  const int G = A.nh / A.nkv, hd = A.hd, hd4 = hd >> 2;
+  const int QB = attn_prefill_qb(G), QG = QB * G;
+  const int g = blockIdx.y, m0 = blockIdx.x * QB;
+  float* Qs = ap_smem;                       // [QG][hd]
+  float* Os = Qs + QG * hd;                  // [QG][hd]
+  float* Ks = Os + QG * hd;                  // [64][hd + 4]
+  float* Vs = Ks + kApT * (hd + 4);          // [64][hd]
+  float* Ps = Vs + kApT * hd;                // [QG][64]
+  float* rmax = Ps + QG * kApT;
+  float* rsum = rmax + QG;
+  float* ralpha = rsum + QG;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  pdl_wait();
+  pdl_trigger();
+  // rows qh = (query i, head j): q of head g*G + j of row m0 + i
+  for (int idx = tid; idx < QG * hd4; idx += kApThreads) {
+    const int qh = idx / hd4, e4 = idx - qh * hd4;
+    const int i = qh / G, j = qh - i * G;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (m0 + i < A.n) v = __ldcg(reinterpret_cast<const float4*>(A.q + (size_t)(m0 + i) * A.nh * hd + (g * G + j) * hd) + e4);
+    reinterpret_cast<float4*>(Qs)[idx] = v;
+    reinterpret_cast<float4*>(Os)[idx] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int qh = tid; qh < QG; qh += kApThreads) {
+    rmax[qh] = -INFINITY;
+    rsum[qh] = 0.f;
+  }
+  const int last = min(A.n, m0 + QB) - 1;      // the CTA's last live row
+  const int maxpos = A.p0 + last;              // the farthest position any of its rows sees
+  const float* kbase = A.kc + (size_t)g * A.max_ctx * hd;
+  const float* vbase = A.vc + (size_t)g * A.max_ctx * hd;
+  for (int t0 = 0; t0 <= maxpos; t0 += kApT) {
+    __syncthreads();  // the previous tile is consumed
+    for (int idx = tid; idx < kApT * hd4; idx += kApThreads) {
+      const int j = idx / hd4, e4 = idx - j * hd4;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (t0 + j <= maxpos) {
+        kv = __ldcg(reinterpret_cast<const float4*>(kbase + (size_t)(t0 + j) * hd) + e4);
+        vv = __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)(t0 + j) * hd) + e4);
+      }
+      reinterpret_cast<float4*>(Ks + j * (hd + 4))[e4] = kv;
+      reinterpret_cast<float4*>(Vs)[idx] = vv;
+    }
+    __syncthreads();
+    // scores (masked positions: -inf)
+    for (int idx = tid; idx < QG * kApT; idx += kApThreads) {
+      const int qh = idx >> 6, j = idx & (kApT - 1);
+      const int i = qh / G;
+      float sc = -INFINITY;
+      if (m0 + i <= last && t0 + j <= A.p0 + m0 + i) {
+        const float4* q4 = reinterpret_cast<const float4*>(Qs + qh * hd);
+        const float4* k4 = reinterpret_cast<const float4*>(Ks + j * (hd + 4));
+        float a0 = 0.f, a1 = 0.f;
+        for (int e = 0; e < hd4; ++e) {
+          const float4 a = q4[e], b = k4[e];
+          a0 = fmaf(a.x, b.x, a0);
+          a1 = fmaf(a.y, b.y, a1);
+          a0 = fmaf(a.z, b.z, a0);
+          a1 = fmaf(a.w, b.w, a1);
+        }
+        sc = (a0 + a1) * A.scale;
+      }
+      Ps[idx] = sc;
+    }
+    __syncthreads();
+    // running softmax per row: warp per row, two positions per lane
+    for (int qh = wid; qh < QG; qh += kApThreads / 32) {
+      const float s0 = Ps[qh * kApT + lane], s1 = Ps[qh * kApT + lane + 32];
+      const float mo = rmax[qh];
+      const float mt = warp_max(fmaxf(s0, s1));
+      const float mn = fmaxf(mo, mt);
+      float p0 = 0.f, p1 = 0.f, alpha = 1.f;
+      if (mn > -INFINITY) {  // rows past the chunk see nothing at all
+        p0 = expf(s0 - mn);
+        p1 = expf(s1 - mn);
+        alpha = expf(mo - mn);
+      }
+      Ps[qh * kApT + lane] = p0;
+      Ps[qh * kApT + lane + 32] = p1;
+      const float ps = warp_sum(p0 + p1);
+      if (lane == 0) {
+        rsum[qh] = rsum[qh] * alpha + ps;
+        rmax[qh] = mn;
+        ralpha[qh] = alpha;
+      }
+    }
+    __syncthreads();
+    // O = O * alpha + P V
+    for (int idx = tid; idx < QG * hd4; idx += kApThreads) {
+      const int qh = idx / hd4, e4 = idx - qh * hd4;
+      float4 o = reinterpret_cast<float4*>(Os)[idx];
+      const float al = ralpha[qh];
+      o.x *= al;
+      o.y *= al;
+      o.z *= al;
+      o.w *= al;
+      const float* pr = Ps + qh * kApT;
+      const float4* v4 = reinterpret_cast<const float4*>(Vs) + e4;
+      for (int j = 0; j < kApT; ++j) {
+        const float p = pr[j];
+        const float4 v = v4[j * hd4];
+        o.x = fmaf(p, v.x, o.x);
+        o.y = fmaf(p, v.y, o.y);
+        o.z = fmaf(p, v.z, o.z);
+        o.w = fmaf(p, v.w, o.w);
+      }
+      reinterpret_cast<float4*>(Os)[idx] = o;
+    }
+  }
+  __syncthreads();
+  for (int idx = tid; idx < QG * hd4; idx += kApThreads) {
+    const int qh = idx / hd4, e4 = idx - qh * hd4;
+    const int i = qh / G, j = qh - i * G;
+    if (m0 + i > last) continue;
+    const float inv = 1.0f / (rsum[qh] + 1e-12f);
+    float4 o = reinterpret_cast<const float4*>(Os)[idx];
+    o.x *= inv;
+    o.y *= inv;
+    o.z *= inv;
+    o.w *= inv;
+    reinterpret_cast<float4*>(A.out + (size_t)(m0 + i) * A.nh * hd + (g * G + j) * hd)[e4] = o;
+  }
 }
 
 // Output RMSNorm + f32 lm_head for B vectors (llm/forward.rs:28,44-46,

@@ -288,6 +288,9 @@ struct gaje_model {
   unsigned* h_bdev = nullptr; // pinned staging of the same
   std::vector<uint32_t> bpos; // per-stream cache length (host)
   std::vector<cudaGraphExec_t> bgraphs;  // [max_streams + 1]: the captured step per batch size
+  int pf_rows = 0;                       // rows of one prefill pass (gaje_load_opts.max_prefill)
+  unsigned* pf_tab = nullptr;            // [3][pf_rows]: tokens, positions, stream ids of a prefill chunk
+  unsigned* h_pf_tab = nullptr;          // pinned staging of the same
   int blm_grid = 0;                      // lm_head CTAs of a batched step
 
   ~gaje_model() {
@@ -300,6 +303,7 @@ struct gaje_model {
     if (h_st) cudaFreeHost(h_st);
     if (h_tok) cudaFreeHost(h_tok);
     if (h_bdev) cudaFreeHost(h_bdev);
+    if (h_pf_tab) cudaFreeHost(h_pf_tab);
     if (stream) cudaStreamDestroy(stream);
   }
 
@@ -755,6 +759,8 @@ int batch_setup(gaje_model* m) {
   if (int e = smem_optin((const void*)k_q4_gemm_skinny<kBatchMT, false, EpiResidBatch>, sk)) return e;
   if (int e = smem_optin((const void*)k_q4_gemm_skinny<kBatchMT, true, EpiSwigluBatch>, sk)) return e;
   if (int e = smem_optin((const void*)k_attn_batch, batch_attn_smem(m))) return e;
+  if (m->pf_rows > 0)
+    if (int e = smem_optin((const void*)k_attn_prefill, attn_prefill_smem(m->nh / m->nkv, m->hd))) return e;
   const size_t lm8 = size_t(8) * m->d * 4, lm16 = size_t(16) * m->d * 4;
   if (int e = smem_optin((const void*)k_lmhead_batch<8, 4>, lm8)) return e;
   if (int e = smem_optin((const void*)k_lmhead_batch<16, 2>, lm16)) return e;
@@ -893,6 +899,58 @@ int launch_batch(gaje_model* m, int Bi) {
   return GAJE_OK;
 }
 
+// One prefill chunk of stream `sid`: rows 0..nc-1 of the prefill table (tokens,
+// positions p0.., the stream id) through every block -- whole-chunk GEMMs,
+// the k/v rows written into the stream's cache by the QKV epilogue, then the
+// causal attention pass -- leaving the residual rows in bx.  With `head`,
+// the output norm + lm_head + argmax of the chunk's last row follow.
+int launch_prefill_chunk(gaje_model* m, int nc, int p0, unsigned sid, bool head) {
+  cudaStream_t st = m->stream;
+  const size_t R = size_t(m->pf_rows);
+  BatchStreams bs{m->pf_tab, m->pf_tab + R, m->pf_tab + 2 * R};
+  const int d = m->d, L = m->L, G = m->nh / m->nkv;
+  const float eps = m->info.eps;
+  cudaError_t e = launch_k(k_embed_batch, dim3(unsigned(nc)), dim3(256), 0, st, false, (const float*)m->embd, m->V,
+                           d, bs, m->bx);
+  const int qb = attn_prefill_qb(G);
+  for (int l = 0; l < L && e == cudaSuccess; ++l) {
+    EpiQkvBatch eq{m->bq, m->bcache, bs, m->rope, m->nh, m->nkv, m->hd, int(m->info.rope_split), l};
+    e = batch_gemm<true>(m, nc, m->qkv[l], m->bx, TcNorm{m->attn_norm[l], eps, m->st, bs.pos, l}, eq);
+    if (e != cudaSuccess) break;
+    AttnPrefillArgs ap{m->bq, m->battn, m->bcache.k + m->bcache.row(sid, l, 0, 0),
+                       m->bcache.v + m->bcache.row(sid, l, 0, 0), nc, p0, m->nh, m->nkv, m->hd, m->max_ctx,
+                       1.0f / sqrtf(float(m->hd))};
+    e = launch_k(k_attn_prefill, dim3(unsigned((nc + qb - 1) / qb), unsigned(m->nkv)), dim3(kApThreads),
+                 attn_prefill_smem(G, m->hd), st, true, ap);
+    if (e != cudaSuccess) break;
+    e = batch_gemm<false>(m, nc, m->wo[l], m->battn, TcNorm{}, EpiResidBatch{m->bx, d, nullptr, bs, l});
+    if (e != cudaSuccess) break;
+    e = batch_gemm<true>(m, nc, m->gate_up[l], m->bx, TcNorm{m->ffn_norm[l], eps, nullptr, bs.pos, l},
+                         EpiSwigluBatch{m->bact, m->ff, m->st, bs, l});
+    if (e != cudaSuccess) break;
+    e = batch_gemm<false>(m, nc, m->down[l], m->bact, TcNorm{}, EpiResidBatch{m->bx, d, m->st, bs, l});
+  }
+  if (e == cudaSuccess && head) {
+    LmBatchArgs la{};
+    la.W = m->lm_head;
+    la.bias = m->lm_bias;
+    la.x = m->bx + size_t(nc - 1) * d;
+    la.norm_w = m->out_norm;
+    la.eps = eps;
+    la.logits = m->blogits;
+    la.part = m->blm_part;
+    la.cnt = m->blm_cnt;
+    la.argmax = m->bdev + 3 * size_t(m->max_streams);
+    la.V = m->V;
+    la.d = d;
+    la.B = 1;
+    la.rows_per_cta = (m->V + m->blm_grid - 1) / m->blm_grid;
+    e = launch_k(k_lmhead_batch<8, 4>, dim3(m->blm_grid), dim3(kLbThreads), size_t(8) * d * 4, st, true, la);
+  }
+  if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  return GAJE_OK;
+}
+
 int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   FlatFile f;
   std::string err;
@@ -914,6 +972,10 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   m->max_streams = opts ? int(opts->max_streams) : 0;
   if (m->max_streams < 0 || m->max_streams > 1024)
     return set_error(GAJE_ERR_INVALID, "max_streams above 1024");
+  m->pf_rows = opts ? int(opts->max_prefill) : 0;
+  if (m->pf_rows < 0 || m->pf_rows > 65536) return set_error(GAJE_ERR_INVALID, "max_prefill above 65536");
+  if (m->pf_rows > 0 && m->max_streams == 0)
+    return set_error(GAJE_ERR_INVALID, "max_prefill needs batched streams (max_streams > 0)");
   m->rng.s = opts ? opts->seed : 0;
   if (m->nh / m->nkv > kAttnMaxGroup) return set_error(GAJE_ERR_UNSUPPORTED, "more than 16 query heads per KV head");
   if (m->hd % 4 != 0) return set_error(GAJE_ERR_UNSUPPORTED, "head_dim must be a multiple of 4");
@@ -990,13 +1052,15 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     m->ll.flags = m->ll.tok + 1;
     if (m->max_streams > 0) {
       const size_t S = size_t(m->max_streams), G = size_t(m->nh / m->nkv);
+      const size_t R = std::max(S, size_t(m->pf_rows));  // rows of a batched step or a prefill chunk
       const size_t bc = S * L * size_t(m->nkv) * m->max_ctx * m->hd;
       m->bcache.k = a.take<float>(bc);
       m->bcache.v = a.take<float>(bc);
-      m->bx = a.take<float>(S * d);
-      m->bq = a.take<float>(S * qd);
-      m->battn = a.take<float>(S * qd);
-      m->bact = a.take<float>(S * m->ff);
+      m->bx = a.take<float>(R * d);
+      m->bq = a.take<float>(R * qd);
+      m->battn = a.take<float>(R * qd);
+      m->bact = a.take<float>(R * m->ff);
+      m->pf_tab = a.take<unsigned>(3 * std::max<size_t>(m->pf_rows, 1));
       m->blogits = a.take<float>(S * V);
       m->bpart_o = a.take<float>(S * m->nkv * kAttnMaxSplits * G * m->hd);
       m->bpart_ml = a.take<float>(S * m->nkv * kAttnMaxSplits * G * 2);
@@ -1012,15 +1076,15 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
                                    {size_t(d), size_t(m->ff)}};
       for (const auto& nk : shapes) {
         const size_t ns = (nk[1] + kSkChunk - 1) / kSkChunk;
-        if (ns > 1) part = std::max(part, ns * nk[0] * S);
-        tiles = std::max(tiles, (nk[0] + 2 * kSkWarps - 1) / (2 * kSkWarps) * ((S + kBatchMT - 1) / kBatchMT));
+        if (ns > 1) part = std::max(part, ns * nk[0] * R);
+        tiles = std::max(tiles, (nk[0] + 2 * kSkWarps - 1) / (2 * kSkWarps) * ((R + kBatchMT - 1) / kBatchMT));
       }
       m->bsk_part = a.take<float>(std::max<size_t>(part, 1));
       m->bsk_cnt = a.take<unsigned>(tiles);
       m->bsk_tiles = tiles;
-      if (S >= size_t(kBatchTcMin)) {
+      if (R >= size_t(kBatchTcMin)) {
         const size_t kmax = std::max({size_t(d), size_t(m->nh) * m->hd, size_t(m->ff)});
-        m->btc_mpad = int((S + 255) / 256 * 256);
+        m->btc_mpad = int((R + 255) / 256 * 256);
         m->btc_hi = a.take<unsigned char>(tc_plane_bytes(m->btc_mpad, int(kmax)));
         m->btc_lo = a.take<unsigned char>(tc_plane_bytes(m->btc_mpad, int(kmax)));
         m->btc_part = a.take<float>(size_t(m->sms) * 256 * kTcRows);  // z * M * N <= SMs * NT * 128
@@ -1076,6 +1140,8 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     CK(cudaHostAlloc(&m->h_bdev, size_t(4) * m->max_streams * sizeof(unsigned), cudaHostAllocDefault));
     m->bpos.assign(size_t(m->max_streams), 0u);
     m->bgraphs.assign(size_t(m->max_streams) + 1, nullptr);
+    if (m->pf_rows > 0)
+      CK(cudaHostAlloc(&m->h_pf_tab, size_t(3) * m->pf_rows * sizeof(unsigned), cudaHostAllocDefault));
     if (int s = batch_setup(m)) return s;
   }
   CK(cudaMemsetAsync(m->kcache, 0, L * size_t(m->nkv) * m->max_ctx * m->hd * 4, m->stream));
@@ -1161,6 +1227,7 @@ void gaje_load_opts_init(gaje_load_opts* o) {
   o->use_graph = 1;
   o->use_megakernel = 1;
   o->max_streams = 0;
+  o->max_prefill = 0;
 }
 
 gaje_model* gaje_cuda_load(const char* flat_path, const gaje_load_opts* opts) {
@@ -1304,6 +1371,46 @@ int gaje_cuda_forward_batch(gaje_model* m, const uint32_t* stream_ids, const uin
   for (size_t b = 0; b < B; ++b) m->bpos[stream_ids[b]] += 1u;
   if (argmax_out)
     for (size_t b = 0; b < B; ++b) argmax_out[b] = m->h_bdev[3 * S + b];
+  return m->check_state();
+}
+
+int gaje_cuda_prefill(gaje_model* m, uint32_t stream_id, const uint32_t* tokens, size_t n, uint32_t* argmax_out,
+                      float* logits_out) {
+  if (!m || (n && !tokens)) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  if (n == 0) return GAJE_OK;
+  if (m->pf_rows <= 0)
+    return set_error(GAJE_ERR_INVALID, "the model was loaded without prefill rows (gaje_load_opts.max_prefill)");
+  if (stream_id >= uint32_t(m->max_streams)) return set_error(GAJE_ERR_INVALID, "stream id out of range");
+  if (m->block_k() > 0)
+    return set_error(GAJE_ERR_UNSUPPORTED, "block K-WTA is not implemented on the batched path");
+  if (m->info.use_genomic_norm)
+    return set_error(GAJE_ERR_UNSUPPORTED, "use_genomic_norm is not implemented on the batched path");
+  if (size_t(m->bpos[stream_id]) + n > size_t(m->max_ctx))
+    return set_error(GAJE_ERR_CONTEXT, "KV cache would overflow (max_ctx positions)");
+  CK(cudaSetDevice(m->device));
+  cudaStream_t st = m->stream;
+  const size_t R = size_t(m->pf_rows);
+  for (size_t c0 = 0; c0 < n; c0 += R) {
+    const int nc = int(std::min(R, n - c0));
+    const unsigned p0 = m->bpos[stream_id];
+    if (c0 > 0) CK(cudaStreamSynchronize(st));  // the pinned table is reused by the next chunk
+    for (int i = 0; i < nc; ++i) {
+      m->h_pf_tab[i] = tokens[c0 + size_t(i)];
+      m->h_pf_tab[R + size_t(i)] = p0 + unsigned(i);
+      m->h_pf_tab[2 * R + size_t(i)] = stream_id;
+    }
+    CK(cudaMemcpyAsync(m->pf_tab, m->h_pf_tab, 3 * R * sizeof(unsigned), cudaMemcpyHostToDevice, st));
+    if (int s = launch_prefill_chunk(m, nc, int(p0), stream_id, c0 + size_t(nc) == n)) return s;
+    m->bpos[stream_id] += unsigned(nc);
+  }
+  const size_t S = size_t(m->max_streams);
+  const int kk = m->logits_k();
+  if (logits_out && kk > 0) k_kwta<<<1, kKwtaThreads, 0, st>>>(m->blogits, m->V, kk);
+  CK(cudaMemcpyAsync(m->h_bdev + 3 * S, m->bdev + 3 * S, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+  if (logits_out) CK(cudaMemcpyAsync(logits_out, m->blogits, size_t(m->V) * 4, cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  if (argmax_out) *argmax_out = m->h_bdev[3 * S];
   return m->check_state();
 }
 

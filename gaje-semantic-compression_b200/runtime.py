@@ -87,7 +87,8 @@ class SynthSpec(C.Structure):
 
 class LoadOpts(C.Structure):
     _fields_ = [("device", C.c_int), ("max_ctx", C.c_uint32), ("seed", C.c_uint64),
-                ("use_graph", C.c_int), ("use_megakernel", C.c_int), ("max_streams", C.c_uint32)]
+                ("use_graph", C.c_int), ("use_megakernel", C.c_int), ("max_streams", C.c_uint32),
+                ("max_prefill", C.c_uint32)]
 
 
 class ModelInfo(C.Structure):
@@ -138,6 +139,7 @@ def lib() -> C.CDLL:
         "gaje_cuda_trace_steps": ([vp, u32, sz, vp, sz, vp], i32),
         "gaje_cuda_attention_decode_static": ([vp, vp, vp, sz, sz, sz, sz, sz, vp, vp], i32),
         "gaje_cuda_forward_batch": ([vp, vp, vp, sz, vp, vp], i32),
+        "gaje_cuda_prefill": ([vp, u32, vp, sz, vp, vp], i32),
         "gaje_cuda_clear_stream": ([vp, u32], i32),
         "gaje_cuda_stream_len": ([vp, u32, vp], i32),
         "gaje_cuda_q4_0_upload": ([vp, sz, sz, vp, i32], vp),
@@ -263,12 +265,14 @@ class GenomicLLM:
     """A `.gaje.flat` model resident on one GPU (the reference's RustGenomicLLM)."""
 
     def __init__(self, path: str, device: int = 0, max_ctx: int = 4096, seed: int = 0,
-                 use_graph: bool = True, use_megakernel: bool = True, max_streams: int = 0):
+                 use_graph: bool = True, use_megakernel: bool = True, max_streams: int = 0,
+                 max_prefill: int = 0):
         opts = LoadOpts()
         lib().gaje_load_opts_init(C.byref(opts))
         opts.device, opts.max_ctx, opts.seed, opts.use_graph = device, max_ctx, seed, int(use_graph)
         opts.use_megakernel = int(use_megakernel)
         opts.max_streams = int(max_streams)
+        opts.max_prefill = int(max_prefill)
         self._m = lib().gaje_cuda_load(path.encode(), C.byref(opts))
         if not self._m:
             raise GajeIOError(2, last_error())
@@ -387,6 +391,17 @@ class GenomicLLM:
         _check(lib().gaje_cuda_forward_batch(self._m, _ptr(sids), _ptr(toks), sids.size, _ptr(am),
                                              _ptr(lg) if logits else None))
         return (am, lg) if logits else am
+
+    def prefill(self, stream_id: int, tokens: Sequence[int], logits: bool = False):
+        """The prompt of one batched stream in one pass (whole-prompt GEMMs and
+        a causal attention pass), as len(tokens) consecutive steps would leave
+        its cache: the last token's greedy argmax, and its logits when asked."""
+        toks = np.ascontiguousarray(list(tokens), dtype=np.uint32)
+        am = np.zeros(1, dtype=np.uint32)
+        lg = np.empty(self.vocab_size, dtype=np.float32) if logits else None
+        _check(lib().gaje_cuda_prefill(self._m, int(stream_id), _ptr(toks), toks.size, _ptr(am),
+                                       _ptr(lg) if logits else None))
+        return (int(am[0]), lg) if logits else int(am[0])
 
     def clear_stream(self, stream_id: int) -> None:
         _check(lib().gaje_cuda_clear_stream(self._m, int(stream_id)))

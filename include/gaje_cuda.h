@@ -138,6 +138,7 @@ typedef struct gaje_load_opts {
   int use_megakernel; /* 1 (default): one persistent cooperative kernel runs
                          whole decode steps; 0: one kernel per phase          */
   uint32_t max_streams; /* KV caches for gaje_cuda_forward_batch (0 = none)   */
+  uint32_t max_prefill; /* rows of one gaje_cuda_prefill pass (0 = no prefill) */
 } gaje_load_opts;
 void gaje_load_opts_init(gaje_load_opts* opts);
 
@@ -203,6 +204,17 @@ int gaje_cuda_decode_greedy(gaje_model* model, uint32_t first_token, size_t n_st
  * and its cache). */
 int gaje_cuda_forward_batch(gaje_model* model, const uint32_t* stream_ids, const uint32_t* tokens,
                             size_t B, uint32_t* argmax_out, float* logits_out);
+/* The prompt part of generate_native_core (src/nn/llm/forward.rs:215-241)
+ * for one batched stream: tokens[n] fed at positions len..len+n-1 (len = the
+ * stream's cache length), as n consecutive forward_core steps would, but as
+ * whole-prompt GEMMs on the tensor cores (gaje_load_opts.max_prefill rows at
+ * a time) and a causal attention pass; argmax_out (host, nullable) and
+ * logits_out (host, vocab_size, nullable) receive the last token's results
+ * (logits K-WTA as gaje_cuda_forward_batch).  The stream's cache afterwards
+ * holds the n new positions.  Needs max_prefill > 0; block K-WTA and
+ * use_genomic_norm are GAJE_ERR_UNSUPPORTED; overflow is GAJE_ERR_CONTEXT. */
+int gaje_cuda_prefill(gaje_model* model, uint32_t stream_id, const uint32_t* tokens, size_t n,
+                      uint32_t* argmax_out, float* logits_out);
 /* clear_cache_core for one batched stream. */
 int gaje_cuda_clear_stream(gaje_model* model, uint32_t stream_id);
 /* A batched stream's cache length. */
