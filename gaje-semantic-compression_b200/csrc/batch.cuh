@@ -159,21 +159,23 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_batch(AttnBatchArgs B) {
 // softmax, out = sum p_t v_t with inv = 1/(sum + 1e-12); here as a
 // flash-style pass over 64-position tiles with a running max and sum (the
 // same values, another rounding order).  CTA: QB consecutive rows x the G
-// query heads of one KV head (QB*G <= 96), K/V tiles in shared memory shared
-// by all of them; 256 threads.
+// query heads of one KV head, padded to 96 (row, head) pairs; K/V tiles in
+// shared memory shared by all of them; 256 threads as a 16 x 16 grid, each
+// holding a 6 x 4 block of scores and a 6-pair x (hd/64) float4 block of the
+// output in registers, so every shared-memory load feeds several FMAs.
 constexpr int kApThreads = 256;
-constexpr int kApT = 64;  // key positions per tile
+constexpr int kApT = 64;   // key positions per tile
+constexpr int kApQG = 96;  // (row, head) pairs per CTA, padded
 __host__ __device__ inline int attn_prefill_qb(int G) {
-  const int q = 96 / G;
-  return q < 1 ? 1 : q > 16 ? 16 : q;
+  const int q = kApQG / G;
+  return q < 1 ? 1 : q;
 }
 __host__ __device__ inline size_t attn_prefill_smem(int G, int hd) {
-  const int qg = attn_prefill_qb(G) * G;
-  return size_t(qg) * hd * 4 * 2                 // Qs, Os
-         + size_t(kApT) * (hd + 4) * 4          // Ks (rows padded by 4 floats)
-         + size_t(kApT) * hd * 4                // Vs
-         + size_t(qg) * kApT * 4                // scores / probabilities
-         + size_t(qg) * 3 * 4;                  // running max, sum, rescale
+  return size_t(kApQG) * (hd + 4) * 4    // Qs (rows padded by 4 floats)
+         + size_t(kApT) * (hd + 4) * 4   // Ks
+         + size_t(kApT) * hd * 4         // Vs
+         + size_t(kApQG) * (kApT + 4) * 4  // scores / probabilities
+         + size_t(kApQG) * 3 * 4;        // running max, sum, rescale
 }
 struct AttnPrefillArgs {
   const float* q;   // [n][nh*hd]
@@ -187,33 +189,41 @@ __global__ void __launch_bounds__(kApThreads) k_attn_prefill(AttnPrefillArgs A) 
   extern __shared__ __align__(16) float ap_smem[];
   const int G = A.nh / A.nkv, hd = A.hd, hd4 = hd >> 2;
   const int QB = attn_prefill_qb(G), QG = QB * G;
-  const int g = blockIdx.y, m0 = blockIdx.x * QB;
-  float* Qs = ap_smem;                       // [QG][hd]
-  float* Os = Qs + QG * hd;                  // [QG][hd]
-  float* Ks = Os + QG * hd;                  // [64][hd + 4]
-  float* Vs = Ks + kApT * (hd + 4);          // [64][hd]
-  float* Ps = Vs + kApT * hd;                // [QG][64]
-  float* rmax = Ps + QG * kApT;
-  float* rsum = rmax + QG;
-  float* ralpha = rsum + QG;
+  // the last row blocks (the longest causal spans) are scheduled first
+  const int g = blockIdx.y, m0 = (gridDim.x - 1 - blockIdx.x) * QB;
+  const int qs = hd + 4, ps = kApT + 4;      // padded row strides (floats)
+  float* Qs = ap_smem;                       // [96][hd + 4]
+  float* Ks = Qs + kApQG * qs;               // [64][hd + 4]
+  float* Vs = Ks + kApT * qs;                // [64][hd]
+  float* Ps = Vs + kApT * hd;                // [96][64 + 4]
+  float* rmax = Ps + kApQG * ps;
+  float* rsum = rmax + kApQG;
+  float* ralpha = rsum + kApQG;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int ta = tid >> 4, tb = tid & 15;    // the thread's place in the 16 x 16 grid
   pdl_wait();
   pdl_trigger();
-  // rows qh = (query i, head j): q of head g*G + j of row m0 + i
-  for (int idx = tid; idx < QG * hd4; idx += kApThreads) {
+  const int last = min(A.n, m0 + QB) - 1;    // the CTA's last live row
+  // pairs qh = (row i, head j): q of head g*G + j of row m0 + i; pads are zero
+  for (int idx = tid; idx < kApQG * hd4; idx += kApThreads) {
     const int qh = idx / hd4, e4 = idx - qh * hd4;
     const int i = qh / G, j = qh - i * G;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (m0 + i < A.n) v = __ldcg(reinterpret_cast<const float4*>(A.q + (size_t)(m0 + i) * A.nh * hd + (g * G + j) * hd) + e4);
-    reinterpret_cast<float4*>(Qs)[idx] = v;
-    reinterpret_cast<float4*>(Os)[idx] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (qh < QG && m0 + i <= last)
+      v = __ldcg(reinterpret_cast<const float4*>(A.q + (size_t)(m0 + i) * A.nh * hd + (g * G + j) * hd) + e4);
+    reinterpret_cast<float4*>(Qs + qh * qs)[e4] = v;
   }
-  for (int qh = tid; qh < QG; qh += kApThreads) {
+  for (int qh = tid; qh < kApQG; qh += kApThreads) {
     rmax[qh] = -INFINITY;
     rsum[qh] = 0.f;
   }
-  const int last = min(A.n, m0 + QB) - 1;      // the CTA's last live row
-  const int maxpos = A.p0 + last;              // the farthest position any of its rows sees
+  constexpr int kMaxD = 2;  // float4 columns of the output per thread: hd <= 128
+  float4 o[6][kMaxD];
+#pragma unroll
+  for (int i = 0; i < 6; ++i)
+#pragma unroll
+    for (int k = 0; k < kMaxD; ++k) o[i][k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int maxpos = A.p0 + last;            // the farthest position any of its rows sees
   const float* kbase = A.kc + (size_t)g * A.max_ctx * hd;
   const float* vbase = A.vc + (size_t)g * A.max_ctx * hd;
   for (int t0 = 0; t0 <= maxpos; t0 += kApT) {
@@ -225,87 +235,110 @@ __global__ void __launch_bounds__(kApThreads) k_attn_prefill(AttnPrefillArgs A) 
         kv = __ldcg(reinterpret_cast<const float4*>(kbase + (size_t)(t0 + j) * hd) + e4);
         vv = __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)(t0 + j) * hd) + e4);
       }
-      reinterpret_cast<float4*>(Ks + j * (hd + 4))[e4] = kv;
+      reinterpret_cast<float4*>(Ks + j * qs)[e4] = kv;
       reinterpret_cast<float4*>(Vs)[idx] = vv;
     }
     __syncthreads();
-    // scores (masked positions: -inf)
-    for (int idx = tid; idx < QG * kApT; idx += kApThreads) {
-      const int qh = idx >> 6, j = idx & (kApT - 1);
-      const int i = qh / G;
-      float sc = -INFINITY;
-      if (m0 + i <= last && t0 + j <= A.p0 + m0 + i) {
-        const float4* q4 = reinterpret_cast<const float4*>(Qs + qh * hd);
-        const float4* k4 = reinterpret_cast<const float4*>(Ks + j * (hd + 4));
-        float a0 = 0.f, a1 = 0.f;
-        for (int e = 0; e < hd4; ++e) {
-          const float4 a = q4[e], b = k4[e];
-          a0 = fmaf(a.x, b.x, a0);
-          a1 = fmaf(a.y, b.y, a1);
-          a0 = fmaf(a.z, b.z, a0);
-          a1 = fmaf(a.w, b.w, a1);
+    // scores: pairs ta + 16r (r < 6) x positions tb + 16c (c < 4)
+    {
+      float acc[6][4];
+#pragma unroll
+      for (int r = 0; r < 6; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = 0.f;
+      for (int e4 = 0; e4 < hd4; ++e4) {
+        float4 kq[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) kq[c] = reinterpret_cast<const float4*>(Ks + (tb + 16 * c) * qs)[e4];
+#pragma unroll
+        for (int r = 0; r < 6; ++r) {
+          const float4 a = reinterpret_cast<const float4*>(Qs + (ta + 16 * r) * qs)[e4];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            acc[r][c] = fmaf(a.x, kq[c].x, acc[r][c]);
+            acc[r][c] = fmaf(a.y, kq[c].y, acc[r][c]);
+            acc[r][c] = fmaf(a.z, kq[c].z, acc[r][c]);
+            acc[r][c] = fmaf(a.w, kq[c].w, acc[r][c]);
+          }
         }
-        sc = (a0 + a1) * A.scale;
       }
-      Ps[idx] = sc;
+#pragma unroll
+      for (int r = 0; r < 6; ++r) {
+        const int qh = ta + 16 * r, i = qh / G;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int j = tb + 16 * c;
+          const bool live = qh < QG && m0 + i <= last && t0 + j <= A.p0 + m0 + i;
+          Ps[qh * ps + j] = live ? acc[r][c] * A.scale : -INFINITY;
+        }
+      }
     }
     __syncthreads();
-    // running softmax per row: warp per row, two positions per lane
-    for (int qh = wid; qh < QG; qh += kApThreads / 32) {
-      const float s0 = Ps[qh * kApT + lane], s1 = Ps[qh * kApT + lane + 32];
+    // running softmax per pair: a warp per pair, two positions per lane
+    for (int qh = wid; qh < kApQG; qh += kApThreads / 32) {
+      const float s0 = Ps[qh * ps + lane], s1 = Ps[qh * ps + lane + 32];
       const float mo = rmax[qh];
-      const float mt = warp_max(fmaxf(s0, s1));
-      const float mn = fmaxf(mo, mt);
+      const float mn = fmaxf(mo, warp_max(fmaxf(s0, s1)));
       float p0 = 0.f, p1 = 0.f, alpha = 1.f;
-      if (mn > -INFINITY) {  // rows past the chunk see nothing at all
+      if (mn > -INFINITY) {  // pads and rows past the chunk see nothing at all
         p0 = expf(s0 - mn);
         p1 = expf(s1 - mn);
         alpha = expf(mo - mn);
       }
-      Ps[qh * kApT + lane] = p0;
-      Ps[qh * kApT + lane + 32] = p1;
-      const float ps = warp_sum(p0 + p1);
+      Ps[qh * ps + lane] = p0;
+      Ps[qh * ps + lane + 32] = p1;
+      const float psum = warp_sum(p0 + p1);
       if (lane == 0) {
-        rsum[qh] = rsum[qh] * alpha + ps;
+        rsum[qh] = rsum[qh] * alpha + psum;
         rmax[qh] = mn;
         ralpha[qh] = alpha;
       }
     }
     __syncthreads();
-    // O = O * alpha + P V
-    for (int idx = tid; idx < QG * hd4; idx += kApThreads) {
-      const int qh = idx / hd4, e4 = idx - qh * hd4;
-      float4 o = reinterpret_cast<float4*>(Os)[idx];
-      const float al = ralpha[qh];
-      o.x *= al;
-      o.y *= al;
-      o.z *= al;
-      o.w *= al;
-      const float* pr = Ps + qh * kApT;
-      const float4* v4 = reinterpret_cast<const float4*>(Vs) + e4;
-      for (int j = 0; j < kApT; ++j) {
-        const float p = pr[j];
-        const float4 v = v4[j * hd4];
-        o.x = fmaf(p, v.x, o.x);
-        o.y = fmaf(p, v.y, o.y);
-        o.z = fmaf(p, v.z, o.z);
-        o.w = fmaf(p, v.w, o.w);
+    // O = O * alpha + P V: pairs ta + 16r x float4 columns tb + 16k
+#pragma unroll
+    for (int r = 0; r < 6; ++r) {
+      const float al = ralpha[ta + 16 * r];
+#pragma unroll
+      for (int k = 0; k < kMaxD; ++k) {
+        o[r][k].x *= al;
+        o[r][k].y *= al;
+        o[r][k].z *= al;
+        o[r][k].w *= al;
       }
-      reinterpret_cast<float4*>(Os)[idx] = o;
+    }
+    for (int j = 0; j < kApT; ++j) {
+      float4 v[kMaxD];
+#pragma unroll
+      for (int k = 0; k < kMaxD; ++k)
+        v[k] = (tb + 16 * k < hd4) ? reinterpret_cast<const float4*>(Vs + j * hd)[tb + 16 * k]
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int r = 0; r < 6; ++r) {
+        const float p = Ps[(ta + 16 * r) * ps + j];
+#pragma unroll
+        for (int k = 0; k < kMaxD; ++k) {
+          o[r][k].x = fmaf(p, v[k].x, o[r][k].x);
+          o[r][k].y = fmaf(p, v[k].y, o[r][k].y);
+          o[r][k].z = fmaf(p, v[k].z, o[r][k].z);
+          o[r][k].w = fmaf(p, v[k].w, o[r][k].w);
+        }
+      }
     }
   }
   __syncthreads();
-  for (int idx = tid; idx < QG * hd4; idx += kApThreads) {
-    const int qh = idx / hd4, e4 = idx - qh * hd4;
-    const int i = qh / G, j = qh - i * G;
-    if (m0 + i > last) continue;
+#pragma unroll
+  for (int r = 0; r < 6; ++r) {
+    const int qh = ta + 16 * r, i = qh / G, j = qh - i * G;
+    if (qh >= QG || m0 + i > last) continue;
     const float inv = 1.0f / (rsum[qh] + 1e-12f);
-    float4 o = reinterpret_cast<const float4*>(Os)[idx];
-    o.x *= inv;
-    o.y *= inv;
-    o.z *= inv;
-    o.w *= inv;
-    reinterpret_cast<float4*>(A.out + (size_t)(m0 + i) * A.nh * hd + (g * G + j) * hd)[e4] = o;
+#pragma unroll
+    for (int k = 0; k < kMaxD; ++k) {
+      const int e4 = tb + 16 * k;
+      if (e4 >= hd4) continue;
+      const float4 v = make_float4(o[r][k].x * inv, o[r][k].y * inv, o[r][k].z * inv, o[r][k].w * inv);
+      reinterpret_cast<float4*>(A.out + (size_t)(m0 + i) * A.nh * hd + (g * G + j) * hd)[e4] = v;
+    }
   }
 }
 

@@ -976,6 +976,8 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   if (m->pf_rows < 0 || m->pf_rows > 65536) return set_error(GAJE_ERR_INVALID, "max_prefill above 65536");
   if (m->pf_rows > 0 && m->max_streams == 0)
     return set_error(GAJE_ERR_INVALID, "max_prefill needs batched streams (max_streams > 0)");
+  if (m->pf_rows > 0 && m->hd > 128)
+    return set_error(GAJE_ERR_UNSUPPORTED, "prefill attention supports head_dim up to 128");
   m->rng.s = opts ? opts->seed : 0;
   if (m->nh / m->nkv > kAttnMaxGroup) return set_error(GAJE_ERR_UNSUPPORTED, "more than 16 query heads per KV head");
   if (m->hd % 4 != 0) return set_error(GAJE_ERR_UNSUPPORTED, "head_dim must be a multiple of 4");
