@@ -275,12 +275,18 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> None:
     step_gbs = sb_mean["total"] / (step_ms_dev / 1000.0) / 1e9
     prof_steps = min(K, 64)
     first3 = prefill()
-    mega = True
-    try:
+    engine = int(model.info().megakernel)
+    mega = engine == 1
+    if engine == 2:
+        # the two-exchange persistent kernel is the whole step: one launch for all K steps
+        kernel = "k_decode_fused (persistent, two exchanges per block: every phase of K decode steps)"
+        k_gbs, k_bytes, k_ms = step_gbs, sb_mean["total"], step_ms_dev
+        launches = 1
+        lm_us = 0.0
+        breakdown = {"note": "one launch per K steps; no per-phase stamps in this kernel"}
+        breakdown_unit = "-"
+    elif mega:
         phases = model.profile_phases(first3, prof_steps, detail=True)
-    except ValueError:
-        mega = False
-    if mega:
         # the persistent kernel is the whole step: one launch for all K steps
         kernel = "k_decode_mega (persistent: every phase of K decode steps)"
         k_gbs, k_bytes, k_ms = step_gbs, sb_mean["total"], step_ms_dev
@@ -334,7 +340,8 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> None:
         "roofline": {"bound": "hbm", "kernel": kernel,
                      "achieved": round(k_gbs, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(k_gbs / peaks["hbm_gbs"], 4),
-                     "traffic": _ncu_traffic("k_decode_mega" if mega else "k_lmhead", cfg_key),
+                     "traffic": _ncu_traffic("k_decode_fused" if engine == 2 else "k_decode_mega" if mega else "k_lmhead",
+                                            cfg_key),
                      "algorithmic_bytes": k_bytes, "ms_per_step": round(k_ms, 4),
                      "peak_source": peaks["source"] + " (MEASURED_PEAKS.json hbm_gbs, of measured)"},
         "lm_head_phase": {"us_per_step": round(lm_us, 2), "bytes": lm_bytes,
@@ -413,14 +420,31 @@ def run_sweep(args) -> None:
         del mat
 
 
+def lpt_assign(lengths, world: int):
+    """Streams to ranks, longest prompt first onto the least-loaded rank that
+    still has room (every rank gets len/world streams: the sharded head is
+    collective, so every rank runs the same number of prefills and the same
+    batch size).  Returns one list of stream indices per rank."""
+    per = len(lengths) // world
+    order = sorted(range(len(lengths)), key=lambda i: (-lengths[i], i))
+    load, out = [0] * world, [[] for _ in range(world)]
+    for i in order:
+        r = min((r for r in range(world) if len(out[r]) < per), key=lambda r: (load[r], r))
+        out[r].append(i)
+        load[r] += lengths[i]
+    return out
+
+
 def run_batched(args, rank: int = 0, world: int = 1, local_rank: int = 0, dist=None) -> None:
-    """BASELINE.json configs[3] shape: B streams, a P-token random prompt each
-    (fed as batched steps, token by token as the reference prefills), then K
-    greedy decode steps (each stream fed its own argmax) through
-    gaje_cuda_forward_batch.  value = all streams' decode tokens / the decode
-    time (CUDA events on the model stream, max over ranks); prefill tok/s
-    likewise.  Under torchrun every rank decodes its own B streams
-    (request-parallel, no collective in the data path)."""
+    """BASELINE.json configs[3] shape (--batch B --prompt P): B streams per GPU,
+    a P-token random prompt each, then K greedy decode steps (each stream fed
+    its own argmax) through gaje_cuda_forward_batch.  With --serve, configs[4]:
+    512 streams in all, prompt lengths uniform in [64, 1024], LPT-balanced over
+    the ranks.  value = all streams' decode tokens / the decode time (CUDA
+    events on the model stream, max over ranks); prefill tok/s likewise.
+    Under torchrun the ranks are request-parallel and the f32 lm_head is split
+    by vocabulary (gaje_cuda_load_sharded): every step all-gathers the
+    residual rows and the argmax keys over NCCL."""
     import numpy as np
     import torch
 
@@ -429,14 +453,31 @@ def run_batched(args, rank: int = 0, world: int = 1, local_rank: int = 0, dist=N
     cfg_key = args.config
     cfg = g.configs.CONFIGS[cfg_key]
     path = _ensure_model(g, cfg_key, SEED, rank, dist)
-    B, P, K = args.batch, args.prompt, args.steps
+    K = args.steps
     pass_prefill = args.prefill_mode == "pass"
-    model = g.load_genomic_auto(path, device=local_rank, max_ctx=P + K + 8, max_streams=B,
-                                max_prefill=min(P, 4096) if pass_prefill else 0)
+    rng = np.random.default_rng(SEED)
+    if args.serve:
+        n_all = 512
+        lengths = [int(v) for v in rng.integers(64, 1025, n_all)]
+        mine = lpt_assign(lengths, world)[rank]
+        all_prompts = [rng.integers(0, cfg["vocab_size"], n) for n in lengths]
+        plist = [all_prompts[i] for i in mine]
+    else:
+        plist = [np.random.default_rng(SEED + rank * 1000 + b).integers(0, cfg["vocab_size"], args.prompt)
+                 for b in range(args.batch)]
+    B = len(plist)
+    P = max(len(p) for p in plist)
+    max_ctx = P + K + 8
+    kw = dict(device=local_rank, max_ctx=max_ctx, max_streams=B,
+              max_prefill=min(P, 4096) if pass_prefill else 0)
+    if world > 1:
+        obj = [g.nccl_unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(obj, src=0)
+        model = g.load_genomic_sharded(path, world, rank, obj[0], **kw)
+    else:
+        model = g.load_genomic_auto(path, **kw)
     model.set_k_wta_ratio(0.0)
     stream = torch.cuda.ExternalStream(model.stream, device=local_rank)
-    rng = np.random.default_rng(SEED + rank)
-    prompts = rng.integers(0, model.vocab_size, (B, P))
     sids = list(range(B))
     # warm-up (also the prefill timing)
     torch.cuda.synchronize()
@@ -446,10 +487,10 @@ def run_batched(args, rank: int = 0, world: int = 1, local_rank: int = 0, dist=N
     e0.record(stream)
     am = None
     if pass_prefill:  # each stream's prompt in one pass (tensor-core GEMMs + causal attention)
-        am = [model.prefill(sid, prompts[sid]) for sid in sids]
-    else:  # token by token as batched steps
+        am = [model.prefill(sid, [int(t) for t in plist[sid]]) for sid in sids]
+    else:  # token by token as batched steps (equal prompt lengths only)
         for t in range(P):
-            am = model.forward_batch(sids, [int(v) for v in prompts[:, t]])
+            am = model.forward_batch(sids, [int(plist[b][t]) for b in sids])
     e1.record(stream)
     e1.synchronize()
     pre_ms = e0.elapsed_time(e1)
@@ -472,11 +513,16 @@ def run_batched(args, rank: int = 0, world: int = 1, local_rank: int = 0, dist=N
     if rank != 0:
         return
     peaks = _peaks()
-    sb = g.configs.step_bytes(cfg, P + K // 2)
-    body_plus_head = sb["total"] - sb.get("kv", 0)
-    kv_per_stream = sb.get("kv", 0)
-    step_bytes = body_plus_head + B * kv_per_stream  # weights once per step, every stream's KV
+    mean_p = sum(len(p) for p in plist) / B
+    sb = g.configs.step_bytes(cfg, int(mean_p + K // 2))
+    # per rank and step: the body once, this rank's share of the lm_head, every local stream's KV
+    lm_share = sb["lm_head"] * (1.0 - 1.0 / world) if world > 1 else 0.0
+    step_bytes = sb["total"] - sb["kv"] - lm_share + B * sb["kv"]
     step_s = dec_max / 1000.0 / K
+    n_prompt_tokens = sum(len(p) for p in plist)
+    workload = (f"{cfg_key} batched serving: 512 streams, prompts uniform in [64, 1024] (LPT over {world} ranks, "
+                f"{B} per rank), {K} greedy steps" if args.serve else
+                f"{cfg_key} batched greedy decode, {B} streams per GPU after a {P}-token prompt each")
     line = {
         "metric": "decode tok/s (batched)",
         "value": round(world * B * K / (dec_max / 1000.0), 2),
@@ -491,18 +537,19 @@ def run_batched(args, rank: int = 0, world: int = 1, local_rank: int = 0, dist=N
         "dtype": "f32",
         "data": "synthetic: seeded random-init N(0,0.02) weights quantised by the Q4_0 exporter restatement, "
                 "uniform random prompt ids",
-        "config": {"workload": f"{cfg_key} batched greedy decode, {B} streams per GPU after a {P}-token prompt "
-                               f"each", "global_batch": world * B, "prompt_len": P, "decode_steps": K,
-                   "parallelism": f"request-parallel x{world}" if world > 1 else "single",
+        "config": {"workload": workload, "global_batch": world * B, "prompt_len": P if not args.serve else "64-1024",
+                   "decode_steps": K,
+                   "parallelism": (f"request-parallel x{world}, lm_head vocab-sharded over NCCL" if world > 1
+                                   else "single"),
                    "l2": "inputs larger than L2"},
-        "prefill": {"value": round(world * B * P / (pre_max / 1000.0), 2), "unit": "tok/s",
+        "prefill": {"value": round(world * n_prompt_tokens / (pre_max / 1000.0), 2), "unit": "tok/s",
                     "how": ("gaje_cuda_prefill: each stream's prompt in one pass (tcgen05 GEMMs over the prompt "
                             "rows, causal attention kernel); the reference prefills token by token"
                             if pass_prefill else "token by token as batched steps (as the reference)")},
         "e2e": {"value": round(world * B * K / (dec_max / 1000.0), 2), "unit": "tok/s",
                 "h2d_bytes_per_step": 12 * B, "d2h_bytes_per_step": 4 * B + 32,
                 "path": "gaje_cuda_forward_batch (host tokens in, host argmax out, a sync per step)"},
-        "roofline": {"bound": "hbm", "kernel": "batched step (skinny Q4 GEMMs + lm_head for B vectors)",
+        "roofline": {"bound": "hbm", "kernel": "batched step (Q4 GEMMs + lm_head for B vectors), bytes per rank",
                      "achieved": round(step_bytes / step_s / 1e9, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(step_bytes / step_s / 1e9 / peaks["hbm_gbs"], 4), "traffic": None,
                      "algorithmic_bytes": step_bytes,
@@ -543,6 +590,8 @@ def main():
     ap.add_argument("--batch", type=int, default=0,
                     help="batched decode of this many streams per GPU (configs[3]/[4] shape) instead of batch 1")
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt tokens per stream (--batch)")
+    ap.add_argument("--serve", action="store_true",
+                    help="configs[4]: 512 streams over all ranks, prompts uniform in [64, 1024], LPT-balanced")
     ap.add_argument("--prefill-mode", choices=["pass", "steps"], default="pass",
                     help="--batch prompts: one gaje_cuda_prefill pass per stream, or token-by-token batched steps")
     ap.add_argument("--sweep", action="store_true",
@@ -577,7 +626,7 @@ def main():
                                  device_id=torch.device(f"cuda:{local_rank}"))
         dist = tdist
     try:
-        if args.batch > 0:
+        if args.batch > 0 or args.serve:
             run_batched(args, rank, world, local_rank, dist)
         else:
             run_ours(args, rank, world, local_rank, dist)

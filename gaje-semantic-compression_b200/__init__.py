@@ -12,6 +12,8 @@ from .runtime import (  # noqa: F401
     GajeValueError,
     GenomicLLM,
     Q4Matrix,
+    argmax_key,
+    argmax_key_index,
     attention_decode,
     decode_header,
     f32_gemv_argmax,
@@ -20,9 +22,12 @@ from .runtime import (  # noqa: F401
     last_error,
     lib,
     load_genomic_auto,
+    load_genomic_sharded,
+    nccl_unique_id,
     quantize_q4_0_native,
     quantize_q8_0_native,
     rms_norm,
+    vocab_shard,
     write_synthetic,
 )
 from . import configs  # noqa: F401

@@ -359,7 +359,9 @@ struct LmBatchArgs {
   float* logits;        // [B][V]
   unsigned long long* part;  // [grid][B]
   unsigned* cnt;        // zero between launches
-  unsigned* argmax;     // [B]
+  unsigned* argmax;     // [B] first-max index (row_offset added), or nullptr
+  unsigned long long* keys;  // [B] the winning amax_key of each vector, or nullptr
+  unsigned row_offset;  // global index of W's row 0 (a vocab shard's first row)
   int V, d, B, rows_per_cta;
 };
 template <int MB, int RPW>
@@ -441,7 +443,7 @@ __global__ void __launch_bounds__(kLbThreads) k_lmhead_batch(LmBatchArgs A) {
         if (b < A.B) {
           const float v = warp_sum(acc[q][b]) + bb;
           if (lane == 0) A.logits[(size_t)b * A.V + r] = v;
-          const unsigned long long key = amax_key(v, (unsigned)r);
+          const unsigned long long key = amax_key(v, (unsigned)r + A.row_offset);
           best[b] = key > best[b] ? key : best[b];
         }
       }
@@ -468,14 +470,19 @@ __global__ void __launch_bounds__(kLbThreads) k_lmhead_batch(LmBatchArgs A) {
       k = v > k ? v : k;
     }
     k = warp_max_u64(k);
-    if (lane == 0) A.argmax[b] = amax_index(k);
+    if (lane == 0) {
+      if (A.argmax) A.argmax[b] = amax_index(k);
+      if (A.keys) A.keys[b] = k;
+    }
   }
   if (tid == 0) *A.cnt = 0u;  // ready for the next launch
 }
 
 // First-max argmax of each row of logits [B][V] (llm/forward.rs:262-271): one
-// CTA of 512 threads per row (the tensor-core lm_head path).
-__global__ void __launch_bounds__(512) k_argmax_rows(const float* logits, int V, unsigned* out) {
+// CTA of 512 threads per row (the tensor-core lm_head path).  Column i is
+// vocab row i + row_offset; keys (nullable) receives each row's winning key.
+__global__ void __launch_bounds__(512) k_argmax_rows(const float* logits, int V, unsigned* out,
+                                                     unsigned row_offset, unsigned long long* keys) {
   __shared__ unsigned long long wb[16];
   pdl_wait();
   pdl_trigger();
@@ -483,7 +490,7 @@ __global__ void __launch_bounds__(512) k_argmax_rows(const float* logits, int V,
   unsigned long long best = 0ull;
 #pragma unroll 4
   for (int i = threadIdx.x; i < V; i += 512) {
-    const unsigned long long k = amax_key(__ldcg(row + i), (unsigned)i);
+    const unsigned long long k = amax_key(__ldcg(row + i), (unsigned)i + row_offset);
     best = k > best ? k : best;
   }
   best = warp_max_u64(best);
@@ -492,7 +499,23 @@ __global__ void __launch_bounds__(512) k_argmax_rows(const float* logits, int V,
   if (threadIdx.x == 0) {
     unsigned long long b = 0ull;
     for (int w = 0; w < 16; ++w) b = wb[w] > b ? wb[w] : b;
-    out[blockIdx.x] = amax_index(b);
+    if (out) out[blockIdx.x] = amax_index(b);
+    if (keys) keys[blockIdx.x] = b;
+  }
+}
+
+// The vocab-sharded argmax merge: keys_all[r][j] is rank r's best key (over
+// its vocab rows) for gathered vector j; this rank's vector b is gathered
+// vector rank*B + b.  The largest key over the ranks is the first maximum
+// over the whole vocabulary (amax_key orders by value, then by lower index).
+__global__ void k_shard_argmax(const unsigned long long* keys_all, int nranks, int B, int rank, unsigned* out) {
+  for (int b = threadIdx.x; b < B; b += blockDim.x) {
+    unsigned long long k = 0ull;
+    for (int r = 0; r < nranks; ++r) {
+      const unsigned long long v = keys_all[(size_t)r * nranks * B + (size_t)rank * B + b];
+      k = v > k ? v : k;
+    }
+    out[b] = amax_index(k);
   }
 }
 

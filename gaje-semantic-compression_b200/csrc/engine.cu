@@ -7,12 +7,17 @@
 // kernels.cuh; generate_native_core (src/nn/llm/forward.rs:215-330) is the
 // same host loop around it with the token selection done on the device.
 #include <cuda_runtime.h>
+#include <dlfcn.h>
+#include <nccl.h>
 
 #include <algorithm>
+#include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
+#include <thread>
 #include <mutex>
 #include <set>
 #include <string>
@@ -25,6 +30,7 @@
 #include "gemm.cuh"
 #include "batch.cuh"
 #include "tc_gemm.cuh"
+#include "fused.cuh"
 
 using namespace gaje;
 
@@ -38,6 +44,65 @@ namespace {
   } while (0)
 
 size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// ---- NCCL, resolved at run time (vocab-sharded serving only).  The library
+// does not link libnccl: a host process that already loaded one (a PyTorch
+// process, a Rust host with its own NCCL) shares it through the soname, and a
+// single-GPU user never needs it.
+struct NcclApi {
+  ncclResult_t (*get_unique_id)(ncclUniqueId*) = nullptr;
+  ncclResult_t (*comm_init_rank)(ncclComm_t*, int, ncclUniqueId, int) = nullptr;
+  ncclResult_t (*all_gather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t) = nullptr;
+  ncclResult_t (*comm_destroy)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_abort)(ncclComm_t) = nullptr;
+  ncclResult_t (*comm_get_async_error)(ncclComm_t, ncclResult_t*) = nullptr;
+  const char* (*error_string)(ncclResult_t) = nullptr;
+  std::string why;  // empty when every symbol resolved
+};
+const NcclApi& nccl_api() {
+  static NcclApi api = [] {
+    NcclApi a;
+    void* h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) {
+      const char* e = dlerror();
+      a.why = std::string("libnccl.so.2 could not be loaded: ") + (e ? e : "?");
+      return a;
+    }
+    auto sym = [&](auto& fn, const char* name) {
+      fn = reinterpret_cast<std::remove_reference_t<decltype(fn)>>(dlsym(h, name));
+      if (!fn && a.why.empty()) a.why = std::string("libnccl lacks ") + name;
+    };
+    sym(a.get_unique_id, "ncclGetUniqueId");
+    sym(a.comm_init_rank, "ncclCommInitRank");
+    sym(a.all_gather, "ncclAllGather");
+    sym(a.comm_destroy, "ncclCommDestroy");
+    sym(a.comm_abort, "ncclCommAbort");
+    sym(a.comm_get_async_error, "ncclCommGetAsyncError");
+    sym(a.error_string, "ncclGetErrorString");
+    return a;
+  }();
+  return api;
+}
+
+// The vocabulary split of the lm_head: rank r owns rows [r*chunk, r*chunk +
+// rows) with chunk = ceil(V / nranks).
+void vocab_shard(int V, int nranks, int rank, int& row0, int& rows) {
+  const int chunk = (V + nranks - 1) / nranks;
+  row0 = std::min(V, rank * chunk);
+  rows = std::max(0, std::min(chunk, V - row0));
+}
+
+// Host twin of the device amax_key: larger value first, then the lower index;
+// NaN and -inf never win; -0.0 ties with +0.0.
+uint64_t host_amax_key(float v, uint32_t idx) {
+  if (!(v > -INFINITY)) return 0ull;
+  if (v == 0.0f) v = 0.0f;
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (uint64_t(u) << 32) | (0xFFFFFFFFu - idx);
+}
 
 // One device allocation carved into aligned pieces.
 struct Arena {
@@ -268,6 +333,19 @@ struct gaje_model {
   size_t phase_ns_cap = 0;
   unsigned long long* trace_ns = nullptr;
   size_t trace_ns_cap = 0;
+  // persistent kernel with two exchanges per block (fused.cuh); preferred
+  // over k_decode_mega when the shape fits it
+  bool fu_ok = false;      // planned (shape fits, buffers allocated)
+  bool use_fused = false;  // planned and launchable
+  FusedPlan fplan{};
+  size_t fused_smem = 0;
+  std::vector<FuLayer> h_fl;
+  FuLayer* d_fl = nullptr;
+  float* fya = nullptr;    // [2][d]
+  float* fyb = nullptr;    // [2][d]
+  uint2* fwords = nullptr; // flags [2][grid], kvnew [2][nkv][hd], mlx [nh][S][2], token
+  size_t fwords_n = 0;
+  unsigned fepoch = 0;
   // batched streams (gaje_cuda_forward_batch)
   int max_streams = 0;
   BatchCache bcache{};
@@ -292,8 +370,20 @@ struct gaje_model {
   unsigned* pf_tab = nullptr;            // [3][pf_rows]: tokens, positions, stream ids of a prefill chunk
   unsigned* h_pf_tab = nullptr;          // pinned staging of the same
   int blm_grid = 0;                      // lm_head CTAs of a batched step
+  // vocab-sharded serving (gaje_cuda_load_sharded): the lm_head holds rows
+  // [v0, v0 + Vl) of the vocabulary; Vl == V and nranks == 1 otherwise
+  int nranks = 1, rank = 0, v0 = 0, Vl = 0;
+  ncclComm_t nccl = nullptr;
+  bool nccl_broken = false;              // a collective failed or timed out: the group is gone
+  float* bxg = nullptr;                  // [nranks * max_streams][d] residual rows of every rank
+  unsigned long long* bkey = nullptr;    // [nranks * max_streams] this rank's best key per gathered row
+  unsigned long long* bkey_all = nullptr;  // [nranks][nranks * max_streams]
 
   ~gaje_model() {
+    if (nccl) {
+      const NcclApi& api = nccl_api();
+      if (nccl_broken ? api.comm_abort : api.comm_destroy) (nccl_broken ? api.comm_abort : api.comm_destroy)(nccl);
+    }
     if (phase_ns) cudaFree(phase_ns);
     if (trace_ns) cudaFree(trace_ns);
     if (graph) cudaGraphExecDestroy(graph);
@@ -460,6 +550,7 @@ struct gaje_model {
   // `trace` (every CTA's in-phase stamps) is only taken when n fits one launch.
   int run_steps(size_t n, unsigned long long* stamps = nullptr, unsigned long long* trace = nullptr) {
     if (n == 0) return GAJE_OK;
+    if (use_fused && block_k() == 0 && !stamps && !trace) return run_fused(n);
     if (!use_mega) {
       for (size_t i = 0; i < n; ++i)
         if (int s = run_step()) return s;
@@ -496,6 +587,52 @@ struct gaje_model {
       CK(cudaLaunchKernelEx(&cfg, k_decode_mega, a));
       n -= size_t(chunk);
       if (stamps) stamps += size_t(chunk) * (5 * L + 1);
+    }
+    const int kk = logits_k();
+    if (kk > 0) {  // masks the returned logits; the argmax is unaffected
+      k_kwta<<<1, kKwtaThreads, 0, stream>>>(logits, V, kk);
+      CK(cudaGetLastError());
+    }
+    return GAJE_OK;
+  }
+
+  // n greedy steps in launches of the two-exchange persistent kernel.
+  int run_fused(size_t n, unsigned long long* trace = nullptr) {
+    while (n > 0) {
+      const int chunk = int(std::min<size_t>(n, 1u << 16));
+      const unsigned long long per = (unsigned long long)chunk * unsigned(2 * L + 1);
+      if ((unsigned long long)fepoch + per >= 0xFFFFFFF0ull) {  // epochs wrap: restart from clean words
+        CK(cudaMemsetAsync(fwords, 0, fwords_n * sizeof(uint2), stream));
+        fepoch = 0;
+      }
+      CK(cudaMemsetAsync(fya, 0, size_t(4) * d * sizeof(float), stream));  // fya and fyb are adjacent
+      FusedArgs a;
+      a.P = P;
+      a.layers = d_layers;
+      a.fl = d_fl;
+      a.plan = fplan;
+      a.ya = fya;
+      a.yb = fyb;
+      a.flags = fwords;
+      a.kvnew = fwords + 2 * size_t(sms);
+      a.mlx = a.kvnew + 2 * size_t(nkv) * hd;
+      a.tok = a.mlx + size_t(nh) * fplan.S * 2;
+      a.epoch0 = fepoch;
+      a.n_steps = chunk;
+      a.trace = chunk == int(n) ? trace : nullptr;
+      fepoch += unsigned(per);
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(sms);
+      cfg.blockDim = dim3(kFuThreads);
+      cfg.dynamicSmemBytes = fused_smem;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeCooperative;
+      attr[0].val.cooperative = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      CK(cudaLaunchKernelEx(&cfg, k_decode_fused, a));
+      n -= size_t(chunk);
     }
     const int kk = logits_k();
     if (kk > 0) {  // masks the returned logits; the argmax is unaffected
@@ -672,6 +809,47 @@ bool plan_mega(gaje_model* m) {
   p.lm_stage_rows = int(std::min<size_t>(kMkConsumerWarps, p.slot_bytes / (size_t(m->d) * 4)));
   m->mega_smem = mega_smem_bytes(p, m->d, m->hd);
   return p.lm_stage_rows >= 1 && m->mega_smem + fa.sharedSizeBytes <= size_t(kMaxDynSmem);
+}
+
+// The two-exchange persistent kernel's plan (fused.cuh), from the shapes
+// alone; false when the model does not fit it (the five-exchange kernel runs).
+bool plan_fused(gaje_model* m) {
+  cudaFuncAttributes fa{};
+  if (cudaFuncGetAttributes(&fa, k_decode_fused) != cudaSuccess) return false;
+  const int d = m->d, hd = m->hd, G = m->sms;
+  if (d % 32 || hd % 32 || hd > 128 || m->ff % 32 || d / 4 > kFuConsumers || m->info.use_genomic_norm) return false;
+  if (m->qkv[0].K != d || m->gate_up[0].K != d || m->wo[0].N != d || m->down[0].N != d) return false;
+  if (m->wo[0].K != m->nh * hd || m->down[0].K != m->ff) return false;
+  FusedPlan& p = m->fplan;
+  const int s_cta = (G - 2 * m->nkv) / m->nh;
+  if (s_cta < 1) return false;
+  const int cached = std::max(1, m->max_ctx - 1);
+  p.S = std::min({s_cta, kFuMaxSplits, std::max(1, (cached + 63) / 64)});
+  p.nA = m->nh * p.S;
+  p.nKV = 2 * m->nkv;
+  p.cap = (cached + p.S - 1) / p.S + 1;
+  p.pv_groups = std::max(1, kFuConsumers / hd);
+  p.kb_max = 0;
+  for (int c = 0; c < G; ++c) {
+    int kb0 = 0, n = 0;
+    fu_kbs(m->ff / 32, G, c, kb0, n);
+    p.kb_max = std::max(p.kb_max, n);
+  }
+  p.lm_rows_per_cta = (m->V + G - 1) / G;
+  const size_t nbq = size_t(m->qkv[0].nb), nbpq = size_t(m->qkv[0].nbp);
+  const size_t nbg = size_t(m->gate_up[0].nb), nbpg = size_t(m->gate_up[0].nbp);
+  const size_t need = std::max({size_t(hd) * (nbq * 16 + nbpq * 4), size_t(hd / 32) * d * 20,
+                                size_t(64) * (nbg * 16 + nbpg * 4), size_t(d) * 20, size_t(d) * 4});
+  p.slot_bytes = unsigned((need + 127) / 128 * 128);
+  p.nslots = 0;
+  const size_t budget = size_t(kMaxDynSmem) - fa.sharedSizeBytes - 1024;
+  const size_t base = fused_smem_bytes(p, d, hd) + 128;  // + the slots' alignment
+  if (base >= budget) return false;
+  p.nslots = int(std::min<size_t>(kFuMaxSlots, (budget - base) / p.slot_bytes));
+  if (p.nslots < 3) return false;
+  p.lm_stage_rows = int(std::min<size_t>(kFuConsumerWarps, p.slot_bytes / (size_t(d) * 4)));
+  m->fused_smem = fused_smem_bytes(p, d, hd) + 128;
+  return p.lm_stage_rows >= 1;
 }
 
 // ---- batched streams (gaje_cuda_forward_batch)
@@ -864,6 +1042,10 @@ int launch_batch(gaje_model* m, int Bi) {
     if (e != cudaSuccess) break;
     e = batch_gemm<false>(m, Bi, m->down[l], m->bact, TcNorm{}, EpiResidBatch{m->bx, d, m->st, bs, l});
   }
+  if (m->nranks > 1) {  // vocab-sharded: the head runs after the step graph (sharded_head)
+    if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+    return GAJE_OK;
+  }
   if (e == cudaSuccess && Bi >= kBatchTcMin && m->btc_hi && d % kTcK == 0) {
     // output norm fused into the split, f32 lm_head on the tensor cores, then the argmax per stream
     const TcPlan p = tc_plan(m->V, d, Bi, m->sms);
@@ -871,7 +1053,8 @@ int launch_batch(gaje_model* m, int Bi) {
     if (tc_gemm_run(p, F32Rows{m->lm_head, m->lm_bias, m->V, d}, m->bx, Bi, EpiStore{m->blogits, m->V}, b, st, true,
                     TcNorm{m->out_norm, eps, nullptr, bs.pos, L}, m->st) != GAJE_OK)
       return set_error(GAJE_ERR_CUDA, "kernel launch: lm_head");
-    e = launch_k(k_argmax_rows, dim3(unsigned(Bi)), dim3(512), 0, st, true, (const float*)m->blogits, m->V, d_argmax);
+    e = launch_k(k_argmax_rows, dim3(unsigned(Bi)), dim3(512), 0, st, true, (const float*)m->blogits, m->V, d_argmax,
+                 0u, (unsigned long long*)nullptr);
     if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
     return GAJE_OK;
   }
@@ -930,7 +1113,7 @@ int launch_prefill_chunk(gaje_model* m, int nc, int p0, unsigned sid, bool head)
     if (e != cudaSuccess) break;
     e = batch_gemm<false>(m, nc, m->down[l], m->bact, TcNorm{}, EpiResidBatch{m->bx, d, m->st, bs, l});
   }
-  if (e == cudaSuccess && head) {
+  if (e == cudaSuccess && head && m->nranks == 1) {
     LmBatchArgs la{};
     la.W = m->lm_head;
     la.bias = m->lm_bias;
@@ -951,6 +1134,102 @@ int launch_prefill_chunk(gaje_model* m, int nc, int p0, unsigned sid, bool head)
   return GAJE_OK;
 }
 
+// ---- the vocab-sharded head of a batched step (gaje_cuda_load_sharded)
+//
+// Every rank holds the whole body and the lm_head rows [v0, v0 + Vl).  After
+// the body of a step (B residual rows of this rank's streams in x_local):
+//   1. all-gather the residual rows of every rank      -> bxg [nranks*B][d]
+//   2. output norm + this rank's lm_head rows for all nranks*B rows, and per
+//      row the best amax_key over those rows (global index) -> bkey
+//   3. all-gather the keys                              -> bkey_all [nranks][nranks*B]
+//   4. per local stream the largest key over the ranks -> its first-max argmax
+// The largest key is the first maximum over the whole vocabulary, as the
+// single-GPU argmax (llm/forward.rs:262-271) gives it.  Every rank must issue
+// the same sequence of sharded calls with the same B: the two all-gathers
+// are collective.
+int sharded_head(gaje_model* m, const float* x_local, int B, unsigned* d_argmax) {
+  const NcclApi& api = nccl_api();
+  cudaStream_t st = m->stream;
+  const int d = m->d, n = m->nranks, M = n * B;
+  const float eps = m->info.eps;
+  auto nccl_fail = [&](ncclResult_t r, const char* what) {
+    m->nccl_broken = true;
+    return set_error(GAJE_ERR_CUDA, std::string("NCCL ") + what + ": " + api.error_string(r));
+  };
+  ncclResult_t r = api.all_gather(x_local, m->bxg, size_t(B) * d, ncclFloat32, m->nccl, st);
+  if (r != ncclSuccess) return nccl_fail(r, "all-gather of the residual rows");
+  cudaError_t e = cudaSuccess;
+  if (M >= kBatchTcMin && m->btc_hi && d % kTcK == 0) {
+    // output norm fused into the split, this rank's vocab rows on the tensor cores
+    const TcPlan p = tc_plan(m->Vl, d, M, m->sms);
+    TcBuffers b{m->btc_hi, m->btc_lo, m->btc_part};
+    if (tc_gemm_run(p, F32Rows{m->lm_head, m->lm_bias, m->Vl, d}, m->bxg, M, EpiStore{m->blogits, m->Vl}, b, st,
+                    false, TcNorm{m->out_norm, eps, nullptr, nullptr, m->L}, m->st) != GAJE_OK)
+      return set_error(GAJE_ERR_CUDA, "kernel launch: sharded lm_head");
+    e = launch_k(k_argmax_rows, dim3(unsigned(M)), dim3(512), 0, st, true, (const float*)m->blogits, m->Vl,
+                 (unsigned*)nullptr, unsigned(m->v0), m->bkey);
+  } else {
+    const int MB = batch_lm_mb(M);
+    for (int b0 = 0; b0 < M && e == cudaSuccess; b0 += MB) {
+      LmBatchArgs la{};
+      la.W = m->lm_head;
+      la.bias = m->lm_bias;
+      la.x = m->bxg + size_t(b0) * d;
+      la.norm_w = m->out_norm;
+      la.eps = eps;
+      la.logits = m->blogits + size_t(b0) * m->Vl;
+      la.part = m->blm_part;
+      la.cnt = m->blm_cnt;
+      la.argmax = nullptr;
+      la.keys = m->bkey + b0;
+      la.row_offset = unsigned(m->v0);
+      la.V = m->Vl;
+      la.d = d;
+      la.B = std::min(MB, M - b0);
+      la.rows_per_cta = (m->Vl + m->blm_grid - 1) / m->blm_grid;
+      const size_t smem = size_t(MB) * d * 4;
+      e = MB == 8 ? launch_k(k_lmhead_batch<8, 4>, dim3(m->blm_grid), dim3(kLbThreads), smem, st, false, la)
+                  : launch_k(k_lmhead_batch<16, 2>, dim3(m->blm_grid), dim3(kLbThreads), smem, st, false, la);
+    }
+  }
+  if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  r = api.all_gather(m->bkey, m->bkey_all, size_t(M), ncclUint64, m->nccl, st);
+  if (r != ncclSuccess) return nccl_fail(r, "all-gather of the argmax keys");
+  k_shard_argmax<<<1, 256, 0, st>>>(m->bkey_all, n, B, m->rank, d_argmax);
+  CK(cudaGetLastError());
+  return GAJE_OK;
+}
+
+// Waits for the model stream after a sharded step, bounded: a rank whose peer
+// died never sees its collective finish, so after GAJE_NCCL_TIMEOUT_S seconds
+// (default 120) the communicator is aborted and the call fails with
+// GAJE_ERR_TIMEOUT; the model then refuses further sharded calls.
+int sync_sharded(gaje_model* m) {
+  const NcclApi& api = nccl_api();
+  double limit = 120.0;
+  if (const char* s = getenv("GAJE_NCCL_TIMEOUT_S")) limit = std::max(0.1, atof(s));
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    const cudaError_t q = cudaStreamQuery(m->stream);
+    if (q == cudaSuccess) return GAJE_OK;
+    if (q != cudaErrorNotReady) return set_error(GAJE_ERR_CUDA, std::string("step: ") + cudaGetErrorString(q));
+    ncclResult_t ae = ncclSuccess;
+    if (api.comm_get_async_error(m->nccl, &ae) == ncclSuccess && ae != ncclSuccess && ae != ncclInProgress) {
+      m->nccl_broken = true;
+      api.comm_abort(m->nccl);
+      m->nccl = nullptr;
+      return set_error(GAJE_ERR_CUDA, std::string("NCCL: ") + api.error_string(ae));
+    }
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > limit) {
+      m->nccl_broken = true;
+      api.comm_abort(m->nccl);
+      m->nccl = nullptr;
+      return set_error(GAJE_ERR_TIMEOUT, "a collective of the sharded step did not finish (a peer rank is gone?)");
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
 int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   FlatFile f;
   std::string err;
@@ -967,6 +1246,7 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   m->ff = int(I.ffn_dim);
   m->V = int(I.vocab_size);
   m->L = int(I.n_blocks);
+  vocab_shard(m->V, m->nranks, m->rank, m->v0, m->Vl);
   m->max_ctx = int(opts && opts->max_ctx ? opts->max_ctx : 4096);
   m->use_graph = !opts || opts->use_graph;
   m->max_streams = opts ? int(opts->max_streams) : 0;
@@ -978,6 +1258,9 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     return set_error(GAJE_ERR_INVALID, "max_prefill needs batched streams (max_streams > 0)");
   if (m->pf_rows > 0 && m->hd > 128)
     return set_error(GAJE_ERR_UNSUPPORTED, "prefill attention supports head_dim up to 128");
+  if (m->nranks > 1 && m->max_streams == 0)
+    return set_error(GAJE_ERR_INVALID, "a vocab-sharded model serves batched streams: set max_streams");
+  if (m->Vl < 1) return set_error(GAJE_ERR_INVALID, "more ranks than vocabulary rows");
   m->rng.s = opts ? opts->seed : 0;
   if (m->nh / m->nkv > kAttnMaxGroup) return set_error(GAJE_ERR_UNSUPPORTED, "more than 16 query heads per KV head");
   if (m->hd % 4 != 0) return set_error(GAJE_ERR_UNSUPPORTED, "head_dim must be a multiple of 4");
@@ -1017,8 +1300,8 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     }
     m->out_norm = a.take<float>(d);
     m->embd = a.take<float>(V * d);
-    m->lm_head = a.take<float>(V * d);
-    m->lm_bias = f.lm_head->bias_len ? a.take<float>(V) : nullptr;
+    m->lm_head = a.take<float>(size_t(m->Vl) * d);  // this rank's vocab rows (all of them unsharded)
+    m->lm_bias = f.lm_head->bias_len ? a.take<float>(size_t(m->Vl)) : nullptr;
     const size_t cache = L * size_t(m->nkv) * m->max_ctx * m->hd;
     m->kcache = a.take<float>(cache);
     m->vcache = a.take<float>(cache);
@@ -1038,6 +1321,22 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     m->pen_ids = a.take<unsigned>(m->max_ctx);
     m->st = a.take<DevState>(1);
     m->d_layers = a.take<LayerW>(L);
+    if (m->fu_ok) {  // K-block-major attn_output / ffn_down, the sums and the exchange words
+      m->h_fl.assign(L, FuLayer{});
+      for (size_t l = 0; l < L; ++l) {
+        const Q4Dev& wo = m->wo[l];
+        const Q4Dev& dn = m->down[l];
+        m->h_fl[l].wo_qs = a.take<uint4>(size_t(wo.N) * wo.nb);
+        m->h_fl[l].wo_sm = a.take<uint32_t>(size_t(wo.N) * wo.nb);
+        m->h_fl[l].dn_qs = a.take<uint4>(size_t(dn.N) * dn.nb);
+        m->h_fl[l].dn_sm = a.take<uint32_t>(size_t(dn.N) * dn.nb);
+      }
+      m->d_fl = a.take<FuLayer>(L);
+      m->fya = a.take<float>(4 * d);
+      m->fyb = m->fya ? m->fya + 2 * d : nullptr;
+      m->fwords_n = 2 * size_t(m->sms) + 2 * size_t(m->nkv) * m->hd + size_t(m->nh) * m->fplan.S * 2 + 1;
+      m->fwords = a.take<uint2>(m->fwords_n);
+    }
     // LL exchange words of the persistent kernel, one contiguous range
     const size_t qd = size_t(m->nh) * m->hd, kvd = size_t(m->nkv) * m->hd;
     // the persistent kernel's split cap (plan_mega sets the same value)
@@ -1063,7 +1362,13 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
       m->battn = a.take<float>(R * qd);
       m->bact = a.take<float>(R * m->ff);
       m->pf_tab = a.take<unsigned>(3 * std::max<size_t>(m->pf_rows, 1));
-      m->blogits = a.take<float>(S * V);
+      const size_t NS = size_t(m->nranks) * S;  // rows the lm_head of a sharded step sees
+      m->blogits = a.take<float>(std::max(S * V, NS * size_t(m->Vl)));
+      if (m->nranks > 1) {
+        m->bxg = a.take<float>(NS * d);
+        m->bkey = a.take<unsigned long long>(NS);
+        m->bkey_all = a.take<unsigned long long>(NS * size_t(m->nranks));
+      }
       m->bpart_o = a.take<float>(S * m->nkv * kAttnMaxSplits * G * m->hd);
       m->bpart_ml = a.take<float>(S * m->nkv * kAttnMaxSplits * G * 2);
       m->bcnt = a.take<unsigned>(S * m->nkv);
@@ -1084,15 +1389,21 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
       m->bsk_part = a.take<float>(std::max<size_t>(part, 1));
       m->bsk_cnt = a.take<unsigned>(tiles);
       m->bsk_tiles = tiles;
-      if (R >= size_t(kBatchTcMin)) {
+      const size_t RT = std::max(R, NS);
+      if (RT >= size_t(kBatchTcMin)) {
         const size_t kmax = std::max({size_t(d), size_t(m->nh) * m->hd, size_t(m->ff)});
-        m->btc_mpad = int((R + 255) / 256 * 256);
+        m->btc_mpad = int((RT + 255) / 256 * 256);
         m->btc_hi = a.take<unsigned char>(tc_plane_bytes(m->btc_mpad, int(kmax)));
         m->btc_lo = a.take<unsigned char>(tc_plane_bytes(m->btc_mpad, int(kmax)));
         m->btc_part = a.take<float>(size_t(m->sms) * 256 * kTcRows);  // z * M * N <= SMs * NT * 128
       }
     }
   };
+  {
+    Arena shapes;  // a first pass fills the matrix shapes the fused plan needs
+    plan(shapes);
+    m->fu_ok = m->nranks == 1 && (!opts || opts->use_megakernel == 1) && plan_fused(m);
+  }
   Arena sizing;
   plan(sizing);
   const size_t staging_words = (staging_bytes + 3) / 4;
@@ -1118,7 +1429,15 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   if (int s = smem_optin((const void*)k_gemv<G_DOWN>, m->pd.smem)) return s;
   if (int s = smem_optin((const void*)k_attn, m->attn_smem)) return s;
   if (int s = smem_optin((const void*)k_lmhead, m->lm_smem)) return s;
-  m->use_mega = (!opts || opts->use_megakernel) && plan_mega(m);
+  m->use_mega = m->nranks == 1 && (!opts || opts->use_megakernel) && plan_mega(m);
+  if (m->fu_ok) {
+    if (int s = smem_optin((const void*)k_decode_fused, m->fused_smem)) return s;
+    int per_sm = 0, coop = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_fused, kFuThreads, m->fused_smem));
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device);
+    m->use_fused = per_sm >= 1 && coop;
+    CK(cudaMemsetAsync(m->fwords, 0, m->fwords_n * sizeof(uint2), m->stream));
+  }
   if (m->use_mega) {
     if (int s = smem_optin((const void*)k_decode_mega, m->mega_smem)) return s;
     int per_sm = 0;
@@ -1161,11 +1480,15 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   }
   CK(cudaMemcpy(m->out_norm, f.blob(f.output_norm->dna_off, d * 4), d * 4, cudaMemcpyHostToDevice));
   CK(cudaMemcpy(m->embd, f.blob(f.token_embd->dna_off, V * d * 4), V * d * 4, cudaMemcpyHostToDevice));
-  CK(cudaMemcpy(m->lm_head, f.blob(f.lm_head->dna_off, V * d * 4), V * d * 4, cudaMemcpyHostToDevice));
+  {  // this rank's lm_head rows [v0, v0 + Vl)
+    const size_t r0 = size_t(m->v0), nr = size_t(m->Vl);
+    CK(cudaMemcpy(m->lm_head, f.blob(f.lm_head->dna_off + r0 * d * 4, nr * d * 4), nr * d * 4,
+                  cudaMemcpyHostToDevice));
+  }
   if (m->lm_bias) {
     std::vector<float> b(V, 0.0f);
     memcpy(b.data(), f.blob(f.lm_head->bias_off, f.lm_head->bias_len), f.lm_head->bias_len);
-    CK(cudaMemcpy(m->lm_bias, b.data(), V * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(m->lm_bias, b.data() + m->v0, size_t(m->Vl) * 4, cudaMemcpyHostToDevice));
   }
   {
     std::vector<float2> rt = rope_table(m->max_ctx, m->hd, I.rope_base);
@@ -1175,6 +1498,17 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     std::vector<LayerW> lw(L);
     for (size_t l = 0; l < L; ++l) lw[l] = m->layer(int(l));
     CK(cudaMemcpy(m->d_layers, lw.data(), L * sizeof(LayerW), cudaMemcpyHostToDevice));
+  }
+  if (m->fu_ok) {  // K-block-major copies of attn_output and ffn_down
+    for (size_t l = 0; l < L; ++l) {
+      k_q4_kbmajor<<<m->sms * 4, 256, 0, m->stream>>>(m->wo[l].view(), const_cast<uint4*>(m->h_fl[l].wo_qs),
+                                                      const_cast<uint32_t*>(m->h_fl[l].wo_sm));
+      k_q4_kbmajor<<<m->sms * 4, 256, 0, m->stream>>>(m->down[l].view(), const_cast<uint4*>(m->h_fl[l].dn_qs),
+                                                      const_cast<uint32_t*>(m->h_fl[l].dn_sm));
+    }
+    CK(cudaGetLastError());
+    CK(cudaMemcpyAsync(m->d_fl, m->h_fl.data(), L * sizeof(FuLayer), cudaMemcpyHostToDevice, m->stream));
+    CK(cudaStreamSynchronize(m->stream));
   }
   CK(cudaHostAlloc(&m->h_st, sizeof(DevState), cudaHostAllocDefault));
   CK(cudaHostAlloc(&m->h_tok, 64 * sizeof(unsigned), cudaHostAllocDefault));
@@ -1232,6 +1566,11 @@ void gaje_load_opts_init(gaje_load_opts* o) {
   o->max_prefill = 0;
 }
 
+static int sharded_only() {
+  return set_error(GAJE_ERR_UNSUPPORTED,
+                   "a vocab-sharded model serves batched streams only (gaje_cuda_forward_batch / gaje_cuda_prefill)");
+}
+
 gaje_model* gaje_cuda_load(const char* flat_path, const gaje_load_opts* opts) {
   std::unique_ptr<gaje_model> m(new gaje_model());
   m->device = opts ? opts->device : 0;
@@ -1242,6 +1581,65 @@ gaje_model* gaje_cuda_load(const char* flat_path, const gaje_load_opts* opts) {
   clear_error();
   return m.release();
 }
+
+int gaje_cuda_nccl_unique_id(uint8_t* id_out) {
+  if (!id_out) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  const NcclApi& api = nccl_api();
+  if (!api.why.empty()) return set_error(GAJE_ERR_UNSUPPORTED, api.why);
+  ncclUniqueId id;
+  const ncclResult_t r = api.get_unique_id(&id);
+  if (r != ncclSuccess) return set_error(GAJE_ERR_CUDA, std::string("ncclGetUniqueId: ") + api.error_string(r));
+  static_assert(sizeof(ncclUniqueId) == GAJE_NCCL_ID_BYTES, "NCCL unique id size");
+  memcpy(id_out, &id, sizeof(id));
+  return GAJE_OK;
+}
+
+gaje_model* gaje_cuda_load_sharded(const char* flat_path, const gaje_load_opts* opts, int nranks, int rank,
+                                   const uint8_t* nccl_id) {
+  if (!nccl_id || nranks < 1 || rank < 0 || rank >= nranks) {
+    set_error(GAJE_ERR_INVALID, "nranks/rank out of range or NULL nccl_id");
+    return nullptr;
+  }
+  const NcclApi& api = nccl_api();
+  if (!api.why.empty()) {
+    set_error(GAJE_ERR_UNSUPPORTED, api.why);
+    return nullptr;
+  }
+  std::unique_ptr<gaje_model> m(new gaje_model());
+  m->device = opts ? opts->device : 0;
+  m->nranks = nranks;
+  m->rank = rank;
+  if (int s = load_impl(m.get(), flat_path, opts)) {
+    (void)s;
+    return nullptr;
+  }
+  if (cudaSetDevice(m->device) != cudaSuccess) {
+    set_error(GAJE_ERR_CUDA, "cudaSetDevice");
+    return nullptr;
+  }
+  ncclUniqueId id;
+  memcpy(&id, nccl_id, sizeof(id));
+  const ncclResult_t r = api.comm_init_rank(&m->nccl, nranks, id, rank);
+  if (r != ncclSuccess) {
+    m->nccl = nullptr;
+    set_error(GAJE_ERR_CUDA, std::string("ncclCommInitRank: ") + api.error_string(r));
+    return nullptr;
+  }
+  clear_error();
+  return m.release();
+}
+
+int gaje_vocab_shard(uint32_t vocab_size, int nranks, int rank, uint32_t* row0, uint32_t* rows) {
+  if (!row0 || !rows || nranks < 1 || rank < 0 || rank >= nranks) return set_error(GAJE_ERR_INVALID, "bad argument");
+  int r0 = 0, n = 0;
+  vocab_shard(int(vocab_size), nranks, rank, r0, n);
+  *row0 = uint32_t(r0);
+  *rows = uint32_t(n);
+  return GAJE_OK;
+}
+
+uint64_t gaje_argmax_key(float value, uint32_t index) { return host_amax_key(value, index); }
+uint32_t gaje_argmax_key_index(uint64_t key) { return amax_index(key); }
 
 void gaje_cuda_free(gaje_model* m) {
   if (!m) return;
@@ -1265,7 +1663,11 @@ int gaje_cuda_model_info(gaje_model* m, gaje_model_info* o) {
   o->k_wta_ratio = m->k_wta_ratio;
   o->device_bytes = m->arena.size;
   o->grid = uint32_t(m->sms);
-  o->megakernel = m->use_mega ? 1u : 0u;
+  o->megakernel = m->use_fused ? 2u : m->use_mega ? 1u : 0u;
+  o->nranks = uint32_t(m->nranks);
+  o->rank = uint32_t(m->rank);
+  o->vocab_row0 = uint32_t(m->v0);
+  o->vocab_rows = uint32_t(m->Vl);
   return GAJE_OK;
 }
 
@@ -1295,6 +1697,7 @@ int gaje_cuda_set_seed(gaje_model* m, uint64_t seed) {
 int gaje_cuda_forward(gaje_model* m, uint32_t token_id, int clear_cache, float* logits_out,
                       uint32_t* argmax_out) {
   if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  if (m->nranks > 1) return sharded_only();
   CK(cudaSetDevice(m->device));
   if (clear_cache)
     if (int s = m->set_pos(0)) return s;
@@ -1323,6 +1726,11 @@ int gaje_cuda_forward_batch(gaje_model* m, const uint32_t* stream_ids, const uin
     return set_error(GAJE_ERR_UNSUPPORTED, "block K-WTA is not implemented on the batched path");
   if (m->info.use_genomic_norm)
     return set_error(GAJE_ERR_UNSUPPORTED, "use_genomic_norm is not implemented on the batched path");
+  if (m->nranks > 1) {
+    if (logits_out)
+      return set_error(GAJE_ERR_UNSUPPORTED, "a vocab-sharded model returns argmax only (no full-vocabulary logits)");
+    if (!m->nccl) return set_error(GAJE_ERR_CUDA, "the sharded group failed earlier; reload the model");
+  }
   const size_t S = size_t(m->max_streams);
   std::vector<char> seen(S, 0);
   for (size_t b = 0; b < B; ++b) {
@@ -1362,6 +1770,8 @@ int gaje_cuda_forward_batch(gaje_model* m, const uint32_t* stream_ids, const uin
     }
     CK(cudaGraphLaunch(ge, st));
   }
+  if (m->nranks > 1)  // the collective head: every rank's rows through this rank's vocab rows
+    if (int s = sharded_head(m, m->bx, Bi, m->bdev + 3 * S)) return s;
   const int kk = m->logits_k();
   if (logits_out && kk > 0)  // K-WTA on the returned logits (llm/forward.rs:58-61); the argmax is unaffected
     for (int b = 0; b < Bi; ++b) k_kwta<<<1, kKwtaThreads, 0, st>>>(m->blogits + size_t(b) * m->V, m->V, kk);
@@ -1369,7 +1779,11 @@ int gaje_cuda_forward_batch(gaje_model* m, const uint32_t* stream_ids, const uin
   if (logits_out)
     CK(cudaMemcpyAsync(logits_out, m->blogits, B * size_t(m->V) * 4, cudaMemcpyDeviceToHost, st));
   CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, st));
-  CK(cudaStreamSynchronize(st));
+  if (m->nranks > 1) {
+    if (int s = sync_sharded(m)) return s;
+  } else {
+    CK(cudaStreamSynchronize(st));
+  }
   for (size_t b = 0; b < B; ++b) m->bpos[stream_ids[b]] += 1u;
   if (argmax_out)
     for (size_t b = 0; b < B; ++b) argmax_out[b] = m->h_bdev[3 * S + b];
@@ -1389,9 +1803,15 @@ int gaje_cuda_prefill(gaje_model* m, uint32_t stream_id, const uint32_t* tokens,
     return set_error(GAJE_ERR_UNSUPPORTED, "use_genomic_norm is not implemented on the batched path");
   if (size_t(m->bpos[stream_id]) + n > size_t(m->max_ctx))
     return set_error(GAJE_ERR_CONTEXT, "KV cache would overflow (max_ctx positions)");
+  if (m->nranks > 1) {
+    if (logits_out)
+      return set_error(GAJE_ERR_UNSUPPORTED, "a vocab-sharded model returns argmax only (no full-vocabulary logits)");
+    if (!m->nccl) return set_error(GAJE_ERR_CUDA, "the sharded group failed earlier; reload the model");
+  }
   CK(cudaSetDevice(m->device));
   cudaStream_t st = m->stream;
   const size_t R = size_t(m->pf_rows);
+  int last_nc = 0;
   for (size_t c0 = 0; c0 < n; c0 += R) {
     const int nc = int(std::min(R, n - c0));
     const unsigned p0 = m->bpos[stream_id];
@@ -1404,14 +1824,21 @@ int gaje_cuda_prefill(gaje_model* m, uint32_t stream_id, const uint32_t* tokens,
     CK(cudaMemcpyAsync(m->pf_tab, m->h_pf_tab, 3 * R * sizeof(unsigned), cudaMemcpyHostToDevice, st));
     if (int s = launch_prefill_chunk(m, nc, int(p0), stream_id, c0 + size_t(nc) == n)) return s;
     m->bpos[stream_id] += unsigned(nc);
+    last_nc = nc;
   }
   const size_t S = size_t(m->max_streams);
+  if (m->nranks > 1)  // the collective head on the prompt's last row
+    if (int s = sharded_head(m, m->bx + size_t(last_nc - 1) * m->d, 1, m->bdev + 3 * S)) return s;
   const int kk = m->logits_k();
   if (logits_out && kk > 0) k_kwta<<<1, kKwtaThreads, 0, st>>>(m->blogits, m->V, kk);
   CK(cudaMemcpyAsync(m->h_bdev + 3 * S, m->bdev + 3 * S, sizeof(unsigned), cudaMemcpyDeviceToHost, st));
   if (logits_out) CK(cudaMemcpyAsync(logits_out, m->blogits, size_t(m->V) * 4, cudaMemcpyDeviceToHost, st));
   CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, st));
-  CK(cudaStreamSynchronize(st));
+  if (m->nranks > 1) {
+    if (int s = sync_sharded(m)) return s;
+  } else {
+    CK(cudaStreamSynchronize(st));
+  }
   if (argmax_out) *argmax_out = m->h_bdev[3 * S];
   return m->check_state();
 }
@@ -1432,6 +1859,7 @@ int gaje_cuda_stream_len(gaje_model* m, uint32_t stream_id, uint32_t* len) {
 
 int gaje_cuda_decode_greedy(gaje_model* m, uint32_t first_token, size_t n_steps, uint32_t* tokens_out) {
   if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  if (m->nranks > 1) return sharded_only();
   CK(cudaSetDevice(m->device));
   if (size_t(m->host_pos) + n_steps > size_t(m->max_ctx))
     return set_error(GAJE_ERR_CONTEXT, "KV cache would overflow (max_ctx positions)");
@@ -1451,6 +1879,7 @@ int gaje_cuda_decode_greedy(gaje_model* m, uint32_t first_token, size_t n_steps,
 int gaje_cuda_profile_steps(gaje_model* m, uint32_t first_token, size_t n_steps, float* ms,
                             uint32_t* launches) {
   if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  if (m->nranks > 1) return sharded_only();
   CK(cudaSetDevice(m->device));
   if (size_t(m->host_pos) + n_steps > size_t(m->max_ctx))
     return set_error(GAJE_ERR_CONTEXT, "KV cache would overflow (max_ctx positions)");
@@ -1518,6 +1947,7 @@ static int mega_stamped_run(gaje_model* m, uint32_t first_token, size_t n_steps,
 int gaje_cuda_profile_phases(gaje_model* m, uint32_t first_token, size_t n_steps, float* us, float* step_us,
                              float* detail_us) {
   if (!m) return set_error(GAJE_ERR_INVALID, "model is NULL");
+  if (m->nranks > 1) return sharded_only();
   if (n_steps == 0) return GAJE_OK;
   std::vector<unsigned long long> ts, tr;
   if (int s = mega_stamped_run(m, first_token, n_steps, detail_us != nullptr, ts, &tr)) return s;
@@ -1567,6 +1997,7 @@ int gaje_cuda_trace_steps(gaje_model* m, uint32_t first_token, size_t n_steps, u
                           size_t* n_written) {
   if (!m || !n_written || (out_len && !out)) return set_error(GAJE_ERR_INVALID, "NULL argument");
   *n_written = 0;
+  if (m->nranks > 1) return sharded_only();
   if (n_steps == 0) return GAJE_OK;
   const size_t need = size_t(m->sms) * n_steps * size_t(5 * m->L + 1) * kMkTrace;
   if (out_len < need) return set_error(GAJE_ERR_INVALID, "trace buffer too small: need grid*n_steps*(5L+1)*6 words");
@@ -1577,11 +2008,42 @@ int gaje_cuda_trace_steps(gaje_model* m, uint32_t first_token, size_t n_steps, u
   return GAJE_OK;
 }
 
+int gaje_cuda_trace_fused(gaje_model* m, uint32_t first_token, size_t n_steps, uint64_t* out, size_t out_len,
+                          size_t* n_written) {
+  if (!m || !n_written || (out_len && !out)) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  *n_written = 0;
+  if (!m->use_fused) return set_error(GAJE_ERR_UNSUPPORTED, "the model does not run the two-exchange kernel");
+  if (n_steps == 0 || n_steps > 4096) return set_error(GAJE_ERR_INVALID, "n_steps must be in 1..4096");
+  const size_t need = size_t(m->sms) * n_steps * size_t(m->L + 1) * kFuTrace;
+  if (out_len < need) return set_error(GAJE_ERR_INVALID, "out_len too small");
+  CK(cudaSetDevice(m->device));
+  if (size_t(m->host_pos) + n_steps > size_t(m->max_ctx))
+    return set_error(GAJE_ERR_CONTEXT, "KV cache would overflow (max_ctx positions)");
+  if (m->trace_ns_cap < need) {
+    if (m->trace_ns) cudaFree(m->trace_ns);
+    m->trace_ns = nullptr;
+    m->trace_ns_cap = 0;
+    CK(cudaMalloc(&m->trace_ns, need * sizeof(unsigned long long)));
+    m->trace_ns_cap = need;
+  }
+  CK(cudaMemsetAsync(m->trace_ns, 0, need * sizeof(unsigned long long), m->stream));
+  m->h_st->token = first_token;
+  CK(cudaMemcpyAsync(&m->st->token, &m->h_st->token, 4, cudaMemcpyHostToDevice, m->stream));
+  if (int s = m->run_fused(n_steps, m->trace_ns)) return s;
+  CK(cudaMemcpyAsync(out, m->trace_ns, need * sizeof(unsigned long long), cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  m->host_pos += uint32_t(n_steps);
+  *n_written = need;
+  return m->check_state();
+}
+
 int gaje_cuda_generate(gaje_model* m, const uint32_t* prompt, size_t n_prompt, size_t max_new,
                        float temperature, float rep_penalty, const uint32_t* eos, size_t n_eos,
                        uint32_t* out, size_t* n_out) {
   if (!m || !n_out || (n_prompt && !prompt) || (n_eos && !eos) || (max_new && !out))
     return set_error(GAJE_ERR_INVALID, "NULL argument");
+  if (m->nranks > 1) return sharded_only();
   *n_out = 0;
   if (n_prompt == 0) return set_error(GAJE_ERR_INVALID, "Prompt tokens cannot be empty");
   CK(cudaSetDevice(m->device));

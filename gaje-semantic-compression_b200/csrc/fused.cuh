@@ -1,0 +1,1016 @@
+// fused.cuh -- persistent batch-1 decode with two exchanges per block.
+//
+// The same step as k_decode_mega (GenomicLLM::forward_core,
+// src/nn/llm/forward.rs:7-63), restructured so that each transformer block
+// costs two all-to-all exchanges instead of five.  The five-exchange kernel
+// is latency-bound: every exchange through L2 costs 1.5-2.5 us of flag
+// latency plus a gather, and a 24-block model pays 121 of them per token.
+//
+// Per block l, with R the residual stream entering the block:
+//
+//   phase A  (the attention half)
+//     KV CTAs (2 * n_kv): attn_norm(R) -> this position's k (RoPE) or v rows
+//       of one KV head -> LL words for the attention CTAs + the cache row.
+//     attention CTAs (n_head * S): attn_norm(R) -> the q rows of one head
+//       (RoPE) -> split-K attention over 1/S of the cached positions (the
+//       last split also takes this position's k/v row) -> unnormalised
+//       output O_s with its (max m_s, sum l_s) -> the head's attn_output
+//       columns times O_s (a d-vector) -> after reading the (m, l) of the
+//       head's other splits, scaled by exp(m_s - M) / (L + 1e-12) and added
+//       into the accumulator YA with red.global.add.
+//   phase B  (the FFN half), every CTA with ffn K-blocks (32 SwiGLU outputs
+//     each): x_a = R + flush(YA) (+ bias); ffn_norm(x_a) -> its gate/up row
+//     pairs -> SwiGLU -> the ffn_down columns of those K-blocks times the 32
+//     outputs (a d-vector) -> red.global.add into YB.
+//   R' = x_a + flush(YB) (+ bias): every CTA forms it from the two sums.
+//
+// Because the attention output projection and the down projection are
+// linear, their inputs never have to be gathered: each CTA adds its
+// contribution to the d-vector sums, and the reference's |y| < 1e-6 flush
+// (genomic.rs:331-335) and bias are applied by the readers to the complete
+// sums.  The float sums are accumulated in arrival order, so results vary
+// from run to run at the rounding level (the parity bar is a tolerance).
+//
+// Exchanges: a CTA that finished its additions raises its flag (a barrier,
+// a gpu-scope fence, then the flag word); a reader polls the writers' flags
+// with one warp, fences, and reads the sums with L2 loads.  The (m, l) pairs
+// of the attention splits and this position's k/v rows travel as LL words
+// ({value, epoch}, self-validating).  The sums are double-buffered by block
+// parity and cleared by the attention CTAs two phases after their last read
+// (every reader of a buffer has raised a flag the clearing CTA waited for).
+//
+// Weights stream through a shared-memory ring (lane 0 of warp 15 is the
+// producer, 1-D TMA bulk copies, full/empty mbarriers) in this CTA's item
+// order: per block its q (or k/v) rows, its attn_output column blocks, then
+// per ffn K-block its gate/up rows and its ffn_down column block; then its
+// lm_head rows.  attn_output and ffn_down are kept a second time K-block
+// major (qsT[kb][row]) so that a CTA's columns are one contiguous run.  The
+// cached K/V rows of a split are fetched by TMA while the CTA waits for its
+// input.  Every wait is bounded (kWaitNs) and reported as DevState::err.
+#pragma once
+
+#include "megakernel.cuh"
+
+namespace gaje {
+
+constexpr int kFuThreads = 512;
+constexpr int kFuConsumerWarps = 15;
+constexpr int kFuConsumers = kFuConsumerWarps * 32;
+constexpr int kFuMaxSlots = 8;
+constexpr int kFuHeader = 1024;
+constexpr int kFuMaxSplits = 16;
+
+// attn_output and ffn_down of a block, K-block major: qs[kb][row], sm[kb][row].
+struct FuLayer {
+  const uint4* wo_qs;
+  const uint32_t* wo_sm;
+  const uint4* dn_qs;
+  const uint32_t* dn_sm;
+};
+
+struct FusedPlan {
+  int S;          // attention splits per q head
+  int nA;         // attention CTAs: n_head * S (CTAs [0, nA))
+  int nKV;        // k/v CTAs: 2 * n_kv (CTAs [nA, nA + nKV))
+  int cap;        // K/V rows one split holds: cached chunk + this position's row
+  int nslots;
+  unsigned slot_bytes;
+  int lm_rows_per_cta, lm_stage_rows;
+  int kb_max;     // ffn K-blocks of the busiest CTA
+  int pv_groups;  // position groups of the P*V partial sums
+};
+
+struct FusedArgs {
+  StepParams P;
+  const LayerW* layers;
+  const FuLayer* fl;
+  FusedPlan plan;
+  float* ya;      // [2][d] attention-projection sums
+  float* yb;      // [2][d] down-projection sums
+  uint2* flags;   // [2][grid]: phase A flags, phase B flags ({0, epoch})
+  uint2* kvnew;   // [2][nkv][hd] this position's k (rotated) and v rows
+  uint2* mlx;     // [nh][S][2] (m, l) of every split
+  uint2* tok;     // [1] the step's argmax
+  unsigned epoch0;
+  int n_steps;
+  unsigned long long* trace;  // optional [grid][n_steps][L+1][kFuTrace] %globaltimer stamps
+};
+
+// Trace points per block (phase A 0-8, phase B 9-14) and for the lm_head
+// (block index L: 0 entry, 1 input ready, 2 staged, 3 rows done, 4 token out).
+constexpr int kFuTrace = 16;
+
+__host__ __device__ inline unsigned fu_epoch(unsigned e0, int L, int step, int l, int ph) {
+  return e0 + unsigned(step) * unsigned(2 * L + 1) + unsigned(2 * l + ph) + 1u;
+}
+// ffn K-blocks of CTA c: count and first.  The remainder goes to the last CTAs
+// (those without attention work).
+__host__ __device__ inline void fu_kbs(int nkb, int grid, int c, int& kb0, int& n) {
+  const int base = nkb / grid, extra = nkb % grid, first_extra = grid - extra;
+  n = base + (c >= first_extra ? 1 : 0);
+  kb0 = c * base + (c > first_extra ? c - first_extra : 0);
+}
+// Cached positions of split s when `cached` positions precede this one.
+__host__ __device__ inline void fu_split(int cached, int S, int s, int& t0, int& n_old) {
+  const int chunk = (cached + S - 1) / S;
+  t0 = s * chunk;
+  n_old = max(0, min(chunk, cached - t0));
+}
+
+struct FuShared {
+  uint64_t* full;
+  uint64_t* empty;
+  uint64_t* kv_bar;
+  volatile int* abort_flag;
+  volatile int* issued;
+  volatile int* cabort;
+  volatile int* kv_armed;
+  volatile int* kv_waited;
+  float* R;      // [d] residual stream entering the block
+  float* XA;     // [d] x_a of the block
+  float* xs;     // [d] staged (normed, pre-scaled, swizzled) row-GEMV input
+  float* xsum;   // [d/32]
+  float* qbuf;   // [hd]
+  float* ps;     // [cap] scores, then exp
+  float* kvbuf;  // [cap][hd] K, then [cap][hd] V
+  float* pv;     // [pv_groups][hd]
+  float* ost;    // [hd] staged O_s, [hd/32] sums after it
+  float* araw;   // [kb_max*32] SwiGLU outputs
+  float* ast;    // [kb_max*32] staged, [kb_max] sums after it
+  float* misc;   // 64 floats: reductions, coefficients
+  unsigned char* slots;
+};
+
+__device__ __forceinline__ void fu_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kFuConsumers) : "memory"); }
+
+__device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+__device__ __forceinline__ float ld_rlx(const float* p) {
+  float v;
+  asm volatile("ld.relaxed.gpu.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_rlx(float* p, float v) {
+  asm volatile("st.relaxed.gpu.global.f32 [%0], %1;" ::"l"(p), "f"(v) : "memory");
+}
+
+// Sum (or max) over the consumer threads, the same value in every thread.
+// `red` holds 16 floats; consecutive calls must alternate buffers.
+__device__ __forceinline__ float fu_total(float v, float* red, bool is_max) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  v = is_max ? warp_max(v) : warp_sum(v);
+  if (lane == 0) red[wid] = v;
+  fu_sync();
+  float t = red[0];
+  for (int k = 1; k < kFuConsumerWarps; ++k) t = is_max ? fmaxf(t, red[k]) : t + red[k];
+  return t;
+}
+
+// Polls flags[0, n) until each carries epoch >= e (one warp, bounded), then a
+// gpu-scope fence; the other consumer warps wait at a named barrier.  False
+// (and the CTA's abort raised) when a flag did not come in time.
+__device__ __noinline__ bool fu_gate(const uint2* flags, int n, unsigned e, volatile int* cabort, DevState* st) {
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    bool ok = true;
+    for (int base = 0; base < n && ok; base += 32 * 8) {
+      uint2 w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const int i = base + lane + 32 * k;
+        w[k] = i < n ? ld_ll(flags + i) : make_uint2(0u, e);
+      }
+      unsigned long long t0 = 0;
+      for (;;) {
+        bool all = true;
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (int(w[k].y - e) < 0) {
+            all = false;
+            w[k] = ld_ll(flags + base + lane + 32 * k);
+          }
+        }
+        if (all) break;
+        const unsigned long long t = global_ns();
+        if (!t0) t0 = t;
+        else if (t - t0 > kWaitNs) {
+          ok = false;
+          break;
+        }
+      }
+    }
+    if (!__all_sync(0xffffffffu, ok) && lane == 0) {
+      flag_timeout(st, 20);
+      *cabort = 1;
+    }
+    fence_acq_rel_gpu();
+    __syncwarp();
+    bar_arrive_n(3);
+  } else {
+    bar_sync_n(3);
+  }
+  return !*cabort;
+}
+// End of a phase whose global writes (red.add, stores) readers wait for: a
+// consumer barrier, then thread 0 fences and raises this CTA's flag.
+__device__ __forceinline__ void fu_publish(uint2* flag, unsigned e) {
+  fu_sync();
+  if (threadIdx.x == 0) {
+    fence_acq_rel_gpu();
+    st_ll(flag, 0.f, e);
+  }
+}
+
+// Reads n LL words of epoch e (bounded) into dst (shared memory).
+__device__ __noinline__ bool fu_ll_read(const uint2* src, int n, unsigned e, float* dst) {
+  bool ok = true;
+  for (int i = threadIdx.x; i < n; i += kFuConsumers) {
+    uint2 w = ld_ll(src + i);
+    unsigned long long t0 = 0;
+    while (w.y != e) {
+      const unsigned long long t = global_ns();
+      if (!t0) t0 = t;
+      else if (t - t0 > kWaitNs) {
+        ok = false;
+        break;
+      }
+      w = ld_ll(src + i);
+    }
+    dst[i] = __uint_as_float(w.x);
+  }
+  return ok;
+}
+
+// ----------------------------------------------------------- producer
+struct FuItem {
+  const void* a;
+  const void* b;
+  uint32_t na, nb;
+};
+// The i-th weight item of this CTA within one block (-1 past the last).
+__device__ __forceinline__ bool fu_block_item(const FusedArgs& A, const LayerW& Lw, const FuLayer& F, int i,
+                                              FuItem& it) {
+  const StepParams& P = A.P;
+  const FusedPlan& pl = A.plan;
+  const int c = blockIdx.x, hd = P.hd, d = P.d;
+  int k = i;
+  const Q4View& Q = Lw.qkv;
+  if (c < pl.nA + pl.nKV) {
+    int row0;
+    if (c < pl.nA) {
+      row0 = (c / pl.S) * hd;
+    } else {
+      const int j = c - pl.nA, kv = j / P.nkv, g = j - kv * P.nkv;
+      row0 = (P.nh + kv * P.nkv + g) * hd;
+    }
+    if (k == 0) {
+      it.a = Q.qs + (size_t)row0 * Q.nb;
+      it.na = uint32_t(hd) * Q.nb * 16;
+      it.b = Q.sm + (size_t)row0 * Q.nbp;
+      it.nb = uint32_t(hd) * Q.nbp * 4;
+      return true;
+    }
+    --k;
+    if (c < pl.nA) {
+      if (k == 0) {
+        const int kb0 = (c / pl.S) * (hd / 32), n = hd / 32;
+        it.a = F.wo_qs + (size_t)kb0 * d;
+        it.na = uint32_t(n) * d * 16;
+        it.b = F.wo_sm + (size_t)kb0 * d;
+        it.nb = uint32_t(n) * d * 4;
+        return true;
+      }
+      --k;
+    }
+  }
+  int kb0, nkb;
+  fu_kbs(P.ff / 32, gridDim.x, c, kb0, nkb);
+  if (k >= 2 * nkb) return false;
+  const int kb = kb0 + k / 2;
+  if ((k & 1) == 0) {  // gate/up rows of the 32 SwiGLU outputs of kb
+    const Q4View& G = Lw.gate_up;
+    it.a = G.qs + (size_t)kb * 64 * G.nb;
+    it.na = 64u * G.nb * 16;
+    it.b = G.sm + (size_t)kb * 64 * G.nbp;
+    it.nb = 64u * G.nbp * 4;
+  } else {  // ffn_down column block kb
+    it.a = F.dn_qs + (size_t)kb * d;
+    it.na = uint32_t(d) * 16;
+    it.b = F.dn_sm + (size_t)kb * d;
+    it.nb = uint32_t(d) * 4;
+  }
+  return true;
+}
+
+__device__ void fu_producer(const FusedArgs& A, const FuShared& S) {
+  const StepParams& P = A.P;
+  const FusedPlan& pl = A.plan;
+  const int rbeg = blockIdx.x * pl.lm_rows_per_cta, rend = min(P.V, rbeg + pl.lm_rows_per_cta);
+  int item = 0;
+  for (int step = 0; step < A.n_steps; ++step) {
+    for (int l = 0; l <= P.n_layers; ++l) {
+      for (int i = 0;; ++i) {
+        FuItem it{nullptr, nullptr, 0u, 0u};
+        if (l < P.n_layers) {
+          if (!fu_block_item(A, A.layers[l], A.fl[l], i, it)) break;
+        } else {
+          const int r = rbeg + i * pl.lm_stage_rows;
+          if (r >= rend) break;
+          it.a = P.lm_head + (size_t)r * P.d;
+          it.na = uint32_t(min(pl.lm_stage_rows, rend - r)) * P.d * 4;
+        }
+        const int slot = item % pl.nslots;
+        if (item >= pl.nslots && !mbar_wait(S.empty + slot, ((item / pl.nslots) - 1) & 1)) {
+          flag_timeout(P.st, 21);
+          *S.abort_flag = 1;
+          return;
+        }
+        if (*S.abort_flag || *S.cabort) return;
+        unsigned char* dst = S.slots + (size_t)slot * pl.slot_bytes;
+        mbar_expect_tx(S.full + slot, it.na + it.nb);
+        bulk_g2s(dst, it.a, it.na, S.full + slot);
+        if (it.nb) bulk_g2s(dst + it.na, it.b, it.nb, S.full + slot);
+        ++item;
+        *S.issued = item;
+      }
+    }
+  }
+}
+
+// ----------------------------------------------------------- consumers
+__device__ __forceinline__ const unsigned char* fu_wait_slot(const FusedArgs& A, const FuShared& S, int item) {
+  const int slot = item % A.plan.nslots;
+  if (!*S.cabort && !*S.abort_flag && !mbar_wait(S.full + slot, (item / A.plan.nslots) & 1)) {
+    flag_timeout(A.P.st, 22);
+    *S.cabort = 1;
+  }
+  if (*S.abort_flag) *S.cabort = 1;
+  return S.slots + (size_t)slot * A.plan.slot_bytes;
+}
+__device__ __forceinline__ void fu_release(const FusedArgs& A, const FuShared& S, int item) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(S.empty + item % A.plan.nslots);
+}
+
+// Row pairs [0, nr/2) of a row-major Q4 item against the staged xs: a warp per
+// pair, lanes over the blocks; epi(p, y0, y1) on lane 0 with the raw dots.
+template <class Epi>
+__device__ __forceinline__ void fu_rows(const unsigned char* slot, int nr, int nb, int nbp, const float* xs,
+                                        const float* xsum, Epi&& epi) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const uint4* qs = reinterpret_cast<const uint4*>(slot);
+  const uint32_t* sm = reinterpret_cast<const uint32_t*>(slot + (size_t)nr * nb * 16);
+#pragma unroll 1
+  for (int p = wid; p < nr / 2; p += kFuConsumerWarps) {
+    const int r0 = 2 * p;
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 1
+    for (int b = lane; b < nb; b += 32) {
+      float A0, A1, sc, mn;
+      q4_pair_qx(qs[(size_t)r0 * nb + b], qs[(size_t)(r0 + 1) * nb + b], true, xs, b, A0, A1);
+      const float xb = xsum[b];
+      unpack_sm(sm[(size_t)r0 * nbp + b], sc, mn);
+      acc0 = fmaf(sc, A0, fmaf(mn, xb, acc0));
+      unpack_sm(sm[(size_t)(r0 + 1) * nbp + b], sc, mn);
+      acc1 = fmaf(sc, A1, fmaf(mn, xb, acc1));
+    }
+    acc0 = warp_sum(acc0);
+    acc1 = warp_sum(acc1);
+    if (lane == 0) epi(p, acc0, acc1);
+  }
+}
+
+// Rows 4t..4t+3 (t < d/4) of nkb K-block-major column blocks against the
+// staged xst/xsum (local block index): y[0..4) accumulates the raw dots.
+__device__ __forceinline__ void fu_cols(const unsigned char* slot, int d, int nkb, const float* xst,
+                                        const float* xsum, float (&y)[4]) {
+  const int t = threadIdx.x;
+  if (t >= d / 4) return;
+  const uint4* qs = reinterpret_cast<const uint4*>(slot);
+  const uint32_t* sm = reinterpret_cast<const uint32_t*>(slot + (size_t)nkb * d * 16);
+#pragma unroll 1
+  for (int kb = 0; kb < nkb; ++kb) {
+    const uint4* q = qs + (size_t)kb * d + 4 * t;
+    const uint4 s4 = *reinterpret_cast<const uint4*>(sm + (size_t)kb * d + 4 * t);
+    const float xb = xsum[kb];
+    float A0, A1, A2, A3, sc, mn;
+    q4_pair_qx(q[0], q[1], true, xst, kb, A0, A1);
+    q4_pair_qx(q[2], q[3], true, xst, kb, A2, A3);
+    unpack_sm(s4.x, sc, mn);
+    y[0] = fmaf(sc, A0, fmaf(mn, xb, y[0]));
+    unpack_sm(s4.y, sc, mn);
+    y[1] = fmaf(sc, A1, fmaf(mn, xb, y[1]));
+    unpack_sm(s4.z, sc, mn);
+    y[2] = fmaf(sc, A2, fmaf(mn, xb, y[2]));
+    unpack_sm(s4.w, sc, mn);
+    y[3] = fmaf(sc, A3, fmaf(mn, xb, y[3]));
+  }
+}
+
+// Issues the TMA copies of split s's cached K/V rows of block l at `cached`
+// preceding positions (thread 0 of the consumers).
+__device__ __forceinline__ void fu_kv_prefetch(const FusedArgs& A, const FuShared& S, int l, int cached) {
+  const StepParams& P = A.P;
+  const int c = blockIdx.x, h = c / A.plan.S, s = c - h * A.plan.S, g = h / (P.nh / P.nkv);
+  int t0, n_old;
+  fu_split(cached, A.plan.S, s, t0, n_old);
+  const uint32_t bytes = uint32_t(n_old) * P.hd * 4;
+  const LayerW& Lw = A.layers[l];
+  fence_acq_rel_gpu();
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  *S.kv_armed = *S.kv_armed + 1;
+  mbar_expect_tx(S.kv_bar, 2 * bytes);
+  if (bytes) {
+    bulk_g2s(S.kvbuf, Lw.kc + ((size_t)g * P.max_ctx + t0) * P.hd, bytes, S.kv_bar);
+    bulk_g2s(S.kvbuf + (size_t)A.plan.cap * P.hd, Lw.vc + ((size_t)g * P.max_ctx + t0) * P.hd, bytes, S.kv_bar);
+  }
+}
+
+// R (or x_a) + flush(sum) + bias for this thread's elements, from the sum
+// buffer (L2 loads).  With nan_layer >= 0 (one CTA) the down projection's NaN
+// guards of block/forward.rs:128-140 are raised.
+__device__ __noinline__ void fu_add_sum(float* dst, const float* base, const float* sum, const float* bias, int d,
+                                        DevState* st, unsigned pos, int nan_layer) {
+#pragma unroll 1
+  for (int i = threadIdx.x; i < d; i += kFuConsumers) {
+    float y = flush_small(ld_rlx(sum + i));
+    if (bias) y += __ldg(bias + i);
+    const float v = base[i] + y;
+    if (nan_layer >= 0) {
+      if (y != y) nan_flag(st, pos, nan_layer, kNanProjFfn);
+      if (v != v) nan_flag(st, pos, nan_layer, kNanResidual);
+    }
+    dst[i] = v;
+  }
+}
+
+// Stages x * w (w nullable) into xs/xsum for the row GEMVs and returns
+// 1/rms of x (the scale of the finished row dots), with the block-input and
+// normed-output NaN guards of block/forward.rs:11-13, :22-24 when guard.
+__device__ __noinline__ float fu_stage_norm(const float* x, const float* w, int d, float eps, float* xs, float* xsum,
+                                            float* red, bool guard, DevState* st, unsigned pos, int layer) {
+  float ss = 0.f;
+#pragma unroll 1
+  for (int i = threadIdx.x; i < d; i += kFuConsumers) {  // whole warps: d % 32 == 0
+    const float v = x[i];
+    ss = fmaf(v, v, ss);
+    mk_stage_elem(xs, xsum, i, w ? v * __ldg(w + i) : v);
+  }
+  const float tot = fu_total(ss, red, false);
+  const float inv = 1.0f / sqrtf(tot / (float)d + eps);
+  if (guard)
+    for (int i = threadIdx.x; i < d; i += kFuConsumers) {
+      const float v = x[i];
+      if (v != v) nan_flag(st, pos, layer, kNanInput);
+      const float nv = (v * inv) * (w ? __ldg(w + i) : 1.f);
+      if (nv != nv) nan_flag(st, pos, layer, kNanAttnNorm);
+    }
+  return inv;
+}
+
+// The step's token: DevState::token for the first step of a launch, else the
+// previous step's LL token word.
+__device__ __forceinline__ bool fu_token(const FusedArgs& A, int step, unsigned& tok) {
+  if (step == 0) {
+    tok = __ldcg(&A.P.st->token);
+    return true;
+  }
+  const unsigned e = fu_epoch(A.epoch0, A.P.n_layers, step - 1, A.P.n_layers, 0);
+  uint2 w = ld_ll(A.tok);
+  unsigned long long t0 = 0;
+  while (w.y != e) {
+    const unsigned long long t = global_ns();
+    if (!t0) t0 = t;
+    else if (t - t0 > kWaitNs) return false;
+    w = ld_ll(A.tok);
+  }
+  tok = w.x;
+  return true;
+}
+
+__device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
+  const StepParams& P = A.P;
+  const FusedPlan& pl = A.plan;
+  DevState* st = P.st;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, c = blockIdx.x;
+  const int L = P.n_layers, d = P.d, hd = P.hd, half = hd >> 1, G = gridDim.x;
+  const bool roleA = c < pl.nA, roleKV = !roleA && c < pl.nA + pl.nKV;
+  const int h = roleA ? c / pl.S : 0, sp = roleA ? c - h * pl.S : 0;
+  const int kvj = roleKV ? c - pl.nA : 0, kvk = kvj / P.nkv, kvg = kvj - kvk * P.nkv;
+  int kb0, nkb;
+  fu_kbs(P.ff / 32, G, c, kb0, nkb);
+  uint2* flA = A.flags;
+  uint2* flB = A.flags + G;
+  float* red0 = S.misc;
+  float* red1 = S.misc + 16;
+  float* coef = S.misc + 32;
+  int item = 0;
+  const unsigned pos0 = __ldcg(&st->pos);
+  auto fmark = [&](int step, int l, int k) {
+    if (A.trace && tid == 0)
+      A.trace[(((size_t)c * A.n_steps + step) * (L + 1) + l) * kFuTrace + k] = global_ns();
+  };
+  // first K/V prefetch (step 0, block 0)
+  if (roleA && tid == 0) fu_kv_prefetch(A, S, 0, int(pos0));
+  for (int step = 0; step < A.n_steps; ++step) {
+    const unsigned pos = pos0 + unsigned(step);
+    unsigned tok = 0;
+    bool have_tok = false;
+    for (int l = 0; l < L; ++l) {
+      const LayerW& Lw = A.layers[l];
+      const int gl = step * L + l;
+      const unsigned eA = fu_epoch(A.epoch0, L, step, l, 0), eB = eA + 1u;
+      float* ya = A.ya + (gl & 1) * d;
+      float* yb = A.yb + (gl & 1) * d;
+      const float* yb_prev = A.yb + ((gl + 1) & 1) * d;  // YB of block l-1
+      const LayerW* Lp = l > 0 ? &A.layers[l - 1] : nullptr;
+      // ============================================================ phase A
+      if (roleA || roleKV) {
+        bool ok = true;
+        fmark(step, l, 0);
+        if (l == 0) {
+          ok = fu_token(A, step, tok);
+          have_tok = true;
+          if (!ok) {
+            flag_timeout(st, 23);
+            *S.cabort = 1;
+          }
+          fu_sync();
+          if (*S.cabort) return;
+          const float* src = P.embd + (size_t)(tok % (unsigned)P.V) * d;  // get_row_core: row token % V
+          for (int i = tid; i < d; i += kFuConsumers) S.R[i] = __ldg(src + i);
+        } else {
+          if (!fu_gate(flB, G, eB - 2u, S.cabort, st)) return;
+          fu_add_sum(S.R, S.XA, yb_prev, Lp->down.bias, d, st, pos, c == 0 ? l - 1 : -1);
+        }
+        if (roleA) {  // clear the sums read two phases ago: YA of block l-1, YB of block l-2
+          const int per = (d + pl.nA - 1) / pl.nA;
+          for (int i = tid; i < per; i += kFuConsumers) {
+            const int j = c * per + i;
+            if (j < d) {
+              st_rlx(A.ya + ((gl + 1) & 1) * d + j, 0.f);
+              st_rlx(yb + j, 0.f);
+            }
+          }
+        }
+        if (L == 1 && roleA && tid == 0 && step > 0) fu_kv_prefetch(A, S, 0, int(pos));
+        fu_sync();
+        fmark(step, l, 1);
+        const float inv = fu_stage_norm(S.R, Lw.attn_norm, d, P.eps, S.xs, S.xsum, red0, c == 0, st, pos, l);
+        fmark(step, l, 2);
+        const float2* rope = P.rope + (size_t)pos * half;
+        const Q4View& Q = Lw.qkv;
+        const unsigned char* slot = fu_wait_slot(A, S, item);
+        fu_sync();
+        if (*S.cabort) return;
+        if (roleKV) {
+          // this position's k (kvk = 0, rotated) or v (kvk = 1) rows of KV head kvg
+          const int row0 = (P.nh + kvk * P.nkv + kvg) * hd;
+          uint2* dst = A.kvnew + (size_t)(kvk * P.nkv + kvg) * hd;
+          float* cache = (kvk ? Lw.vc : Lw.kc) + ((size_t)kvg * P.max_ctx + pos) * hd;
+          fu_rows(slot, hd, Q.nb, Q.nbp, S.xs, S.xsum, [&](int p, float y0, float y1) {
+            y0 = flush_small(y0 * inv);
+            y1 = flush_small(y1 * inv);
+            if (Q.bias) {
+              y0 += __ldg(Q.bias + row0 + 2 * p);
+              y1 += __ldg(Q.bias + row0 + 2 * p + 1);
+            }
+            if (kvk == 0) {  // RoPE: v0*cos - v1*sin, v0*sin + v1*cos
+              const float2 cs = __ldg(rope + p);
+              const float o0 = y0 * cs.x - y1 * cs.y, o1 = y0 * cs.y + y1 * cs.x;
+              y0 = o0;
+              y1 = o1;
+            }
+            const int c0 = P.rope_split ? p : 2 * p, c1 = P.rope_split ? p + half : 2 * p + 1;
+            cache[c0] = y0;
+            cache[c1] = y1;
+            st_ll(dst + c0, y0, eA);
+            st_ll(dst + c1, y1, eA);
+          });
+          fu_release(A, S, item++);
+          fmark(step, l, 3);
+        } else {
+          // ---- q rows of head h (RoPE), into qbuf
+          const int row0 = h * hd;
+          fu_rows(slot, hd, Q.nb, Q.nbp, S.xs, S.xsum, [&](int p, float y0, float y1) {
+            y0 = flush_small(y0 * inv);
+            y1 = flush_small(y1 * inv);
+            if (Q.bias) {
+              y0 += __ldg(Q.bias + row0 + 2 * p);
+              y1 += __ldg(Q.bias + row0 + 2 * p + 1);
+            }
+            const float2 cs = __ldg(rope + p);
+            const int c0 = P.rope_split ? p : 2 * p, c1 = P.rope_split ? p + half : 2 * p + 1;
+            S.qbuf[c0] = y0 * cs.x - y1 * cs.y;
+            S.qbuf[c1] = y0 * cs.y + y1 * cs.x;
+          });
+          fu_release(A, S, item++);
+          fmark(step, l, 3);
+          // ---- attention over this split's positions
+          int t0, n_old;
+          fu_split(int(pos), pl.S, sp, t0, n_old);
+          const bool last = sp == pl.S - 1;
+          const int n = n_old + (last ? 1 : 0);
+          float* Ks = S.kvbuf;
+          float* Vs = S.kvbuf + (size_t)pl.cap * hd;
+          const int g = h / (P.nh / P.nkv);
+          if (last) {
+            ok = fu_ll_read(A.kvnew + (size_t)g * hd, hd, eA, Ks + (size_t)n_old * hd) &&
+                 fu_ll_read(A.kvnew + (size_t)(P.nkv + g) * hd, hd, eA, Vs + (size_t)n_old * hd);
+          }
+          const int use = *S.kv_waited;
+          if (ok && !*S.cabort && !mbar_wait(S.kv_bar, use & 1)) ok = false;
+          if (!ok) {
+            flag_timeout(st, 24);
+            *S.cabort = 1;
+          }
+          fu_sync();
+          if (*S.cabort) return;
+          if (tid == 0) *S.kv_waited = use + 1;
+          fmark(step, l, 4);
+          const int H4 = hd >> 2;
+          float m = -INFINITY;
+#pragma unroll 1
+          for (int t = tid; t < n; t += kFuConsumers) {
+            const float4* kr = reinterpret_cast<const float4*>(Ks + (size_t)t * hd);
+            const float4* qr = reinterpret_cast<const float4*>(S.qbuf);
+            float a0 = 0.f, a1 = 0.f;
+            int cc = t % H4;  // rotated start: conflict-free rows
+#pragma unroll 4
+            for (int k = 0; k < H4; ++k) {
+              const float4 kk = kr[cc], qq = qr[cc];
+              a0 = fmaf(qq.x, kk.x, a0);
+              a1 = fmaf(qq.y, kk.y, a1);
+              a0 = fmaf(qq.z, kk.z, a0);
+              a1 = fmaf(qq.w, kk.w, a1);
+              cc = cc + 1 == H4 ? 0 : cc + 1;
+            }
+            const float sc = (a0 + a1) * P.attn_scale;
+            S.ps[t] = sc;
+            m = fmaxf(m, sc);
+          }
+          m = fu_total(m, red0, true);
+          float lsum = 0.f;
+          for (int t = tid; t < n; t += kFuConsumers) {
+            const float ev = expf(S.ps[t] - m);
+            S.ps[t] = ev;
+            lsum += ev;
+          }
+          lsum = fu_total(lsum, red1, false);  // also publishes ps
+          if (tid == 0 && n > 0) {             // (m, l) of this split
+            uint2* ml = A.mlx + ((size_t)h * pl.S + sp) * 2;
+            st_ll(ml, m, eA);
+            st_ll(ml + 1, lsum, eA);
+          }
+          // P*V: position groups j of e-columns, summed in group order
+          {
+            const int J = pl.pv_groups;
+            if (tid < J * hd) {
+              const int e = tid % hd, j = tid / hd;
+              float o = 0.f;
+#pragma unroll 4
+              for (int t = j; t < n; t += J) o = fmaf(S.ps[t], Vs[(size_t)t * hd + e], o);
+              S.pv[j * hd + e] = o;
+            }
+            fu_sync();
+            // K/V buffer free: prefetch the next block's (or next step's) rows
+            if (tid == 0) {
+              if (l + 1 < L) fu_kv_prefetch(A, S, l + 1, int(pos));
+              else if (step + 1 < A.n_steps && L > 1) fu_kv_prefetch(A, S, 0, int(pos) + 1);
+            }
+            if (tid < hd) {
+              float o = 0.f;
+              for (int j = 0; j < J; ++j) o += S.pv[j * hd + tid];
+              S.pv[tid] = o;  // group 0 is read only by this thread
+            }
+            fu_sync();
+            for (int i = tid; i < hd; i += kFuConsumers) mk_stage_elem(S.ost, S.ost + hd, i, S.pv[i]);
+            fu_sync();
+            fmark(step, l, 5);
+          }
+          // ---- attn_output columns of head h times O_s
+          const unsigned char* wslot = fu_wait_slot(A, S, item);
+          fu_sync();
+          if (*S.cabort) return;
+          float y[4] = {0.f, 0.f, 0.f, 0.f};
+          if (n > 0) fu_cols(wslot, d, hd / 32, S.ost, S.ost + hd, y);
+          fu_release(A, S, item++);
+          fmark(step, l, 6);
+          // ---- the head's split weights: exp(m_s - M) / (sum_s exp(m_s - M) l_s + 1e-12)
+          if (wid == 0) {
+            const uint2* ml = A.mlx + (size_t)h * pl.S * 2;
+            float ms = -INFINITY, ls = 0.f;
+            bool good = true;
+            if (lane < pl.S) {
+              int t0s, nos;
+              fu_split(int(pos), pl.S, lane, t0s, nos);
+              if (nos + (lane == pl.S - 1 ? 1 : 0) > 0) {  // splits without positions publish nothing
+                uint2 wm = ld_ll(ml + 2 * lane), wl = ld_ll(ml + 2 * lane + 1);
+                unsigned long long tw = 0;
+                while (wm.y != eA || wl.y != eA) {
+                  const unsigned long long t = global_ns();
+                  if (!tw) tw = t;
+                  else if (t - tw > kWaitNs) {
+                    good = false;
+                    break;
+                  }
+                  wm = ld_ll(ml + 2 * lane);
+                  wl = ld_ll(ml + 2 * lane + 1);
+                }
+                ms = __uint_as_float(wm.x);
+                ls = __uint_as_float(wl.x);
+              }
+            }
+            if (!__all_sync(0xffffffffu, good) && lane == 0) {
+              flag_timeout(st, 25);
+              *S.cabort = 1;
+            }
+            const float M = warp_max(ms);
+            float wsum = 0.f;
+            for (int k = 0; k < pl.S; ++k) {  // split order
+              const float mk = __shfl_sync(0xffffffffu, ms, k), lk = __shfl_sync(0xffffffffu, ls, k);
+              if (mk > -INFINITY) wsum = fmaf(expf(mk - M), lk, wsum);
+            }
+            if (lane == 0) coef[0] = n > 0 ? expf(m - M) / (wsum + 1e-12f) : 0.f;
+          }
+          fu_sync();
+          if (*S.cabort) return;
+          const float cf = coef[0];
+          fmark(step, l, 7);
+          if (n > 0 && tid < d / 4) red_add4(ya + 4 * tid, cf * y[0], cf * y[1], cf * y[2], cf * y[3]);
+          fu_publish(flA + c, eA);
+          fmark(step, l, 8);
+        }
+      }
+      // ============================================================ phase B
+      if (!fu_gate(flA, pl.nA, eA, S.cabort, st)) return;
+      fmark(step, l, 9);
+      if (!(roleA || roleKV)) {  // R of this block from the sums of the previous one
+        if (l == 0) {
+          if (!have_tok) {
+            if (!fu_token(A, step, tok)) {
+              flag_timeout(st, 23);
+              *S.cabort = 1;
+            }
+            have_tok = true;
+          }
+          const float* src = P.embd + (size_t)(tok % (unsigned)P.V) * d;
+          for (int i = tid; i < d; i += kFuConsumers) S.R[i] = __ldg(src + i);
+        } else {
+          fu_add_sum(S.R, S.XA, yb_prev, Lp->down.bias, d, st, pos, -1);
+        }
+        fu_sync();
+      }
+      fu_add_sum(S.XA, S.R, ya, Lw.wo.bias, d, st, pos, -1);
+      fu_sync();
+      if (*S.cabort) return;
+      fmark(step, l, 10);
+      if (nkb > 0) {
+        const float inv = fu_stage_norm(S.XA, Lw.ffn_norm, d, P.eps, S.xs, S.xsum, red0, false, st, pos, l);
+        fmark(step, l, 11);
+        const Q4View& Gu = Lw.gate_up;
+        float y[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 1
+        for (int k = 0; k < nkb; ++k) {
+          const int kb = kb0 + k;
+          const unsigned char* gslot = fu_wait_slot(A, S, item);
+          fu_sync();
+          if (*S.cabort) return;
+          fu_rows(gslot, 64, Gu.nb, Gu.nbp, S.xs, S.xsum, [&](int p, float g0, float u0) {
+            const int u = kb * 32 + p;
+            float gv = flush_small(g0 * inv), uv = flush_small(u0 * inv);
+            if (Gu.bias) {
+              gv += __ldg(Gu.bias + 2 * u);
+              uv += __ldg(Gu.bias + 2 * u + 1);
+            }
+            if (uv != uv) nan_flag(st, pos, l, kNanUp);
+            const float a = swiglu_balanced(gv, uv);
+            if (a != a) nan_flag(st, pos, l, kNanFfnOut);
+            S.araw[k * 32 + p] = a;
+          });
+          fu_release(A, S, item++);
+          fu_sync();
+          if (k == 0) fmark(step, l, 12);
+          if (wid == 0) mk_stage_elem(S.ast, S.ast + pl.kb_max * 32, k * 32 + lane, S.araw[k * 32 + lane]);
+          const unsigned char* dslot = fu_wait_slot(A, S, item);
+          fu_sync();
+          if (*S.cabort) return;
+          // one column block: local block index k of the staged outputs
+          {
+            const int t = tid;
+            if (t < d / 4) {
+              const uint4* qs = reinterpret_cast<const uint4*>(dslot) + 4 * t;
+              const uint4 s4 = *reinterpret_cast<const uint4*>(dslot + (size_t)d * 16 + 16 * t);
+              const float xb = S.ast[pl.kb_max * 32 + k];
+              float A0, A1, A2, A3, sc, mn;
+              q4_pair_qx(qs[0], qs[1], true, S.ast, k, A0, A1);
+              q4_pair_qx(qs[2], qs[3], true, S.ast, k, A2, A3);
+              unpack_sm(s4.x, sc, mn);
+              y[0] = fmaf(sc, A0, fmaf(mn, xb, y[0]));
+              unpack_sm(s4.y, sc, mn);
+              y[1] = fmaf(sc, A1, fmaf(mn, xb, y[1]));
+              unpack_sm(s4.z, sc, mn);
+              y[2] = fmaf(sc, A2, fmaf(mn, xb, y[2]));
+              unpack_sm(s4.w, sc, mn);
+              y[3] = fmaf(sc, A3, fmaf(mn, xb, y[3]));
+            }
+          }
+          fu_release(A, S, item++);
+        }
+        fmark(step, l, 13);
+        if (tid < d / 4) red_add4(yb + 4 * tid, y[0], y[1], y[2], y[3]);
+      }
+      fu_publish(flB + c, eB);
+      fmark(step, l, 14);
+    }
+    // ================================================================ LM
+    {
+      const unsigned eLastB = fu_epoch(A.epoch0, L, step, L - 1, 1);
+      fmark(step, L, 0);
+      if (!fu_gate(flB, G, eLastB, S.cabort, st)) return;
+      fmark(step, L, 1);
+      const int gl = step * L + L - 1;
+      fu_add_sum(S.R, S.XA, A.yb + (gl & 1) * d, A.layers[L - 1].down.bias, d, st, pos, c == 0 ? L - 1 : -1);
+      fu_sync();
+      float ss = 0.f;
+      for (int i = tid; i < d; i += kFuConsumers) {
+        const float v = S.R[i];
+        ss = fmaf(v, v, ss);
+        S.xs[i] = v * __ldg(P.out_norm + i);
+      }
+      const float scale = 1.0f / sqrtf(fu_total(ss, red0, false) / (float)d + P.eps);
+      fmark(step, L, 2);
+      const float4* x4 = reinterpret_cast<const float4*>(S.xs);
+      const int K4 = d >> 2;
+      unsigned long long best = 0ull;
+      const int rbeg = c * pl.lm_rows_per_cta;
+      const int nrows = max(0, min(P.V, rbeg + pl.lm_rows_per_cta) - rbeg);
+      const int nitems = (nrows + pl.lm_stage_rows - 1) / pl.lm_stage_rows;
+      int cur = -1;
+      const unsigned char* slot = nullptr;
+#pragma unroll 1
+      for (int k = wid; k < nrows; k += kFuConsumerWarps) {
+        const int it = k / pl.lm_stage_rows;
+        while (cur < it) {
+          if (cur >= 0) fu_release(A, S, item + cur);
+          ++cur;
+          slot = fu_wait_slot(A, S, item + cur);
+        }
+        const float4* w4 = reinterpret_cast<const float4*>(slot) + (size_t)(k - it * pl.lm_stage_rows) * K4;
+        float a0 = 0.f, a1 = 0.f;
+#pragma unroll 2
+        for (int j = lane; j < K4; j += 32) {
+          const float4 u = w4[j], xv = x4[j];
+          a0 = fmaf(u.x, xv.x, a0);
+          a1 = fmaf(u.y, xv.y, a1);
+          a0 = fmaf(u.z, xv.z, a0);
+          a1 = fmaf(u.w, xv.w, a1);
+        }
+        const int row = rbeg + k;
+        float v = warp_sum(a0 + a1) * scale;
+        if (P.lm_bias) v += __ldg(P.lm_bias + row);
+        if (lane == 0) P.logits[row] = v;
+        const unsigned long long key = amax_key(v, (unsigned)row);
+        best = key > best ? key : best;
+      }
+      while (cur < nitems - 1) {
+        if (cur >= 0) fu_release(A, S, item + cur);
+        ++cur;
+        fu_wait_slot(A, S, item + cur);
+      }
+      if (cur >= 0) fu_release(A, S, item + cur);
+      item += nitems;
+      fmark(step, L, 3);
+      best = warp_max_u64(best);
+      __shared__ unsigned long long wbest[kFuConsumerWarps];
+      __shared__ int is_last;
+      if (lane == 0) wbest[wid] = best;
+      fu_sync();
+      if (*S.cabort) return;
+      if (tid == 0) {
+        unsigned long long b = 0;
+        for (int i = 0; i < kFuConsumerWarps; ++i) b = wbest[i] > b ? wbest[i] : b;
+        P.amax_part[c] = b;
+        __threadfence();
+        is_last = (atomicAdd(P.amax_cnt, 1u) == unsigned(G) - 1u);
+      }
+      fu_sync();
+      if (is_last) {
+        __threadfence();
+        unsigned long long b = 0;
+        for (int i = tid; i < G; i += kFuConsumers) {
+          const unsigned long long v = __ldcg(P.amax_part + i);
+          b = v > b ? v : b;
+        }
+        b = warp_max_u64(b);
+        if (lane == 0) wbest[wid] = b;
+        fu_sync();
+        if (tid == 0) {
+          unsigned long long r = 0;
+          for (int i = 0; i < kFuConsumerWarps; ++i) r = wbest[i] > r ? wbest[i] : r;
+          const unsigned idx = amax_index(r);
+          st->argmax = idx;
+          st->token = idx;
+          if (st->hist_len < P.hist_cap) P.tok_hist[st->hist_len] = idx;
+          st->hist_len += 1u;
+          st->pos = pos + 1u;
+          *P.amax_cnt = 0u;
+          fence_acq_rel_gpu();  // the state and the counter reset before the token word
+          st_ll(A.tok, __uint_as_float(idx), fu_epoch(A.epoch0, L, step, L, 0));
+        }
+      }
+      fu_sync();
+      fmark(step, L, 4);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kFuThreads, 1) k_decode_fused(FusedArgs A) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const FusedPlan& pl = A.plan;
+  const int d = A.P.d, hd = A.P.hd;
+  FuShared S;
+  S.full = reinterpret_cast<uint64_t*>(smem_raw);
+  S.empty = S.full + kFuMaxSlots;
+  S.kv_bar = S.empty + kFuMaxSlots;
+  S.abort_flag = reinterpret_cast<volatile int*>(S.kv_bar + 1);
+  S.issued = S.abort_flag + 1;
+  S.cabort = S.abort_flag + 2;
+  S.kv_armed = S.abort_flag + 3;
+  S.kv_waited = S.abort_flag + 4;
+  float* f = reinterpret_cast<float*>(smem_raw + kFuHeader);
+  S.R = f;
+  f += d;
+  S.XA = f;
+  f += d;
+  S.xs = f;
+  f += d;
+  S.xsum = f;
+  f += mk_round32(d / 32);
+  S.qbuf = f;
+  f += hd;
+  S.ps = f;
+  f += mk_round32(pl.cap);
+  S.kvbuf = f;
+  f += 2 * (size_t)pl.cap * hd;
+  S.pv = f;
+  f += (size_t)pl.pv_groups * hd;
+  S.ost = f;
+  f += hd + 32;
+  S.araw = f;
+  f += pl.kb_max * 32;
+  S.ast = f;
+  f += pl.kb_max * 32 + 32;
+  S.misc = f;
+  f += 64;
+  S.slots = reinterpret_cast<unsigned char*>(f);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < pl.nslots; ++i) {
+      mbar_init(S.full + i, 1);
+      mbar_init(S.empty + i, kFuConsumerWarps);
+    }
+    mbar_init(S.kv_bar, 1);
+    *S.abort_flag = 0;
+    *S.issued = 0;
+    *S.cabort = 0;
+    *S.kv_armed = 0;
+    *S.kv_waited = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x >= kFuConsumers) {
+    if (threadIdx.x == kFuConsumers) {
+      fu_producer(A, S);
+      const int issued = *S.issued;  // every issued copy lands before the CTA exits
+      for (int it = max(0, issued - pl.nslots); it < issued; ++it)
+        mbar_wait(S.full + it % pl.nslots, (it / pl.nslots) & 1);
+    }
+    return;
+  }
+  fu_consumer(A, S);
+  // a K/V copy may still be in flight (the last prefetch, or an abort): it must land first
+  if (threadIdx.x == 0 && *S.kv_armed > *S.kv_waited) mbar_wait(S.kv_bar, (*S.kv_waited) & 1);
+}
+
+// Dynamic shared memory of the fused kernel.
+__host__ __device__ inline size_t fused_smem_bytes(const FusedPlan& p, int d, int hd) {
+  const size_t floats = size_t(3) * d + mk_round32(d / 32) + hd + mk_round32(p.cap) + size_t(2) * p.cap * hd +
+                        size_t(p.pv_groups) * hd + hd + 32 + size_t(p.kb_max) * 64 + 32 + 64;
+  return kFuHeader + floats * 4 + size_t(p.nslots) * p.slot_bytes;
+}
+
+// K-block-major copy of a row-major Q4 matrix: qsT[kb][row] = qs[row][kb],
+// smT[kb][row] = sm[row][kb].
+__global__ void k_q4_kbmajor(Q4View W, uint4* qsT, uint32_t* smT) {
+  const size_t n = (size_t)W.N * W.nb;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const int kb = int(i / W.N), row = int(i - (size_t)kb * W.N);
+    qsT[i] = W.qs[(size_t)row * W.nb + kb];
+    smT[i] = W.sm[(size_t)row * W.nbp + kb];
+  }
+}
+
+}  // namespace gaje

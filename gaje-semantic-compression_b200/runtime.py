@@ -96,7 +96,11 @@ class ModelInfo(C.Structure):
                 ("n_head_kv", C.c_uint32), ("n_blocks", C.c_uint32), ("head_dim", C.c_uint32),
                 ("ffn_dim", C.c_uint32), ("max_ctx", C.c_uint32), ("cache_len", C.c_uint32),
                 ("eps", C.c_float), ("rope_base", C.c_float), ("k_wta_ratio", C.c_float),
-                ("device_bytes", C.c_size_t), ("grid", C.c_uint32), ("megakernel", C.c_uint32)]
+                ("device_bytes", C.c_size_t), ("grid", C.c_uint32), ("megakernel", C.c_uint32),
+                ("nranks", C.c_uint32), ("rank", C.c_uint32), ("vocab_row0", C.c_uint32),
+                ("vocab_rows", C.c_uint32)]
+
+NCCL_ID_BYTES = 128
 
 
 _lib = None
@@ -137,6 +141,7 @@ def lib() -> C.CDLL:
         "gaje_cuda_profile_steps": ([vp, u32, sz, vp, vp], i32),
         "gaje_cuda_profile_phases": ([vp, u32, sz, vp, vp, vp], i32),
         "gaje_cuda_trace_steps": ([vp, u32, sz, vp, sz, vp], i32),
+        "gaje_cuda_trace_fused": ([vp, u32, sz, vp, sz, vp], i32),
         "gaje_cuda_attention_decode_static": ([vp, vp, vp, sz, sz, sz, sz, sz, vp, vp], i32),
         "gaje_cuda_forward_batch": ([vp, vp, vp, sz, vp, vp], i32),
         "gaje_cuda_prefill": ([vp, u32, vp, sz, vp, vp], i32),
@@ -150,6 +155,11 @@ def lib() -> C.CDLL:
         "gaje_cuda_rms_norm": ([vp, vp, f32, sz, vp, vp], i32),
         "gaje_cuda_attention_decode": ([vp, vp, vp, sz, sz, sz, sz, sz, vp, vp], i32),
         "gaje_cuda_kwta": ([vp, sz, sz, vp], i32),
+        "gaje_cuda_nccl_unique_id": ([vp], i32),
+        "gaje_cuda_load_sharded": ([C.c_char_p, C.POINTER(LoadOpts), i32, i32, vp], vp),
+        "gaje_vocab_shard": ([u32, i32, i32, C.POINTER(u32), C.POINTER(u32)], i32),
+        "gaje_argmax_key": ([f32, u32], u64),
+        "gaje_argmax_key_index": ([u64], u32),
     }
     for name, (args, res) in sig.items():
         fn = getattr(L, name)
@@ -266,14 +276,19 @@ class GenomicLLM:
 
     def __init__(self, path: str, device: int = 0, max_ctx: int = 4096, seed: int = 0,
                  use_graph: bool = True, use_megakernel: bool = True, max_streams: int = 0,
-                 max_prefill: int = 0):
+                 max_prefill: int = 0, shard: Optional[tuple] = None):
         opts = LoadOpts()
         lib().gaje_load_opts_init(C.byref(opts))
         opts.device, opts.max_ctx, opts.seed, opts.use_graph = device, max_ctx, seed, int(use_graph)
         opts.use_megakernel = int(use_megakernel)
         opts.max_streams = int(max_streams)
         opts.max_prefill = int(max_prefill)
-        self._m = lib().gaje_cuda_load(path.encode(), C.byref(opts))
+        if shard is None:
+            self._m = lib().gaje_cuda_load(path.encode(), C.byref(opts))
+        else:  # (nranks, rank, nccl_id): one rank of a vocab-sharded group (collective)
+            nranks, rank, nid = shard
+            idb = C.create_string_buffer(bytes(nid), NCCL_ID_BYTES)
+            self._m = lib().gaje_cuda_load_sharded(path.encode(), C.byref(opts), int(nranks), int(rank), idb)
         if not self._m:
             raise GajeIOError(2, last_error())
         info = self.info()
@@ -424,6 +439,17 @@ class GenomicLLM:
                                            C.byref(n)))
         return out
 
+    def trace_fused(self, first_token: int, n_steps: int) -> np.ndarray:
+        """The two-exchange kernel's trace stamps (ns) of n_steps greedy steps in
+        one launch: shape [grid, n_steps, n_blocks+1, 16] (see
+        gaje_cuda_trace_fused for the points)."""
+        inf = self.info()
+        out = np.zeros((inf.grid, int(n_steps), inf.n_blocks + 1, 16), dtype=np.uint64)
+        n = C.c_size_t(0)
+        _check(lib().gaje_cuda_trace_fused(self._m, int(first_token), int(n_steps), _ptr(out), C.c_size_t(out.size),
+                                           C.byref(n)))
+        return out
+
     def generate_native_py(self, prompt_tokens: Sequence[int], max_new_tokens: int = 30,
                            temperature: float = 0.7, repetition_penalty: float = 1.0,
                            eos_token_ids: Iterable[int] = (2, 151643, 151645)) -> list:
@@ -437,6 +463,39 @@ class GenomicLLM:
         return [int(t) for t in out[: n.value]]
 
     generate = generate_native_py
+
+
+def nccl_unique_id() -> bytes:
+    """A fresh NCCL unique id (GAJE_NCCL_ID_BYTES bytes) for load_genomic_sharded."""
+    buf = C.create_string_buffer(NCCL_ID_BYTES)
+    _check(lib().gaje_cuda_nccl_unique_id(buf))
+    return buf.raw
+
+
+def vocab_shard(vocab_size: int, nranks: int, rank: int) -> tuple:
+    """(row0, rows): the lm_head rows rank `rank` of `nranks` holds."""
+    r0, n = C.c_uint32(0), C.c_uint32(0)
+    _check(lib().gaje_vocab_shard(int(vocab_size), int(nranks), int(rank), C.byref(r0), C.byref(n)))
+    return int(r0.value), int(n.value)
+
+
+def argmax_key(value: float, index: int) -> int:
+    """The orderable (value, first index) key the sharded ranks exchange."""
+    return int(lib().gaje_argmax_key(float(value), int(index)))
+
+
+def argmax_key_index(key: int) -> int:
+    return int(lib().gaje_argmax_key_index(int(key)))
+
+
+def load_genomic_sharded(path: str, nranks: int, rank: int, nccl_id: bytes, **kw) -> GenomicLLM:
+    """One rank of a request-parallel group with the f32 lm_head split by
+    vocabulary over `nranks` GPUs (every rank calls it together with the same
+    nccl_id).  Batched calls only (forward_batch / prefill, collective: the
+    same sequence with the same batch size on every rank)."""
+    if kw.get("max_streams", 0) <= 0:
+        raise ValueError("a vocab-sharded model serves batched streams: pass max_streams > 0")
+    return GenomicLLM(path, shard=(nranks, rank, nccl_id), **kw)
 
 
 def load_genomic_auto(path: str, **kw) -> GenomicLLM:

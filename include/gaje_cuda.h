@@ -136,7 +136,10 @@ typedef struct gaje_load_opts {
   int use_graph;      /* kernel-per-phase engine: replay each step as a CUDA
                          graph (1, default) or launch kernel by kernel (0)    */
   int use_megakernel; /* 1 (default): one persistent cooperative kernel runs
-                         whole decode steps; 0: one kernel per phase          */
+                         whole decode steps -- the two-exchange-per-block
+                         kernel when the shape fits it, else the five-exchange
+                         one; 2: the five-exchange kernel only; 0: one kernel
+                         per phase                                          */
   uint32_t max_streams; /* KV caches for gaje_cuda_forward_batch (0 = none)   */
   uint32_t max_prefill; /* rows of one gaje_cuda_prefill pass (0 = no prefill) */
 } gaje_load_opts;
@@ -156,7 +159,10 @@ typedef struct gaje_model_info {
   float eps, rope_base, k_wta_ratio;
   size_t device_bytes; /* weights + KV cache + scratch held on the device */
   uint32_t grid;        /* CTAs of the persistent kernel (one per SM) */
-  uint32_t megakernel;  /* 1 when steps run in the persistent kernel */
+  uint32_t megakernel;  /* 2: the two-exchange persistent kernel, 1: the
+                           five-exchange one, 0: one kernel per phase */
+  uint32_t nranks, rank;           /* the vocab-sharded group (1, 0 when unsharded) */
+  uint32_t vocab_row0, vocab_rows; /* lm_head rows this model holds */
 } gaje_model_info;
 int gaje_cuda_model_info(gaje_model* model, gaje_model_info* info);
 
@@ -215,6 +221,46 @@ int gaje_cuda_forward_batch(gaje_model* model, const uint32_t* stream_ids, const
  * use_genomic_norm are GAJE_ERR_UNSUPPORTED; overflow is GAJE_ERR_CONTEXT. */
 int gaje_cuda_prefill(gaje_model* model, uint32_t stream_id, const uint32_t* tokens, size_t n,
                       uint32_t* argmax_out, float* logits_out);
+/* ------------------------------------------------- multi-GPU batched serving */
+/* Request-parallel serving over several GPUs: one process
+ * (or thread) per GPU, each holding the whole Q4 body and its own streams'
+ * KV caches, and only a vocabulary slice of the f32 lm_head.  Each batched
+ * step runs the body for the rank's own streams, all-gathers the residual
+ * rows of every rank over NCCL, runs the output norm + lm_head slice for all
+ * of them, all-gathers the per-row best (value, index) keys and keeps, per
+ * local stream, the first maximum over the whole vocabulary: the same token
+ * the single-GPU argmax (src/nn/llm/forward.rs:262-271) picks.  The
+ * reference is single-process CPU code with no counterpart; the calls below
+ * replace load_genomic_auto (src/io/flat_reader.rs:240-251) for one rank.
+ *
+ * Collective contract: every rank calls gaje_cuda_load_sharded together, and
+ * then the same sequence of gaje_cuda_forward_batch / gaje_cuda_prefill calls
+ * with the same B (each with its own streams and tokens).  A sharded model
+ * returns argmax only (logits_out must be NULL: GAJE_ERR_UNSUPPORTED) and
+ * refuses the single-stream calls (gaje_cuda_forward, _generate,
+ * _decode_greedy, _profile_*, _trace_steps).  A collective that does not
+ * finish within GAJE_NCCL_TIMEOUT_S seconds (environment, default 120) aborts
+ * the communicator and the call returns GAJE_ERR_TIMEOUT; a failed NCCL call
+ * returns GAJE_ERR_CUDA; either way the model must be reloaded.
+ * NCCL is resolved at run time (dlopen of libnccl.so.2): a host process that
+ * already loaded one shares it; GAJE_ERR_UNSUPPORTED when none is found. */
+#define GAJE_NCCL_ID_BYTES 128
+/* ncclGetUniqueId: one rank creates the id and the host hands it to the others. */
+int gaje_cuda_nccl_unique_id(uint8_t* id_out /* GAJE_NCCL_ID_BYTES */);
+/* gaje_cuda_load for rank `rank` of `nranks` (opts->device is this rank's GPU;
+ * opts->max_streams must be > 0).  The lm_head rows held are those of
+ * gaje_vocab_shard.  Collective: all ranks call it together.  NULL on error. */
+gaje_model* gaje_cuda_load_sharded(const char* flat_path, const gaje_load_opts* opts, int nranks, int rank,
+                                   const uint8_t* nccl_id /* GAJE_NCCL_ID_BYTES */);
+/* The vocabulary split: rank r holds lm_head rows [row0, row0 + rows) with
+ * chunk = ceil(V / nranks), row0 = r * chunk. */
+int gaje_vocab_shard(uint32_t vocab_size, int nranks, int rank, uint32_t* row0, uint32_t* rows);
+/* The orderable argmax key the ranks exchange: larger value first, then the
+ * lower index, so the largest key over all shards is the first maximum
+ * (llm/forward.rs:262-271); NaN and -inf give 0 (never win); -0.0 == +0.0. */
+uint64_t gaje_argmax_key(float value, uint32_t index);
+uint32_t gaje_argmax_key_index(uint64_t key);
+
 /* clear_cache_core for one batched stream. */
 int gaje_cuda_clear_stream(gaje_model* model, uint32_t stream_id);
 /* A batched stream's cache length. */
@@ -269,6 +315,20 @@ int gaje_cuda_profile_phases(gaje_model* model, uint32_t first_token, size_t n_s
  * gaje_model_info.grid); *n_written receives the count.  No counterpart in the
  * reference: a diagnostic of the persistent kernel's critical path. */
 int gaje_cuda_trace_steps(gaje_model* model, uint32_t first_token, size_t n_steps,
+                          uint64_t* out, size_t out_len, size_t* n_written);
+
+/* The same for the two-exchange persistent kernel (gaje_model_info.megakernel
+ * == 2): out[((cta*n_steps + step)*(L+1) + l)*16 + k] is the %globaltimer
+ * value (ns) of trace point k of block l on that CTA (0 where the CTA had no
+ * such point).  Block points: 0 phase A entry, 1 input ready, 2 input staged,
+ * 3 q (or k/v) rows done, 4 K/V rows landed, 5 attention done, 6 output
+ * projection done, 7 split weights known, 8 phase A published, 9 phase B
+ * input flags seen, 10 x_a formed, 11 staged, 12 first gate/up block done,
+ * 13 down columns done, 14 phase B published.  l = L: 0 entry, 1 input
+ * ready, 2 staged, 3 lm_head rows done, 4 token published.  out_len must be
+ * at least grid*n_steps*(L+1)*16.  No counterpart in the reference: a
+ * diagnostic of the kernel's critical path. */
+int gaje_cuda_trace_fused(gaje_model* model, uint32_t first_token, size_t n_steps,
                           uint64_t* out, size_t out_len, size_t* n_written);
 
 /* ---------------------------------------------------------------- op level */

@@ -19,7 +19,9 @@ def _rel(a, b):
     return float(np.max(np.abs(a - b)) / max(np.max(np.abs(b)), 1e-30))
 
 
-ENGINES = [pytest.param(True, id="mega"), pytest.param(False, id="phase")]
+# use_megakernel: 1 = the two-exchange persistent kernel (fused.cuh) where the
+# shape fits, 2 = the five-exchange persistent kernel, 0 = a kernel per phase
+ENGINES = [pytest.param(1, id="fused"), pytest.param(2, id="mega"), pytest.param(0, id="phase")]
 
 
 def _pair(g, O, path, **kw):
@@ -225,11 +227,13 @@ def test_engines_agree_and_phase_profile(g, make_model):
         b.profile_phases(1, 2)
 
 
-def test_megakernel_long_context_splits(g, O, make_model):
+@pytest.mark.parametrize("mega", [pytest.param(1, id="fused"), pytest.param(2, id="mega")])
+def test_megakernel_long_context_splits(g, O, make_model, mega):
     """Contexts past 64 splits x 32 positions (chunks grow beyond 32) and the
     split cap of heads x splits <= CTAs, on a 3-KV-head model."""
     path = make_model("small", seed=21, n_embd=384, n_head=6, n_head_kv=3)
-    gpu, ref = _pair(g, O, path, max_ctx=2600, use_megakernel=True)
+    gpu, ref = _pair(g, O, path, max_ctx=2600, use_megakernel=mega)
+    assert gpu.info().megakernel == {1: 2, 2: 1}[mega]  # info: 2 = two-exchange kernel, 1 = five-exchange
     gpu.set_k_wta_ratio(0.0)
     ref.set_k_wta_ratio(0.0)
     worst = 0.0
