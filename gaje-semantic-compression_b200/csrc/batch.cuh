@@ -129,6 +129,7 @@ struct AttnBatchArgs {
   unsigned* cnt;   // [B][nkv], zero between launches
   int layer, nh;
   float scale;
+  int max_splits;  // splits per (stream, KV head) at most (the grid's y)
 };
 __global__ void __launch_bounds__(kAttnThreads) k_attn_batch(AttnBatchArgs B) {
   const int b = blockIdx.z;
@@ -149,6 +150,7 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_batch(AttnBatchArgs B) {
   a.scale = B.scale;
   a.st = nullptr;
   a.fresh = 1;  // the stream's row at pos is written by the QKV kernel just before
+  a.max_splits = B.max_splits;
   attn_split(a, blockIdx.x, blockIdx.y);
 }
 

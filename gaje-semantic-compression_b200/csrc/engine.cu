@@ -925,8 +925,19 @@ int tc_gemm_run(const TcPlan& p, const WS& W, const float* x, int M, Epi epi, co
   return GAJE_OK;
 }
 
-size_t batch_attn_smem(const gaje_model* m) {
-  return attn_smem_bytes(m->nh / m->nkv, m->hd, attn_chunk_max(m->max_ctx));
+// Attention splits of a batched step of Bi streams, at most: enough (stream,
+// KV head, split) CTAs to fill the SMs twice, and never chunks of more than
+// kBatchAttnRows cached rows (the shared-memory size below), so that long
+// contexts are split only as far as needed and the combine stays short.
+constexpr int kBatchAttnRows = 96;
+int batch_attn_splits(const gaje_model* m, int Bi) {
+  const int by_smem = (m->max_ctx + kBatchAttnRows - 1) / kBatchAttnRows;
+  const int by_fill = (2 * m->sms + Bi * m->nkv - 1) / (Bi * m->nkv);
+  return std::max(1, std::min(kAttnMaxSplits, std::max(by_smem, by_fill)));
+}
+size_t batch_attn_smem(const gaje_model* m) {  // the largest chunk any batch size gives
+  const int ms = std::min(kAttnMaxSplits, std::max(1, (m->max_ctx + kBatchAttnRows - 1) / kBatchAttnRows));
+  return attn_smem_bytes(m->nh / m->nkv, m->hd, attn_chunk_max(m->max_ctx, ms));
 }
 
 // Shared-memory opt-ins and the lm_head grid, once at load (never during a
@@ -1022,8 +1033,9 @@ int launch_batch(gaje_model* m, int Bi) {
   const float eps = m->info.eps;
   constexpr int MT = kBatchMT;
   const size_t sk = skinny_smem_bytes(MT);
+  const int asplit = batch_attn_splits(m, Bi);
   int ns_max = 1, ch_max = 1;  // attention splits at the longest context
-  attn_splits(m->max_ctx, ns_max, ch_max);
+  attn_splits(m->max_ctx, ns_max, ch_max, asplit);
   cudaError_t e = launch_k(k_embed_batch, dim3(Bi), dim3(256), 0, st, false, (const float*)m->embd, m->V, d, bs,
                            m->bx);
   for (int l = 0; l < L && e == cudaSuccess; ++l) {
@@ -1031,7 +1043,7 @@ int launch_batch(gaje_model* m, int Bi) {
     e = batch_gemm<true>(m, Bi, m->qkv[l], m->bx, TcNorm{m->attn_norm[l], eps, m->st, bs.pos, l}, eq);
     if (e != cudaSuccess) break;
     AttnBatchArgs aa{m->bq, m->battn, m->bcache, bs, m->bpart_o, m->bpart_ml, m->bcnt, l, m->nh,
-                     1.0f / sqrtf(float(m->hd))};
+                     1.0f / sqrtf(float(m->hd)), asplit};
     e = launch_k(k_attn_batch, dim3(unsigned(m->nkv), unsigned(ns_max), unsigned(Bi)), dim3(kAttnThreads),
                  batch_attn_smem(m), st, true, aa);
     if (e != cudaSuccess) break;

@@ -80,6 +80,30 @@ struct FusedPlan {
   int pv_groups;  // position groups of the P*V partial sums
 };
 
+// One block of 32 weights for four rows sharing the staged activations of
+// block b (the arithmetic of q4_pair_qx, with the activation loads shared).
+__device__ __forceinline__ void q4_quad_qx(const uint4 q0, const uint4 q1, const uint4 q2, const uint4 q3,
+                                           const float* xs, int b, float& A0, float& A1, float& A2, float& A3) {
+  const float4* x4 = reinterpret_cast<const float4*>(xs + (b << 5));
+  const int sw = b & 7;
+  unsigned long long r00 = 0ull, r01 = 0ull, r10 = 0ull, r11 = 0ull, r20 = 0ull, r21 = 0ull, r30 = 0ull,
+                     r31 = 0ull;
+  const uint32_t w0[4] = {q0.x, q0.y, q0.z, q0.w}, w1[4] = {q1.x, q1.y, q1.z, q1.w};
+  const uint32_t w2[4] = {q2.x, q2.y, q2.z, q2.w}, w3[4] = {q3.x, q3.y, q3.z, q3.w};
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const float4 xa = x4[(2 * w) ^ sw], xb = x4[(2 * w + 1) ^ sw];
+    q4_word_qx(w0[w], xa, xb, r00, r01);
+    q4_word_qx(w1[w], xa, xb, r10, r11);
+    q4_word_qx(w2[w], xa, xb, r20, r21);
+    q4_word_qx(w3[w], xa, xb, r30, r31);
+  }
+  A0 = hsum2(r00, r01);
+  A1 = hsum2(r10, r11);
+  A2 = hsum2(r20, r21);
+  A3 = hsum2(r30, r31);
+}
+
 struct FusedArgs {
   StepParams P;
   const LayerW* layers;
@@ -135,8 +159,12 @@ struct FuShared {
   float* kvbuf;  // [cap][hd] K, then [cap][hd] V
   float* pv;     // [pv_groups][hd]
   float* ost;    // [hd] staged O_s, [hd/32] sums after it
-  float* araw;   // [kb_max*32] SwiGLU outputs
-  float* ast;    // [kb_max*32] staged, [kb_max] sums after it
+  float* ast;    // [32] staged SwiGLU outputs of one K-block, [1] sum after it
+  float* nw;     // [d] the norm weights of the next staging (prefetched)
+  float* rb;     // [hd] RoPE (cos, sin) of the position, [hd] this CTA's q/k/v bias rows
+  float* gub;    // [kb_max*64] gate/up bias rows of this CTA's K-blocks
+  float* raw;    // [max(hd, 64)] raw row dots of a row GEMV
+  float* ycol;   // [d] column-GEMV accumulators (rows 4t..4t+3 owned by thread t)
   float* misc;   // 64 floats: reductions, coefficients
   unsigned char* slots;
 };
@@ -355,59 +383,79 @@ __device__ __forceinline__ void fu_release(const FusedArgs& A, const FuShared& S
   if ((threadIdx.x & 31) == 0) mbar_arrive(S.empty + item % A.plan.nslots);
 }
 
-// Row pairs [0, nr/2) of a row-major Q4 item against the staged xs: a warp per
-// pair, lanes over the blocks; epi(p, y0, y1) on lane 0 with the raw dots.
-template <class Epi>
-__device__ __forceinline__ void fu_rows(const unsigned char* slot, int nr, int nb, int nbp, const float* xs,
-                                        const float* xsum, Epi&& epi) {
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+// Raw dots of the nr rows of a row-major Q4 item against the staged xs, into
+// out[nr] (shared memory): a warp takes two row pairs at a time (four
+// accumulator chains), lanes over the blocks.
+__device__ __forceinline__ void fu_rows_raw(const unsigned char* slot, int nr, int nb, int nbp, const float* xs,
+                                         const float* xsum, float* out) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, np = nr / 2;
   const uint4* qs = reinterpret_cast<const uint4*>(slot);
   const uint32_t* sm = reinterpret_cast<const uint32_t*>(slot + (size_t)nr * nb * 16);
 #pragma unroll 1
-  for (int p = wid; p < nr / 2; p += kFuConsumerWarps) {
-    const int r0 = 2 * p;
-    float acc0 = 0.f, acc1 = 0.f;
+  for (int p = wid; p < np; p += 2 * kFuConsumerWarps) {
+    const int p2 = min(p + kFuConsumerWarps, np - 1);  // a duplicate of p's last pair when past the end
+    const int ra = 2 * p, rb = 2 * p2;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
 #pragma unroll 1
     for (int b = lane; b < nb; b += 32) {
-      float A0, A1, sc, mn;
-      q4_pair_qx(qs[(size_t)r0 * nb + b], qs[(size_t)(r0 + 1) * nb + b], true, xs, b, A0, A1);
+      float A0, A1, A2, A3, sc, mn;
+      q4_quad_qx(qs[(size_t)ra * nb + b], qs[(size_t)(ra + 1) * nb + b], qs[(size_t)rb * nb + b],
+                 qs[(size_t)(rb + 1) * nb + b], xs, b, A0, A1, A2, A3);
       const float xb = xsum[b];
-      unpack_sm(sm[(size_t)r0 * nbp + b], sc, mn);
-      acc0 = fmaf(sc, A0, fmaf(mn, xb, acc0));
-      unpack_sm(sm[(size_t)(r0 + 1) * nbp + b], sc, mn);
-      acc1 = fmaf(sc, A1, fmaf(mn, xb, acc1));
+      unpack_sm(sm[(size_t)ra * nbp + b], sc, mn);
+      a0 = fmaf(sc, A0, fmaf(mn, xb, a0));
+      unpack_sm(sm[(size_t)(ra + 1) * nbp + b], sc, mn);
+      a1 = fmaf(sc, A1, fmaf(mn, xb, a1));
+      unpack_sm(sm[(size_t)rb * nbp + b], sc, mn);
+      a2 = fmaf(sc, A2, fmaf(mn, xb, a2));
+      unpack_sm(sm[(size_t)(rb + 1) * nbp + b], sc, mn);
+      a3 = fmaf(sc, A3, fmaf(mn, xb, a3));
     }
-    acc0 = warp_sum(acc0);
-    acc1 = warp_sum(acc1);
-    if (lane == 0) epi(p, acc0, acc1);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+      a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+      a2 += __shfl_xor_sync(0xffffffffu, a2, o);
+      a3 += __shfl_xor_sync(0xffffffffu, a3, o);
+    }
+    if (lane == 0) {
+      out[ra] = a0;
+      out[ra + 1] = a1;
+      if (p + kFuConsumerWarps < np) {
+        out[rb] = a2;
+        out[rb + 1] = a3;
+      }
+    }
   }
 }
 
-// Rows 4t..4t+3 (t < d/4) of nkb K-block-major column blocks against the
-// staged xst/xsum (local block index): y[0..4) accumulates the raw dots.
-__device__ __forceinline__ void fu_cols(const unsigned char* slot, int d, int nkb, const float* xst,
-                                        const float* xsum, float (&y)[4]) {
+// ycol[4t..4t+3] (+)= the raw dots of rows 4t..4t+3 (t < d/4) over nkb
+// K-block-major column blocks against the staged xst / xsum (local block
+// index); init starts the accumulators at zero.
+__device__ __forceinline__ void fu_cols(const unsigned char* slot, int d, int nkb, const float* xst, const float* xsum,
+                                     float* ycol, bool init) {
   const int t = threadIdx.x;
   if (t >= d / 4) return;
   const uint4* qs = reinterpret_cast<const uint4*>(slot);
   const uint32_t* sm = reinterpret_cast<const uint32_t*>(slot + (size_t)nkb * d * 16);
+  float4 y = init ? make_float4(0.f, 0.f, 0.f, 0.f) : reinterpret_cast<const float4*>(ycol)[t];
 #pragma unroll 1
   for (int kb = 0; kb < nkb; ++kb) {
     const uint4* q = qs + (size_t)kb * d + 4 * t;
     const uint4 s4 = *reinterpret_cast<const uint4*>(sm + (size_t)kb * d + 4 * t);
     const float xb = xsum[kb];
     float A0, A1, A2, A3, sc, mn;
-    q4_pair_qx(q[0], q[1], true, xst, kb, A0, A1);
-    q4_pair_qx(q[2], q[3], true, xst, kb, A2, A3);
+    q4_quad_qx(q[0], q[1], q[2], q[3], xst, kb, A0, A1, A2, A3);
     unpack_sm(s4.x, sc, mn);
-    y[0] = fmaf(sc, A0, fmaf(mn, xb, y[0]));
+    y.x = fmaf(sc, A0, fmaf(mn, xb, y.x));
     unpack_sm(s4.y, sc, mn);
-    y[1] = fmaf(sc, A1, fmaf(mn, xb, y[1]));
+    y.y = fmaf(sc, A1, fmaf(mn, xb, y.y));
     unpack_sm(s4.z, sc, mn);
-    y[2] = fmaf(sc, A2, fmaf(mn, xb, y[2]));
+    y.z = fmaf(sc, A2, fmaf(mn, xb, y.z));
     unpack_sm(s4.w, sc, mn);
-    y[3] = fmaf(sc, A3, fmaf(mn, xb, y[3]));
+    y.w = fmaf(sc, A3, fmaf(mn, xb, y.w));
   }
+  reinterpret_cast<float4*>(ycol)[t] = y;
 }
 
 // Issues the TMA copies of split s's cached K/V rows of block l at `cached`
@@ -429,35 +477,42 @@ __device__ __forceinline__ void fu_kv_prefetch(const FusedArgs& A, const FuShare
   }
 }
 
-// R (or x_a) + flush(sum) + bias for this thread's elements, from the sum
-// buffer (L2 loads).  With nan_layer >= 0 (one CTA) the down projection's NaN
-// guards of block/forward.rs:128-140 are raised.
-__device__ __noinline__ void fu_add_sum(float* dst, const float* base, const float* sum, const float* bias, int d,
+// dst = base + flush(sum) + bias for this thread's elements (sum read from L2
+// after an acquiring gate).  With nan_layer >= 0 (one CTA) the down
+// projection's NaN guards of block/forward.rs:128-140 are raised.
+__device__ __forceinline__ void fu_add_sum(float* dst, const float* base, const float* sum, const float* bias, int d,
                                         DevState* st, unsigned pos, int nan_layer) {
-#pragma unroll 1
-  for (int i = threadIdx.x; i < d; i += kFuConsumers) {
-    float y = flush_small(ld_rlx(sum + i));
-    if (bias) y += __ldg(bias + i);
-    const float v = base[i] + y;
-    if (nan_layer >= 0) {
-      if (y != y) nan_flag(st, pos, nan_layer, kNanProjFfn);
-      if (v != v) nan_flag(st, pos, nan_layer, kNanResidual);
+  for (int i0 = threadIdx.x; i0 < d; i0 += 2 * kFuConsumers) {
+    const int i1 = i0 + kFuConsumers;
+    const float s0 = __ldcg(sum + i0), s1 = i1 < d ? __ldcg(sum + i1) : 0.f;
+    const float b0 = bias ? __ldg(bias + i0) : 0.f, b1 = (bias && i1 < d) ? __ldg(bias + i1) : 0.f;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int i = k ? i1 : i0;
+      if (i >= d) break;
+      const float y = flush_small(k ? s1 : s0) + (k ? b1 : b0);
+      const float v = base[i] + y;
+      if (nan_layer >= 0) {
+        if (y != y) nan_flag(st, pos, nan_layer, kNanProjFfn);
+        if (v != v) nan_flag(st, pos, nan_layer, kNanResidual);
+      }
+      dst[i] = v;
     }
-    dst[i] = v;
   }
 }
 
-// Stages x * w (w nullable) into xs/xsum for the row GEMVs and returns
-// 1/rms of x (the scale of the finished row dots), with the block-input and
-// normed-output NaN guards of block/forward.rs:11-13, :22-24 when guard.
-__device__ __noinline__ float fu_stage_norm(const float* x, const float* w, int d, float eps, float* xs, float* xsum,
-                                            float* red, bool guard, DevState* st, unsigned pos, int layer) {
+// Stages x * nw into xs/xsum for the row GEMVs and returns 1/rms of x (the
+// scale of the finished row dots), with the block-input and normed-output NaN
+// guards of block/forward.rs:11-13, :22-24 when guard.
+__device__ __forceinline__ float fu_stage_norm(const float* x, const float* nw, int d, float eps, float* xs,
+                                            float* xsum, float* red, bool guard, DevState* st, unsigned pos,
+                                            int layer) {
   float ss = 0.f;
 #pragma unroll 1
   for (int i = threadIdx.x; i < d; i += kFuConsumers) {  // whole warps: d % 32 == 0
     const float v = x[i];
     ss = fmaf(v, v, ss);
-    mk_stage_elem(xs, xsum, i, w ? v * __ldg(w + i) : v);
+    mk_stage_elem(xs, xsum, i, v * nw[i]);
   }
   const float tot = fu_total(ss, red, false);
   const float inv = 1.0f / sqrtf(tot / (float)d + eps);
@@ -465,7 +520,7 @@ __device__ __noinline__ float fu_stage_norm(const float* x, const float* w, int 
     for (int i = threadIdx.x; i < d; i += kFuConsumers) {
       const float v = x[i];
       if (v != v) nan_flag(st, pos, layer, kNanInput);
-      const float nv = (v * inv) * (w ? __ldg(w + i) : 1.f);
+      const float nv = (v * inv) * nw[i];
       if (nv != nv) nan_flag(st, pos, layer, kNanAttnNorm);
     }
   return inv;
@@ -491,6 +546,255 @@ __device__ __forceinline__ bool fu_token(const FusedArgs& A, int step, unsigned&
   return true;
 }
 
+// Loads n floats of global memory into shared memory (zeros without src).
+__device__ __forceinline__ void fu_prefetch(float* dst, const float* src, int n) {
+  for (int i = threadIdx.x; i < n; i += kFuConsumers) dst[i] = src ? __ldg(src + i) : 0.f;
+}
+
+// The attention of split sp of head h at position pos (q in S.qbuf): the
+// cached rows landed by TMA, this position's k/v row (LL words) for the last
+// split, scores, softmax, (m, l) published, P*V, O staged for the output
+// projection.  Returns the split's position count, or -1 on an abort.
+__device__ __forceinline__ int fu_attend(const FusedArgs& A, const FuShared& S, int l, int step, unsigned pos, int h,
+                                      int sp, unsigned eA) {
+  const StepParams& P = A.P;
+  const FusedPlan& pl = A.plan;
+  DevState* st = P.st;
+  const int tid = threadIdx.x, hd = P.hd, L = P.n_layers;
+  int t0, n_old;
+  fu_split(int(pos), pl.S, sp, t0, n_old);
+  const bool last = sp == pl.S - 1;
+  const int n = n_old + (last ? 1 : 0);
+  float* Ks = S.kvbuf;
+  float* Vs = S.kvbuf + (size_t)pl.cap * hd;
+  const int g = h / (P.nh / P.nkv);
+  bool ok = true;
+  if (last)
+    ok = fu_ll_read(A.kvnew + (size_t)g * hd, hd, eA, Ks + (size_t)n_old * hd) &&
+         fu_ll_read(A.kvnew + (size_t)(P.nkv + g) * hd, hd, eA, Vs + (size_t)n_old * hd);
+  const int use = *S.kv_waited;
+  if (ok && !*S.cabort && !mbar_wait(S.kv_bar, use & 1)) ok = false;
+  if (!ok) {
+    flag_timeout(st, 24);
+    *S.cabort = 1;
+  }
+  fu_sync();
+  if (*S.cabort) return -1;
+  if (tid == 0) *S.kv_waited = use + 1;
+  const int H4 = hd >> 2;
+  float m = -INFINITY;
+#pragma unroll 1
+  for (int t = tid; t < n; t += kFuConsumers) {
+    const float4* kr = reinterpret_cast<const float4*>(Ks + (size_t)t * hd);
+    const float4* qr = reinterpret_cast<const float4*>(S.qbuf);
+    float a0 = 0.f, a1 = 0.f;
+    int cc = t % H4;  // rotated start: conflict-free rows
+#pragma unroll 4
+    for (int k = 0; k < H4; ++k) {
+      const float4 kk = kr[cc], qq = qr[cc];
+      a0 = fmaf(qq.x, kk.x, a0);
+      a1 = fmaf(qq.y, kk.y, a1);
+      a0 = fmaf(qq.z, kk.z, a0);
+      a1 = fmaf(qq.w, kk.w, a1);
+      cc = cc + 1 == H4 ? 0 : cc + 1;
+    }
+    const float sc = (a0 + a1) * P.attn_scale;
+    S.ps[t] = sc;
+    m = fmaxf(m, sc);
+  }
+  m = fu_total(m, S.misc, true);
+  float lsum = 0.f;
+  for (int t = tid; t < n; t += kFuConsumers) {
+    const float ev = expf(S.ps[t] - m);
+    S.ps[t] = ev;
+    lsum += ev;
+  }
+  lsum = fu_total(lsum, S.misc + 16, false);  // also publishes ps
+  if (tid == 0) {
+    S.misc[40] = m;
+    if (n > 0) {  // (m, l) of this split
+      uint2* ml = A.mlx + ((size_t)h * pl.S + sp) * 2;
+      st_ll(ml, m, eA);
+      st_ll(ml + 1, lsum, eA);
+    }
+  }
+  // P*V: position groups j of e-columns, summed in group order
+  const int J = pl.pv_groups;
+  if (tid < J * hd) {
+    const int e = tid % hd, j = tid / hd;
+    float o = 0.f;
+#pragma unroll 4
+    for (int t = j; t < n; t += J) o = fmaf(S.ps[t], Vs[(size_t)t * hd + e], o);
+    S.pv[j * hd + e] = o;
+  }
+  fu_sync();
+  if (tid == 0) {  // K/V buffer free: the next block's (or next step's) rows
+    if (l + 1 < L) fu_kv_prefetch(A, S, l + 1, int(pos));
+    else if (step + 1 < A.n_steps && L > 1) fu_kv_prefetch(A, S, 0, int(pos) + 1);
+  }
+  if (tid < hd) {
+    float o = 0.f;
+    for (int j = 0; j < J; ++j) o += S.pv[j * hd + tid];
+    S.pv[tid] = o;  // group 0 is read only by this thread
+  }
+  fu_sync();
+  for (int i = tid; i < hd; i += kFuConsumers) mk_stage_elem(S.ost, S.ost + hd, i, S.pv[i]);
+  return n;
+}
+
+// The split weight of this CTA's O_s: exp(m_s - M) / (sum_s exp(m_s - M) l_s
+// + 1e-12) over the head's splits, from their LL (m, l) words (warp 0), into
+// S.misc[32].
+__device__ __forceinline__ void fu_split_weight(const FusedArgs& A, const FuShared& S, unsigned pos, int h, int n,
+                                             unsigned eA) {
+  const FusedPlan& pl = A.plan;
+  const int lane = threadIdx.x & 31;
+  const uint2* ml = A.mlx + (size_t)h * pl.S * 2;
+  float ms = -INFINITY, ls = 0.f;
+  bool good = true;
+  if (lane < pl.S) {
+    int t0s, nos;
+    fu_split(int(pos), pl.S, lane, t0s, nos);
+    if (nos + (lane == pl.S - 1 ? 1 : 0) > 0) {  // splits without positions publish nothing
+      uint2 wm = ld_ll(ml + 2 * lane), wl = ld_ll(ml + 2 * lane + 1);
+      unsigned long long tw = 0;
+      while (wm.y != eA || wl.y != eA) {
+        const unsigned long long t = global_ns();
+        if (!tw) tw = t;
+        else if (t - tw > kWaitNs) {
+          good = false;
+          break;
+        }
+        wm = ld_ll(ml + 2 * lane);
+        wl = ld_ll(ml + 2 * lane + 1);
+      }
+      ms = __uint_as_float(wm.x);
+      ls = __uint_as_float(wl.x);
+    }
+  }
+  if (!__all_sync(0xffffffffu, good) && lane == 0) {
+    flag_timeout(A.P.st, 25);
+    *S.cabort = 1;
+  }
+  const float M = warp_max(ms);
+  float wsum = 0.f;
+  for (int k = 0; k < pl.S; ++k) {  // split order
+    const float mk = __shfl_sync(0xffffffffu, ms, k), lk = __shfl_sync(0xffffffffu, ls, k);
+    if (mk > -INFINITY) wsum = fmaf(expf(mk - M), lk, wsum);
+  }
+  if (lane == 0) S.misc[32] = n > 0 ? expf(S.misc[40] - M) / (wsum + 1e-12f) : 0.f;
+}
+
+// output_norm + this CTA's lm_head rows (ring stages) + argmax; the last CTA
+// to finish publishes the step's token.  Returns false on an abort.
+__device__ __forceinline__ bool fu_lm(const FusedArgs& A, const FuShared& S, int step, unsigned pos, int* item_io,
+                                   unsigned long long* trace_row) {
+  const StepParams& P = A.P;
+  const FusedPlan& pl = A.plan;
+  DevState* st = P.st;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, c = blockIdx.x, d = P.d, L = P.n_layers;
+  const int G = gridDim.x;
+  __shared__ unsigned long long wbest[kFuConsumerWarps];
+  __shared__ int is_last;
+  fu_prefetch(S.nw, P.out_norm, d);
+  const unsigned eLastB = fu_epoch(A.epoch0, L, step, L - 1, 1);
+  if (trace_row && tid == 0) trace_row[0] = global_ns();
+  if (!fu_gate(A.flags + G, G, eLastB, S.cabort, st)) return false;
+  if (trace_row && tid == 0) trace_row[1] = global_ns();
+  const int gl = step * L + L - 1;
+  fu_add_sum(S.R, S.XA, A.yb + (gl & 1) * d, A.layers[L - 1].down.bias, d, st, pos, c == 0 ? L - 1 : -1);
+  fu_sync();
+  float ss = 0.f;
+  for (int i = tid; i < d; i += kFuConsumers) {
+    const float v = S.R[i];
+    ss = fmaf(v, v, ss);
+    S.xs[i] = v * S.nw[i];
+  }
+  const float scale = 1.0f / sqrtf(fu_total(ss, S.misc, false) / (float)d + P.eps);
+  if (trace_row && tid == 0) trace_row[2] = global_ns();
+  const float4* x4 = reinterpret_cast<const float4*>(S.xs);
+  const int K4 = d >> 2;
+  unsigned long long best = 0ull;
+  const int rbeg = c * pl.lm_rows_per_cta;
+  const int nrows = max(0, min(P.V, rbeg + pl.lm_rows_per_cta) - rbeg);
+  const int nitems = (nrows + pl.lm_stage_rows - 1) / pl.lm_stage_rows;
+  const int item = *item_io;
+  int cur = -1;
+  const unsigned char* slot = nullptr;
+#pragma unroll 1
+  for (int k = wid; k < nrows; k += kFuConsumerWarps) {
+    const int it = k / pl.lm_stage_rows;
+    while (cur < it) {
+      if (cur >= 0) fu_release(A, S, item + cur);
+      ++cur;
+      slot = fu_wait_slot(A, S, item + cur);
+    }
+    const float4* w4 = reinterpret_cast<const float4*>(slot) + (size_t)(k - it * pl.lm_stage_rows) * K4;
+    float a0 = 0.f, a1 = 0.f;
+#pragma unroll 2
+    for (int j = lane; j < K4; j += 32) {
+      const float4 u = w4[j], xv = x4[j];
+      a0 = fmaf(u.x, xv.x, a0);
+      a1 = fmaf(u.y, xv.y, a1);
+      a0 = fmaf(u.z, xv.z, a0);
+      a1 = fmaf(u.w, xv.w, a1);
+    }
+    const int row = rbeg + k;
+    float v = warp_sum(a0 + a1) * scale;
+    if (P.lm_bias) v += __ldg(P.lm_bias + row);
+    if (lane == 0) P.logits[row] = v;
+    const unsigned long long key = amax_key(v, (unsigned)row);
+    best = key > best ? key : best;
+  }
+  while (cur < nitems - 1) {
+    if (cur >= 0) fu_release(A, S, item + cur);
+    ++cur;
+    fu_wait_slot(A, S, item + cur);
+  }
+  if (cur >= 0) fu_release(A, S, item + cur);
+  *item_io = item + nitems;
+  if (trace_row && tid == 0) trace_row[3] = global_ns();
+  best = warp_max_u64(best);
+  if (lane == 0) wbest[wid] = best;
+  fu_sync();
+  if (*S.cabort) return false;
+  if (tid == 0) {
+    unsigned long long b = 0;
+    for (int i = 0; i < kFuConsumerWarps; ++i) b = wbest[i] > b ? wbest[i] : b;
+    P.amax_part[c] = b;
+    __threadfence();
+    is_last = (atomicAdd(P.amax_cnt, 1u) == unsigned(G) - 1u);
+  }
+  fu_sync();
+  if (is_last) {
+    __threadfence();
+    unsigned long long b = 0;
+    for (int i = tid; i < G; i += kFuConsumers) {
+      const unsigned long long v = __ldcg(P.amax_part + i);
+      b = v > b ? v : b;
+    }
+    b = warp_max_u64(b);
+    if (lane == 0) wbest[wid] = b;
+    fu_sync();
+    if (tid == 0) {
+      unsigned long long r = 0;
+      for (int i = 0; i < kFuConsumerWarps; ++i) r = wbest[i] > r ? wbest[i] : r;
+      const unsigned idx = amax_index(r);
+      st->argmax = idx;
+      st->token = idx;
+      if (st->hist_len < P.hist_cap) P.tok_hist[st->hist_len] = idx;
+      st->hist_len += 1u;
+      st->pos = pos + 1u;
+      *P.amax_cnt = 0u;
+      fence_acq_rel_gpu();  // the state and the counter reset before the token word
+      st_ll(A.tok, __uint_as_float(idx), fu_epoch(A.epoch0, L, step, L, 0));
+    }
+  }
+  fu_sync();
+  if (trace_row && tid == 0) trace_row[4] = global_ns();
+  return true;
+}
+
 __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
   const StepParams& P = A.P;
   const FusedPlan& pl = A.plan;
@@ -500,39 +804,42 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
   const bool roleA = c < pl.nA, roleKV = !roleA && c < pl.nA + pl.nKV;
   const int h = roleA ? c / pl.S : 0, sp = roleA ? c - h * pl.S : 0;
   const int kvj = roleKV ? c - pl.nA : 0, kvk = kvj / P.nkv, kvg = kvj - kvk * P.nkv;
+  // this CTA's first q/k/v row (pair-interleaved storage)
+  const int qrow0 = roleA ? h * hd : (P.nh + kvk * P.nkv + kvg) * hd;
   int kb0, nkb;
   fu_kbs(P.ff / 32, G, c, kb0, nkb);
   uint2* flA = A.flags;
   uint2* flB = A.flags + G;
-  float* red0 = S.misc;
-  float* red1 = S.misc + 16;
-  float* coef = S.misc + 32;
   int item = 0;
   const unsigned pos0 = __ldcg(&st->pos);
   auto fmark = [&](int step, int l, int k) {
     if (A.trace && tid == 0)
       A.trace[(((size_t)c * A.n_steps + step) * (L + 1) + l) * kFuTrace + k] = global_ns();
   };
-  // first K/V prefetch (step 0, block 0)
-  if (roleA && tid == 0) fu_kv_prefetch(A, S, 0, int(pos0));
+  if (roleA && tid == 0) fu_kv_prefetch(A, S, 0, int(pos0));  // step 0, block 0
   for (int step = 0; step < A.n_steps; ++step) {
     const unsigned pos = pos0 + unsigned(step);
     unsigned tok = 0;
     bool have_tok = false;
     for (int l = 0; l < L; ++l) {
       const LayerW& Lw = A.layers[l];
+      const Q4View& Q = Lw.qkv;
       const int gl = step * L + l;
       const unsigned eA = fu_epoch(A.epoch0, L, step, l, 0), eB = eA + 1u;
       float* ya = A.ya + (gl & 1) * d;
       float* yb = A.yb + (gl & 1) * d;
       const float* yb_prev = A.yb + ((gl + 1) & 1) * d;  // YB of block l-1
-      const LayerW* Lp = l > 0 ? &A.layers[l - 1] : nullptr;
+      const float* dn_bias_prev = l > 0 ? A.layers[l - 1].down.bias : nullptr;
       // ============================================================ phase A
       if (roleA || roleKV) {
-        bool ok = true;
         fmark(step, l, 0);
+        // constants of the phase while the input is in flight
+        fu_prefetch(S.nw, Lw.attn_norm, d);
+        for (int i = tid; i < half; i += kFuConsumers)
+          reinterpret_cast<float2*>(S.rb)[i] = __ldg(P.rope + (size_t)pos * half + i);
+        fu_prefetch(S.rb + hd, Q.bias ? Q.bias + qrow0 : nullptr, hd);
         if (l == 0) {
-          ok = fu_token(A, step, tok);
+          const bool ok = fu_token(A, step, tok);
           have_tok = true;
           if (!ok) {
             flag_timeout(st, 23);
@@ -544,7 +851,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
           for (int i = tid; i < d; i += kFuConsumers) S.R[i] = __ldg(src + i);
         } else {
           if (!fu_gate(flB, G, eB - 2u, S.cabort, st)) return;
-          fu_add_sum(S.R, S.XA, yb_prev, Lp->down.bias, d, st, pos, c == 0 ? l - 1 : -1);
+          fu_add_sum(S.R, S.XA, yb_prev, dn_bias_prev, d, st, pos, c == 0 ? l - 1 : -1);
         }
         if (roleA) {  // clear the sums read two phases ago: YA of block l-1, YB of block l-2
           const int per = (d + pl.nA - 1) / pl.nA;
@@ -559,193 +866,66 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
         if (L == 1 && roleA && tid == 0 && step > 0) fu_kv_prefetch(A, S, 0, int(pos));
         fu_sync();
         fmark(step, l, 1);
-        const float inv = fu_stage_norm(S.R, Lw.attn_norm, d, P.eps, S.xs, S.xsum, red0, c == 0, st, pos, l);
+        const float inv = fu_stage_norm(S.R, S.nw, d, P.eps, S.xs, S.xsum, S.misc, c == 0, st, pos, l);
         fmark(step, l, 2);
-        const float2* rope = P.rope + (size_t)pos * half;
-        const Q4View& Q = Lw.qkv;
         const unsigned char* slot = fu_wait_slot(A, S, item);
         fu_sync();
         if (*S.cabort) return;
-        if (roleKV) {
-          // this position's k (kvk = 0, rotated) or v (kvk = 1) rows of KV head kvg
-          const int row0 = (P.nh + kvk * P.nkv + kvg) * hd;
-          uint2* dst = A.kvnew + (size_t)(kvk * P.nkv + kvg) * hd;
-          float* cache = (kvk ? Lw.vc : Lw.kc) + ((size_t)kvg * P.max_ctx + pos) * hd;
-          fu_rows(slot, hd, Q.nb, Q.nbp, S.xs, S.xsum, [&](int p, float y0, float y1) {
-            y0 = flush_small(y0 * inv);
-            y1 = flush_small(y1 * inv);
-            if (Q.bias) {
-              y0 += __ldg(Q.bias + row0 + 2 * p);
-              y1 += __ldg(Q.bias + row0 + 2 * p + 1);
-            }
-            if (kvk == 0) {  // RoPE: v0*cos - v1*sin, v0*sin + v1*cos
-              const float2 cs = __ldg(rope + p);
-              const float o0 = y0 * cs.x - y1 * cs.y, o1 = y0 * cs.y + y1 * cs.x;
-              y0 = o0;
-              y1 = o1;
-            }
-            const int c0 = P.rope_split ? p : 2 * p, c1 = P.rope_split ? p + half : 2 * p + 1;
+        fu_rows_raw(slot, hd, Q.nb, Q.nbp, S.xs, S.xsum, S.raw);
+        fu_release(A, S, item++);
+        fu_sync();
+        // epilogue, a thread per row pair: flush, bias, RoPE (q, k)
+        if (tid < half) {
+          const int p = tid;
+          float y0 = flush_small(S.raw[2 * p] * inv) + S.rb[hd + 2 * p];
+          float y1 = flush_small(S.raw[2 * p + 1] * inv) + S.rb[hd + 2 * p + 1];
+          if (roleA || kvk == 0) {  // RoPE: v0*cos - v1*sin, v0*sin + v1*cos
+            const float cs = S.rb[2 * p], sn = S.rb[2 * p + 1];
+            const float o0 = y0 * cs - y1 * sn, o1 = y0 * sn + y1 * cs;
+            y0 = o0;
+            y1 = o1;
+          }
+          const int c0 = P.rope_split ? p : 2 * p, c1 = P.rope_split ? p + half : 2 * p + 1;
+          if (roleA) {
+            S.qbuf[c0] = y0;
+            S.qbuf[c1] = y1;
+          } else {  // this position's k or v row: the cache row, and LL words for the last splits
+            float* cache = (kvk ? Lw.vc : Lw.kc) + ((size_t)kvg * P.max_ctx + pos) * hd;
+            uint2* dst = A.kvnew + (size_t)(kvk * P.nkv + kvg) * hd;
             cache[c0] = y0;
             cache[c1] = y1;
             st_ll(dst + c0, y0, eA);
             st_ll(dst + c1, y1, eA);
-          });
-          fu_release(A, S, item++);
-          fmark(step, l, 3);
-        } else {
-          // ---- q rows of head h (RoPE), into qbuf
-          const int row0 = h * hd;
-          fu_rows(slot, hd, Q.nb, Q.nbp, S.xs, S.xsum, [&](int p, float y0, float y1) {
-            y0 = flush_small(y0 * inv);
-            y1 = flush_small(y1 * inv);
-            if (Q.bias) {
-              y0 += __ldg(Q.bias + row0 + 2 * p);
-              y1 += __ldg(Q.bias + row0 + 2 * p + 1);
-            }
-            const float2 cs = __ldg(rope + p);
-            const int c0 = P.rope_split ? p : 2 * p, c1 = P.rope_split ? p + half : 2 * p + 1;
-            S.qbuf[c0] = y0 * cs.x - y1 * cs.y;
-            S.qbuf[c1] = y0 * cs.y + y1 * cs.x;
-          });
-          fu_release(A, S, item++);
-          fmark(step, l, 3);
-          // ---- attention over this split's positions
-          int t0, n_old;
-          fu_split(int(pos), pl.S, sp, t0, n_old);
-          const bool last = sp == pl.S - 1;
-          const int n = n_old + (last ? 1 : 0);
-          float* Ks = S.kvbuf;
-          float* Vs = S.kvbuf + (size_t)pl.cap * hd;
-          const int g = h / (P.nh / P.nkv);
-          if (last) {
-            ok = fu_ll_read(A.kvnew + (size_t)g * hd, hd, eA, Ks + (size_t)n_old * hd) &&
-                 fu_ll_read(A.kvnew + (size_t)(P.nkv + g) * hd, hd, eA, Vs + (size_t)n_old * hd);
           }
-          const int use = *S.kv_waited;
-          if (ok && !*S.cabort && !mbar_wait(S.kv_bar, use & 1)) ok = false;
-          if (!ok) {
-            flag_timeout(st, 24);
-            *S.cabort = 1;
-          }
-          fu_sync();
-          if (*S.cabort) return;
-          if (tid == 0) *S.kv_waited = use + 1;
-          fmark(step, l, 4);
-          const int H4 = hd >> 2;
-          float m = -INFINITY;
-#pragma unroll 1
-          for (int t = tid; t < n; t += kFuConsumers) {
-            const float4* kr = reinterpret_cast<const float4*>(Ks + (size_t)t * hd);
-            const float4* qr = reinterpret_cast<const float4*>(S.qbuf);
-            float a0 = 0.f, a1 = 0.f;
-            int cc = t % H4;  // rotated start: conflict-free rows
-#pragma unroll 4
-            for (int k = 0; k < H4; ++k) {
-              const float4 kk = kr[cc], qq = qr[cc];
-              a0 = fmaf(qq.x, kk.x, a0);
-              a1 = fmaf(qq.y, kk.y, a1);
-              a0 = fmaf(qq.z, kk.z, a0);
-              a1 = fmaf(qq.w, kk.w, a1);
-              cc = cc + 1 == H4 ? 0 : cc + 1;
-            }
-            const float sc = (a0 + a1) * P.attn_scale;
-            S.ps[t] = sc;
-            m = fmaxf(m, sc);
-          }
-          m = fu_total(m, red0, true);
-          float lsum = 0.f;
-          for (int t = tid; t < n; t += kFuConsumers) {
-            const float ev = expf(S.ps[t] - m);
-            S.ps[t] = ev;
-            lsum += ev;
-          }
-          lsum = fu_total(lsum, red1, false);  // also publishes ps
-          if (tid == 0 && n > 0) {             // (m, l) of this split
-            uint2* ml = A.mlx + ((size_t)h * pl.S + sp) * 2;
-            st_ll(ml, m, eA);
-            st_ll(ml + 1, lsum, eA);
-          }
-          // P*V: position groups j of e-columns, summed in group order
-          {
-            const int J = pl.pv_groups;
-            if (tid < J * hd) {
-              const int e = tid % hd, j = tid / hd;
-              float o = 0.f;
-#pragma unroll 4
-              for (int t = j; t < n; t += J) o = fmaf(S.ps[t], Vs[(size_t)t * hd + e], o);
-              S.pv[j * hd + e] = o;
-            }
-            fu_sync();
-            // K/V buffer free: prefetch the next block's (or next step's) rows
-            if (tid == 0) {
-              if (l + 1 < L) fu_kv_prefetch(A, S, l + 1, int(pos));
-              else if (step + 1 < A.n_steps && L > 1) fu_kv_prefetch(A, S, 0, int(pos) + 1);
-            }
-            if (tid < hd) {
-              float o = 0.f;
-              for (int j = 0; j < J; ++j) o += S.pv[j * hd + tid];
-              S.pv[tid] = o;  // group 0 is read only by this thread
-            }
-            fu_sync();
-            for (int i = tid; i < hd; i += kFuConsumers) mk_stage_elem(S.ost, S.ost + hd, i, S.pv[i]);
-            fu_sync();
-            fmark(step, l, 5);
-          }
-          // ---- attn_output columns of head h times O_s
+        }
+        fu_sync();
+        fmark(step, l, 3);
+        if (roleA) {
+          const int n = fu_attend(A, S, l, step, pos, h, sp, eA);
+          if (n < 0) return;
+          fmark(step, l, 5);
           const unsigned char* wslot = fu_wait_slot(A, S, item);
           fu_sync();
           if (*S.cabort) return;
-          float y[4] = {0.f, 0.f, 0.f, 0.f};
-          if (n > 0) fu_cols(wslot, d, hd / 32, S.ost, S.ost + hd, y);
+          if (n > 0) fu_cols(wslot, d, hd / 32, S.ost, S.ost + hd, S.ycol, true);
           fu_release(A, S, item++);
           fmark(step, l, 6);
-          // ---- the head's split weights: exp(m_s - M) / (sum_s exp(m_s - M) l_s + 1e-12)
-          if (wid == 0) {
-            const uint2* ml = A.mlx + (size_t)h * pl.S * 2;
-            float ms = -INFINITY, ls = 0.f;
-            bool good = true;
-            if (lane < pl.S) {
-              int t0s, nos;
-              fu_split(int(pos), pl.S, lane, t0s, nos);
-              if (nos + (lane == pl.S - 1 ? 1 : 0) > 0) {  // splits without positions publish nothing
-                uint2 wm = ld_ll(ml + 2 * lane), wl = ld_ll(ml + 2 * lane + 1);
-                unsigned long long tw = 0;
-                while (wm.y != eA || wl.y != eA) {
-                  const unsigned long long t = global_ns();
-                  if (!tw) tw = t;
-                  else if (t - tw > kWaitNs) {
-                    good = false;
-                    break;
-                  }
-                  wm = ld_ll(ml + 2 * lane);
-                  wl = ld_ll(ml + 2 * lane + 1);
-                }
-                ms = __uint_as_float(wm.x);
-                ls = __uint_as_float(wl.x);
-              }
-            }
-            if (!__all_sync(0xffffffffu, good) && lane == 0) {
-              flag_timeout(st, 25);
-              *S.cabort = 1;
-            }
-            const float M = warp_max(ms);
-            float wsum = 0.f;
-            for (int k = 0; k < pl.S; ++k) {  // split order
-              const float mk = __shfl_sync(0xffffffffu, ms, k), lk = __shfl_sync(0xffffffffu, ls, k);
-              if (mk > -INFINITY) wsum = fmaf(expf(mk - M), lk, wsum);
-            }
-            if (lane == 0) coef[0] = n > 0 ? expf(m - M) / (wsum + 1e-12f) : 0.f;
-          }
+          if (wid == 0) fu_split_weight(A, S, pos, h, n, eA);
           fu_sync();
           if (*S.cabort) return;
-          const float cf = coef[0];
+          const float cf = S.misc[32];
           fmark(step, l, 7);
-          if (n > 0 && tid < d / 4) red_add4(ya + 4 * tid, cf * y[0], cf * y[1], cf * y[2], cf * y[3]);
+          if (n > 0 && tid < d / 4) {
+            const float4 y = reinterpret_cast<const float4*>(S.ycol)[tid];
+            red_add4(ya + 4 * tid, cf * y.x, cf * y.y, cf * y.z, cf * y.w);
+          }
           fu_publish(flA + c, eA);
           fmark(step, l, 8);
         }
       }
       // ============================================================ phase B
+      fu_prefetch(S.nw, Lw.ffn_norm, d);
+      if (nkb > 0) fu_prefetch(S.gub, Lw.gate_up.bias ? Lw.gate_up.bias + (size_t)kb0 * 64 : nullptr, nkb * 64);
       if (!fu_gate(flA, pl.nA, eA, S.cabort, st)) return;
       fmark(step, l, 9);
       if (!(roleA || roleKV)) {  // R of this block from the sums of the previous one
@@ -760,7 +940,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
           const float* src = P.embd + (size_t)(tok % (unsigned)P.V) * d;
           for (int i = tid; i < d; i += kFuConsumers) S.R[i] = __ldg(src + i);
         } else {
-          fu_add_sum(S.R, S.XA, yb_prev, Lp->down.bias, d, st, pos, -1);
+          fu_add_sum(S.R, S.XA, yb_prev, dn_bias_prev, d, st, pos, -1);
         }
         fu_sync();
       }
@@ -769,162 +949,47 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
       if (*S.cabort) return;
       fmark(step, l, 10);
       if (nkb > 0) {
-        const float inv = fu_stage_norm(S.XA, Lw.ffn_norm, d, P.eps, S.xs, S.xsum, red0, false, st, pos, l);
+        const float inv = fu_stage_norm(S.XA, S.nw, d, P.eps, S.xs, S.xsum, S.misc, false, st, pos, l);
         fmark(step, l, 11);
         const Q4View& Gu = Lw.gate_up;
-        float y[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
         for (int k = 0; k < nkb; ++k) {
-          const int kb = kb0 + k;
           const unsigned char* gslot = fu_wait_slot(A, S, item);
           fu_sync();
           if (*S.cabort) return;
-          fu_rows(gslot, 64, Gu.nb, Gu.nbp, S.xs, S.xsum, [&](int p, float g0, float u0) {
-            const int u = kb * 32 + p;
-            float gv = flush_small(g0 * inv), uv = flush_small(u0 * inv);
-            if (Gu.bias) {
-              gv += __ldg(Gu.bias + 2 * u);
-              uv += __ldg(Gu.bias + 2 * u + 1);
-            }
+          fu_rows_raw(gslot, 64, Gu.nb, Gu.nbp, S.xs, S.xsum, S.raw);
+          fu_release(A, S, item++);
+          fu_sync();
+          if (wid == 0) {  // SwiGLU of the K-block's 32 outputs, staged for the down columns
+            const int u = (kb0 + k) * 32 + lane;
+            const float gv = flush_small(S.raw[2 * lane] * inv) + S.gub[k * 64 + 2 * lane];
+            const float uv = flush_small(S.raw[2 * lane + 1] * inv) + S.gub[k * 64 + 2 * lane + 1];
             if (uv != uv) nan_flag(st, pos, l, kNanUp);
             const float a = swiglu_balanced(gv, uv);
             if (a != a) nan_flag(st, pos, l, kNanFfnOut);
-            S.araw[k * 32 + p] = a;
-          });
-          fu_release(A, S, item++);
-          fu_sync();
+            (void)u;
+            mk_stage_elem(S.ast, S.ast + 32, lane, a);
+          }
           if (k == 0) fmark(step, l, 12);
-          if (wid == 0) mk_stage_elem(S.ast, S.ast + pl.kb_max * 32, k * 32 + lane, S.araw[k * 32 + lane]);
           const unsigned char* dslot = fu_wait_slot(A, S, item);
           fu_sync();
           if (*S.cabort) return;
-          // one column block: local block index k of the staged outputs
-          {
-            const int t = tid;
-            if (t < d / 4) {
-              const uint4* qs = reinterpret_cast<const uint4*>(dslot) + 4 * t;
-              const uint4 s4 = *reinterpret_cast<const uint4*>(dslot + (size_t)d * 16 + 16 * t);
-              const float xb = S.ast[pl.kb_max * 32 + k];
-              float A0, A1, A2, A3, sc, mn;
-              q4_pair_qx(qs[0], qs[1], true, S.ast, k, A0, A1);
-              q4_pair_qx(qs[2], qs[3], true, S.ast, k, A2, A3);
-              unpack_sm(s4.x, sc, mn);
-              y[0] = fmaf(sc, A0, fmaf(mn, xb, y[0]));
-              unpack_sm(s4.y, sc, mn);
-              y[1] = fmaf(sc, A1, fmaf(mn, xb, y[1]));
-              unpack_sm(s4.z, sc, mn);
-              y[2] = fmaf(sc, A2, fmaf(mn, xb, y[2]));
-              unpack_sm(s4.w, sc, mn);
-              y[3] = fmaf(sc, A3, fmaf(mn, xb, y[3]));
-            }
-          }
+          fu_cols(dslot, d, 1, S.ast, S.ast + 32, S.ycol, k == 0);
           fu_release(A, S, item++);
         }
         fmark(step, l, 13);
-        if (tid < d / 4) red_add4(yb + 4 * tid, y[0], y[1], y[2], y[3]);
+        if (tid < d / 4) {
+          const float4 y = reinterpret_cast<const float4*>(S.ycol)[tid];
+          red_add4(yb + 4 * tid, y.x, y.y, y.z, y.w);
+        }
       }
       fu_publish(flB + c, eB);
       fmark(step, l, 14);
     }
     // ================================================================ LM
-    {
-      const unsigned eLastB = fu_epoch(A.epoch0, L, step, L - 1, 1);
-      fmark(step, L, 0);
-      if (!fu_gate(flB, G, eLastB, S.cabort, st)) return;
-      fmark(step, L, 1);
-      const int gl = step * L + L - 1;
-      fu_add_sum(S.R, S.XA, A.yb + (gl & 1) * d, A.layers[L - 1].down.bias, d, st, pos, c == 0 ? L - 1 : -1);
-      fu_sync();
-      float ss = 0.f;
-      for (int i = tid; i < d; i += kFuConsumers) {
-        const float v = S.R[i];
-        ss = fmaf(v, v, ss);
-        S.xs[i] = v * __ldg(P.out_norm + i);
-      }
-      const float scale = 1.0f / sqrtf(fu_total(ss, red0, false) / (float)d + P.eps);
-      fmark(step, L, 2);
-      const float4* x4 = reinterpret_cast<const float4*>(S.xs);
-      const int K4 = d >> 2;
-      unsigned long long best = 0ull;
-      const int rbeg = c * pl.lm_rows_per_cta;
-      const int nrows = max(0, min(P.V, rbeg + pl.lm_rows_per_cta) - rbeg);
-      const int nitems = (nrows + pl.lm_stage_rows - 1) / pl.lm_stage_rows;
-      int cur = -1;
-      const unsigned char* slot = nullptr;
-#pragma unroll 1
-      for (int k = wid; k < nrows; k += kFuConsumerWarps) {
-        const int it = k / pl.lm_stage_rows;
-        while (cur < it) {
-          if (cur >= 0) fu_release(A, S, item + cur);
-          ++cur;
-          slot = fu_wait_slot(A, S, item + cur);
-        }
-        const float4* w4 = reinterpret_cast<const float4*>(slot) + (size_t)(k - it * pl.lm_stage_rows) * K4;
-        float a0 = 0.f, a1 = 0.f;
-#pragma unroll 2
-        for (int j = lane; j < K4; j += 32) {
-          const float4 u = w4[j], xv = x4[j];
-          a0 = fmaf(u.x, xv.x, a0);
-          a1 = fmaf(u.y, xv.y, a1);
-          a0 = fmaf(u.z, xv.z, a0);
-          a1 = fmaf(u.w, xv.w, a1);
-        }
-        const int row = rbeg + k;
-        float v = warp_sum(a0 + a1) * scale;
-        if (P.lm_bias) v += __ldg(P.lm_bias + row);
-        if (lane == 0) P.logits[row] = v;
-        const unsigned long long key = amax_key(v, (unsigned)row);
-        best = key > best ? key : best;
-      }
-      while (cur < nitems - 1) {
-        if (cur >= 0) fu_release(A, S, item + cur);
-        ++cur;
-        fu_wait_slot(A, S, item + cur);
-      }
-      if (cur >= 0) fu_release(A, S, item + cur);
-      item += nitems;
-      fmark(step, L, 3);
-      best = warp_max_u64(best);
-      __shared__ unsigned long long wbest[kFuConsumerWarps];
-      __shared__ int is_last;
-      if (lane == 0) wbest[wid] = best;
-      fu_sync();
-      if (*S.cabort) return;
-      if (tid == 0) {
-        unsigned long long b = 0;
-        for (int i = 0; i < kFuConsumerWarps; ++i) b = wbest[i] > b ? wbest[i] : b;
-        P.amax_part[c] = b;
-        __threadfence();
-        is_last = (atomicAdd(P.amax_cnt, 1u) == unsigned(G) - 1u);
-      }
-      fu_sync();
-      if (is_last) {
-        __threadfence();
-        unsigned long long b = 0;
-        for (int i = tid; i < G; i += kFuConsumers) {
-          const unsigned long long v = __ldcg(P.amax_part + i);
-          b = v > b ? v : b;
-        }
-        b = warp_max_u64(b);
-        if (lane == 0) wbest[wid] = b;
-        fu_sync();
-        if (tid == 0) {
-          unsigned long long r = 0;
-          for (int i = 0; i < kFuConsumerWarps; ++i) r = wbest[i] > r ? wbest[i] : r;
-          const unsigned idx = amax_index(r);
-          st->argmax = idx;
-          st->token = idx;
-          if (st->hist_len < P.hist_cap) P.tok_hist[st->hist_len] = idx;
-          st->hist_len += 1u;
-          st->pos = pos + 1u;
-          *P.amax_cnt = 0u;
-          fence_acq_rel_gpu();  // the state and the counter reset before the token word
-          st_ll(A.tok, __uint_as_float(idx), fu_epoch(A.epoch0, L, step, L, 0));
-        }
-      }
-      fu_sync();
-      fmark(step, L, 4);
-    }
+    unsigned long long* trow =
+        A.trace ? A.trace + (((size_t)c * A.n_steps + step) * (L + 1) + L) * kFuTrace : nullptr;
+    if (!fu_lm(A, S, step, pos, &item, trow)) return;
   }
 }
 
@@ -960,10 +1025,18 @@ __global__ void __launch_bounds__(kFuThreads, 1) k_decode_fused(FusedArgs A) {
   f += (size_t)pl.pv_groups * hd;
   S.ost = f;
   f += hd + 32;
-  S.araw = f;
-  f += pl.kb_max * 32;
   S.ast = f;
-  f += pl.kb_max * 32 + 32;
+  f += 64;
+  S.nw = f;
+  f += d;
+  S.rb = f;
+  f += 2 * hd;
+  S.gub = f;
+  f += pl.kb_max * 64;
+  S.raw = f;
+  f += mk_round32(hd > 64 ? hd : 64);
+  S.ycol = f;
+  f += d;
   S.misc = f;
   f += 64;
   S.slots = reinterpret_cast<unsigned char*>(f);
@@ -998,7 +1071,8 @@ __global__ void __launch_bounds__(kFuThreads, 1) k_decode_fused(FusedArgs A) {
 // Dynamic shared memory of the fused kernel.
 __host__ __device__ inline size_t fused_smem_bytes(const FusedPlan& p, int d, int hd) {
   const size_t floats = size_t(3) * d + mk_round32(d / 32) + hd + mk_round32(p.cap) + size_t(2) * p.cap * hd +
-                        size_t(p.pv_groups) * hd + hd + 32 + size_t(p.kb_max) * 64 + 32 + 64;
+                        size_t(p.pv_groups) * hd + hd + 32 + 64 + d + 2 * hd + size_t(p.kb_max) * 64 +
+                        mk_round32(hd > 64 ? hd : 64) + d + 64;
   return kFuHeader + floats * 4 + size_t(p.nslots) * p.slot_bytes;
 }
 

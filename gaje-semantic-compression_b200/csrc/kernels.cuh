@@ -511,6 +511,7 @@ struct AttnArgs {
   float scale;
   DevState* st;     // decode state (step) or nullptr (op level)
   int fresh;        // with ctx > 0: row ctx-1 is written by the preceding kernel (batched steps)
+  int max_splits;   // 0: kAttnMaxSplits (the launch's grid.y must cover the splits)
 };
 
 // One CTA per (kv head g, split s).  The split's cached K/V rows (positions
@@ -531,7 +532,7 @@ __device__ __forceinline__ void attn_split(const AttnArgs& A, const int g, const
   // the decode position is stable here (written two or more kernels back)
   const int ctx = A.ctx > 0 ? A.ctx : (int)__ldcg(&A.st->pos) + 1;
   int nsplit, chunk;
-  attn_splits(ctx, nsplit, chunk);
+  attn_splits(ctx, nsplit, chunk, A.max_splits > 0 ? A.max_splits : kAttnMaxSplits);
   if (s >= nsplit) return;
   const int t0 = s * chunk;
   const int n = min(ctx, t0 + chunk) - t0;
@@ -656,13 +657,18 @@ __device__ __forceinline__ void attn_split(const AttnArgs& A, const int g, const
   __syncthreads();
   for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
     const int j = idx / hd, e = idx - j * hd;
+    const float* po = A.part_o + ((size_t)g * kAttnMaxSplits * G + j) * hd + e;  // split r at + r*G*hd
     float O0 = 0.f, O1 = 0.f;
-    int r = 0;
-    for (; r + 1 < nsplit; r += 2) {
-      O0 += __ldcg(A.part_o + (((size_t)g * kAttnMaxSplits + r) * G + j) * hd + e) * wsh[j * nsplit + r];
-      O1 += __ldcg(A.part_o + (((size_t)g * kAttnMaxSplits + r + 1) * G + j) * hd + e) * wsh[j * nsplit + r + 1];
+    for (int r0 = 0; r0 < nsplit; r0 += 8) {  // eight partials in flight per thread
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = r0 + k < nsplit ? __ldcg(po + (size_t)(r0 + k) * G * hd) : 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; k += 2) {
+        if (r0 + k < nsplit) O0 += v[k] * wsh[j * nsplit + r0 + k];
+        if (r0 + k + 1 < nsplit) O1 += v[k + 1] * wsh[j * nsplit + r0 + k + 1];
+      }
     }
-    if (r < nsplit) O0 += __ldcg(A.part_o + (((size_t)g * kAttnMaxSplits + r) * G + j) * hd + e) * wsh[j * nsplit + r];
     A.out[((size_t)g * G + j) * hd + e] = (O0 + O1) * linv[j];
   }
   if (threadIdx.x == 0) A.cnt[g] = 0u;  // ready for the next launch
