@@ -1024,8 +1024,27 @@ cudaError_t batch_gemm(gaje_model* m, int Bi, const Q4Dev& q, const float* x, co
 // table (already on the device), in stream order, every launch after the
 // first a programmatic dependent launch.  Nothing here depends on the
 // streams' positions, so the sequence is captured once per Bi.
-int launch_batch(gaje_model* m, int Bi) {
+// Per-class timing of one eagerly launched batched step (profiling only).
+struct StepProf {
+  cudaEvent_t e0 = nullptr, e1 = nullptr;
+  float ms[GAJE_K_COUNT] = {};
+  uint32_t n[GAJE_K_COUNT] = {};
+};
+
+int launch_batch(gaje_model* m, int Bi, StepProf* prof = nullptr) {
   cudaStream_t st = m->stream;
+  auto t0 = [&]() {
+    if (prof) cudaEventRecord(prof->e0, st);
+  };
+  auto t1 = [&](int cls) {
+    if (!prof) return;
+    cudaEventRecord(prof->e1, st);
+    cudaEventSynchronize(prof->e1);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, prof->e0, prof->e1);
+    prof->ms[cls] += ms;
+    prof->n[cls] += 1;
+  };
   const size_t S = size_t(m->max_streams);
   BatchStreams bs{m->bdev, m->bdev + S, m->bdev + 2 * S};
   unsigned* d_argmax = m->bdev + 3 * S;
@@ -1040,20 +1059,31 @@ int launch_batch(gaje_model* m, int Bi) {
                            m->bx);
   for (int l = 0; l < L && e == cudaSuccess; ++l) {
     EpiQkvBatch eq{m->bq, m->bcache, bs, m->rope, m->nh, m->nkv, m->hd, int(m->info.rope_split), l};
+    t0();
     e = batch_gemm<true>(m, Bi, m->qkv[l], m->bx, TcNorm{m->attn_norm[l], eps, m->st, bs.pos, l}, eq);
+    t1(GAJE_K_QKV);
     if (e != cudaSuccess) break;
     AttnBatchArgs aa{m->bq, m->battn, m->bcache, bs, m->bpart_o, m->bpart_ml, m->bcnt, l, m->nh,
                      1.0f / sqrtf(float(m->hd)), asplit};
+    t0();
     e = launch_k(k_attn_batch, dim3(unsigned(m->nkv), unsigned(ns_max), unsigned(Bi)), dim3(kAttnThreads),
                  batch_attn_smem(m), st, true, aa);
+    t1(GAJE_K_ATTN);
     if (e != cudaSuccess) break;
+    t0();
     e = batch_gemm<false>(m, Bi, m->wo[l], m->battn, TcNorm{}, EpiResidBatch{m->bx, d, nullptr, bs, l});
+    t1(GAJE_K_OPROJ);
     if (e != cudaSuccess) break;
+    t0();
     e = batch_gemm<true>(m, Bi, m->gate_up[l], m->bx, TcNorm{m->ffn_norm[l], eps, nullptr, bs.pos, l},
                          EpiSwigluBatch{m->bact, m->ff, m->st, bs, l});
+    t1(GAJE_K_GATEUP);
     if (e != cudaSuccess) break;
+    t0();
     e = batch_gemm<false>(m, Bi, m->down[l], m->bact, TcNorm{}, EpiResidBatch{m->bx, d, m->st, bs, l});
+    t1(GAJE_K_DOWN);
   }
+  t0();
   if (m->nranks > 1) {  // vocab-sharded: the head runs after the step graph (sharded_head)
     if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
     return GAJE_OK;
@@ -1067,6 +1097,7 @@ int launch_batch(gaje_model* m, int Bi) {
       return set_error(GAJE_ERR_CUDA, "kernel launch: lm_head");
     e = launch_k(k_argmax_rows, dim3(unsigned(Bi)), dim3(512), 0, st, true, (const float*)m->blogits, m->V, d_argmax,
                  0u, (unsigned long long*)nullptr);
+    t1(GAJE_K_LMHEAD);
     if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
     return GAJE_OK;
   }
@@ -1090,6 +1121,7 @@ int launch_batch(gaje_model* m, int Bi) {
     e = MB == 8 ? launch_k(k_lmhead_batch<8, 4>, dim3(m->blm_grid), dim3(kLbThreads), smem, st, true, la)
                 : launch_k(k_lmhead_batch<16, 2>, dim3(m->blm_grid), dim3(kLbThreads), smem, st, true, la);
   }
+  t1(GAJE_K_LMHEAD);
   if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
   return GAJE_OK;
 }
@@ -1799,6 +1831,43 @@ int gaje_cuda_forward_batch(gaje_model* m, const uint32_t* stream_ids, const uin
   for (size_t b = 0; b < B; ++b) m->bpos[stream_ids[b]] += 1u;
   if (argmax_out)
     for (size_t b = 0; b < B; ++b) argmax_out[b] = m->h_bdev[3 * S + b];
+  return m->check_state();
+}
+
+int gaje_cuda_profile_batch(gaje_model* m, const uint32_t* stream_ids, const uint32_t* tokens, size_t B, float* ms,
+                            uint32_t* launches) {
+  if (!m || !B || !stream_ids || !tokens) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  if (m->max_streams <= 0 || B > size_t(m->max_streams)) return set_error(GAJE_ERR_INVALID, "bad batch size");
+  if (m->nranks > 1) return set_error(GAJE_ERR_UNSUPPORTED, "profile a single-GPU model");
+  if (m->block_k() > 0 || m->info.use_genomic_norm)
+    return set_error(GAJE_ERR_UNSUPPORTED, "block K-WTA / use_genomic_norm are not implemented on the batched path");
+  const size_t S = size_t(m->max_streams);
+  std::vector<char> seen(S, 0);
+  for (size_t b = 0; b < B; ++b) {
+    const uint32_t sid = stream_ids[b];
+    if (sid >= S || seen[sid]) return set_error(GAJE_ERR_INVALID, "stream ids must be distinct and < max_streams");
+    seen[sid] = 1;
+    if (m->bpos[sid] >= uint32_t(m->max_ctx)) return set_error(GAJE_ERR_CONTEXT, "KV cache full (max_ctx positions)");
+    m->h_bdev[b] = tokens[b];
+    m->h_bdev[S + b] = m->bpos[sid];
+    m->h_bdev[2 * S + b] = sid;
+  }
+  CK(cudaSetDevice(m->device));
+  CK(cudaMemcpyAsync(m->bdev, m->h_bdev, 3 * S * sizeof(unsigned), cudaMemcpyHostToDevice, m->stream));
+  StepProf prof;
+  CK(cudaEventCreate(&prof.e0));
+  CK(cudaEventCreate(&prof.e1));
+  const int s = launch_batch(m, int(B), &prof);
+  cudaEventDestroy(prof.e0);
+  cudaEventDestroy(prof.e1);
+  if (s) return s;
+  CK(cudaMemcpyAsync(m->h_st, m->st, sizeof(DevState), cudaMemcpyDeviceToHost, m->stream));
+  CK(cudaStreamSynchronize(m->stream));
+  for (size_t b = 0; b < B; ++b) m->bpos[stream_ids[b]] += 1u;
+  for (int k = 0; k < GAJE_K_COUNT; ++k) {
+    if (ms) ms[k] = prof.ms[k];
+    if (launches) launches[k] = prof.n[k];
+  }
   return m->check_state();
 }
 

@@ -142,6 +142,7 @@ def lib() -> C.CDLL:
         "gaje_cuda_profile_phases": ([vp, u32, sz, vp, vp, vp], i32),
         "gaje_cuda_trace_steps": ([vp, u32, sz, vp, sz, vp], i32),
         "gaje_cuda_trace_fused": ([vp, u32, sz, vp, sz, vp], i32),
+        "gaje_cuda_profile_batch": ([vp, vp, vp, sz, vp, vp], i32),
         "gaje_cuda_attention_decode_static": ([vp, vp, vp, sz, sz, sz, sz, sz, vp, vp], i32),
         "gaje_cuda_forward_batch": ([vp, vp, vp, sz, vp, vp], i32),
         "gaje_cuda_prefill": ([vp, u32, vp, sz, vp, vp], i32),
@@ -417,6 +418,17 @@ class GenomicLLM:
         _check(lib().gaje_cuda_prefill(self._m, int(stream_id), _ptr(toks), toks.size, _ptr(am),
                                        _ptr(lg) if logits else None))
         return (int(am[0]), lg) if logits else int(am[0])
+
+    def profile_batch(self, stream_ids: Sequence[int], tokens: Sequence[int]) -> dict:
+        """One batched step launched kernel by kernel: milliseconds per kernel
+        class (all blocks together)."""
+        sids = np.ascontiguousarray(list(stream_ids), dtype=np.uint32)
+        toks = np.ascontiguousarray(list(tokens), dtype=np.uint32)
+        ms = np.zeros(7, dtype=np.float32)
+        n = np.zeros(7, dtype=np.uint32)
+        _check(lib().gaje_cuda_profile_batch(self._m, _ptr(sids), _ptr(toks), sids.size, _ptr(ms), _ptr(n)))
+        names = ["qkv", "attn", "oproj", "gateup", "down", "lmhead", "kwta"]
+        return {names[k]: float(ms[k]) for k in range(6)}
 
     def clear_stream(self, stream_id: int) -> None:
         _check(lib().gaje_cuda_clear_stream(self._m, int(stream_id)))

@@ -261,6 +261,16 @@ int gaje_vocab_shard(uint32_t vocab_size, int nranks, int rank, uint32_t* row0, 
 uint64_t gaje_argmax_key(float value, uint32_t index);
 uint32_t gaje_argmax_key_index(uint64_t key);
 
+/* One batched step (the arguments of gaje_cuda_forward_batch, argmax and
+ * logits not returned) launched kernel by kernel with CUDA events around each
+ * kernel class: ms[GAJE_K_COUNT] receives the milliseconds spent in each
+ * class (all blocks together), launches[GAJE_K_COUNT] the event brackets per
+ * class (either may be NULL).  The streams advance as by a real step.  The
+ * reference's counterpart is the GAJE_PROFILE_VERBOSE timing of
+ * src/nn/llm/forward.rs:23-55. */
+int gaje_cuda_profile_batch(gaje_model* model, const uint32_t* stream_ids, const uint32_t* tokens, size_t B,
+                            float* ms, uint32_t* launches);
+
 /* clear_cache_core for one batched stream. */
 int gaje_cuda_clear_stream(gaje_model* model, uint32_t stream_id);
 /* A batched stream's cache length. */
