@@ -154,6 +154,248 @@ __global__ void __launch_bounds__(kAttnThreads) k_attn_batch(AttnBatchArgs B) {
   attn_split(a, blockIdx.x, blockIdx.y);
 }
 
+// Batched decode attention, streamed: one CTA per (KV head, split, stream)
+// over positions [t0, t0 + n) of the stream's cache (the step's own row
+// included: the QKV kernel wrote it before this one).  The split's K rows and
+// then its V rows pass through a ring of kAbStages shared-memory tiles of
+// kAbTile rows (1-D TMA bulk copies, one mbarrier per stage), so loads run
+// ahead of the arithmetic.  Scores: warp w takes positions 4w..4w+3 of a
+// tile, lane l holds dims [VEC*l, VEC*l + VEC) of each of the G query heads in
+// registers, and one butterfly reduce-scatter per warp turns the 4*G partial
+// dots into one sum per lane.  Softmax over the split as in
+// attention.rs:88-127 (split max, exp, sum).  P*V: warp j < G owns query head
+// j, lane l its VEC dims, summing over the split's positions in order.  One
+// split: out = O * (1/(l + 1e-12)); several: partials, and the last CTA of the
+// (stream, KV head) combines them (attn_combine).
+constexpr int kAbThreads = 256;
+constexpr int kAbWarps = kAbThreads / 32;
+constexpr int kAbTile = 32;       // positions per tile
+constexpr int kAbStages = 4;
+constexpr int kAbMaxChunk = 512;  // positions per split (scores held in shared memory)
+constexpr int kAbMaxGroup = 8;    // query heads per KV head
+__host__ __device__ inline size_t attn_batch2_smem(int G, int hd) {
+  return 128 + size_t(kAbStages) * kAbTile * hd * 4 + size_t(G) * kAbMaxChunk * 4;
+}
+// Splits of a stream at context ctx when a launch allows at most ms.
+__host__ __device__ inline void attn_batch2_splits(int ctx, int ms, int& nsplit, int& chunk) {
+  int n0 = (ctx + 63) / 64;
+  if (n0 > ms) n0 = ms;
+  if (n0 < 1) n0 = 1;
+  chunk = (ctx + n0 - 1) / n0;
+  nsplit = (ctx + chunk - 1) / chunk;
+}
+
+// The combine of the last CTA of (stream, KV head): weights e^{m_s - M},
+// out = (sum_s O_s w_s) * (1/(sum_s l_s w_s + 1e-12)).
+__device__ __forceinline__ void attn_combine(const float* part_o, const float* part_ml, int G, int hd, int nsplit,
+                                             float* out, float* wsh, float* linv) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int idx = threadIdx.x; idx < G * nsplit; idx += blockDim.x) {
+    const int j = idx / nsplit, r = idx - j * nsplit;
+    wsh[idx] = __ldcg(part_ml + ((size_t)r * G + j) * 2);
+  }
+  __syncthreads();
+  for (int j = wid; j < G; j += nw) {
+    float M = -INFINITY;
+    for (int r = lane; r < nsplit; r += kWarp) M = fmaxf(M, wsh[j * nsplit + r]);
+    M = warp_max(M);
+    float Lsum = 0.f;
+    for (int r = lane; r < nsplit; r += kWarp) {
+      const float w = expf(wsh[j * nsplit + r] - M);
+      wsh[j * nsplit + r] = w;
+      Lsum += __ldcg(part_ml + ((size_t)r * G + j) * 2 + 1) * w;
+    }
+    Lsum = warp_sum(Lsum);
+    if (lane == 0) linv[j] = 1.0f / (Lsum + 1e-12f);
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
+    const int j = idx / hd, e = idx - j * hd;
+    const float* po = part_o + (size_t)j * hd + e;  // split r at + r*G*hd
+    float O0 = 0.f, O1 = 0.f;
+    for (int r0 = 0; r0 < nsplit; r0 += 8) {  // eight partials in flight per thread
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = r0 + k < nsplit ? __ldcg(po + (size_t)(r0 + k) * G * hd) : 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; k += 2) {
+        if (r0 + k < nsplit) O0 += v[k] * wsh[j * nsplit + r0 + k];
+        if (r0 + k + 1 < nsplit) O1 += v[k + 1] * wsh[j * nsplit + r0 + k + 1];
+      }
+    }
+    out[(size_t)j * hd + e] = (O0 + O1) * linv[j];
+  }
+}
+
+template <int VEC>
+__global__ void __launch_bounds__(kAbThreads) k_attn_batch2(AttnBatchArgs B) {
+  constexpr int HD = 32 * VEC;
+  extern __shared__ __align__(128) unsigned char ab_smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(ab_smem);  // [kAbStages]
+  float* tiles = reinterpret_cast<float*>(ab_smem + 128);   // [kAbStages][kAbTile][HD]
+  float* ps = tiles + (size_t)kAbStages * kAbTile * HD;     // [G][kAbMaxChunk]
+  __shared__ float ml_s[2 * kAbMaxGroup];
+  __shared__ float wsh[kAbMaxGroup * kAttnMaxSplits];
+  __shared__ float linv[kAbMaxGroup];
+  __shared__ int is_last;
+  const int g = blockIdx.x, s = blockIdx.y, b = blockIdx.z;
+  const int nkv = B.cache.nkv, G = B.nh / nkv;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  pdl_wait();
+  pdl_trigger();
+  const int ctx = int(B.bs.pos[b]) + 1;
+  int nsplit, chunk;
+  attn_batch2_splits(ctx, B.max_splits, nsplit, chunk);
+  if (s >= nsplit) return;
+  const int t0 = s * chunk, n = min(ctx, t0 + chunk) - t0;
+  const int ntile = (n + kAbTile - 1) / kAbTile;
+  const int nitems = 2 * ntile;  // K tiles, then V tiles
+  const unsigned sid = B.bs.sid[b];
+  const float* kbase = B.cache.k + B.cache.row(sid, B.layer, g, unsigned(t0));
+  const float* vbase = B.cache.v + B.cache.row(sid, B.layer, g, unsigned(t0));
+  if (tid == 0) {
+    for (int i = 0; i < kAbStages; ++i) mbar_init(full + i, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  auto issue = [&](int it) {  // thread 0: item it into stage it % kAbStages
+    const int k = it < ntile ? it : it - ntile;
+    const int rows = min(kAbTile, n - k * kAbTile);
+    const float* src = (it < ntile ? kbase : vbase) + (size_t)k * kAbTile * HD;
+    const uint32_t bytes = uint32_t(rows) * HD * 4;
+    uint64_t* bar = full + (it % kAbStages);
+    mbar_expect_tx(bar, bytes);
+    bulk_g2s(tiles + (size_t)(it % kAbStages) * kAbTile * HD, src, bytes, bar);
+  };
+  if (tid == 0)
+    for (int it = 0; it < min(kAbStages, nitems); ++it) issue(it);
+  // this lane's dims of the G query heads
+  float q[kAbMaxGroup][VEC];
+  const float* qg = B.q + (size_t)b * B.nh * HD + (size_t)g * G * HD;
+#pragma unroll
+  for (int j = 0; j < kAbMaxGroup; ++j)
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) q[j][v] = j < G ? __ldcg(qg + (size_t)j * HD + VEC * lane + v) : 0.f;
+  bool ok = true;
+  // ---- scores: warp w, positions 4w..4w+3 of each tile
+  for (int k = 0; k < ntile; ++k) {
+    if (!mbar_wait(full + (k % kAbStages), (k / kAbStages) & 1)) ok = false;
+    const float* tk = tiles + (size_t)(k % kAbStages) * kAbTile * HD;
+    float part[4 * kAbMaxGroup];  // value (head j, position 4w+tq) at [j*4 + tq]
+#pragma unroll
+    for (int tq = 0; tq < 4; ++tq) {
+      const int t = 4 * wid + tq;
+      float kv[VEC];
+      if constexpr (VEC == 4) {
+        const float4 x = reinterpret_cast<const float4*>(tk + (size_t)t * HD)[lane];
+        kv[0] = x.x; kv[1] = x.y; kv[2] = x.z; kv[3] = x.w;
+      } else if constexpr (VEC == 2) {
+        const float2 x = reinterpret_cast<const float2*>(tk + (size_t)t * HD)[lane];
+        kv[0] = x.x; kv[1] = x.y;
+      } else {
+        kv[0] = tk[(size_t)t * HD + lane];
+      }
+#pragma unroll
+      for (int j = 0; j < kAbMaxGroup; ++j) {
+        float a = 0.f;
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) a = fmaf(q[j][v], kv[v], a);
+        part[j * 4 + tq] = a;
+      }
+    }
+    // butterfly reduce-scatter of 32 values over 32 lanes: lane l ends with
+    // the full sum of value l
+#pragma unroll
+    for (int o = 16, h = 16; o >= 1; o >>= 1, h >>= 1) {
+      const bool up = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < h; ++i) {
+        const float send = up ? part[i] : part[i + h];
+        const float keep = up ? part[i + h] : part[i];
+        part[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+    }
+    {
+      // level o keeps the half of the values selected by lane bit o, so after
+      // the five levels lane l holds value index l
+      const int j = lane >> 2, tq = lane & 3;
+      const int t = k * kAbTile + 4 * wid + tq;
+      if (j < G && t < n) ps[j * kAbMaxChunk + t] = part[0] * B.scale;
+    }
+    __syncthreads();  // the stage is consumed
+    if (tid == 0 && k + kAbStages < nitems) issue(k + kAbStages);
+  }
+  // ---- softmax over the split: warp j < G owns head j
+  if (wid < G) {
+    float* pr = ps + wid * kAbMaxChunk;
+    float m = -INFINITY;
+    for (int t = lane; t < n; t += kWarp) m = fmaxf(m, pr[t]);
+    m = warp_max(m);
+    float l = 0.f;
+    for (int t = lane; t < n; t += kWarp) {
+      const float e = expf(pr[t] - m);
+      pr[t] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) {
+      ml_s[2 * wid] = m;
+      ml_s[2 * wid + 1] = l;
+    }
+  }
+  __syncthreads();
+  // ---- P*V
+  float acc[VEC];
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
+  for (int k = 0; k < ntile; ++k) {
+    const int it = ntile + k;
+    if (!mbar_wait(full + (it % kAbStages), (it / kAbStages) & 1)) ok = false;
+    const float* tv = tiles + (size_t)(it % kAbStages) * kAbTile * HD;
+    if (wid < G) {
+      const float* pr = ps + wid * kAbMaxChunk + k * kAbTile;
+      const int rows = min(kAbTile, n - k * kAbTile);
+      for (int t = 0; t < rows; ++t) {
+        const float p = pr[t];
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) acc[v] = fmaf(p, tv[(size_t)t * HD + VEC * lane + v], acc[v]);
+      }
+    }
+    __syncthreads();
+    if (tid == 0 && it + kAbStages < nitems) issue(it + kAbStages);
+  }
+  if (!ok) return;  // a copy that never landed: the step's outputs stay stale (bounded waits, no hang)
+  float* outg = B.out + (size_t)b * B.nh * HD + (size_t)g * G * HD;
+  if (nsplit == 1) {
+    if (wid < G) {
+      const float inv = 1.0f / (ml_s[2 * wid + 1] + 1e-12f);
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) outg[(size_t)wid * HD + VEC * lane + v] = acc[v] * inv;
+    }
+    return;
+  }
+  const size_t pbase = ((size_t)b * nkv + g) * kAttnMaxSplits;  // (stream, KV head) partials
+  float* po = B.part_o + (pbase + s) * G * HD;
+  float* pml = B.part_ml + (pbase + s) * G * 2;
+  if (wid < G) {
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) po[(size_t)wid * HD + VEC * lane + v] = acc[v];
+    if (lane == 0) {
+      pml[2 * wid] = ml_s[2 * wid];
+      pml[2 * wid + 1] = ml_s[2 * wid + 1];
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  unsigned* cnt = B.cnt + (size_t)b * nkv + g;
+  if (tid == 0) is_last = (atomicAdd(cnt, 1u) == (unsigned)nsplit - 1u);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  attn_combine(B.part_o + pbase * G * HD, B.part_ml + pbase * G * 2, G, HD, nsplit, outg, wsh, linv);
+  if (tid == 0) *cnt = 0u;  // ready for the next launch
+}
+
 // Causal attention for a prefill chunk of one stream: rows m = 0..n-1 at
 // positions p0 + m, each attending to its stream's cached positions
 // 0..p0+m (the chunk's own k/v rows are written by the QKV kernel before

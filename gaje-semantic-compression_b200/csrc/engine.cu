@@ -935,6 +935,26 @@ int batch_attn_splits(const gaje_model* m, int Bi) {
   const int by_fill = (2 * m->sms + Bi * m->nkv - 1) / (Bi * m->nkv);
   return std::max(1, std::min(kAttnMaxSplits, std::max(by_smem, by_fill)));
 }
+// The streamed attention kernel (k_attn_batch2) serves head_dim 32/64/128 with
+// at most kAbMaxGroup query heads per KV head; its splits hold at most
+// kAbMaxChunk positions and fill the SMs twice.
+bool batch_attn2(const gaje_model* m) {
+  return (m->hd == 32 || m->hd == 64 || m->hd == 128) && m->nh / m->nkv <= kAbMaxGroup;
+}
+int batch_attn2_splits(const gaje_model* m, int Bi) {
+  const int by_len = (m->max_ctx + kAbMaxChunk - 1) / kAbMaxChunk;
+  const int by_fill = (2 * m->sms + Bi * m->nkv - 1) / (Bi * m->nkv);
+  return std::max(1, std::min(kAttnMaxSplits, std::max(by_len, by_fill)));
+}
+cudaError_t launch_attn2(gaje_model* m, int Bi, const AttnBatchArgs& aa) {
+  const dim3 grid(unsigned(m->nkv), unsigned(aa.max_splits), unsigned(Bi));
+  const size_t smem = attn_batch2_smem(m->nh / m->nkv, m->hd);
+  switch (m->hd) {
+    case 32: return launch_k(k_attn_batch2<1>, grid, dim3(kAbThreads), smem, m->stream, true, aa);
+    case 64: return launch_k(k_attn_batch2<2>, grid, dim3(kAbThreads), smem, m->stream, true, aa);
+    default: return launch_k(k_attn_batch2<4>, grid, dim3(kAbThreads), smem, m->stream, true, aa);
+  }
+}
 size_t batch_attn_smem(const gaje_model* m) {  // the largest chunk any batch size gives
   const int ms = std::min(kAttnMaxSplits, std::max(1, (m->max_ctx + kBatchAttnRows - 1) / kBatchAttnRows));
   return attn_smem_bytes(m->nh / m->nkv, m->hd, attn_chunk_max(m->max_ctx, ms));
@@ -948,6 +968,12 @@ int batch_setup(gaje_model* m) {
   if (int e = smem_optin((const void*)k_q4_gemm_skinny<kBatchMT, false, EpiResidBatch>, sk)) return e;
   if (int e = smem_optin((const void*)k_q4_gemm_skinny<kBatchMT, true, EpiSwigluBatch>, sk)) return e;
   if (int e = smem_optin((const void*)k_attn_batch, batch_attn_smem(m))) return e;
+  if (batch_attn2(m)) {
+    const size_t s2 = attn_batch2_smem(m->nh / m->nkv, m->hd);
+    if (int e = smem_optin((const void*)k_attn_batch2<1>, s2)) return e;
+    if (int e = smem_optin((const void*)k_attn_batch2<2>, s2)) return e;
+    if (int e = smem_optin((const void*)k_attn_batch2<4>, s2)) return e;
+  }
   if (m->pf_rows > 0)
     if (int e = smem_optin((const void*)k_attn_prefill, attn_prefill_smem(m->nh / m->nkv, m->hd))) return e;
   const size_t lm8 = size_t(8) * m->d * 4, lm16 = size_t(16) * m->d * 4;
@@ -1066,8 +1092,13 @@ int launch_batch(gaje_model* m, int Bi, StepProf* prof = nullptr) {
     AttnBatchArgs aa{m->bq, m->battn, m->bcache, bs, m->bpart_o, m->bpart_ml, m->bcnt, l, m->nh,
                      1.0f / sqrtf(float(m->hd)), asplit};
     t0();
-    e = launch_k(k_attn_batch, dim3(unsigned(m->nkv), unsigned(ns_max), unsigned(Bi)), dim3(kAttnThreads),
-                 batch_attn_smem(m), st, true, aa);
+    if (batch_attn2(m)) {
+      aa.max_splits = batch_attn2_splits(m, Bi);
+      e = launch_attn2(m, Bi, aa);
+    } else {
+      e = launch_k(k_attn_batch, dim3(unsigned(m->nkv), unsigned(ns_max), unsigned(Bi)), dim3(kAttnThreads),
+                   batch_attn_smem(m), st, true, aa);
+    }
     t1(GAJE_K_ATTN);
     if (e != cudaSuccess) break;
     t0();

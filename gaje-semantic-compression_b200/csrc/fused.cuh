@@ -429,33 +429,34 @@ __device__ __forceinline__ void fu_rows_raw(const unsigned char* slot, int nr, i
   }
 }
 
-// ycol[4t..4t+3] (+)= the raw dots of rows 4t..4t+3 (t < d/4) over nkb
+// ycol[2p], ycol[2p+1] (+)= the raw dots of rows 2p, 2p+1 over nkb
 // K-block-major column blocks against the staged xst / xsum (local block
-// index); init starts the accumulators at zero.
+// index), a thread per row pair (pairs p = tid, tid + 480, ...); init starts
+// the accumulators at zero.
 __device__ __forceinline__ void fu_cols(const unsigned char* slot, int d, int nkb, const float* xst, const float* xsum,
                                      float* ycol, bool init) {
-  const int t = threadIdx.x;
-  if (t >= d / 4) return;
   const uint4* qs = reinterpret_cast<const uint4*>(slot);
   const uint32_t* sm = reinterpret_cast<const uint32_t*>(slot + (size_t)nkb * d * 16);
-  float4 y = init ? make_float4(0.f, 0.f, 0.f, 0.f) : reinterpret_cast<const float4*>(ycol)[t];
 #pragma unroll 1
-  for (int kb = 0; kb < nkb; ++kb) {
-    const uint4* q = qs + (size_t)kb * d + 4 * t;
-    const uint4 s4 = *reinterpret_cast<const uint4*>(sm + (size_t)kb * d + 4 * t);
-    const float xb = xsum[kb];
-    float A0, A1, A2, A3, sc, mn;
-    q4_quad_qx(q[0], q[1], q[2], q[3], xst, kb, A0, A1, A2, A3);
-    unpack_sm(s4.x, sc, mn);
-    y.x = fmaf(sc, A0, fmaf(mn, xb, y.x));
-    unpack_sm(s4.y, sc, mn);
-    y.y = fmaf(sc, A1, fmaf(mn, xb, y.y));
-    unpack_sm(s4.z, sc, mn);
-    y.z = fmaf(sc, A2, fmaf(mn, xb, y.z));
-    unpack_sm(s4.w, sc, mn);
-    y.w = fmaf(sc, A3, fmaf(mn, xb, y.w));
+  for (int p = threadIdx.x; p < d / 2; p += kFuConsumers) {
+    float2 y = init ? make_float2(0.f, 0.f) : reinterpret_cast<const float2*>(ycol)[p];
+#pragma unroll 1
+    for (int kb = 0; kb < nkb; ++kb) {
+      const uint4* q = qs + (size_t)kb * d + 2 * p;
+      const uint2 s2 = *reinterpret_cast<const uint2*>(sm + (size_t)kb * d + 2 * p);
+      const float xb = xsum[kb];
+      float A0, A1, sc, mn;
+      q4_pair_qx(q[0], q[1], true, xst, kb, A0, A1);
+      unpack_sm(s2.x, sc, mn);
+      y.x = fmaf(sc, A0, fmaf(mn, xb, y.x));
+      unpack_sm(s2.y, sc, mn);
+      y.y = fmaf(sc, A1, fmaf(mn, xb, y.y));
+    }
+    reinterpret_cast<float2*>(ycol)[p] = y;
   }
-  reinterpret_cast<float4*>(ycol)[t] = y;
+}
+__device__ __forceinline__ void red_add2(float* p, float a, float b) {
+  asm volatile("red.relaxed.gpu.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
 }
 
 // Issues the TMA copies of split s's cached K/V rows of block l at `cached`
@@ -911,14 +912,16 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
           fu_release(A, S, item++);
           fmark(step, l, 6);
           if (wid == 0) fu_split_weight(A, S, pos, h, n, eA);
+          fmark(step, l, 15);
           fu_sync();
           if (*S.cabort) return;
           const float cf = S.misc[32];
           fmark(step, l, 7);
-          if (n > 0 && tid < d / 4) {
-            const float4 y = reinterpret_cast<const float4*>(S.ycol)[tid];
-            red_add4(ya + 4 * tid, cf * y.x, cf * y.y, cf * y.z, cf * y.w);
-          }
+          if (n > 0)
+            for (int p = tid; p < d / 2; p += kFuConsumers) {
+              const float2 y = reinterpret_cast<const float2*>(S.ycol)[p];
+              red_add2(ya + 2 * p, cf * y.x, cf * y.y);
+            }
           fu_publish(flA + c, eA);
           fmark(step, l, 8);
         }
@@ -978,9 +981,9 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
           fu_release(A, S, item++);
         }
         fmark(step, l, 13);
-        if (tid < d / 4) {
-          const float4 y = reinterpret_cast<const float4*>(S.ycol)[tid];
-          red_add4(yb + 4 * tid, y.x, y.y, y.z, y.w);
+        for (int p = tid; p < d / 2; p += kFuConsumers) {
+          const float2 y = reinterpret_cast<const float2*>(S.ycol)[p];
+          red_add2(yb + 2 * p, y.x, y.y);
         }
       }
       fu_publish(flB + c, eB);
