@@ -607,6 +607,7 @@ struct LmBatchArgs {
   unsigned long long* keys;  // [B] the winning amax_key of each vector, or nullptr
   unsigned row_offset;  // global index of W's row 0 (a vocab shard's first row)
   int V, d, B, rows_per_cta;
+  int flush;            // 1: flush |t| < 1e-6 to 0 before the bias (a Q8_0 lm_head)
 };
 template <int MB, int RPW>
 __global__ void __launch_bounds__(kLbThreads) k_lmhead_batch(LmBatchArgs A) {
@@ -685,7 +686,9 @@ __global__ void __launch_bounds__(kLbThreads) k_lmhead_batch(LmBatchArgs A) {
 #pragma unroll
       for (int b = 0; b < MB; ++b) {
         if (b < A.B) {
-          const float v = warp_sum(acc[q][b]) + bb;
+          float v = warp_sum(acc[q][b]);
+          if (A.flush) v = flush_small(v);
+          v += bb;
           if (lane == 0) A.logits[(size_t)b * A.V + r] = v;
           const unsigned long long key = amax_key(v, (unsigned)r + A.row_offset);
           best[b] = key > best[b] ? key : best[b];

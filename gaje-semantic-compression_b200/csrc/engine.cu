@@ -449,6 +449,7 @@ struct gaje_model {
     LmArgs a;
     a.W = lm_head;
     a.bias = lm_bias;
+    a.flush = P.lm_flush;
     a.x = x;
     a.norm_w = out_norm;
     a.eps = P.eps;
@@ -1148,6 +1149,7 @@ int launch_batch(gaje_model* m, int Bi, StepProf* prof = nullptr) {
     la.d = d;
     la.B = std::min(MB, Bi - b0);
     la.rows_per_cta = (m->V + m->blm_grid - 1) / m->blm_grid;
+    la.flush = m->P.lm_flush;
     const size_t smem = size_t(MB) * d * 4;
     e = MB == 8 ? launch_k(k_lmhead_batch<8, 4>, dim3(m->blm_grid), dim3(kLbThreads), smem, st, true, la)
                 : launch_k(k_lmhead_batch<16, 2>, dim3(m->blm_grid), dim3(kLbThreads), smem, st, true, la);
@@ -1203,6 +1205,7 @@ int launch_prefill_chunk(gaje_model* m, int nc, int p0, unsigned sid, bool head)
     la.d = d;
     la.B = 1;
     la.rows_per_cta = (m->V + m->blm_grid - 1) / m->blm_grid;
+    la.flush = m->P.lm_flush;
     e = launch_k(k_lmhead_batch<8, 4>, dim3(m->blm_grid), dim3(kLbThreads), size_t(8) * d * 4, st, true, la);
   }
   if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
@@ -1262,6 +1265,7 @@ int sharded_head(gaje_model* m, const float* x_local, int B, unsigned* d_argmax)
       la.d = d;
       la.B = std::min(MB, M - b0);
       la.rows_per_cta = (m->Vl + m->blm_grid - 1) / m->blm_grid;
+      la.flush = m->P.lm_flush;
       const size_t smem = size_t(MB) * d * 4;
       e = MB == 8 ? launch_k(k_lmhead_batch<8, 4>, dim3(m->blm_grid), dim3(kLbThreads), smem, st, false, la)
                   : launch_k(k_lmhead_batch<16, 2>, dim3(m->blm_grid), dim3(kLbThreads), smem, st, false, la);
@@ -1310,8 +1314,8 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   std::string err;
   if (int s = f.open(path, err)) return set_error(s, err);
   const gaje_flat_info& I = f.info;
-  if (I.embd_bit_depth != 32 || I.lm_head_bit_depth != 32)
-    return set_error(GAJE_ERR_UNSUPPORTED, "Q8_0 token_embd/lm_head are not implemented on the device yet");
+  if ((I.embd_bit_depth != 32 && I.embd_bit_depth != 8) || (I.lm_head_bit_depth != 32 && I.lm_head_bit_depth != 8))
+    return set_error(GAJE_ERR_UNSUPPORTED, "token_embd/lm_head must be f32 or Q8_0");
   if (I.n_embd % 32 != 0) return set_error(GAJE_ERR_UNSUPPORTED, "n_embd must be a multiple of 32");
   m->info = I;
   m->d = int(I.n_embd);
@@ -1554,12 +1558,31 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     CK(cudaMemcpy(m->ffn_norm[l], f.blob(b.ffn_norm->dna_off, d * 4), d * 4, cudaMemcpyHostToDevice));
   }
   CK(cudaMemcpy(m->out_norm, f.blob(f.output_norm->dna_off, d * 4), d * 4, cudaMemcpyHostToDevice));
-  CK(cudaMemcpy(m->embd, f.blob(f.token_embd->dna_off, V * d * 4), V * d * 4, cudaMemcpyHostToDevice));
-  {  // this rank's lm_head rows [v0, v0 + Vl)
-    const size_t r0 = size_t(m->v0), nr = size_t(m->Vl);
-    CK(cudaMemcpy(m->lm_head, f.blob(f.lm_head->dna_off + r0 * d * 4, nr * d * 4), nr * d * 4,
-                  cudaMemcpyHostToDevice));
-  }
+  // f32 rows as stored; Q8_0 rows (--quant-embed exports) dequantised to the
+  // f32 values the reference computes, q * scale (blocks.rs:44-48, exact)
+  auto upload_rows = [&](const FlatEntry* e, size_t r0, size_t nr, float* dst) -> int {
+    if (e->bit_depth == 32) {
+      CK(cudaMemcpy(dst, f.blob(e->dna_off + r0 * d * 4, nr * d * 4), nr * d * 4, cudaMemcpyHostToDevice));
+      return GAJE_OK;
+    }
+    const size_t nb = d / 32;
+    const uint8_t* src = f.blob(e->dna_off + r0 * nb * 34, nr * nb * 34);
+    if (!src) return set_error(GAJE_ERR_IO, "Q8_0 rows out of range");
+    std::vector<float> host(nr * d);
+#pragma omp parallel for schedule(static)
+    for (long long r = 0; r < (long long)nr; ++r)
+      for (size_t b = 0; b < nb; ++b) {
+        const uint8_t* blk = src + (size_t(r) * nb + b) * 34;
+        uint16_t hs;
+        memcpy(&hs, blk, 2);
+        const float sc = f16_to_f32(hs);
+        for (int k = 0; k < 32; ++k) host[size_t(r) * d + b * 32 + k] = float(int8_t(blk[2 + k])) * sc;
+      }
+    CK(cudaMemcpy(dst, host.data(), nr * d * 4, cudaMemcpyHostToDevice));
+    return GAJE_OK;
+  };
+  if (int s = upload_rows(f.token_embd, 0, V, m->embd)) return s;
+  if (int s = upload_rows(f.lm_head, size_t(m->v0), size_t(m->Vl), m->lm_head)) return s;  // this rank's rows
   if (m->lm_bias) {
     std::vector<float> b(V, 0.0f);
     memcpy(b.data(), f.blob(f.lm_head->bias_off, f.lm_head->bias_len), f.lm_head->bias_len);
@@ -1608,6 +1631,7 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   P.embd = m->embd;
   P.lm_head = m->lm_head;
   P.lm_bias = m->lm_bias;
+  P.lm_flush = I.lm_head_bit_depth == 8 ? 1 : 0;
   P.out_norm = m->out_norm;
   P.rope = m->rope;
   P.x = m->x;

@@ -108,6 +108,7 @@ struct StepParams {
   const float* embd;     // f32 [V][d]
   const float* lm_head;  // f32 [V][d]
   const float* lm_bias;  // [V] or nullptr
+  int lm_flush;          // 1: the |t| < 1e-6 -> 0 flush of a Q8_0 lm_head row dot (genomic.rs:444-448)
   const float* out_norm;
   const float2* rope;    // [max_ctx][hd/2] (cos, sin) from host libm
   float* x;              // residual stream [d]
@@ -698,6 +699,7 @@ struct LmArgs {
   float eps;
   float* logits;       // [N] or nullptr
   int N, K, rows_per_cta, stages;
+  int flush;           // 1: flush |t| < 1e-6 to 0 before the bias (a Q8_0 lm_head)
   unsigned long long* part;
   unsigned* cnt;
   unsigned* result;
@@ -808,6 +810,7 @@ __global__ void __launch_bounds__(kLmThreads) k_lmhead(LmArgs A) {
           a1 = fmaf(u.w, xv.w, a1);
         }
         float a = warp_sum(a0 + a1);
+        if (A.flush) a = flush_small(a);
         if (A.bias) a += A.bias[row];
         if (lane == 0 && A.logits) A.logits[row] = a;
         const unsigned long long key = amax_key(a, (unsigned)row);

@@ -1000,6 +1000,7 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
           }
           const int row = rbeg + k;
           float sacc = warp_sum(a0 + a1) * scale;
+          if (P.lm_flush) sacc = flush_small(sacc);
           if (P.lm_bias) sacc += __ldg(P.lm_bias + row);
           if (lane == 0) P.logits[row] = sacc;
           const unsigned long long key = amax_key(sacc, (unsigned)row);
