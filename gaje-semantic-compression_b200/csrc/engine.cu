@@ -830,17 +830,21 @@ bool plan_fused(gaje_model* m) {
   p.nKV = 2 * m->nkv;
   p.cap = (cached + p.S - 1) / p.S + 1;
   p.pv_groups = std::max(1, kFuConsumers / hd);
-  p.kb_max = 0;
+  p.ob_max = 0;
+  p.cb_max = 1;
   for (int c = 0; c < G; ++c) {
-    int kb0 = 0, n = 0;
-    fu_kbs(m->ff / 32, G, c, kb0, n);
-    p.kb_max = std::max(p.kb_max, n);
+    int u0 = 0, n = 0;
+    fu_outs(m->ff, G, c, u0, n);
+    p.ob_max = std::max(p.ob_max, n);
+    if (n > 0) p.cb_max = std::max(p.cb_max, (u0 + n - 1) / 32 - u0 / 32 + 1);
   }
+  if (2 * p.ob_max > kFuConsumers || p.cb_max > kFuConsumerWarps) return false;
   p.lm_rows_per_cta = (m->V + G - 1) / G;
   const size_t nbq = size_t(m->qkv[0].nb), nbpq = size_t(m->qkv[0].nbp);
   const size_t nbg = size_t(m->gate_up[0].nb), nbpg = size_t(m->gate_up[0].nbp);
   const size_t need = std::max({size_t(hd) * (nbq * 16 + nbpq * 4), size_t(hd / 32) * d * 20,
-                                size_t(64) * (nbg * 16 + nbpg * 4), size_t(d) * 20, size_t(d) * 4});
+                                size_t(2 * p.ob_max) * (nbg * 16 + nbpg * 4), size_t(p.cb_max) * d * 20,
+                                size_t(d) * 4});
   p.slot_bytes = unsigned((need + 127) / 128 * 128);
   p.nslots = 0;
   const size_t budget = size_t(kMaxDynSmem) - fa.sharedSizeBytes - 1024;

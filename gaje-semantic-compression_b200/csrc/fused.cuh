@@ -76,7 +76,8 @@ struct FusedPlan {
   int nslots;
   unsigned slot_bytes;
   int lm_rows_per_cta, lm_stage_rows;
-  int kb_max;     // ffn K-blocks of the busiest CTA
+  int ob_max;     // SwiGLU outputs of the busiest CTA
+  int cb_max;     // ffn_down column blocks one CTA's outputs touch, at most
   int pv_groups;  // position groups of the P*V partial sums
 };
 
@@ -127,12 +128,16 @@ constexpr int kFuTrace = 16;
 __host__ __device__ inline unsigned fu_epoch(unsigned e0, int L, int step, int l, int ph) {
   return e0 + unsigned(step) * unsigned(2 * L + 1) + unsigned(2 * l + ph) + 1u;
 }
-// ffn K-blocks of CTA c: count and first.  The remainder goes to the last CTAs
-// (those without attention work).
-__host__ __device__ inline void fu_kbs(int nkb, int grid, int c, int& kb0, int& n) {
-  const int base = nkb / grid, extra = nkb % grid, first_extra = grid - extra;
+// The FFN half of a block: CTA c computes the SwiGLU outputs [u0, u0 + n)
+// (its 2n gate/up rows, contiguous in the pair-interleaved layout) and their
+// share of ffn_down (the 1-3 column blocks the range touches, the outputs of
+// other CTAs staged as zeros).  The counts differ by at most one across the
+// CTAs, the larger ones on the last CTAs (those without attention work): one
+// GEMV and one column pass per CTA, whatever ff / grid is.
+__host__ __device__ inline void fu_outs(int ff, int grid, int c, int& u0, int& n) {
+  const int base = ff / grid, extra = ff % grid, first_extra = grid - extra;
   n = base + (c >= first_extra ? 1 : 0);
-  kb0 = c * base + (c > first_extra ? c - first_extra : 0);
+  u0 = c * base + (c > first_extra ? c - first_extra : 0);
 }
 // Cached positions of split s when `cached` positions precede this one.
 __host__ __device__ inline void fu_split(int cached, int S, int s, int& t0, int& n_old) {
@@ -141,6 +146,11 @@ __host__ __device__ inline void fu_split(int cached, int S, int s, int& t0, int&
   n_old = max(0, min(chunk, cached - t0));
 }
 
+// Raw row dots of one row GEMV: the q / k / v rows of a head, or a CTA's gate/up rows.
+__host__ __device__ inline size_t fu_raw_floats(const FusedPlan& p, int hd) {
+  const int r = 2 * p.ob_max > hd ? 2 * p.ob_max : hd;
+  return size_t(mk_round32(r));
+}
 __host__ __device__ inline size_t fu_pv_floats(const FusedPlan& p, int hd) {
   const size_t a = size_t(p.pv_groups) * hd;
   return a > size_t(kFuConsumers) ? a : size_t(kFuConsumers);
@@ -164,11 +174,11 @@ struct FuShared {
   float* kvbuf;  // [cap][hd] K, then [cap][hd] V
   float* pv;     // [pv_groups][hd]
   float* ost;    // [hd] staged O_s, [hd/32] sums after it
-  float* ast;    // [32] staged SwiGLU outputs of one K-block, [1] sum after it
+  float* ast;    // [cb_max*32] staged SwiGLU outputs of the CTA's column blocks, [cb_max] sums after them
   float* nw;     // [d] the norm weights of the next staging (prefetched)
   float* rb;     // [hd] RoPE (cos, sin) of the position, [hd] this CTA's q/k/v bias rows
-  float* gub;    // [kb_max*64] gate/up bias rows of this CTA's K-blocks
-  float* raw;    // [max(hd, 64)] raw row dots of a row GEMV
+  float* gub;    // [ob_max*2] gate/up bias rows of this CTA's outputs
+  float* raw;    // [max(hd, 2*ob_max)] raw row dots of a row GEMV
   float* ycol;   // [d] column-GEMV accumulators (rows 4t..4t+3 owned by thread t)
   float* misc;   // 64 floats: reductions, coefficients
   unsigned char* slots;
@@ -319,21 +329,21 @@ __device__ __forceinline__ bool fu_block_item(const FusedArgs& A, const LayerW& 
       --k;
     }
   }
-  int kb0, nkb;
-  fu_kbs(P.ff / 32, gridDim.x, c, kb0, nkb);
-  if (k >= 2 * nkb) return false;
-  const int kb = kb0 + k / 2;
-  if ((k & 1) == 0) {  // gate/up rows of the 32 SwiGLU outputs of kb
+  int u0, n;
+  fu_outs(P.ff, gridDim.x, c, u0, n);
+  if (n == 0 || k >= 2) return false;
+  if (k == 0) {  // gate/up rows of the CTA's SwiGLU outputs
     const Q4View& G = Lw.gate_up;
-    it.a = G.qs + (size_t)kb * 64 * G.nb;
-    it.na = 64u * G.nb * 16;
-    it.b = G.sm + (size_t)kb * 64 * G.nbp;
-    it.nb = 64u * G.nbp * 4;
-  } else {  // ffn_down column block kb
-    it.a = F.dn_qs + (size_t)kb * d;
-    it.na = uint32_t(d) * 16;
-    it.b = F.dn_sm + (size_t)kb * d;
-    it.nb = uint32_t(d) * 4;
+    it.a = G.qs + (size_t)(2 * u0) * G.nb;
+    it.na = uint32_t(2 * n) * G.nb * 16;
+    it.b = G.sm + (size_t)(2 * u0) * G.nbp;
+    it.nb = uint32_t(2 * n) * G.nbp * 4;
+  } else {  // the ffn_down column blocks the outputs touch
+    const int kb0 = u0 / 32, nblk = (u0 + n - 1) / 32 - kb0 + 1;
+    it.a = F.dn_qs + (size_t)kb0 * d;
+    it.na = uint32_t(nblk) * d * 16;
+    it.b = F.dn_sm + (size_t)kb0 * d;
+    it.nb = uint32_t(nblk) * d * 4;
   }
   return true;
 }
@@ -800,8 +810,9 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
   const int kvj = roleKV ? c - pl.nA : 0, kvk = kvj / P.nkv, kvg = kvj - kvk * P.nkv;
   // this CTA's first q/k/v row (pair-interleaved storage)
   const int qrow0 = roleA ? h * hd : (P.nh + kvk * P.nkv + kvg) * hd;
-  int kb0, nkb;
-  fu_kbs(P.ff / 32, G, c, kb0, nkb);
+  int fo0, nfo;  // this CTA's SwiGLU outputs [fo0, fo0 + nfo)
+  fu_outs(P.ff, G, c, fo0, nfo);
+  const int fkb0 = fo0 / 32, fnblk = nfo > 0 ? (fo0 + nfo - 1) / 32 - fkb0 + 1 : 0;
   uint2* flA = A.flags;
   uint2* flB = A.flags + G;
   int item = 0;
@@ -921,7 +932,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
       }
       // ============================================================ phase B
       fu_prefetch(S.nw, Lw.ffn_norm, d);
-      if (nkb > 0) fu_prefetch(S.gub, Lw.gate_up.bias ? Lw.gate_up.bias + (size_t)kb0 * 64 : nullptr, nkb * 64);
+      if (nfo > 0) fu_prefetch(S.gub, Lw.gate_up.bias ? Lw.gate_up.bias + (size_t)fo0 * 2 : nullptr, nfo * 2);
       if (!fu_gate(flA, pl.nA, eA, S.cabort, st)) return;
       fmark(step, l, 9);
       if (!(roleA || roleKV)) {  // R of this block from the sums of the previous one
@@ -944,35 +955,35 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
       fu_sync();
       if (*S.cabort) return;
       fmark(step, l, 10);
-      if (nkb > 0) {
+      if (nfo > 0) {
         const float inv = fu_stage_norm(S.XA, S.nw, d, P.eps, S.xs, S.xsum, S.misc, false, st, pos, l);
         fmark(step, l, 11);
         const Q4View& Gu = Lw.gate_up;
-#pragma unroll 1
-        for (int k = 0; k < nkb; ++k) {
-          const unsigned char* gslot = fu_wait_slot(A, S, item);
-          fu_sync();
-          if (*S.cabort) return;
-          fu_rows_raw(gslot, 64, Gu.nb, Gu.nbp, S.xs, S.xsum, S.pv, S.raw);
-          fu_release(A, S, item++);
-          fu_sync();
-          if (wid == 0) {  // SwiGLU of the K-block's 32 outputs, staged for the down columns
-            const int u = (kb0 + k) * 32 + lane;
-            const float gv = flush_small(S.raw[2 * lane] * inv) + S.gub[k * 64 + 2 * lane];
-            const float uv = flush_small(S.raw[2 * lane + 1] * inv) + S.gub[k * 64 + 2 * lane + 1];
+        const unsigned char* gslot = fu_wait_slot(A, S, item);
+        fu_sync();
+        if (*S.cabort) return;
+        fu_rows_raw(gslot, 2 * nfo, Gu.nb, Gu.nbp, S.xs, S.xsum, S.pv, S.raw);
+        fu_release(A, S, item++);
+        fu_sync();
+        // SwiGLU of the outputs, staged over the column blocks (zeros for other CTAs' outputs)
+        if (wid < fnblk) {
+          const int e = wid * 32 + lane, j = fkb0 * 32 + e - fo0;  // j: this CTA's output index
+          float a = 0.f;
+          if (j >= 0 && j < nfo) {
+            const float gv = flush_small(S.raw[2 * j] * inv) + S.gub[2 * j];
+            const float uv = flush_small(S.raw[2 * j + 1] * inv) + S.gub[2 * j + 1];
             if (uv != uv) nan_flag(st, pos, l, kNanUp);
-            const float a = swiglu_balanced(gv, uv);
+            a = swiglu_balanced(gv, uv);
             if (a != a) nan_flag(st, pos, l, kNanFfnOut);
-            (void)u;
-            mk_stage_elem(S.ast, S.ast + 32, lane, a);
           }
-          if (k == 0) fmark(step, l, 12);
-          const unsigned char* dslot = fu_wait_slot(A, S, item);
-          fu_sync();
-          if (*S.cabort) return;
-          fu_cols(dslot, d, 1, S.ast, S.ast + 32, S.ycol, k == 0);
-          fu_release(A, S, item++);
+          mk_stage_elem(S.ast, S.ast + pl.cb_max * 32, e, a);
         }
+        fmark(step, l, 12);
+        const unsigned char* dslot = fu_wait_slot(A, S, item);
+        fu_sync();
+        if (*S.cabort) return;
+        fu_cols(dslot, d, fnblk, S.ast, S.ast + pl.cb_max * 32, S.ycol, true);
+        fu_release(A, S, item++);
         fmark(step, l, 13);
         for (int p = tid; p < d / 2; p += kFuConsumers) {
           const float2 y = reinterpret_cast<const float2*>(S.ycol)[p];
@@ -1022,15 +1033,15 @@ __global__ void __launch_bounds__(kFuThreads, 1) k_decode_fused(FusedArgs A) {
   S.ost = f;
   f += hd + 32;
   S.ast = f;
-  f += 64;
+  f += mk_round32(pl.cb_max * 33);
   S.nw = f;
   f += d;
   S.rb = f;
   f += 2 * hd;
   S.gub = f;
-  f += pl.kb_max * 64;
+  f += mk_round32(pl.ob_max * 2);
   S.raw = f;
-  f += mk_round32(hd > 64 ? hd : 64);
+  f += fu_raw_floats(pl, hd);
   S.ycol = f;
   f += d;
   S.misc = f;
@@ -1067,8 +1078,8 @@ __global__ void __launch_bounds__(kFuThreads, 1) k_decode_fused(FusedArgs A) {
 // Dynamic shared memory of the fused kernel.
 __host__ __device__ inline size_t fused_smem_bytes(const FusedPlan& p, int d, int hd) {
   const size_t floats = size_t(3) * d + mk_round32(d / 32) + hd + mk_round32(p.cap) + size_t(2) * p.cap * hd +
-                        fu_pv_floats(p, hd) + hd + 32 + 64 + d + 2 * hd + size_t(p.kb_max) * 64 +
-                        mk_round32(hd > 64 ? hd : 64) + d + 64;
+                        fu_pv_floats(p, hd) + hd + 32 + mk_round32(p.cb_max * 33) + d + 2 * hd + mk_round32(p.ob_max * 2) +
+                        fu_raw_floats(p, hd) + d + 64;
   return kFuHeader + floats * 4 + size_t(p.nslots) * p.slot_bytes;
 }
 
