@@ -818,7 +818,7 @@ bool plan_fused(gaje_model* m) {
   cudaFuncAttributes fa{};
   if (cudaFuncGetAttributes(&fa, k_decode_fused) != cudaSuccess) return false;
   const int d = m->d, hd = m->hd, G = m->sms;
-  if (d % 32 || hd % 32 || hd > 128 || m->ff % 32 || d / 4 > kFuConsumers || m->info.use_genomic_norm) return false;
+  if (d % 32 || (hd != 32 && hd != 64 && hd != 128) || m->ff % 32 || m->info.use_genomic_norm) return false;
   if (m->qkv[0].K != d || m->gate_up[0].K != d || m->wo[0].N != d || m->down[0].N != d) return false;
   if (m->wo[0].K != m->nh * hd || m->down[0].K != m->ff) return false;
   FusedPlan& p = m->fplan;

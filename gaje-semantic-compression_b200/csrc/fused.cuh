@@ -554,66 +554,104 @@ __device__ __forceinline__ void fu_prefetch(float* dst, const float* src, int n)
   for (int i = threadIdx.x; i < n; i += kFuConsumers) dst[i] = src ? __ldg(src + i) : 0.f;
 }
 
-// The attention of split sp of head h at position pos (q in S.qbuf): the
-// cached rows landed by TMA, this position's k/v row (LL words) for the last
-// split, scores, softmax, (m, l) published, P*V, O staged for the output
-// projection.  Returns the split's position count, or -1 on an abort.
-__device__ __forceinline__ int fu_attend(const FusedArgs& A, const FuShared& S, int l, int step, unsigned pos, int h,
-                                      int sp, unsigned eA) {
+// The attention of split sp of head h at position pos (q in S.qbuf), by one
+// warp (the caller's warp 0; no CTA barrier inside): the cached rows landed by
+// TMA, this position's k/v row (LL words) for the last split, scores,
+// softmax, (m, l) published, P*V, O staged for the output projection.  Lane
+// l owns dims l, l+32, ... of q, k and v.  Scores go 32 positions at a time:
+// each lane forms its partial dot for every position of the group and one
+// butterfly reduce-scatter leaves position i's dot in lane i.  Returns the
+// split's position count, or -1 when a wait ran out (the CTA's abort raised).
+template <int VEC>
+__device__ __forceinline__ int fu_attend_warp(const FusedArgs& A, const FuShared& S, int l, int step, unsigned pos,
+                                              int h, int sp, unsigned eA) {
   const StepParams& P = A.P;
   const FusedPlan& pl = A.plan;
   DevState* st = P.st;
-  const int tid = threadIdx.x, hd = P.hd, L = P.n_layers;
+  constexpr int HD = 32 * VEC;
+  const int lane = threadIdx.x & 31, L = P.n_layers;
   int t0, n_old;
   fu_split(int(pos), pl.S, sp, t0, n_old);
   const bool last = sp == pl.S - 1;
   const int n = n_old + (last ? 1 : 0);
   float* Ks = S.kvbuf;
-  float* Vs = S.kvbuf + (size_t)pl.cap * hd;
+  float* Vs = S.kvbuf + (size_t)pl.cap * HD;
   const int g = h / (P.nh / P.nkv);
   bool ok = true;
-  if (last)
-    ok = fu_ll_read(A.kvnew + (size_t)g * hd, hd, eA, Ks + (size_t)n_old * hd) &&
-         fu_ll_read(A.kvnew + (size_t)(P.nkv + g) * hd, hd, eA, Vs + (size_t)n_old * hd);
-  const int use = *S.kv_waited;
-  if (ok && !*S.cabort && !mbar_wait(S.kv_bar, use & 1)) ok = false;
-  if (!ok) {
-    flag_timeout(st, 24);
-    *S.cabort = 1;
-  }
-  fu_sync();
-  if (*S.cabort) return -1;
-  if (tid == 0) *S.kv_waited = use + 1;
-  const int H4 = hd >> 2;
-  float m = -INFINITY;
-#pragma unroll 1
-  for (int t = tid; t < n; t += kFuConsumers) {
-    const float4* kr = reinterpret_cast<const float4*>(Ks + (size_t)t * hd);
-    const float4* qr = reinterpret_cast<const float4*>(S.qbuf);
-    float a0 = 0.f, a1 = 0.f;
-    int cc = t % H4;  // rotated start: conflict-free rows
-#pragma unroll 4
-    for (int k = 0; k < H4; ++k) {
-      const float4 kk = kr[cc], qq = qr[cc];
-      a0 = fmaf(qq.x, kk.x, a0);
-      a1 = fmaf(qq.y, kk.y, a1);
-      a0 = fmaf(qq.z, kk.z, a0);
-      a1 = fmaf(qq.w, kk.w, a1);
-      cc = cc + 1 == H4 ? 0 : cc + 1;
+  if (last) {  // this position's k and v rows: LL words of the KV CTAs
+    const uint2* src = A.kvnew + (size_t)g * HD;
+    const uint2* srcv = A.kvnew + (size_t)(P.nkv + g) * HD;
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) {
+      const int e = lane + 32 * v;
+      uint2 wk = ld_ll(src + e), wv = ld_ll(srcv + e);
+      unsigned long long tw = 0;
+      while (wk.y != eA || wv.y != eA) {
+        const unsigned long long t = global_ns();
+        if (!tw) tw = t;
+        else if (t - tw > kWaitNs) {
+          ok = false;
+          break;
+        }
+        wk = ld_ll(src + e);
+        wv = ld_ll(srcv + e);
+      }
+      Ks[(size_t)n_old * HD + e] = __uint_as_float(wk.x);
+      Vs[(size_t)n_old * HD + e] = __uint_as_float(wv.x);
     }
-    const float sc = (a0 + a1) * P.attn_scale;
-    S.ps[t] = sc;
-    m = fmaxf(m, sc);
   }
-  m = fu_total(m, S.misc, true);
+  const int use = *S.kv_waited;
+  if (ok && !mbar_wait(S.kv_bar, use & 1)) ok = false;
+  if (!__all_sync(0xffffffffu, ok)) {
+    if (lane == 0) {
+      flag_timeout(st, 24);
+      *S.cabort = 1;
+    }
+    return -1;
+  }
+  __syncwarp();
+  if (lane == 0) *S.kv_waited = use + 1;
+  float q[VEC];
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) q[v] = S.qbuf[lane + 32 * v];
+  float m = -INFINITY;
+  for (int g0 = 0; g0 < n; g0 += 32) {
+    float part[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const int t = min(g0 + i, n - 1);  // past the end: a repeat, discarded
+      float a = 0.f;
+#pragma unroll
+      for (int v = 0; v < VEC; ++v) a = fmaf(q[v], Ks[(size_t)t * HD + lane + 32 * v], a);
+      part[i] = a;
+    }
+#pragma unroll
+    for (int o = 16, hh = 16; o >= 1; o >>= 1, hh >>= 1) {
+      const bool up = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < hh; ++i) {
+        const float send = up ? part[i] : part[i + hh];
+        const float keep = up ? part[i + hh] : part[i];
+        part[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+      }
+    }
+    if (g0 + lane < n) {
+      const float sc = part[0] * P.attn_scale;
+      S.ps[g0 + lane] = sc;
+      m = fmaxf(m, sc);
+    }
+  }
+  m = warp_max(m);
+  __syncwarp();
   float lsum = 0.f;
-  for (int t = tid; t < n; t += kFuConsumers) {
-    const float ev = expf(S.ps[t] - m);
-    S.ps[t] = ev;
-    lsum += ev;
+  for (int t = lane; t < n; t += 32) {
+    const float e = expf(S.ps[t] - m);
+    S.ps[t] = e;
+    lsum += e;
   }
-  lsum = fu_total(lsum, S.misc + 16, false);  // also publishes ps
-  if (tid == 0) {
+  lsum = warp_sum(lsum);
+  __syncwarp();
+  if (lane == 0) {
     S.misc[40] = m;
     if (n > 0) {  // (m, l) of this split
       uint2* ml = A.mlx + ((size_t)h * pl.S + sp) * 2;
@@ -621,27 +659,22 @@ __device__ __forceinline__ int fu_attend(const FusedArgs& A, const FuShared& S, 
       st_ll(ml + 1, lsum, eA);
     }
   }
-  // P*V: position groups j of e-columns, summed in group order
-  const int J = pl.pv_groups;
-  if (tid < J * hd) {
-    const int e = tid % hd, j = tid / hd;
-    float o = 0.f;
+  float acc[VEC];
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) acc[v] = 0.f;
 #pragma unroll 4
-    for (int t = j; t < n; t += J) o = fmaf(S.ps[t], Vs[(size_t)t * hd + e], o);
-    S.pv[j * hd + e] = o;
+  for (int t = 0; t < n; ++t) {
+    const float p = S.ps[t];
+#pragma unroll
+    for (int v = 0; v < VEC; ++v) acc[v] = fmaf(p, Vs[(size_t)t * HD + lane + 32 * v], acc[v]);
   }
-  fu_sync();
-  if (tid == 0) {  // K/V buffer free: the next block's (or next step's) rows
+  __syncwarp();
+  if (lane == 0) {  // K/V buffer free: the next block's (or next step's) rows
     if (l + 1 < L) fu_kv_prefetch(A, S, l + 1, int(pos));
     else if (step + 1 < A.n_steps && L > 1) fu_kv_prefetch(A, S, 0, int(pos) + 1);
   }
-  if (tid < hd) {
-    float o = 0.f;
-    for (int j = 0; j < J; ++j) o += S.pv[j * hd + tid];
-    S.pv[tid] = o;  // group 0 is read only by this thread
-  }
-  fu_sync();
-  for (int i = tid; i < hd; i += kFuConsumers) mk_stage_elem(S.ost, S.ost + hd, i, S.pv[i]);
+#pragma unroll
+  for (int v = 0; v < VEC; ++v) mk_stage_elem(S.ost, S.ost + HD, lane + 32 * v, acc[v]);
   return n;
 }
 
@@ -906,8 +939,16 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
         fu_sync();
         fmark(step, l, 3);
         if (roleA) {
-          const int n = fu_attend(A, S, l, step, pos, h, sp, eA);
-          if (n < 0) return;
+          if (wid == 0) {
+            int na = -1;
+            if (hd == 32) na = fu_attend_warp<1>(A, S, l, step, pos, h, sp, eA);
+            else if (hd == 64) na = fu_attend_warp<2>(A, S, l, step, pos, h, sp, eA);
+            else na = fu_attend_warp<4>(A, S, l, step, pos, h, sp, eA);
+            if (lane == 0) reinterpret_cast<int*>(S.misc)[41] = na;
+          }
+          fu_sync();
+          const int n = reinterpret_cast<const int*>(S.misc)[41];
+          if (n < 0 || *S.cabort) return;
           fmark(step, l, 5);
           const unsigned char* wslot = fu_wait_slot(A, S, item);
           fu_sync();
