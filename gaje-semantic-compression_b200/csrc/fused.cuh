@@ -953,10 +953,14 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
           const unsigned char* wslot = fu_wait_slot(A, S, item);
           fu_sync();
           if (*S.cabort) return;
-          if (n > 0) fu_cols(wslot, d, hd / 32, S.ost, S.ost + hd, S.ycol, true);
+          // the head's split weight: by the last warp while the others run the
+          // output projection when it has no rows of it (d/2 <= 448), else after
+          const bool sw_overlap = d / 2 <= (kFuConsumerWarps - 1) * 32;
+          if (sw_overlap && wid == kFuConsumerWarps - 1) fu_split_weight(A, S, pos, h, n, eA);
+          else if (n > 0) fu_cols(wslot, d, hd / 32, S.ost, S.ost + hd, S.ycol, true);
           fu_release(A, S, item++);
           fmark(step, l, 6);
-          if (wid == 0) fu_split_weight(A, S, pos, h, n, eA);
+          if (!sw_overlap && wid == 0) fu_split_weight(A, S, pos, h, n, eA);
           fmark(step, l, 15);
           fu_sync();
           if (*S.cabort) return;
