@@ -865,7 +865,7 @@ int batch_lm_mb(int B) { return B <= 8 ? 8 : 16; }
 
 // The work split of one tensor-core GEMM: vectors per CTA (the MMA's N), the
 // padded vector count, and K split across CTAs when the row x vector tiles
-// alone would leave SMs idle (every CTA keeps at least two 64-K stages).
+// alone would leave SMs idle (every CTA keeps at least four 32-K stages).
 struct TcPlan {
   int nt = 0, mpad = 0, z = 1;
   dim3 grid;
@@ -877,7 +877,7 @@ TcPlan tc_plan(int N, int K, int M, int sms) {
   p.mpad = (M + p.nt - 1) / p.nt * p.nt;
   const int gx = (N + kTcRows - 1) / kTcRows, gy = p.mpad / p.nt, nkt = K / kTcK;
   const int want = sms / std::max(1, gx * gy);
-  p.z = std::max(1, std::min(want, nkt / 2));
+  p.z = std::max(1, std::min(want, nkt / 4));
   p.grid = dim3(unsigned(gx), unsigned(gy), unsigned(p.z));
   p.part_floats = p.z > 1 ? size_t(p.z) * M * N : 0;
   p.tiles = size_t(gx) * gy;

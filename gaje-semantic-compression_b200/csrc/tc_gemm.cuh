@@ -13,22 +13,28 @@
 //
 // Activations are split once per GEMM by k_tc_split (optionally fused with
 // the RMSNorm that precedes the projection) into a tiled bf16 layout whose
-// (64-K stage, 8-row group) blocks are the MMA's canonical K-major
+// (32-K stage, 8-row group) blocks are the MMA's canonical K-major
 // no-swizzle core-matrix layout: 8 rows x 16 bytes per core matrix, the
-// eight 8-element K chunks of a row group 128 B apart (LBO), row groups
-// 1 KB apart (SBO).  A CTA's activation tile for one stage is then one
+// four 8-element K chunks of a row group 128 B apart (LBO), row groups
+// 512 B apart (SBO).  A CTA's activation tile for one stage is then one
 // contiguous run per plane, fetched by a 1-D TMA bulk copy.
 //
-// CTA: 128 weight rows (the MMA's M) x NT vectors (its N), S stages of 64 K.
-// Warps 0-7 dequantise one Q4 block each per row and stage (two threads per
-// row; the next stage's words fetched one stage ahead) into the A tiles and
-// arrive on a_full; warp 8 lane 0 issues the activation copies (b_full,
-// transaction bytes) and, once both halves of a stage are in, 4 k-steps x 3
-// MMAs, committed to the stage's `done` barrier, which gates the stage's
-// reuse.  The f32 accumulator is NT columns of tensor memory; warp w reads
-// lane quarter w%4, column half w/4, with tcgen05.ld for the epilogue.  With
-// gridDim.z > 1 the K stages are split across CTAs: partial tiles go to
-// sp.part and k_tc_reduce adds them in split order and runs the epilogue.
+// CTA: 128 weight rows (the MMA's M) x NT vectors (its N), S stages of 32 K
+// (one Q4 block per row; S = 4 at NT = 256, up to 8 for narrower tiles).
+// Warp roles, each waiting only on the barriers it consumes:
+// - warps 0-7 make the A tiles (for Q4: warps 0-3 stream the raw words
+//   through a shared-memory ring, warps 4-7 dequantise them) and arrive on
+//   a_full;
+// - warp 8 lane 0 issues a stage's 2 k-steps x 3 MMAs once a_full and b_full
+//   are complete and commits them to the stage's `done` barrier;
+// - warp 9 lane 0 issues the activation copies of a stage (b_full, transaction
+//   bytes) once `done` says the stage's previous MMAs are through.
+// The MMA lane never waits on an MMA completion, so the tensor pipe's queue
+// stays full while the copies and the dequantisation run ahead.  The f32
+// accumulator is NT columns of tensor memory; warp w < 8 reads lane quarter
+// w%4, column half w/4, with tcgen05.ld for the epilogue.  With gridDim.z > 1
+// the K stages are split across CTAs: partial tiles go to sp.part and
+// k_tc_reduce adds them in split order and runs the epilogue.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -38,19 +44,28 @@
 namespace gaje {
 
 constexpr int kTcProducers = 256;                 // warps 0-7: two threads per weight row
-constexpr int kTcThreads = kTcProducers + 32;     // + the issue warp
+constexpr int kTcMmaWarp = kTcProducers / 32;     // lane 0 issues the MMAs
+constexpr int kTcCopyWarp = kTcMmaWarp + 1;       // lane 0 issues the activation copies
+constexpr int kTcThreads = kTcProducers + 64;
 constexpr int kTcRows = 128;                      // weight rows per CTA (MMA M)
-constexpr int kTcK = 64;                          // K per stage
+constexpr int kTcK = 32;                          // K per stage: one Q4 block of every row
+constexpr int kTcChunks = kTcK / 8;               // 16-byte K chunks of a row per stage
 constexpr unsigned kTcKidTimeout = 15;
 
 __host__ __device__ constexpr size_t tc_stage_bytes(int nt) {
   return size_t(2) * kTcRows * kTcK * 2 + size_t(2) * nt * kTcK * 2;  // A hi/lo + B hi/lo (bf16)
 }
+// As many stages as fit 200 KB, at most 8: at 256 vectors a stage is 48 KB
+// (four in flight), at 16 vectors 18 KB.
 __host__ __device__ constexpr int tc_stages(int nt) {
-  return int((200 * 1024) / tc_stage_bytes(nt)) > 4 ? 4 : int((200 * 1024) / tc_stage_bytes(nt));
+  return int((200 * 1024) / tc_stage_bytes(nt)) > 8 ? 8 : int((200 * 1024) / tc_stage_bytes(nt));
 }
-__host__ __device__ constexpr size_t tc_smem_bytes(int nt) {
-  return 1024 + size_t(tc_stages(nt)) * tc_stage_bytes(nt);  // 1 KB header (barriers, TMEM address)
+// Raw Q4 words of one stage (128 rows x 16 B nibbles + 128 x 4 B scale/min),
+// kTcRawStages of them in flight ahead of the dequantising warps.
+constexpr int kTcRawStages = 8;
+constexpr int kTcRawSlot = kTcRows * 20;
+__host__ __device__ constexpr size_t tc_smem_bytes(int nt) {  // 1 KB header (barriers, TMEM address)
+  return 1024 + size_t(tc_stages(nt)) * tc_stage_bytes(nt) + size_t(kTcRawStages) * kTcRawSlot;
 }
 __host__ __device__ constexpr int tc_tmem_cols(int nt) { return nt < 32 ? 32 : nt; }
 // Bytes of one bf16 plane of split activations for Mpad rows x K.
@@ -110,20 +125,30 @@ __device__ __forceinline__ void tc_split8(const float (&v)[8], uint4& hi, uint4&
 }
 
 // Byte offset of (row r, 8-element K chunk c) in a K-major no-swizzle stage
-// tile with 64 K per row: core matrix (r/8, c) at (r/8)*1024 + c*128, row
-// r%8 at +16.
-__device__ __forceinline__ uint32_t tc_off(int r, int c) { return uint32_t((r >> 3) * 1024 + c * 128 + (r & 7) * 16); }
+// tile with 32 K per row: core matrix (r/8, c) at (r/8)*512 + c*128 (LBO 128
+// between K chunks, SBO 512 between row groups), row r%8 at +16.
+constexpr uint32_t kTcLbo = 128, kTcSbo = kTcChunks * 128;
+__device__ __forceinline__ uint32_t tc_off(int r, int c) {
+  return uint32_t((r >> 3) * kTcSbo + c * kTcLbo + (r & 7) * 16);
+}
 // Byte offset of (row r, K chunk c) in the split-activation planes of mpad rows:
-// stage c/8, row group r/8, chunk c%8, row r%8.
+// stage c/4, row group r/8, chunk c%4, row r%8 -- a CTA's activation tile of
+// one stage is one contiguous run.
 __host__ __device__ __forceinline__ size_t tc_xoff(int r, int c, int mpad) {
-  return ((size_t(c >> 3) * (mpad >> 3) + (r >> 3)) * 8 + (c & 7)) * 128 + (r & 7) * 16;
+  return ((size_t(c / kTcChunks) * (mpad >> 3) + (r >> 3)) * kTcChunks + (c % kTcChunks)) * 128 + (r & 7) * 16;
 }
 
-// Weight sources of the A operand: a thread owns 32 consecutive elements
-// (one Q4 block) of one row per stage; `load` fetches their raw words into
-// registers, `values` gives the 8 floats of chunk w (0..3) from them.
+// Weight sources of the A operand.  Q4Rows (kRawRing): four loader warps
+// copy each stage's raw words (one Q4 block of each of the 128 rows) into a
+// shared-memory ring kTcRawStages deep with cp.async, tracked by an
+// mbarrier; four converter warps, a row per thread, dequantise a whole block
+// per stage into the A tiles.  The converters issue no global loads, so the
+// proxy fence that publishes their tile writes to the tensor cores waits on
+// nothing else.  F32Rows: a thread owns 16 consecutive elements (half h of a
+// 32-element block) of one row per stage, kDepth stages ahead in registers.
 struct Q4Rows {  // Q4_0: w = fma(q, scale, min) (genomic.rs:267-336)
   Q4View W;
+  static constexpr bool kRawRing = true;  // words staged through shared memory by loader warps
   struct Regs {
     uint4 q;
     uint32_t s;
@@ -131,13 +156,14 @@ struct Q4Rows {  // Q4_0: w = fma(q, scale, min) (genomic.rs:267-336)
   __host__ __device__ __forceinline__ int N() const { return W.N; }
   __host__ __device__ __forceinline__ int K() const { return W.K; }
   __host__ __device__ __forceinline__ const float* bias() const { return W.bias; }
-  __device__ __forceinline__ void load(Regs& g, int r, int blk) const {
-    g.q = __ldg(W.qs + (size_t)r * W.nb + blk);
-    g.s = __ldg(W.sm + (size_t)r * W.nbp + blk);
+  // row r's block blk into raw slot row rl (asynchronous copies of the issuing thread)
+  __device__ __forceinline__ void copy_raw(unsigned char* slot, int rl, int r, int blk) const {
+    cp_async16(slot + rl * 16, W.qs + (size_t)r * W.nb + blk);
+    cp_async4(slot + kTcRows * 16 + rl * 4, W.sm + (size_t)r * W.nbp + blk);
   }
-  __device__ __forceinline__ void zero(Regs& g) const {
-    g.q = make_uint4(0u, 0u, 0u, 0u);
-    g.s = 0u;
+  __device__ __forceinline__ void read_raw(Regs& g, const unsigned char* slot, int rl) const {
+    g.q = *reinterpret_cast<const uint4*>(slot + rl * 16);
+    g.s = *reinterpret_cast<const uint32_t*>(slot + kTcRows * 16 + rl * 4);
   }
   __device__ __forceinline__ void values(const Regs& g, int w, float (&v)[8]) const {
     float sc, mn;
@@ -152,20 +178,22 @@ struct F32Rows {  // plain f32 rows [N][K] (the lm_head, linear/forward.rs:20-32
   const float* W;
   const float* b;
   int n, k;
+  static constexpr bool kRawRing = false;
+  static constexpr int kDepth = 4;  // stages of rows in flight per thread (a register ring)
   struct Regs {
-    float4 f[8];
+    float4 f[4];
   };
   __host__ __device__ __forceinline__ int N() const { return n; }
   __host__ __device__ __forceinline__ int K() const { return k; }
   __host__ __device__ __forceinline__ const float* bias() const { return b; }
-  __device__ __forceinline__ void load(Regs& g, int r, int blk) const {
-    const float4* p = reinterpret_cast<const float4*>(W + (size_t)r * k + blk * 32);
+  __device__ __forceinline__ void load(Regs& g, int r, int blk, int h) const {
+    const float4* p = reinterpret_cast<const float4*>(W + (size_t)r * k + blk * 32 + h * 16);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) g.f[i] = __ldcs(p + i);
+    for (int i = 0; i < 4; ++i) g.f[i] = __ldcs(p + i);
   }
   __device__ __forceinline__ void zero(Regs& g) const {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) g.f[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = 0; i < 4; ++i) g.f[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
   __device__ __forceinline__ void values(const Regs& g, int w, float (&v)[8]) const {
     const float4 a = g.f[2 * w], c = g.f[2 * w + 1];
@@ -253,7 +281,7 @@ struct TcSplit {
 // Launch: grid (ceil(N/128), mpad/NT, Z), kTcThreads, tc_smem_bytes(NT);
 // K % 64 == 0; the K stages are divided evenly over Z (Z > 1 needs sp).
 template <int NT, class WS, class Epi>
-__global__ void __launch_bounds__(kTcThreads) k_q4_gemm_tc(WS W, const unsigned char* xhi,
+__global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(WS W, const unsigned char* xhi,
                                                            const unsigned char* xlo, int M, int mpad, TcSplit sp,
                                                            Epi epi, DevState* st) {
   static_assert(NT % 16 == 0 && NT >= 16 && NT <= 256, "MMA N");
@@ -262,6 +290,8 @@ __global__ void __launch_bounds__(kTcThreads) k_q4_gemm_tc(WS W, const unsigned 
   uint64_t* a_full = reinterpret_cast<uint64_t*>(tc_smem);  // [S] 128 producer arrivals
   uint64_t* b_full = a_full + S;                             // [S] activation copies landed
   uint64_t* done = b_full + S;                               // [S] MMAs of the stage complete
+  uint64_t* raw_full = done + S;                             // [kTcRawStages] raw words landed
+  uint64_t* raw_empty = raw_full + kTcRawStages;             // [kTcRawStages] raw words read
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tc_smem + 512);
   unsigned char* stage0 = tc_smem + 1024;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -279,9 +309,13 @@ __global__ void __launch_bounds__(kTcThreads) k_q4_gemm_tc(WS W, const unsigned 
   }
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(a_full + s, kTcProducers);
+      mbar_init(a_full + s, WS::kRawRing ? kTcRows : kTcProducers);
       mbar_init(b_full + s, 1);
       mbar_init(done + s, 1);
+    }
+    for (int s = 0; s < kTcRawStages; ++s) {
+      mbar_init(raw_full + s, kTcRows);   // one (asynchronous) arrival per loader thread
+      mbar_init(raw_empty + s, kTcRows);  // one per converter thread
     }
     fence_mbar_init();
   }
@@ -292,82 +326,141 @@ __global__ void __launch_bounds__(kTcThreads) k_q4_gemm_tc(WS W, const unsigned 
   bool ok = true;
   int issued = 0, committed = -1;  // the issue lane's copies and last commit (for the drain)
   if (wid < kTcProducers / 32) {
-    // ---------------- A producers: thread t = weight row row0 + t/2, block half t&1 of each stage
-    const int rl = tid >> 1, h = tid & 1;
-    const int r = row0 + rl;
-    const bool rok = r < W.N();
-    typename WS::Regs g;
-    W.zero(g);
-    if (rok && n > 0) W.load(g, r, 2 * kb + h);  // weights never depend on the previous kernel
-    pdl_wait();
-    pdl_trigger();
-    for (int i = 0; i < n; ++i) {
-      const int s = i % S;
-      unsigned char* A_hi = stage0 + s * tc_stage_bytes(NT);
-      unsigned char* A_lo = A_hi + kA;
-      if (i >= S && ok) ok = mbar_wait(done + s, ((i / S) - 1) & 1);  // the stage's previous MMAs are done
-      const typename WS::Regs gc = g;
-      if (i + 1 < n && rok) W.load(g, r, 2 * (kb + i + 1) + h);  // the next stage's words, one stage ahead
-#pragma unroll
-      for (int w = 0; w < 4; ++w) {  // chunk w of the thread's 32 elements = stage chunk 4h + w
-        float v[8];
-        W.values(gc, w, v);
-        uint4 hi, lo;
-        tc_split8(v, hi, lo);
-        const uint32_t off = tc_off(rl, 4 * h + w);
-        *reinterpret_cast<uint4*>(A_hi + off) = hi;
-        *reinterpret_cast<uint4*>(A_lo + off) = lo;
+    if constexpr (WS::kRawRing) {
+      unsigned char* raw0 = stage0 + S * tc_stage_bytes(NT);
+      if (wid < 4) {
+        // ---------------- loaders: thread = weight row; raw words up to kTcRawStages stages ahead
+        const int rl = tid, r = row0 + rl;
+        const bool rok = r < W.N();
+        for (int j = 0; j < n; ++j) {  // weights never depend on the previous kernel
+          const int slot = j % kTcRawStages;
+          if (j >= kTcRawStages && !(ok = mbar_wait(raw_empty + slot, ((j / kTcRawStages) - 1) & 1))) break;
+          if (rok) {
+            W.copy_raw(raw0 + slot * kTcRawSlot, rl, r, kb + j);
+            cp_async_mbar_arrive(raw_full + slot);
+          } else {
+            mbar_arrive(raw_full + slot);  // rows past N: whatever the slot holds, their outputs are dropped
+          }
+        }
+        cp_async_wait_all();  // none of this thread's copies still lands in shared memory
+        pdl_wait();
+        pdl_trigger();
+      } else {
+        // ---------------- converters: thread = weight row; a whole block per stage into the A tiles
+        const int rl = tid - 128;
+        pdl_wait();
+        pdl_trigger();
+        for (int i = 0; i < n; ++i) {
+          const int s = i % S, slot = i % kTcRawStages;
+          if (i >= S && !(ok = mbar_wait(done + s, ((i / S) - 1) & 1))) break;  // the stage's previous MMAs
+          if (!(ok = mbar_wait(raw_full + slot, (i / kTcRawStages) & 1))) break;
+          typename WS::Regs g;
+          W.read_raw(g, raw0 + slot * kTcRawSlot, rl);
+          mbar_arrive(raw_empty + slot);
+          unsigned char* A_hi = stage0 + s * tc_stage_bytes(NT);
+          unsigned char* A_lo = A_hi + kA;
+          #pragma unroll
+          for (int w = 0; w < kTcChunks; ++w) {
+            float v[8];
+            W.values(g, w, v);
+            uint4 hi, lo;
+            tc_split8(v, hi, lo);
+            const uint32_t off = tc_off(rl, w);
+            *reinterpret_cast<uint4*>(A_hi + off) = hi;
+            *reinterpret_cast<uint4*>(A_lo + off) = lo;
+          }
+          fence_async_smem();  // these generic-proxy writes, visible to the tensor cores
+          mbar_arrive(a_full + s);
+        }
       }
-      fence_async_smem();  // these generic-proxy writes, visible to the tensor cores
-      mbar_arrive(a_full + s);
+    } else {
+      // ---------------- f32 rows: thread t = weight row row0 + t/2, half t&1 of the stage's block
+      const int rl = tid >> 1, h = tid & 1;
+      const int r = row0 + rl;
+      const bool rok = r < W.N();
+      constexpr int P = WS::kDepth;
+      typename WS::Regs g[P];
+      #pragma unroll
+      for (int u = 0; u < P; ++u) {  // weights never depend on the previous kernel
+        W.zero(g[u]);
+        if (rok && u < n) W.load(g[u], r, kb + u, h);
+      }
+      pdl_wait();
+      pdl_trigger();
+      #pragma unroll 1
+      for (int i0 = 0; i0 < n; i0 += P) {
+        #pragma unroll
+        for (int u = 0; u < P; ++u) {  // stage i's words sit in ring entry i % P
+          const int i = i0 + u;
+          if (i < n) {
+            const int s = i % S;
+            unsigned char* A_hi = stage0 + s * tc_stage_bytes(NT);
+            unsigned char* A_lo = A_hi + kA;
+            if (i >= S && ok) ok = mbar_wait(done + s, ((i / S) - 1) & 1);  // the stage's previous MMAs are done
+            const typename WS::Regs gc = g[u];
+            if (i + P < n && rok) W.load(g[u], r, kb + i + P, h);  // P stages ahead
+            #pragma unroll
+            for (int w = 0; w < 2; ++w) {  // chunk w of the thread's 16 elements = stage chunk 2h + w
+              float v[8];
+              W.values(gc, w, v);
+              uint4 hi, lo;
+              tc_split8(v, hi, lo);
+              const uint32_t off = tc_off(rl, 2 * h + w);
+              *reinterpret_cast<uint4*>(A_hi + off) = hi;
+              *reinterpret_cast<uint4*>(A_lo + off) = lo;
+            }
+            fence_async_smem();  // these generic-proxy writes, visible to the tensor cores
+            mbar_arrive(a_full + s);
+          }
+        }
+      }
     }
-  } else {
-    // ---------------- issue warp: activation copies and the MMAs
+  } else if (wid == kTcMmaWarp) {
+    // ---------------- MMA warp: a stage's MMAs as soon as its A and B tiles are in
     pdl_wait();
     pdl_trigger();
     if (lane == 0) {
-      const size_t gstride = tc_plane_bytes(mpad, kTcK);  // bytes of one 64-K stage of a plane
-      auto load = [&](int j) {
-        const int s = j % S;
-        unsigned char* B_hi = stage0 + s * tc_stage_bytes(NT) + 2 * kA;
-        const size_t src = size_t(kb + j) * gstride + size_t(m0 >> 3) * 1024;
-        mbar_expect_tx(b_full + s, 2 * kB);
-        bulk_g2s(B_hi, xhi + src, kB, b_full + s);
-        bulk_g2s(B_hi + kB, xlo + src, kB, b_full + s);
-        issued = j + 1;
-      };
-      for (int j = 0; j < n && j < S; ++j) load(j);
       constexpr uint32_t idesc = tc_idesc(kTcRows, NT);
-      for (int i = 0; i < n && ok; ++i) {
+      for (int i = 0; i < n; ++i) {
         const int s = i % S;
         const uint32_t ph = (i / S) & 1;
-        ok = mbar_wait(b_full + s, ph) && mbar_wait(a_full + s, ph);
-        if (!ok) break;
+        if (!(ok = mbar_wait(b_full + s, ph) && mbar_wait(a_full + s, ph))) break;
         tc_fence_after();
         unsigned char* A_hi = stage0 + s * tc_stage_bytes(NT);
         const uint32_t ah = smem_u32(A_hi), al = ah + kA, bh = al + kA, bl = bh + kB;
 #pragma unroll
         for (int k = 0; k < kTcK / 16; ++k) {  // a 16-wide k-step spans two core matrices: +256 B
-          const uint32_t o = uint32_t(k) * 256u;
-          const uint64_t dah = tc_desc(ah + o, 128, 1024), dal = tc_desc(al + o, 128, 1024);
-          const uint64_t dbh = tc_desc(bh + o, 128, 1024), dbl = tc_desc(bl + o, 128, 1024);
+          const uint32_t o = uint32_t(k) * 2u * kTcLbo;
+          const uint64_t dah = tc_desc(ah + o, kTcLbo, kTcSbo), dal = tc_desc(al + o, kTcLbo, kTcSbo);
+          const uint64_t dbh = tc_desc(bh + o, kTcLbo, kTcSbo), dbl = tc_desc(bl + o, kTcLbo, kTcSbo);
           tc_mma(tmem, dah, dbh, idesc, (i > 0 || k > 0) ? 1u : 0u);
           tc_mma(tmem, dah, dbl, idesc, 1u);
           tc_mma(tmem, dal, dbh, idesc, 1u);
         }
         tc_commit(done + s);
         committed = i;
-        // refill the stage used one step back once its MMAs are through
-        if (i >= 1 && i - 1 + S < n) {
-          const int sp_ = (i - 1) % S;
-          if (!(ok = mbar_wait(done + sp_, ((i - 1) / S) & 1))) break;
-          load(i - 1 + S);
-        }
+      }
+    }
+  } else {
+    // ---------------- copy warp: a stage's activation tiles as soon as its previous MMAs are through
+    pdl_wait();
+    pdl_trigger();
+    if (lane == 0) {
+      const size_t gstride = tc_plane_bytes(mpad, kTcK);  // bytes of one stage of a plane
+      for (int j = 0; j < n; ++j) {
+        const int s = j % S;
+        if (j >= S && !(ok = mbar_wait(done + s, ((j / S) - 1) & 1))) break;
+        unsigned char* B_hi = stage0 + s * tc_stage_bytes(NT) + 2 * kA;
+        const size_t src = size_t(kb + j) * gstride + size_t(m0 >> 3) * kTcSbo;
+        mbar_expect_tx(b_full + s, 2 * kB);
+        bulk_g2s(B_hi, xhi + src, kB, b_full + s);
+        bulk_g2s(B_hi + kB, xlo + src, kB, b_full + s);
+        issued = j + 1;
       }
     }
   }
   // the last commit covers every MMA issued before it
-  constexpr int kIssueWarp = kTcProducers / 32;
+  constexpr int kIssueWarp = kTcMmaWarp;
   if (wid < kIssueWarp && n > 0) {
     const bool fin = mbar_wait(done + (n - 1) % S, ((n - 1) / S) & 1);
     ok = ok && fin;
@@ -377,8 +470,8 @@ __global__ void __launch_bounds__(kTcThreads) k_q4_gemm_tc(WS W, const unsigned 
     if (tid == 0 && st) flag_timeout(st, kTcKidTimeout);
     // nothing may still write shared or tensor memory when they are released:
     // wait (bounded again) for the last MMAs and every stage's latest copy
-    if (wid == kIssueWarp && lane == 0) {
-      if (committed >= 0) mbar_wait(done + committed % S, (committed / S) & 1);
+    if (wid == kTcMmaWarp && lane == 0 && committed >= 0) mbar_wait(done + committed % S, (committed / S) & 1);
+    if (wid == kTcCopyWarp && lane == 0) {
       for (int s = 0; s < S && s < issued; ++s) {
         const int j = s + S * ((issued - 1 - s) / S);  // the stage's latest copy
         mbar_wait(b_full + s, (j / S) & 1);
