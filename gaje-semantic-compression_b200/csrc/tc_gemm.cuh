@@ -22,13 +22,15 @@
 // CTA: 128 weight rows (the MMA's M) x NT vectors (its N), S stages of 32 K
 // (one Q4 block per row; S = 4 at NT = 256, up to 8 for narrower tiles).
 // Warp roles, each waiting only on the barriers it consumes:
-// - warps 0-7 make the A tiles (for Q4: warps 0-3 stream the raw words
-//   through a shared-memory ring, warps 4-7 dequantise them) and arrive on
-//   a_full;
+// - warps 0-7 make the A tiles (two threads per weight row) and arrive on
+//   a_full; for Q4 they dequantise raw words that warp 10 streams through a
+//   shared-memory ring with cp.async, kTcRawStages stages ahead;
 // - warp 8 lane 0 issues a stage's 2 k-steps x 3 MMAs once a_full and b_full
 //   are complete and commits them to the stage's `done` barrier;
 // - warp 9 lane 0 issues the activation copies of a stage (b_full, transaction
 //   bytes) once `done` says the stage's previous MMAs are through.
+// The epilogue reads the accumulator 32 columns per tcgen05.ld (one wait per
+// 32 columns).
 // The MMA lane never waits on an MMA completion, so the tensor pipe's queue
 // stays full while the copies and the dequantisation run ahead.  The f32
 // accumulator is NT columns of tensor memory; warp w < 8 reads lane quarter
@@ -46,7 +48,8 @@ namespace gaje {
 constexpr int kTcProducers = 256;                 // warps 0-7: two threads per weight row
 constexpr int kTcMmaWarp = kTcProducers / 32;     // lane 0 issues the MMAs
 constexpr int kTcCopyWarp = kTcMmaWarp + 1;       // lane 0 issues the activation copies
-constexpr int kTcThreads = kTcProducers + 64;
+constexpr int kTcLoadWarp = kTcMmaWarp + 2;       // streams raw Q4 words (Q4 sources)
+constexpr int kTcThreads = kTcProducers + 96;
 constexpr int kTcRows = 128;                      // weight rows per CTA (MMA M)
 constexpr int kTcK = 32;                          // K per stage: one Q4 block of every row
 constexpr int kTcChunks = kTcK / 8;               // 16-byte K chunks of a row per stage
@@ -98,8 +101,12 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-// 32 lanes x 8 consecutive 32-bit columns of tensor memory into 8 registers.
-__device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
+// 32 lanes x N consecutive 32-bit columns of tensor memory into N registers
+// per thread (one load, one wait).
+template <int N>
+__device__ __forceinline__ void tc_ld(uint32_t taddr, float (&v)[N]);
+template <>
+__device__ __forceinline__ void tc_ld<8>(uint32_t taddr, float (&v)[8]) {
   uint32_t r[8];
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
@@ -107,6 +114,26 @@ __device__ __forceinline__ void tc_ld8(uint32_t taddr, float (&v)[8]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
   for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+template <>
+__device__ __forceinline__ void tc_ld<16>(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+template <>
+__device__ __forceinline__ void tc_ld<32>(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // (hi, lo) bf16 pairs of 8 consecutive floats: 16 bytes each.
@@ -138,19 +165,20 @@ __host__ __device__ __forceinline__ size_t tc_xoff(int r, int c, int mpad) {
   return ((size_t(c / kTcChunks) * (mpad >> 3) + (r >> 3)) * kTcChunks + (c % kTcChunks)) * 128 + (r & 7) * 16;
 }
 
-// Weight sources of the A operand.  Q4Rows (kRawRing): four loader warps
-// copy each stage's raw words (one Q4 block of each of the 128 rows) into a
-// shared-memory ring kTcRawStages deep with cp.async, tracked by an
-// mbarrier; four converter warps, a row per thread, dequantise a whole block
-// per stage into the A tiles.  The converters issue no global loads, so the
-// proxy fence that publishes their tile writes to the tensor cores waits on
-// nothing else.  F32Rows: a thread owns 16 consecutive elements (half h of a
-// 32-element block) of one row per stage, kDepth stages ahead in registers.
+// Weight sources of the A operand.  Q4Rows (kRawRing): the loader warp
+// copies each stage's raw words (one Q4 block of each of the 128 rows, four
+// rows per lane) into a shared-memory ring kTcRawStages deep with cp.async,
+// tracked by an mbarrier; warps 0-7 dequantise them into the A tiles, two
+// threads per row (half a block each).  The converters issue no global
+// loads, so the proxy fence that publishes their tile writes to the tensor
+// cores waits on nothing else.  F32Rows: a thread owns 16 consecutive
+// elements (half h of a 32-element block) of one row per stage, kDepth
+// stages ahead in registers.
 struct Q4Rows {  // Q4_0: w = fma(q, scale, min) (genomic.rs:267-336)
   Q4View W;
-  static constexpr bool kRawRing = true;  // words staged through shared memory by loader warps
+  static constexpr bool kRawRing = true;  // words staged through shared memory by the loader warp
   struct Regs {
-    uint4 q;
+    uint2 q;
     uint32_t s;
   };
   __host__ __device__ __forceinline__ int N() const { return W.N; }
@@ -161,14 +189,15 @@ struct Q4Rows {  // Q4_0: w = fma(q, scale, min) (genomic.rs:267-336)
     cp_async16(slot + rl * 16, W.qs + (size_t)r * W.nb + blk);
     cp_async4(slot + kTcRows * 16 + rl * 4, W.sm + (size_t)r * W.nbp + blk);
   }
-  __device__ __forceinline__ void read_raw(Regs& g, const unsigned char* slot, int rl) const {
-    g.q = *reinterpret_cast<const uint4*>(slot + rl * 16);
+  // half h (16 elements) of slot row rl
+  __device__ __forceinline__ void read_raw(Regs& g, const unsigned char* slot, int rl, int h) const {
+    g.q = *reinterpret_cast<const uint2*>(slot + rl * 16 + h * 8);
     g.s = *reinterpret_cast<const uint32_t*>(slot + kTcRows * 16 + rl * 4);
   }
   __device__ __forceinline__ void values(const Regs& g, int w, float (&v)[8]) const {
     float sc, mn;
     unpack_sm(g.s, sc, mn);
-    const uint32_t wd = w == 0 ? g.q.x : w == 1 ? g.q.y : w == 2 ? g.q.z : g.q.w;
+    const uint32_t wd = w == 0 ? g.q.x : g.q.y;
 #pragma unroll
     for (int e = 0; e < 8; ++e)  // exact q: the nibble in the mantissa of 2^23, minus 2^23
       v[e] = fmaf(__uint_as_float(((wd >> (4 * e)) & 0xFu) | 0x4B000000u) - 8388608.0f, sc, mn);
@@ -309,13 +338,13 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(WS W, const unsign
   }
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
-      mbar_init(a_full + s, WS::kRawRing ? kTcRows : kTcProducers);
+      mbar_init(a_full + s, kTcProducers);
       mbar_init(b_full + s, 1);
       mbar_init(done + s, 1);
     }
     for (int s = 0; s < kTcRawStages; ++s) {
-      mbar_init(raw_full + s, kTcRows);   // one (asynchronous) arrival per loader thread
-      mbar_init(raw_empty + s, kTcRows);  // one per converter thread
+      mbar_init(raw_full + s, 32);             // one (asynchronous) arrival per loader lane
+      mbar_init(raw_empty + s, kTcProducers);  // one per converter thread
     }
     fence_mbar_init();
   }
@@ -327,51 +356,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(WS W, const unsign
   int issued = 0, committed = -1;  // the issue lane's copies and last commit (for the drain)
   if (wid < kTcProducers / 32) {
     if constexpr (WS::kRawRing) {
+      // ---------------- converters: rows (t & 7) | ((t >> 4) << 3), half (t >> 3) & 1 -- the
+      // eight threads of a quarter warp write eight consecutive 16-byte rows of a core matrix
       unsigned char* raw0 = stage0 + S * tc_stage_bytes(NT);
-      if (wid < 4) {
-        // ---------------- loaders: thread = weight row; raw words up to kTcRawStages stages ahead
-        const int rl = tid, r = row0 + rl;
-        const bool rok = r < W.N();
-        for (int j = 0; j < n; ++j) {  // weights never depend on the previous kernel
-          const int slot = j % kTcRawStages;
-          if (j >= kTcRawStages && !(ok = mbar_wait(raw_empty + slot, ((j / kTcRawStages) - 1) & 1))) break;
-          if (rok) {
-            W.copy_raw(raw0 + slot * kTcRawSlot, rl, r, kb + j);
-            cp_async_mbar_arrive(raw_full + slot);
-          } else {
-            mbar_arrive(raw_full + slot);  // rows past N: whatever the slot holds, their outputs are dropped
-          }
+      const int rl = (tid & 7) | ((tid >> 4) << 3), h = (tid >> 3) & 1;
+      pdl_wait();
+      pdl_trigger();
+      for (int i = 0; i < n; ++i) {
+        const int s = i % S, slot = i % kTcRawStages;
+        if (i >= S && !(ok = mbar_wait(done + s, ((i / S) - 1) & 1))) break;  // the stage's previous MMAs
+        if (!(ok = mbar_wait(raw_full + slot, (i / kTcRawStages) & 1))) break;
+        typename WS::Regs g;
+        W.read_raw(g, raw0 + slot * kTcRawSlot, rl, h);
+        mbar_arrive(raw_empty + slot);
+        unsigned char* A_hi = stage0 + s * tc_stage_bytes(NT);
+        unsigned char* A_lo = A_hi + kA;
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {  // chunk w of the thread's 16 elements = stage chunk 2h + w
+          float v[8];
+          W.values(g, w, v);
+          uint4 hi, lo;
+          tc_split8(v, hi, lo);
+          const uint32_t off = tc_off(rl, 2 * h + w);
+          *reinterpret_cast<uint4*>(A_hi + off) = hi;
+          *reinterpret_cast<uint4*>(A_lo + off) = lo;
         }
-        cp_async_wait_all();  // none of this thread's copies still lands in shared memory
-        pdl_wait();
-        pdl_trigger();
-      } else {
-        // ---------------- converters: thread = weight row; a whole block per stage into the A tiles
-        const int rl = tid - 128;
-        pdl_wait();
-        pdl_trigger();
-        for (int i = 0; i < n; ++i) {
-          const int s = i % S, slot = i % kTcRawStages;
-          if (i >= S && !(ok = mbar_wait(done + s, ((i / S) - 1) & 1))) break;  // the stage's previous MMAs
-          if (!(ok = mbar_wait(raw_full + slot, (i / kTcRawStages) & 1))) break;
-          typename WS::Regs g;
-          W.read_raw(g, raw0 + slot * kTcRawSlot, rl);
-          mbar_arrive(raw_empty + slot);
-          unsigned char* A_hi = stage0 + s * tc_stage_bytes(NT);
-          unsigned char* A_lo = A_hi + kA;
-          #pragma unroll
-          for (int w = 0; w < kTcChunks; ++w) {
-            float v[8];
-            W.values(g, w, v);
-            uint4 hi, lo;
-            tc_split8(v, hi, lo);
-            const uint32_t off = tc_off(rl, w);
-            *reinterpret_cast<uint4*>(A_hi + off) = hi;
-            *reinterpret_cast<uint4*>(A_lo + off) = lo;
-          }
-          fence_async_smem();  // these generic-proxy writes, visible to the tensor cores
-          mbar_arrive(a_full + s);
-        }
+        fence_async_smem();  // these generic-proxy writes, visible to the tensor cores
+        mbar_arrive(a_full + s);
       }
     } else {
       // ---------------- f32 rows: thread t = weight row row0 + t/2, half t&1 of the stage's block
@@ -415,6 +426,25 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(WS W, const unsign
         }
       }
     }
+  } else if (wid == kTcLoadWarp) {
+    // ---------------- loader warp (Q4): lane l copies rows l, l+32, l+64, l+96 of each stage's
+    // block up to kTcRawStages stages ahead; weights never depend on the previous kernel
+    if constexpr (WS::kRawRing) {
+      unsigned char* raw0 = stage0 + S * tc_stage_bytes(NT);
+      for (int j = 0; j < n; ++j) {
+        const int slot = j % kTcRawStages;
+        if (j >= kTcRawStages && !(ok = mbar_wait(raw_empty + slot, ((j / kTcRawStages) - 1) & 1))) break;
+#pragma unroll
+        for (int q = 0; q < kTcRows / 32; ++q) {  // rows past N: whatever the slot holds, their outputs are dropped
+          const int rl = lane + 32 * q;
+          if (row0 + rl < W.N()) W.copy_raw(raw0 + slot * kTcRawSlot, rl, row0 + rl, kb + j);
+        }
+        cp_async_mbar_arrive(raw_full + slot);
+      }
+      cp_async_wait_all();  // none of this lane's copies still lands in shared memory
+    }
+    pdl_wait();
+    pdl_trigger();
   } else if (wid == kTcMmaWarp) {
     // ---------------- MMA warp: a stage's MMAs as soon as its A and B tiles are in
     pdl_wait();
@@ -489,18 +519,19 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(WS W, const unsign
     const float bias = (bp && has0) ? __ldg(bp + rr) : 0.f;
     const float bias1 = __shfl_down_sync(0xffffffffu, bias, 1);
     constexpr int kHalf = NT / 2 < 8 ? 8 : NT / 2;
+    constexpr int kC = kHalf < 32 ? kHalf : 32;  // columns per TMEM load (kHalf is a multiple)
     const int cb = (wid >> 2) * kHalf, ce = min(NT, cb + kHalf);
 #pragma unroll 1
-    for (int c0 = cb; c0 < ce; c0 += 8) {
-      float v[8];
-      tc_ld8(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
+    for (int c0 = cb; c0 < ce; c0 += kC) {
+      float v[kC];
+      tc_ld<kC>(tmem + (uint32_t(q * 32) << 16) + uint32_t(c0), v);
       if (Z > 1) {  // partial tile -> part[z][m][row]
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
+        for (int j = 0; j < kC; ++j)
           if (has0 && m0 + c0 + j < M) sp.part[((size_t)blockIdx.z * M + m0 + c0 + j) * WN + rr] = v[j];
       } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
+        for (int j = 0; j < kC; ++j) {
           const float f = flush_small(v[j]);
           const float f1 = __shfl_down_sync(0xffffffffu, f, 1);  // row rr + 1
           if ((lane & 1) == 0 && has0 && m0 + c0 + j < M) epi(m0 + c0 + j, rr, f + bias, has1, f1 + bias1);
@@ -527,10 +558,28 @@ __global__ void __launch_bounds__(256) k_tc_reduce(const float* part, int Z, int
   const int m = int(it / np), r0 = 2 * int(it - (long)m * np);
   const bool has1 = r0 + 1 < N;
   float s0 = 0.f, s1 = 0.f;
-  for (int z = 0; z < Z; ++z) {
-    const float* p = part + ((size_t)z * M + m) * N + r0;
-    s0 += __ldcg(p);
-    if (has1) s1 += __ldcg(p + 1);
+  if ((N & 1) == 0) {  // row pairs are 8-byte aligned: eight splits' loads in flight, added in split order
+    const size_t zs = (size_t)M * N;
+    const float* p = part + (size_t)m * N + r0;
+#pragma unroll 1
+    for (int z0 = 0; z0 < Z; z0 += 8) {
+      float2 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        v[u] = z0 + u < Z ? __ldcg(reinterpret_cast<const float2*>(p + (z0 + u) * zs)) : make_float2(0.f, 0.f);
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (z0 + u < Z) {
+          s0 += v[u].x;
+          s1 += v[u].y;
+        }
+    }
+  } else {
+    for (int z = 0; z < Z; ++z) {
+      const float* p = part + ((size_t)z * M + m) * N + r0;
+      s0 += __ldcg(p);
+      if (has1) s1 += __ldcg(p + 1);
+    }
   }
   const float b0 = bias ? __ldg(bias + r0) : 0.f;
   const float b1 = (bias && has1) ? __ldg(bias + r0 + 1) : 0.f;
