@@ -911,7 +911,7 @@ template <class WS, class Epi>
 int tc_gemm_run(const TcPlan& p, const WS& W, const float* x, int M, Epi epi, const TcBuffers& b, cudaStream_t s,
                 bool pdl, const TcNorm& nm, DevState* st = nullptr) {
   TcSplitArgs sa{x, M, W.K(), p.mpad, nm.w, nm.eps, b.hi, b.lo, nm.st, nm.pos, nm.layer};
-  cudaError_t e = launch_k(k_tc_split, dim3(unsigned((p.mpad + 3) / 4)), dim3(128), 0, s, pdl, sa);
+  cudaError_t e = launch_k(k_tc_split, dim3(unsigned(p.mpad)), dim3(kTsThreads), 0, s, pdl, sa);
   if (e == cudaSuccess) {
     switch (p.nt) {
       case 16: e = tc_launch_nt<16>(p, W, M, epi, b, s, true, st); break;

@@ -303,16 +303,14 @@ __device__ __forceinline__ void nan_flag(DevState* st, unsigned pos, int layer, 
   atomicMin(&st->nan_code, pos * 4096u + unsigned(layer) * 8u + check);
 }
 
-// SwiGLU of activation.rs:35-51 (swiglu_balanced).
+// SwiGLU of activation.rs:35-51 (swiglu_balanced): sigma = 1 / (1 + e^-g) for
+// g >= 0, e^g / (1 + e^g) below, on the clamped g.  Both arms take the same
+// exponential, e^-|g|, so one expf, one select and one division give the two
+// arms' values exactly, without divergent branches.
 __device__ __forceinline__ float swiglu_balanced(float g, float u) {
   const float gs = rclamp(g, -64.0f, 64.0f);
-  float sig;
-  if (gs >= 0.0f) {
-    sig = 1.0f / (1.0f + expf(-gs));
-  } else {
-    const float ex = expf(gs);
-    sig = ex / (1.0f + ex);
-  }
+  const float ex = expf(-fabsf(gs));
+  const float sig = (gs >= 0.0f ? 1.0f : ex) / (1.0f + ex);
   return (g * sig) * u;
 }
 

@@ -232,8 +232,9 @@ struct F32Rows {  // plain f32 rows [N][K] (the lm_head, linear/forward.rs:20-32
 };
 
 // x [M][K] f32 (optionally RMSNorm'd: (x * inv) * w, norm.rs:17-87) -> the
-// split planes hi/lo [mpad rows]; rows M..mpad-1 are zero.  One warp per row;
-// launch ceil(mpad/4) CTAs of 128 threads.  With st, the block-input and
+// split planes hi/lo [mpad rows]; rows M..mpad-1 are zero.  One CTA of
+// kTsThreads per row (the sum of squares by a block reduction, added warp by
+// warp in a fixed order); launch mpad CTAs.  With st, the block-input and
 // normed-output NaN guards (block/forward.rs:11-13, :22-24) at pos[row].
 struct TcSplitArgs {
   const float* x;
@@ -246,19 +247,22 @@ struct TcSplitArgs {
   const unsigned* pos;
   int layer;
 };
-__global__ void __launch_bounds__(128) k_tc_split(TcSplitArgs A) {
+constexpr int kTsThreads = 256;
+__global__ void __launch_bounds__(kTsThreads) k_tc_split(TcSplitArgs A) {
   pdl_wait();
   pdl_trigger();
-  const int lane = threadIdx.x & 31;
-  const int r = blockIdx.x * 4 + (threadIdx.x >> 5);
+  __shared__ float red[kTsThreads / 32];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int r = blockIdx.x;
   if (r >= A.mpad) return;
   const bool live = r < A.M;
-  const float* xr = A.x + (size_t)min(r, A.M - 1) * A.K;
+  const float* xr = A.x + (size_t)(live ? r : 0) * A.K;
   float inv = 1.f;
-  if (A.norm_w && live) {
+  const bool norm = A.norm_w && live;  // uniform over the CTA
+  if (norm) {
     float ss = 0.f;
     int bad = 0;
-    for (int j = lane; j < (A.K >> 2); j += 32) {
+    for (int j = tid; j < (A.K >> 2); j += kTsThreads) {
       const float4 v = __ldg(reinterpret_cast<const float4*>(xr) + j);
       ss = fmaf(v.x, v.x, ss);
       ss = fmaf(v.y, v.y, ss);
@@ -267,11 +271,16 @@ __global__ void __launch_bounds__(128) k_tc_split(TcSplitArgs A) {
       bad |= (v.x != v.x) | (v.y != v.y) | (v.z != v.z) | (v.w != v.w);
     }
     ss = warp_sum(ss);
-    inv = 1.0f / sqrtf(ss / (float)A.K + A.eps);
-    if (A.st && __any_sync(0xffffffffu, bad) && lane == 0) nan_flag(A.st, A.pos[r], A.layer, kNanInput);
+    if (lane == 0) red[wid] = ss;
+    bad = __syncthreads_or(bad);
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kTsThreads / 32; ++w) tot += red[w];
+    inv = 1.0f / sqrtf(tot / (float)A.K + A.eps);
+    if (A.st && bad && tid == 0) nan_flag(A.st, A.pos[r], A.layer, kNanInput);
   }
   int bad_out = 0;
-  for (int c = lane; c < (A.K >> 3); c += 32) {
+  for (int c = tid; c < (A.K >> 3); c += kTsThreads) {
     float v[8];
     if (live) {
       const float4 a = __ldg(reinterpret_cast<const float4*>(xr + c * 8));
@@ -298,8 +307,10 @@ __global__ void __launch_bounds__(128) k_tc_split(TcSplitArgs A) {
     *reinterpret_cast<uint4*>(A.hi + off) = hi;
     *reinterpret_cast<uint4*>(A.lo + off) = lo;
   }
-  if (A.st && A.norm_w && live && __any_sync(0xffffffffu, bad_out) && lane == 0)
-    nan_flag(A.st, A.pos[r], A.layer, kNanAttnNorm);
+  if (A.st && norm) {
+    bad_out = __syncthreads_or(bad_out);
+    if (bad_out && tid == 0) nan_flag(A.st, A.pos[r], A.layer, kNanAttnNorm);
+  }
 }
 
 // Split-K work area: part[z][M][N] f32 partial tiles, finished by k_tc_reduce.
@@ -514,10 +525,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(WS W, const unsign
     const int q = wid & 3;
     const int rr = row0 + q * 32 + lane;  // TMEM lane = tile row
     const int WN = W.N();
-    const bool has0 = rr < WN, has1 = rr + 1 < WN;
+    const bool has0 = rr < WN;
     const float* bp = W.bias();
-    const float bias = (bp && has0) ? __ldg(bp + rr) : 0.f;
-    const float bias1 = __shfl_down_sync(0xffffffffu, bias, 1);
+    const float bias = (bp && has0) ? __ldg(bp + rr) : 0.f;  // this lane's row
     constexpr int kHalf = NT / 2 < 8 ? 8 : NT / 2;
     constexpr int kC = kHalf < 32 ? kHalf : 32;  // columns per TMEM load (kHalf is a multiple)
     const int cb = (wid >> 2) * kHalf, ce = min(NT, cb + kHalf);
@@ -530,11 +540,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(WS W, const unsign
         for (int j = 0; j < kC; ++j)
           if (has0 && m0 + c0 + j < M) sp.part[((size_t)blockIdx.z * M + m0 + c0 + j) * WN + rr] = v[j];
       } else {
+        // row pair (r0, r0 + 1) = lanes (2p, 2p + 1): of columns j, j + 1 the even lane
+        // finishes column j and the odd lane column j + 1, one exchange per column pair
+        const bool odd = lane & 1;
+        const int r0 = rr & ~1;
+        const bool p0 = r0 < WN, p1 = r0 + 1 < WN;
 #pragma unroll
-        for (int j = 0; j < kC; ++j) {
-          const float f = flush_small(v[j]);
-          const float f1 = __shfl_down_sync(0xffffffffu, f, 1);  // row rr + 1
-          if ((lane & 1) == 0 && has0 && m0 + c0 + j < M) epi(m0 + c0 + j, rr, f + bias, has1, f1 + bias1);
+        for (int j = 0; j < kC; j += 2) {
+          const float fa = flush_small(v[j]) + bias, fb = flush_small(v[j + 1]) + bias;
+          const float recv = __shfl_xor_sync(0xffffffffu, odd ? fa : fb, 1);
+          const int col = m0 + c0 + j + (odd ? 1 : 0);
+          if (p0 && col < M) epi(col, r0, odd ? recv : fa, p1, odd ? fb : recv);
         }
       }
     }
