@@ -18,6 +18,8 @@
 // attention.rs:88-127, swiglu_balanced.
 #pragma once
 
+#include <cuda_bf16.h>
+
 #include "gemm.cuh"
 
 namespace gaje {
@@ -583,6 +585,220 @@ __global__ void __launch_bounds__(kApThreads) k_attn_prefill(AttnPrefillArgs A) 
       const float4 v = make_float4(o[r][k].x * inv, o[r][k].y * inv, o[r][k].z * inv, o[r][k].w * inv);
       reinterpret_cast<float4*>(A.out + (size_t)(m0 + i) * A.nh * hd + (g * G + j) * hd)[e4] = v;
     }
+  }
+}
+
+// The same causal prefill attention on the tensor cores (legacy mma.sync
+// m16n8k16 bf16, f32 accumulate), for head_dim 64 and 128.  A warp owns 16
+// (row, query head) pairs of the CTA's 96 -- the pairing of k_attn_prefill
+// -- with its q rows as bf16 hi/lo A fragments in registers; K/V arrive in
+// 64-position tiles, split into bf16 hi/lo planes in padded shared memory
+// and read with ldmatrix (transposed for V).  Scores S = q.k take three MMAs
+// per 16-wide k-step (hi.hi + hi.lo + lo.hi, the products' dropped terms
+// below 2^-16 relative), then scale, the causal mask and the running
+// max/sum in f32 registers; the probabilities, split hi/lo the same way,
+// are fed straight from the score accumulators as the A fragments of P.V
+// (three MMAs again).  The register-resident P is why this uses mma.sync
+// rather than tcgen05 (whose A operand would have to round-trip through
+// shared or tensor memory for every 64-position tile).
+constexpr int kAtWarps = kApQG / 16;        // 6 warps x 16 pairs
+constexpr int kAtThreads = kAtWarps * 32;
+constexpr int kAtT = 64;                    // key positions per tile
+__host__ __device__ constexpr int attn_tc_stride(int hd) { return hd + 8; }  // bf16 per smem row (ldmatrix conflict-free)
+__host__ __device__ constexpr size_t attn_tc_smem(int hd) { return size_t(4) * kAtT * attn_tc_stride(hd) * 2; }
+
+__device__ __forceinline__ void at_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void at_ldsm4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void at_ldsm4t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// (x, y) -> bf16x2 hi (x in the low half) and the residues' bf16x2 lo.
+__device__ __forceinline__ void at_split2(float x, float y, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(x, y);
+  const float2 f = __bfloat1622float2(h);
+  const __nv_bfloat162 l = __floats2bfloat162_rn(x - f.x, y - f.y);
+  hi = *reinterpret_cast<const uint32_t*>(&h);
+  lo = *reinterpret_cast<const uint32_t*>(&l);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(kAtThreads, 1) k_attn_prefill_tc(AttnPrefillArgs A) {
+  static_assert(HD == 64 || HD == 128, "head_dim");
+  constexpr int SR = attn_tc_stride(HD), KS = HD / 16, ND = HD / 8;
+  extern __shared__ __align__(16) unsigned char at_smem[];
+  __nv_bfloat16* Khi = reinterpret_cast<__nv_bfloat16*>(at_smem);
+  __nv_bfloat16* Klo = Khi + kAtT * SR;
+  __nv_bfloat16* Vhi = Klo + kAtT * SR;
+  __nv_bfloat16* Vlo = Vhi + kAtT * SR;
+  const int G = A.nh / A.nkv, QB = attn_prefill_qb(G), QG = QB * G;
+  const int gk = blockIdx.y, m0 = (gridDim.x - 1 - blockIdx.x) * QB;  // longest causal spans first
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int gq = lane >> 2, tq = lane & 3;
+  pdl_wait();
+  pdl_trigger();
+  const int last = min(A.n, m0 + QB) - 1;
+  // this thread's two pairs (rows gq, gq + 8 of the warp's 16): the last position each sees
+  int plim[2];
+  const float* qrow[2];
+  float* orow[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int qh = 16 * wid + gq + 8 * h, i = qh / G, j = qh - i * G;
+    const bool live = qh < QG && m0 + i <= last;
+    plim[h] = live ? A.p0 + m0 + i : -1;
+    const size_t off = live ? (size_t)(m0 + i) * A.nh * HD + (size_t)(gk * G + j) * HD : 0;
+    qrow[h] = live ? A.q + off : nullptr;
+    orow[h] = live ? A.out + off : nullptr;
+  }
+  int wlim = max(plim[0], plim[1]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) wlim = max(wlim, __shfl_xor_sync(0xffffffffu, wlim, o));
+  // q A fragments: k-step kk, regs (row gq, dims 2tq..), (row gq+8, ..), (row gq, +8), (row gq+8, +8)
+  uint32_t qa[KS][4], ql[KS][4];
+#pragma unroll
+  for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int h = r & 1, dim = 16 * kk + 2 * tq + 8 * (r >> 1);
+      float2 v = make_float2(0.f, 0.f);
+      if (qrow[h]) v = __ldcg(reinterpret_cast<const float2*>(qrow[h] + dim));
+      at_split2(v.x, v.y, qa[kk][r], ql[kk][r]);
+    }
+  float o[ND][4];
+#pragma unroll
+  for (int nd = 0; nd < ND; ++nd) o[nd][0] = o[nd][1] = o[nd][2] = o[nd][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+  const int maxpos = A.p0 + last;
+  const float* kbase = A.kc + (size_t)gk * A.max_ctx * HD;
+  const float* vbase = A.vc + (size_t)gk * A.max_ctx * HD;
+  const uint32_t sKhi = smem_u32(Khi), sKlo = smem_u32(Klo), sVhi = smem_u32(Vhi), sVlo = smem_u32(Vlo);
+  // ldmatrix row addresses of this lane: matrix mi = lane / 8, row ri = lane % 8
+  const int mi = lane >> 3, ri = lane & 7;
+  const uint32_t koff = uint32_t(((mi >> 1) * 8 + ri) * SR + (mi & 1) * 8) * 2u;  // + 16 pos per pair, + 16 dims per k-step
+  const uint32_t voff = uint32_t(((mi & 1) * 8 + ri) * SR + (mi >> 1) * 8) * 2u;  // + 16 pos per k-step, + 16 dims per pair
+  for (int t0 = 0; t0 <= maxpos; t0 += kAtT) {
+    __syncthreads();  // the previous tile is consumed
+    for (int idx = tid; idx < kAtT * (HD / 4); idx += kAtThreads) {
+      const int jp = idx / (HD / 4), e4 = idx - jp * (HD / 4);
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (t0 + jp <= maxpos) {
+        kv = __ldcg(reinterpret_cast<const float4*>(kbase + (size_t)(t0 + jp) * HD) + e4);
+        vv = __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)(t0 + jp) * HD) + e4);
+      }
+      uint2 h2, l2;
+      at_split2(kv.x, kv.y, h2.x, l2.x);
+      at_split2(kv.z, kv.w, h2.y, l2.y);
+      *reinterpret_cast<uint2*>(Khi + jp * SR + 4 * e4) = h2;
+      *reinterpret_cast<uint2*>(Klo + jp * SR + 4 * e4) = l2;
+      at_split2(vv.x, vv.y, h2.x, l2.x);
+      at_split2(vv.z, vv.w, h2.y, l2.y);
+      *reinterpret_cast<uint2*>(Vhi + jp * SR + 4 * e4) = h2;
+      *reinterpret_cast<uint2*>(Vlo + jp * SR + 4 * e4) = l2;
+    }
+    __syncthreads();
+    if (t0 > wlim) continue;  // no pair of this warp sees the tile (warp-uniform)
+    // S = q k^T over the tile: n-tiles nt of 8 positions
+    float sc[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk)
+#pragma unroll
+      for (int np = 0; np < 4; ++np) {
+        const uint32_t a = koff + uint32_t(16 * np * SR + 16 * kk) * 2u;
+        uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+        at_ldsm4(sKhi + a, h0, h1, h2, h3);
+        at_ldsm4(sKlo + a, l0, l1, l2, l3);
+        at_mma(sc[2 * np], qa[kk], h0, h1);
+        at_mma(sc[2 * np], qa[kk], l0, l1);
+        at_mma(sc[2 * np], ql[kk], h0, h1);
+        at_mma(sc[2 * np + 1], qa[kk], h2, h3);
+        at_mma(sc[2 * np + 1], qa[kk], l2, l3);
+        at_mma(sc[2 * np + 1], ql[kk], h2, h3);
+      }
+    // scale, causal mask, running max / sum (rows gq, gq + 8: a quad of lanes per row)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int pos = t0 + nt * 8 + 2 * tq + e;
+          const float v = pos <= plim[h] ? sc[nt][2 * h + e] * A.scale : -INFINITY;
+          sc[nt][2 * h + e] = v;
+          mx = fmaxf(mx, v);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(mrow[h], mx);
+      float alpha = 1.f, psum = 0.f;
+      if (mn > -INFINITY) {  // pads and rows that see nothing yet keep p = 0
+        alpha = expf(mrow[h] - mn);
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float p = expf(sc[nt][2 * h + e] - mn);
+            sc[nt][2 * h + e] = p;
+            psum += p;
+          }
+      } else {
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) sc[nt][2 * h] = sc[nt][2 * h + 1] = 0.f;
+      }
+      psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+      psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+      lrow[h] = lrow[h] * alpha + psum;
+      mrow[h] = mn;
+#pragma unroll
+      for (int nd = 0; nd < ND; ++nd) {
+        o[nd][2 * h] *= alpha;
+        o[nd][2 * h + 1] *= alpha;
+      }
+    }
+    // O += P V: k-steps of 16 positions, P's A fragments straight from the score accumulators
+#pragma unroll
+    for (int kp = 0; kp < 4; ++kp) {
+      uint32_t pa[4], pl[4];
+      at_split2(sc[2 * kp][0], sc[2 * kp][1], pa[0], pl[0]);
+      at_split2(sc[2 * kp][2], sc[2 * kp][3], pa[1], pl[1]);
+      at_split2(sc[2 * kp + 1][0], sc[2 * kp + 1][1], pa[2], pl[2]);
+      at_split2(sc[2 * kp + 1][2], sc[2 * kp + 1][3], pa[3], pl[3]);
+#pragma unroll
+      for (int dp = 0; dp < ND / 2; ++dp) {
+        const uint32_t a = voff + uint32_t(16 * kp * SR + 16 * dp) * 2u;
+        uint32_t h0, h1, h2, h3, l0, l1, l2, l3;
+        at_ldsm4t(sVhi + a, h0, h1, h2, h3);
+        at_ldsm4t(sVlo + a, l0, l1, l2, l3);
+        at_mma(o[2 * dp], pa, h0, h1);
+        at_mma(o[2 * dp], pa, l0, l1);
+        at_mma(o[2 * dp], pl, h0, h1);
+        at_mma(o[2 * dp + 1], pa, h2, h3);
+        at_mma(o[2 * dp + 1], pa, l2, l3);
+        at_mma(o[2 * dp + 1], pl, h2, h3);
+      }
+    }
+  }
+  // out = O / (sum + 1e-12) (attention.rs:106-127)
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    if (!orow[h]) continue;
+    const float inv = 1.0f / (lrow[h] + 1e-12f);
+#pragma unroll
+    for (int nd = 0; nd < ND; ++nd)
+      *reinterpret_cast<float2*>(orow[h] + nd * 8 + 2 * tq) = make_float2(o[nd][2 * h] * inv, o[nd][2 * h + 1] * inv);
   }
 }
 

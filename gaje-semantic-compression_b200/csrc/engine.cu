@@ -979,8 +979,13 @@ int batch_setup(gaje_model* m) {
     if (int e = smem_optin((const void*)k_attn_batch2<2>, s2)) return e;
     if (int e = smem_optin((const void*)k_attn_batch2<4>, s2)) return e;
   }
-  if (m->pf_rows > 0)
+  if (m->pf_rows > 0) {
     if (int e = smem_optin((const void*)k_attn_prefill, attn_prefill_smem(m->nh / m->nkv, m->hd))) return e;
+    if (m->hd == 64)
+      if (int e = smem_optin((const void*)k_attn_prefill_tc<64>, attn_tc_smem(64))) return e;
+    if (m->hd == 128)
+      if (int e = smem_optin((const void*)k_attn_prefill_tc<128>, attn_tc_smem(128))) return e;
+  }
   const size_t lm8 = size_t(8) * m->d * 4, lm16 = size_t(16) * m->d * 4;
   if (int e = smem_optin((const void*)k_lmhead_batch<8, 4>, lm8)) return e;
   if (int e = smem_optin((const void*)k_lmhead_batch<16, 2>, lm16)) return e;
@@ -1184,8 +1189,13 @@ int launch_prefill_chunk(gaje_model* m, int nc, int p0, unsigned sid, bool head)
     AttnPrefillArgs ap{m->bq, m->battn, m->bcache.k + m->bcache.row(sid, l, 0, 0),
                        m->bcache.v + m->bcache.row(sid, l, 0, 0), nc, p0, m->nh, m->nkv, m->hd, m->max_ctx,
                        1.0f / sqrtf(float(m->hd))};
-    e = launch_k(k_attn_prefill, dim3(unsigned((nc + qb - 1) / qb), unsigned(m->nkv)), dim3(kApThreads),
-                 attn_prefill_smem(G, m->hd), st, true, ap);
+    const dim3 agrid(unsigned((nc + qb - 1) / qb), unsigned(m->nkv));
+    if (m->hd == 64)  // tensor cores for the head dims the configs use
+      e = launch_k(k_attn_prefill_tc<64>, agrid, dim3(kAtThreads), attn_tc_smem(64), st, true, ap);
+    else if (m->hd == 128)
+      e = launch_k(k_attn_prefill_tc<128>, agrid, dim3(kAtThreads), attn_tc_smem(128), st, true, ap);
+    else
+      e = launch_k(k_attn_prefill, agrid, dim3(kApThreads), attn_prefill_smem(G, m->hd), st, true, ap);
     if (e != cudaSuccess) break;
     e = batch_gemm<false>(m, nc, m->wo[l], m->battn, TcNorm{}, EpiResidBatch{m->bx, d, nullptr, bs, l});
     if (e != cudaSuccess) break;

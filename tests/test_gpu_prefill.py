@@ -37,11 +37,15 @@ def _decode_and_compare(gpu, ref, sid, first, steps):
     return worst
 
 
-@pytest.mark.parametrize("name,P,rows", [("tiny", 37, 64), ("small", 70, 32), ("smollm2-135m", 100, 128),
-                                         ("qwen2-0.5b", 90, 40)])
-def test_prefill_matches_token_by_token(g, O, make_model, name, P, rows):
+# head_dim 32 (tiny, small: the CUDA-core attention kernel), 64 (SmolLM2 G=3,
+# Qwen2 G=7) and 128 (G=6 as Qwen2.5-1.5B, G=2) for the tensor-core kernel
+@pytest.mark.parametrize("name,P,rows,over", [
+    ("tiny", 37, 64, {}), ("small", 70, 32, {}), ("smollm2-135m", 100, 128, {}), ("qwen2-0.5b", 90, 40, {}),
+    ("small", 150, 64, dict(n_embd=768, n_head=6, n_head_kv=1)),
+    ("small", 97, 48, dict(n_embd=512, n_head=4, n_head_kv=2))])
+def test_prefill_matches_token_by_token(g, O, make_model, name, P, rows, over):
     """rows < P: chunked prefill (later chunks attend to the cached ones)."""
-    path = make_model(name, seed=41)
+    path = make_model(name, seed=41, **over)
     gpu = g.load_genomic_auto(path, max_ctx=P + 16, max_streams=2, max_prefill=rows)
     gpu.set_k_wta_ratio(0.0)
     rng = np.random.default_rng(P)
