@@ -579,6 +579,34 @@ def run_ncu_case(args) -> None:
                       "last_token": int(toks[-1])}), flush=True)
 
 
+def run_ncu_batch(args) -> None:
+    """Profiling case for the batched kernels (no timing): --ncu-case with
+    --batch B runs args.steps batched greedy steps of B streams from empty
+    caches (no prefill, so a launch list stays short); with --prompt-only P
+    it prefills two streams with P-token prompts instead."""
+    import numpy as np
+    import torch
+
+    g = _pkg()
+    torch.cuda.set_device(0)
+    path = _ensure_model(g, args.config, SEED, 0, None)
+    rng = np.random.default_rng(SEED)
+    if args.prompt_only > 0:
+        P = args.prompt_only
+        model = g.load_genomic_auto(path, device=0, max_ctx=P + 16, max_streams=2, max_prefill=P)
+        model.set_k_wta_ratio(0.0)
+        out = [int(model.prefill(s, [int(t) for t in rng.integers(0, model.vocab_size, P)])) for s in range(2)]
+        print(json.dumps({"ncu_case": args.config, "prefill": P, "streams": 2, "argmax": out}), flush=True)
+        return
+    B = args.batch
+    model = g.load_genomic_auto(path, device=0, max_ctx=args.steps + 16, max_streams=B)
+    model.set_k_wta_ratio(0.0)
+    toks = [int(t) for t in rng.integers(0, model.vocab_size, B)]
+    for _ in range(args.steps):
+        toks = [int(t) for t in model.forward_batch(list(range(B)), toks)]
+    print(json.dumps({"ncu_case": args.config, "streams": B, "steps": args.steps, "tokens": toks[:4]}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -596,9 +624,13 @@ def main():
                     help="--batch prompts: one gaje_cuda_prefill pass per stream, or token-by-token batched steps")
     ap.add_argument("--sweep", action="store_true",
                     help="the isolated Q4_0 GEMV/GEMM sweep of configs[2] instead of the decode benchmark")
+    ap.add_argument("--prompt-only", type=int, default=0,
+                    help="with --ncu-case: prefill two streams with prompts of this many tokens (profiling)")
     ap.add_argument("--ncu-case", action="store_true",
                     help="the small profiling case: one launch filling the prompt's positions, then one "
-                         "launch of --steps decode steps (capture it with -k regex:k_decode_mega -s 1 -c 1)")
+                         "launch of --steps decode steps (capture it with -k regex:k_decode_fused -s 1 -c 1); "
+                         "with --batch B: --steps batched steps of B streams from empty caches; with "
+                         "--prompt-only P: two P-token prefills")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -609,7 +641,10 @@ def main():
         run_reference(args, rank)
         return
     if args.ncu_case:
-        run_ncu_case(args)
+        if args.batch > 0 or args.prompt_only > 0:
+            run_ncu_batch(args)
+        else:
+            run_ncu_case(args)
         return
     if args.sweep:
         run_sweep(args)
