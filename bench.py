@@ -581,9 +581,9 @@ def run_ncu_case(args) -> None:
 
 def run_ncu_batch(args) -> None:
     """Profiling case for the batched kernels (no timing): --ncu-case with
-    --batch B runs args.steps batched greedy steps of B streams from empty
-    caches (no prefill, so a launch list stays short); with --prompt-only P
-    it prefills two streams with P-token prompts instead."""
+    --batch B runs args.steps batched greedy steps of B streams, from empty
+    caches unless --context P prefills each stream with P tokens first; with
+    --prompt-only P it prefills two streams with P-token prompts instead."""
     import numpy as np
     import torch
 
@@ -598,10 +598,13 @@ def run_ncu_batch(args) -> None:
         out = [int(model.prefill(s, [int(t) for t in rng.integers(0, model.vocab_size, P)])) for s in range(2)]
         print(json.dumps({"ncu_case": args.config, "prefill": P, "streams": 2, "argmax": out}), flush=True)
         return
-    B = args.batch
-    model = g.load_genomic_auto(path, device=0, max_ctx=args.steps + 16, max_streams=B)
+    B, P = args.batch, args.context
+    model = g.load_genomic_auto(path, device=0, max_ctx=P + args.steps + 16, max_streams=B,
+                                max_prefill=max(P, 16))
     model.set_k_wta_ratio(0.0)
     toks = [int(t) for t in rng.integers(0, model.vocab_size, B)]
+    if P > 0:  # each stream's cache filled by one prefill pass first
+        toks = [int(model.prefill(s, [int(t) for t in rng.integers(0, model.vocab_size, P)])) for s in range(B)]
     for _ in range(args.steps):
         toks = [int(t) for t in model.forward_batch(list(range(B)), toks)]
     print(json.dumps({"ncu_case": args.config, "streams": B, "steps": args.steps, "tokens": toks[:4]}), flush=True)
@@ -624,6 +627,8 @@ def main():
                     help="--batch prompts: one gaje_cuda_prefill pass per stream, or token-by-token batched steps")
     ap.add_argument("--sweep", action="store_true",
                     help="the isolated Q4_0 GEMV/GEMM sweep of configs[2] instead of the decode benchmark")
+    ap.add_argument("--context", type=int, default=0,
+                    help="with --ncu-case --batch B: prefill each stream with this many tokens first")
     ap.add_argument("--prompt-only", type=int, default=0,
                     help="with --ncu-case: prefill two streams with prompts of this many tokens (profiling)")
     ap.add_argument("--ncu-case", action="store_true",
