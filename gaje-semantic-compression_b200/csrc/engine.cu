@@ -937,7 +937,7 @@ int tc_gemm_run(const TcPlan& p, const WS& W, const float* x, int M, Epi epi, co
 constexpr int kBatchAttnRows = 96;
 int batch_attn_splits(const gaje_model* m, int Bi) {
   const int by_smem = (m->max_ctx + kBatchAttnRows - 1) / kBatchAttnRows;
-  const int by_fill = (2 * m->sms + Bi * m->nkv - 1) / (Bi * m->nkv);
+  const int by_fill = (2 * m->sms) / (Bi * m->nkv);  // two CTAs per SM at most: no tail wave
   return std::max(1, std::min(kAttnMaxSplits, std::max(by_smem, by_fill)));
 }
 // The streamed attention kernel (k_attn_batch2) serves head_dim 32/64/128 with
@@ -948,7 +948,7 @@ bool batch_attn2(const gaje_model* m) {
 }
 int batch_attn2_splits(const gaje_model* m, int Bi) {
   const int by_len = (m->max_ctx + kAbMaxChunk - 1) / kAbMaxChunk;
-  const int by_fill = (2 * m->sms + Bi * m->nkv - 1) / (Bi * m->nkv);
+  const int by_fill = (2 * m->sms) / (Bi * m->nkv);  // two CTAs per SM at most: no tail wave
   return std::max(1, std::min(kAttnMaxSplits, std::max(by_len, by_fill)));
 }
 cudaError_t launch_attn2(gaje_model* m, int Bi, const AttnBatchArgs& aa) {
