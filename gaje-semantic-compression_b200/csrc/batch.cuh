@@ -592,8 +592,9 @@ __global__ void __launch_bounds__(kApThreads) k_attn_prefill(AttnPrefillArgs A) 
 // m16n8k16 bf16, f32 accumulate), for head_dim 64 and 128.  A warp owns 16
 // (row, query head) pairs of the CTA's 96 -- the pairing of k_attn_prefill
 // -- with its q rows as bf16 hi/lo A fragments in registers; K/V arrive in
-// 64-position tiles, split into bf16 hi/lo planes in padded shared memory
-// and read with ldmatrix (transposed for V).  Scores S = q.k take three MMAs
+// 64-position tiles (cp.async brings the next tile's f32 rows into a staging
+// buffer while the current tile's MMAs run), split into bf16 hi/lo planes in
+// padded shared memory and read with ldmatrix (transposed for V).  Scores S = q.k take three MMAs
 // per 16-wide k-step (hi.hi + hi.lo + lo.hi, the products' dropped terms
 // below 2^-16 relative), then scale, the causal mask and the running
 // max/sum in f32 registers; the probabilities, split hi/lo the same way,
@@ -605,7 +606,10 @@ constexpr int kAtWarps = kApQG / 16;        // 6 warps x 16 pairs
 constexpr int kAtThreads = kAtWarps * 32;
 constexpr int kAtT = 64;                    // key positions per tile
 __host__ __device__ constexpr int attn_tc_stride(int hd) { return hd + 8; }  // bf16 per smem row (ldmatrix conflict-free)
-__host__ __device__ constexpr size_t attn_tc_smem(int hd) { return size_t(4) * kAtT * attn_tc_stride(hd) * 2; }
+// bf16 hi/lo K and V planes + the f32 staging of the next tile's K and V rows
+__host__ __device__ constexpr size_t attn_tc_smem(int hd) {
+  return size_t(4) * kAtT * attn_tc_stride(hd) * 2 + size_t(2) * kAtT * hd * 4;
+}
 
 __device__ __forceinline__ void at_mma(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -641,6 +645,8 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_attn_prefill_tc(AttnPrefillAr
   __nv_bfloat16* Klo = Khi + kAtT * SR;
   __nv_bfloat16* Vhi = Klo + kAtT * SR;
   __nv_bfloat16* Vlo = Vhi + kAtT * SR;
+  float* Kst = reinterpret_cast<float*>(Vlo + kAtT * SR);  // [kAtT][HD] f32 staging
+  float* Vst = Kst + kAtT * HD;
   const int G = A.nh / A.nkv, QB = attn_prefill_qb(G), QG = QB * G;
   const int gk = blockIdx.y, m0 = (gridDim.x - 1 - blockIdx.x) * QB;  // longest causal spans first
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -687,14 +693,26 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_attn_prefill_tc(AttnPrefillAr
   const int mi = lane >> 3, ri = lane & 7;
   const uint32_t koff = uint32_t(((mi >> 1) * 8 + ri) * SR + (mi & 1) * 8) * 2u;  // + 16 pos per pair, + 16 dims per k-step
   const uint32_t voff = uint32_t(((mi & 1) * 8 + ri) * SR + (mi >> 1) * 8) * 2u;  // + 16 pos per k-step, + 16 dims per pair
+  // a tile's rows (positions <= maxpos) into the staging buffer: this thread's 16-byte pieces
+  auto stage = [&](int ts) {
+    for (int idx = tid; idx < kAtT * (HD / 4); idx += kAtThreads) {
+      const int jp = idx / (HD / 4), e4 = idx - jp * (HD / 4);
+      if (ts + jp <= maxpos) {
+        cp_async16(Kst + 4 * idx, kbase + (size_t)(ts + jp) * HD + 4 * e4);
+        cp_async16(Vst + 4 * idx, vbase + (size_t)(ts + jp) * HD + 4 * e4);
+      }
+    }
+  };
+  stage(0);
   for (int t0 = 0; t0 <= maxpos; t0 += kAtT) {
-    __syncthreads();  // the previous tile is consumed
+    cp_async_wait_all();  // this thread's pieces of tile t0 have landed
+    __syncthreads();      // ... everyone's, and the previous tile's planes are consumed
     for (int idx = tid; idx < kAtT * (HD / 4); idx += kAtThreads) {
       const int jp = idx / (HD / 4), e4 = idx - jp * (HD / 4);
       float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
       if (t0 + jp <= maxpos) {
-        kv = __ldcg(reinterpret_cast<const float4*>(kbase + (size_t)(t0 + jp) * HD) + e4);
-        vv = __ldcg(reinterpret_cast<const float4*>(vbase + (size_t)(t0 + jp) * HD) + e4);
+        kv = reinterpret_cast<const float4*>(Kst)[idx];
+        vv = reinterpret_cast<const float4*>(Vst)[idx];
       }
       uint2 h2, l2;
       at_split2(kv.x, kv.y, h2.x, l2.x);
@@ -706,7 +724,8 @@ __global__ void __launch_bounds__(kAtThreads, 1) k_attn_prefill_tc(AttnPrefillAr
       *reinterpret_cast<uint2*>(Vhi + jp * SR + 4 * e4) = h2;
       *reinterpret_cast<uint2*>(Vlo + jp * SR + 4 * e4) = l2;
     }
-    __syncthreads();
+    __syncthreads();  // planes ready, staging free
+    if (t0 + kAtT <= maxpos) stage(t0 + kAtT);  // the next tile's rows land during this tile's MMAs
     if (t0 > wlim) continue;  // no pair of this warp sees the tile (warp-uniform)
     // S = q k^T over the tile: n-tiles nt of 8 positions
     float sc[8][4];
