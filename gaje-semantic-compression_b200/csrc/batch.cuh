@@ -211,21 +211,37 @@ __device__ __forceinline__ void attn_combine(const float* part_o, const float* p
     if (lane == 0) linv[j] = 1.0f / (Lsum + 1e-12f);
   }
   __syncthreads();
-  for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
-    const int j = idx / hd, e = idx - j * hd;
-    const float* po = part_o + (size_t)j * hd + e;  // split r at + r*G*hd
-    float O0 = 0.f, O1 = 0.f;
-    for (int r0 = 0; r0 < nsplit; r0 += 8) {  // eight partials in flight per thread
-      float v[8];
+  // up to four outputs per thread at once, eight partials each: 32 loads in
+  // flight; every output adds its splits in the same order as one at a time
+  const int total = G * hd, nt = blockDim.x;
+  for (int base = threadIdx.x; base < total; base += 4 * nt) {
+    float O0[4] = {0.f, 0.f, 0.f, 0.f}, O1[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int r0 = 0; r0 < nsplit; r0 += 8) {
+      float v[4][8];
 #pragma unroll
-      for (int k = 0; k < 8; ++k) v[k] = r0 + k < nsplit ? __ldcg(po + (size_t)(r0 + k) * G * hd) : 0.f;
+      for (int u = 0; u < 4; ++u) {
+        const int idx = base + u * nt;  // = j * hd + e: split r at part_o + r*G*hd + idx
 #pragma unroll
-      for (int k = 0; k < 8; k += 2) {
-        if (r0 + k < nsplit) O0 += v[k] * wsh[j * nsplit + r0 + k];
-        if (r0 + k + 1 < nsplit) O1 += v[k + 1] * wsh[j * nsplit + r0 + k + 1];
+        for (int k = 0; k < 8; ++k)
+          v[u][k] = (idx < total && r0 + k < nsplit) ? __ldcg(part_o + (size_t)(r0 + k) * total + idx) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = base + u * nt;
+        if (idx >= total) continue;
+        const int j = idx / hd;
+#pragma unroll
+        for (int k = 0; k < 8; k += 2) {
+          if (r0 + k < nsplit) O0[u] += v[u][k] * wsh[j * nsplit + r0 + k];
+          if (r0 + k + 1 < nsplit) O1[u] += v[u][k + 1] * wsh[j * nsplit + r0 + k + 1];
+        }
       }
     }
-    out[(size_t)j * hd + e] = (O0 + O1) * linv[j];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int idx = base + u * nt;
+      if (idx < total) out[idx] = (O0[u] + O1[u]) * linv[idx / hd];
+    }
   }
 }
 
