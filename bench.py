@@ -207,7 +207,7 @@ def run_ours(args, rank: int, world: int, local_rank: int, dist) -> None:
     path = _ensure_model(g, cfg_key, SEED, rank, dist)
     K, W = args.steps, args.warmup
     max_ctx = PROMPT_LEN + max(K, W) + 64
-    model = g.load_genomic_auto(path, device=local_rank, max_ctx=max_ctx)
+    model = g.load_genomic_auto(path, device=local_rank, max_ctx=max_ctx, use_megakernel=ENGINES[args.engine])
     model.set_k_wta_ratio(0.0)
     prompt = _prompt(model.vocab_size, PROMPT_LEN, SEED + rank)
     stream = torch.cuda.ExternalStream(model.stream, device=local_rank)
@@ -560,6 +560,11 @@ def run_batched(args, rank: int = 0, world: int = 1, local_rank: int = 0, dist=N
     print(json.dumps(line), flush=True)
 
 
+# batch-1 engines (the load option use_megakernel): the two-exchange fused
+# kernel (default), the five-exchange persistent kernel, a kernel per phase
+ENGINES = {"fused": 1, "mega": 2, "phase": 0}
+
+
 def run_ncu_case(args) -> None:
     """Two launches of the persistent kernel on one GPU: PROMPT_LEN greedy steps
     (the context a bench step sees), then args.steps steps, the launch a
@@ -570,7 +575,8 @@ def run_ncu_case(args) -> None:
     g = _pkg()
     torch.cuda.set_device(0)
     path = _ensure_model(g, args.config, SEED, 0, None)
-    model = g.load_genomic_auto(path, device=0, max_ctx=PROMPT_LEN + args.steps + 64)
+    model = g.load_genomic_auto(path, device=0, max_ctx=PROMPT_LEN + args.steps + 64,
+                                use_megakernel=ENGINES[args.engine])
     model.set_k_wta_ratio(0.0)
     model.clear_cache_py()
     t = model.decode_greedy(5, PROMPT_LEN)[-1]
@@ -627,6 +633,8 @@ def main():
                     help="--batch prompts: one gaje_cuda_prefill pass per stream, or token-by-token batched steps")
     ap.add_argument("--sweep", action="store_true",
                     help="the isolated Q4_0 GEMV/GEMM sweep of configs[2] instead of the decode benchmark")
+    ap.add_argument("--engine", choices=sorted(ENGINES), default="fused",
+                    help="batch-1 engine: fused (two exchanges per block, default), mega (five), phase")
     ap.add_argument("--context", type=int, default=0,
                     help="with --ncu-case --batch B: prefill each stream with this many tokens first")
     ap.add_argument("--prompt-only", type=int, default=0,
