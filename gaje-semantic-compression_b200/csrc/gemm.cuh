@@ -1,6 +1,6 @@
 // gemm.cuh -- Q4_0 matrix times a few activation vectors: the batched-decode
 // projections (gaje_cuda_forward_batch) and the op-level M > 1 path of
-// gaje_cuda_q4_0_gemv (SURVEY configs[2] M = 8).
+// gaje_cuda_q4_0_gemv (the isolated GEMV sweep at M = 8).
 //
 // y[m][n] = flush(sum_b scale_b*A_b + min_b*X_b) + bias[n] with
 // A_b = sum_k q_k x_mk over block b (the AVX2 arm of genomic.rs:267-336

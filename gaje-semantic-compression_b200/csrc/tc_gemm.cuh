@@ -1,7 +1,7 @@
 // tc_gemm.cuh -- Q4_0 matrix times many activation vectors on the 5th-gen
 // tensor cores (tcgen05): the prefill and wide-batch projections, and the
-// op-level M >= 16 path of gaje_cuda_q4_0_gemv (SURVEY configs[2] M = 64,
-// 512).
+// op-level M >= 16 path of gaje_cuda_q4_0_gemv (the isolated GEMM sweep at
+// M = 64, 512).
 //
 // y[m][n] = flush(sum_k w_nk x_mk) + bias[n] with w = fma(q, scale, min) per
 // element, the reference's own dequantisation (genomic.rs:267-336 AVX2 arm:
