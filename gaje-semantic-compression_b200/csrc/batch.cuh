@@ -1,6 +1,6 @@
 // batch.cuh -- one decode step for B independent streams of the same model
-// (gaje_cuda_forward_batch; BASELINE configs[3] decode and the per-rank body
-// of configs[4]).  Each stream has its own KV cache and position; the weights
+// (gaje_cuda_forward_batch: decode of a few streams after long prompts, and
+// the per-rank body of multi-GPU serving).  Each stream has its own KV cache and position; the weights
 // of a step are read once for all B streams.
 //
 // A step is a chain of kernels on the model's stream, captured once per batch

@@ -378,8 +378,16 @@ struct gaje_model {
   float* bxg = nullptr;                  // [nranks * max_streams][d] residual rows of every rank
   unsigned long long* bkey = nullptr;    // [nranks * max_streams] this rank's best key per gathered row
   unsigned long long* bkey_all = nullptr;  // [nranks][nranks * max_streams]
+  // segment timers of the sharded step (events on the model stream): body,
+  // residual all-gather, norm + lm_head slice + row argmax, key all-gather +
+  // merge; accumulated over the calls since the last gaje_cuda_shard_timings
+  cudaEvent_t tev[5] = {};
+  double tacc[4] = {0, 0, 0, 0};
+  unsigned tcount = 0;
 
   ~gaje_model() {
+    for (cudaEvent_t e : tev)
+      if (e) cudaEventDestroy(e);
     if (nccl) {
       const NcclApi& api = nccl_api();
       if (nccl_broken ? api.comm_abort : api.comm_destroy) (nccl_broken ? api.comm_abort : api.comm_destroy)(nccl);
@@ -434,6 +442,7 @@ struct gaje_model {
     a.part_o = part_o;
     a.part_ml = part_ml;
     a.cnt = attn_cnt;
+    a.bad = nullptr;  // a timeout is reported through st
     a.ctx = 0;
     a.stride = max_ctx;
     a.nh = nh;
@@ -1250,6 +1259,7 @@ int sharded_head(gaje_model* m, const float* x_local, int B, unsigned* d_argmax)
   };
   ncclResult_t r = api.all_gather(x_local, m->bxg, size_t(B) * d, ncclFloat32, m->nccl, st);
   if (r != ncclSuccess) return nccl_fail(r, "all-gather of the residual rows");
+  if (m->tev[2]) CK(cudaEventRecord(m->tev[2], st));
   cudaError_t e = cudaSuccess;
   if (M >= kBatchTcMin && m->btc_hi && d % kTcK == 0) {
     // output norm fused into the split, this rank's vocab rows on the tensor cores
@@ -1286,10 +1296,12 @@ int sharded_head(gaje_model* m, const float* x_local, int B, unsigned* d_argmax)
     }
   }
   if (e != cudaSuccess) return set_error(GAJE_ERR_CUDA, std::string("kernel launch: ") + cudaGetErrorString(e));
+  if (m->tev[3]) CK(cudaEventRecord(m->tev[3], st));
   r = api.all_gather(m->bkey, m->bkey_all, size_t(M), ncclUint64, m->nccl, st);
   if (r != ncclSuccess) return nccl_fail(r, "all-gather of the argmax keys");
   k_shard_argmax<<<1, 256, 0, st>>>(m->bkey_all, n, B, m->rank, d_argmax);
   CK(cudaGetLastError());
+  if (m->tev[4]) CK(cudaEventRecord(m->tev[4], st));
   return GAJE_OK;
 }
 
@@ -1556,6 +1568,7 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     m->bgraphs.assign(size_t(m->max_streams) + 1, nullptr);
     if (m->pf_rows > 0)
       CK(cudaHostAlloc(&m->h_pf_tab, size_t(3) * m->pf_rows * sizeof(unsigned), cudaHostAllocDefault));
+    for (cudaEvent_t& e : m->tev) CK(cudaEventCreate(&e));
     if (int s = batch_setup(m)) return s;
   }
   CK(cudaMemsetAsync(m->kcache, 0, L * size_t(m->nkv) * m->max_ctx * m->hd * 4, m->stream));
@@ -1860,6 +1873,8 @@ int gaje_cuda_forward_batch(gaje_model* m, const uint32_t* stream_ids, const uin
   cudaStream_t st = m->stream;
   const int Bi = int(B);
   CK(cudaMemcpyAsync(m->bdev, m->h_bdev, 3 * S * sizeof(unsigned), cudaMemcpyHostToDevice, st));
+  const bool timed = m->tev[0] != nullptr;
+  if (timed) CK(cudaEventRecord(m->tev[0], st));
   if (!m->use_graph) {
     if (int s = launch_batch(m, Bi)) return s;
   } else {
@@ -1883,8 +1898,12 @@ int gaje_cuda_forward_batch(gaje_model* m, const uint32_t* stream_ids, const uin
     }
     CK(cudaGraphLaunch(ge, st));
   }
-  if (m->nranks > 1)  // the collective head: every rank's rows through this rank's vocab rows
+  if (timed) CK(cudaEventRecord(m->tev[1], st));
+  if (m->nranks > 1) {  // the collective head: every rank's rows through this rank's vocab rows
     if (int s = sharded_head(m, m->bx, Bi, m->bdev + 3 * S)) return s;
+  } else if (timed) {  // one GPU: the head ran inside the step graph
+    for (int k = 2; k < 5; ++k) CK(cudaEventRecord(m->tev[k], st));
+  }
   const int kk = m->logits_k();
   if (logits_out && kk > 0)  // K-WTA on the returned logits (llm/forward.rs:58-61); the argmax is unaffected
     for (int b = 0; b < Bi; ++b) k_kwta<<<1, kKwtaThreads, 0, st>>>(m->blogits + size_t(b) * m->V, m->V, kk);
@@ -1897,10 +1916,29 @@ int gaje_cuda_forward_batch(gaje_model* m, const uint32_t* stream_ids, const uin
   } else {
     CK(cudaStreamSynchronize(st));
   }
+  if (timed) {
+    for (int k = 0; k < 4; ++k) {
+      float ms = 0.f;
+      if (cudaEventElapsedTime(&ms, m->tev[k], m->tev[k + 1]) == cudaSuccess) m->tacc[k] += ms;
+    }
+    m->tcount += 1;
+  }
   for (size_t b = 0; b < B; ++b) m->bpos[stream_ids[b]] += 1u;
   if (argmax_out)
     for (size_t b = 0; b < B; ++b) argmax_out[b] = m->h_bdev[3 * S + b];
   return m->check_state();
+}
+
+int gaje_cuda_batch_timings(gaje_model* m, float* ms_out, uint32_t* steps_out, int reset) {
+  if (!m || !ms_out) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  if (!m->tev[0]) return set_error(GAJE_ERR_INVALID, "the model was loaded without batched streams");
+  for (int k = 0; k < 4; ++k) ms_out[k] = float(m->tacc[k]);
+  if (steps_out) *steps_out = m->tcount;
+  if (reset) {
+    for (double& v : m->tacc) v = 0.0;
+    m->tcount = 0;
+  }
+  return GAJE_OK;
 }
 
 int gaje_cuda_profile_batch(gaje_model* m, const uint32_t* stream_ids, const uint32_t* tokens, size_t B, float* ms,
@@ -2293,7 +2331,7 @@ struct OpWorkspace {
 OpWorkspace g_ws[64];
 OpWorkspace g_ws_tc[64];  // the tensor-core GEMM op: [split-K partials][split planes]
 // layout: [DevState][argmax partials, kWsArgmaxParts x u64][argmax counter]
-//         then, from kWsAttnBase: [attention counters][part_ml][part_o]
+//         then, from kWsAttnBase: [attention counters][timeout marks][part_ml][part_o]
 constexpr size_t kWsArgmaxParts = 4096;
 constexpr size_t kWsPartsOff = 256;
 constexpr size_t kWsCntOff = kWsPartsOff + kWsArgmaxParts * 8;
@@ -2470,20 +2508,40 @@ int gaje_cuda_rms_norm(const float* x, const float* w, float eps, size_t n, floa
   return GAJE_OK;
 }
 
-int gaje_cuda_attention_decode(const float* q, const float* k_cache, const float* v_cache, size_t ctx,
-                               size_t cache_stride, size_t n_head, size_t n_head_kv, size_t head_dim, float* out,
-                               void* stream) {
+}  // extern "C"
+
+// The per-KV-head counters (64 x u32) and timeout marks (64 x u32) ahead of an
+// attention call's split partials.
+constexpr size_t kAttnScratchHeader = 512;
+
+// Argument checks shared by the two decode-attention entry points, before any
+// CUDA call: k_attn bulk-copies cache rows with cp.async.bulk, whose global
+// source must be 16-byte aligned, so the caches (and q / out, read and written
+// as rows) must be 16-byte aligned and head_dim a multiple of 4.
+static int attn_check_args(const float* q, const float* k_cache, const float* v_cache, const float* out, size_t ctx,
+                           size_t cache_stride, size_t n_head, size_t n_head_kv, size_t head_dim) {
   if (!q || !k_cache || !v_cache || !out || !ctx || !n_head || !n_head_kv || !head_dim)
     return set_error(GAJE_ERR_INVALID, "bad argument");
+  if (((uintptr_t)q | (uintptr_t)k_cache | (uintptr_t)v_cache | (uintptr_t)out) & 15u)
+    return set_error(GAJE_ERR_INVALID, "q, k_cache, v_cache and out must be 16-byte aligned");
   if (n_head % n_head_kv || n_head / n_head_kv > size_t(kAttnMaxGroup) || ctx > cache_stride || head_dim % 4 ||
       n_head_kv > 64 || cache_stride > (1u << 24))
     return set_error(GAJE_ERR_UNSUPPORTED, "unsupported attention geometry");
+  return GAJE_OK;
+}
+
+extern "C" {
+
+int gaje_cuda_attention_decode(const float* q, const float* k_cache, const float* v_cache, size_t ctx,
+                               size_t cache_stride, size_t n_head, size_t n_head_kv, size_t head_dim, float* out,
+                               void* stream) {
+  if (int s = attn_check_args(q, k_cache, v_cache, out, ctx, cache_stride, n_head, n_head_kv, head_dim)) return s;
   int dev;
   CK(cudaGetDevice(&dev));
   const size_t G = n_head / n_head_kv;
   const size_t po = n_head_kv * kAttnMaxSplits * G * head_dim, pml = n_head_kv * kAttnMaxSplits * G * 2;
   char* ws;
-  if (int s = ws_get(dev, kWsAttnBase + 256 + (pml + po) * 4 + 256, &ws)) return s;
+  if (int s = ws_get(dev, kWsAttnBase + kAttnScratchHeader + (pml + po) * 4 + 256, &ws)) return s;
   char* w = ws + kWsAttnBase;
   AttnArgs a{};
   a.q = q;
@@ -2491,7 +2549,8 @@ int gaje_cuda_attention_decode(const float* q, const float* k_cache, const float
   a.vc = v_cache;
   a.out = out;
   a.cnt = reinterpret_cast<unsigned*>(w);
-  a.part_ml = reinterpret_cast<float*>(w + 256);
+  a.bad = reinterpret_cast<unsigned*>(w + 256);
+  a.part_ml = reinterpret_cast<float*>(w + kAttnScratchHeader);
   a.part_o = a.part_ml + pml;
   a.ctx = int(ctx);
   a.stride = int(cache_stride);
@@ -2516,48 +2575,40 @@ int gaje_cuda_attention_decode(const float* q, const float* k_cache, const float
 // when a larger geometry arrives).
 constexpr size_t kAttnStaticScratchBytes = size_t(1) << 20;  // 1 MiB per device
 static __device__ __align__(256) unsigned char g_attn_scratch[kAttnStaticScratchBytes];
-static std::mutex g_attn_scratch_mu;
-static void* g_attn_scratch_ptr[64] = {};
 
 int gaje_cuda_attention_decode_static(const float* q, const float* k_cache, const float* v_cache, size_t ctx,
                                       size_t cache_stride, size_t n_head, size_t n_head_kv, size_t head_dim,
                                       float* out, void* stream) {
-  if (!q || !k_cache || !v_cache || !out || !ctx || !n_head || !n_head_kv || !head_dim)
-    return set_error(GAJE_ERR_INVALID, "bad argument");
-  if (n_head % n_head_kv || n_head / n_head_kv > size_t(kAttnMaxGroup) || ctx > cache_stride || head_dim % 4 ||
-      n_head_kv > 64 || cache_stride > (1u << 24))
-    return set_error(GAJE_ERR_UNSUPPORTED, "unsupported attention geometry");
+  if (int s = attn_check_args(q, k_cache, v_cache, out, ctx, cache_stride, n_head, n_head_kv, head_dim)) return s;
   const size_t G = n_head / n_head_kv;
   const size_t po = n_head_kv * kAttnMaxSplits * G * head_dim, pml = n_head_kv * kAttnMaxSplits * G * 2;
-  const size_t need = 256 + (pml + po) * 4;
+  const size_t need = kAttnScratchHeader + (pml + po) * 4;
   if (need > kAttnStaticScratchBytes)
     return set_error(GAJE_ERR_UNSUPPORTED,
                      "attention geometry needs " + std::to_string(need) +
-                         " bytes of scratch (256 + n_head*64*(head_dim+2)*4); the static buffer holds " +
+                         " bytes of scratch (512 + n_head*64*(head_dim+2)*4); the static buffer holds " +
                          std::to_string(kAttnStaticScratchBytes));
   int dev;
   CK(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return set_error(GAJE_ERR_INVALID, "device ordinal out of range");
-  char* w;
-  {
-    std::lock_guard<std::mutex> lk(g_attn_scratch_mu);
-    if (!g_attn_scratch_ptr[dev]) {  // once per device, with that device current
-      void* p = nullptr;
-      const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);
-      if (e != cudaSuccess || !p)
-        return set_error(GAJE_ERR_CUDA, std::string("cudaGetSymbolAddress of the attention scratch failed: ") +
-                                            cudaGetErrorString(e));
-      g_attn_scratch_ptr[dev] = p;
-    }
-    w = static_cast<char*>(g_attn_scratch_ptr[dev]);
-  }
+  // The buffer's device address, looked up with the device current.  The
+  // first call on a device does this set-up (it may load the module); later
+  // calls look it up again, which allocates nothing and keeps the address
+  // valid after the context has been torn down and created again.
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);
+  if (e != cudaSuccess || !p)
+    return set_error(GAJE_ERR_CUDA,
+                     std::string("cudaGetSymbolAddress of the attention scratch failed: ") + cudaGetErrorString(e));
+  char* w = static_cast<char*>(p);
   AttnArgs a{};
   a.q = q;
   a.kc = k_cache;
   a.vc = v_cache;
   a.out = out;
-  a.cnt = reinterpret_cast<unsigned*>(w);  // zero at module load; every completed call leaves them zero
-  a.part_ml = reinterpret_cast<float*>(w + 256);
+  // zero at module load; every call, completed or timed out, leaves them zero
+  a.cnt = reinterpret_cast<unsigned*>(w);
+  a.bad = reinterpret_cast<unsigned*>(w + 256);
+  a.part_ml = reinterpret_cast<float*>(w + kAttnScratchHeader);
   a.part_o = a.part_ml + pml;
   a.ctx = int(ctx);
   a.stride = int(cache_stride);

@@ -518,6 +518,7 @@ struct AttnArgs {
   float* part_o;
   float* part_ml;
   unsigned* cnt;    // [nkv]
+  unsigned* bad;    // [nkv] or nullptr: a split of the group timed out (its output becomes NaN)
   int ctx;          // >0: fixed context (op level); 0: st->pos + 1
   int stride, nh, nkv, hd;
   float scale;
@@ -579,12 +580,22 @@ __device__ __forceinline__ void attn_split(const AttnArgs& A, const int g, const
     Ks[(size_t)n_old * hd + i] = __ldcg(kbase + (size_t)n_old * hd + i);
     Vs[(size_t)n_old * hd + i] = __ldcg(vbase + (size_t)n_old * hd + i);
   }
-  __syncthreads();
-  if (!mbar_wait(bar, 0)) {
+  // a wait that ran out still arrives on the group's counter below, so the
+  // counter cannot stay at a partial count; the group's output becomes NaN
+  const bool ok = __syncthreads_and(mbar_wait(bar, 0)) != 0;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const size_t pbase = ((size_t)g * kAttnMaxSplits + s) * G;
+  // one split: the combine below reduces to O * (1/(l + 1e-12)), written here
+  const bool single = nsplit == 1;
+  if (!ok) {
     if (threadIdx.x == 0 && A.st) flag_timeout(A.st, 8);
-    mbar_wait(bar, 0);
-    return;
-  }
+    mbar_wait(bar, 0);  // the copies land before the CTA leaves (bounded again)
+    if (single) {
+      for (int i = threadIdx.x; i < G * hd; i += blockDim.x) A.out[(size_t)g * G * hd + i] = __int_as_float(0x7fc00000);
+      return;
+    }
+    if (threadIdx.x == 0 && A.bad) atomicExch(A.bad + g, 1u);
+  } else {
   // scores: thread per (head j, position t); the (e + t) % hd walk keeps the
   // 32 positions of a warp on 32 different banks
   for (int idx = threadIdx.x; idx < G * n; idx += blockDim.x) {
@@ -602,7 +613,6 @@ __device__ __forceinline__ void attn_split(const AttnArgs& A, const int g, const
     ps[j * cm + t] = (a0 + a1) * A.scale;
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   for (int j = wid; j < G; j += nw) {
     float m = -INFINITY;
     for (int t = lane; t < n; t += kWarp) m = fmaxf(m, ps[j * cm + t]);
@@ -620,9 +630,6 @@ __device__ __forceinline__ void attn_split(const AttnArgs& A, const int g, const
     }
   }
   __syncthreads();
-  const size_t pbase = ((size_t)g * kAttnMaxSplits + s) * G;
-  // one split: the combine below reduces to O * (1/(l + 1e-12)), written here
-  const bool single = nsplit == 1;
   for (int idx = threadIdx.x; idx < G * hd; idx += blockDim.x) {
     const int j = idx / hd, e = idx - j * hd;
     const float* pr = ps + j * cm;
@@ -641,12 +648,22 @@ __device__ __forceinline__ void attn_split(const AttnArgs& A, const int g, const
     A.part_ml[(pbase + threadIdx.x) * 2] = mls[2 * threadIdx.x];
     A.part_ml[(pbase + threadIdx.x) * 2 + 1] = mls[2 * threadIdx.x + 1];
   }
+  }  // ok
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) is_last = (atomicAdd(A.cnt + g, 1u) == (unsigned)nsplit - 1u);
   __syncthreads();
   if (!is_last) return;
   __threadfence();
+  if (A.bad && __ldcg(A.bad + g)) {  // a split of the group gave up: no valid partials
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) A.out[(size_t)g * G * hd + i] = __int_as_float(0x7fc00000);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      A.bad[g] = 0u;
+      A.cnt[g] = 0u;
+    }
+    return;
+  }
   // combine: per-split weights w = e^{m_s - M} in smem, then O in parallel
   for (int idx = threadIdx.x; idx < G * nsplit; idx += blockDim.x) {
     const int j = idx / nsplit, r = idx - j * nsplit;

@@ -159,6 +159,7 @@ def lib() -> C.CDLL:
         "gaje_cuda_nccl_unique_id": ([vp], i32),
         "gaje_cuda_load_sharded": ([C.c_char_p, C.POINTER(LoadOpts), i32, i32, vp], vp),
         "gaje_vocab_shard": ([u32, i32, i32, C.POINTER(u32), C.POINTER(u32)], i32),
+        "gaje_cuda_batch_timings": ([vp, vp, C.POINTER(u32), i32], i32),
         "gaje_argmax_key": ([f32, u32], u64),
         "gaje_argmax_key_index": ([u64], u32),
     }
@@ -429,6 +430,19 @@ class GenomicLLM:
         _check(lib().gaje_cuda_profile_batch(self._m, _ptr(sids), _ptr(toks), sids.size, _ptr(ms), _ptr(n)))
         names = ["qkv", "attn", "oproj", "gateup", "down", "lmhead", "kwta"]
         return {names[k]: float(ms[k]) for k in range(6)}
+
+    BATCH_SEGMENTS = ("body", "gather_rows", "lm_head", "gather_keys")
+
+    def batch_timings(self, reset: bool = False) -> dict:
+        """Device time of the batched steps per segment (ms, summed over the
+        forward_batch calls since the last reset) and the number of calls; on
+        one GPU "body" is the whole step."""
+        ms = np.zeros(4, dtype=np.float32)
+        n = C.c_uint32(0)
+        _check(lib().gaje_cuda_batch_timings(self._m, _ptr(ms), C.byref(n), 1 if reset else 0))
+        out = {k: float(ms[i]) for i, k in enumerate(self.BATCH_SEGMENTS)}
+        out["steps"] = int(n.value)
+        return out
 
     def clear_stream(self, stream_id: int) -> None:
         _check(lib().gaje_cuda_clear_stream(self._m, int(stream_id)))

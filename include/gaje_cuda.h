@@ -197,7 +197,8 @@ int gaje_cuda_set_seed(gaje_model* model, uint64_t seed);
 int gaje_cuda_decode_greedy(gaje_model* model, uint32_t first_token, size_t n_steps,
                             uint32_t* tokens_out);
 
-/* Batched decode (BASELINE configs[3]/[4]): one forward_core step
+/* Batched decode (a few streams after long prompts, or hundreds of serving
+ * streams): one forward_core step
  * (src/nn/llm/forward.rs:7-63) for each of B streams of the same model, each
  * with its own KV cache and position (its cache length).  stream_ids[B]
  * (distinct, < gaje_load_opts.max_streams) select the caches, tokens[B] are the
@@ -222,7 +223,7 @@ int gaje_cuda_forward_batch(gaje_model* model, const uint32_t* stream_ids, const
 int gaje_cuda_prefill(gaje_model* model, uint32_t stream_id, const uint32_t* tokens, size_t n,
                       uint32_t* argmax_out, float* logits_out);
 /* ------------------------------------------------- multi-GPU batched serving */
-/* Request-parallel serving over several GPUs: one process
+/* Request-parallel serving of many streams over several GPUs: one process
  * (or thread) per GPU, each holding the whole Q4 body and its own streams'
  * KV caches, and only a vocabulary slice of the f32 lm_head.  Each batched
  * step runs the body for the rank's own streams, all-gathers the residual
@@ -252,6 +253,16 @@ int gaje_cuda_nccl_unique_id(uint8_t* id_out /* GAJE_NCCL_ID_BYTES */);
  * gaje_vocab_shard.  Collective: all ranks call it together.  NULL on error. */
 gaje_model* gaje_cuda_load_sharded(const char* flat_path, const gaje_load_opts* opts, int nranks, int rank,
                                    const uint8_t* nccl_id /* GAJE_NCCL_ID_BYTES */);
+/* Where a batched model's gaje_cuda_forward_batch steps spend their device
+ * time, summed over the calls since the last reset (CUDA events on the model
+ * stream, host round trips excluded).  Sharded model: ms_out[0] the body
+ * (embedding rows through the last block), [1] the all-gather of the residual
+ * rows, [2] output norm + this rank's lm_head rows + the per-row best keys,
+ * [3] the all-gather of the keys + the merge.  One GPU: ms_out[0] the whole
+ * step (body and head), [1..3] zero.  *steps_out (nullable) counts the calls;
+ * reset != 0 zeroes both.  GAJE_ERR_INVALID without batched streams.  No
+ * reference counterpart (the reference decodes one stream in one process). */
+int gaje_cuda_batch_timings(gaje_model* model, float* ms_out /* [4] */, uint32_t* steps_out, int reset);
 /* The vocabulary split: rank r holds lm_head rows [row0, row0 + rows) with
  * chunk = ceil(V / nranks), row0 = r * chunk. */
 int gaje_vocab_shard(uint32_t vocab_size, int nranks, int rank, uint32_t* row0, uint32_t* rows);
@@ -374,7 +385,11 @@ int gaje_cuda_rms_norm(const float* x, const float* w, float eps, size_t n, floa
 
 /* Decode attention for one new position (src/nn/attention.rs:88-127): q[n_head*hd]
  * against ctx cached positions; k/v caches are [n_head_kv][cache_stride][hd]
- * (device).  out[n_head*hd]. */
+ * (device).  out[n_head*hd].  q, k_cache, v_cache and out must be 16-byte
+ * aligned (the cache rows are fetched with bulk copies) and head_dim a multiple
+ * of 4; otherwise GAJE_ERR_INVALID / GAJE_ERR_UNSUPPORTED before any CUDA call.
+ * A split whose copies do not land within the kernel's bounded wait (2 s)
+ * leaves its KV-head group's outputs NaN; the next call starts clean. */
 int gaje_cuda_attention_decode(const float* q, const float* k_cache, const float* v_cache,
                                size_t ctx, size_t cache_stride, size_t n_head,
                                size_t n_head_kv, size_t head_dim, float* out,
@@ -388,17 +403,23 @@ int gaje_cuda_attention_decode(const float* q, const float* k_cache, const float
  * device synchronise, when a larger geometry arrives).  No counterpart in the
  * reference, whose attention runs on the CPU.
  *
- * Same arguments, results and kernel as gaje_cuda_attention_decode.  The
- * split partials and the per-KV-head counters live in a 1 MiB buffer of static
- * device memory per device: the geometry must satisfy
- *   256 + n_head * 64 * (head_dim + 2) * 4 <= 1048576 bytes
+ * Same arguments, alignment rules, results and kernel as
+ * gaje_cuda_attention_decode.  The split partials, the per-KV-head counters and
+ * the per-KV-head timeout marks live in a 1 MiB buffer of static device memory
+ * per device (held by every GPU that loads the library until the process
+ * exits): the geometry must satisfy
+ *   512 + n_head * 64 * (head_dim + 2) * 4 <= 1048576 bytes
  * (e.g. n_head 14 / head_dim 64, n_head 12 / head_dim 128); a larger one is
  * rejected with GAJE_ERR_UNSUPPORTED and a message giving both sizes.  The
- * counters (the first 256 bytes) must be zero when a call starts: they are
- * zero when the library loads and every completed call leaves them zero.  The
- * first call on a device looks the buffer's address up with
- * cudaGetSymbolAddress (with that device current); make that first call before
- * any stream capture.  Calls that overlap on the same device race on the one
+ * counters and marks (the first 512 bytes) must be zero when a call starts:
+ * they are zero when the library loads, and every call leaves them zero,
+ * including one whose bounded wait ran out (that call's affected KV-head
+ * group reads NaN in out; nothing else needs resetting).  The first call on a
+ * device looks the buffer's address up with cudaGetSymbolAddress (with that
+ * device current; it may load the module): make that first call before any
+ * stream capture.  Every call repeats the lookup, which allocates nothing, so
+ * the entry point stays usable after a cudaDeviceReset; the buffer then starts
+ * from zero again.  Calls that overlap on the same device race on the one
  * buffer: serialise them (one stream, or events). */
 int gaje_cuda_attention_decode_static(const float* q, const float* k_cache, const float* v_cache,
                                       size_t ctx, size_t cache_stride, size_t n_head,

@@ -998,6 +998,35 @@ struct or_model {
   std::string err;
 };
 
+// The synthetic weights of the benchmark and test models, restated from the
+// product's description of its generator so that the CPU arm can write the
+// same `.gaje.flat` file without loading the product: key = splitmix64
+// finaliser of (seed ^ FNV-1a(name)); element pair p takes the finalised
+// key + golden * (2p+1) and key + golden * (2p+2), u1 = ((a >> 11) + 1) / 2^53,
+// u2 = (b >> 11) / 2^53, and Box-Muller in double: std * r cos(2 pi u2),
+// std * r sin(2 pi u2) with r = sqrt(-2 ln u1), each rounded to f32.
+static uint64_t syn_mix(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+void or_fill_normal(float* v, size_t n, uint64_t seed, const char* name, float std_) {
+  uint64_t h = 0xCBF29CE484222325ull;
+  for (const char* c = name; *c; ++c) h = (h ^ uint8_t(*c)) * 0x100000001B3ull;
+  const uint64_t key = syn_mix(seed ^ h);
+  const long long pairs = (long long)((n + 1) / 2);
+#pragma omp parallel for schedule(static)
+  for (long long p = 0; p < pairs; ++p) {
+    const uint64_t a = syn_mix(key + 0x9E3779B97F4A7C15ull * uint64_t(2 * p + 1));
+    const uint64_t b = syn_mix(key + 0x9E3779B97F4A7C15ull * uint64_t(2 * p + 2));
+    const double u1 = double((a >> 11) + 1) * (1.0 / 9007199254740992.0);
+    const double u2 = double(b >> 11) * (1.0 / 9007199254740992.0);
+    const double r = sqrt(-2.0 * log(u1));
+    v[size_t(2 * p)] = float(double(std_) * (r * cos(6.283185307179586 * u2)));
+    if (size_t(2 * p + 1) < n) v[size_t(2 * p + 1)] = float(double(std_) * (r * sin(6.283185307179586 * u2)));
+  }
+}
+
 void or_set_threads(int n) {
 #ifdef _OPENMP
   if (n > 0) omp_set_num_threads(n);

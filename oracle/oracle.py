@@ -78,6 +78,7 @@ def lib():
     L.or_generate.argtypes = [C.c_void_p, _szp, sz, sz, f32, f32, _szp, sz, C.c_uint64, _szp,
                               C.POINTER(C.c_size_t)]
     L.or_generate.restype = i32
+    L.or_fill_normal.argtypes = [_f32p, sz, C.c_uint64, C.c_char_p, f32]
     _lib = L
     return L
 
@@ -176,6 +177,14 @@ def f32_gemv(W, x) -> np.ndarray:
     y = np.zeros(W.shape[0], dtype=np.float32)
     lib().or_f32_gemv(W, np.ascontiguousarray(x, np.float32), W.shape[0], W.shape[1], y)
     return y
+
+
+def synthetic_normal(n: int, seed: int, name: str, std: float = 0.02) -> np.ndarray:
+    """The synthetic N(0, std) weights of tensor `name` (or `name.bias`) of a
+    benchmark / test model, as the product's synthetic writer draws them."""
+    v = np.empty(int(n), dtype=np.float32)
+    lib().or_fill_normal(v, v.size, int(seed) & 0xFFFFFFFFFFFFFFFF, name.encode(), float(std))
+    return v
 
 
 # -------------------------------------------------------------------- model

@@ -94,3 +94,33 @@ def write_flat(path, *, name, arch_family, n_embd, n_head, n_head_kv, n_blocks, 
             f.write(b"\x00" * pad)
         f.write(blob_bytes)
     return path
+
+
+def write_synthetic(path, *, seed, arch_family, n_embd, n_head, n_head_kv, n_blocks, ffn_dim, vocab_size, eps,
+                    rope_base, qkv_bias, embd_bit_depth=32, std=0.02):
+    """The benchmark / test model files without the product: the oracle's
+    restatement of the synthetic N(0, std) generator, the oracle's quantisers
+    and write_flat, in the synthetic writer's tensor order (tied token_embd /
+    lm_head written twice, unit norms).  Byte-identical to the product's
+    gaje_flat_write_synthetic (tests/test_format.py)."""
+    d, hd = n_embd, n_embd // n_head
+    qd, kvd, ff, V = n_head * hd, n_head_kv * hd, ffn_dim, vocab_size
+
+    def normal(rows, cols, name):
+        return oracle.synthetic_normal(rows * cols, seed, name, std).reshape(rows, cols)
+
+    ones = np.ones(d, np.float32)
+    emb = normal(V, d, "token_embd")
+    tensors = [("linear", "token_embd", embd_bit_depth, emb, None), ("norm", "output_norm", ones),
+               ("linear", "lm_head", embd_bit_depth, emb, None)]
+    for i in range(n_blocks):
+        p = f"blk.{i}."
+        bias = oracle.synthetic_normal(qd + 2 * kvd, seed, p + "attn_qkv.bias", std) if qkv_bias else None
+        tensors += [("norm", p + "attn_norm", ones), ("norm", p + "ffn_norm", ones),
+                    ("linear", p + "attn_qkv", 4, normal(qd + 2 * kvd, d, p + "attn_qkv"), bias),
+                    ("linear", p + "attn_output", 4, normal(d, qd, p + "attn_output"), None),
+                    ("linear", p + "ffn_gate_up", 4, normal(2 * ff, d, p + "ffn_gate_up"), None),
+                    ("linear", p + "ffn_down", 4, normal(d, ff, p + "ffn_down"), None)]
+    return write_flat(path, name=f"synthetic-family{arch_family}", arch_family=arch_family, n_embd=n_embd,
+                      n_head=n_head, n_head_kv=n_head_kv, n_blocks=n_blocks, vocab_size=vocab_size, eps=eps,
+                      rope_base=rope_base, qk_permute=1 if arch_family in (1, 2) else 0, tensors=tensors)

@@ -114,6 +114,19 @@ def test_writer_matches_numpy_exporter_bytes(g, tmp_path, bits_embd):
     assert open(a, "rb").read() == open(b, "rb").read()
 
 
+@pytest.mark.parametrize("name,over", [("tiny", {}), ("small", {}), ("tiny", {"embd_bit_depth": 8}),
+                                       ("small", {"n_embd": 384, "n_head": 6, "n_head_kv": 3})])
+def test_synthetic_model_without_the_product_is_byte_identical(g, tmp_path, name, over):
+    """bench.py's CPU arm writes its model with the oracle and the numpy writer
+    only; the file must be the product's synthetic model byte for byte."""
+    cfg = dict(g.configs.CONFIGS[name])
+    cfg.update(over)
+    a, b = str(tmp_path / "numpy.flat"), str(tmp_path / "product.flat")
+    flat_numpy.write_synthetic(a, seed=77, **cfg)
+    g.write_synthetic(b, seed=77, **cfg)
+    assert open(a, "rb").read() == open(b, "rb").read()
+
+
 def test_inspect_reads_config_and_descriptor(g, make_model):
     info = g.inspect_flat(make_model("small"))
     assert info["n_embd"] == 256 and info["n_head"] == 8 and info["n_head_kv"] == 2
