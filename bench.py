@@ -79,7 +79,7 @@ def _batch1_config(cfg_key: str, K: int, world: int) -> dict:
     return {"workload": f"{cfg_key} batch-1 greedy decode after a {PROMPT_LEN}-token prompt",
             "global_batch": world, "prompt_len": PROMPT_LEN, "decode_steps": K,
             "parallelism": f"replicas{world}" if world > 1 else "single",
-            "l2": "inputs larger than L2 (778 MB of weights streamed per step vs 126 MB L2)"}
+            "l2": "inputs larger than L2 (the weights streamed per step exceed the 126 MB L2)"}
 
 
 def _serve_config(K: int, world: int) -> dict:
@@ -780,7 +780,8 @@ def run_trace_fused(args) -> None:
     info = model.info()
     # attention CTAs stamp 0-8 and 15; every CTA with FFN outputs stamps 9-14
     segs_a = [("input gate + residual (A)", 0, 1), ("attn_norm staging", 1, 2), ("q/k/v GEMV + RoPE", 2, 3),
-              ("split attention", 3, 5), ("attn_output columns", 5, 6), ("split weight", 6, 15),
+              ("K/V rows wait", 3, 4), ("split attention math", 4, 5), ("attn_output columns", 5, 6),
+              ("split weight", 6, 15),
               ("red.add + publish (A)", 7, 8)]
     segs_b = [("residual x_a", 9, 10), ("ffn_norm staging", 10, 11), ("gate/up GEMV + SwiGLU", 11, 12),
               ("ffn_down columns", 12, 13), ("red.add + publish (B)", 13, 14)]

@@ -24,9 +24,12 @@ from .runtime import (  # noqa: F401
     load_genomic_auto,
     load_genomic_sharded,
     nccl_unique_id,
+    quantize_q4_0_device,
     quantize_q4_0_native,
+    quantize_q8_0_device,
     quantize_q8_0_native,
     rms_norm,
+    sample_top_p,
     vocab_shard,
     write_synthetic,
 )

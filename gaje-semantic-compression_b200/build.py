@@ -14,7 +14,8 @@ REPO = os.path.dirname(PKG_DIR)
 CSRC = os.path.join(PKG_DIR, "csrc")
 LIB_PATH = os.path.join(PKG_DIR, "libgaje_cuda.so")
 SOURCES = ["engine.cu", "flat_format.cpp"]
-HEADERS = ["kernels.cuh", "megakernel.cuh", "fused.cuh", "gemm.cuh", "batch.cuh", "tc_gemm.cuh", "flat_format.h"]
+HEADERS = ["kernels.cuh", "megakernel.cuh", "fused.cuh", "gemm.cuh", "batch.cuh", "tc_gemm.cuh", "quant.cuh", "sample.cuh",
+           "flat_format.h"]
 NVCC = os.environ.get("GAJE_NVCC", "/usr/local/cuda/bin/nvcc")
 
 NVCC_FLAGS = [

@@ -23,6 +23,8 @@ SMALL = dict(arch_family=2, n_embd=256, n_head=8, n_head_kv=2, n_blocks=4, ffn_d
 CONFIGS = {
     "smollm2-135m": SMOLLM2_135M,
     "qwen2-0.5b": QWEN2_0_5B,
+    # the exporter's --quant-embed variant: Q8_0 token_embd / lm_head
+    "qwen2-0.5b-q8e": dict(QWEN2_0_5B, embd_bit_depth=8),
     "qwen2.5-1.5b": QWEN2_5_1_5B,
     "tiny": TINY,
     "small": SMALL,
@@ -39,15 +41,17 @@ def q4_body_bytes(c: dict) -> int:
 
 def step_bytes(c: dict, ctx: int) -> dict:
     """Algorithmic HBM bytes of one batch-1 decode step at cache length ctx
-    (Q4 body + norms + bias + f32 lm_head + embedding row + KV reads)."""
+    (Q4 body + norms + bias + lm_head (f32, or Q8_0 bytes) + embedding row +
+    KV reads)."""
     d, hd = c["n_embd"], c["n_embd"] // c["n_head"]
     qd, kvd = c["n_head"] * hd, c["n_head_kv"] * hd
     L, V = c["n_blocks"], c["vocab_size"]
     body = q4_body_bytes(c)
     norms = (2 * L + 1) * d * 4
     bias = (qd + 2 * kvd) * 4 * L if c.get("qkv_bias") else 0
-    lm = V * d * 4
-    emb = d * 4
+    q8 = c.get("embd_bit_depth", 32) == 8
+    lm = V * (d // 32) * 34 if q8 else V * d * 4  # Q8_0: 34 bytes per 32 weights
+    emb = (d // 32) * 34 if q8 else d * 4
     kv = 2 * L * kvd * 4 * ctx
     return dict(body=body, norms=norms, bias=bias, lm_head=lm, embd=emb, kv=kv,
                 total=body + norms + bias + lm + emb + kv)

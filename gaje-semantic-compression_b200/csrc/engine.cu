@@ -31,6 +31,8 @@
 #include "batch.cuh"
 #include "tc_gemm.cuh"
 #include "fused.cuh"
+#include "quant.cuh"
+#include "sample.cuh"
 
 using namespace gaje;
 
@@ -121,7 +123,8 @@ struct Q4Dev {
   uint32_t* sm = nullptr;
   float* bias = nullptr;
   int N = 0, K = 0, nb = 0, nbp = 0;
-  Q4View view() const { return Q4View{qs, sm, bias, N, K, nb, nbp}; }
+  float* lut = nullptr;  // Genomic4Bit centroid tables [N][nb][16] (qs: codes, sm unused)
+  Q4View view() const { return Q4View{qs, sm, bias, N, K, nb, nbp, lut}; }
 };
 
 constexpr int kMaxDynSmem = 227 * 1024;
@@ -157,9 +160,11 @@ GemvPlan plan_gemv(int mode, const Q4Dev& m, int units, int sms) {
   GemvPlan p;
   p.units = units;
   p.upc = (units + sms - 1) / sms;
-  while (p.upc > 1 && gemv_smem_bytes(mode, m.K, m.nb, m.nbp, p.upc) > size_t(kMaxDynSmem)) p.upc = (p.upc + 1) / 2;
+  const bool lut = m.lut != nullptr;
+  while (p.upc > 1 && gemv_smem_bytes(mode, m.K, m.nb, m.nbp, p.upc, lut) > size_t(kMaxDynSmem))
+    p.upc = (p.upc + 1) / 2;
   p.grid = (units + p.upc - 1) / p.upc;
-  p.smem = gemv_smem_bytes(mode, m.K, m.nb, m.nbp, p.upc);
+  p.smem = gemv_smem_bytes(mode, m.K, m.nb, m.nbp, p.upc, lut);
   return p;
 }
 
@@ -337,7 +342,10 @@ struct gaje_model {
   // over k_decode_mega when the shape fits it
   bool fu_ok = false;      // planned (shape fits, buffers allocated)
   bool use_fused = false;  // planned and launchable
+  bool has_lut = false;             // Genomic4Bit tables in the body (kernel-per-phase engine only)
   FusedPlan fplan{};
+  int lm_row_bytes = 0;            // bytes of one lm_head row streamed by the fused kernel
+  unsigned char* lm_q8 = nullptr;  // fused kernel, Q8_0 lm_head: [Vl][lm_row_bytes] int8 codes, f16 scales
   size_t fused_smem = 0;
   std::vector<FuLayer> h_fl;
   FuLayer* d_fl = nullptr;
@@ -750,6 +758,56 @@ int upload_q4(gaje_model* m, const FlatFile& f, const MatrixRef& ref, Q4Dev& dst
   return GAJE_OK;
 }
 
+// Genomic4Bit rows as the engine keeps them (GenomicLinear::new,
+// init.rs:29-38 and :109-124): the code of element 2k, stored in the HIGH
+// nibble of byte k in the file, moves to the low nibble (the Q4_0 order the
+// kernels read), and the centroid table -- 16 floats for the whole matrix,
+// 16 per block column, or 16 per (row, block) -- is expanded to one table
+// per (row, block).  Rows take the permutation `mode`, as upload_q4's do.
+void lut4_rows_host(const uint8_t* nib, const float* cents, size_t n_cents, int N, int K, int mode, int hd,
+                    std::vector<uint32_t>& qs_words, std::vector<float>& lut) {
+  const size_t nb = size_t(K) / 32;
+  qs_words.assign(size_t(N) * nb * 4, 0u);
+  lut.assign(size_t(N) * nb * 16, 0.0f);
+#pragma omp parallel for schedule(static)
+  for (long long r = 0; r < (long long)N; ++r) {
+    const size_t src = size_t(repack_src_row(mode, int(r), hd, N / 2));
+    for (size_t b = 0; b < nb; ++b) {
+      uint8_t bytes[16];
+      for (int k = 0; k < 16; ++k) {
+        const uint8_t v = nib[(src * nb + b) * 16 + k];
+        bytes[k] = uint8_t((v >> 4) | (v << 4));
+      }
+      memcpy(&qs_words[(size_t(r) * nb + b) * 4], bytes, 16);
+      const float* c = n_cents == 16 ? cents : n_cents == nb * 16 ? cents + b * 16 : cents + (src * nb + b) * 16;
+      memcpy(&lut[(size_t(r) * nb + b) * 16], c, 64);
+    }
+  }
+}
+
+int upload_lut4(gaje_model* m, const FlatFile& f, const MatrixRef& ref, Q4Dev& dst, int mode) {
+  const FlatEntry* e = ref.parts[0];  // tables are never split (FlatFile::resolve)
+  std::vector<uint32_t> words;
+  std::vector<float> lut;
+  const float* cents = reinterpret_cast<const float*>(f.blob(e->c_off, e->c_len));
+  std::vector<float> cbuf(e->c_len / 4);
+  memcpy(cbuf.data(), cents, e->c_len);  // the blob is 64-byte aligned in the file, copied to be safe
+  lut4_rows_host(f.blob(e->dna_off, e->dna_len), cbuf.data(), cbuf.size(), dst.N, dst.K, mode, m->hd, words, lut);
+  CK(cudaMemcpy(dst.qs, words.data(), words.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(dst.lut, lut.data(), lut.size() * 4, cudaMemcpyHostToDevice));
+  if (dst.bias) {
+    std::vector<float> b(dst.N, 0.0f), perm(dst.N, 0.0f);
+    if (e->bias_len) memcpy(b.data(), f.blob(e->bias_off, e->bias_len), e->bias_len);
+    for (int r = 0; r < dst.N; ++r) perm[r] = b[repack_src_row(mode, r, m->hd, dst.N / 2)];
+    CK(cudaMemcpy(dst.bias, perm.data(), size_t(dst.N) * 4, cudaMemcpyHostToDevice));
+  }
+  return GAJE_OK;
+}
+
+int upload_matrix(gaje_model* m, const FlatFile& f, const MatrixRef& ref, Q4Dev& dst, uint32_t* staging, int mode) {
+  return ref.lut ? upload_lut4(m, f, ref, dst, mode) : upload_q4(m, f, ref, dst, staging, mode);
+}
+
 // Host libm RoPE table (attention.rs:62-84): freq = 1/powf(base, 2i/hd),
 // theta = pos*freq, (cosf, sinf) -- the same glibc calls Rust std makes.
 std::vector<float2> rope_table(int max_ctx, int hd, float base) {
@@ -778,6 +836,8 @@ bool plan_mega(gaje_model* m) {
   const int qd = m->nh * m->hd;
   const int xs = (std::max({m->d, qd, m->ff}) + 31) / 32 * 32;
   if (m->d > kMkMaxNormVec * kMkConsumers || qd != m->d) return false;
+  // the split combine keeps kMkCombineElems attention outputs per consumer thread
+  if (qd > kMkCombineElems * kMkConsumers) return false;
   MegaPlan& p = m->mplan;
   p.xs_floats = xs;
   if (m->nkv > m->sms) return false;  // one (head, split) unit per CTA at least
@@ -823,6 +883,10 @@ bool plan_mega(gaje_model* m) {
 
 // The two-exchange persistent kernel's plan (fused.cuh), from the shapes
 // alone; false when the model does not fit it (the five-exchange kernel runs).
+// Bytes of one Q8_0 lm_head row as the fused kernel streams it: int8 codes,
+// then the f16 scales of its 32-blocks, padded to 16 bytes (bulk copies).
+int q8_row_bytes(int d) { return (d + 2 * (d / 32) + 15) / 16 * 16; }
+
 bool plan_fused(gaje_model* m) {
   cudaFuncAttributes fa{};
   if (cudaFuncGetAttributes(&fa, k_decode_fused) != cudaSuccess) return false;
@@ -861,7 +925,8 @@ bool plan_fused(gaje_model* m) {
   if (base >= budget) return false;
   p.nslots = int(std::min<size_t>(kFuMaxSlots, (budget - base) / p.slot_bytes));
   if (p.nslots < 3) return false;
-  p.lm_stage_rows = int(std::min<size_t>(kFuConsumerWarps, p.slot_bytes / (size_t(d) * 4)));
+  m->lm_row_bytes = m->info.lm_head_bit_depth == 8 ? q8_row_bytes(d) : d * 4;
+  p.lm_stage_rows = int(std::min<size_t>(kFuConsumerWarps, p.slot_bytes / size_t(m->lm_row_bytes)));
   m->fused_smem = fused_smem_bytes(p, d, hd) + 128;
   return p.lm_stage_rows >= 1;
 }
@@ -1343,6 +1408,23 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   if ((I.embd_bit_depth != 32 && I.embd_bit_depth != 8) || (I.lm_head_bit_depth != 32 && I.lm_head_bit_depth != 8))
     return set_error(GAJE_ERR_UNSUPPORTED, "token_embd/lm_head must be f32 or Q8_0");
   if (I.n_embd % 32 != 0) return set_error(GAJE_ERR_UNSUPPORTED, "n_embd must be a multiple of 32");
+  // Genomic4Bit tables (init.rs:36-37) run on the kernel-per-phase engine,
+  // whose GEMV launches are planned once per matrix kind: a kind is a table
+  // in every block or in none
+  m->has_lut = false;
+  for (int k = 0; k < 4 && !f.blocks.empty(); ++k) {
+    auto pick = [k](const BlockRefs& b) { return k == 0 ? b.qkv.lut : k == 1 ? b.wo.lut : k == 2 ? b.gate_up.lut : b.down.lut; };
+    const bool first = pick(f.blocks[0]);
+    for (const BlockRefs& b : f.blocks)
+      if (pick(b) != first)
+        return set_error(GAJE_ERR_UNSUPPORTED, "a matrix kind mixes Genomic4Bit tables and Q4_0 blocks across blocks");
+    m->has_lut |= first;
+  }
+  if (m->has_lut && opts && (opts->max_streams > 0 || opts->max_prefill > 0))
+    return set_error(GAJE_ERR_UNSUPPORTED,
+                     "Genomic4Bit tables run on the single-stream engine only (max_streams and max_prefill must be 0)");
+  if (m->has_lut && m->nranks > 1)
+    return set_error(GAJE_ERR_UNSUPPORTED, "Genomic4Bit tables are not supported by the sharded engine");
   m->info = I;
   m->d = int(I.n_embd);
   m->nh = int(I.n_head);
@@ -1394,7 +1476,8 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
         q.nb = q.K / 32;
         q.nbp = (q.nb + 3) / 4 * 4;
         q.qs = a.take<uint4>(size_t(q.N) * q.nb);
-        q.sm = a.take<uint32_t>(size_t(q.N) * q.nbp);
+        q.sm = refs[k]->lut ? nullptr : a.take<uint32_t>(size_t(q.N) * q.nbp);
+        q.lut = refs[k]->lut ? a.take<float>(size_t(q.N) * q.nb * 16) : nullptr;
         q.bias = refs[k]->has_bias ? a.take<float>(q.N) : nullptr;
         size_t tot = 0;
         for (const FlatEntry* e : refs[k]->parts) tot += e->dna_len;
@@ -1441,6 +1524,7 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
       m->fyb = m->fya ? m->fya + 2 * d : nullptr;
       m->fwords_n = 2 * size_t(m->sms) + 2 * size_t(m->nkv) * m->hd + size_t(m->nh) * m->fplan.S * 2 + 1;
       m->fwords = a.take<uint2>(m->fwords_n);
+      m->lm_q8 = I.lm_head_bit_depth == 8 ? a.take<unsigned char>(size_t(m->Vl) * m->lm_row_bytes) : nullptr;
     }
     // LL exchange words of the persistent kernel, one contiguous range
     const size_t qd = size_t(m->nh) * m->hd, kvd = size_t(m->nkv) * m->hd;
@@ -1507,7 +1591,7 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   {
     Arena shapes;  // a first pass fills the matrix shapes the fused plan needs
     plan(shapes);
-    m->fu_ok = m->nranks == 1 && (!opts || opts->use_megakernel == 1) && plan_fused(m);
+    m->fu_ok = m->nranks == 1 && !m->has_lut && (!opts || opts->use_megakernel == 1) && plan_fused(m);
   }
   Arena sizing;
   plan(sizing);
@@ -1534,7 +1618,7 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   if (int s = smem_optin((const void*)k_gemv<G_DOWN>, m->pd.smem)) return s;
   if (int s = smem_optin((const void*)k_attn, m->attn_smem)) return s;
   if (int s = smem_optin((const void*)k_lmhead, m->lm_smem)) return s;
-  m->use_mega = m->nranks == 1 && (!opts || opts->use_megakernel) && plan_mega(m);
+  m->use_mega = m->nranks == 1 && !m->has_lut && (!opts || opts->use_megakernel) && plan_mega(m);
   if (m->fu_ok) {
     if (int s = smem_optin((const void*)k_decode_fused, m->fused_smem)) return s;
     int per_sm = 0, coop = 0;
@@ -1577,10 +1661,10 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   const int qkv_mode = I.rope_split ? 1 : 2;
   for (size_t l = 0; l < L; ++l) {
     const BlockRefs& b = f.blocks[l];
-    if (int s = upload_q4(m, f, b.qkv, m->qkv[l], staging, qkv_mode)) return s;
-    if (int s = upload_q4(m, f, b.wo, m->wo[l], staging, 0)) return s;
-    if (int s = upload_q4(m, f, b.gate_up, m->gate_up[l], staging, 3)) return s;
-    if (int s = upload_q4(m, f, b.down, m->down[l], staging, 0)) return s;
+    if (int s = upload_matrix(m, f, b.qkv, m->qkv[l], staging, qkv_mode)) return s;
+    if (int s = upload_matrix(m, f, b.wo, m->wo[l], staging, 0)) return s;
+    if (int s = upload_matrix(m, f, b.gate_up, m->gate_up[l], staging, 3)) return s;
+    if (int s = upload_matrix(m, f, b.down, m->down[l], staging, 0)) return s;
     CK(cudaMemcpy(m->attn_norm[l], f.blob(b.attn_norm->dna_off, d * 4), d * 4, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(m->ffn_norm[l], f.blob(b.ffn_norm->dna_off, d * 4), d * 4, cudaMemcpyHostToDevice));
   }
@@ -1610,6 +1694,21 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   };
   if (int s = upload_rows(f.token_embd, 0, V, m->embd)) return s;
   if (int s = upload_rows(f.lm_head, size_t(m->v0), size_t(m->Vl), m->lm_head)) return s;  // this rank's rows
+  if (m->lm_q8) {  // the fused kernel's Q8_0 rows: int8 codes of the row, then its f16 scales
+    const size_t nb = d / 32, rb = size_t(m->lm_row_bytes), nr = size_t(m->Vl);
+    const uint8_t* src = f.blob(f.lm_head->dna_off + size_t(m->v0) * nb * 34, nr * nb * 34);
+    if (!src) return set_error(GAJE_ERR_IO, "Q8_0 rows out of range");
+    std::vector<uint8_t> host(nr * rb, 0);
+#pragma omp parallel for schedule(static)
+    for (long long r = 0; r < (long long)nr; ++r)
+      for (size_t b = 0; b < nb; ++b) {
+        const uint8_t* blk = src + (size_t(r) * nb + b) * 34;
+        uint8_t* row = host.data() + size_t(r) * rb;
+        memcpy(row + b * 32, blk + 2, 32);
+        memcpy(row + d + 2 * b, blk, 2);
+      }
+    CK(cudaMemcpy(m->lm_q8, host.data(), host.size(), cudaMemcpyHostToDevice));
+  }
   if (m->lm_bias) {
     std::vector<float> b(V, 0.0f);
     memcpy(b.data(), f.blob(f.lm_head->bias_off, f.lm_head->bias_len), f.lm_head->bias_len);
@@ -1659,6 +1758,8 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   P.lm_head = m->lm_head;
   P.lm_bias = m->lm_bias;
   P.lm_flush = I.lm_head_bit_depth == 8 ? 1 : 0;
+  P.lm_q8 = m->lm_q8;
+  P.lm_row_bytes = m->lm_q8 ? m->lm_row_bytes : int(d) * 4;
   P.out_norm = m->out_norm;
   P.rope = m->rope;
   P.x = m->x;
@@ -2416,6 +2517,56 @@ gaje_q4_matrix* gaje_cuda_q4_0_upload(const uint8_t* blocks, size_t N, size_t K,
   return h.release();
 }
 
+gaje_q4_matrix* gaje_cuda_lut4_upload(const uint8_t* nibbles, const float* centroids, size_t n_centroids, size_t N,
+                                      size_t K, const float* bias, int device) {
+  if (!nibbles || !centroids || !N || !K || K % 32 || N > 0x7FFFFFFF || K > 0x7FFFFFFF) {
+    set_error(GAJE_ERR_INVALID, "nibbles / centroids must be non-NULL with K a multiple of 32");
+    return nullptr;
+  }
+  const size_t nb = K / 32;
+  if (n_centroids != 16 && n_centroids != nb * 16 && n_centroids != N * nb * 16) {
+    set_error(GAJE_ERR_SHAPE, "unsupported centroid count (16, K/32*16 or N*K/32*16)");
+    return nullptr;
+  }
+  if (cudaSetDevice(device) != cudaSuccess) {
+    set_error(GAJE_ERR_CUDA, "cudaSetDevice failed");
+    return nullptr;
+  }
+  std::unique_ptr<gaje_q4_matrix> h(new gaje_q4_matrix());
+  h->device = device;
+  auto carve = [&](Arena& ar) {
+    h->m.qs = ar.take<uint4>(N * nb);
+    h->m.lut = ar.take<float>(N * nb * 16);
+    h->m.bias = bias ? ar.take<float>(N) : nullptr;
+  };
+  Arena a;
+  carve(a);
+  if (cudaMalloc(&h->mem, a.used) != cudaSuccess) {
+    set_error(GAJE_ERR_CUDA, "cudaMalloc failed");
+    return nullptr;
+  }
+  Arena b;
+  b.base = static_cast<char*>(h->mem);
+  carve(b);
+  h->m.sm = nullptr;
+  h->m.N = int(N);
+  h->m.K = int(K);
+  h->m.nb = int(nb);
+  h->m.nbp = int((nb + 3) / 4 * 4);
+  std::vector<uint32_t> words;
+  std::vector<float> lut;
+  lut4_rows_host(nibbles, centroids, n_centroids, int(N), int(K), 0, 0, words, lut);
+  if (cudaMemcpy(h->m.qs, words.data(), words.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      cudaMemcpy(h->m.lut, lut.data(), lut.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+      (bias && cudaMemcpy(h->m.bias, bias, N * 4, cudaMemcpyHostToDevice) != cudaSuccess)) {
+    cudaFree(h->mem);
+    set_error(GAJE_ERR_CUDA, "upload failed");
+    return nullptr;
+  }
+  clear_error();
+  return h.release();
+}
+
 void gaje_cuda_q4_0_release(gaje_q4_matrix* h) {
   if (!h) return;
   cudaSetDevice(h->device);
@@ -2429,7 +2580,7 @@ int gaje_cuda_q4_0_gemv(const gaje_q4_matrix* h, const float* x, float* y, size_
   if (M > 65535) return set_error(GAJE_ERR_INVALID, "M above 65535");
   CK(cudaSetDevice(h->device));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (M == 1) {  // the decode kernel itself (staged rows, one CTA per SM)
+  if (M == 1 || h->m.lut) {  // the decode kernel itself (staged rows); a Genomic4Bit table: once per vector
     char* ws;
     if (int st = ws_get(h->device, kWsAttnBase, &ws)) return st;
     GemvPlan p = plan_gemv(G_PLAIN, h->m, h->m.N, sm_count(h->device));
@@ -2437,8 +2588,10 @@ int gaje_cuda_q4_0_gemv(const gaje_q4_matrix* h, const float* x, float* y, size_
     StepParams P{};
     P.st = reinterpret_cast<DevState*>(ws);
     LayerW L{};
-    GemvArgs a{h->m.view(), p.units, p.upc, x, y, 0};
-    CK(launch_k(k_gemv<G_PLAIN>, dim3(p.grid), dim3(kGemvThreads), p.smem, s, false, P, L, a));
+    for (size_t i = 0; i < M; ++i) {
+      GemvArgs a{h->m.view(), p.units, p.upc, x + i * size_t(h->m.K), y + i * size_t(h->m.N), 0};
+      CK(launch_k(k_gemv<G_PLAIN>, dim3(p.grid), dim3(kGemvThreads), p.smem, s, false, P, L, a));
+    }
     return GAJE_OK;
   }
   if (reinterpret_cast<uintptr_t>(x) & 15u) return set_error(GAJE_ERR_INVALID, "x must be 16-byte aligned");
@@ -2624,6 +2777,46 @@ int gaje_cuda_attention_decode_static(const float* q, const float* k_cache, cons
   CK(launch_k(k_attn, dim3(unsigned(n_head_kv), kAttnMaxSplits), dim3(kAttnThreads), smem, (cudaStream_t)stream,
               false, a));
   return GAJE_OK;
+}
+
+// ---- quantisers on the device (quant.cuh)
+static int quantize_device(const float* w, size_t n, uint8_t* out, void* stream, bool q8) {
+  if (!w || !out) return set_error(GAJE_ERR_INVALID, "NULL pointer");
+  if (n % 32) return set_error(GAJE_ERR_INVALID, "Weights length must be divisible by 32");
+  if ((uintptr_t)w & 15u) return set_error(GAJE_ERR_INVALID, "w must be 16-byte aligned");
+  if ((uintptr_t)out & (q8 ? 1u : 3u))
+    return set_error(GAJE_ERR_INVALID, q8 ? "out must be 2-byte aligned" : "out must be 4-byte aligned");
+  const size_t nblocks = n / 32;
+  if (!nblocks) return GAJE_OK;
+  int dev;
+  CK(cudaGetDevice(&dev));
+  const size_t tiles = (nblocks + kQuantThreads - 1) / kQuantThreads;
+  const unsigned grid = unsigned(std::min<size_t>(tiles, size_t(sm_count(dev)) * 6));
+  if (q8)
+    k_quantize_q8_0<<<grid, kQuantThreads, 0, (cudaStream_t)stream>>>(w, nblocks, out);
+  else
+    k_quantize_q4_0<<<grid, kQuantThreads, 0, (cudaStream_t)stream>>>(w, nblocks, out);
+  CK(cudaGetLastError());
+  return GAJE_OK;
+}
+
+int gaje_cuda_sample_top_p(const float* logits, size_t n, float temperature, float top_p, float r, uint32_t* token,
+                           uint32_t* kept, void* stream) {
+  if (!logits || !token) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  if (n > (size_t(1) << 23)) return set_error(GAJE_ERR_INVALID, "n above 2^23");
+  if (!(temperature > 0.0f) || !(r >= 0.0f && r < 1.0f) || top_p != top_p)
+    return set_error(GAJE_ERR_INVALID, "temperature must be > 0, r in [0, 1), top_p a number");
+  k_sample_top_p<<<1, kSampleThreads, 0, (cudaStream_t)stream>>>(logits, int(n), temperature, top_p, r, token, kept);
+  CK(cudaGetLastError());
+  return GAJE_OK;
+}
+
+int gaje_cuda_quantize_q4_0(const float* w, size_t n, uint8_t* out, void* stream) {
+  return quantize_device(w, n, out, stream, false);
+}
+
+int gaje_cuda_quantize_q8_0(const float* w, size_t n, uint8_t* out, void* stream) {
+  return quantize_device(w, n, out, stream, true);
 }
 
 int gaje_cuda_kwta(float* scores, size_t n, size_t k, void* stream) {

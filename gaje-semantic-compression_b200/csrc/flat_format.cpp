@@ -514,11 +514,25 @@ int FlatFile::resolve(std::string& err) {
     }
     if (matrix) {
       int bits = int(e->bit_depth);
-      if (bits == 4 && e->c_len != 0) {
-        err = "tensor '" + e->name + "' is a 16-centroid Genomic4Bit table (not implemented)";
-        return GAJE_ERR_UNSUPPORTED;
-      }
-      if (bits != 4 && bits != 8 && bits != 32) {
+      if (bits == 4 && e->c_len != 0) {  // Genomic4Bit: nibbles + 16-centroid tables (init.rs:29-38, 109-124)
+        const uint64_t nb = e->in / 32;
+        if (e->in % 32 != 0) {
+          err = "tensor '" + e->name + "': in_features is not a multiple of 32";
+          return GAJE_ERR_SHAPE;
+        }
+        if (e->dna_len != e->out * e->in / 2) {
+          err = "tensor '" + e->name + "': dna_len does not match out_features x in_features / 2";
+          return GAJE_ERR_SHAPE;
+        }
+        if (e->c_len != 64 && e->c_len != nb * 64 && e->c_len != e->out * nb * 64) {
+          err = "unsupported centroid count for " + e->name;
+          return GAJE_ERR_SHAPE;
+        }
+        if (e->bias_len % 4 != 0 || e->bias_len > e->out * 4) {
+          err = "tensor '" + e->name + "': bias_len is not a multiple of 4 up to out_features";
+          return GAJE_ERR_SHAPE;
+        }
+      } else if (bits != 4 && bits != 8 && bits != 32) {
         err = "tensor '" + e->name + "' has unsupported bit_depth " + std::to_string(bits);
         return GAJE_ERR_UNSUPPORTED;
       }
@@ -526,7 +540,7 @@ int FlatFile::resolve(std::string& err) {
         err = "tensor '" + e->name + "': in_features is not a multiple of 32";
         return GAJE_ERR_SHAPE;
       }
-      if (e->dna_len != data_bytes(bits, e->out, e->in)) {
+      if (!(bits == 4 && e->c_len != 0) && e->dna_len != data_bytes(bits, e->out, e->in)) {
         err = "tensor '" + e->name + "': dna_len does not match out_features x in_features";
         return GAJE_ERR_SHAPE;
       }
@@ -548,11 +562,14 @@ int FlatFile::resolve(std::string& err) {
       const FlatEntry* e;
       if (int s = need(n, e)) return s;
       if (int s = check_entry(e, true)) return s;
-      if (!m.parts.empty() && (int(e->bit_depth) != m.bit_depth || e->in != m.in)) {
+      const bool lut = e->bit_depth == 4 && e->c_len != 0;
+      if (!m.parts.empty() && (int(e->bit_depth) != m.bit_depth || e->in != m.in || lut || m.lut)) {
         err = "unfused tensors '" + names[0] + "' and '" + n + "' differ in format or in_features";
+        if (lut || m.lut) err = "unfused q/k/v or gate/up tensors must not be Genomic4Bit tables ('" + n + "')";
         return GAJE_ERR_UNSUPPORTED;
       }
       m.parts.push_back(e);
+      m.lut = lut;
       m.bit_depth = int(e->bit_depth);
       m.in = e->in;
       m.out += e->out;

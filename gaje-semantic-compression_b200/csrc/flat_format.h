@@ -26,7 +26,8 @@ struct FlatEntry {
 struct MatrixRef {
   std::vector<const FlatEntry*> parts;
   uint64_t out = 0, in = 0;
-  int bit_depth = 0;  // 4 (Q4_0), 8 (Q8_0), 32 (f32)
+  int bit_depth = 0;  // 4 (Q4_0, or Genomic4Bit with lut), 8 (Q8_0), 32 (f32)
+  bool lut = false;   // Genomic4Bit: nibbles (high nibble first) + 16-centroid tables
   bool has_bias = false;
 };
 

@@ -43,7 +43,8 @@
 // producer, 1-D TMA bulk copies, full/empty mbarriers) in this CTA's item
 // order: per block its q (or k/v) rows, its attn_output column blocks, then
 // per ffn K-block its gate/up rows and its ffn_down column block; then its
-// lm_head rows.  attn_output and ffn_down are kept a second time K-block
+// lm_head rows (f32, or for a Q8_0 lm_head the int8 codes and f16 scales of
+// each row, dequantised in the dot: 3.7x fewer bytes than the f32 rows).  attn_output and ffn_down are kept a second time K-block
 // major (qsT[kb][row]) so that a CTA's columns are one contiguous run.  The
 // cached K/V rows of a split are fetched by TMA while the CTA waits for its
 // input.  Every wait is bounded (kWaitNs) and reported as DevState::err.
@@ -362,8 +363,8 @@ __device__ void fu_producer(const FusedArgs& A, const FuShared& S) {
         } else {
           const int r = rbeg + i * pl.lm_stage_rows;
           if (r >= rend) break;
-          it.a = P.lm_head + (size_t)r * P.d;
-          it.na = uint32_t(min(pl.lm_stage_rows, rend - r)) * P.d * 4;
+          it.a = P.lm_q8 ? (const void*)(P.lm_q8 + (size_t)r * P.lm_row_bytes) : (const void*)(P.lm_head + (size_t)r * P.d);
+          it.na = uint32_t(min(pl.lm_stage_rows, rend - r)) * uint32_t(P.lm_row_bytes);
         }
         const int slot = item % pl.nslots;
         if (item >= pl.nslots && !mbar_wait(S.empty + slot, ((item / pl.nslots) - 1) & 1)) {
@@ -610,7 +611,11 @@ __device__ __forceinline__ int fu_attend_warp(const FusedArgs& A, const FuShared
     return -1;
   }
   __syncwarp();
-  if (lane == 0) *S.kv_waited = use + 1;
+  if (lane == 0) {
+    *S.kv_waited = use + 1;
+    if (A.trace)  // trace point 4: this split's K/V rows landed
+      A.trace[(((size_t)blockIdx.x * A.n_steps + step) * (L + 1) + l) * kFuTrace + 4] = global_ns();
+  }
   float q[VEC];
 #pragma unroll
   for (int v = 0; v < VEC; ++v) q[v] = S.qbuf[lane + 32 * v];
@@ -765,15 +770,34 @@ __device__ __forceinline__ bool fu_lm(const FusedArgs& A, const FuShared& S, int
       ++cur;
       slot = fu_wait_slot(A, S, item + cur);
     }
-    const float4* w4 = reinterpret_cast<const float4*>(slot) + (size_t)(k - it * pl.lm_stage_rows) * K4;
+    const unsigned char* rowp = slot + (size_t)(k - it * pl.lm_stage_rows) * P.lm_row_bytes;
     float a0 = 0.f, a1 = 0.f;
+    if (P.lm_q8) {
+      // Q8_0 row: element e is int8 q[e] times the f16 scale of its 32-block,
+      // the f32 value q * scale of blocks.rs:44-48 (exact), in the f32 path's
+      // order, so the logits equal those of the dequantised rows
+      const uint32_t* q4w = reinterpret_cast<const uint32_t*>(rowp);
+      const __half* sc = reinterpret_cast<const __half*>(rowp + d);
 #pragma unroll 2
-    for (int j = lane; j < K4; j += 32) {
-      const float4 u = w4[j], xv = x4[j];
-      a0 = fmaf(u.x, xv.x, a0);
-      a1 = fmaf(u.y, xv.y, a1);
-      a0 = fmaf(u.z, xv.z, a0);
-      a1 = fmaf(u.w, xv.w, a1);
+      for (int j = lane; j < K4; j += 32) {
+        const uint32_t w = q4w[j];
+        const float s = __half2float(sc[j >> 3]);
+        const float4 xv = x4[j];
+        a0 = fmaf(__fmul_rn(float(int8_t(w & 0xFFu)), s), xv.x, a0);
+        a1 = fmaf(__fmul_rn(float(int8_t((w >> 8) & 0xFFu)), s), xv.y, a1);
+        a0 = fmaf(__fmul_rn(float(int8_t((w >> 16) & 0xFFu)), s), xv.z, a0);
+        a1 = fmaf(__fmul_rn(float(int8_t(w >> 24)), s), xv.w, a1);
+      }
+    } else {
+      const float4* w4 = reinterpret_cast<const float4*>(rowp);
+#pragma unroll 2
+      for (int j = lane; j < K4; j += 32) {
+        const float4 u = w4[j], xv = x4[j];
+        a0 = fmaf(u.x, xv.x, a0);
+        a1 = fmaf(u.y, xv.y, a1);
+        a0 = fmaf(u.z, xv.z, a0);
+        a1 = fmaf(u.w, xv.w, a1);
+      }
     }
     const int row = rbeg + k;
     float v = warp_sum(a0 + a1) * scale;

@@ -91,6 +91,10 @@ struct Q4View {
   const uint32_t* sm;
   const float* bias;  // [N] or nullptr
   int N, K, nb, nbp;
+  // Genomic4Bit (genomic.rs:149-204): 16 f32 centroids per (row, block)
+  // [N][nb][16]; qs then holds the codes (element 2k in the low nibble of
+  // byte k, as for Q4_0) and sm is unused.  nullptr for Q4_0.
+  const float* lut;
 };
 
 struct LayerW {
@@ -109,6 +113,8 @@ struct StepParams {
   const float* lm_head;  // f32 [V][d]
   const float* lm_bias;  // [V] or nullptr
   int lm_flush;          // 1: the |t| < 1e-6 -> 0 flush of a Q8_0 lm_head row dot (genomic.rs:444-448)
+  const unsigned char* lm_q8;  // Q8_0 lm_head rows [V][lm_row_bytes] (int8[d], f16[d/32], pad) or nullptr
+  int lm_row_bytes;      // bytes of one streamed lm_head row: d*4 (f32) or the Q8_0 row above
   const float* out_norm;
   const float2* rope;    // [max_ctx][hd/2] (cos, sin) from host libm
   float* x;              // residual stream [d]
@@ -285,6 +291,22 @@ __device__ __forceinline__ float q4_row_smem(const uint4* qs_row, const uint32_t
   return flush_small(warp_sum(acc));
 }
 
+// Genomic4Bit row dot (genomic.rs:149-204: sum of c[code] * x, each product
+// rounded then added, |t| < 1e-6 flushed) from staged codes and centroid
+// tables: lane l takes element l of every block, so the 32 lanes read one
+// block's 64-byte table (no bank conflicts) and its 32 consecutive x.
+__device__ __forceinline__ float lut4_row_smem(const uint4* qs_row, const float* lut_row, int nb, const float* xs,
+                                              int lane) {
+  const unsigned char* codes = reinterpret_cast<const unsigned char*>(qs_row);
+  float acc = 0.f;
+#pragma unroll 4
+  for (int b = 0; b < nb; ++b) {
+    const unsigned code = (codes[b * 16 + (lane >> 1)] >> ((lane & 1) * 4)) & 0xFu;
+    acc = __fadd_rn(acc, __fmul_rn(lut_row[b * 16 + code], xs[swz((b << 5) + lane)]));
+  }
+  return flush_small(warp_sum(acc));
+}
+
 // Row dot straight from global memory (op-level M > 1 path).
 __device__ __forceinline__ float q4_row_global(const Q4View& W, int row, const float* xs, int lane) {
   const uint4* qs = W.qs + (size_t)row * W.nb;
@@ -328,10 +350,11 @@ struct GemvArgs {
 
 __host__ __device__ constexpr int gemv_rows_per_unit(int mode) { return (mode == G_QKV || mode == G_GATEUP) ? 2 : 1; }
 
-// Dynamic shared memory of a GEMV CTA: header + x (K floats) + staged rows.
-__host__ __device__ inline size_t gemv_smem_bytes(int mode, int K, int nb, int nbp, int upc) {
+// Dynamic shared memory of a GEMV CTA: header + x (K floats) + staged rows
+// (Q4_0 codes and scale/min words, or Genomic4Bit codes and centroid tables).
+__host__ __device__ inline size_t gemv_smem_bytes(int mode, int K, int nb, int nbp, int upc, bool lut = false) {
   const size_t rows = size_t(upc) * gemv_rows_per_unit(mode);
-  return kSmemHeader + size_t(K) * 4 + rows * nb * 16 + rows * nbp * 4;
+  return kSmemHeader + size_t(K) * 4 + rows * nb * 16 + (lut ? rows * nb * 64 : rows * nbp * 4);
 }
 
 // One CTA owns units [u0, u1) = a contiguous row range of the (pair-
@@ -350,6 +373,7 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(StepParams P, LayerW L, G
   const int u1 = min(A.units, u0 + A.upc);
   const int r0 = u0 * RPU, nrows = (u1 - u0) * RPU;
   uint32_t* sm_s = reinterpret_cast<uint32_t*>(qs_s + (size_t)A.upc * RPU * nb);
+  float* lut_s = reinterpret_cast<float*>(sm_s);  // Genomic4Bit: the centroid tables in place of sm
 
   // 1. stage this CTA's weight rows (independent of the previous kernel)
   if (threadIdx.x == 0) {
@@ -358,10 +382,12 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(StepParams P, LayerW L, G
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    const uint32_t qb = uint32_t(nrows) * nb * 16, sb = uint32_t(nrows) * nbp * 4;
+    const uint32_t qb = uint32_t(nrows) * nb * 16;
+    const uint32_t sb = W.lut ? uint32_t(nrows) * nb * 64 : uint32_t(nrows) * nbp * 4;
     mbar_expect_tx(bar, qb + sb);
     bulk_g2s(qs_s, W.qs + (size_t)r0 * nb, qb, bar);
-    bulk_g2s(sm_s, W.sm + (size_t)r0 * nbp, sb, bar);
+    if (W.lut) bulk_g2s(lut_s, W.lut + (size_t)r0 * nb * 16, sb, bar);
+    else bulk_g2s(sm_s, W.sm + (size_t)r0 * nbp, sb, bar);
   }
   // 2. wait for the previous kernel, release the next one
   pdl_wait();
@@ -436,7 +462,8 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(StepParams P, LayerW L, G
   for (int u = u0 + wid; u < u1; u += nwarps) {
     const int lr = (u - u0) * RPU;
     if (RPU == 1) {
-      float y = q4_row_smem(qs_s + (size_t)lr * nb, sm_s + (size_t)lr * nbp, nb, xs, lane);
+      float y = W.lut ? lut4_row_smem(qs_s + (size_t)lr * nb, lut_s + (size_t)lr * nb * 16, nb, xs, lane)
+                      : q4_row_smem(qs_s + (size_t)lr * nb, sm_s + (size_t)lr * nbp, nb, xs, lane);
       if (lane == 0) {
         const int r = r0 + lr;
         if (W.bias) y += W.bias[r];
@@ -452,8 +479,14 @@ __global__ void __launch_bounds__(kGemvThreads) k_gemv(StepParams P, LayerW L, G
         }
       }
     } else {
-      float y0 = q4_row_smem(qs_s + (size_t)lr * nb, sm_s + (size_t)lr * nbp, nb, xs, lane);
-      float y1 = q4_row_smem(qs_s + (size_t)(lr + 1) * nb, sm_s + (size_t)(lr + 1) * nbp, nb, xs, lane);
+      float y0, y1;
+      if (W.lut) {
+        y0 = lut4_row_smem(qs_s + (size_t)lr * nb, lut_s + (size_t)lr * nb * 16, nb, xs, lane);
+        y1 = lut4_row_smem(qs_s + (size_t)(lr + 1) * nb, lut_s + (size_t)(lr + 1) * nb * 16, nb, xs, lane);
+      } else {
+        y0 = q4_row_smem(qs_s + (size_t)lr * nb, sm_s + (size_t)lr * nbp, nb, xs, lane);
+        y1 = q4_row_smem(qs_s + (size_t)(lr + 1) * nb, sm_s + (size_t)(lr + 1) * nbp, nb, xs, lane);
+      }
       if (lane == 0) {
         if (W.bias) {
           y0 += W.bias[r0 + lr];
@@ -971,6 +1004,7 @@ __global__ void k_repack_q4(const uint32_t* __restrict__ raw, int N, int nb, int
 }
 
 // Bit-exact dequantisation: w = fmaf(q, scale, min) (genomic.rs:298).
+// Genomic4Bit: w = c[code] (get_row_core, linear/forward.rs:195-285).
 __global__ void k_dequant_q4(Q4View W, float* out) {
   const size_t total = (size_t)W.N * W.K;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
@@ -978,11 +1012,15 @@ __global__ void k_dequant_q4(Q4View W, float* out) {
     const int col = (int)(i - row * W.K);
     const int b = col >> 5, e = col & 31;
     const uint4 q = W.qs[row * W.nb + b];
-    float scale, mn;
-    unpack_sm(W.sm[row * W.nbp + b], scale, mn);
     const uint32_t word = (e < 8) ? q.x : (e < 16) ? q.y : (e < 24) ? q.z : q.w;
     const int byte = (e & 7) >> 1;
     const uint32_t code = (word >> (8 * byte + 4 * (e & 1))) & 0xFu;
+    if (W.lut) {
+      out[i] = W.lut[(row * W.nb + b) * 16 + code];
+      continue;
+    }
+    float scale, mn;
+    unpack_sm(W.sm[row * W.nbp + b], scale, mn);
     out[i] = fmaf((float)code, scale, mn);
   }
 }

@@ -73,6 +73,7 @@ constexpr int kMkRound = 12;          // LL words per consumer thread per read r
 constexpr int kMkMaxNormVec = 4;      // norm weights per thread (d <= 1920)
 constexpr int kMkMinChunk = 64;       // positions per attention split (minimum)
 constexpr int kMkCombine = 4;         // attention splits combined per read round
+constexpr int kMkCombineElems = 2;    // attention outputs one consumer thread combines (n_head*head_dim <= 960)
 // Trace points of a phase, per CTA: 0 entry, 1 input flags seen, 2 input
 // staged (attention: cached K/V landed), 3 rows done (attention: scores
 // done), 4 outputs published, 5 first weight slot ready.
@@ -803,8 +804,9 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
         // across splits): weights exp(m_s - M), out = O / (L + 1e-12).  Per
         // round of kMkCombine splits every word is requested at once: the
         // (m, l) pairs by one thread each into shared memory, the o words of
-        // this thread's elements (at most two: qd <= 960) into registers.
-        constexpr int kE = 2;
+        // this thread's elements (at most kMkCombineElems; plan_mega rejects
+        // larger n_head * head_dim) into registers.
+        constexpr int kE = kMkCombineElems;
         float M[kE], O[kE], Ls[kE];
         const uint2* ob[kE];
 #pragma unroll

@@ -150,12 +150,16 @@ def lib() -> C.CDLL:
         "gaje_cuda_stream_len": ([vp, u32, vp], i32),
         "gaje_cuda_q4_0_upload": ([vp, sz, sz, vp, i32], vp),
         "gaje_cuda_q4_0_release": ([vp], None),
+        "gaje_cuda_lut4_upload": ([vp, vp, sz, sz, sz, vp, i32], vp),
         "gaje_cuda_q4_0_gemv": ([vp, vp, vp, sz, vp], i32),
         "gaje_cuda_q4_0_dequant": ([vp, vp, vp], i32),
         "gaje_cuda_f32_gemv_argmax": ([vp, vp, sz, sz, vp, vp, vp], i32),
         "gaje_cuda_rms_norm": ([vp, vp, f32, sz, vp, vp], i32),
         "gaje_cuda_attention_decode": ([vp, vp, vp, sz, sz, sz, sz, sz, vp, vp], i32),
         "gaje_cuda_kwta": ([vp, sz, sz, vp], i32),
+        "gaje_cuda_sample_top_p": ([vp, sz, f32, f32, f32, vp, vp, vp], i32),
+        "gaje_cuda_quantize_q4_0": ([vp, sz, vp, vp], i32),
+        "gaje_cuda_quantize_q8_0": ([vp, sz, vp, vp], i32),
         "gaje_cuda_nccl_unique_id": ([vp], i32),
         "gaje_cuda_load_sharded": ([C.c_char_p, C.POINTER(LoadOpts), i32, i32, vp], vp),
         "gaje_vocab_shard": ([u32, i32, i32, C.POINTER(u32), C.POINTER(u32)], i32),
@@ -549,6 +553,24 @@ class Q4Matrix:
         if not self._h:
             raise GajeValueError(1, last_error())
 
+    @classmethod
+    def from_lut4(cls, nibbles: np.ndarray, centroids: np.ndarray, N: int, K: int,
+                  bias: Optional[np.ndarray] = None, device: int = 0) -> "Q4Matrix":
+        """A Genomic4Bit matrix: nibbles [N*K/2] (high nibble first) and a
+        centroid table of 16, K/32*16 or N*K/32*16 floats."""
+        nib = np.ascontiguousarray(nibbles, dtype=np.uint8)
+        cen = np.ascontiguousarray(centroids, dtype=np.float32)
+        if nib.size != N * K // 2:
+            raise ValueError("nibbles size does not match N x K")
+        bias_a = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+        self = cls.__new__(cls)
+        self.N, self.K = N, K
+        self._h = lib().gaje_cuda_lut4_upload(_ptr(nib), _ptr(cen), cen.size, N, K,
+                                              None if bias_a is None else _ptr(bias_a), device)
+        if not self._h:
+            raise GajeValueError(1, last_error())
+        return self
+
     def __del__(self):
         if getattr(self, "_h", None):
             lib().gaje_cuda_q4_0_release(self._h)
@@ -578,3 +600,21 @@ def attention_decode(q_ptr: int, k_ptr: int, v_ptr: int, ctx: int, cache_stride:
 
 def kwta(scores_ptr: int, n: int, k: int, stream: int = 0) -> None:
     _check(lib().gaje_cuda_kwta(scores_ptr, n, k, stream or None))
+
+
+def quantize_q4_0_device(w_ptr: int, n: int, out_ptr: int, stream: int = 0) -> None:
+    """quantize_q4_0_native on the device: n f32 at w_ptr -> n/32 20-byte blocks at out_ptr."""
+    _check(lib().gaje_cuda_quantize_q4_0(w_ptr, n, out_ptr, stream or None))
+
+
+def quantize_q8_0_device(w_ptr: int, n: int, out_ptr: int, stream: int = 0) -> None:
+    """The Q8_0 quantiser on the device: n f32 at w_ptr -> n/32 34-byte blocks at out_ptr."""
+    _check(lib().gaje_cuda_quantize_q8_0(w_ptr, n, out_ptr, stream or None))
+
+
+def sample_top_p(logits_ptr: int, n: int, temperature: float, top_p: float, r: float, token_ptr: int,
+                 kept_ptr: Optional[int] = None, stream: int = 0) -> None:
+    """sample_top_p (src/compute/sampling.rs:14-55) on the device with the
+    uniform draw r in [0, 1) given: the token into token_ptr (device u32)."""
+    _check(lib().gaje_cuda_sample_top_p(logits_ptr, n, float(temperature), float(top_p), float(r), token_ptr,
+                                        kept_ptr, stream or None))

@@ -369,6 +369,17 @@ void gaje_cuda_q4_0_release(gaje_q4_matrix* m);
  * compute_single_row's Q4_0 arm (src/nn/linear/forward.rs:84-92, 113-115). */
 int gaje_cuda_q4_0_gemv(const gaje_q4_matrix* m, const float* x, float* y, size_t M,
                         void* stream);
+/* A Genomic4Bit matrix (the 16-centroid LUT format; GenomicLinear::new,
+ * src/nn/linear/init.rs:29-38 and :109-124) uploaded for the op-level calls:
+ * nibbles (host, N*K/2 bytes, element 2k in the HIGH nibble of byte k, as
+ * genomize_4bit_core writes them) and centroids (host f32: 16 for the whole
+ * matrix, K/32*16 per block column, or N*K/32*16 per row block).  The handle
+ * works with gaje_cuda_q4_0_gemv (genomic_dot_product_4bit,
+ * src/compute/kernels/genomic.rs:149-204, then the |t| < 1e-6 flush and the
+ * bias; one launch per input vector), gaje_cuda_q4_0_dequant (w = c[code])
+ * and gaje_cuda_q4_0_release.  NULL on error. */
+gaje_q4_matrix* gaje_cuda_lut4_upload(const uint8_t* nibbles, const float* centroids, size_t n_centroids,
+                                      size_t N, size_t K, const float* bias, int device);
 /* Dequantised weights w[N][K] (device) with the AVX2 kernel's fused
  * fma(q, scale, min) (src/compute/kernels/genomic.rs:298). */
 int gaje_cuda_q4_0_dequant(const gaje_q4_matrix* m, float* w, void* stream);
@@ -429,6 +440,29 @@ int gaje_cuda_attention_decode_static(const float* q, const float* k_cache, cons
 /* lateral_inhibition_kwta (src/compute/kernels/lut.rs:45-61) in place on
  * scores[n] (device): values below the k-th largest become -1e9. */
 int gaje_cuda_kwta(float* scores, size_t n, size_t k, void* stream);
+
+/* sample_top_p_core (src/compute/sampling.rs:14-55) on the device: logits[n]
+ * (device) -> *token (device u32): p = exp((l - max) / temperature)
+ * normalised, sorted by descending p (equal p in index order), the nucleus
+ * cut after the first prefix whose sum exceeds top_p, then the first nucleus
+ * token whose running sum reaches r * (the nucleus' sum).  r in [0, 1) is the
+ * caller's uniform draw (the reference takes one from thread_rng, unseeded);
+ * *kept (device u32, nullable) receives the nucleus size.  Sums are exact
+ * (2^-40 fixed point), so the choice is deterministic; it can differ from the
+ * reference's f32 running sums only where r or top_p is within their rounding
+ * of a boundary.  One CTA, no scratch memory; n <= 2^23.  Asynchronous. */
+int gaje_cuda_sample_top_p(const float* logits, size_t n, float temperature, float top_p, float r,
+                           uint32_t* token, uint32_t* kept, void* stream);
+
+/* quantize_q4_0_native (src/compute/quantize/python.rs:152-232) on the device:
+ * w[n] (device f32, 16-byte aligned, n % 32 == 0) -> out (device, n/32 blocks
+ * of 20 bytes, 4-byte aligned), the same bytes gaje_quantize_q4_0 writes on
+ * the host.  Asynchronous on `stream`. */
+int gaje_cuda_quantize_q4_0(const float* w, size_t n, uint8_t* out, void* stream);
+/* The Q8_0 quantiser (python.rs, the 8-bit arm beside quantize_q4_0_native;
+ * blocks.rs:37-50) on the device: n/32 blocks of 34 bytes (out 2-byte
+ * aligned), the bytes of gaje_quantize_q8_0. */
+int gaje_cuda_quantize_q8_0(const float* w, size_t n, uint8_t* out, void* stream);
 
 #ifdef __cplusplus
 }

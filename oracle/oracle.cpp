@@ -998,6 +998,94 @@ struct or_model {
   std::string err;
 };
 
+// genomize_4bit_core (src/compute/quantize/genomize.rs:286-382) without
+// anchors: per block of 32, min / max by strict comparison from f32::MAX /
+// f32::MIN, step = (max - min) / 15, c[j] = min + j * step (two roundings),
+// each value to the first nearest centroid by |v - c[j]| < best; byte k
+// holds element 2k in its HIGH nibble.  nibbles[n/2], centroids[n/32 * 16].
+void or_genomize_4bit(const float* w, size_t n, uint8_t* nibbles, float* centroids) {
+  const long long nb = (long long)(n / 32);
+#pragma omp parallel for schedule(static)
+  for (long long i = 0; i < nb; ++i) {
+    const float* b = w + i * 32;
+    float mn = 3.40282347e+38f, mx = -3.40282347e+38f;
+    for (int k = 0; k < 32; ++k) {
+      if (b[k] < mn) mn = b[k];
+      if (b[k] > mx) mx = b[k];
+    }
+    volatile float range = mx - mn;
+    const float step = range / 15.0f;
+    float c[16];
+    for (int j = 0; j < 16; ++j) {
+      volatile float t = float(j) * step;
+      c[j] = mn + t;
+      centroids[i * 16 + j] = c[j];
+    }
+    for (int k = 0; k < 16; ++k) {
+      uint8_t byte = 0;
+      for (int s2 = 0; s2 < 2; ++s2) {
+        const float v = b[2 * k + s2];
+        int best = 0;
+        float md = 3.40282347e+38f;
+        for (int j = 0; j < 16; ++j) {
+          volatile float diff = v - c[j];
+          const float dist = std::fabs(diff);
+          if (dist < md) {
+            md = dist;
+            best = j;
+          }
+        }
+        byte |= s2 == 0 ? uint8_t(best << 4) : uint8_t(best);
+      }
+      nibbles[i * 16 + k] = byte;
+    }
+  }
+}
+
+// sample_top_p_core (src/compute/sampling.rs:14-55) with the uniform r in
+// [0, 1) passed in (the reference draws it from thread_rng): probabilities
+// exp((l - max) / T) summed in index order, normalised, stably sorted by
+// descending probability, cut after the first prefix whose running sum
+// exceeds top_p, then the first kept token whose running sum reaches
+// r * (sum of the kept probabilities); the largest-probability token when
+// none does.  Also returns the kept count through *kept.
+size_t or_sample_top_p(const float* logits, size_t n, float temperature, float top_p, float r, size_t* kept) {
+  if (kept) *kept = 0;
+  if (n == 0) return 0;
+  float mx = -INFINITY;
+  for (size_t i = 0; i < n; ++i) mx = std::fmax(mx, logits[i]);
+  std::vector<std::pair<size_t, float>> probs(n);
+  float sum_exp = 0.0f;
+  for (size_t i = 0; i < n; ++i) {
+    volatile float z = (logits[i] - mx) / temperature;
+    probs[i] = {i, std::exp(float(z))};
+  }
+  for (size_t i = 0; i < n; ++i) sum_exp += probs[i].second;
+  if (!(sum_exp > 0.0f)) return 0;
+  for (auto& p : probs) p.second /= sum_exp;
+  std::stable_sort(probs.begin(), probs.end(),
+                   [](const std::pair<size_t, float>& a, const std::pair<size_t, float>& b) { return a.second > b.second; });
+  float cum = 0.0f;
+  size_t cutoff = n;
+  for (size_t i = 0; i < n; ++i) {
+    cum += probs[i].second;
+    if (cum > top_p) {
+      cutoff = i + 1;
+      break;
+    }
+  }
+  if (kept) *kept = cutoff;
+  float final_sum = 0.0f;
+  for (size_t i = 0; i < cutoff; ++i) final_sum += probs[i].second;
+  const float target = r * final_sum;
+  float cur = 0.0f;
+  for (size_t i = 0; i < cutoff; ++i) {
+    cur += probs[i].second;
+    if (target <= cur) return probs[i].first;
+  }
+  return probs[0].first;
+}
+
 // The synthetic weights of the benchmark and test models, restated from the
 // product's description of its generator so that the CPU arm can write the
 // same `.gaje.flat` file without loading the product: key = splitmix64

@@ -79,6 +79,9 @@ def lib():
                               C.POINTER(C.c_size_t)]
     L.or_generate.restype = i32
     L.or_fill_normal.argtypes = [_f32p, sz, C.c_uint64, C.c_char_p, f32]
+    L.or_genomize_4bit.argtypes = [_f32p, sz, _u8p, _f32p]
+    L.or_sample_top_p.argtypes = [_f32p, sz, f32, f32, f32, C.POINTER(C.c_size_t)]
+    L.or_sample_top_p.restype = sz
     _lib = L
     return L
 
@@ -107,6 +110,33 @@ def quantize_q8_0(w: np.ndarray) -> np.ndarray:
     if lib().or_quantize_q8_0(w, w.size, out) != 0:
         raise ValueError("Weights length must be divisible by 32")
     return out
+
+
+def sample_top_p(logits, temperature: float, top_p: float, r: float):
+    """sample_top_p_core (src/compute/sampling.rs:14-55) with the uniform r
+    given: (token, number of tokens kept in the nucleus)."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    kept = C.c_size_t(0)
+    tok = lib().or_sample_top_p(lg, lg.size, float(temperature), float(top_p), float(r), C.byref(kept))
+    return int(tok), int(kept.value)
+
+
+def genomize_4bit(w: np.ndarray):
+    """genomize_4bit_core (src/compute/quantize/genomize.rs:286-382), no
+    anchors: (nibbles [n/2] high nibble first, centroids [n/32 * 16])."""
+    w = np.ascontiguousarray(w, dtype=np.float32).ravel()
+    if w.size % 32:
+        raise ValueError("length must be divisible by 32")
+    nib = np.zeros(w.size // 2, dtype=np.uint8)
+    cen = np.zeros(w.size // 32 * 16, dtype=np.float32)
+    lib().or_genomize_4bit(w, w.size, nib, cen)
+    return nib, cen
+
+
+def lut4_dot(nibbles, x, centroids, n_blocks: int) -> float:
+    """genomic_dot_product_4bit (genomic.rs:149-204) over one row."""
+    return float(lib().or_lut4_dot(np.ascontiguousarray(nibbles, np.uint8), np.ascontiguousarray(x, np.float32),
+                                   np.ascontiguousarray(centroids, np.float32), 16, int(n_blocks)))
 
 
 def q4_0_dequant(blocks: np.ndarray, fused: bool = True) -> np.ndarray:

@@ -57,6 +57,20 @@ def write_flat(path, *, name, arch_family, n_embd, n_head, n_head_kv, n_blocks, 
                                      "c_len": 0, "anc_off": 0, "anc_len": 0, "bias_off": 0,
                                      "bias_len": 0})
             continue
+        if t[0] == "lut4":  # Genomic4Bit: nibbles + a centroid table of 16, nb*16 or out*nb*16 floats
+            _, nm, out_f, in_f, nibbles, cents, bias = t
+            dna_off, dna_len = add_blob_data(np.asarray(nibbles, np.uint8).tobytes())
+            c_off, c_len = add_blob_data(np.asarray(cents, np.float32).tobytes())
+            anc_off, anc_len = add_blob_data(b"")
+            bias_off, bias_len = 0, 0
+            if bias is not None and len(bias) > 0:
+                bias_off, bias_len = add_blob_data(np.asarray(bias, np.float32).tobytes())
+            tensor_directory.append({"name": nm, "bit_depth": 4, "out_features": int(out_f),
+                                     "in_features": int(in_f), "dna_off": int(dna_off), "dna_len": int(dna_len),
+                                     "c_off": int(c_off), "c_len": int(c_len), "anc_off": int(anc_off),
+                                     "anc_len": int(anc_len), "bias_off": int(bias_off),
+                                     "bias_len": int(bias_len)})
+            continue
         _, nm, bits, W, bias = t
         W = np.ascontiguousarray(W, np.float32)
         if bits == 4:
@@ -121,6 +135,57 @@ def write_synthetic(path, *, seed, arch_family, n_embd, n_head, n_head_kv, n_blo
                     ("linear", p + "attn_output", 4, normal(d, qd, p + "attn_output"), None),
                     ("linear", p + "ffn_gate_up", 4, normal(2 * ff, d, p + "ffn_gate_up"), None),
                     ("linear", p + "ffn_down", 4, normal(d, ff, p + "ffn_down"), None)]
+    return write_flat(path, name=f"synthetic-family{arch_family}", arch_family=arch_family, n_embd=n_embd,
+                      n_head=n_head, n_head_kv=n_head_kv, n_blocks=n_blocks, vocab_size=vocab_size, eps=eps,
+                      rope_base=rope_base, qk_permute=1 if arch_family in (1, 2) else 0, tensors=tensors)
+
+
+def write_synthetic_lut4(path, *, seed, arch_family, n_embd, n_head, n_head_kv, n_blocks, ffn_dim, vocab_size, eps,
+                         rope_base, qkv_bias, std=0.02, lut_tensors=("attn_qkv", "attn_output", "ffn_gate_up",
+                                                                      "ffn_down"), centroid_layout="full"):
+    """A synthetic model whose listed body matrices are Genomic4Bit tables
+    (genomize_4bit_core of the same N(0, std) weights as write_synthetic) and
+    the rest Q4_0.  centroid_layout: "full" (out*nb*16 floats, the quantiser's
+    output), "column" (nb*16: the first row's tables shared by every row) or
+    "shared" (16: block 0's table for the whole matrix), the three layouts
+    GenomicLinear::new expands (src/nn/linear/init.rs:109-124); the nibbles are
+    re-chosen against the shared tables."""
+    d, hd = n_embd, n_embd // n_head
+    qd, kvd, ff, V = n_head * hd, n_head_kv * hd, ffn_dim, vocab_size
+
+    def normal(rows, cols, name):
+        return oracle.synthetic_normal(rows * cols, seed, name, std).reshape(rows, cols)
+
+    def lut(name, W, bias):
+        out_f, in_f = W.shape
+        nib, cen = oracle.genomize_4bit(W)
+        nb = in_f // 32
+        if centroid_layout != "full":
+            cen3 = cen.reshape(out_f, nb, 16)
+            table = cen3[0] if centroid_layout == "column" else cen3[0, 0]  # [nb, 16] or [16]
+            full = np.broadcast_to(table, (out_f, nb, 16))
+            wb = W.reshape(out_f, nb, 32)
+            idx = np.argmin(np.abs(wb[..., None] - full[:, :, None, :]), axis=-1).astype(np.uint8)
+            nib = ((idx[..., 0::2] << 4) | idx[..., 1::2]).reshape(-1)
+            cen = np.ascontiguousarray(table, np.float32).reshape(-1)
+        return ("lut4", name, out_f, in_f, nib, cen, bias)
+
+    def mat(name, W, bias=None):
+        short = name.split(".")[-1]
+        return lut(name, W, bias) if short in lut_tensors else ("linear", name, 4, W, bias)
+
+    ones = np.ones(d, np.float32)
+    emb = normal(V, d, "token_embd")
+    tensors = [("linear", "token_embd", 32, emb, None), ("norm", "output_norm", ones),
+               ("linear", "lm_head", 32, emb, None)]
+    for i in range(n_blocks):
+        p = f"blk.{i}."
+        bias = oracle.synthetic_normal(qd + 2 * kvd, seed, p + "attn_qkv.bias", std) if qkv_bias else None
+        tensors += [("norm", p + "attn_norm", ones), ("norm", p + "ffn_norm", ones),
+                    mat(p + "attn_qkv", normal(qd + 2 * kvd, d, p + "attn_qkv"), bias),
+                    mat(p + "attn_output", normal(d, qd, p + "attn_output")),
+                    mat(p + "ffn_gate_up", normal(2 * ff, d, p + "ffn_gate_up")),
+                    mat(p + "ffn_down", normal(d, ff, p + "ffn_down"))]
     return write_flat(path, name=f"synthetic-family{arch_family}", arch_family=arch_family, n_embd=n_embd,
                       n_head=n_head, n_head_kv=n_head_kv, n_blocks=n_blocks, vocab_size=vocab_size, eps=eps,
                       rope_base=rope_base, qk_permute=1 if arch_family in (1, 2) else 0, tensors=tensors)

@@ -201,7 +201,7 @@ def _set(name, key, val):
     ("in_features", "GAJE_ERR_SHAPE"),
     ("past_eof", "GAJE_ERR_IO"),
     ("anchors", "GAJE_ERR_UNSUPPORTED"),
-    ("centroids", "GAJE_ERR_UNSUPPORTED"),
+    ("centroids", "GAJE_ERR_SHAPE"),  # a Q4_0 block buffer is not Genomic4Bit nibbles
 ])
 def test_loader_errors_are_status_codes(g, tmp_path, case, status):
     def edit(raw):
@@ -278,3 +278,39 @@ def test_unfused_tensors_load(g, O, tmp_path):
     a, b = O.OracleModel(fused), O.OracleModel(unf)
     for tok in (3, 17, 5):
         assert np.array_equal(a.forward(tok), b.forward(tok))
+
+
+def test_lut4_files_resolve_and_engine_limits(g, tmp_path):
+    """Genomic4Bit body tensors (bit_depth 4 with a centroid blob) resolve; the
+    engine takes them on the single-stream path only, and a matrix kind must
+    be a table in every block or in none (checked before any CUDA call)."""
+    cfg = dict(g.configs.CONFIGS["tiny"])
+    path = str(tmp_path / "lut.flat")
+    flat_numpy.write_synthetic_lut4(path, seed=2, **cfg)
+    info = g.inspect_flat(path)
+    assert info["n_blocks"] == cfg["n_blocks"]
+    with pytest.raises(IOError) as e:  # load_genomic_auto failures are io::Error (flat_reader.rs:240)
+        g.load_genomic_auto(path, max_ctx=16, max_streams=2)
+    assert "single-stream" in str(e.value)
+
+    mixed = str(tmp_path / "mixed.flat")
+    flat_numpy.write_synthetic_lut4(mixed, seed=2, **cfg)
+    raw = bytearray(open(mixed, "rb").read())
+    q4 = str(tmp_path / "q4.flat")
+    g.write_synthetic(q4, seed=2, **cfg)
+    # block 1's ffn_down back to a Q4_0 entry: a kind that mixes formats
+    meta, dlen = struct.unpack_from("<Q", raw, 16)[0], struct.unpack_from("<Q", raw, 24)[0]
+    d = json.loads(bytes(raw[4096 + meta:4096 + meta + dlen]))
+    e1 = next(x for x in d if x["name"] == "blk.1.ffn_down")
+    e1["c_len"] = 0
+    e1["dna_len"] = e1["out_features"] * e1["in_features"] // 32 * 20
+    new = json.dumps(d).encode()
+    assert len(new) <= dlen
+    raw[4096 + meta:4096 + meta + dlen] = new + b" " * (dlen - len(new))
+    weights_len = struct.unpack_from("<Q", raw, 40)[0]
+    raw.extend(b"\0" * (e1["dna_len"]))  # room for the reinterpreted blob
+    struct.pack_into("<Q", raw, 40, weights_len + e1["dna_len"])
+    open(mixed, "wb").write(raw)
+    with pytest.raises(IOError) as e:
+        g.load_genomic_auto(mixed, max_ctx=16)
+    assert "mixes Genomic4Bit tables and Q4_0 blocks" in str(e.value)

@@ -139,6 +139,16 @@ def test_batch1_workload_as_benchmarked(g, O, make_model, name, prompt_len, step
     gpu.close()
 
 
+def test_q8_lm_head_fused_kernel(g, O, make_model):
+    """The exporter's --quant-embed variant of the Qwen2-0.5B shape (Q8_0
+    token_embd / lm_head): the fused kernel streams the Q8_0 rows themselves
+    (genomic.rs:381-448 values, q * scale) instead of dequantised f32 rows."""
+    path = make_model("qwen2-0.5b-q8e", seed=SEED)
+    gpu, _ = _host_loop_parity(g, O, path, _bench_prompt(151936, 32), 64, "qwen2-0.5b-q8e host loop")
+    assert gpu.info().megakernel == 2
+    gpu.close()
+
+
 def test_fused_kernel_run_to_run(g, make_model):
     """Two runs of the fused kernel on one prompt and 64 greedy steps: the
     token streams are identical; the logit spread between the runs is printed
@@ -171,12 +181,16 @@ def q15(make_model):
     return make_model("qwen2.5-1.5b", seed=SEED)
 
 
-def test_q15_batch1_engine(g, O, q15):
-    """The batch-1 path on head_dim 128 / d 1536 (the engine load_genomic_auto
-    picks for the shape)."""
+@pytest.mark.parametrize("engine", [1, 2, 0], ids=["default", "five-exchange", "phase"])
+def test_q15_batch1_engine(g, O, q15, engine):
+    """The batch-1 path on head_dim 128 / d 1536, whichever engine the load
+    option leads to for the shape (n_head * head_dim = 1536 is past what the
+    persistent kernels' plans accept, so every option must end on an engine
+    that computes it)."""
     rng = np.random.default_rng(15)
     prompt = [int(t) for t in rng.integers(0, 151936, 24)]
-    gpu, _ = _host_loop_parity(g, O, q15, prompt, 64, "qwen2.5-1.5b batch-1")
+    gpu, _ = _host_loop_parity(g, O, q15, prompt, 64, f"qwen2.5-1.5b batch-1 (option {engine})",
+                               use_megakernel=engine)
     print(f"qwen2.5-1.5b batch-1 engine: {gpu.info().megakernel}")
     gpu.close()
 
