@@ -774,13 +774,16 @@ def run_trace_fused(args) -> None:
     first = 0
     for i, t in enumerate(prompt):
         first = model.forward_argmax(t, i == 0)
-    tr = model.trace_fused(first, args.steps).astype(np.float64) / 1000.0  # [grid, steps, L+1, 16] us
+    tr = model.trace_fused(first, args.steps) / 1000.0  # [grid, steps, L+1, 24] us
     G, K, L1, _ = tr.shape
     L = L1 - 1
     info = model.info()
-    # attention CTAs stamp 0-8 and 15; every CTA with FFN outputs stamps 9-14
+    # attention CTAs stamp 0-8 and 15-20; every CTA with FFN outputs stamps 9-14
     segs_a = [("input gate + residual (A)", 0, 1), ("attn_norm staging", 1, 2), ("q/k/v GEMV + RoPE", 2, 3),
-              ("K/V rows wait", 3, 4), ("split attention math", 4, 5), ("attn_output columns", 5, 6),
+              ("K/V rows wait", 3, 4), ("split attention math", 4, 5),
+              ("  attention entry -> K/V landed", 16, 4), ("  scores", 4, 17), ("  softmax + (m, l)", 17, 18),
+              ("  P*V", 18, 19), ("  next K/V request", 19, 20), ("  return -> CTA barrier", 20, 5),
+              ("attn_output columns", 5, 6),
               ("split weight", 6, 15),
               ("red.add + publish (A)", 7, 8)]
     segs_b = [("residual x_a", 9, 10), ("ffn_norm staging", 10, 11), ("gate/up GEMV + SwiGLU", 11, 12),

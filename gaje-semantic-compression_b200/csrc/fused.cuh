@@ -122,9 +122,16 @@ struct FusedArgs {
   unsigned long long* trace;  // optional [grid][n_steps][L+1][kFuTrace] %globaltimer stamps
 };
 
-// Trace points per block (phase A 0-8, phase B 9-14) and for the lm_head
-// (block index L: 0 entry, 1 input ready, 2 staged, 3 rows done, 4 token out).
-constexpr int kFuTrace = 16;
+// Trace points per block (phase A 0-8 and 15-20, phase B 9-14) and for the
+// lm_head (block index L: 0 entry, 1 input ready, 2 staged, 3 rows done, 4
+// token out).
+constexpr int kFuTrace = 24;
+
+// Trace stamps are SM cycle counts (clock64: fine-grained, but per SM); each
+// CTA also records (globaltimer, clock64) anchor pairs at its start and end,
+// in the lm_head row of step 0 (slots 22, 23) and of the last step (slots 20,
+// 21), from which the host maps its cycles onto the global nanosecond clock.
+__device__ __forceinline__ unsigned long long fu_tstamp() { return (unsigned long long)clock64(); }
 
 __host__ __device__ inline unsigned fu_epoch(unsigned e0, int L, int step, int l, int ph) {
   return e0 + unsigned(step) * unsigned(2 * L + 1) + unsigned(2 * l + ph) + 1u;
@@ -571,6 +578,9 @@ __device__ __forceinline__ int fu_attend_warp(const FusedArgs& A, const FuShared
   DevState* st = P.st;
   constexpr int HD = 32 * VEC;
   const int lane = threadIdx.x & 31, L = P.n_layers;
+  unsigned long long* trow = A.trace ? A.trace + (((size_t)blockIdx.x * A.n_steps + step) * (L + 1) + l) * kFuTrace
+                                     : nullptr;
+  if (trow && lane == 0) trow[16] = fu_tstamp();  // trace point 16: the split's attention starts
   int t0, n_old;
   fu_split(int(pos), pl.S, sp, t0, n_old);
   const bool last = sp == pl.S - 1;
@@ -613,39 +623,36 @@ __device__ __forceinline__ int fu_attend_warp(const FusedArgs& A, const FuShared
   __syncwarp();
   if (lane == 0) {
     *S.kv_waited = use + 1;
-    if (A.trace)  // trace point 4: this split's K/V rows landed
-      A.trace[(((size_t)blockIdx.x * A.n_steps + step) * (L + 1) + l) * kFuTrace + 4] = global_ns();
+    if (trow) trow[4] = fu_tstamp();  // trace point 4: this split's K/V rows landed
   }
-  float q[VEC];
-#pragma unroll
-  for (int v = 0; v < VEC; ++v) q[v] = S.qbuf[lane + 32 * v];
+  // Scores, a lane per position: lane i of group g0 forms dot(q, K[g0 + i]) over
+  // float4 columns visited in the rotated order (j + i) mod HD/4, so that any 8
+  // consecutive lanes touch 8 distinct 16-byte bank groups of K and of q (no
+  // bank conflict).  A rolled loop: far less code than the unrolled
+  // 32-position butterfly it replaced, for the same arithmetic.
+  constexpr int H4 = HD / 4;
+  const float4* q4 = reinterpret_cast<const float4*>(S.qbuf);
   float m = -INFINITY;
   for (int g0 = 0; g0 < n; g0 += 32) {
-    float part[32];
-#pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      const int t = min(g0 + i, n - 1);  // past the end: a repeat, discarded
-      float a = 0.f;
-#pragma unroll
-      for (int v = 0; v < VEC; ++v) a = fmaf(q[v], Ks[(size_t)t * HD + lane + 32 * v], a);
-      part[i] = a;
-    }
-#pragma unroll
-    for (int o = 16, hh = 16; o >= 1; o >>= 1, hh >>= 1) {
-      const bool up = (lane & o) != 0;
-#pragma unroll
-      for (int i = 0; i < hh; ++i) {
-        const float send = up ? part[i] : part[i + hh];
-        const float keep = up ? part[i + hh] : part[i];
-        part[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    const int t = g0 + lane;
+    if (t < n) {
+      const float4* kr = reinterpret_cast<const float4*>(Ks + (size_t)t * HD);
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll 4
+      for (int j = 0; j < H4; ++j) {
+        const int jj = (j + lane) & (H4 - 1);
+        const float4 kv = kr[jj], qv = q4[jj];
+        a0 = fmaf(qv.x, kv.x, a0);
+        a1 = fmaf(qv.y, kv.y, a1);
+        a0 = fmaf(qv.z, kv.z, a0);
+        a1 = fmaf(qv.w, kv.w, a1);
       }
-    }
-    if (g0 + lane < n) {
-      const float sc = part[0] * P.attn_scale;
-      S.ps[g0 + lane] = sc;
+      const float sc = (a0 + a1) * P.attn_scale;
+      S.ps[t] = sc;
       m = fmaxf(m, sc);
     }
   }
+  if (trow && lane == 0) trow[17] = fu_tstamp();  // trace point 17: scores done
   m = warp_max(m);
   __syncwarp();
   float lsum = 0.f;
@@ -663,6 +670,7 @@ __device__ __forceinline__ int fu_attend_warp(const FusedArgs& A, const FuShared
       st_ll(ml, m, eA);
       st_ll(ml + 1, lsum, eA);
     }
+    if (trow) trow[18] = fu_tstamp();  // trace point 18: softmax done, (m, l) published
   }
   float acc[VEC];
 #pragma unroll
@@ -675,8 +683,10 @@ __device__ __forceinline__ int fu_attend_warp(const FusedArgs& A, const FuShared
   }
   __syncwarp();
   if (lane == 0) {  // K/V buffer free: the next block's (or next step's) rows
+    if (trow) trow[19] = fu_tstamp();  // trace point 19: P*V done
     if (l + 1 < L) fu_kv_prefetch(A, S, l + 1, int(pos));
     else if (step + 1 < A.n_steps && L > 1) fu_kv_prefetch(A, S, 0, int(pos) + 1);
+    if (trow) trow[20] = fu_tstamp();  // trace point 20: next K/V rows requested
   }
 #pragma unroll
   for (int v = 0; v < VEC; ++v) mk_stage_elem(S.ost, S.ost + HD, lane + 32 * v, acc[v]);
@@ -739,9 +749,9 @@ __device__ __forceinline__ bool fu_lm(const FusedArgs& A, const FuShared& S, int
   __shared__ int is_last;
   fu_prefetch(S.nw, P.out_norm, d);
   const unsigned eLastB = fu_epoch(A.epoch0, L, step, L - 1, 1);
-  if (trace_row && tid == 0) trace_row[0] = global_ns();
+  if (trace_row && tid == 0) trace_row[0] = fu_tstamp();
   if (!fu_gate(A.flags + G, G, eLastB, S.cabort, st)) return false;
-  if (trace_row && tid == 0) trace_row[1] = global_ns();
+  if (trace_row && tid == 0) trace_row[1] = fu_tstamp();
   const int gl = step * L + L - 1;
   fu_add_sum(S.R, S.XA, A.yb + (gl & 1) * d, A.layers[L - 1].down.bias, d, st, pos, c == 0 ? L - 1 : -1);
   fu_sync();
@@ -752,7 +762,7 @@ __device__ __forceinline__ bool fu_lm(const FusedArgs& A, const FuShared& S, int
     S.xs[i] = v * S.nw[i];
   }
   const float scale = 1.0f / sqrtf(fu_total(ss, S.misc, false) / (float)d + P.eps);
-  if (trace_row && tid == 0) trace_row[2] = global_ns();
+  if (trace_row && tid == 0) trace_row[2] = fu_tstamp();
   const float4* x4 = reinterpret_cast<const float4*>(S.xs);
   const int K4 = d >> 2;
   unsigned long long best = 0ull;
@@ -814,7 +824,7 @@ __device__ __forceinline__ bool fu_lm(const FusedArgs& A, const FuShared& S, int
   }
   if (cur >= 0) fu_release(A, S, item + cur);
   *item_io = item + nitems;
-  if (trace_row && tid == 0) trace_row[3] = global_ns();
+  if (trace_row && tid == 0) trace_row[3] = fu_tstamp();
   best = warp_max_u64(best);
   if (lane == 0) wbest[wid] = best;
   fu_sync();
@@ -852,7 +862,7 @@ __device__ __forceinline__ bool fu_lm(const FusedArgs& A, const FuShared& S, int
     }
   }
   fu_sync();
-  if (trace_row && tid == 0) trace_row[4] = global_ns();
+  if (trace_row && tid == 0) trace_row[4] = fu_tstamp();
   return true;
 }
 
@@ -876,7 +886,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
   const unsigned pos0 = __ldcg(&st->pos);
   auto fmark = [&](int step, int l, int k) {
     if (A.trace && tid == 0)
-      A.trace[(((size_t)c * A.n_steps + step) * (L + 1) + l) * kFuTrace + k] = global_ns();
+      A.trace[(((size_t)c * A.n_steps + step) * (L + 1) + l) * kFuTrace + k] = fu_tstamp();
   };
   if (roleA && tid == 0) fu_kv_prefetch(A, S, 0, int(pos0));  // step 0, block 0
   for (int step = 0; step < A.n_steps; ++step) {
@@ -1069,7 +1079,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
   }
 }
 
-__global__ void __launch_bounds__(kFuThreads, 1) k_decode_fused(FusedArgs A) {
+__global__ void __launch_bounds__(kFuThreads, 1) k_decode_fused(const __grid_constant__ FusedArgs A) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const FusedPlan& pl = A.plan;
   const int d = A.P.d, hd = A.P.hd;
@@ -1139,9 +1149,20 @@ __global__ void __launch_bounds__(kFuThreads, 1) k_decode_fused(FusedArgs A) {
     }
     return;
   }
+  unsigned long long* anchor =
+      A.trace ? A.trace + (((size_t)blockIdx.x * A.n_steps) * (A.P.n_layers + 1) + A.P.n_layers) * kFuTrace : nullptr;
+  if (anchor && threadIdx.x == 0) {
+    anchor[22] = global_ns();
+    anchor[23] = fu_tstamp();
+  }
   fu_consumer(A, S);
   // a K/V copy may still be in flight (the last prefetch, or an abort): it must land first
   if (threadIdx.x == 0 && *S.kv_armed > *S.kv_waited) mbar_wait(S.kv_bar, (*S.kv_waited) & 1);
+  if (anchor && threadIdx.x == 0) {
+    unsigned long long* last = anchor + (size_t)(A.n_steps - 1) * (A.P.n_layers + 1) * kFuTrace;
+    last[21] = fu_tstamp();
+    last[20] = global_ns();
+  }
 }
 
 // Dynamic shared memory of the fused kernel.

@@ -470,15 +470,31 @@ class GenomicLLM:
         return out
 
     def trace_fused(self, first_token: int, n_steps: int) -> np.ndarray:
-        """The two-exchange kernel's trace stamps (ns) of n_steps greedy steps in
-        one launch: shape [grid, n_steps, n_blocks+1, 16] (see
-        gaje_cuda_trace_fused for the points)."""
+        """The two-exchange kernel's trace stamps of n_steps greedy steps in one
+        launch, in nanoseconds of the global timer from the first CTA's start
+        (float64, 0 where a CTA had no such point): shape [grid, n_steps, n_blocks+1, 24] (see
+        gaje_cuda_trace_fused for the points).  The kernel stamps SM cycles;
+        each CTA's (globaltimer, cycle) anchors at its start and end map them
+        onto the global clock."""
         inf = self.info()
-        out = np.zeros((inf.grid, int(n_steps), inf.n_blocks + 1, 16), dtype=np.uint64)
+        L = inf.n_blocks
+        raw = np.zeros((inf.grid, int(n_steps), L + 1, 24), dtype=np.uint64)
         n = C.c_size_t(0)
-        _check(lib().gaje_cuda_trace_fused(self._m, int(first_token), int(n_steps), _ptr(out), C.c_size_t(out.size),
+        _check(lib().gaje_cuda_trace_fused(self._m, int(first_token), int(n_steps), _ptr(raw), C.c_size_t(raw.size),
                                            C.byref(n)))
-        return out
+        # differences in integers first: float64 cannot resolve single
+        # nanoseconds (or cycles) at the timers' absolute magnitudes
+        g0i, c0i = raw[:, 0, L, 22].copy(), raw[:, 0, L, 23].copy()
+        g1i, c1i = raw[:, -1, L, 20].copy(), raw[:, -1, L, 21].copy()
+        base = int(g0i.min())
+        g0 = (g0i - np.uint64(base)).astype(np.float64)
+        rate = (g1i - g0i).astype(np.float64) / np.maximum((c1i - c0i).astype(np.float64), 1.0)  # ns per cycle
+        raw[:, 0, L, 22:24] = 0
+        raw[:, -1, L, 20:22] = 0
+        shape = (-1,) + (1,) * 3
+        rel = (raw.astype(np.int64) - c0i.astype(np.int64).reshape(shape)).astype(np.float64)
+        ns = 1.0 + g0.reshape(shape) + rel * rate.reshape(shape)  # > 0 for every stamp
+        return np.where(raw > 0, ns, 0.0)
 
     def generate_native_py(self, prompt_tokens: Sequence[int], max_new_tokens: int = 30,
                            temperature: float = 0.7, repetition_penalty: float = 1.0,

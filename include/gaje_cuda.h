@@ -339,15 +339,20 @@ int gaje_cuda_trace_steps(gaje_model* model, uint32_t first_token, size_t n_step
                           uint64_t* out, size_t out_len, size_t* n_written);
 
 /* The same for the two-exchange persistent kernel (gaje_model_info.megakernel
- * == 2): out[((cta*n_steps + step)*(L+1) + l)*16 + k] is the %globaltimer
- * value (ns) of trace point k of block l on that CTA (0 where the CTA had no
- * such point).  Block points: 0 phase A entry, 1 input ready, 2 input staged,
+ * == 2): out[((cta*n_steps + step)*(L+1) + l)*24 + k] is the SM cycle
+ * count (clock64) of trace point k of block l on that CTA (0 where the CTA had
+ * no such point).  Anchors map each CTA's cycles onto the global nanosecond
+ * timer: out[(cta*n_steps*(L+1) + L)*24 + 22, 23] = (%globaltimer, clock64)
+ * at the CTA's start, and the same row of the last step holds them at its
+ * end in slots 20, 21.  Block points: 0 phase A entry, 1 input ready, 2 input staged,
  * 3 q (or k/v) rows done, 4 K/V rows landed, 5 attention done, 6 output
  * projection done, 7 split weights known, 8 phase A published, 9 phase B
  * input flags seen, 10 x_a formed, 11 staged, 12 first gate/up block done,
- * 13 down columns done, 14 phase B published.  l = L: 0 entry, 1 input
- * ready, 2 staged, 3 lm_head rows done, 4 token published.  out_len must be
- * at least grid*n_steps*(L+1)*16.  No counterpart in the reference: a
+ * 13 down columns done, 14 phase B published, 15 split weight done, 16 the
+ * split's attention starts, 17 scores done, 18 softmax done, 19 P*V done,
+ * 20 next K/V rows requested.  l = L: 0 entry, 1 input ready, 2 staged, 3
+ * lm_head rows done, 4 token published.  out_len must be at least
+ * grid*n_steps*(L+1)*24.  No counterpart in the reference: a
  * diagnostic of the kernel's critical path. */
 int gaje_cuda_trace_fused(gaje_model* model, uint32_t first_token, size_t n_steps,
                           uint64_t* out, size_t out_len, size_t* n_written);

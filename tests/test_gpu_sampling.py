@@ -3,7 +3,8 @@ the oracle's restatement of sample_top_p_core (src/compute/sampling.rs:14-55)
 with the same uniform draw r.
 
 The device sums probabilities exactly (fixed point); the reference runs f32
-running sums, which over 10^5 terms drift from the exact sums by about 1e-5.
+running sums, whose normalising sum over 10^5 terms drifts from the exact sum
+by about 2e-4 relative (measured per case by _f32_drift).
 The two choices agree unless the draw (or top_p) lies within that drift of a
 boundary between tokens; every disagreement must be such a near tie, checked
 in float64 on the reference's own ordering (EPS below).
@@ -30,7 +31,24 @@ def _f64_walk(logits, T, top_p, r):
     return ps, order, cum, cutoff, target
 
 
-EPS = 1e-4  # the f32 running sums' drift over a 151936-token vocabulary, with margin
+EPS = 1e-4  # the floor of the tolerance below
+
+
+def _f32_drift(logits, T, top_p):
+    """How far the reference's f32 arithmetic moves the cumulative masses from
+    their exact values on this case: the normalising sum is an f32 running sum
+    over the whole vocabulary (about 2e-4 relative over 151936 terms), and the
+    sorted running sum adds its own rounding.  Returned with a 25 % margin and
+    never below EPS."""
+    lg = logits.astype(np.float32)
+    p32 = np.exp(((lg - lg.max()) / np.float32(T)).astype(np.float32))
+    s32 = np.cumsum(p32, dtype=np.float32)[-1]
+    p64 = p32.astype(np.float64)
+    q64 = p64 / p64.sum()
+    order = np.argsort(-q64, kind="stable")
+    c64 = np.cumsum(q64[order])
+    c32 = np.cumsum((p32 / s32)[order], dtype=np.float32)
+    return max(EPS, 1.25 * float(np.abs(c32.astype(np.float64) - c64).max()))
 
 
 def _near_tie(logits, T, top_p, r, a, b, eps=EPS):
@@ -66,6 +84,7 @@ def test_top_p_matches_oracle(g, O, T, top_p):
     for name, lg in _cases():
         d = torch.from_numpy(lg).cuda()
         rs = [0.0] + list(np.random.default_rng(len(lg)).random(23)) + [0.999999]
+        eps = _f32_drift(lg, T, top_p)
         for r in rs:
             r = float(np.float32(r))
             if r >= 1.0:
@@ -77,10 +96,12 @@ def test_top_p_matches_oracle(g, O, T, top_p):
             total += 1
             if tok != otok:
                 mism += 1
-                assert _near_tie(lg, T, top_p, r, tok, otok), (name, T, top_p, r, tok, otok)
+                assert _near_tie(lg, T, top_p, r, tok, otok, eps), (name, T, top_p, r, tok, otok, eps)
             if kept != okept:
                 ps, order, cum, cutoff, target = _f64_walk(lg, T, top_p, r)
-                assert abs(cum[min(kept, okept) - 1] - top_p) <= EPS, (name, kept, okept)
+                # every kept count between the two sits at a cumulative mass within the drift of top_p
+                assert all(abs(cum[k - 1] - top_p) <= eps for k in range(min(kept, okept), max(kept, okept))), (
+                    name, kept, okept, eps)
     assert mism <= total // 2, (mism, total)  # near ties are the exception, not the rule
 
 
