@@ -30,6 +30,7 @@ from .runtime import (  # noqa: F401
     quantize_q8_0_native,
     rms_norm,
     sample_top_p,
+    set_wait_limit,
     vocab_shard,
     write_synthetic,
 )

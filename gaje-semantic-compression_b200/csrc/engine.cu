@@ -354,6 +354,7 @@ struct gaje_model {
   uint2* fwords = nullptr; // flags [2][grid], kvnew [2][nkv][hd], mlx [nh][S][2], token
   size_t fwords_n = 0;
   unsigned fepoch = 0;
+  int withhold_cta = -1;   // gaje_cuda_debug_withhold_flag: for the next fused launch only
   // batched streams (gaje_cuda_forward_batch)
   int max_streams = 0;
   BatchCache bcache{};
@@ -638,6 +639,8 @@ struct gaje_model {
       a.epoch0 = fepoch;
       a.n_steps = chunk;
       a.trace = chunk == int(n) ? trace : nullptr;
+      a.withhold = withhold_cta;
+      withhold_cta = -1;
       fepoch += unsigned(per);
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(sms);
@@ -2294,6 +2297,25 @@ int gaje_cuda_trace_steps(gaje_model* m, uint32_t first_token, size_t n_steps, u
   if (int s = mega_stamped_run(m, first_token, n_steps, true, ts, &tr)) return s;
   std::memcpy(out, tr.data(), need * 8);
   *n_written = need;
+  return GAJE_OK;
+}
+
+int gaje_cuda_set_wait_limit(int device, uint64_t ns) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n)
+    return set_error(GAJE_ERR_INVALID, "no such CUDA device");
+  const unsigned long long v = ns ? (unsigned long long)ns : kWaitNsDefault;
+  CK(cudaSetDevice(device));
+  CK(cudaMemcpyToSymbol(c_wait_ns, &v, sizeof(v)));
+  CK(cudaDeviceSynchronize());
+  return GAJE_OK;
+}
+
+int gaje_cuda_debug_withhold_flag(gaje_model* m, int cta) {
+  if (!m) return set_error(GAJE_ERR_INVALID, "NULL argument");
+  if (!m->use_fused) return set_error(GAJE_ERR_UNSUPPORTED, "the model does not run the two-exchange kernel");
+  if (cta < 0 || cta >= int(m->fplan.nA)) return set_error(GAJE_ERR_INVALID, "cta must be an attention CTA");
+  m->withhold_cta = cta;
   return GAJE_OK;
 }
 

@@ -57,7 +57,11 @@ constexpr int kLmMaxStages = 8;
 constexpr size_t kLmSmemBudget = 200 * 1024;  // ring + x, below the 227 KB per-CTA limit
 constexpr int kKwtaThreads = 1024;
 constexpr int kSmemHeader = 128;        // mbarriers at the start of dynamic smem
-constexpr unsigned long long kWaitNs = 2000000000ull;  // bounded mbarrier waits: 2 s
+// Limit of every bounded device-side wait (mbarrier phases, exchange flags and
+// words), in ns of %globaltimer: 2 s unless gaje_cuda_set_wait_limit changed it
+// for the device.
+constexpr unsigned long long kWaitNsDefault = 2000000000ull;
+__constant__ unsigned long long c_wait_ns = kWaitNsDefault;
 
 // NaN guard codes, in the order block/forward.rs checks them.
 enum NanCheck : unsigned {
@@ -165,12 +169,12 @@ __device__ __forceinline__ unsigned long long global_ns() {
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
   return t;
 }
-// Bounded wait on an mbarrier phase: false after kWaitNs without completion.
+// Bounded wait on an mbarrier phase: false after c_wait_ns without completion.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   while (!mbar_try_wait(bar, parity))
-    if (global_ns() - t0 > kWaitNs) return false;
+    if (global_ns() - t0 > c_wait_ns) return false;
   return true;
 }
 // 1-D TMA bulk copy global -> this CTA's shared memory (no multicast).

@@ -54,7 +54,7 @@
 // 2^-p, so (f - 2^23) * x' = q * x exactly; the subtract and the FMA run as
 // packed f32x2 instructions.
 //
-// Every wait is bounded (kWaitNs); a wait that runs out sets DevState::err and
+// Every wait is bounded (c_wait_ns); a wait that runs out sets DevState::err and
 // the CTA's abort flag; the consumers leave together at their next barrier,
 // the producer drains its in-flight copies (bounded) and exits.
 #pragma once
@@ -229,7 +229,7 @@ __device__ __forceinline__ bool ll_gather(const uint2* src, int n, unsigned e, f
       if (all) break;
       const unsigned long long t = global_ns();
       if (!t0) t0 = t;
-      else if (t - t0 > kWaitNs) return false;
+      else if (t - t0 > c_wait_ns) return false;
     }
 #pragma unroll
     for (int k = 0; k < R; ++k) {
@@ -291,7 +291,7 @@ __device__ __forceinline__ void mk_gate(const uint2* fl, int nw, unsigned e, vol
         if (all) break;
         const unsigned long long t = global_ns();
         if (!t0) t0 = t;
-        else if (t - t0 > kWaitNs) {
+        else if (t - t0 > c_wait_ns) {
           ok = false;
           break;
         }
@@ -861,7 +861,7 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
             if (all) break;
             const unsigned long long t = global_ns();
             if (!tw) tw = t;
-            else if (t - tw > kWaitNs) {
+            else if (t - tw > c_wait_ns) {
               ok = false;
               break;
             }
@@ -912,7 +912,7 @@ __device__ void mk_consumer(const MegaArgs& A, const MkShared& S) {
             while (w.y != e_prev) {
               const unsigned long long t = global_ns();
               if (!t0) t0 = t;
-              else if (t - t0 > kWaitNs) {
+              else if (t - t0 > c_wait_ns) {
                 ok = false;
                 break;
               }

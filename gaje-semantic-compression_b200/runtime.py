@@ -142,6 +142,8 @@ def lib() -> C.CDLL:
         "gaje_cuda_profile_phases": ([vp, u32, sz, vp, vp, vp], i32),
         "gaje_cuda_trace_steps": ([vp, u32, sz, vp, sz, vp], i32),
         "gaje_cuda_trace_fused": ([vp, u32, sz, vp, sz, vp], i32),
+        "gaje_cuda_set_wait_limit": ([i32, u64], i32),
+        "gaje_cuda_debug_withhold_flag": ([vp, i32], i32),
         "gaje_cuda_profile_batch": ([vp, vp, vp, sz, vp, vp], i32),
         "gaje_cuda_attention_decode_static": ([vp, vp, vp, sz, sz, sz, sz, sz, vp, vp], i32),
         "gaje_cuda_forward_batch": ([vp, vp, vp, sz, vp, vp], i32),
@@ -469,6 +471,12 @@ class GenomicLLM:
                                            C.byref(n)))
         return out
 
+    def debug_withhold_flag(self, cta: int) -> None:
+        """Failure-path diagnostic (gaje_cuda_debug_withhold_flag): attention CTA
+        `cta` raises no flag in the next launch of the two-exchange kernel, so
+        that call returns GAJE_ERR_TIMEOUT once the bounded waits run out."""
+        _check(lib().gaje_cuda_debug_withhold_flag(self._m, int(cta)))
+
     def trace_fused(self, first_token: int, n_steps: int) -> np.ndarray:
         """The two-exchange kernel's trace stamps of n_steps greedy steps in one
         launch, in nanoseconds of the global timer from the first CTA's start
@@ -509,6 +517,12 @@ class GenomicLLM:
         return [int(t) for t in out[: n.value]]
 
     generate = generate_native_py
+
+
+def set_wait_limit(device: int, ns: int) -> None:
+    """The limit of every bounded device-side wait of the library's kernels on
+    `device` (gaje_cuda_set_wait_limit); 0 restores the default of 2 s."""
+    _check(lib().gaje_cuda_set_wait_limit(int(device), int(ns)))
 
 
 def nccl_unique_id() -> bytes:

@@ -357,6 +357,24 @@ int gaje_cuda_trace_steps(gaje_model* model, uint32_t first_token, size_t n_step
 int gaje_cuda_trace_fused(gaje_model* model, uint32_t first_token, size_t n_steps,
                           uint64_t* out, size_t out_len, size_t* n_written);
 
+/* The limit of every bounded device-side wait of this library's kernels on
+ * `device` (mbarrier phases, exchange flags and words), in nanoseconds; 0
+ * restores the default of 2 s.  A wait that runs out makes the call return
+ * GAJE_ERR_TIMEOUT and leaves the CUDA context usable.  Applies to every model
+ * on the device; call it while none of them is running a step.  No
+ * counterpart in the reference (a CPU engine has no device waits). */
+int gaje_cuda_set_wait_limit(int device, uint64_t ns);
+
+/* Diagnostic of the failure path: in the model's next launch of the
+ * two-exchange kernel, CTA `cta` (an attention CTA, 0 <= cta < n_head *
+ * splits) raises no flag after the attention half of the first block, so
+ * every other CTA's bounded wait for it runs out and the call returns
+ * GAJE_ERR_TIMEOUT (after about two wait limits).  Applies to one launch;
+ * the model's cache is then in an undefined state (clear it or reload).
+ * GAJE_ERR_UNSUPPORTED when the model runs another engine.  No counterpart in
+ * the reference. */
+int gaje_cuda_debug_withhold_flag(gaje_model* model, int cta);
+
 /* ---------------------------------------------------------------- op level */
 /* Device-pointer entry points for the isolated kernel checks and sweeps.
  * `stream` is a cudaStream_t (NULL = legacy default stream). */
