@@ -782,7 +782,7 @@ def run_trace_fused(args) -> None:
     segs_a = [("input gate + residual (A)", 0, 1), ("attn_norm staging", 1, 2), ("q/k/v GEMV + RoPE", 2, 3),
               ("K/V rows wait", 3, 4), ("split attention math", 4, 5),
               ("  attention entry -> K/V landed", 16, 4), ("  scores", 4, 17), ("  softmax + (m, l)", 17, 18),
-              ("  P*V", 18, 19), ("  next K/V request", 19, 20), ("  return -> CTA barrier", 20, 5),
+              ("  P*V", 18, 19), ("  return -> CTA barrier", 19, 5),
               ("attn_output columns", 5, 6),
               ("split weight", 6, 15),
               ("red.add + publish (A)", 7, 8)]

@@ -479,7 +479,9 @@ __device__ __forceinline__ void fu_kv_prefetch(const FusedArgs& A, const FuShare
   fu_split(cached, A.plan.S, s, t0, n_old);
   const uint32_t bytes = uint32_t(n_old) * P.hd * 4;
   const LayerW& Lw = A.layers[l];
-  fence_acq_rel_gpu();
+  // the rows were written by the KV CTAs of earlier blocks, and this thread
+  // has acquired them since (its gate's fence): a proxy fence is enough to
+  // hand them to the asynchronous (TMA) reads
   asm volatile("fence.proxy.async.global;" ::: "memory");
   *S.kv_armed = *S.kv_armed + 1;
   mbar_expect_tx(S.kv_bar, 2 * bytes);
@@ -683,12 +685,7 @@ __device__ __forceinline__ int fu_attend_warp(const FusedArgs& A, const FuShared
     for (int v = 0; v < VEC; ++v) acc[v] = fmaf(p, Vs[(size_t)t * HD + lane + 32 * v], acc[v]);
   }
   __syncwarp();
-  if (lane == 0) {  // K/V buffer free: the next block's (or next step's) rows
-    if (trow) trow[19] = fu_tstamp();  // trace point 19: P*V done
-    if (l + 1 < L) fu_kv_prefetch(A, S, l + 1, int(pos));
-    else if (step + 1 < A.n_steps && L > 1) fu_kv_prefetch(A, S, 0, int(pos) + 1);
-    if (trow) trow[20] = fu_tstamp();  // trace point 20: next K/V rows requested
-  }
+  if (lane == 0 && trow) trow[19] = fu_tstamp();  // trace point 19: P*V done
 #pragma unroll
   for (int v = 0; v < VEC; ++v) mk_stage_elem(S.ost, S.ost + HD, lane + 32 * v, acc[v]);
   return n;
@@ -1008,6 +1005,13 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
             }
           if (c == A.withhold && l == 0 && step == 0) fu_sync();  // the readers' waits run out
           else fu_publish(flA + c, eA);
+          // the K/V buffer is free: the next block's (or next step's) cached rows,
+          // requested off the critical path while the FFN half waits
+          if (tid == 0) {
+            if (l + 1 < L) fu_kv_prefetch(A, S, l + 1, int(pos));
+            else if (step + 1 < A.n_steps && L > 1) fu_kv_prefetch(A, S, 0, int(pos) + 1);
+            if (A.trace) A.trace[(((size_t)c * A.n_steps + step) * (L + 1) + l) * kFuTrace + 20] = fu_tstamp();
+          }
           fmark(step, l, 8);
         }
       }

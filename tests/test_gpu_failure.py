@@ -78,6 +78,15 @@ def test_withhold_rejects_bad_arguments(g, make_model):
     m.close()
 
 
+def _post(q, item, exit_after=False):
+    """Queue.put is asynchronous: flush the feeder before an os._exit."""
+    q.put(item)
+    if exit_after:
+        q.close()
+        q.join_thread()
+        os._exit(0)
+
+
 def _leaver(rank, world, nid, path, B, P, steps, q, ev):
     try:
         os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -99,8 +108,7 @@ def _leaver(rank, world, nid, path, B, P, steps, q, ev):
         if rank == 1:  # leaves between steps: nothing of it in flight
             q.put((rank, "left", None, 0.0))
             ev.wait(120)  # stays alive (and silent) until rank 0 has seen the timeout
-            q.put((rank, "done", None, 0.0))
-            os._exit(0)
+            _post(q, (rank, "done", None, 0.0), exit_after=True)
         time.sleep(0.5)
         t0 = time.time()
         status = None
@@ -115,11 +123,10 @@ def _leaver(rank, world, nid, path, B, P, steps, q, ev):
         except g.GajeError as e:
             after = e.status
         ev.set()
-        q.put((rank, status, after, elapsed))
-        os._exit(0)
+        _post(q, (rank, status, after, elapsed), exit_after=True)
     except Exception as e:  # noqa: BLE001
         ev.set()
-        q.put((rank, repr(e), None, 0.0))
+        _post(q, (rank, repr(e), None, 0.0), exit_after=True)
 
 
 def test_sharded_rank_leaving_makes_peer_time_out(g, make_model):
@@ -138,7 +145,7 @@ def test_sharded_rank_leaving_makes_peer_time_out(g, make_model):
     res = {}
     try:
         for _ in range(3):
-            rank, a, b, t = q.get(timeout=300)
+            rank, a, b, t = q.get(timeout=180)
             res.setdefault(rank, []).append((a, b, t))
     finally:
         ev.set()
