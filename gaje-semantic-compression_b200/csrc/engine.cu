@@ -351,7 +351,7 @@ struct gaje_model {
   FuLayer* d_fl = nullptr;
   float* fya = nullptr;    // [2][d]
   float* fyb = nullptr;    // [2][d]
-  uint2* fwords = nullptr; // flags [2][grid], kvnew [2][nkv][hd], mlx [nh][S][2], token
+  uint2* fwords = nullptr; // phase counters [2 u32] (in a [2][grid] region), kvnew [2][nkv][hd], mlx [nh][S][2], token
   size_t fwords_n = 0;
   unsigned fepoch = 0;
   int withhold_cta = -1;   // gaje_cuda_debug_withhold_flag: for the next fused launch only
@@ -617,14 +617,17 @@ struct gaje_model {
 
   // n greedy steps in launches of the two-exchange persistent kernel.
   int run_fused(size_t n, unsigned long long* trace = nullptr) {
+    // a launch's phase counters reach (steps * L) * grid: keep that below 2^32
+    const size_t max_chunk = std::min<size_t>(size_t(1) << 16, (size_t(0xFFFFFFFFu) / (size_t(sms) * L)) - 1);
     while (n > 0) {
-      const int chunk = int(std::min<size_t>(n, 1u << 16));
+      const int chunk = int(std::min<size_t>(n, max_chunk));
       const unsigned long long per = (unsigned long long)chunk * unsigned(2 * L + 1);
       if ((unsigned long long)fepoch + per >= 0xFFFFFFF0ull) {  // epochs wrap: restart from clean words
         CK(cudaMemsetAsync(fwords, 0, fwords_n * sizeof(uint2), stream));
         fepoch = 0;
       }
       CK(cudaMemsetAsync(fya, 0, size_t(4) * d * sizeof(float), stream));  // fya and fyb are adjacent
+      CK(cudaMemsetAsync(fwords, 0, 2 * sizeof(unsigned), stream));        // the phase counters
       FusedArgs a;
       a.P = P;
       a.layers = d_layers;
@@ -632,7 +635,7 @@ struct gaje_model {
       a.plan = fplan;
       a.ya = fya;
       a.yb = fyb;
-      a.flags = fwords;
+      a.cnt = reinterpret_cast<unsigned*>(fwords);
       a.kvnew = fwords + 2 * size_t(sms);
       a.mlx = a.kvnew + 2 * size_t(nkv) * hd;
       a.tok = a.mlx + size_t(nh) * fplan.S * 2;

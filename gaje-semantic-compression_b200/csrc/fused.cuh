@@ -31,13 +31,14 @@
 // sums.  The float sums are accumulated in arrival order, so results vary
 // from run to run at the rounding level (the parity bar is a tolerance).
 //
-// Exchanges: a CTA that finished its additions raises its flag (a barrier,
-// a gpu-scope fence, then the flag word); a reader polls the writers' flags
-// with one warp, fences, and reads the sums with L2 loads.  The (m, l) pairs
-// of the attention splits and this position's k/v rows travel as LL words
-// ({value, epoch}, self-validating).  The sums are double-buffered by block
-// parity and cleared by the attention CTAs two phases after their last read
-// (every reader of a buffer has raised a flag the clearing CTA waited for).
+// Exchanges: a CTA that finished its additions adds 1 to the phase's counter
+// with release semantics (after a barrier); a reader polls the counter until
+// every writer of the phase so far has added, loads it once with acquire
+// semantics, and reads the sums with L2 loads.  The (m, l) pairs of the
+// attention splits and this position's k/v rows travel as LL words ({value,
+// epoch}, self-validating).  The sums are double-buffered by block parity and
+// cleared by the attention CTAs two phases after their last read (every reader
+// of a buffer has published to a counter the clearing CTA waited for).
 //
 // Weights stream through a shared-memory ring (lane 0 of warp 15 is the
 // producer, 1-D TMA bulk copies, full/empty mbarriers) in this CTA's item
@@ -113,7 +114,7 @@ struct FusedArgs {
   FusedPlan plan;
   float* ya;      // [2][d] attention-projection sums
   float* yb;      // [2][d] down-projection sums
-  uint2* flags;   // [2][grid]: phase A flags, phase B flags ({0, epoch})
+  unsigned* cnt;  // [2]: attention-half and FFN-half phase counters (zero at launch)
   uint2* kvnew;   // [2][nkv][hd] this position's k (rotated) and v rows
   uint2* mlx;     // [nh][S][2] (m, l) of every split
   uint2* tok;     // [1] the step's argmax
@@ -221,44 +222,44 @@ __device__ __forceinline__ float fu_total(float v, float* red, bool is_max) {
   return t;
 }
 
-// Polls flags[0, n) until each carries epoch >= e (one warp, bounded), then a
-// gpu-scope fence; the other consumer warps wait at a named barrier.  False
-// (and the CTA's abort raised) when a flag did not come in time.
-__device__ __noinline__ bool fu_gate(const uint2* flags, int n, unsigned e, volatile int* cabort, DevState* st) {
+// Phase counters: every CTA that finished a phase's global writes (red.add,
+// stores) adds 1 to the phase's counter with release semantics; a reader polls
+// the counter (one lane, relaxed loads, bounded) until it reaches the number of
+// writers so far, then loads it once with acquire semantics, which synchronises
+// with every writer's release (each add continues the release sequence of the
+// ones before it).  The other consumer warps wait at a named barrier, which
+// orders their reads after the acquire.  False (and the CTA's abort raised)
+// when the count did not come in time.  The counters start at zero in every
+// launch, so a target is (blocks so far) * (writers per block).
+__device__ __forceinline__ unsigned ld_rlx_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned ld_acq_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __noinline__ bool fu_gate(const unsigned* cnt, unsigned target, volatile int* cabort, DevState* st) {
   if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    bool ok = true;
-    for (int base = 0; base < n && ok; base += 32 * 8) {
-      uint2 w[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        const int i = base + lane + 32 * k;
-        w[k] = i < n ? ld_ll(flags + i) : make_uint2(0u, e);
-      }
-      unsigned long long t0 = 0;
-      for (;;) {
-        bool all = true;
-#pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          if (int(w[k].y - e) < 0) {
-            all = false;
-            w[k] = ld_ll(flags + base + lane + 32 * k);
+    if (threadIdx.x == 0) {
+      bool ok = true;
+      if (int(ld_rlx_u32(cnt) - target) < 0) {
+        const unsigned long long t0 = global_ns();
+        while (int(ld_rlx_u32(cnt) - target) < 0) {
+          if (global_ns() - t0 > c_wait_ns) {
+            ok = false;
+            break;
           }
         }
-        if (all) break;
-        const unsigned long long t = global_ns();
-        if (!t0) t0 = t;
-        else if (t - t0 > c_wait_ns) {
-          ok = false;
-          break;
-        }
+      }
+      if (ok) (void)ld_acq_u32(cnt);
+      else {
+        flag_timeout(st, 20);
+        *cabort = 1;
       }
     }
-    if (!__all_sync(0xffffffffu, ok) && lane == 0) {
-      flag_timeout(st, 20);
-      *cabort = 1;
-    }
-    fence_acq_rel_gpu();
     __syncwarp();
     bar_arrive_n(3);
   } else {
@@ -266,14 +267,11 @@ __device__ __noinline__ bool fu_gate(const uint2* flags, int n, unsigned e, vola
   }
   return !*cabort;
 }
-// End of a phase whose global writes (red.add, stores) readers wait for: a
-// consumer barrier, then thread 0 fences and raises this CTA's flag.
-__device__ __forceinline__ void fu_publish(uint2* flag, unsigned e) {
+// End of a phase whose global writes readers wait for: a consumer barrier,
+// then thread 0 adds this CTA's 1 to the phase counter (release).
+__device__ __forceinline__ void fu_publish(unsigned* cnt) {
   fu_sync();
-  if (threadIdx.x == 0) {
-    fence_acq_rel_gpu();
-    st_ll(flag, 0.f, e);
-  }
+  if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
 }
 
 // Reads n LL words of epoch e (bounded) into dst (shared memory).
@@ -746,9 +744,8 @@ __device__ __forceinline__ bool fu_lm(const FusedArgs& A, const FuShared& S, int
   __shared__ unsigned long long wbest[kFuConsumerWarps];
   __shared__ int is_last;
   fu_prefetch(S.nw, P.out_norm, d);
-  const unsigned eLastB = fu_epoch(A.epoch0, L, step, L - 1, 1);
   if (trace_row && tid == 0) trace_row[0] = fu_tstamp();
-  if (!fu_gate(A.flags + G, G, eLastB, S.cabort, st)) return false;
+  if (!fu_gate(A.cnt + 1, unsigned((step + 1) * L) * unsigned(G), S.cabort, st)) return false;
   if (trace_row && tid == 0) trace_row[1] = fu_tstamp();
   const int gl = step * L + L - 1;
   fu_add_sum(S.R, S.XA, A.yb + (gl & 1) * d, A.layers[L - 1].down.bias, d, st, pos, c == 0 ? L - 1 : -1);
@@ -878,8 +875,8 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
   int fo0, nfo;  // this CTA's SwiGLU outputs [fo0, fo0 + nfo)
   fu_outs(P.ff, G, c, fo0, nfo);
   const int fkb0 = fo0 / 32, fnblk = nfo > 0 ? (fo0 + nfo - 1) / 32 - fkb0 + 1 : 0;
-  uint2* flA = A.flags;
-  uint2* flB = A.flags + G;
+  unsigned* cntA = A.cnt;
+  unsigned* cntB = A.cnt + 1;
   int item = 0;
   const unsigned pos0 = __ldcg(&st->pos);
   auto fmark = [&](int step, int l, int k) {
@@ -895,7 +892,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
       const LayerW& Lw = A.layers[l];
       const Q4View& Q = Lw.qkv;
       const int gl = step * L + l;
-      const unsigned eA = fu_epoch(A.epoch0, L, step, l, 0), eB = eA + 1u;
+      const unsigned eA = fu_epoch(A.epoch0, L, step, l, 0);
       float* ya = A.ya + (gl & 1) * d;
       float* yb = A.yb + (gl & 1) * d;
       const float* yb_prev = A.yb + ((gl + 1) & 1) * d;  // YB of block l-1
@@ -920,7 +917,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
           const float* src = P.embd + (size_t)(tok % (unsigned)P.V) * d;  // get_row_core: row token % V
           for (int i = tid; i < d; i += kFuConsumers) S.R[i] = __ldg(src + i);
         } else {
-          if (!fu_gate(flB, G, eB - 2u, S.cabort, st)) return;
+          if (!fu_gate(cntB, unsigned(gl) * unsigned(G), S.cabort, st)) return;
           fu_add_sum(S.R, S.XA, yb_prev, dn_bias_prev, d, st, pos, c == 0 ? l - 1 : -1);
         }
         if (roleA) {  // clear the sums read two phases ago: YA of block l-1, YB of block l-2
@@ -1004,7 +1001,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
               red_add2(ya + 2 * p, cf * y.x, cf * y.y);
             }
           if (c == A.withhold && l == 0 && step == 0) fu_sync();  // the readers' waits run out
-          else fu_publish(flA + c, eA);
+          else fu_publish(cntA);
           // the K/V buffer is free: the next block's (or next step's) cached rows,
           // requested off the critical path while the FFN half waits
           if (tid == 0) {
@@ -1018,7 +1015,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
       // ============================================================ phase B
       fu_prefetch(S.nw, Lw.ffn_norm, d);
       if (nfo > 0) fu_prefetch(S.gub, Lw.gate_up.bias ? Lw.gate_up.bias + (size_t)fo0 * 2 : nullptr, nfo * 2);
-      if (!fu_gate(flA, pl.nA, eA, S.cabort, st)) return;
+      if (!fu_gate(cntA, unsigned(gl + 1) * unsigned(pl.nA), S.cabort, st)) return;
       fmark(step, l, 9);
       if (!(roleA || roleKV)) {  // R of this block from the sums of the previous one
         if (l == 0) {
@@ -1075,7 +1072,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
           red_add2(yb + 2 * p, y.x, y.y);
         }
       }
-      fu_publish(flB + c, eB);
+      fu_publish(cntB);
       fmark(step, l, 14);
     }
     // ================================================================ LM
