@@ -1,7 +1,7 @@
 """Decode benchmark for the B200 `.gaje.flat` engine.
 
-Workload, plain `python bench.py` (N=1): the Qwen2-0.5B-shaped model of
-configs[1] -- random-init weights N(0, 0.02) written as `.gaje.flat` v2 by the
+Workload, plain `python bench.py` (N=1): the Qwen2-0.5B-shaped model --
+random-init weights N(0, 0.02) written as `.gaje.flat` v2 by the
 synthetic writer (Q4_0 body, tied FP32 embedding / lm_head), batch 1, a
 256-token uniform-random prompt, then greedy decode.  One "step" is one
 decode step (one token).  K-WTA is off, as
@@ -466,7 +466,7 @@ SWEEP_M = [1, 8, 64, 512]
 
 
 def run_sweep(args) -> None:
-    """the isolated Q4_0 dequant-GEMV/GEMM sweep.  One
+    """The isolated Q4_0 dequant-GEMV/GEMM sweep.  One
     JSON line per (M, N, K): weights N(0, 0.02) quantised by the Q4_0 quantiser,
     activations N(0, 1); each launch timed alone with CUDA events after an L2
     flush (a 256 MB write), median of the timed launches.  GB/s counts the
@@ -507,7 +507,7 @@ def run_sweep(args) -> None:
             # the tensor-core kernel issues three bf16 MMAs per product (hi*hi, hi*lo, lo*hi):
             # its ceiling in useful TFLOP/s is a third of the measured bf16 peak
             tpeak = peaks.get("bf16_tflops", 1.0) / (3.0 if tc else 1.0)
-            line = {"metric": "q4_0 dequant-GEMV/GEMM", "config": {"workload": "configs[2] sweep", "M": M, "N": N,
+            line = {"metric": "q4_0 dequant-GEMV/GEMM", "config": {"workload": "isolated Q4_0 GEMV/GEMM sweep", "M": M, "N": N,
                                                                  "K": K, "l2": "flushed (256 MB write) before each launch"},
                     "us": round(t * 1e6, 2), "gbs": round(gbs, 1), "tflops": round(tfl, 3),
                     "kernel": ("k_gemv<G_PLAIN>" if M == 1 else
@@ -868,14 +868,14 @@ def main():
     ap.add_argument("--no-serving", action="store_true",
                     help="plain N=1 run: skip the serving workload's N=1 measurement (the 'serving' object)")
     ap.add_argument("--batch", type=int, default=0,
-                    help="batched decode of this many streams per GPU (configs[3]/[4] shape) instead of batch 1")
+                    help="batched decode of this many streams per GPU (Qwen2.5-1.5B shape by default) instead of batch 1")
     ap.add_argument("--prompt", type=int, default=PROMPT_LEN, help="prompt tokens per stream (--batch)")
     ap.add_argument("--serve", action="store_true",
-                    help="configs[4]: 512 streams over all ranks, prompts uniform in [64, 1024], LPT-balanced")
+                    help="batched serving: 512 streams over all ranks, prompts uniform in [64, 1024], LPT-balanced")
     ap.add_argument("--prefill-mode", choices=["pass", "steps"], default="pass",
                     help="--batch prompts: one gaje_cuda_prefill pass per stream, or token-by-token batched steps")
     ap.add_argument("--sweep", action="store_true",
-                    help="the isolated Q4_0 GEMV/GEMM sweep of configs[2] instead of the decode benchmark")
+                    help="the isolated Q4_0 GEMV/GEMM sweep instead of the decode benchmark")
     ap.add_argument("--engine", choices=sorted(ENGINES), default="fused",
                     help="batch-1 engine: fused (two exchanges per block, default), mega (five), phase")
     ap.add_argument("--context", type=int, default=0,

@@ -181,7 +181,7 @@ def test_nan_guard_reports_reference_message(g, O, tmp_path, mega):
 @pytest.mark.parametrize("name,steps,mega", [("smollm2-135m", 64, True), ("smollm2-135m", 64, False),
                                              ("qwen2-0.5b", 64, True)])
 def test_baseline_configs_parity(g, O, make_model, name, steps, mega):
-    """The BASELINE shapes: 16 prompt tokens then `steps` greedy steps, logits
+    """The benchmarked model shapes: 16 prompt tokens then `steps` greedy steps, logits
     every step within 1e-3 and the identical greedy stream."""
     path = make_model(name, seed=1234)
     gpu, ref = _pair(g, O, path, max_ctx=512, use_megakernel=mega)
