@@ -124,7 +124,14 @@ struct Q4Dev {
   float* bias = nullptr;
   int N = 0, K = 0, nb = 0, nbp = 0;
   float* lut = nullptr;  // Genomic4Bit centroid tables [N][nb][16] (qs: codes, sm unused)
+  // K-block-major copy for the tensor-core GEMM's weight stream (and the fused
+  // kernel's column passes): qsT[kb][ldT], smT[kb][ldT], ldT = N rounded up to
+  // a multiple of 4; nullptr when the model has no tensor-core path
+  uint4* qsT = nullptr;
+  uint32_t* smT = nullptr;
+  int ldT = 0;
   Q4View view() const { return Q4View{qs, sm, bias, N, K, nb, nbp, lut}; }
+  Q4Rows tc_rows() const { return Q4Rows{view(), qsT, smT, ldT}; }
 };
 
 constexpr int kMaxDynSmem = 227 * 1024;
@@ -1123,10 +1130,10 @@ SkLaunch sk_plan(const gaje_model* m, const Q4Dev& q, int Bi) {
 // RMSNorm fused into the activation staging (w == nullptr: none).
 template <bool NORM, class Epi>
 cudaError_t batch_gemm(gaje_model* m, int Bi, const Q4Dev& q, const float* x, const TcNorm& norm, Epi epi) {
-  if (Bi >= kBatchTcMin && m->btc_hi && q.K % kTcK == 0) {
+  if (Bi >= kBatchTcMin && m->btc_hi && q.K % kTcK == 0 && q.qsT) {
     const TcPlan p = tc_plan(q.N, q.K, Bi, m->sms);
     TcBuffers b{m->btc_hi, m->btc_lo, m->btc_part};
-    return tc_gemm_run(p, Q4Rows{q.view()}, x, Bi, epi, b, m->stream, true, norm, m->st) == GAJE_OK
+    return tc_gemm_run(p, q.tc_rows(), x, Bi, epi, b, m->stream, true, norm, m->st) == GAJE_OK
                ? cudaSuccess
                : cudaErrorLaunchFailure;
   }
@@ -1464,6 +1471,11 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   // ---- plan the arena (sizes only), then allocate and carve for real
   const size_t V = m->V, d = m->d, L = m->L;
   size_t staging_bytes = 0;
+  // the batched engine's tensor-core GEMMs (see the btc_* buffers below) and
+  // the K-block-major weight copies they stream
+  const size_t tc_rows = std::max(std::max(size_t(m->max_streams), size_t(m->pf_rows)),
+                                  size_t(m->nranks) * size_t(m->max_streams));
+  const bool tc_on = m->max_streams > 0 && tc_rows >= size_t(kBatchTcMin);
   auto plan = [&](Arena& a) {
     m->qkv.assign(L, Q4Dev());
     m->wo.assign(L, Q4Dev());
@@ -1485,6 +1497,11 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
         q.sm = refs[k]->lut ? nullptr : a.take<uint32_t>(size_t(q.N) * q.nbp);
         q.lut = refs[k]->lut ? a.take<float>(size_t(q.N) * q.nb * 16) : nullptr;
         q.bias = refs[k]->has_bias ? a.take<float>(q.N) : nullptr;
+        if (tc_on && !refs[k]->lut) {  // the tensor-core GEMMs stream this copy
+          q.ldT = (q.N + 3) / 4 * 4;
+          q.qsT = a.take<uint4>(size_t(q.ldT) * q.nb);
+          q.smT = a.take<uint32_t>(size_t(q.ldT) * q.nb);
+        }
         size_t tot = 0;
         for (const FlatEntry* e : refs[k]->parts) tot += e->dna_len;
         staging_bytes = std::max(staging_bytes, tot);
@@ -1520,10 +1537,12 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
       for (size_t l = 0; l < L; ++l) {
         const Q4Dev& wo = m->wo[l];
         const Q4Dev& dn = m->down[l];
-        m->h_fl[l].wo_qs = a.take<uint4>(size_t(wo.N) * wo.nb);
-        m->h_fl[l].wo_sm = a.take<uint32_t>(size_t(wo.N) * wo.nb);
-        m->h_fl[l].dn_qs = a.take<uint4>(size_t(dn.N) * dn.nb);
-        m->h_fl[l].dn_sm = a.take<uint32_t>(size_t(dn.N) * dn.nb);
+        // the tensor-core copies have the same layout when their rows need no padding
+        const bool share_wo = wo.qsT && wo.ldT == wo.N, share_dn = dn.qsT && dn.ldT == dn.N;
+        m->h_fl[l].wo_qs = share_wo ? wo.qsT : a.take<uint4>(size_t(wo.N) * wo.nb);
+        m->h_fl[l].wo_sm = share_wo ? wo.smT : a.take<uint32_t>(size_t(wo.N) * wo.nb);
+        m->h_fl[l].dn_qs = share_dn ? dn.qsT : a.take<uint4>(size_t(dn.N) * dn.nb);
+        m->h_fl[l].dn_sm = share_dn ? dn.smT : a.take<uint32_t>(size_t(dn.N) * dn.nb);
       }
       m->d_fl = a.take<FuLayer>(L);
       m->fya = a.take<float>(4 * d);
@@ -1729,12 +1748,19 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
     for (size_t l = 0; l < L; ++l) lw[l] = m->layer(int(l));
     CK(cudaMemcpy(m->d_layers, lw.data(), L * sizeof(LayerW), cudaMemcpyHostToDevice));
   }
-  if (m->fu_ok) {  // K-block-major copies of attn_output and ffn_down
+  for (size_t l = 0; l < L; ++l) {  // K-block-major copies for the tensor-core GEMMs' weight streams
+    for (Q4Dev* q : {&m->qkv[l], &m->wo[l], &m->gate_up[l], &m->down[l]})
+      if (q->qsT) k_q4_kbmajor<<<m->sms * 4, 256, 0, m->stream>>>(q->view(), q->qsT, q->smT, q->ldT);
+  }
+  CK(cudaGetLastError());
+  if (m->fu_ok) {  // K-block-major copies of attn_output and ffn_down (shared with the above when made)
     for (size_t l = 0; l < L; ++l) {
-      k_q4_kbmajor<<<m->sms * 4, 256, 0, m->stream>>>(m->wo[l].view(), const_cast<uint4*>(m->h_fl[l].wo_qs),
-                                                      const_cast<uint32_t*>(m->h_fl[l].wo_sm));
-      k_q4_kbmajor<<<m->sms * 4, 256, 0, m->stream>>>(m->down[l].view(), const_cast<uint4*>(m->h_fl[l].dn_qs),
-                                                      const_cast<uint32_t*>(m->h_fl[l].dn_sm));
+      if (!m->wo[l].qsT)
+        k_q4_kbmajor<<<m->sms * 4, 256, 0, m->stream>>>(m->wo[l].view(), const_cast<uint4*>(m->h_fl[l].wo_qs),
+                                                        const_cast<uint32_t*>(m->h_fl[l].wo_sm), m->wo[l].N);
+      if (!m->down[l].qsT)
+        k_q4_kbmajor<<<m->sms * 4, 256, 0, m->stream>>>(m->down[l].view(), const_cast<uint4*>(m->h_fl[l].dn_qs),
+                                                        const_cast<uint32_t*>(m->h_fl[l].dn_sm), m->down[l].N);
     }
     CK(cudaGetLastError());
     CK(cudaMemcpyAsync(m->d_fl, m->h_fl.data(), L * sizeof(FuLayer), cudaMemcpyHostToDevice, m->stream));
@@ -2505,10 +2531,13 @@ gaje_q4_matrix* gaje_cuda_q4_0_upload(const uint8_t* blocks, size_t N, size_t K,
   h->device = device;
   const size_t nb = K / 32, nbp = (nb + 3) / 4 * 4, nblk = N * nb;
   uint32_t* raw = nullptr;
+  const size_t ldT = (N + 3) / 4 * 4;
   auto carve = [&](Arena& ar) {
     h->m.qs = ar.take<uint4>(nblk);
     h->m.sm = ar.take<uint32_t>(N * nbp);
     h->m.bias = bias ? ar.take<float>(N) : nullptr;
+    h->m.qsT = ar.take<uint4>(ldT * nb);  // the tensor-core path's weight stream (M >= 16)
+    h->m.smT = ar.take<uint32_t>(ldT * nb);
     raw = ar.take<uint32_t>(nblk * 5);
   };
   Arena a;
@@ -2524,6 +2553,7 @@ gaje_q4_matrix* gaje_cuda_q4_0_upload(const uint8_t* blocks, size_t N, size_t K,
   h->m.K = int(K);
   h->m.nb = int(nb);
   h->m.nbp = int(nbp);
+  h->m.ldT = int(ldT);
   if (cudaMemcpy(raw, blocks, nblk * 20, cudaMemcpyHostToDevice) != cudaSuccess ||
       cudaMemset(h->m.sm, 0, N * nbp * 4) != cudaSuccess ||
       (bias && cudaMemcpy(h->m.bias, bias, N * 4, cudaMemcpyHostToDevice) != cudaSuccess)) {
@@ -2533,6 +2563,7 @@ gaje_q4_matrix* gaje_cuda_q4_0_upload(const uint8_t* blocks, size_t N, size_t K,
   }
   k_repack_q4<<<int(std::min<size_t>((nblk + 255) / 256, 8192)), 256>>>(raw, int(N), int(nb), int(nbp), 0, 0, 0,
                                                                         h->m.qs, h->m.sm);
+  k_q4_kbmajor<<<int(std::min<size_t>((nblk + 255) / 256, 8192)), 256>>>(h->m.view(), h->m.qsT, h->m.smT, int(ldT));
   if (cudaDeviceSynchronize() != cudaSuccess) {
     cudaFree(h->mem);
     set_error(GAJE_ERR_CUDA, "repack failed");
@@ -2630,7 +2661,7 @@ int gaje_cuda_q4_0_gemv(const gaje_q4_matrix* h, const float* x, float* y, size_
     tb.part = reinterpret_cast<float*>(ws);
     tb.hi = reinterpret_cast<unsigned char*>(ws + part_b);
     tb.lo = tb.hi + plane;
-    return tc_gemm_run(p, Q4Rows{h->m.view()}, x, int(M), EpiStore{y, h->m.N}, tb, s, false, TcNorm{});
+    return tc_gemm_run(p, h->m.tc_rows(), x, int(M), EpiStore{y, h->m.N}, tb, s, false, TcNorm{});
   }
   // 1 < M < 16: every weight word is turned into floats once per CTA for 8
   // vectors; the CTA walks the K splits itself (no workspace)

@@ -1177,13 +1177,14 @@ __host__ __device__ inline size_t fused_smem_bytes(const FusedPlan& p, int d, in
 }
 
 // K-block-major copy of a row-major Q4 matrix: qsT[kb][row] = qs[row][kb],
-// smT[kb][row] = sm[row][kb].
-__global__ void k_q4_kbmajor(Q4View W, uint4* qsT, uint32_t* smT) {
+// smT[kb][row] = sm[row][kb], rows ld apart (ld >= N; rows N..ld-1 are not
+// written).
+__global__ void k_q4_kbmajor(Q4View W, uint4* qsT, uint32_t* smT, int ld) {
   const size_t n = (size_t)W.N * W.nb;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
     const int kb = int(i / W.N), row = int(i - (size_t)kb * W.N);
-    qsT[i] = W.qs[(size_t)row * W.nb + kb];
-    smT[i] = W.sm[(size_t)row * W.nbp + kb];
+    qsT[(size_t)kb * ld + row] = W.qs[(size_t)row * W.nb + kb];
+    smT[(size_t)kb * ld + row] = W.sm[(size_t)row * W.nbp + kb];
   }
 }
 

@@ -20,11 +20,12 @@
 // contiguous run per plane, fetched by a 1-D TMA bulk copy.
 //
 // CTA: 128 weight rows (the MMA's M) x NT vectors (its N), S stages of 32 K
-// (one Q4 block per row; S = 4 at NT = 256, up to 8 for narrower tiles).
+// (one Q4 block per row; S = 4 at NT = 256, 4-6 for narrower tiles).
 // Warp roles, each waiting only on the barriers it consumes:
 // - warps 0-7 make the A tiles (two threads per weight row) and arrive on
-//   a_full; for Q4 they dequantise raw words that warp 10 streams through a
-//   shared-memory ring with cp.async, kTcRawStages stages ahead;
+//   a_full; for Q4 they dequantise raw words that lane 0 of warp 10 streams
+//   from the K-block-major copy of the matrix through a shared-memory ring
+//   with TMA bulk copies, tc_raw_stages(NT) stages ahead;
 // - warp 8 lane 0 issues a stage's 2 k-steps x 3 MMAs once a_full and b_full
 //   are complete and commits them to the stage's `done` barrier;
 // - warp 9 lane 0 issues the activation copies of a stage (b_full, transaction
@@ -58,18 +59,24 @@ constexpr unsigned kTcKidTimeout = 15;
 __host__ __device__ constexpr size_t tc_stage_bytes(int nt) {
   return size_t(2) * kTcRows * kTcK * 2 + size_t(2) * nt * kTcK * 2;  // A hi/lo + B hi/lo (bf16)
 }
-// As many stages as fit 200 KB, at most 8: at 256 vectors a stage is 48 KB
-// (four in flight), at 16 vectors 18 KB.
-__host__ __device__ constexpr int tc_stages(int nt) {
-  return int((200 * 1024) / tc_stage_bytes(nt)) > 8 ? 8 : int((200 * 1024) / tc_stage_bytes(nt));
-}
 // Raw Q4 words of one stage (128 rows x 16 B nibbles + 128 x 4 B scale/min),
-// kTcRawStages of them in flight ahead of the dequantising warps.
-constexpr int kTcRawStages = 8;
+// tc_raw_stages(NT) of them in flight ahead of the dequantising warps.  A
+// narrow tile has little MMA work per stage, so its weight stream must run
+// further ahead to cover the HBM latency: 8 slots (20 KB) at 256 vectors,
+// 40 (100 KB) at 16-32.
 constexpr int kTcRawSlot = kTcRows * 20;
-__host__ __device__ constexpr size_t tc_smem_bytes(int nt) {  // 1 KB header (barriers, TMEM address)
-  return 1024 + size_t(tc_stages(nt)) * tc_stage_bytes(nt) + size_t(kTcRawStages) * kTcRawSlot;
+__host__ __device__ constexpr int tc_raw_stages(int nt) { return nt >= 256 ? 8 : nt >= 128 ? 24 : nt >= 64 ? 32 : 40; }
+// MMA stages: as many as fit beside the raw ring in 213 KB, at most 8 (four
+// at 256 vectors, a stage is 48 KB there; six at 16 vectors, 18 KB).
+__host__ __device__ constexpr int tc_stages(int nt) {
+  return int((213 * 1024 - 1024 - tc_raw_stages(nt) * kTcRawSlot) / tc_stage_bytes(nt)) > 8
+             ? 8
+             : int((213 * 1024 - 1024 - tc_raw_stages(nt) * kTcRawSlot) / tc_stage_bytes(nt));
 }
+__host__ __device__ constexpr size_t tc_smem_bytes(int nt) {  // 1 KB header (barriers, TMEM address)
+  return 1024 + size_t(tc_stages(nt)) * tc_stage_bytes(nt) + size_t(tc_raw_stages(nt)) * kTcRawSlot;
+}
+static_assert(3 * 8 + 2 * 40 <= 126, "the barriers and the TMEM address fit the 1 KB header");
 __host__ __device__ constexpr int tc_tmem_cols(int nt) { return nt < 32 ? 32 : nt; }
 // Bytes of one bf16 plane of split activations for Mpad rows x K.
 __host__ __device__ inline size_t tc_plane_bytes(int mpad, int K) { return size_t(mpad) * K * 2; }
@@ -165,18 +172,23 @@ __host__ __device__ __forceinline__ size_t tc_xoff(int r, int c, int mpad) {
   return ((size_t(c / kTcChunks) * (mpad >> 3) + (r >> 3)) * kTcChunks + (c % kTcChunks)) * 128 + (r & 7) * 16;
 }
 
-// Weight sources of the A operand.  Q4Rows (kRawRing): the loader warp
-// copies each stage's raw words (one Q4 block of each of the 128 rows, four
-// rows per lane) into a shared-memory ring kTcRawStages deep with cp.async,
-// tracked by an mbarrier; warps 0-7 dequantise them into the A tiles, two
-// threads per row (half a block each).  The converters issue no global
+// Weight sources of the A operand.  Q4Rows (kRawRing): the loader lane
+// copies each stage's raw words (one Q4 block of each of the 128 rows) from
+// the K-block-major copy of the matrix -- qsT[kb][row], smT[kb][row], rows
+// ld apart, so a stage is one contiguous run of each -- into a shared-memory
+// ring tc_raw_stages(NT) deep with two 1-D TMA bulk copies, tracked by an
+// mbarrier; warps 0-7 dequantise them into the A tiles, two threads per row
+// (half a block each).  The converters issue no global
 // loads, so the proxy fence that publishes their tile writes to the tensor
 // cores waits on nothing else.  F32Rows: a thread owns 16 consecutive
 // elements (half h of a 32-element block) of one row per stage, kDepth
 // stages ahead in registers.
 struct Q4Rows {  // Q4_0: w = fma(q, scale, min) (genomic.rs:267-336)
   Q4View W;
-  static constexpr bool kRawRing = true;  // words staged through shared memory by the loader warp
+  const uint4* qsT;     // [nb][ld] 16-byte nibble words, K-block major
+  const uint32_t* smT;  // [nb][ld] scale | min << 16
+  int ld;               // rows of a K block in qsT / smT: N rounded up to a multiple of 4
+  static constexpr bool kRawRing = true;  // words staged through shared memory by the loader lane
   struct Regs {
     uint2 q;
     uint32_t s;
@@ -184,10 +196,15 @@ struct Q4Rows {  // Q4_0: w = fma(q, scale, min) (genomic.rs:267-336)
   __host__ __device__ __forceinline__ int N() const { return W.N; }
   __host__ __device__ __forceinline__ int K() const { return W.K; }
   __host__ __device__ __forceinline__ const float* bias() const { return W.bias; }
-  // row r's block blk into raw slot row rl (asynchronous copies of the issuing thread)
-  __device__ __forceinline__ void copy_raw(unsigned char* slot, int rl, int r, int blk) const {
-    cp_async16(slot + rl * 16, W.qs + (size_t)r * W.nb + blk);
-    cp_async4(slot + kTcRows * 16 + rl * 4, W.sm + (size_t)r * W.nbp + blk);
+  // rows [row0, row0 + 128) of block blk into a raw slot: slot rows past ld
+  // keep whatever they held (their outputs are dropped); both runs start on
+  // 16-byte boundaries and are multiples of 16 bytes (ld % 4 == 0)
+  __device__ __forceinline__ void issue_raw(unsigned char* slot, int row0, int blk, uint64_t* bar) const {
+    const int rows = min(kTcRows, ld - row0);
+    const size_t o = (size_t)blk * ld + row0;
+    mbar_expect_tx(bar, uint32_t(rows) * 20u);
+    bulk_g2s(slot, qsT + o, uint32_t(rows) * 16u, bar);
+    bulk_g2s(slot + kTcRows * 16, smT + o, uint32_t(rows) * 4u, bar);
   }
   // half h (16 elements) of slot row rl
   __device__ __forceinline__ void read_raw(Regs& g, const unsigned char* slot, int rl, int h) const {
@@ -330,9 +347,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(WS W, const unsign
   uint64_t* a_full = reinterpret_cast<uint64_t*>(tc_smem);  // [S] 128 producer arrivals
   uint64_t* b_full = a_full + S;                             // [S] activation copies landed
   uint64_t* done = b_full + S;                               // [S] MMAs of the stage complete
-  uint64_t* raw_full = done + S;                             // [kTcRawStages] raw words landed
-  uint64_t* raw_empty = raw_full + kTcRawStages;             // [kTcRawStages] raw words read
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tc_smem + 512);
+  constexpr int R = tc_raw_stages(NT);
+  uint64_t* raw_full = done + S;                             // [R] raw words landed
+  uint64_t* raw_empty = raw_full + R;                        // [R] raw words read
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tc_smem + 1016);
   unsigned char* stage0 = tc_smem + 1024;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int row0 = blockIdx.x * kTcRows, m0 = blockIdx.y * NT;
@@ -353,8 +371,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(WS W, const unsign
       mbar_init(b_full + s, 1);
       mbar_init(done + s, 1);
     }
-    for (int s = 0; s < kTcRawStages; ++s) {
-      mbar_init(raw_full + s, 32);             // one (asynchronous) arrival per loader lane
+    for (int s = 0; s < R; ++s) {
+      mbar_init(raw_full + s, 1);              // the loader lane's arrival with the copies' bytes
       mbar_init(raw_empty + s, kTcProducers);  // one per converter thread
     }
     fence_mbar_init();
@@ -374,12 +392,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(WS W, const unsign
       pdl_wait();
       pdl_trigger();
       for (int i = 0; i < n; ++i) {
-        const int s = i % S, slot = i % kTcRawStages;
+        const int s = i % S, slot = i % R;
         if (i >= S && !(ok = mbar_wait(done + s, ((i / S) - 1) & 1))) break;  // the stage's previous MMAs
-        if (!(ok = mbar_wait(raw_full + slot, (i / kTcRawStages) & 1))) break;
+        if (!(ok = mbar_wait(raw_full + slot, (i / R) & 1))) break;
         typename WS::Regs g;
         W.read_raw(g, raw0 + slot * kTcRawSlot, rl, h);
-        mbar_arrive(raw_empty + slot);
         unsigned char* A_hi = stage0 + s * tc_stage_bytes(NT);
         unsigned char* A_lo = A_hi + kA;
 #pragma unroll
@@ -392,6 +409,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(WS W, const unsign
           *reinterpret_cast<uint4*>(A_hi + off) = hi;
           *reinterpret_cast<uint4*>(A_lo + off) = lo;
         }
+        // the slot is released only once its words have been used: the next TMA
+        // copy into it (asynchronous proxy) must not overtake a read still in flight
+        mbar_arrive(raw_empty + slot);
         fence_async_smem();  // these generic-proxy writes, visible to the tensor cores
         mbar_arrive(a_full + s);
       }
@@ -438,21 +458,21 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_q4_gemm_tc(WS W, const unsign
       }
     }
   } else if (wid == kTcLoadWarp) {
-    // ---------------- loader warp (Q4): lane l copies rows l, l+32, l+64, l+96 of each stage's
-    // block up to kTcRawStages stages ahead; weights never depend on the previous kernel
+    // ---------------- loader lane (Q4): each stage's block of the 128 rows, up to
+    // R stages ahead; weights never depend on the previous kernel
     if constexpr (WS::kRawRing) {
-      unsigned char* raw0 = stage0 + S * tc_stage_bytes(NT);
-      for (int j = 0; j < n; ++j) {
-        const int slot = j % kTcRawStages;
-        if (j >= kTcRawStages && !(ok = mbar_wait(raw_empty + slot, ((j / kTcRawStages) - 1) & 1))) break;
-#pragma unroll
-        for (int q = 0; q < kTcRows / 32; ++q) {  // rows past N: whatever the slot holds, their outputs are dropped
-          const int rl = lane + 32 * q;
-          if (row0 + rl < W.N()) W.copy_raw(raw0 + slot * kTcRawSlot, rl, row0 + rl, kb + j);
+      if (lane == 0) {
+        unsigned char* raw0 = stage0 + S * tc_stage_bytes(NT);
+        int j = 0;
+        for (; j < n; ++j) {
+          const int slot = j % R;
+          if (j >= R && !(ok = mbar_wait(raw_empty + slot, ((j / R) - 1) & 1))) break;
+          W.issue_raw(raw0 + slot * kTcRawSlot, row0, kb + j, raw_full + slot);
         }
-        cp_async_mbar_arrive(raw_full + slot);
+        // none of these copies may still land in shared memory when the CTA
+        // exits: wait (bounded) for the latest copy of every slot used
+        for (int t = j - 1; t >= 0 && t >= j - R; --t) mbar_wait(raw_full + t % R, (t / R) & 1);
       }
-      cp_async_wait_all();  // none of this lane's copies still lands in shared memory
     }
     pdl_wait();
     pdl_trigger();
