@@ -911,10 +911,11 @@ bool plan_fused(gaje_model* m) {
   const int s_cta = (G - 2 * m->nkv) / m->nh;
   if (s_cta < 1) return false;
   const int cached = std::max(1, m->max_ctx - 1);
-  p.S = std::min({s_cta, kFuMaxSplits, std::max(1, (cached + 63) / 64)});
+  // splits of ~48 cached positions, plus the one that takes this position's row
+  p.S = std::min({s_cta, kFuMaxSplits, std::max(1, (cached + 47) / 48 + 1)});
   p.nA = m->nh * p.S;
   p.nKV = 2 * m->nkv;
-  p.cap = (cached + p.S - 1) / p.S + 1;
+  p.cap = (cached + std::max(1, p.S - 1) - 1) / std::max(1, p.S - 1) + 1;  // fu_split's largest chunk + this row
   p.pv_groups = std::max(1, kFuConsumers / hd);
   p.ob_max = 0;
   p.cb_max = 1;

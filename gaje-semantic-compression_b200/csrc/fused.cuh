@@ -149,9 +149,19 @@ __host__ __device__ inline void fu_outs(int ff, int grid, int c, int& u0, int& n
   n = base + (c >= first_extra ? 1 : 0);
   u0 = c * base + (c > first_extra ? c - first_extra : 0);
 }
-// Cached positions of split s when `cached` positions precede this one.
+// Cached positions of split s when `cached` positions precede this one.  The
+// last split also takes this position's row, which it has to wait for (the
+// KV CTAs compute it in the same phase), so with more than one split it takes
+// that row only and the others share the cached positions: its wait then
+// overlaps their longer chunks instead of adding to a full one.
 __host__ __device__ inline void fu_split(int cached, int S, int s, int& t0, int& n_old) {
-  const int chunk = (cached + S - 1) / S;
+  if (S > 1 && s == S - 1) {
+    t0 = cached;
+    n_old = 0;
+    return;
+  }
+  const int P = S > 1 ? S - 1 : 1;
+  const int chunk = (cached + P - 1) / P;
   t0 = s * chunk;
   n_old = max(0, min(chunk, cached - t0));
 }
