@@ -246,7 +246,7 @@ __device__ __forceinline__ void attn_combine(const float* part_o, const float* p
 }
 
 template <int VEC>
-__global__ void __launch_bounds__(kAbThreads) k_attn_batch2(AttnBatchArgs B) {
+__global__ void __launch_bounds__(kAbThreads, 2) k_attn_batch2(AttnBatchArgs B) {
   constexpr int HD = 32 * VEC;
   extern __shared__ __align__(128) unsigned char ab_smem[];
   uint64_t* full = reinterpret_cast<uint64_t*>(ab_smem);  // [kAbStages]
