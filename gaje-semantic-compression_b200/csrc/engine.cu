@@ -662,7 +662,7 @@ struct gaje_model {
       attr[0].val.cooperative = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      CK(cudaLaunchKernelEx(&cfg, k_decode_fused, a));
+      CK(cudaLaunchKernelEx(&cfg, fused_kernel(hd, a.trace != nullptr), a));
       n -= size_t(chunk);
     }
     const int kk = logits_k();
@@ -902,9 +902,13 @@ int q8_row_bytes(int d) { return (d + 2 * (d / 32) + 15) / 16 * 16; }
 
 bool plan_fused(gaje_model* m) {
   cudaFuncAttributes fa{};
-  if (cudaFuncGetAttributes(&fa, k_decode_fused) != cudaSuccess) return false;
   const int d = m->d, hd = m->hd, G = m->sms;
   if (d % 32 || (hd != 32 && hd != 64 && hd != 128) || m->ff % 32 || m->info.use_genomic_norm) return false;
+  cudaFuncAttributes ft{};
+  if (cudaFuncGetAttributes(&fa, fused_kernel(hd, false)) != cudaSuccess ||
+      cudaFuncGetAttributes(&ft, fused_kernel(hd, true)) != cudaSuccess)
+    return false;
+  fa.sharedSizeBytes = std::max(fa.sharedSizeBytes, ft.sharedSizeBytes);
   if (m->qkv[0].K != d || m->gate_up[0].K != d || m->wo[0].N != d || m->down[0].N != d) return false;
   if (m->wo[0].K != m->nh * hd || m->down[0].K != m->ff) return false;
   FusedPlan& p = m->fplan;
@@ -1646,9 +1650,12 @@ int load_impl(gaje_model* m, const char* path, const gaje_load_opts* opts) {
   if (int s = smem_optin((const void*)k_lmhead, m->lm_smem)) return s;
   m->use_mega = m->nranks == 1 && !m->has_lut && (!opts || opts->use_megakernel) && plan_mega(m);
   if (m->fu_ok) {
-    if (int s = smem_optin((const void*)k_decode_fused, m->fused_smem)) return s;
-    int per_sm = 0, coop = 0;
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_fused, kFuThreads, m->fused_smem));
+    if (int s = smem_optin((const void*)fused_kernel(m->hd, false), m->fused_smem)) return s;
+    if (int s = smem_optin((const void*)fused_kernel(m->hd, true), m->fused_smem)) return s;
+    int per_sm = 0, per_sm_t = 0, coop = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fused_kernel(m->hd, false), kFuThreads, m->fused_smem));
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_t, fused_kernel(m->hd, true), kFuThreads, m->fused_smem));
+    per_sm = std::min(per_sm, per_sm_t);
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, m->device);
     m->use_fused = per_sm >= 1 && coop;
     CK(cudaMemsetAsync(m->fwords, 0, m->fwords_n * sizeof(uint2), m->stream));

@@ -134,6 +134,9 @@ constexpr int kFuTrace = 24;
 // in the lm_head row of step 0 (slots 22, 23) and of the last step (slots 20,
 // 21), from which the host maps its cycles onto the global nanosecond clock.
 __device__ __forceinline__ unsigned long long fu_tstamp() { return (unsigned long long)clock64(); }
+// The trace buffer of an instantiation: compiled out (a constant null) unless TRACE.
+template <bool TRACE>
+__device__ __forceinline__ unsigned long long* fu_trace(const FusedArgs& A) { return TRACE ? A.trace : nullptr; }
 
 __host__ __device__ inline unsigned fu_epoch(unsigned e0, int L, int step, int l, int ph) {
   return e0 + unsigned(step) * unsigned(2 * L + 1) + unsigned(2 * l + ph) + 1u;
@@ -504,6 +507,7 @@ __device__ __forceinline__ void fu_kv_prefetch(const FusedArgs& A, const FuShare
 // projection's NaN guards of block/forward.rs:128-140 are raised.
 __device__ __forceinline__ void fu_add_sum(float* dst, const float* base, const float* sum, const float* bias, int d,
                                         DevState* st, unsigned pos, int nan_layer) {
+#pragma unroll 1
   for (int i0 = threadIdx.x; i0 < d; i0 += 2 * kFuConsumers) {
     const int i1 = i0 + kFuConsumers;
     const float s0 = __ldcg(sum + i0), s1 = i1 < d ? __ldcg(sum + i1) : 0.f;
@@ -523,28 +527,41 @@ __device__ __forceinline__ void fu_add_sum(float* dst, const float* base, const 
   }
 }
 
+// The block-input and normed-output NaN guards of block/forward.rs:11-13,
+// :22-24 over this thread's elements.  Out of line: it only runs when one of
+// them can fire.
+__device__ __noinline__ void fu_norm_guard(const float* x, const float* nw, int d, float inv, DevState* st,
+                                           unsigned pos, int layer) {
+  for (int i = threadIdx.x; i < d; i += kFuConsumers) {
+    const float v = x[i];
+    if (v != v) nan_flag(st, pos, layer, kNanInput);
+    const float nv = (v * inv) * nw[i];
+    if (nv != nv) nan_flag(st, pos, layer, kNanAttnNorm);
+  }
+}
+
 // Stages x * nw into xs/xsum for the row GEMVs and returns 1/rms of x (the
-// scale of the finished row dots), with the block-input and normed-output NaN
-// guards of block/forward.rs:11-13, :22-24 when guard.
+// scale of the finished row dots), with the NaN guards when guard.  An input
+// or normed output of this thread can only be NaN when the sum of squares or
+// 1/rms is not finite (a non-finite x makes it so) or one of its norm weights
+// is not: otherwise |x * inv| <= sqrt(d) and the product with a finite weight
+// is a number, so the element checks are skipped.
 __device__ __forceinline__ float fu_stage_norm(const float* x, const float* nw, int d, float eps, float* xs,
                                             float* xsum, float* red, bool guard, DevState* st, unsigned pos,
                                             int layer) {
   float ss = 0.f;
+  bool wbad = false;
 #pragma unroll 1
   for (int i = threadIdx.x; i < d; i += kFuConsumers) {  // whole warps: d % 32 == 0
-    const float v = x[i];
+    const float v = x[i], w = nw[i];
     ss = fmaf(v, v, ss);
-    mk_stage_elem(xs, xsum, i, v * nw[i]);
+    wbad |= !(fabsf(w) <= 3.402823466e38f);
+    mk_stage_elem(xs, xsum, i, v * w);
   }
   const float tot = fu_total(ss, red, false);
   const float inv = 1.0f / sqrtf(tot / (float)d + eps);
-  if (guard)
-    for (int i = threadIdx.x; i < d; i += kFuConsumers) {
-      const float v = x[i];
-      if (v != v) nan_flag(st, pos, layer, kNanInput);
-      const float nv = (v * inv) * nw[i];
-      if (nv != nv) nan_flag(st, pos, layer, kNanAttnNorm);
-    }
+  if (guard && (wbad || !(tot <= 3.402823466e38f) || !(inv <= 3.402823466e38f)))
+    fu_norm_guard(x, nw, d, inv, st, pos, layer);
   return inv;
 }
 
@@ -570,7 +587,13 @@ __device__ __forceinline__ bool fu_token(const FusedArgs& A, int step, unsigned&
 
 // Loads n floats of global memory into shared memory (zeros without src).
 __device__ __forceinline__ void fu_prefetch(float* dst, const float* src, int n) {
-  for (int i = threadIdx.x; i < n; i += kFuConsumers) dst[i] = src ? __ldg(src + i) : 0.f;
+#pragma unroll 1
+  for (int i0 = threadIdx.x; i0 < n; i0 += 2 * kFuConsumers) {  // both loads in flight together
+    const int i1 = i0 + kFuConsumers;
+    const float a = src ? __ldg(src + i0) : 0.f, b = (src && i1 < n) ? __ldg(src + i1) : 0.f;
+    dst[i0] = a;
+    if (i1 < n) dst[i1] = b;
+  }
 }
 
 // The attention of split sp of head h at position pos (q in S.qbuf), by one
@@ -581,7 +604,7 @@ __device__ __forceinline__ void fu_prefetch(float* dst, const float* src, int n)
 // each lane forms its partial dot for every position of the group and one
 // butterfly reduce-scatter leaves position i's dot in lane i.  Returns the
 // split's position count, or -1 when a wait ran out (the CTA's abort raised).
-template <int VEC>
+template <int VEC, bool TRACE>
 __device__ __forceinline__ int fu_attend_warp(const FusedArgs& A, const FuShared& S, int l, int step, unsigned pos,
                                               int h, int sp, unsigned eA) {
   const StepParams& P = A.P;
@@ -589,8 +612,8 @@ __device__ __forceinline__ int fu_attend_warp(const FusedArgs& A, const FuShared
   DevState* st = P.st;
   constexpr int HD = 32 * VEC;
   const int lane = threadIdx.x & 31, L = P.n_layers;
-  unsigned long long* trow = A.trace ? A.trace + (((size_t)blockIdx.x * A.n_steps + step) * (L + 1) + l) * kFuTrace
-                                     : nullptr;
+  unsigned long long* const tr = fu_trace<TRACE>(A);
+  unsigned long long* trow = tr ? tr + (((size_t)blockIdx.x * A.n_steps + step) * (L + 1) + l) * kFuTrace : nullptr;
   if (trow && lane == 0) trow[16] = fu_tstamp();  // trace point 16: the split's attention starts
   int t0, n_old;
   fu_split(int(pos), pl.S, sp, t0, n_old);
@@ -735,6 +758,7 @@ __device__ __forceinline__ void fu_split_weight(const FusedArgs& A, const FuShar
   }
   const float M = warp_max(ms);
   float wsum = 0.f;
+#pragma unroll 1
   for (int k = 0; k < pl.S; ++k) {  // split order
     const float mk = __shfl_sync(0xffffffffu, ms, k), lk = __shfl_sync(0xffffffffu, ls, k);
     if (mk > -INFINITY) wsum = fmaf(expf(mk - M), lk, wsum);
@@ -744,6 +768,7 @@ __device__ __forceinline__ void fu_split_weight(const FusedArgs& A, const FuShar
 
 // output_norm + this CTA's lm_head rows (ring stages) + argmax; the last CTA
 // to finish publishes the step's token.  Returns false on an abort.
+template <bool TRACE>
 __device__ __forceinline__ bool fu_lm(const FusedArgs& A, const FuShared& S, int step, unsigned pos, int* item_io,
                                    unsigned long long* trace_row) {
   const StepParams& P = A.P;
@@ -871,6 +896,7 @@ __device__ __forceinline__ bool fu_lm(const FusedArgs& A, const FuShared& S, int
   return true;
 }
 
+template <int HD, bool TRACE>
 __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
   const StepParams& P = A.P;
   const FusedPlan& pl = A.plan;
@@ -889,9 +915,9 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
   unsigned* cntB = A.cnt + 1;
   int item = 0;
   const unsigned pos0 = __ldcg(&st->pos);
+  unsigned long long* const trace = fu_trace<TRACE>(A);
   auto fmark = [&](int step, int l, int k) {
-    if (A.trace && tid == 0)
-      A.trace[(((size_t)c * A.n_steps + step) * (L + 1) + l) * kFuTrace + k] = fu_tstamp();
+    if (trace && tid == 0) trace[(((size_t)c * A.n_steps + step) * (L + 1) + l) * kFuTrace + k] = fu_tstamp();
   };
   if (roleA && tid == 0) fu_kv_prefetch(A, S, 0, int(pos0));  // step 0, block 0
   for (int step = 0; step < A.n_steps; ++step) {
@@ -912,6 +938,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
         fmark(step, l, 0);
         // constants of the phase while the input is in flight
         fu_prefetch(S.nw, Lw.attn_norm, d);
+#pragma unroll 1
         for (int i = tid; i < half; i += kFuConsumers)
           reinterpret_cast<float2*>(S.rb)[i] = __ldg(P.rope + (size_t)pos * half + i);
         fu_prefetch(S.rb + hd, Q.bias ? Q.bias + qrow0 : nullptr, hd);
@@ -925,6 +952,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
           fu_sync();
           if (*S.cabort) return;
           const float* src = P.embd + (size_t)(tok % (unsigned)P.V) * d;  // get_row_core: row token % V
+#pragma unroll 1
           for (int i = tid; i < d; i += kFuConsumers) S.R[i] = __ldg(src + i);
         } else {
           if (!fu_gate(cntB, unsigned(gl) * unsigned(G), S.cabort, st)) return;
@@ -932,6 +960,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
         }
         if (roleA) {  // clear the sums read two phases ago: YA of block l-1, YB of block l-2
           const int per = (d + pl.nA - 1) / pl.nA;
+#pragma unroll 1
           for (int i = tid; i < per; i += kFuConsumers) {
             const int j = c * per + i;
             if (j < d) {
@@ -979,10 +1008,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
         fmark(step, l, 3);
         if (roleA) {
           if (wid == 0) {
-            int na = -1;
-            if (hd == 32) na = fu_attend_warp<1>(A, S, l, step, pos, h, sp, eA);
-            else if (hd == 64) na = fu_attend_warp<2>(A, S, l, step, pos, h, sp, eA);
-            else na = fu_attend_warp<4>(A, S, l, step, pos, h, sp, eA);
+            const int na = fu_attend_warp<HD / 32, TRACE>(A, S, l, step, pos, h, sp, eA);
             if (lane == 0) reinterpret_cast<int*>(S.misc)[41] = na;
           }
           fu_sync();
@@ -992,24 +1018,25 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
           const unsigned char* wslot = fu_wait_slot(A, S, item);
           fu_sync();
           if (*S.cabort) return;
-          // the head's split weight: by the last warp while the others run the
-          // output projection when it has no rows of it (d/2 <= 448), else after
-          const bool sw_overlap = d / 2 <= (kFuConsumerWarps - 1) * 32;
-          if (sw_overlap && wid == kFuConsumerWarps - 1) fu_split_weight(A, S, pos, h, n, eA);
-          else if (n > 0) fu_cols(wslot, d, hd / 32, S.ost, S.ost + hd, S.ycol, true);
+          // the head's split weight, by the last warp: it has no rows of the
+          // output projection when d/2 <= 448 (the weight overlaps the column
+          // pass), else it takes its rows after the weight
+          if (wid == kFuConsumerWarps - 1) fu_split_weight(A, S, pos, h, n, eA);
+          if (n > 0) fu_cols(wslot, d, hd / 32, S.ost, S.ost + hd, S.ycol, true);
           fu_release(A, S, item++);
           fmark(step, l, 6);
-          if (!sw_overlap && wid == 0) fu_split_weight(A, S, pos, h, n, eA);
           fmark(step, l, 15);
           fu_sync();
           if (*S.cabort) return;
           const float cf = S.misc[32];
           fmark(step, l, 7);
-          if (n > 0)
+          if (n > 0) {
+#pragma unroll 1
             for (int p = tid; p < d / 2; p += kFuConsumers) {
               const float2 y = reinterpret_cast<const float2*>(S.ycol)[p];
               red_add2(ya + 2 * p, cf * y.x, cf * y.y);
             }
+          }
           if (c == A.withhold && l == 0 && step == 0) fu_sync();  // the readers' waits run out
           else fu_publish(cntA);
           // the K/V buffer is free: the next block's (or next step's) cached rows,
@@ -1017,7 +1044,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
           if (tid == 0) {
             if (l + 1 < L) fu_kv_prefetch(A, S, l + 1, int(pos));
             else if (step + 1 < A.n_steps && L > 1) fu_kv_prefetch(A, S, 0, int(pos) + 1);
-            if (A.trace) A.trace[(((size_t)c * A.n_steps + step) * (L + 1) + l) * kFuTrace + 20] = fu_tstamp();
+            if (trace) trace[(((size_t)c * A.n_steps + step) * (L + 1) + l) * kFuTrace + 20] = fu_tstamp();
           }
           fmark(step, l, 8);
         }
@@ -1037,6 +1064,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
             have_tok = true;
           }
           const float* src = P.embd + (size_t)(tok % (unsigned)P.V) * d;
+#pragma unroll 1
           for (int i = tid; i < d; i += kFuConsumers) S.R[i] = __ldg(src + i);
         } else {
           fu_add_sum(S.R, S.XA, yb_prev, dn_bias_prev, d, st, pos, -1);
@@ -1077,6 +1105,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
         fu_cols(dslot, d, fnblk, S.ast, S.ast + pl.cb_max * 32, S.ycol, true);
         fu_release(A, S, item++);
         fmark(step, l, 13);
+#pragma unroll 1
         for (int p = tid; p < d / 2; p += kFuConsumers) {
           const float2 y = reinterpret_cast<const float2*>(S.ycol)[p];
           red_add2(yb + 2 * p, y.x, y.y);
@@ -1086,12 +1115,15 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
       fmark(step, l, 14);
     }
     // ================================================================ LM
-    unsigned long long* trow =
-        A.trace ? A.trace + (((size_t)c * A.n_steps + step) * (L + 1) + L) * kFuTrace : nullptr;
-    if (!fu_lm(A, S, step, pos, &item, trow)) return;
+    unsigned long long* trow = trace ? trace + (((size_t)c * A.n_steps + step) * (L + 1) + L) * kFuTrace : nullptr;
+    if (!fu_lm<TRACE>(A, S, step, pos, &item, trow)) return;
   }
 }
 
+// One instantiation per head size (the split attention's lanes hold HD / 32
+// dims each) and with or without the trace stamps: each launch runs only the
+// code of its shapes, which keeps the per-block instruction working set small.
+template <int HD, bool TRACE>
 __global__ void __launch_bounds__(kFuThreads, 1) k_decode_fused(const __grid_constant__ FusedArgs A) {
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const FusedPlan& pl = A.plan;
@@ -1162,13 +1194,14 @@ __global__ void __launch_bounds__(kFuThreads, 1) k_decode_fused(const __grid_con
     }
     return;
   }
+  unsigned long long* const trace = fu_trace<TRACE>(A);
   unsigned long long* anchor =
-      A.trace ? A.trace + (((size_t)blockIdx.x * A.n_steps) * (A.P.n_layers + 1) + A.P.n_layers) * kFuTrace : nullptr;
+      trace ? trace + (((size_t)blockIdx.x * A.n_steps) * (A.P.n_layers + 1) + A.P.n_layers) * kFuTrace : nullptr;
   if (anchor && threadIdx.x == 0) {
     anchor[22] = global_ns();
     anchor[23] = fu_tstamp();
   }
-  fu_consumer(A, S);
+  fu_consumer<HD, TRACE>(A, S);
   // a K/V copy may still be in flight (the last prefetch, or an abort): it must land first
   if (threadIdx.x == 0 && *S.kv_armed > *S.kv_waited) mbar_wait(S.kv_bar, (*S.kv_waited) & 1);
   if (anchor && threadIdx.x == 0) {
@@ -1176,6 +1209,14 @@ __global__ void __launch_bounds__(kFuThreads, 1) k_decode_fused(const __grid_con
     last[21] = fu_tstamp();
     last[20] = global_ns();
   }
+}
+
+// The instantiation for a head size (32, 64 or 128), with or without trace stamps.
+using FusedKernel = void (*)(const FusedArgs);
+inline FusedKernel fused_kernel(int hd, bool trace) {
+  if (hd == 32) return trace ? k_decode_fused<32, true> : k_decode_fused<32, false>;
+  if (hd == 64) return trace ? k_decode_fused<64, true> : k_decode_fused<64, false>;
+  return trace ? k_decode_fused<128, true> : k_decode_fused<128, false>;
 }
 
 // Dynamic shared memory of the fused kernel.
