@@ -481,14 +481,20 @@ __device__ __forceinline__ void red_add2(float* p, float a, float b) {
   asm volatile("red.relaxed.gpu.global.add.v2.f32 [%0], {%1, %2};" ::"l"(p), "f"(a), "f"(b) : "memory");
 }
 
-// Issues the TMA copies of split s's cached K/V rows of block l at `cached`
-// preceding positions (thread 0 of the consumers).
-__device__ __forceinline__ void fu_kv_prefetch(const FusedArgs& A, const FuShared& S, int l, int cached) {
-  const StepParams& P = A.P;
-  const int c = blockIdx.x, h = c / A.plan.S, s = c - h * A.plan.S, g = h / (P.nh / P.nkv);
+// The cached K/V rows split s of a head of KV group g reads when `cached`
+// positions precede this one: their first element in the group's cache and
+// their bytes per cache.
+__device__ __forceinline__ void fu_kv_span(const FusedArgs& A, int g, int s, int cached, size_t& row0,
+                                           uint32_t& bytes) {
   int t0, n_old;
   fu_split(cached, A.plan.S, s, t0, n_old);
-  const uint32_t bytes = uint32_t(n_old) * P.hd * 4;
+  row0 = ((size_t)g * A.P.max_ctx + t0) * A.P.hd;
+  bytes = uint32_t(n_old) * A.P.hd * 4;
+}
+// Issues the TMA copies of a split's cached K/V rows of block l (a span of
+// fu_kv_span; thread 0 of the consumers).
+__device__ __forceinline__ void fu_kv_prefetch(const FusedArgs& A, const FuShared& S, int l, size_t row0,
+                                               uint32_t bytes) {
   const LayerW& Lw = A.layers[l];
   // the rows were written by the KV CTAs of earlier blocks, and this thread
   // has acquired them since (its gate's fence): a proxy fence is enough to
@@ -497,8 +503,8 @@ __device__ __forceinline__ void fu_kv_prefetch(const FusedArgs& A, const FuShare
   *S.kv_armed = *S.kv_armed + 1;
   mbar_expect_tx(S.kv_bar, 2 * bytes);
   if (bytes) {
-    bulk_g2s(S.kvbuf, Lw.kc + ((size_t)g * P.max_ctx + t0) * P.hd, bytes, S.kv_bar);
-    bulk_g2s(S.kvbuf + (size_t)A.plan.cap * P.hd, Lw.vc + ((size_t)g * P.max_ctx + t0) * P.hd, bytes, S.kv_bar);
+    bulk_g2s(S.kvbuf, Lw.kc + row0, bytes, S.kv_bar);
+    bulk_g2s(S.kvbuf + (size_t)A.plan.cap * A.P.hd, Lw.vc + row0, bytes, S.kv_bar);
   }
 }
 
@@ -919,11 +925,19 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
   auto fmark = [&](int step, int l, int k) {
     if (trace && tid == 0) trace[(((size_t)c * A.n_steps + step) * (L + 1) + l) * kFuTrace + k] = fu_tstamp();
   };
-  if (roleA && tid == 0) fu_kv_prefetch(A, S, 0, int(pos0));  // step 0, block 0
+  // this split's cached K/V rows at this step's position (cur) and the next one's (nxt)
+  const int kv_g = roleA ? h / (P.nh / P.nkv) : 0;
+  size_t kv_row_cur = 0, kv_row_nxt = 0;
+  uint32_t kv_b_cur = 0, kv_b_nxt = 0;
+  if (roleA) fu_kv_span(A, kv_g, sp, int(pos0), kv_row_cur, kv_b_cur);
+  if (roleA && tid == 0) fu_kv_prefetch(A, S, 0, kv_row_cur, kv_b_cur);  // step 0, block 0
   for (int step = 0; step < A.n_steps; ++step) {
     const unsigned pos = pos0 + unsigned(step);
-    unsigned tok = 0;
-    bool have_tok = false;
+    if (step > 0) {
+      kv_row_cur = kv_row_nxt;
+      kv_b_cur = kv_b_nxt;
+    }
+    if (roleA) fu_kv_span(A, kv_g, sp, int(pos) + 1, kv_row_nxt, kv_b_nxt);
     for (int l = 0; l < L; ++l) {
       const LayerW& Lw = A.layers[l];
       const Q4View& Q = Lw.qkv;
@@ -933,31 +947,37 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
       float* yb = A.yb + (gl & 1) * d;
       const float* yb_prev = A.yb + ((gl + 1) & 1) * d;  // YB of block l-1
       const float* dn_bias_prev = l > 0 ? A.layers[l - 1].down.bias : nullptr;
-      // ============================================================ phase A
-      if (roleA || roleKV) {
+      // ===================================================== block input R
+      // every CTA: the step's embedding row, or the previous block's x_a plus
+      // its down-projection sum once every CTA has added to it
+      const bool roleAttn = roleA || roleKV;
+      if (roleAttn) {
         fmark(step, l, 0);
-        // constants of the phase while the input is in flight
+        // constants of the attention half while the input is in flight
         fu_prefetch(S.nw, Lw.attn_norm, d);
 #pragma unroll 1
         for (int i = tid; i < half; i += kFuConsumers)
           reinterpret_cast<float2*>(S.rb)[i] = __ldg(P.rope + (size_t)pos * half + i);
         fu_prefetch(S.rb + hd, Q.bias ? Q.bias + qrow0 : nullptr, hd);
-        if (l == 0) {
-          const bool ok = fu_token(A, step, tok);
-          have_tok = true;
-          if (!ok) {
-            flag_timeout(st, 23);
-            *S.cabort = 1;
-          }
-          fu_sync();
-          if (*S.cabort) return;
-          const float* src = P.embd + (size_t)(tok % (unsigned)P.V) * d;  // get_row_core: row token % V
-#pragma unroll 1
-          for (int i = tid; i < d; i += kFuConsumers) S.R[i] = __ldg(src + i);
-        } else {
-          if (!fu_gate(cntB, unsigned(gl) * unsigned(G), S.cabort, st)) return;
-          fu_add_sum(S.R, S.XA, yb_prev, dn_bias_prev, d, st, pos, c == 0 ? l - 1 : -1);
+      }
+      if (l == 0) {
+        unsigned tok = 0;
+        if (!fu_token(A, step, tok)) {
+          flag_timeout(st, 23);
+          *S.cabort = 1;
         }
+        fu_sync();
+        if (*S.cabort) return;
+        const float* src = P.embd + (size_t)(tok % (unsigned)P.V) * d;  // get_row_core: row token % V
+#pragma unroll 1
+        for (int i = tid; i < d; i += kFuConsumers) S.R[i] = __ldg(src + i);
+      } else {
+        if (!fu_gate(cntB, unsigned(gl) * unsigned(G), S.cabort, st)) return;
+        fu_add_sum(S.R, S.XA, yb_prev, dn_bias_prev, d, st, pos, c == 0 ? l - 1 : -1);
+      }
+      if (!roleAttn) fu_sync();  // (the attention half has its own barrier after the clearing)
+      // ============================================================ phase A
+      if (roleAttn) {
         if (roleA) {  // clear the sums read two phases ago: YA of block l-1, YB of block l-2
           const int per = (d + pl.nA - 1) / pl.nA;
 #pragma unroll 1
@@ -969,7 +989,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
             }
           }
         }
-        if (L == 1 && roleA && tid == 0 && step > 0) fu_kv_prefetch(A, S, 0, int(pos));
+        if (L == 1 && roleA && tid == 0 && step > 0) fu_kv_prefetch(A, S, 0, kv_row_cur, kv_b_cur);
         fu_sync();
         fmark(step, l, 1);
         const float inv = fu_stage_norm(S.R, S.nw, d, P.eps, S.xs, S.xsum, S.misc, c == 0, st, pos, l);
@@ -1042,8 +1062,10 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
           // the K/V buffer is free: the next block's (or next step's) cached rows,
           // requested off the critical path while the FFN half waits
           if (tid == 0) {
-            if (l + 1 < L) fu_kv_prefetch(A, S, l + 1, int(pos));
-            else if (step + 1 < A.n_steps && L > 1) fu_kv_prefetch(A, S, 0, int(pos) + 1);
+            const bool same_step = l + 1 < L;
+            if (same_step || (step + 1 < A.n_steps && L > 1))
+              fu_kv_prefetch(A, S, same_step ? l + 1 : 0, same_step ? kv_row_cur : kv_row_nxt,
+                             same_step ? kv_b_cur : kv_b_nxt);
             if (trace) trace[(((size_t)c * A.n_steps + step) * (L + 1) + l) * kFuTrace + 20] = fu_tstamp();
           }
           fmark(step, l, 8);
@@ -1054,23 +1076,6 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
       if (nfo > 0) fu_prefetch(S.gub, Lw.gate_up.bias ? Lw.gate_up.bias + (size_t)fo0 * 2 : nullptr, nfo * 2);
       if (!fu_gate(cntA, unsigned(gl + 1) * unsigned(pl.nA), S.cabort, st)) return;
       fmark(step, l, 9);
-      if (!(roleA || roleKV)) {  // R of this block from the sums of the previous one
-        if (l == 0) {
-          if (!have_tok) {
-            if (!fu_token(A, step, tok)) {
-              flag_timeout(st, 23);
-              *S.cabort = 1;
-            }
-            have_tok = true;
-          }
-          const float* src = P.embd + (size_t)(tok % (unsigned)P.V) * d;
-#pragma unroll 1
-          for (int i = tid; i < d; i += kFuConsumers) S.R[i] = __ldg(src + i);
-        } else {
-          fu_add_sum(S.R, S.XA, yb_prev, dn_bias_prev, d, st, pos, -1);
-        }
-        fu_sync();
-      }
       fu_add_sum(S.XA, S.R, ya, Lw.wo.bias, d, st, pos, -1);
       fu_sync();
       if (*S.cabort) return;
