@@ -124,9 +124,9 @@ struct FusedArgs {
   int withhold;  // diagnostic: this CTA raises no attention-half flag in block 0 of step 0 (-1: none)
 };
 
-// Trace points per block (phase A 0-8 and 15-20, phase B 9-14) and for the
+// Trace points per block (phase A 0-8, 15-21, phase B 9-14) and for the
 // lm_head (block index L: 0 entry, 1 input ready, 2 staged, 3 rows done, 4
-// token out).
+// token out); slot 22 of step 0's block 0 holds the CTA's SM id.
 constexpr int kFuTrace = 24;
 
 // Trace stamps are SM cycle counts (clock64: fine-grained, but per SM); each
@@ -973,6 +973,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
         for (int i = tid; i < d; i += kFuConsumers) S.R[i] = __ldg(src + i);
       } else {
         if (!fu_gate(cntB, unsigned(gl) * unsigned(G), S.cabort, st)) return;
+        fmark(step, l, 21);
         fu_add_sum(S.R, S.XA, yb_prev, dn_bias_prev, d, st, pos, c == 0 ? l - 1 : -1);
       }
       if (!roleAttn) fu_sync();  // (the attention half has its own barrier after the clearing)
@@ -1205,6 +1206,9 @@ __global__ void __launch_bounds__(kFuThreads, 1) k_decode_fused(const __grid_con
   if (anchor && threadIdx.x == 0) {
     anchor[22] = global_ns();
     anchor[23] = fu_tstamp();
+    unsigned smid;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+    trace[((size_t)blockIdx.x * A.n_steps) * (A.P.n_layers + 1) * kFuTrace + 22] = smid;  // block 0 row of step 0
   }
   fu_consumer<HD, TRACE>(A, S);
   // a K/V copy may still be in flight (the last prefetch, or an abort): it must land first

@@ -483,13 +483,15 @@ class GenomicLLM:
         (float64, 0 where a CTA had no such point): shape [grid, n_steps, n_blocks+1, 24] (see
         gaje_cuda_trace_fused for the points).  The kernel stamps SM cycles;
         each CTA's (globaltimer, cycle) anchors at its start and end map them
-        onto the global clock."""
+        onto the global clock.  The CTAs' SM ids are left in self.trace_smid."""
         inf = self.info()
         L = inf.n_blocks
         raw = np.zeros((inf.grid, int(n_steps), L + 1, 24), dtype=np.uint64)
         n = C.c_size_t(0)
         _check(lib().gaje_cuda_trace_fused(self._m, int(first_token), int(n_steps), _ptr(raw), C.c_size_t(raw.size),
                                            C.byref(n)))
+        self.trace_smid = raw[:, 0, 0, 22].astype(np.int64)  # each CTA's SM
+        raw[:, 0, 0, 22] = 0
         # differences in integers first: float64 cannot resolve single
         # nanoseconds (or cycles) at the timers' absolute magnitudes
         g0i, c0i = raw[:, 0, L, 22].copy(), raw[:, 0, L, 23].copy()

@@ -350,8 +350,10 @@ int gaje_cuda_trace_steps(gaje_model* model, uint32_t first_token, size_t n_step
  * input flags seen, 10 x_a formed, 11 staged, 12 first gate/up block done,
  * 13 down columns done, 14 phase B published, 15 split weight done, 16 the
  * split's attention starts, 17 scores done, 18 softmax done, 19 P*V done,
- * 20 next block's K/V rows requested (after 8).  l = L: 0 entry, 1 input ready, 2 staged, 3
- * lm_head rows done, 4 token published.  out_len must be at least
+ * 20 next block's K/V rows requested (after 8), 21 the block input's flags
+ * seen (blocks after the first).  l = L: 0 entry, 1 input ready, 2 staged, 3
+ * lm_head rows done, 4 token published.  Slot 22 of (step 0, block 0) holds
+ * the CTA's SM id (%smid) instead of a cycle count.  out_len must be at least
  * grid*n_steps*(L+1)*24.  No counterpart in the reference: a
  * diagnostic of the kernel's critical path. */
 int gaje_cuda_trace_fused(gaje_model* model, uint32_t first_token, size_t n_steps,
