@@ -918,7 +918,12 @@ bool plan_fused(gaje_model* m) {
   // splits of ~48 cached positions, plus the one that takes this position's row
   p.S = std::min({s_cta, kFuMaxSplits, std::max(1, (cached + 47) / 48 + 1)});
   p.nA = m->nh * p.S;
-  p.nKV = 2 * m->nkv;
+  // the k/v rows of this position on as many CTAs as are left (the last
+  // splits wait for them), up to 8 per head, an even row count each
+  p.kv_split = 1;
+  while (p.kv_split < 8 && p.nA + 2 * m->nkv * 2 * p.kv_split <= G && (hd / (2 * p.kv_split)) % 2 == 0)
+    p.kv_split *= 2;
+  p.nKV = 2 * m->nkv * p.kv_split;
   p.cap = (cached + std::max(1, p.S - 1) - 1) / std::max(1, p.S - 1) + 1;  // fu_split's largest chunk + this row
   p.pv_groups = std::max(1, kFuConsumers / hd);
   p.ob_max = 0;

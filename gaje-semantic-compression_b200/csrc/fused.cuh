@@ -73,7 +73,8 @@ struct FuLayer {
 struct FusedPlan {
   int S;          // attention splits per q head
   int nA;         // attention CTAs: n_head * S (CTAs [0, nA))
-  int nKV;        // k/v CTAs: 2 * n_kv (CTAs [nA, nA + nKV))
+  int nKV;        // k/v CTAs: 2 * n_kv * kv_split (CTAs [nA, nA + nKV))
+  int kv_split;   // CTAs per k or v head, each hd / kv_split of its rows
   int cap;        // K/V rows one split holds: cached chunk + this position's row
   int nslots;
   unsigned slot_bytes;
@@ -322,18 +323,19 @@ __device__ __forceinline__ bool fu_block_item(const FusedArgs& A, const LayerW& 
   int k = i;
   const Q4View& Q = Lw.qkv;
   if (c < pl.nA + pl.nKV) {
-    int row0;
+    int row0, nr = hd;
     if (c < pl.nA) {
       row0 = (c / pl.S) * hd;
     } else {
-      const int j = c - pl.nA, kv = j / P.nkv, g = j - kv * P.nkv;
-      row0 = (P.nh + kv * P.nkv + g) * hd;
+      const int j = c - pl.nA, hv = j / pl.kv_split, sl = j - hv * pl.kv_split, kv = hv / P.nkv, g = hv - kv * P.nkv;
+      nr = hd / pl.kv_split;
+      row0 = (P.nh + kv * P.nkv + g) * hd + sl * nr;
     }
     if (k == 0) {
       it.a = Q.qs + (size_t)row0 * Q.nb;
-      it.na = uint32_t(hd) * Q.nb * 16;
+      it.na = uint32_t(nr) * Q.nb * 16;
       it.b = Q.sm + (size_t)row0 * Q.nbp;
-      it.nb = uint32_t(hd) * Q.nbp * 4;
+      it.nb = uint32_t(nr) * Q.nbp * 4;
       return true;
     }
     --k;
@@ -911,9 +913,14 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
   const int L = P.n_layers, d = P.d, hd = P.hd, half = hd >> 1, G = gridDim.x;
   const bool roleA = c < pl.nA, roleKV = !roleA && c < pl.nA + pl.nKV;
   const int h = roleA ? c / pl.S : 0, sp = roleA ? c - h * pl.S : 0;
-  const int kvj = roleKV ? c - pl.nA : 0, kvk = kvj / P.nkv, kvg = kvj - kvk * P.nkv;
-  // this CTA's first q/k/v row (pair-interleaved storage)
-  const int qrow0 = roleA ? h * hd : (P.nh + kvk * P.nkv + kvg) * hd;
+  // a k/v CTA: slice kvs of the rows of k (kvk 0) or v head kvg
+  const int kvj = roleKV ? c - pl.nA : 0, kvh = kvj / pl.kv_split, kvs = kvj - kvh * pl.kv_split;
+  const int kvk = kvh / P.nkv, kvg = kvh - kvk * P.nkv;
+  // this CTA's q/k/v rows [qrow0, qrow0 + nqr) (pair-interleaved storage) and
+  // the head's RoPE pair of their first two
+  const int nqr = roleA ? hd : hd / pl.kv_split;
+  const int qrow0 = roleA ? h * hd : (P.nh + kvk * P.nkv + kvg) * hd + kvs * nqr;
+  const int pbase = roleA ? 0 : kvs * (nqr >> 1);
   int fo0, nfo;  // this CTA's SwiGLU outputs [fo0, fo0 + nfo)
   fu_outs(P.ff, G, c, fo0, nfo);
   const int fkb0 = fo0 / 32, fnblk = nfo > 0 ? (fo0 + nfo - 1) / 32 - fkb0 + 1 : 0;
@@ -958,7 +965,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
 #pragma unroll 1
         for (int i = tid; i < half; i += kFuConsumers)
           reinterpret_cast<float2*>(S.rb)[i] = __ldg(P.rope + (size_t)pos * half + i);
-        fu_prefetch(S.rb + hd, Q.bias ? Q.bias + qrow0 : nullptr, hd);
+        fu_prefetch(S.rb + hd, Q.bias ? Q.bias + qrow0 : nullptr, nqr);
       }
       if (l == 0) {
         unsigned tok = 0;
@@ -998,14 +1005,14 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
         const unsigned char* slot = fu_wait_slot(A, S, item);
         fu_sync();
         if (*S.cabort) return;
-        fu_rows_raw(slot, hd, Q.nb, Q.nbp, S.xs, S.xsum, S.pv, S.raw);
+        fu_rows_raw(slot, nqr, Q.nb, Q.nbp, S.xs, S.xsum, S.pv, S.raw);
         fu_release(A, S, item++);
         fu_sync();
         // epilogue, a thread per row pair: flush, bias, RoPE (q, k)
-        if (tid < half) {
-          const int p = tid;
-          float y0 = flush_small(S.raw[2 * p] * inv) + S.rb[hd + 2 * p];
-          float y1 = flush_small(S.raw[2 * p + 1] * inv) + S.rb[hd + 2 * p + 1];
+        if (tid < (nqr >> 1)) {
+          const int p = pbase + tid;  // the pair within the head
+          float y0 = flush_small(S.raw[2 * tid] * inv) + S.rb[hd + 2 * tid];
+          float y1 = flush_small(S.raw[2 * tid + 1] * inv) + S.rb[hd + 2 * tid + 1];
           if (roleA || kvk == 0) {  // RoPE: v0*cos - v1*sin, v0*sin + v1*cos
             const float cs = S.rb[2 * p], sn = S.rb[2 * p + 1];
             const float o0 = y0 * cs - y1 * sn, o1 = y0 * sn + y1 * cs;
