@@ -256,8 +256,10 @@ __device__ __forceinline__ unsigned ld_acq_u32(const unsigned* p) {
   return v;
 }
 __device__ __noinline__ bool fu_gate(const unsigned* cnt, unsigned target, volatile int* cabort, DevState* st) {
-  if (threadIdx.x < 32) {
-    if (threadIdx.x == 0) {
+  // the last consumer warp polls: thread 0 may still be busy with its
+  // release add and the next K/V request when the gate is reached
+  if ((threadIdx.x >> 5) == kFuConsumerWarps - 1) {
+    if ((threadIdx.x & 31) == 0) {
       bool ok = true;
       if (int(ld_rlx_u32(cnt) - target) < 0) {
         const unsigned long long t0 = global_ns();
