@@ -561,12 +561,29 @@ __device__ __forceinline__ float fu_stage_norm(const float* x, const float* nw, 
                                             int layer) {
   float ss = 0.f;
   bool wbad = false;
+  const int lane = threadIdx.x & 31;
+  // two elements per pass (whole warps: d % 32 == 0), their block sums'
+  // shuffles interleaved
 #pragma unroll 1
-  for (int i = threadIdx.x; i < d; i += kFuConsumers) {  // whole warps: d % 32 == 0
-    const float v = x[i], w = nw[i];
-    ss = fmaf(v, v, ss);
-    wbad |= !(fabsf(w) <= 3.402823466e38f);
-    mk_stage_elem(xs, xsum, i, v * w);
+  for (int i0 = threadIdx.x; i0 < d; i0 += 2 * kFuConsumers) {
+    const int i1 = i0 + kFuConsumers;
+    const bool h1 = i1 < d;  // warp-uniform
+    const float v0 = x[i0], w0 = nw[i0], v1 = h1 ? x[i1] : 0.f, w1 = h1 ? nw[i1] : 0.f;
+    ss = fmaf(v0, v0, ss);
+    if (h1) ss = fmaf(v1, v1, ss);
+    wbad |= !(fabsf(w0) <= 3.402823466e38f) || !(fabsf(w1) <= 3.402823466e38f);
+    float s0 = v0 * w0, s1 = v1 * w1;
+    xs[swz(i0)] = s0 * nib_prescale(i0 & 7);
+    if (h1) xs[swz(i1)] = s1 * nib_prescale(i1 & 7);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      s0 += __shfl_xor_sync(0xffffffffu, s0, o);
+      s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+    }
+    if (lane == 0) {
+      xsum[i0 >> 5] = s0;
+      if (h1) xsum[i1 >> 5] = s1;
+    }
   }
   const float tot = fu_total(ss, red, false);
   const float inv = 1.0f / sqrtf(tot / (float)d + eps);
@@ -616,7 +633,7 @@ __device__ __forceinline__ void fu_prefetch(float* dst, const float* src, int n)
 // split's position count, or -1 when a wait ran out (the CTA's abort raised).
 template <int VEC, bool TRACE>
 __device__ __forceinline__ int fu_attend_warp(const FusedArgs& A, const FuShared& S, int l, int step, unsigned pos,
-                                              int h, int sp, unsigned eA) {
+                                              int h, int sp, unsigned eA, uint32_t kv_bytes) {
   const StepParams& P = A.P;
   const FusedPlan& pl = A.plan;
   DevState* st = P.st;
@@ -625,8 +642,7 @@ __device__ __forceinline__ int fu_attend_warp(const FusedArgs& A, const FuShared
   unsigned long long* const tr = fu_trace<TRACE>(A);
   unsigned long long* trow = tr ? tr + (((size_t)blockIdx.x * A.n_steps + step) * (L + 1) + l) * kFuTrace : nullptr;
   if (trow && lane == 0) trow[16] = fu_tstamp();  // trace point 16: the split's attention starts
-  int t0, n_old;
-  fu_split(int(pos), pl.S, sp, t0, n_old);
+  const int n_old = int(kv_bytes / (HD * 4));  // the split's cached rows (fu_kv_span at this position)
   const bool last = sp == pl.S - 1;
   const int n = n_old + (last ? 1 : 0);
   float* Ks = S.kvbuf;
@@ -1038,7 +1054,7 @@ __device__ void fu_consumer(const FusedArgs& A, const FuShared& S) {
         fmark(step, l, 3);
         if (roleA) {
           if (wid == 0) {
-            const int na = fu_attend_warp<HD / 32, TRACE>(A, S, l, step, pos, h, sp, eA);
+            const int na = fu_attend_warp<HD / 32, TRACE>(A, S, l, step, pos, h, sp, eA, kv_b_cur);
             if (lane == 0) reinterpret_cast<int*>(S.misc)[41] = na;
           }
           fu_sync();
