@@ -950,6 +950,7 @@ bool plan_fused(gaje_model* m) {
   if (p.nslots < 3) return false;
   m->lm_row_bytes = m->info.lm_head_bit_depth == 8 ? q8_row_bytes(d) : d * 4;
   p.lm_stage_rows = int(std::min<size_t>(kFuConsumerWarps, p.slot_bytes / size_t(m->lm_row_bytes)));
+
   m->fused_smem = fused_smem_bytes(p, d, hd) + 128;
   return p.lm_stage_rows >= 1;
 }

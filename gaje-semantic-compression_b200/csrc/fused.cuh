@@ -372,10 +372,19 @@ __device__ __forceinline__ bool fu_block_item(const FusedArgs& A, const LayerW& 
   return true;
 }
 
+// Every weight byte (body and lm_head) is read once per step and the weights
+// are far larger than L2, so the streams are loaded with an evict-first L2
+// policy: they do not displace the lines that are reused (the exchange sums,
+// LL words, the K/V cache rows): 517.4 -> 513.8 and 518.7 -> 515.0 us per
+// step on two boxes.  (Holding part of the lm_head in L2 across steps with an
+// evict-last policy was slower: 48 MB 514.8, 80 MB 517.5, 110 MB 524.2 us;
+// loading the K/V rows evict-last did not help either.)
 __device__ void fu_producer(const FusedArgs& A, const FuShared& S) {
   const StepParams& P = A.P;
   const FusedPlan& pl = A.plan;
   const int rbeg = blockIdx.x * pl.lm_rows_per_cta, rend = min(P.V, rbeg + pl.lm_rows_per_cta);
+  const uint64_t pol = l2_policy_evict_first();
+  const unsigned char* lm_base = P.lm_q8 ? P.lm_q8 : reinterpret_cast<const unsigned char*>(P.lm_head);
   int item = 0;
   for (int step = 0; step < A.n_steps; ++step) {
     for (int l = 0; l <= P.n_layers; ++l) {
@@ -386,7 +395,7 @@ __device__ void fu_producer(const FusedArgs& A, const FuShared& S) {
         } else {
           const int r = rbeg + i * pl.lm_stage_rows;
           if (r >= rend) break;
-          it.a = P.lm_q8 ? (const void*)(P.lm_q8 + (size_t)r * P.lm_row_bytes) : (const void*)(P.lm_head + (size_t)r * P.d);
+          it.a = lm_base + (size_t)r * P.lm_row_bytes;
           it.na = uint32_t(min(pl.lm_stage_rows, rend - r)) * uint32_t(P.lm_row_bytes);
         }
         const int slot = item % pl.nslots;
@@ -398,8 +407,8 @@ __device__ void fu_producer(const FusedArgs& A, const FuShared& S) {
         if (*S.abort_flag || *S.cabort) return;
         unsigned char* dst = S.slots + (size_t)slot * pl.slot_bytes;
         mbar_expect_tx(S.full + slot, it.na + it.nb);
-        bulk_g2s(dst, it.a, it.na, S.full + slot);
-        if (it.nb) bulk_g2s(dst + it.na, it.b, it.nb, S.full + slot);
+        bulk_g2s_hint(dst, it.a, it.na, S.full + slot, pol);
+        if (it.nb) bulk_g2s_hint(dst + it.na, it.b, it.nb, S.full + slot, pol);
         ++item;
         *S.issued = item;
       }
