@@ -283,7 +283,8 @@ __global__ void __launch_bounds__(kAbThreads, 2) k_attn_batch2(AttnBatchArgs B) 
     const uint32_t bytes = uint32_t(rows) * HD * 4;
     uint64_t* bar = full + (it % kAbStages);
     mbar_expect_tx(bar, bytes);
-    bulk_g2s(tiles + (size_t)(it % kAbStages) * kAbTile * HD, src, bytes, bar);
+    // cache rows are read once per step: evict-first keeps L2 for the reused data
+    bulk_g2s_hint(tiles + (size_t)(it % kAbStages) * kAbTile * HD, src, bytes, bar, l2_policy_evict_first());
   };
   if (tid == 0)
     for (int it = 0; it < min(kAbStages, nitems); ++it) issue(it);

@@ -203,8 +203,9 @@ struct Q4Rows {  // Q4_0: w = fma(q, scale, min) (genomic.rs:267-336)
     const int rows = min(kTcRows, ld - row0);
     const size_t o = (size_t)blk * ld + row0;
     mbar_expect_tx(bar, uint32_t(rows) * 20u);
-    bulk_g2s(slot, qsT + o, uint32_t(rows) * 16u, bar);
-    bulk_g2s(slot + kTcRows * 16, smT + o, uint32_t(rows) * 4u, bar);
+    const uint64_t pol = l2_policy_evict_first();  // read once per step: keep L2 for the activations
+    bulk_g2s_hint(slot, qsT + o, uint32_t(rows) * 16u, bar, pol);
+    bulk_g2s_hint(slot + kTcRows * 16, smT + o, uint32_t(rows) * 4u, bar, pol);
   }
   // half h (16 elements) of slot row rl
   __device__ __forceinline__ void read_raw(Regs& g, const unsigned char* slot, int rl, int h) const {
