@@ -863,7 +863,8 @@ def main():
     ap.add_argument("--steps", type=int, default=256)
     ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--config", default=CONFIG_KEY)
+    ap.add_argument("--config", default=None,
+                    help="model shape (configs.py); default qwen2-0.5b, or qwen2.5-1.5b with --batch")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-serving", action="store_true",
                     help="plain N=1 run: skip the serving workload's N=1 measurement (the 'serving' object)")
@@ -892,6 +893,8 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.config is None:  # configs[3] (--batch) is quoted on the Qwen2.5-1.5B shape
+        args.config = SERVE_CONFIG if args.batch > 0 else CONFIG_KEY
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
