@@ -84,30 +84,6 @@ struct FusedPlan {
   int pv_groups;  // position groups of the P*V partial sums
 };
 
-// One block of 32 weights for four rows sharing the staged activations of
-// block b (the arithmetic of q4_pair_qx, with the activation loads shared).
-__device__ __forceinline__ void q4_quad_qx(const uint4 q0, const uint4 q1, const uint4 q2, const uint4 q3,
-                                           const float* xs, int b, float& A0, float& A1, float& A2, float& A3) {
-  const float4* x4 = reinterpret_cast<const float4*>(xs + (b << 5));
-  const int sw = b & 7;
-  unsigned long long r00 = 0ull, r01 = 0ull, r10 = 0ull, r11 = 0ull, r20 = 0ull, r21 = 0ull, r30 = 0ull,
-                     r31 = 0ull;
-  const uint32_t w0[4] = {q0.x, q0.y, q0.z, q0.w}, w1[4] = {q1.x, q1.y, q1.z, q1.w};
-  const uint32_t w2[4] = {q2.x, q2.y, q2.z, q2.w}, w3[4] = {q3.x, q3.y, q3.z, q3.w};
-#pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    const float4 xa = x4[(2 * w) ^ sw], xb = x4[(2 * w + 1) ^ sw];
-    q4_word_qx(w0[w], xa, xb, r00, r01);
-    q4_word_qx(w1[w], xa, xb, r10, r11);
-    q4_word_qx(w2[w], xa, xb, r20, r21);
-    q4_word_qx(w3[w], xa, xb, r30, r31);
-  }
-  A0 = hsum2(r00, r01);
-  A1 = hsum2(r10, r11);
-  A2 = hsum2(r20, r21);
-  A3 = hsum2(r30, r31);
-}
-
 struct FusedArgs {
   StepParams P;
   const LayerW* layers;
@@ -210,11 +186,6 @@ struct FuShared {
 
 __device__ __forceinline__ void fu_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kFuConsumers) : "memory"); }
 
-__device__ __forceinline__ void red_add4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c),
-               "f"(d)
-               : "memory");
-}
 __device__ __forceinline__ float ld_rlx(const float* p) {
   float v;
   asm volatile("ld.relaxed.gpu.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
@@ -288,26 +259,6 @@ __device__ __noinline__ bool fu_gate(const unsigned* cnt, unsigned target, volat
 __device__ __forceinline__ void fu_publish(unsigned* cnt) {
   fu_sync();
   if (threadIdx.x == 0) asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(cnt) : "memory");
-}
-
-// Reads n LL words of epoch e (bounded) into dst (shared memory).
-__device__ __noinline__ bool fu_ll_read(const uint2* src, int n, unsigned e, float* dst) {
-  bool ok = true;
-  for (int i = threadIdx.x; i < n; i += kFuConsumers) {
-    uint2 w = ld_ll(src + i);
-    unsigned long long t0 = 0;
-    while (w.y != e) {
-      const unsigned long long t = global_ns();
-      if (!t0) t0 = t;
-      else if (t - t0 > c_wait_ns) {
-        ok = false;
-        break;
-      }
-      w = ld_ll(src + i);
-    }
-    dst[i] = __uint_as_float(w.x);
-  }
-  return ok;
 }
 
 // ----------------------------------------------------------- producer
